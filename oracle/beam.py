@@ -1,0 +1,90 @@
+"""Oracle: shortlist head + beam search (chain and tree), fp32 CPU, test infrastructure.
+
+Restates ``FlowDrafterProposer._beam_chains`` (reference
+``src/chain_flow/vllm_plugin/flow_proposer.py:1188-1269``) and ``_beam_tree`` (``:1273-1332``)
+with the one-pass head (``CF_TWOPASS_M=0``), ``CF_FEEDBACK=0`` and ``CF_PATH_TRIM=1``.
+"""
+from __future__ import annotations
+
+import torch
+
+from .flow import FlowConfig, path_residual, markov_bias
+
+
+def head_logprobs(W, emb, hw, w2_sl, h, lastp, order, nlive):
+    """log_softmax over the shortlist of (h + path residual) @ hw^T + markov bias
+    (reference flow_proposer.py:1021-1025, 1247-1249). Returns (logits, logprobs) [N, R]."""
+    res = path_residual(W, emb, lastp, order, nlive)
+    logits = (h.float() + res) @ hw.float().T + markov_bias(W, w2_sl, lastp[:, 0])
+    return logits, torch.log_softmax(logits, dim=-1)
+
+
+def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int, K: int):
+    """Chain beam over the integrated hiddens ``pred`` [B, draft_length, D].
+
+    Depth 0 is seeded with the committed token (one live beam, cum = [0, -inf, ...]); depths
+    1..K each rescore every beam with the path residual + markov bias, keep the top ``width``
+    extensions of the width x width candidates, then the best path is walked back.
+    Returns [B, K] int64 global token ids.
+    """
+    B = pred.shape[0]
+    Wd, order = width, cfg.path_order
+    lastp = torch.full((B, Wd, order), -1, dtype=torch.long)
+    lastp[:, :, 0] = known0.view(B, 1)
+    cum = torch.full((B, Wd), float("-inf"))
+    cum[:, 0] = 0.0
+    steps = min(K + 1, pred.shape[1])
+    toks, bps = [], []
+    for step in range(1, steps):
+        h = pred[:, step].float().unsqueeze(1).expand(B, Wd, -1).reshape(B * Wd, -1)
+        _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * Wd, order), order, step)
+        cv, ci = lp.topk(Wd, dim=-1)                                    # [B*W, W]
+        ci = ci.reshape(B, Wd * Wd)
+        cand = (cum.reshape(B * Wd, 1) + cv).reshape(B, Wd * Wd)
+        cum, flat = cand.topk(Wd, dim=-1)
+        src = flat // Wd
+        newtok = sl[ci.gather(1, flat)]
+        lastp = lastp.gather(1, src.unsqueeze(-1).expand(B, Wd, order))
+        lastp = torch.cat([newtok.unsqueeze(-1), lastp[:, :, :-1]], dim=-1)
+        toks.append(newtok)
+        bps.append(src)
+    idx = cum.argmax(dim=-1)
+    seq = [None] * len(toks)
+    for step in range(len(toks) - 1, -1, -1):
+        seq[step] = toks[step].gather(1, idx.unsqueeze(1)).squeeze(1)
+        idx = bps[step].gather(1, idx.unsqueeze(1)).squeeze(1)
+    return torch.stack(seq, dim=1)
+
+
+def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, topb: int,
+              depth: int):
+    """Tree draft: every surviving extension becomes a BFS-ordered node. Returns [B, 2N]
+    = N global token ids followed by N parent node indices (-1 for depth-1 nodes)."""
+    B = pred.shape[0]
+    order = cfg.path_order
+    fr = 1
+    lastp = torch.full((B, fr, order), -1, dtype=torch.long)
+    lastp[:, :, 0] = known0.view(B, 1)
+    cum = torch.zeros(B, fr)
+    prev_ids = torch.full((B, fr), -1, dtype=torch.long)
+    toks, pars = [], []
+    base = 0
+    nstep = min(depth, pred.shape[1] - 1)
+    for step in range(1, nstep + 1):
+        h = pred[:, step].float().unsqueeze(1).expand(B, fr, -1).reshape(B * fr, -1)
+        _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * fr, order), order, step)
+        cv, ci = lp.topk(topb, dim=-1)                                  # [B*fr, TB]
+        ci = ci.reshape(B, fr * topb)
+        cand = (cum.reshape(B * fr, 1) + cv).reshape(B, fr * topb)
+        k = min(keep, fr * topb)
+        cum, flat = cand.topk(k, dim=-1)
+        src = flat // topb
+        newtok = sl[ci.gather(1, flat)]
+        toks.append(newtok)
+        pars.append(prev_ids.gather(1, src))
+        lastp = lastp.gather(1, src.unsqueeze(-1).expand(B, k, order))
+        lastp = torch.cat([newtok.unsqueeze(-1), lastp[:, :, :-1]], dim=-1)
+        prev_ids = base + torch.arange(k).expand(B, k)
+        base += k
+        fr = k
+    return torch.cat(toks + pars, dim=1)

@@ -1,0 +1,65 @@
+"""Oracle: tree-aware Gated-DeltaNet recurrence (fp32, CPU, test infrastructure).
+
+Restates ``tree_gated_delta_scan`` and ``sequential_path_output`` from the reference
+``src/chain_flow/kernels/tree_scan.py:25-96``. Per node n with parent p (p = -1 for a root,
+which reads the shared prefix state):
+
+    S_n = S_p * exp(g_n)
+    S_n = S_n + k_n (x) (beta_n * (v_n - S_n^T k_n))
+    o_n = S_n^T q_n
+
+with q, k L2-normalised as x / (||x|| + 1e-6) and q scaled by Dk**-0.5. States are
+[H, Dk, Dv] fp32.
+"""
+from __future__ import annotations
+
+import torch
+
+
+def _l2n(x, eps=1e-6):
+    return x / (x.norm(dim=-1, keepdim=True) + eps)
+
+
+def _step(S, q, k, v, g, beta):
+    S = S * g.exp()[..., None, None]
+    kv = (S * k[..., None]).sum(-2)                     # S^T k  [.., Dv]
+    S = S + k[..., None] * ((v - kv) * beta[..., None])[..., None, :]
+    o = (S * q[..., None]).sum(-2)
+    return S, o
+
+
+def tree_gdn_scan(q, k, v, g, beta, parent, depth, init, use_qk_l2norm=True):
+    """q,k [N,H,Dk]; v [N,H,Dv]; g,beta [N,H]; parent,depth [N]; init [H,Dk,Dv]
+    -> (o [N,H,Dv], states [N,H,Dk,Dv]). Depth-synchronous, like the reference."""
+    q, k, v, g, beta = (t.float() for t in (q, k, v, g, beta))
+    if use_qk_l2norm:
+        q, k = _l2n(q), _l2n(k)
+    N, H, Dk = q.shape
+    Dv = v.shape[-1]
+    q = q * Dk ** -0.5
+    states = torch.zeros(N, H, Dk, Dv)
+    out = torch.zeros(N, H, Dv)
+    init = init.float()
+    maxd = int(depth.max()) if N else -1
+    for d in range(maxd + 1):
+        idx = (depth == d).nonzero(as_tuple=True)[0]
+        if idx.numel() == 0:
+            continue
+        Sp = init.unsqueeze(0).expand(idx.numel(), -1, -1, -1) if d == 0 else states[parent[idx]]
+        Sn, o = _step(Sp, q[idx], k[idx], v[idx], g[idx], beta[idx])
+        states[idx] = Sn
+        out[idx] = o
+    return out, states
+
+
+def path_gdn_output(q, k, v, g, beta, path, init, use_qk_l2norm=True):
+    """Sequential recurrence along one root..node path; returns the last node's o [H, Dv]."""
+    q, k, v, g, beta = (t.float() for t in (q, k, v, g, beta))
+    if use_qk_l2norm:
+        q, k = _l2n(q), _l2n(k)
+    q = q * q.shape[-1] ** -0.5
+    S = init.float().clone().unsqueeze(0)
+    o = None
+    for n in path:
+        S, o = _step(S, q[n:n + 1], k[n:n + 1], v[n:n + 1], g[n:n + 1], beta[n:n + 1])
+    return o[0]
