@@ -1,0 +1,128 @@
+// cfb_common.cuh -- device helpers shared by the sm_100a kernels of libcfb.so.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#define CFB_DEV __device__ __forceinline__
+
+#include "../../include/cfb.h"
+// Host: record the CUDA error of the last launch (if any) for cfb_last_cuda_error(); returns the
+// status the C ABI reports. Defined in cfb_engine.cu.
+cfb_status cfb_launch_status(const char* what);
+
+namespace cfb {
+
+// Device error word values (written into the workspace, read by cfb_plan_error).
+enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_GRID = 1, DEV_TIMEOUT_FULL = 2, DEV_TIMEOUT_EMPTY = 3,
+                    DEV_TIMEOUT_SLOT = 4, DEV_BAD_PHASE = 5 };
+
+// Every device-side wait is bounded by this many nanoseconds of %globaltimer. On expiry the
+// waiter records an error and returns, so a broken schedule ends the launch instead of hanging
+// the GPU.
+constexpr unsigned long long kWaitBudgetNs = 1000000000ull;   // 1 s
+
+CFB_DEV unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+CFB_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier -------------------------------------------------------------------------------
+CFB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+CFB_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+CFB_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+               :: "r"(smem_u32(bar)) : "memory");
+}
+CFB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+CFB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.b32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+CFB_DEV int ld_volatile_int(const int* p);
+
+// Bounded wait; returns false on timeout, or at once when `err` (if given) is already set,
+// so that after the first failure the rest of a launch runs through without waiting.
+CFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (err && ld_volatile_int(err) != 0) return false;
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitBudgetNs) return false;
+    if (err && ld_volatile_int(err) != 0) return false;
+  }
+  return true;
+}
+
+// ---- bulk copy global -> shared (the TMA unit, 1-D form; no multicast) -------------------
+CFB_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// ---- named barrier among the consumer warps ------------------------------------------------
+CFB_DEV void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" :: "r"(nthreads) : "memory");
+}
+
+// ---- tensor core (legacy warp-level MMA, m16n8k16, fp16 in, fp32 accumulate) -------------
+CFB_DEV void mma16816(float (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+CFB_DEV uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+CFB_DEV float2 unpack_half2(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+
+// ---- gpu-scope atomics / loads with explicit ordering ------------------------------------
+CFB_DEV unsigned atom_add_acqrel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+CFB_DEV unsigned atom_add_release(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+CFB_DEV unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+CFB_DEV int ld_volatile_int(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+CFB_DEV float gelu_erf(float x) {   // nn.GELU() default (exact erf form)
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+}  // namespace cfb

@@ -1,0 +1,1429 @@
+// cfb_engine.cu -- the persistent drafting engine of libcfb.so (sm_100a).
+//
+// One cooperative launch runs a whole draft: the flow integrator (both chunk experts, every
+// HiddenKVFlowBlock, every Euler step, cross-K/V hoisted once per draft), then per draft depth
+// the path residual, the markov-bias gather, the shortlist head with online log-sum-exp + top-k
+// (no logits reach HBM) and the beam step. The host side (cfb_plan_build, C++ below) lowers a
+// (drafter, run) pair into a table of phases; the kernel walks the table with a bounded grid
+// barrier between phases.
+//
+// Per CTA: one producer thread streams the packed weight units of every GEMM phase through an
+// 8-stage shared-memory ring with cp.async.bulk (the TMA copy engine, no multicast) and runs
+// ahead across phase boundaries, since weights never depend on activations. 16 consumer warps
+// multiply each unit (64 output features x 128 k) with tensor-core MMAs against fp16 activation
+// fragments read from L2 one unit ahead, reduce across warps in a fixed order, and finish each
+// 64-feature tile with a fused epilogue. Work is split stream-K style: the units of a phase are
+// cut into equal contiguous ranges, one per CTA; a tile shared by two CTAs is completed by
+// whichever arrives last, summing the partials in k order (deterministic, no float atomics).
+//
+// A LayerNorm in front of a linear is folded at pack time (W <- W diag(gamma), b <- b + W beta);
+// the engine feeds the fp16 activation straight into the MMA and applies
+//     y = (acc - mean * colsum(W)) * rstd + b
+// in the epilogue, with the row statistics combined from per-64-column parts that the producing
+// epilogue wrote (Chan's parallel mean/M2 merge, fixed order).
+//
+// Reference behaviour restated (paths relative to the reference checkout):
+//   HiddenKVFlowBlock            src/chain_flow/drafters/chunked_flow.py:168-202
+//   HiddenKVFlowExpert pre/post  src/chain_flow/drafters/chunked_flow.py:333-414
+//   Euler integrate / chunks     src/chain_flow/drafters/tree_flow.py:163-235
+//   path residual                src/chain_flow/drafters/tree_flow.py:434-450
+//   head / bias / map / beams    src/chain_flow/vllm_plugin/flow_proposer.py:1021-1028, 1188-1332
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <cstring>
+#include <cmath>
+#include <cstdio>
+#include <vector>
+#include <algorithm>
+
+#include "cfb_common.cuh"
+#include "../../include/cfb.h"
+
+namespace cfb {
+
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = kConsumerWarps * 32;     // 512
+constexpr int kThreads = kConsumers + 32;           // + 1 producer warp
+constexpr int kTileRows = 64;                       // output features per tile (4 x m16)
+constexpr int kUnitK = 8;                           // 16-wide k blocks per streamed unit
+constexpr int kBlockBytes = 512;                    // one 16x16 fp16 fragment tile
+constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB
+constexpr int kStages = 8;
+constexpr int kRowsMax = 64;                        // activation rows per job
+constexpr int kTopMax = 8;                          // top-k per beam row
+constexpr int kMaxExperts = 4;
+constexpr int kStatCols = 64;                       // columns per row-statistics part
+constexpr int kHeadPartFloats = 2 + 2 * kTopMax;
+constexpr int kSlices = 8;                          // epilogue threads per row
+
+enum XKind : int { XK_F16 = 0, XK_PATH = 1 };
+enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
+enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
+                   EK_HEADIN = 5, EK_HEAD = 6 };
+enum PKind : int { PK_PREP = 0, PK_GEMM = 1 };
+enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2 };
+
+struct AttnTask {
+  const float* q; int ldq, qoff;
+  const float* k; int ldk, koff;
+  const float* v; int ldv, voff;
+  __half* out; int ldo;
+  int rows_per_req, keys_per_req, B, hd, heads, causal, nsec, Dsec;
+  float scale;
+  unsigned* cnt;          // [heads]
+};
+
+struct ExpertRT {
+  float* x32[2]; __half* x16[2]; float2* xstat[2];   // residual stream, by Euler step parity
+  int S; int start;
+  const float* pos; const float* temb;
+};
+
+struct Job {
+  const uint4* w;
+  int Mt, Kt, Kstride, nkc, rows, nout;
+  int unit_base, tile_base;
+  // activation source (fp16 fragments)
+  int xkind;
+  const __half* x; int ldx;
+  int gin, gstride, goff;                  // source row = (r / gin) * gstride + goff + r % gin
+  int ln; const float2* stats; int nparts; const float* colsum;
+  const int64_t* lastp; int order; const __half* emb; int D;   // XK_PATH gather
+  // epilogue
+  int ekind;
+  const float* bias;
+  float* out32; __half* out16; int ldo;
+  float2* ostats; int onparts;
+  int attn;                                // -1 or AttnTask index (trigger after the tile)
+  int e_idx, step, last_step, wrows, nlive, R, topb;
+  float dt;
+  const float* p0;                         // EK_PATHH: offset biases [order][D]
+};
+
+struct Phase {
+  int kind;
+  int job0, njobs, nunits, ntiles;
+  int post;
+  int side_markov;
+  int step, rows, fr, keep, topb, base, base_prev, last;
+};
+
+struct Plan {
+  int G, nphases, mode, B, D, DL, n_experts, chunk, C, steps, order, rank, vocab, R;
+  int width, depth, keep, topb, Wmax, N;
+  const Phase* phases;
+  const Job* jobs;
+  const AttnTask* attn;
+  ExpertRT ex[kMaxExperts];
+  unsigned* bar; unsigned* exitcnt; unsigned* headcnt; int* err;
+  unsigned* tilecnt; int ntilecnt;
+  unsigned* attncnt; int nattncnt;
+  float* gpart;             // [G][2][kTileRows*kRowsMax]
+  float* hpart;             // [G][kRowsMax][kHeadPartFloats]
+  const __half* ctx; const __half* z0; float* pred; float2* ctxstat;
+  const int64_t* known0; int64_t* lastp; float* cum; int64_t* toks; int* bps; int64_t* tokens;
+  const int64_t* shortlist; const __half* markov_w1; __half* xhead; int ldxhead;
+  void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
+};
+
+struct Smem {
+  uint8_t ring[kStages][kUnitBytes];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  float slots[kConsumerWarps * 16 * kRowsMax];     // warp partials; attention / merge scratch
+  float red[kTileRows * kRowsMax];                 // one reduced tile [feature][row]
+  float2 rowstat[kRowsMax];
+  int flag;
+};
+
+struct HeadState { float m, s; float tv[kTopMax]; int ti[kTopMax]; };
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV void set_err(const Plan& P, int code) { atomicCAS(P.err, 0, code); }
+
+CFB_DEV long long cta_start(long long U, int G, int c) { return (long long)c * U / G; }
+CFB_DEV int cta_of(long long u, long long U, int G) {       // the CTA whose range holds unit u
+  return (int)(((u + 1) * G + U - 1) / U - 1);
+}
+// the next CTA after c whose (non-empty) range holds units; CTAs with empty ranges are skipped
+CFB_DEV int next_contributor(int c, long long U, int G) {
+  return cta_of(cta_start(U, G, c + 1), U, G);
+}
+
+// grid barrier over the consumer threads of all CTAs; bounded; false once an error is set
+CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch) {
+  consumer_sync(kConsumers);
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    ++epoch;
+    __threadfence();
+    atom_add_release(P.bar, 1u);
+    const unsigned target = epoch * (unsigned)P.G;
+    int ok = 1;
+    if (ld_acquire(P.bar) < target) {
+      const unsigned long long t0 = globaltimer();
+      while (ld_acquire(P.bar) < target) {
+        if (ld_volatile_int(P.err) != 0) { ok = 0; break; }
+        if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_GRID); ok = 0; break; }
+      }
+    }
+    if (ld_volatile_int(P.err) != 0) ok = 0;
+    s_ok = ok;
+  }
+  consumer_sync(kConsumers);
+  return s_ok != 0;
+}
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV int src_row(const Job& J, int r) { return (r / J.gin) * J.gstride + J.goff + r % J.gin; }
+
+// B fragment (16 k x 8 rows) of k-block kb for n-tile nt: {X[row][2t..2t+1], X[row][2t+8..2t+9]}
+template <int NT>
+CFB_DEV void load_frag(const Job& J, int kb, int lane, uint32_t (&f)[NT][2]) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int r = nt * 8 + g;
+    f[nt][0] = f[nt][1] = 0u;
+    if (r >= J.rows) continue;
+    const int sr = src_row(J, r);
+    const int k = kb * 16 + 2 * t;
+    const __half* p;
+    if (J.xkind == XK_PATH) {
+      const int j = k / J.D, d = k - j * J.D;
+      const int64_t tok = J.lastp[(size_t)sr * J.order + j];
+      if (tok < 0) continue;
+      p = J.emb + (size_t)tok * J.D + d;
+    } else {
+      p = J.x + (size_t)sr * J.ldx + k;
+    }
+    f[nt][0] = *reinterpret_cast<const uint32_t*>(p);
+    f[nt][1] = *reinterpret_cast<const uint32_t*>(p + 8);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV void chan_merge(float& n, float& m, float& M2, float nb, float mb, float M2b) {
+  const float nn = n + nb;
+  if (nn == 0.f) return;
+  const float d = mb - m;
+  const float f = nb / nn;
+  m = m + d * f;
+  M2 = M2 + M2b + d * d * n * f;
+  n = nn;
+}
+
+// Merge (n, mean, M2) across `width` adjacent lanes; the lower lane is always the left operand,
+// so the result does not depend on scheduling.
+CFB_DEV void chan_group(float& n, float& m, float& M2, int width) {
+  const int lane = threadIdx.x & 31;
+  for (int off = 1; off < width; off <<= 1) {
+    const float nb = __shfl_xor_sync(0xffffffffu, n, off);
+    const float mb = __shfl_xor_sync(0xffffffffu, m, off);
+    const float M2b = __shfl_xor_sync(0xffffffffu, M2, off);
+    if (lane & off) { float tn = n, tm = m, tM = M2; n = nb; m = mb; M2 = M2b; chan_merge(n, m, M2, tn, tm, tM); }
+    else chan_merge(n, m, M2, nb, mb, M2b);
+  }
+}
+
+// row LayerNorm statistics of the job's source rows -> S.rowstat[r] = (mean, rstd)
+CFB_DEV void job_rowstats(const Job& J, Smem& S) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (J.ln == LN_PARTS) {
+    for (int r = warp; r < J.rows; r += kConsumerWarps) {
+      const int sr = src_row(J, r);
+      float n = 0.f, m = 0.f, M2 = 0.f;
+      for (int p = lane; p < J.nparts; p += 32) {
+        const float2 st = __ldcg(J.stats + (size_t)sr * J.nparts + p);
+        chan_merge(n, m, M2, (float)kStatCols, st.x, st.y);
+      }
+      chan_group(n, m, M2, 32);
+      if (lane == 0) S.rowstat[r] = make_float2(m, rsqrtf(M2 / n + 1e-5f));
+    }
+  } else if (J.ln == LN_DIRECT) {
+    for (int r = tid; r < J.rows; r += kConsumers) S.rowstat[r] = __ldcg(J.stats + src_row(J, r));
+  } else {
+    for (int r = tid; r < J.rows; r += kConsumers) S.rowstat[r] = make_float2(0.f, 1.f);
+  }
+  consumer_sync(kConsumers);
+}
+
+CFB_DEV float epi_val(const Job& J, const Smem& S, int f, int r, int col) {
+  const float2 rs = S.rowstat[r];
+  const float cs = J.colsum ? J.colsum[col] : 0.f;
+  return (S.red[f * kRowsMax + r] - rs.x * cs) * rs.y + (J.bias ? J.bias[col] : 0.f);
+}
+
+// ------------------------------------------------------------------------------------------
+// attention of one head, run by the CTA that completes the last tile of that head's columns
+CFB_DEV void run_attention(const AttnTask& A, int h, Smem& S) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Sq = A.rows_per_req, Kn = A.keys_per_req, hd = A.hd;
+  float* qs = S.slots;
+  float* ks = qs + Sq * hd;
+  float* vs = ks + Kn * hd;
+  float* sc = vs + Kn * hd;
+  for (int b = 0; b < A.B; ++b) {
+    for (int e = tid; e < Sq * hd; e += kConsumers) {
+      const int i = e / hd, d = e - i * hd;
+      qs[e] = __ldcg(A.q + (size_t)(b * Sq + i) * A.ldq + A.qoff + h * hd + d);
+    }
+    for (int e = tid; e < Kn * hd; e += kConsumers) {
+      const int j = e / hd, d = e - j * hd;
+      ks[e] = __ldcg(A.k + (size_t)(b * Kn + j) * A.ldk + A.koff + h * hd + d);
+      vs[e] = __ldcg(A.v + (size_t)(b * Kn + j) * A.ldv + A.voff + h * hd + d);
+    }
+    consumer_sync(kConsumers);
+    for (int pr = warp; pr < Sq * Kn; pr += kConsumerWarps) {
+      const int i = pr / Kn, j = pr - i * Kn;
+      float s = 0.f;
+      for (int d = lane; d < hd; d += 32) s += qs[i * hd + d] * ks[j * hd + d];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      if (lane == 0) sc[pr] = (A.causal && j > i) ? -INFINITY : s * A.scale;
+    }
+    consumer_sync(kConsumers);
+    if (tid < Sq) {
+      float mx = -INFINITY;
+      for (int j = 0; j < Kn; ++j) mx = fmaxf(mx, sc[tid * Kn + j]);
+      float sum = 0.f;
+      for (int j = 0; j < Kn; ++j) { const float e = __expf(sc[tid * Kn + j] - mx); sc[tid * Kn + j] = e; sum += e; }
+      const float inv = 1.f / sum;
+      for (int j = 0; j < Kn; ++j) sc[tid * Kn + j] *= inv;
+    }
+    consumer_sync(kConsumers);
+    for (int e = tid; e < Sq * hd; e += kConsumers) {
+      const int i = e / hd, d = e - i * hd;
+      float o = 0.f;
+      for (int j = 0; j < Kn; ++j) o += sc[i * Kn + j] * vs[j * hd + d];
+      A.out[(size_t)(b * Sq + i) * A.ldo + h * hd + d] = __float2half_rn(o);
+    }
+    consumer_sync(kConsumers);
+  }
+}
+
+CFB_DEV void attn_trigger(const Plan& P, const Job& J, int tile, Smem& S) {
+  const AttnTask& A = P.attn[J.attn];
+  const int c0 = (tile * kTileRows) % A.Dsec;
+  const int h0 = c0 / A.hd, h1 = min((c0 + kTileRows - 1) / A.hd, A.heads - 1);
+  for (int h = h0; h <= h1; ++h) {
+    if (threadIdx.x == 0) {
+      const unsigned expect = (unsigned)A.nsec *
+          (unsigned)(((h + 1) * A.hd - 1) / kTileRows - (h * A.hd) / kTileRows + 1);
+      const unsigned old = atom_add_acqrel(A.cnt + h, 1u);
+      S.flag = (old + 1 == expect);
+      if (old + 1 == expect) A.cnt[h] = 0u;
+    }
+    consumer_sync(kConsumers);
+    const int go = S.flag;
+    consumer_sync(kConsumers);
+    if (go) { __threadfence(); run_attention(A, h, S); }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV bool better(float v, int i, float w, int j) { return v > w || (v == w && i < j); }
+
+// static-index insertion into a descending top list (stays in registers)
+CFB_DEV void top_insert(HeadState& H, int K, float v, int id) {
+#pragma unroll
+  for (int i = 0; i < kTopMax; ++i) {
+    if (i < K && better(v, id, H.tv[i], H.ti[i])) {
+      const float tv = H.tv[i]; const int ti = H.ti[i];
+      H.tv[i] = v; H.ti[i] = id; v = tv; id = ti;
+    }
+  }
+}
+
+CFB_DEV void head_reset(HeadState& H) {
+  H.m = -INFINITY; H.s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kTopMax; ++i) { H.tv[i] = -INFINITY; H.ti[i] = 0x7fffffff; }
+}
+
+CFB_DEV void head_merge(HeadState& A, const HeadState& B, int K) {
+  const float M = fmaxf(A.m, B.m);
+  A.s = (M == -INFINITY) ? 0.f : A.s * __expf(A.m - M) + B.s * __expf(B.m - M);
+  A.m = M;
+#pragma unroll
+  for (int i = 0; i < kTopMax; ++i) if (i < K) top_insert(A, K, B.tv[i], B.ti[i]);
+}
+
+// merge across `width` adjacent lanes, lower lane on the left
+CFB_DEV void head_group(HeadState& H, int K, int width) {
+  const int lane = threadIdx.x & 31;
+  for (int off = 1; off < width; off <<= 1) {
+    HeadState O;
+    O.m = __shfl_xor_sync(0xffffffffu, H.m, off);
+    O.s = __shfl_xor_sync(0xffffffffu, H.s, off);
+#pragma unroll
+    for (int i = 0; i < kTopMax; ++i) {
+      O.tv[i] = __shfl_xor_sync(0xffffffffu, H.tv[i], off);
+      O.ti[i] = __shfl_xor_sync(0xffffffffu, H.ti[i], off);
+    }
+    if (lane & off) { HeadState T = H; H = O; head_merge(H, T, K); }
+    else head_merge(H, O, K);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadState& H) {
+  const int tid = threadIdx.x;
+  const int rows = J.rows;
+  const int col0 = tile * kTileRows;
+  switch (J.ekind) {
+    case EK_STORE:
+    case EK_GELU16:
+    case EK_HEADIN: {
+      for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+        const int f = e / rows, r = e - f * rows;
+        const int col = col0 + f;
+        if (col >= J.nout) continue;
+        const float v = epi_val(J, S, f, r, col);
+        if (J.ekind == EK_STORE) J.out32[(size_t)r * J.ldo + col] = v;
+        else if (J.ekind == EK_GELU16) J.out16[(size_t)r * J.ldo + col] = __float2half_rn(gelu_erf(v));
+        else {
+          const int b = r / J.wrows;
+          J.out16[(size_t)r * J.ldo + col] =
+              __float2half_rn(v + P.pred[((size_t)b * P.DL + J.step) * P.D + col]);
+        }
+      }
+      break;
+    }
+    case EK_RESID:
+    case EK_PATHH: {
+      // thread (r, q): 8 consecutive columns of row r, statistics merged over the 8 slices
+      const int r = tid / kSlices, q = tid % kSlices;
+      if (r < ((rows + 3) / 4) * 4) {          // whole 32-lane groups enter the shuffles
+        float n = 0.f, m = 0.f, M2 = 0.f;
+        if (r < rows) {
+          for (int f = q * 8; f < q * 8 + 8; ++f) {
+            const int col = col0 + f;
+            float v = epi_val(J, S, f, r, col);
+            if (J.ekind == EK_RESID) {
+              v += J.out32[(size_t)r * J.ldo + col];
+              J.out32[(size_t)r * J.ldo + col] = v;
+            } else {
+              for (int j = 0; j < J.nlive; ++j)
+                if (J.lastp[(size_t)r * J.order + j] >= 0) v += J.p0[(size_t)j * J.D + col];
+            }
+            J.out16[(size_t)r * J.ldo + col] = __float2half_rn(v);
+            n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
+          }
+        }
+        chan_group(n, m, M2, kSlices);
+        if (q == 0 && r < rows) J.ostats[(size_t)r * J.onparts + tile] = make_float2(m, M2);
+      }
+      break;
+    }
+    case EK_EULER: {
+      const int r = tid / kSlices, q = tid % kSlices;
+      if (r < ((rows + 3) / 4) * 4) {
+        float n[kMaxExperts], m[kMaxExperts], M2[kMaxExperts];
+#pragma unroll
+        for (int e = 0; e < kMaxExperts; ++e) { n[e] = 0.f; m[e] = 0.f; M2[e] = 0.f; }
+        const int b = r / P.chunk, c = r - b * P.chunk;
+        const ExpertRT& E = P.ex[J.e_idx];
+        const int pos = E.start + c;
+        const int nx = (J.step + 1) & 1;
+        if (r < rows) {
+          for (int f = q * 8; f < q * 8 + 8; ++f) {
+            const int col = col0 + f;
+            const float v = epi_val(J, S, f, r, col);
+            float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col;
+            const float z = *zp + J.dt * v;
+            *zp = z;
+            if (!J.last_step) {
+#pragma unroll
+              for (int e = 0; e < kMaxExperts; ++e) {
+                if (e >= P.n_experts) break;
+                const ExpertRT& X = P.ex[e];
+                if (pos >= X.S) continue;
+                float xv = z + X.pos[(size_t)pos * P.D + col];
+                if (pos >= X.start) xv += X.temb[(size_t)(J.step + 1) * P.D + col];
+                const size_t xi = ((size_t)b * X.S + pos) * P.D + col;
+                X.x32[nx][xi] = xv;
+                X.x16[nx][xi] = __float2half_rn(xv);
+                n[e] += 1.f; const float d = xv - m[e]; m[e] += d / n[e]; M2[e] += d * (xv - m[e]);
+              }
+            }
+          }
+        }
+        if (!J.last_step) {
+#pragma unroll
+          for (int e = 0; e < kMaxExperts; ++e) {
+            if (e >= P.n_experts) break;
+            chan_group(n[e], m[e], M2[e], kSlices);
+            const ExpertRT& X = P.ex[e];
+            if (q == 0 && r < rows && pos < X.S)
+              X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m[e], M2[e]);
+          }
+        }
+      }
+      break;
+    }
+    case EK_HEAD: {
+      const int r = tid / kSlices, q = tid % kSlices;
+      if (r < rows) {
+        for (int f = q * 8; f < q * 8 + 8; ++f) {
+          const int j = col0 + f;
+          if (j >= J.R) break;
+          const float v = S.red[f * kRowsMax + r];
+          if (v > H.m) { H.s = H.s * __expf(H.m - v) + 1.f; H.m = v; }
+          else H.s += __expf(v - H.m);
+          top_insert(H, J.topb, v, j);
+        }
+      }
+      break;
+    }
+  }
+  __threadfence();
+  consumer_sync(kConsumers);
+  if (J.attn >= 0) attn_trigger(P, J, tile, S);
+}
+
+// ------------------------------------------------------------------------------------------
+// reduce the 16 warps' partials of one tile, then finish it (directly, or through the fixup)
+template <int NT>
+CFB_DEV void tile_end(const Plan& P, const Job& J, int tile, bool complete, long long U,
+                      long long ug_first, float (&acc)[NT][4], Smem& S, HeadState& H) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int RP = NT * 8;
+  float* sl = S.slots + warp * 16 * RP;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int r0 = nt * 8 + 2 * t;
+    sl[g * RP + r0] = acc[nt][0];
+    sl[g * RP + r0 + 1] = acc[nt][1];
+    sl[(g + 8) * RP + r0] = acc[nt][2];
+    sl[(g + 8) * RP + r0 + 1] = acc[nt][3];
+    acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  }
+  consumer_sync(kConsumers);
+  const int rows = J.rows;
+  // feature f = 16 i + ff comes from warps i, i+4, i+8, i+12 (one per k slice), summed in order
+  for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+    const int f = e / rows, r = e - f * rows;
+    const int i = f >> 4, ff = f & 15;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) s += S.slots[((i + 4 * w) * 16 + ff) * RP + r];
+    S.red[f * kRowsMax + r] = s;
+  }
+  consumer_sync(kConsumers);
+  if (!complete) {
+    // contributors: the CTAs whose ranges hold this tile's units, in k order; when a phase has
+    // fewer units than CTAs, CTAs with empty ranges sit between them and are not counted
+    const int c = blockIdx.x;
+    const long long ug_last = ug_first + J.nkc - 1;
+    const int c_first = cta_of(ug_first, U, P.G);
+    int ncontrib = 0;
+    for (int cc = c_first; cc < P.G && cta_start(U, P.G, cc) <= ug_last; cc = next_contributor(cc, U, P.G))
+      ++ncontrib;
+    const int slot = (cta_start(U, P.G, c) >= ug_first) ? 0 : 1;
+    float* mine = P.gpart + ((size_t)c * 2 + slot) * (kTileRows * kRowsMax);
+    for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+      const int f = e / rows, r = e - f * rows;
+      __stcg(mine + f * kRowsMax + r, S.red[f * kRowsMax + r]);
+    }
+    __threadfence();
+    consumer_sync(kConsumers);
+    if (tid == 0) {
+      unsigned* cnt = P.tilecnt + J.tile_base + tile;
+      const unsigned old = atom_add_acqrel(cnt, 1u);
+      const bool last = (old + 1 == (unsigned)ncontrib);
+      if (last) *cnt = 0u;
+      S.flag = last;
+    }
+    consumer_sync(kConsumers);
+    const bool last = S.flag;
+    consumer_sync(kConsumers);
+    if (!last) return;
+    __threadfence();
+    for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+      const int f = e / rows, r = e - f * rows;
+      float s = 0.f;
+      for (int cc = c_first; cc < P.G && cta_start(U, P.G, cc) <= ug_last; cc = next_contributor(cc, U, P.G)) {
+        const int sl2 = (cta_start(U, P.G, cc) >= ug_first) ? 0 : 1;
+        s += __ldcg(P.gpart + ((size_t)cc * 2 + sl2) * (kTileRows * kRowsMax) + f * kRowsMax + r);
+      }
+      S.red[f * kRowsMax + r] = s;
+    }
+    consumer_sync(kConsumers);
+  }
+  tile_epilogue(P, J, tile, S, H);
+}
+
+// ------------------------------------------------------------------------------------------
+template <int NT>
+CFB_DEV void gemm_job(const Plan& P, const Job& J, long long U, int ju0, int ju1, uint32_t& ci,
+                      Smem& S, HeadState& H) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice of a unit
+  job_rowstats(J, S);
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  uint32_t nx[2][NT][2];
+  auto prefetch = [&](int ju) {
+    const int kc = ju % J.nkc;
+    const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int blk = ks + 4 * i;
+      if (blk < nkb) load_frag<NT>(J, kc * kUnitK + blk, lane, nx[i]);
+    }
+  };
+  prefetch(ju0);
+  for (int ju = ju0; ju < ju1; ++ju) {
+    const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
+    const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
+    uint32_t cx[2][NT][2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) { cx[i][nt][0] = nx[i][nt][0]; cx[i][nt][1] = nx[i][nt][1]; }
+    if (ju + 1 < ju1) prefetch(ju + 1);
+    const int stage = ci % kStages;
+    if (!mbar_wait(&S.full[stage], (ci / kStages) & 1, P.err)) set_err(P, DEV_TIMEOUT_FULL);
+    const uint8_t* st = S.ring[stage];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int blk = ks + 4 * i;
+      if (blk < nkb) {
+        const uint4 a = *reinterpret_cast<const uint4*>(st + (blk * 4 + mi) * kBlockBytes + lane * 16);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a, cx[i][nt][0], cx[i][nt][1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.empty[stage]);
+    ++ci;
+    if (kc == J.nkc - 1 || ju == ju1 - 1) {
+      const bool complete = (ju0 <= tile * J.nkc) && (ju1 >= (tile + 1) * J.nkc);
+      tile_end<NT>(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, acc, S, H);
+    }
+  }
+}
+
+CFB_DEV void gemm_phase(const Plan& P, const Phase& ph, uint32_t& ci, Smem& S, HeadState& H) {
+  const long long U = ph.nunits;
+  const long long u0 = cta_start(U, P.G, blockIdx.x), u1 = cta_start(U, P.G, blockIdx.x + 1);
+  for (int jx = 0; jx < ph.njobs; ++jx) {
+    const Job& J = P.jobs[ph.job0 + jx];
+    const long long jb = J.unit_base, je = jb + (long long)J.Mt * J.nkc;
+    const long long a = max(u0, jb), b = min(u1, je);
+    if (a >= b) continue;
+    const int ju0 = (int)(a - jb), ju1 = (int)(b - jb);
+    switch ((J.rows + 7) / 8) {
+      case 1: gemm_job<1>(P, J, U, ju0, ju1, ci, S, H); break;
+      case 2: gemm_job<2>(P, J, U, ju0, ju1, ci, S, H); break;
+      case 3: case 4: gemm_job<4>(P, J, U, ju0, ju1, ci, S, H); break;
+      default: gemm_job<8>(P, J, U, ju0, ju1, ci, S, H); break;
+    }
+  }
+}
+
+// producer: stream this CTA's units of every GEMM phase, running ahead of the consumers
+CFB_DEV void producer(const Plan& P, Smem& S) {
+  uint32_t pi = 0;
+  bool ok = true;
+  for (int p = 0; p < P.nphases && ok; ++p) {
+    const Phase& ph = P.phases[p];
+    if (ph.kind != PK_GEMM) continue;
+    const long long U = ph.nunits;
+    const long long u0 = cta_start(U, P.G, blockIdx.x), u1 = cta_start(U, P.G, blockIdx.x + 1);
+    for (int jx = 0; jx < ph.njobs && ok; ++jx) {
+      const Job& J = P.jobs[ph.job0 + jx];
+      const long long jb = J.unit_base, je = jb + (long long)J.Mt * J.nkc;
+      const long long a = max(u0, jb), b = min(u1, je);
+      for (long long u = a; u < b; ++u) {
+        const int ju = (int)(u - jb);
+        const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
+        const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(J.w) +
+            ((size_t)tile * J.Kstride + (size_t)kc * kUnitK) * 4 * kBlockBytes;
+        const uint32_t bytes = (uint32_t)(nkb * 4 * kBlockBytes);
+        const int stage = pi % kStages;
+        if (!mbar_wait(&S.empty[stage], ((pi / kStages) & 1) ^ 1, P.err)) {
+          set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
+        }
+        mbar_arrive_expect_tx(&S.full[stage], bytes);
+        bulk_g2s(S.ring[stage], src, bytes, &S.full[stage]);
+        ++pi;
+      }
+    }
+  }
+  // every issued copy must land before this CTA may exit (copies complete on their own)
+  const uint32_t first = pi > (uint32_t)kStages ? pi - kStages : 0u;
+  for (uint32_t i = first; i < pi; ++i) mbar_wait(&S.full[i % kStages], (i / kStages) & 1);
+}
+
+// ------------------------------------------------------------------------------------------
+CFB_DEV void prep_phase(const Plan& P) {
+  const int tid = threadIdx.x;
+  const long long gtid = (long long)blockIdx.x * kConsumers + tid;
+  const long long gthreads = (long long)P.G * kConsumers;
+  for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
+  for (long long i = gtid; i < P.nattncnt; i += gthreads) P.attncnt[i] = 0u;
+  if (gtid == 0) *P.headcnt = 0u;
+  const bool flow = (P.mode == CFB_MODE_FLOW || P.mode == CFB_MODE_CHAIN || P.mode == CFB_MODE_TREE);
+  const int D = P.D, nparts = D / kStatCols;
+  if (flow) {
+    const long long nz = (long long)P.B * P.DL * D;
+    for (long long i = gtid; i < nz; i += gthreads) P.pred[i] = __half2float(P.z0[i]);
+    // step-0 inputs of every expert: z0 + position embedding (+ time embedding on its chunk)
+    for (int e = 0; e < P.n_experts; ++e) {
+      const ExpertRT& X = P.ex[e];
+      const long long items = (long long)P.B * X.S * nparts;
+      for (long long it = gtid; it < items; it += gthreads) {
+        const int part = (int)(it % nparts);
+        const long long row = it / nparts;
+        const int b = (int)(row / X.S), pos = (int)(row % X.S);
+        float n = 0.f, m = 0.f, M2 = 0.f;
+        for (int f = 0; f < kStatCols; ++f) {
+          const int col = part * kStatCols + f;
+          float v = __half2float(P.z0[((size_t)b * P.DL + pos) * D + col]) + X.pos[(size_t)pos * D + col];
+          if (pos >= X.start) v += X.temb[col];
+          X.x32[0][(size_t)row * D + col] = v;
+          X.x16[0][(size_t)row * D + col] = __float2half_rn(v);
+          n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
+        }
+        X.xstat[0][(size_t)row * nparts + part] = make_float2(m, M2);
+      }
+    }
+    // context LayerNorm statistics (two-pass), one warp per row
+    const int lane = tid & 31;
+    const long long gw = gtid >> 5, nw = gthreads >> 5;
+    const long long crows = (long long)P.B * P.C;
+    for (long long r = gw; r < crows; r += nw) {
+      float s = 0.f;
+      for (int c = lane; c < D; c += 32) s += __half2float(P.ctx[r * D + c]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      const float mean = s / D;
+      float q = 0.f;
+      for (int c = lane; c < D; c += 32) { const float d = __half2float(P.ctx[r * D + c]) - mean; q += d * d; }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+      if (lane == 0) P.ctxstat[r] = make_float2(mean, rsqrtf(q / D + 1e-5f));
+    }
+  }
+  if (P.mode != CFB_MODE_FLOW) {
+    // chain: W beams per request (rows b*W + w), cum = [0, -inf, ...] (flow_proposer.py:1220-1224)
+    // tree: a one-node frontier per request (row b), cum = 0 (flow_proposer.py:1289-1292)
+    const bool treem = (P.mode == CFB_MODE_TREE || P.mode == CFB_MODE_BEAM_TREE);
+    const int Wm = P.Wmax, per = treem ? 1 : Wm;
+    for (long long i = gtid; i < (long long)P.B * per; i += gthreads) {
+      const int b = (int)(i / per);
+      for (int j = 0; j < P.order; ++j) P.lastp[i * P.order + j] = (j == 0) ? P.known0[b] : -1;
+    }
+    for (long long i = gtid; i < (long long)P.B * Wm; i += gthreads)
+      P.cum[i] = (i % Wm == 0) ? 0.f : -INFINITY;
+  }
+}
+
+// markov bias rows of the head input: xhead[r, D + j] = w1[lastp[r, 0], j]
+CFB_DEV void markov_side(const Plan& P, const Phase& ph) {
+  const long long gtid = (long long)blockIdx.x * kConsumers + threadIdx.x;
+  const long long gthreads = (long long)P.G * kConsumers;
+  const long long n = (long long)ph.rows * P.rank;
+  for (long long i = gtid; i < n; i += gthreads) {
+    const int r = (int)(i / P.rank), j = (int)(i % P.rank);
+    const int64_t tok = P.lastp[(size_t)r * P.order];
+    P.xhead[(size_t)r * P.ldxhead + P.D + j] = P.markov_w1[(size_t)tok * P.rank + j];
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// after the head GEMM: every CTA publishes (max, sumexp, top-k) per beam row; the last CTA to
+// arrive merges them in CTA order, finishes the log-softmax and takes the beam step
+CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rows = ph.rows, TB = ph.topb;
+  {
+    const int r = tid / kSlices, q = tid % kSlices;
+    if (r < ((rows + 3) / 4) * 4) {
+      head_group(H, TB, kSlices);
+      if (q == 0 && r < rows) {
+        float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + r) * kHeadPartFloats;
+        __stcg(hp + 0, H.m); __stcg(hp + 1, H.s);
+#pragma unroll
+        for (int i = 0; i < kTopMax; ++i) { __stcg(hp + 2 + i, H.tv[i]); __stcg(hp + 2 + kTopMax + i, __int_as_float(H.ti[i])); }
+      }
+    }
+  }
+  __threadfence();
+  consumer_sync(kConsumers);
+  if (tid == 0) {
+    const unsigned old = atom_add_acqrel(P.headcnt, 1u);
+    S.flag = (old + 1 == (unsigned)P.G);
+    if (old + 1 == (unsigned)P.G) *P.headcnt = 0u;
+  }
+  consumer_sync(kConsumers);
+  const bool last = S.flag;
+  consumer_sync(kConsumers);
+  if (!last) return;
+  __threadfence();
+  float* lp = S.red;                                  // [rows][kTopMax] log-probs
+  int* lid = reinterpret_cast<int*>(S.slots);         // [rows][kTopMax] shortlist-local ids
+  for (int r = warp; r < rows; r += kConsumerWarps) {
+    HeadState A; head_reset(A);
+    for (int c = lane; c < P.G; c += 32) {
+      const float* hp = P.hpart + ((size_t)c * kRowsMax + r) * kHeadPartFloats;
+      HeadState B;
+      B.m = __ldcg(hp); B.s = __ldcg(hp + 1);
+#pragma unroll
+      for (int i = 0; i < kTopMax; ++i) { B.tv[i] = __ldcg(hp + 2 + i); B.ti[i] = __float_as_int(__ldcg(hp + 2 + kTopMax + i)); }
+      head_merge(A, B, TB);
+    }
+    head_group(A, TB, 32);
+    if (lane == 0) {
+      const bool okrow = (A.s > 0.f) && isfinite(A.m) && isfinite(A.s);
+      const float lse = okrow ? A.m + logf(A.s) : 0.f;
+#pragma unroll
+      for (int i = 0; i < kTopMax; ++i)
+        if (i < TB) {
+          const bool ok = okrow && A.ti[i] >= 0 && A.ti[i] < P.R && !isnan(A.tv[i]);
+          lp[r * kTopMax + i] = ok ? A.tv[i] - lse : -INFINITY;
+          lid[r * kTopMax + i] = ok ? A.ti[i] : 0;
+        }
+    }
+  }
+  consumer_sync(kConsumers);
+  // beam step, one thread per request: pick the survivors, then (after every thread has read
+  // its old rows) write the new frontier; the tree frontier changes width, so rows move
+  const int step = ph.step;
+  const int order = P.order;
+  const bool treem = (ph.post == PO_BEAM_TREE);
+  const int fr = treem ? ph.fr : P.width;
+  const int TB2 = treem ? ph.topb : P.width;
+  const int k = treem ? min(ph.keep, fr * TB2) : P.width;
+  HeadState C; head_reset(C);       // candidates: tv = cumulative log-prob, ti = w * TB2 + i
+  int64_t old[kTopMax][8];
+  const int b = tid;
+  if (b < P.B) {
+    for (int w = 0; w < fr; ++w)
+      for (int i = 0; i < TB2; ++i)
+        top_insert(C, k, P.cum[b * P.Wmax + w] + lp[(b * fr + w) * kTopMax + i], w * TB2 + i);
+    for (int w = 0; w < fr; ++w)
+      for (int j = 0; j < order; ++j) old[w][j] = P.lastp[((size_t)b * fr + w) * order + j];
+  }
+  consumer_sync(kConsumers);
+  if (b < P.B) {
+#pragma unroll
+    for (int i = 0; i < kTopMax; ++i) {
+      if (i >= k) break;
+      // candidate ids are < fr * TB2 by construction; clamp anyway so that no value read back
+      // from memory can ever become an out-of-range index
+      const int cid = min(max(C.ti[i], 0), fr * TB2 - 1);
+      const int src = cid / TB2, ii = cid % TB2;
+      const int loc = lid[(b * fr + src) * kTopMax + ii];
+      const int64_t tok = (loc >= 0 && loc < P.R) ? P.shortlist[loc] : (int64_t)0;
+      P.cum[b * P.Wmax + i] = C.tv[i];
+      int64_t* lpn = P.lastp + ((size_t)b * k + i) * order;
+      lpn[0] = tok;
+      for (int j = 1; j < order; ++j) lpn[j] = old[src][j - 1];
+      if (treem) {
+        P.tokens[(size_t)b * 2 * P.N + ph.base + i] = tok;
+        P.tokens[(size_t)b * 2 * P.N + P.N + ph.base + i] =
+            (step == 1) ? (int64_t)-1 : (int64_t)(ph.base_prev + src);
+      } else {
+        P.toks[((size_t)(step - 1) * P.B + b) * P.width + i] = tok;
+        P.bps[((size_t)(step - 1) * P.B + b) * P.width + i] = src;
+      }
+    }
+    if (!treem && ph.last) {
+      // walk the best beam back (flow_proposer.py:1261-1267); argmax keeps the first maximum
+      const int W = P.width;
+      int idx = 0;
+      for (int i = 1; i < W; ++i) if (P.cum[b * W + i] > P.cum[b * W + idx]) idx = i;
+      for (int s2 = step; s2 >= 1; --s2) {
+        P.tokens[(size_t)b * P.depth + (s2 - 1)] = P.toks[((size_t)(s2 - 1) * P.B + b) * W + idx];
+        idx = P.bps[((size_t)(s2 - 1) * P.B + b) * W + idx];
+      }
+    }
+  }
+  __threadfence();
+  consumer_sync(kConsumers);
+}
+
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+  const Plan& P = *Pp;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kConsumerWarps); }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid >= kConsumers) {
+    if (tid == kConsumers) producer(P, S);
+    return;
+  }
+  uint32_t ci = 0;
+  unsigned epoch = 0;
+  bool ok = true;
+  HeadState H;
+  head_reset(H);
+  for (int p = 0; p < P.nphases && ok; ++p) {
+    const Phase& ph = P.phases[p];
+    if (ph.kind == PK_PREP) {
+      prep_phase(P);
+    } else {
+      if (ph.side_markov) markov_side(P, ph);
+      if (ph.post != PO_NONE) head_reset(H);
+      gemm_phase(P, ph, ci, S, H);
+      if (ph.post != PO_NONE) head_post(P, ph, S, H);
+    }
+    ok = grid_sync(P, epoch);
+  }
+  if (tid == 0) {
+    __threadfence();
+    const unsigned old = atomicAdd(P.exitcnt, 1u);
+    if (old + 1 == (unsigned)P.G) { *P.bar = 0u; *P.exitcnt = 0u; __threadfence(); }
+  }
+}
+
+}  // namespace cfb
+
+// ============================================================================================
+// host side: lowering a (drafter, run) pair to the phase table
+// ============================================================================================
+namespace {
+
+thread_local char g_cuda_err[256] = "";
+
+cfb_status cuda_fail(cudaError_t e, const char* what) {
+  snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", what, cudaGetErrorString(e));
+  return CFB_ERR_CUDA;
+}
+
+}  // namespace
+
+cfb_status cfb_launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CFB_OK : cuda_fail(e, what);
+}
+
+namespace {
+
+struct Arena {
+  size_t off = 0;
+  size_t take(size_t bytes, size_t align = 256) {
+    off = (off + align - 1) / align * align;
+    const size_t o = off;
+    off += bytes;
+    return o;
+  }
+};
+
+// fixed offsets at the start of every workspace: plan record, then the 64-byte barrier block
+// (bar, exitcnt, headcnt, err; launch record at +32)
+constexpr size_t kOffPlan = 0;
+size_t off_barrier() { Arena A; A.take(sizeof(cfb::Plan)); return A.take(64); }
+
+struct Builder {
+  const cfb_drafter* d;
+  const cfb_run* r;
+  uint8_t* base;                 // device base (pointer arithmetic only)
+  Arena A;
+  std::vector<cfb::Phase> phases;
+  std::vector<cfb::Job> jobs;
+  std::vector<cfb::AttnTask> attn;
+  cfb::Plan P{};
+  size_t off_phases = 0, off_jobs = 0, off_attn = 0;
+  int max_tiles = 0;
+  template <class T> T* dptr(size_t off) { return reinterpret_cast<T*>(base + off); }
+};
+
+bool lin_ok(const cfb_linear& l, int nout, int k) {
+  return l.w && l.nout == nout && l.k == k && (k % 16) == 0 &&
+         (reinterpret_cast<uintptr_t>(l.w) % 16) == 0;
+}
+
+cfb::Job make_job(const cfb_linear& L, int rows) {
+  cfb::Job J{};
+  J.w = static_cast<const uint4*>(L.w);
+  J.Mt = (L.nout + cfb::kTileRows - 1) / cfb::kTileRows;
+  J.Kt = L.k / 16;
+  J.Kstride = L.k / 16;
+  J.nkc = (J.Kt + cfb::kUnitK - 1) / cfb::kUnitK;
+  J.rows = rows;
+  J.nout = L.nout;
+  J.gin = rows > 0 ? rows : 1; J.gstride = 0; J.goff = 0;
+  J.bias = L.bias;
+  J.colsum = L.colsum;
+  J.attn = -1;
+  return J;
+}
+
+void add_phase(Builder& B, cfb::Phase ph, const std::vector<cfb::Job>& js) {
+  ph.kind = cfb::PK_GEMM;
+  ph.job0 = (int)B.jobs.size();
+  ph.njobs = (int)js.size();
+  long long u = 0; int t = 0;
+  for (auto j : js) {
+    j.unit_base = (int)u; j.tile_base = t;
+    u += (long long)j.Mt * j.nkc; t += j.Mt;
+    B.jobs.push_back(j);
+  }
+  ph.nunits = (int)u; ph.ntiles = t;
+  B.max_tiles = std::max(B.max_tiles, t);
+  B.phases.push_back(ph);
+}
+
+cfb_status lower(Builder& B, size_t* bytes) {
+  const cfb_drafter& d = *B.d;
+  const cfb_run& r = *B.r;
+  const int D = d.hidden, Bq = r.batch, C = d.ctx_rows, DL = d.draft_len, E = d.n_experts;
+  const int mode = r.mode;
+  if (mode < CFB_MODE_FLOW || mode > CFB_MODE_BEAM_TREE) return CFB_ERR_INVALID_ARG;
+  const bool flow = mode == CFB_MODE_FLOW || mode == CFB_MODE_CHAIN || mode == CFB_MODE_TREE;
+  const bool beam = mode != CFB_MODE_FLOW;
+  const bool tree = mode == CFB_MODE_TREE || mode == CFB_MODE_BEAM_TREE;
+  if (D <= 0 || D % cfb::kStatCols || Bq <= 0) return CFB_ERR_UNSUPPORTED;
+  if (E <= 0 || E > cfb::kMaxExperts || d.chunk <= 0 || E * d.chunk != DL) return CFB_ERR_UNSUPPORTED;
+  if (!r.pred) return CFB_ERR_INVALID_ARG;
+  if (flow) {
+    if (!r.ctx || !r.z0 || !d.experts || d.heads <= 0 || D % d.heads || d.layers <= 0 || d.steps <= 0)
+      return CFB_ERR_INVALID_ARG;
+    if (Bq * DL > cfb::kRowsMax || Bq * C > cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
+    const int hd = D / d.heads, Kmax = std::max(DL, C);
+    if ((DL + 2 * Kmax) * hd + DL * Kmax > cfb::kConsumerWarps * 16 * cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
+  }
+  int Wmax = 0, K = 0;
+  if (beam) {
+    if (!r.known0 || !r.tokens || !d.shortlist || !d.embed || !d.markov_w1) return CFB_ERR_INVALID_ARG;
+    if (d.path_order < 1 || d.path_order > 8 || d.markov_rank <= 0 || d.markov_rank % 16) return CFB_ERR_UNSUPPORTED;
+    if (tree) {
+      if (r.tree_keep < 1 || r.tree_topb < 1 || r.tree_topb > cfb::kTopMax || r.tree_keep > cfb::kTopMax)
+        return CFB_ERR_UNSUPPORTED;
+      Wmax = r.tree_keep;
+    } else {
+      if (r.width < 1 || r.width > cfb::kTopMax) return CFB_ERR_UNSUPPORTED;
+      Wmax = r.width;
+    }
+    K = std::min(r.depth, DL - 1);
+    if (K < 1 || (!tree && K != r.depth)) return CFB_ERR_UNSUPPORTED;
+    if (Bq * Wmax > cfb::kRowsMax || Bq > cfb::kConsumers) return CFB_ERR_UNSUPPORTED;
+    if (!lin_ok(d.head, d.shortlist_rows, D + d.markov_rank)) return CFB_ERR_INVALID_ARG;
+    if (!lin_ok(d.path_offsets, D, d.path_order * D) || !lin_ok(d.path_up, d.path_up.nout, D) ||
+        !lin_ok(d.path_down, D, d.path_up.nout) || !d.path_offset_bias || !d.path_down.bias ||
+        d.path_up.nout % 16)
+      return CFB_ERR_INVALID_ARG;
+  }
+  int G = r.grid;
+  if (G <= 0) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+      sms = 148;
+    G = sms;
+  }
+
+  Arena& A = B.A;
+  A.off = 0;
+  A.take(sizeof(cfb::Plan));
+  const size_t o_bar = A.take(64);
+  const int nparts = D / cfb::kStatCols;
+  std::vector<size_t> o_x32(2 * E), o_x16(2 * E), o_xs(2 * E), o_qkv(E), o_o(E), o_qc(E), o_u(E), o_kvc(E);
+  int FM = 0;
+  if (flow) {
+    FM = d.experts[0].blocks[0].ffn_up.nout / D;
+    if (FM <= 0) return CFB_ERR_INVALID_ARG;
+    for (int e = 0; e < E; ++e) {
+      const int rows = Bq * (e + 1) * d.chunk;
+      for (int q = 0; q < 2; ++q) {
+        o_x32[2 * e + q] = A.take((size_t)rows * D * 4);
+        o_x16[2 * e + q] = A.take((size_t)rows * D * 2);
+        o_xs[2 * e + q] = A.take((size_t)rows * nparts * 8);
+      }
+      o_qkv[e] = A.take((size_t)rows * 3 * D * 4);
+      o_o[e] = A.take((size_t)rows * D * 2);
+      o_qc[e] = A.take((size_t)rows * D * 4);
+      o_u[e] = A.take((size_t)rows * FM * D * 2);
+      o_kvc[e] = A.take((size_t)d.layers * Bq * C * 2 * D * 4);
+    }
+  }
+  const size_t o_ctxs = A.take((size_t)Bq * C * 8);
+  const int rank = d.markov_rank, order = d.path_order;
+  const int P2 = beam ? d.path_up.nout : 0;
+  const int rowsB = Bq * std::max(Wmax, 1);
+  size_t o_lastp = 0, o_cum = 0, o_toks = 0, o_bps = 0, o_h16 = 0, o_hstat = 0, o_mpath = 0, o_xhead = 0;
+  if (beam) {
+    o_lastp = A.take((size_t)rowsB * order * 8);
+    o_cum = A.take((size_t)rowsB * 4);
+    o_toks = A.take((size_t)(K + 1) * rowsB * 8);
+    o_bps = A.take((size_t)(K + 1) * rowsB * 4);
+    o_h16 = A.take((size_t)rowsB * D * 2);
+    o_hstat = A.take((size_t)rowsB * nparts * 8);
+    o_mpath = A.take((size_t)rowsB * P2 * 2);
+    o_xhead = A.take((size_t)rowsB * (D + rank) * 2);
+  }
+  const size_t o_gpart = A.take((size_t)G * 2 * cfb::kTileRows * cfb::kRowsMax * 4);
+  const size_t o_hpart = A.take((size_t)G * cfb::kRowsMax * cfb::kHeadPartFloats * 4);
+
+  auto& ph = B.phases; ph.clear();
+  B.jobs.clear();
+  auto& at = B.attn; at.clear();
+  B.max_tiles = 0;
+  B.P.nattncnt = 0;
+
+  { cfb::Phase p{}; p.kind = cfb::PK_PREP; ph.push_back(p); }
+
+  if (flow) {
+    const int L = d.layers, T = d.steps, hd = D / d.heads;
+    {   // cross K/V of every (expert, block), once per draft
+      std::vector<cfb::Job> js;
+      for (int e = 0; e < E; ++e)
+        for (int l = 0; l < L; ++l) {
+          const cfb_linear& lin = d.experts[e].blocks[l].cross_kv;
+          if (!lin_ok(lin, 2 * D, D)) return CFB_ERR_INVALID_ARG;
+          cfb::Job J = make_job(lin, Bq * C);
+          J.xkind = cfb::XK_F16; J.x = static_cast<const __half*>(r.ctx); J.ldx = D;
+          J.ln = cfb::LN_DIRECT; J.stats = B.dptr<float2>(o_ctxs);
+          J.ekind = cfb::EK_STORE;
+          J.out32 = B.dptr<float>(o_kvc[e]) + (size_t)l * Bq * C * 2 * D; J.ldo = 2 * D;
+          js.push_back(J);
+        }
+      add_phase(B, cfb::Phase{}, js);
+    }
+    std::vector<int> at_self(E), at_cross(E * L);
+    int cntoff = 0;
+    for (int e = 0; e < E; ++e) {
+      const int S = (e + 1) * d.chunk;
+      cfb::AttnTask a{};
+      a.q = B.dptr<float>(o_qkv[e]); a.ldq = 3 * D; a.qoff = 0;
+      a.k = a.q; a.ldk = 3 * D; a.koff = D;
+      a.v = a.q; a.ldv = 3 * D; a.voff = 2 * D;
+      a.out = B.dptr<__half>(o_o[e]); a.ldo = D;
+      a.rows_per_req = S; a.keys_per_req = S; a.B = Bq; a.hd = hd; a.heads = d.heads;
+      a.causal = 1; a.nsec = 3; a.Dsec = D; a.scale = 1.0f / std::sqrt((float)hd);
+      a.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
+      at_self[e] = (int)at.size(); at.push_back(a);
+      for (int l = 0; l < L; ++l) {
+        cfb::AttnTask c{};
+        c.q = B.dptr<float>(o_qc[e]); c.ldq = D; c.qoff = 0;
+        c.k = B.dptr<float>(o_kvc[e]) + (size_t)l * Bq * C * 2 * D; c.ldk = 2 * D; c.koff = 0;
+        c.v = c.k; c.ldv = 2 * D; c.voff = D;
+        c.out = B.dptr<__half>(o_o[e]); c.ldo = D;
+        c.rows_per_req = S; c.keys_per_req = C; c.B = Bq; c.hd = hd; c.heads = d.heads;
+        c.causal = 0; c.nsec = 1; c.Dsec = D; c.scale = 1.0f / std::sqrt((float)hd);
+        c.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
+        at_cross[e * L + l] = (int)at.size(); at.push_back(c);
+      }
+    }
+    B.P.nattncnt = cntoff;
+    for (int s = 0; s < T; ++s) {
+      const int pb = s & 1;
+      auto ln_job = [&](const cfb_linear& lin, int e) {
+        const int S = (e + 1) * d.chunk;
+        cfb::Job J = make_job(lin, Bq * S);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_x16[2 * e + pb]); J.ldx = D;
+        J.ln = cfb::LN_PARTS; J.stats = B.dptr<float2>(o_xs[2 * e + pb]); J.nparts = nparts;
+        return J;
+      };
+      auto resid_job = [&](const cfb_linear& lin, int e, size_t o_in, int ldin) {
+        const int S = (e + 1) * d.chunk;
+        cfb::Job J = make_job(lin, Bq * S);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_in); J.ldx = ldin;
+        J.ekind = cfb::EK_RESID; J.out32 = B.dptr<float>(o_x32[2 * e + pb]);
+        J.out16 = B.dptr<__half>(o_x16[2 * e + pb]); J.ldo = D;
+        J.ostats = B.dptr<float2>(o_xs[2 * e + pb]); J.onparts = nparts;
+        return J;
+      };
+      for (int l = 0; l < L; ++l) {
+        std::vector<cfb::Job> js;
+        for (int e = 0; e < E; ++e) {           // LN + self-attention in-projection
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.qkv, 3 * D, D)) return CFB_ERR_INVALID_ARG;
+          cfb::Job J = ln_job(bl.qkv, e);
+          J.ekind = cfb::EK_STORE; J.out32 = B.dptr<float>(o_qkv[e]); J.ldo = 3 * D;
+          J.attn = at_self[e];
+          js.push_back(J);
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+        for (int e = 0; e < E; ++e) {           // out-projection + residual
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.self_out, D, D)) return CFB_ERR_INVALID_ARG;
+          js.push_back(resid_job(bl.self_out, e, o_o[e], D));
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+        for (int e = 0; e < E; ++e) {           // LN + cross-attention query projection
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.cross_q, D, D)) return CFB_ERR_INVALID_ARG;
+          cfb::Job J = ln_job(bl.cross_q, e);
+          J.ekind = cfb::EK_STORE; J.out32 = B.dptr<float>(o_qc[e]); J.ldo = D;
+          J.attn = at_cross[e * L + l];
+          js.push_back(J);
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+        for (int e = 0; e < E; ++e) {
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.cross_out, D, D)) return CFB_ERR_INVALID_ARG;
+          js.push_back(resid_job(bl.cross_out, e, o_o[e], D));
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+        for (int e = 0; e < E; ++e) {           // LN + FFN up + GELU
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.ffn_up, FM * D, D)) return CFB_ERR_INVALID_ARG;
+          cfb::Job J = ln_job(bl.ffn_up, e);
+          J.ekind = cfb::EK_GELU16; J.out16 = B.dptr<__half>(o_u[e]); J.ldo = FM * D;
+          js.push_back(J);
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+        for (int e = 0; e < E; ++e) {           // FFN down + residual
+          const cfb_block& bl = d.experts[e].blocks[l];
+          if (!lin_ok(bl.ffn_down, D, FM * D)) return CFB_ERR_INVALID_ARG;
+          js.push_back(resid_job(bl.ffn_down, e, o_u[e], FM * D));
+        }
+        add_phase(B, cfb::Phase{}, js); js.clear();
+      }
+      std::vector<cfb::Job> js;                 // out_norm + out_proj, Euler, next inputs
+      for (int e = 0; e < E; ++e) {
+        const cfb_expert& ex = d.experts[e];
+        const int S = (e + 1) * d.chunk;
+        if (!lin_ok(ex.out_proj, D, D) || !ex.out_proj.bias) return CFB_ERR_INVALID_ARG;
+        cfb::Job J = ln_job(ex.out_proj, e);
+        J.rows = Bq * d.chunk;
+        J.gin = d.chunk; J.gstride = S; J.goff = e * d.chunk;
+        J.ekind = cfb::EK_EULER; J.e_idx = e; J.step = s; J.last_step = (s == T - 1);
+        J.dt = 1.0f / (float)T;
+        js.push_back(J);
+      }
+      add_phase(B, cfb::Phase{}, js);
+    }
+  }
+  if (beam) {
+    int fr = tree ? 1 : Wmax, base = 0, base_prev = 0;
+    const int TB = tree ? r.tree_topb : r.width;
+    for (int step = 1; step <= K; ++step) {
+      const int rows = Bq * fr;
+      const int nlive = std::min(step, order);
+      {   // h = sum_j mask_j (W_j emb(lastp_j) + b_j) over the live offsets (CF_PATH_TRIM)
+        cfb::Job J = make_job(d.path_offsets, rows);
+        J.Kt = nlive * D / 16;
+        J.nkc = (J.Kt + cfb::kUnitK - 1) / cfb::kUnitK;
+        J.xkind = cfb::XK_PATH; J.lastp = B.dptr<int64_t>(o_lastp); J.order = order;
+        J.emb = static_cast<const __half*>(d.embed); J.D = D;
+        J.ekind = cfb::EK_PATHH; J.bias = nullptr; J.colsum = nullptr;
+        J.p0 = d.path_offset_bias; J.nlive = nlive;
+        J.out16 = B.dptr<__half>(o_h16); J.ldo = D;
+        J.ostats = B.dptr<float2>(o_hstat); J.onparts = nparts;
+        cfb::Phase p{}; p.side_markov = 1; p.rows = rows; p.step = step;
+        add_phase(B, p, {J});
+      }
+      {   // LayerNorm + Linear(D, 2D) + GELU
+        cfb::Job J = make_job(d.path_up, rows);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_h16); J.ldx = D;
+        J.ln = cfb::LN_PARTS; J.stats = B.dptr<float2>(o_hstat); J.nparts = nparts;
+        J.ekind = cfb::EK_GELU16; J.out16 = B.dptr<__half>(o_mpath); J.ldo = P2;
+        add_phase(B, cfb::Phase{}, {J});
+      }
+      {   // Linear(2D, D) + the flow hidden of this depth -> head input rows
+        cfb::Job J = make_job(d.path_down, rows);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_mpath); J.ldx = P2;
+        J.ekind = cfb::EK_HEADIN; J.out16 = B.dptr<__half>(o_xhead); J.ldo = D + rank;
+        J.step = step; J.wrows = fr;
+        add_phase(B, cfb::Phase{}, {J});
+      }
+      {   // shortlist head + markov bias with online LSE + top-k, then the beam step
+        cfb::Job J = make_job(d.head, rows);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_xhead); J.ldx = D + rank;
+        J.ekind = cfb::EK_HEAD; J.R = d.shortlist_rows; J.topb = TB; J.bias = nullptr; J.colsum = nullptr;
+        cfb::Phase p{};
+        p.post = tree ? cfb::PO_BEAM_TREE : cfb::PO_BEAM_CHAIN;
+        p.rows = rows; p.step = step; p.fr = fr; p.keep = Wmax; p.topb = TB;
+        p.base = base; p.base_prev = base_prev; p.last = (step == K);
+        add_phase(B, p, {J});
+      }
+      if (tree) {
+        const int k = std::min(Wmax, fr * TB);
+        base_prev = base; base += k; fr = k;
+      }
+    }
+    B.P.N = base;
+  }
+  const size_t o_tilecnt = A.take((size_t)std::max(B.max_tiles, 1) * 4);
+  const size_t o_attncnt = A.take((size_t)std::max(B.P.nattncnt, 1) * 4);
+  B.off_phases = A.take(ph.size() * sizeof(cfb::Phase));
+  B.off_jobs = A.take(std::max<size_t>(B.jobs.size(), 1) * sizeof(cfb::Job));
+  B.off_attn = A.take(std::max<size_t>(at.size(), 1) * sizeof(cfb::AttnTask));
+  *bytes = A.take(0);
+  for (auto& a : at) a.cnt = B.dptr<unsigned>(o_attncnt) + reinterpret_cast<uintptr_t>(a.cnt);
+
+  cfb::Plan& P = B.P;
+  P.G = G; P.nphases = (int)ph.size(); P.mode = mode; P.B = Bq; P.D = D; P.DL = DL;
+  P.n_experts = E; P.chunk = d.chunk; P.C = C; P.steps = d.steps; P.order = order; P.rank = rank;
+  P.vocab = d.vocab; P.R = d.shortlist_rows; P.width = r.width; P.depth = r.depth;
+  P.keep = r.tree_keep; P.topb = r.tree_topb; P.Wmax = Wmax;
+  P.phases = B.dptr<cfb::Phase>(B.off_phases);
+  P.jobs = B.dptr<cfb::Job>(B.off_jobs);
+  P.attn = B.dptr<cfb::AttnTask>(B.off_attn);
+  if (flow) {
+    for (int e = 0; e < E; ++e) {
+      cfb::ExpertRT& X = P.ex[e];
+      for (int q = 0; q < 2; ++q) {
+        X.x32[q] = B.dptr<float>(o_x32[2 * e + q]);
+        X.x16[q] = B.dptr<__half>(o_x16[2 * e + q]);
+        X.xstat[q] = B.dptr<float2>(o_xs[2 * e + q]);
+      }
+      X.S = (e + 1) * d.chunk; X.start = e * d.chunk;
+      X.pos = d.experts[e].pos_emb; X.temb = d.experts[e].temb;
+      if (!X.pos || !X.temb) return CFB_ERR_INVALID_ARG;
+    }
+  }
+  P.bar = B.dptr<unsigned>(o_bar); P.exitcnt = P.bar + 1; P.headcnt = P.bar + 2;
+  P.err = reinterpret_cast<int*>(P.bar + 3);
+  P.tilecnt = B.dptr<unsigned>(o_tilecnt); P.ntilecnt = B.max_tiles;
+  P.attncnt = B.dptr<unsigned>(o_attncnt);
+  P.gpart = B.dptr<float>(o_gpart); P.hpart = B.dptr<float>(o_hpart);
+  P.ctx = static_cast<const __half*>(r.ctx); P.z0 = static_cast<const __half*>(r.z0);
+  P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs);
+  P.known0 = r.known0; P.tokens = r.tokens;
+  {
+    auto expose = [&](int i, size_t off, size_t nbytes) { P.buf[i] = B.dptr<void>(off); P.buf_bytes[i] = nbytes; };
+    if (beam) {
+      expose(CFB_BUF_PATH_H16, o_h16, (size_t)rowsB * D * 2);
+      expose(CFB_BUF_PATH_MID, o_mpath, (size_t)rowsB * P2 * 2);
+      expose(CFB_BUF_HEAD_IN, o_xhead, (size_t)rowsB * (D + rank) * 2);
+      expose(CFB_BUF_LASTP, o_lastp, (size_t)rowsB * order * 8);
+      expose(CFB_BUF_CUM, o_cum, (size_t)rowsB * 4);
+    }
+    if (flow) {
+      const size_t rows1 = (size_t)Bq * d.chunk;
+      expose(CFB_BUF_QKV0, o_qkv[0], rows1 * 3 * D * 4);
+      expose(CFB_BUF_X32_0, o_x32[0], rows1 * D * 4);
+      expose(CFB_BUF_KVC0, o_kvc[0], (size_t)d.layers * Bq * C * 2 * D * 4);
+    }
+  }
+  if (beam) {
+    P.lastp = B.dptr<int64_t>(o_lastp); P.cum = B.dptr<float>(o_cum);
+    P.toks = B.dptr<int64_t>(o_toks); P.bps = B.dptr<int>(o_bps);
+    P.shortlist = d.shortlist; P.markov_w1 = static_cast<const __half*>(d.markov_w1);
+    P.xhead = B.dptr<__half>(o_xhead); P.ldxhead = D + rank;
+  }
+  return CFB_OK;
+}
+
+struct LaunchRecord { int G, phases, smem, pad; };
+struct LaunchRec { void* ws; int G; };
+std::vector<LaunchRec> g_launch;     // grid of the plan last built in each workspace
+void remember_grid(void* ws, int G) {
+  for (auto& l : g_launch) if (l.ws == ws) { l.G = G; return; }
+  g_launch.push_back({ws, G});
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cfb_last_cuda_error(void) { return g_cuda_err; }
+int cfb_abi_version(void) { return CFB_ABI_VERSION; }
+
+cfb_status cfb_plan_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes) {
+  if (!d || !r || !bytes) return CFB_ERR_INVALID_ARG;
+  Builder B; B.d = d; B.r = r; B.base = nullptr;
+  return lower(B, bytes);
+}
+
+cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes) {
+  if (!d || !r || !ws) return CFB_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return CFB_ERR_INVALID_ARG;
+  Builder B; B.d = d; B.r = r; B.base = static_cast<uint8_t*>(ws);
+  size_t need = 0;
+  cfb_status st = lower(B, &need);
+  if (st != CFB_OK) return st;
+  if (need > bytes) return CFB_ERR_WORKSPACE;
+  cudaError_t e;
+  static bool attr_done = false;
+  if (!attr_done) {
+    if ((e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(cfb::Smem))) != cudaSuccess)
+      return cuda_fail(e, "smem attribute");
+    attr_done = true;
+  }
+  int per_sm = 0, dev = 0, sms = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfb::engine_kernel, cfb::kThreads,
+                                                         sizeof(cfb::Smem))) != cudaSuccess)
+    return cuda_fail(e, "occupancy");
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (per_sm < 1 || B.P.G > per_sm * sms) return CFB_ERR_COOP_LAUNCH;
+  if ((e = cudaMemcpy(B.base + B.off_phases, B.phases.data(), B.phases.size() * sizeof(cfb::Phase),
+                      cudaMemcpyHostToDevice)) != cudaSuccess) return cuda_fail(e, "copy phases");
+  if (!B.jobs.empty() &&
+      (e = cudaMemcpy(B.base + B.off_jobs, B.jobs.data(), B.jobs.size() * sizeof(cfb::Job),
+                      cudaMemcpyHostToDevice)) != cudaSuccess) return cuda_fail(e, "copy jobs");
+  if (!B.attn.empty() &&
+      (e = cudaMemcpy(B.base + B.off_attn, B.attn.data(), B.attn.size() * sizeof(cfb::AttnTask),
+                      cudaMemcpyHostToDevice)) != cudaSuccess) return cuda_fail(e, "copy attention tasks");
+  if ((e = cudaMemcpy(B.base + kOffPlan, &B.P, sizeof(cfb::Plan), cudaMemcpyHostToDevice)) != cudaSuccess)
+    return cuda_fail(e, "copy plan");
+  const size_t ob = off_barrier();
+  if ((e = cudaMemset(B.base + ob, 0, 64)) != cudaSuccess) return cuda_fail(e, "zero barrier");
+  LaunchRecord h{B.P.G, B.P.nphases, (int)sizeof(cfb::Smem), 0};
+  if ((e = cudaMemcpy(B.base + ob + 32, &h, sizeof(h), cudaMemcpyHostToDevice)) != cudaSuccess)
+    return cuda_fail(e, "copy launch record");
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "plan build sync");
+  remember_grid(ws, B.P.G);
+  return CFB_OK;
+}
+
+cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases) {
+  if (!ws) return CFB_ERR_INVALID_ARG;
+  LaunchRecord h{};
+  cudaError_t e = cudaMemcpy(&h, static_cast<uint8_t*>(ws) + off_barrier() + 32, sizeof(h),
+                             cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read launch record");
+  if (grid) *grid = h.G;
+  if (threads) *threads = cfb::kThreads;
+  if (smem) *smem = h.smem;
+  if (phases) *phases = h.phases;
+  return CFB_OK;
+}
+
+cfb_status cfb_plan_run(void* ws, void* stream) {
+  if (!ws) return CFB_ERR_INVALID_ARG;
+  int G = -1;
+  for (auto& l : g_launch) if (l.ws == ws) G = l.G;
+  if (G < 0) {
+    cfb_status st = cfb_plan_info(ws, &G, nullptr, nullptr, nullptr);
+    if (st != CFB_OK) return st;
+    remember_grid(ws, G);
+  }
+  const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
+  void* args[] = {(void*)&P};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)cfb::engine_kernel, dim3(G), dim3(cfb::kThreads),
+                                              args, sizeof(cfb::Smem), static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;
+  if (e != cudaSuccess) return cuda_fail(e, "engine launch");
+  return CFB_OK;
+}
+
+cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes) {
+  if (!ws || !ptr || which < 0 || which >= 16) return CFB_ERR_INVALID_ARG;
+  cfb::Plan P;
+  cudaError_t e = cudaMemcpy(&P, static_cast<uint8_t*>(ws) + kOffPlan, sizeof(P), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read plan record");
+  *ptr = P.buf[which];
+  if (bytes) *bytes = P.buf_bytes[which];
+  return P.buf[which] ? CFB_OK : CFB_ERR_INVALID_ARG;
+}
+
+cfb_status cfb_plan_error(void* ws, int* device_error) {
+  if (!ws || !device_error) return CFB_ERR_INVALID_ARG;
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, static_cast<uint8_t*>(ws) + off_barrier() + 12, sizeof(int),
+                             cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read error word");
+  *device_error = v;
+  return v == 0 ? CFB_OK : CFB_ERR_DEVICE_TIMEOUT;
+}
+
+}  // extern "C"

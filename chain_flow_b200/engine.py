@@ -1,0 +1,95 @@
+"""One persistent-kernel plan per (drafter weights, run shape): caller-owned, graph-stable buffers.
+
+The reference keeps one scratch set per (expert, batch) and never resizes it because CUDA graphs
+bake addresses (reference src/chain_flow/cuda_block.py:243-263, 382-388); a ``Plan`` is the
+same contract for the whole draft: inputs, outputs and workspace are allocated here once, bound
+into the phase table by ``cfb_plan_build``, and every ``run()`` is a single cooperative launch
+with no allocation and no host synchronisation (capturable in a CUDA graph).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .weights import DrafterWeights
+
+
+def tree_levels(keep: int, topb: int, depth: int) -> list[int]:
+    """Nodes added per tree level: depth 1 expands one node (reference flow_proposer.py:1315)."""
+    fr, out = 1, []
+    for _ in range(depth):
+        k = min(keep, fr * topb)
+        out.append(k)
+        fr = k
+    return out
+
+
+class Plan:
+    def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
+                 tree_keep: int = 4, tree_topb: int = 8, grid: int = 0):
+        self.w, self.mode, self.batch = w, mode, batch
+        cfg, dev = w.cfg, w.dev
+        D = cfg.hidden
+        self.lib = w.lib
+        self.ctx = torch.zeros(batch, cfg.context_size, D, dtype=torch.float16, device=dev)
+        self.z0 = torch.zeros(batch, cfg.draft_length, D, dtype=torch.float16, device=dev)
+        self.known0 = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.pred = torch.zeros(batch, cfg.draft_length, D, dtype=torch.float32, device=dev)
+        self.tree = mode in (_lib.MODE_TREE, _lib.MODE_BEAM_TREE)
+        if self.tree:
+            depth = min(depth, cfg.draft_length - 1)
+            self.levels = tree_levels(tree_keep, tree_topb, depth)
+            self.N = sum(self.levels)
+            self.tokens = torch.zeros(batch, 2 * self.N, dtype=torch.int64, device=dev)
+        else:
+            self.N = depth
+            self.tokens = torch.zeros(batch, depth, dtype=torch.int64, device=dev)
+        r = _lib.Run()
+        r.mode, r.batch, r.width, r.depth = mode, batch, width, depth
+        r.tree_keep, r.tree_topb, r.grid = tree_keep, tree_topb, grid
+        r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
+        r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
+        self.run_desc = r
+        nbytes = C.c_size_t(0)
+        _lib.check(self.lib.cfb_plan_workspace(C.byref(w.desc), C.byref(r), C.byref(nbytes)),
+                   "cfb_plan_workspace")
+        self.ws = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=dev)
+        self.ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        _lib.check(self.lib.cfb_plan_build(C.byref(w.desc), C.byref(r), C.c_void_p(self.ws_ptr),
+                                           C.c_size_t(int(nbytes.value))), "cfb_plan_build")
+        g, t, s, p = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        _lib.check(self.lib.cfb_plan_info(C.c_void_p(self.ws_ptr), C.byref(g), C.byref(t), C.byref(s),
+                                          C.byref(p)), "cfb_plan_info")
+        self.grid, self.threads, self.smem, self.phases = g.value, t.value, s.value, p.value
+
+    def run(self, stream=None) -> None:
+        """One persistent launch on `stream` (default: torch's current stream)."""
+        _lib.check(self.lib.cfb_plan_run(C.c_void_p(self.ws_ptr), C.c_void_p(_lib.stream_ptr(stream))),
+                   "cfb_plan_run")
+
+    def buffer(self, which: int, dtype, shape) -> torch.Tensor:
+        """A copy of one intermediate buffer of this plan (CFB_BUF_*), for stage-by-stage checks."""
+        ptr, nbytes = C.c_void_p(), C.c_size_t()
+        _lib.check(self.lib.cfb_plan_buffer(C.c_void_p(self.ws_ptr), which, C.byref(ptr), C.byref(nbytes)),
+                   "cfb_plan_buffer")
+        off = ptr.value - self.ws.data_ptr()
+        n = 1
+        for s_ in shape:
+            n *= s_
+        elt = torch.empty(0, dtype=dtype).element_size()
+        if off < 0 or off + n * elt > self.ws.numel() or n * elt > nbytes.value:
+            raise _lib.CfbError("buffer view out of range")
+        return self.ws[off:off + n * elt].view(dtype).view(*shape).clone()
+
+    def device_error(self) -> int:
+        """Synchronous read of the device error word (0 = the last run completed normally)."""
+        v = C.c_int(0)
+        self.lib.cfb_plan_error(C.c_void_p(self.ws_ptr), C.byref(v))
+        return v.value
+
+    def check(self) -> None:
+        err = self.device_error()
+        if err:
+            raise _lib.CfbError(f"device-side wait timed out (code {err}); outputs are invalid")

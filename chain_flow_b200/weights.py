@@ -1,0 +1,196 @@
+"""Drafter weights in the engine's device layout.
+
+``DrafterWeights`` takes a ``TreeFlowDrafter`` state dict (the reference checkpoint's parameter
+names, i.e. the ``drafter.``-prefixed keys of ``model.safetensors`` with the prefix removed,
+reference src/chain_flow/vllm_plugin/flow_proposer.py:638-648) plus the target model's input
+embedding and ``lm_head`` and the shortlist ids, and prepares everything once on the GPU with
+the C-ABI packing kernels:
+
+* every Linear -> packed fp16 stream layout, with the LayerNorm in front of it folded in
+  (gamma into the columns, beta into the bias, column sums for the mean correction);
+* ``time_mlp`` evaluated at every Euler step's tau (it is the same for every row);
+* the shortlist head ``[lm_head[sl] | markov.w2[sl]]`` packed as ONE [R, D + rank] matrix, so the
+  head GEMV and the markov bias are a single stream (reference flow_proposer.py:739-740, 1021-1025);
+* the PathHead offset projections packed side by side as one [D, order*D] matrix
+  (the batched form of reference vllm_plugin/fused.py:14-39).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+
+@dataclass
+class DraftConfig:
+    """The ``TreeFlowConfig`` fields the drafting path needs (reference tree_flow.py:39-72)."""
+    hidden: int
+    context_size: int = 8
+    draft_length: int = 6
+    chunk_size: int = 3
+    num_heads: int = 8
+    ffn_multiplier: int = 6
+    num_drafter_layers: int = 4
+    num_flow_steps: int = 8
+    path_order: int = 4
+    path_ffn_multiplier: int = 2
+    markov_rank: int = 256
+
+    @property
+    def n_experts(self) -> int:
+        return self.draft_length // self.chunk_size
+
+    @staticmethod
+    def from_model_args(args: dict, hidden: int) -> "DraftConfig":
+        keys = {f for f in DraftConfig.__dataclass_fields__ if f != "hidden"}
+        return DraftConfig(hidden=hidden, **{k: v for k, v in args.items() if k in keys})
+
+
+def expert_prefix(e: int) -> str:
+    return "expert." if e == 0 else f"extra_experts.{e - 1}."
+
+
+class DrafterWeights:
+    def __init__(self, sd: dict, cfg: DraftConfig, embed: torch.Tensor, lm_head: torch.Tensor,
+                 shortlist: torch.Tensor, device=None):
+        self.lib = _lib.load()
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise _lib.CfbError("DrafterWeights needs a CUDA device: the engine has no CPU path")
+        self.dev, self.cfg = dev, cfg
+        D = cfg.hidden
+        if D % 64 or cfg.draft_length % cfg.chunk_size:
+            raise _lib.CfbError(f"unsupported drafter shape: hidden={D} must be a multiple of 64")
+        self._keep = []            # every device tensor the packed structs point at
+        self.stream = torch.cuda.current_stream(dev)
+        f16 = lambda t: t.to(device=dev, dtype=torch.float16).contiguous()
+        f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
+        self.sd16 = {k: f16(v) for k, v in sd.items()}
+        self.sd32 = {}
+
+        def p32(name):
+            if name not in self.sd32:
+                self.sd32[name] = f32(sd[name])
+            return self.sd32[name]
+
+        self.embed = f16(embed)
+        self.vocab = self.embed.shape[0]
+        sl = shortlist.to(device=dev, dtype=torch.int64).contiguous()
+        self.shortlist = sl
+        R = sl.numel()
+        rank = cfg.markov_rank
+
+        self.experts = (_lib.Expert * cfg.n_experts)()
+        self._blocks = []
+        for e in range(cfg.n_experts):
+            p = expert_prefix(e)
+            blocks = (_lib.Block * cfg.num_drafter_layers)()
+            for l in range(cfg.num_drafter_layers):
+                b = f"{p}blocks.{l}."
+                w_in = self.sd16[b + "self_attn.in_proj_weight"]
+                b_in = p32(b + "self_attn.in_proj_bias")
+                cw = self.sd16[b + "cross_attn.in_proj_weight"]
+                cb = p32(b + "cross_attn.in_proj_bias")
+                blocks[l].qkv = self.linear(w_in, b_in, ln=(p32(b + "self_norm.weight"), p32(b + "self_norm.bias")))
+                blocks[l].self_out = self.linear(self.sd16[b + "self_attn.out_proj.weight"], p32(b + "self_attn.out_proj.bias"))
+                blocks[l].cross_q = self.linear(cw[:D], cb[:D], ln=(p32(b + "cross_norm.weight"), p32(b + "cross_norm.bias")))
+                blocks[l].cross_kv = self.linear(cw[D:], cb[D:], ln=(p32(b + "context_norm.weight"), p32(b + "context_norm.bias")))
+                blocks[l].cross_out = self.linear(self.sd16[b + "cross_attn.out_proj.weight"], p32(b + "cross_attn.out_proj.bias"))
+                blocks[l].ffn_up = self.linear(self.sd16[b + "ffn.1.weight"], p32(b + "ffn.1.bias"), ln=(p32(b + "ffn.0.weight"), p32(b + "ffn.0.bias")))
+                blocks[l].ffn_down = self.linear(self.sd16[b + "ffn.4.weight"], p32(b + "ffn.4.bias"))
+            self._blocks.append(blocks)
+            ex = self.experts[e]
+            pos = p32(p + "position_embedding.weight")
+            temb = torch.empty(cfg.num_flow_steps, D, device=dev, dtype=torch.float32)
+            _lib.check(self.lib.cfb_time_embed(
+                p32(p + "time_mlp.0.weight")[:, 0].contiguous().data_ptr(), p32(p + "time_mlp.0.bias").data_ptr(),
+                self.sd16[p + "time_mlp.2.weight"].data_ptr(), p32(p + "time_mlp.2.bias").data_ptr(),
+                D, cfg.num_flow_steps, temb.data_ptr(), self.stream.cuda_stream), "cfb_time_embed")
+            self._keep += [pos, temb]
+            ex.pos_emb, ex.temb = pos.data_ptr(), temb.data_ptr()
+            ex.out_proj = self.linear(self.sd16[p + "out_proj.weight"], p32(p + "out_proj.bias"),
+                                      ln=(p32(p + "out_norm.weight"), p32(p + "out_norm.bias")))
+            ex.blocks = C.cast(blocks, C.POINTER(_lib.Block))
+
+        # ---- path head, markov bias, shortlist head
+        order = cfg.path_order
+        po = self.pack_buffer(D, order * D)
+        for j in range(order):
+            self._pack_into(self.sd16[f"path_head.offset_proj.{j}.weight"], po, D, D, order * D, j * D)
+        self.path_offsets = _lib.Linear(po.data_ptr(), None, None, D, order * D)
+        self.path_offset_bias = torch.stack([p32(f"path_head.offset_proj.{j}.bias") for j in range(order)]).contiguous()
+        self._keep.append(self.path_offset_bias)
+        self.path_up = self.linear(self.sd16["path_head.mlp.0.weight"], p32("path_head.mlp.0.bias"),
+                                   ln=(p32("path_head.norm.weight"), p32("path_head.norm.bias")))
+        self.path_down = self.linear(self.sd16["path_head.mlp.3.weight"], p32("path_head.mlp.3.bias"))
+        self.markov_w1 = self.sd16["markov.w1.weight"]
+        hb = self.pack_buffer(R, D + rank)
+        lm16 = f16(lm_head)
+        self._pack_into(lm16, hb, R, D, D + rank, 0, rows=sl)
+        self._pack_into(self.sd16["markov.w2.weight"], hb, R, rank, D + rank, D, rows=sl)
+        del lm16
+        self.head = _lib.Linear(hb.data_ptr(), None, None, R, D + rank)
+        self.R = R
+
+        d = _lib.Drafter()
+        d.hidden, d.heads, d.layers, d.steps = D, cfg.num_heads, cfg.num_drafter_layers, cfg.num_flow_steps
+        d.draft_len, d.chunk, d.ctx_rows, d.n_experts = cfg.draft_length, cfg.chunk_size, cfg.context_size, cfg.n_experts
+        d.experts = C.cast(self.experts, C.POINTER(_lib.Expert))
+        d.path_order, d.markov_rank, d.vocab, d.shortlist_rows = order, rank, self.vocab, R
+        d.embed = self.embed.data_ptr()
+        d.path_offsets = self.path_offsets
+        d.path_offset_bias = self.path_offset_bias.data_ptr()
+        d.path_up, d.path_down = self.path_up, self.path_down
+        d.markov_w1 = self.markov_w1.data_ptr()
+        d.head = self.head
+        d.shortlist = sl.data_ptr()
+        self.desc = d
+        # the raw fp16 state dict is no longer needed except the tables the engine reads
+        keep = {"markov.w1.weight"}
+        self.sd16 = {k: v for k, v in self.sd16.items() if k in keep}
+        self.sd32 = {}
+        torch.cuda.synchronize(dev)
+
+    # ------------------------------------------------------------------------------------------
+    def pack_buffer(self, nout: int, k: int) -> torch.Tensor:
+        nbytes = self.lib.cfb_packed_bytes(nout, k)
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
+        self._keep.append(buf)
+        return buf
+
+    def _pack_into(self, w16: torch.Tensor, buf: torch.Tensor, nout: int, k: int, ktotal: int, kofs: int,
+                   rows: torch.Tensor | None = None, gamma: torch.Tensor | None = None):
+        _lib.check(self.lib.cfb_pack_linear(
+            w16.data_ptr(), w16.stride(0), rows.data_ptr() if rows is not None else None, nout, k,
+            gamma.data_ptr() if gamma is not None else None, buf.data_ptr(), ktotal, kofs,
+            self.stream.cuda_stream), "cfb_pack_linear")
+
+    def linear(self, w16: torch.Tensor, bias32: torch.Tensor | None, ln=None) -> "_lib.Linear":
+        """Pack one nn.Linear (optionally with the LayerNorm (gamma, beta) that feeds it)."""
+        w16 = w16.contiguous()
+        nout, k = w16.shape
+        buf = self.pack_buffer(nout, k)
+        gamma = ln[0] if ln is not None else None
+        self._pack_into(w16, buf, nout, k, k, 0, gamma=gamma)
+        colsum = None
+        if ln is not None:
+            b_out = torch.empty(nout, device=self.dev, dtype=torch.float32)
+            colsum = torch.empty(nout, device=self.dev, dtype=torch.float32)
+            _lib.check(self.lib.cfb_fold_bias(
+                w16.data_ptr(), w16.stride(0), nout, k, ln[0].data_ptr(), ln[1].data_ptr(),
+                bias32.data_ptr() if bias32 is not None else None, b_out.data_ptr(), colsum.data_ptr(),
+                self.stream.cuda_stream), "cfb_fold_bias")
+            bias32 = b_out
+            self._keep.append(colsum)
+        if bias32 is not None:
+            bias32 = bias32.contiguous()
+            self._keep.append(bias32)
+        return _lib.Linear(buf.data_ptr(), bias32.data_ptr() if bias32 is not None else None,
+                           colsum.data_ptr() if colsum is not None else None, nout, k)
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self._keep) + self.embed.numel() * 2

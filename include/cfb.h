@@ -1,0 +1,190 @@
+/*
+ * cfb.h -- C ABI of libcfb.so, the sm_100a drafting engine of chain_flow_b200.
+ *
+ * Plain C: device pointers, sizes and a cudaStream_t passed as void*. No torch types.
+ * Every buffer (weights, inputs, outputs, workspace) is allocated by the CALLER; the library
+ * allocates nothing per call, so every run entry point can be captured in a CUDA graph.
+ *
+ * Reference interfaces replaced (paths relative to the reference checkout):
+ *   src/chain_flow/csrc/fused_block.cu:784-862  cf_fused_block.{expert, cross_kv, max_grid}
+ *       -> cfb_plan_workspace / cfb_plan_build / cfb_plan_run (the whole integrator, both
+ *          chunk experts, all Euler steps, cross-K/V hoist, in one persistent launch)
+ *   src/chain_flow/cuda_block.py:266-311 (weight packing)  -> cfb_pack_linear / cfb_fold_bias
+ *   src/chain_flow/drafters/chunked_flow.py:230-234, 313-321 (time_mlp at tau = s/T)
+ *                                                       -> cfb_time_embed
+ *   src/chain_flow/vllm_plugin/flow_proposer.py:1188-1269 (_beam_chains) and :1273-1332
+ *       (_beam_tree), :1021-1028 (_head/_bias/_map), drafters/tree_flow.py:434-450
+ *       (_residual_from_lastp)                        -> CFB_MODE_CHAIN / CFB_MODE_TREE plans
+ *   src/chain_flow/kernels/tree_scan.py:43-78 (tree_gated_delta_scan) and the fork's
+ *       tree_gdn_verify.cu gdn_verify_kernel (patch:4401-4562) -> cfb_tree_gdn
+ */
+#ifndef CFB_H_
+#define CFB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CFB_ABI_VERSION 1
+
+typedef enum cfb_status {
+  CFB_OK = 0,
+  CFB_ERR_INVALID_ARG = 1,     /* null pointer, negative size, misaligned buffer */
+  CFB_ERR_UNSUPPORTED = 2,     /* shape outside what the kernels are built for */
+  CFB_ERR_WORKSPACE = 3,       /* workspace smaller than cfb_plan_workspace() asked for */
+  CFB_ERR_CUDA = 4,            /* a CUDA runtime call failed (cfb_last_cuda_error() says which) */
+  CFB_ERR_COOP_LAUNCH = 5,     /* the persistent grid cannot be co-resident on this device */
+  CFB_ERR_DEVICE_TIMEOUT = 6   /* a bounded device-side wait expired; outputs are invalid */
+} cfb_status;
+
+/* ---- packed weights --------------------------------------------------------------------
+ * A packed linear holds W (fp16, [nout, k] like nn.Linear.weight) in the engine's streaming
+ * layout: rows padded to a multiple of 64, then [nout/64][k/16][4][512 B], where each 512-byte
+ * block is one 16x16 tile pre-swizzled into the register order of a tensor-core A fragment
+ * (one warp reads it as 32 contiguous 16-byte vectors). A streamed unit is 8 consecutive k
+ * blocks of one 64-row tile: 16 KiB, contiguous. A LayerNorm in front of the linear is folded
+ * in: W' = fp16(W diag(gamma)), bias' = b + W beta and colsum = sum_k W'[:, k]; the engine then
+ * computes y = (W' x - mean * colsum) * rstd + bias' from the un-normalised fp16 input. */
+typedef struct cfb_linear {
+  const void*  w;       /* packed fp16, cfb_packed_bytes(nout, k) bytes, 16-byte aligned */
+  const float* bias;    /* fp32 [nout] or NULL */
+  const float* colsum;  /* fp32 [nout] when a LayerNorm is folded in, else NULL */
+  int nout;
+  int k;                /* multiple of 16 */
+} cfb_linear;
+
+/* one HiddenKVFlowBlock (reference drafters/chunked_flow.py:168-202) */
+typedef struct cfb_block {
+  cfb_linear qkv;        /* self_attn.in_proj, self_norm folded          [3D, D] */
+  cfb_linear self_out;   /* self_attn.out_proj                           [D, D]  */
+  cfb_linear cross_q;    /* cross_attn.in_proj rows [0,D), cross_norm folded   [D, D]  */
+  cfb_linear cross_kv;   /* cross_attn.in_proj rows [D,3D), context_norm folded [2D, D] */
+  cfb_linear cross_out;  /* cross_attn.out_proj                          [D, D]  */
+  cfb_linear ffn_up;     /* ffn.1, ffn.0 (LayerNorm) folded              [FM*D, D] */
+  cfb_linear ffn_down;   /* ffn.4                                        [D, FM*D] */
+} cfb_block;
+
+/* one HiddenKVFlowExpert (reference drafters/chunked_flow.py:205-414) */
+typedef struct cfb_expert {
+  const float* pos_emb;     /* fp32 [draft_len, D]: position_embedding.weight */
+  const float* temb;        /* fp32 [steps, D]: time_mlp(s / steps), from cfb_time_embed */
+  cfb_linear out_proj;      /* out_proj, out_norm folded [D, D] */
+  const cfb_block* blocks;  /* HOST array [layers] */
+} cfb_expert;
+
+typedef struct cfb_drafter {
+  int hidden;          /* D == target hidden size (TreeFlowDrafter, tree_flow.py:113-114) */
+  int heads;           /* attention heads (8) */
+  int layers;          /* blocks per expert */
+  int steps;           /* Euler steps */
+  int draft_len;       /* flow positions (draft_length) */
+  int chunk;           /* rows per chunk expert (chunk_size) */
+  int ctx_rows;        /* context window rows (context_size) */
+  int n_experts;       /* draft_len / chunk */
+  const cfb_expert* experts;   /* HOST array [n_experts] */
+  /* path head, markov bias and shortlist head (the beam) */
+  int path_order;
+  int markov_rank;
+  int vocab;
+  int shortlist_rows;          /* R */
+  const void* embed;           /* fp16 [vocab, D] target input embeddings */
+  cfb_linear path_offsets;     /* [D, order*D]: offset_proj.j.weight side by side; bias NULL */
+  const float* path_offset_bias; /* fp32 [order, D] */
+  cfb_linear path_up;          /* path_head.mlp.0, path_head.norm folded [2D, D] */
+  cfb_linear path_down;        /* path_head.mlp.3 [D, 2D] */
+  const void* markov_w1;       /* fp16 [vocab, rank] */
+  cfb_linear head;             /* [R, D + rank] = [lm_head.weight[sl] | markov.w2.weight[sl]] */
+  const int64_t* shortlist;    /* int64 [R] global token ids (sorted, unique) */
+} cfb_drafter;
+
+typedef enum cfb_mode {
+  CFB_MODE_FLOW = 0,        /* integrate only:  ctx, z0 -> pred */
+  CFB_MODE_CHAIN = 1,       /* flow + chain beam: ctx, z0, known0 -> tokens [B, depth] */
+  CFB_MODE_TREE = 2,        /* flow + tree beam:  ctx, z0, known0 -> tokens [B, 2N] */
+  CFB_MODE_BEAM_CHAIN = 3,  /* chain beam over a given pred */
+  CFB_MODE_BEAM_TREE = 4    /* tree beam over a given pred */
+} cfb_mode;
+
+typedef struct cfb_run {
+  int mode;            /* cfb_mode */
+  int batch;           /* requests B */
+  int width;           /* chain beam width (CF_WIDTH, reference flow_proposer.py:374) */
+  int depth;           /* chain: emitted tokens K; tree: levels (CF_TREE_DEPTH) */
+  int tree_keep;       /* CF_TREE_KEEP */
+  int tree_topb;       /* CF_TREE_TOPB */
+  int grid;            /* persistent CTAs; 0 = one per SM */
+  /* device I/O, bound at cfb_plan_build time (graph-stable addresses) */
+  const void* ctx;     /* fp16 [B, ctx_rows, D] */
+  const void* z0;      /* fp16 [B, draft_len, D] initial latents */
+  const int64_t* known0;  /* int64 [B] committed token per request */
+  float* pred;         /* fp32 [B, draft_len, D]: output of the flow, input of BEAM_* modes */
+  int64_t* tokens;     /* int64 chain [B, depth]; tree [B, 2N] (N tokens, then N parents) */
+} cfb_run;
+
+int cfb_abi_version(void);
+const char* cfb_last_cuda_error(void);
+
+/* bytes of a packed [nout, k] linear */
+size_t cfb_packed_bytes(int nout, int k);
+
+/* Pack fp16 W[rows[i] or i, :k] (row stride ldw elements) into columns [kofs, kofs+k) of a
+ * packed [nout, ktotal] buffer, scaling column j by gamma[j] when gamma != NULL. */
+cfb_status cfb_pack_linear(const void* w, int64_t ldw, const int64_t* rows, int nout, int k,
+                           const float* gamma, void* dst, int ktotal, int kofs, void* stream);
+
+/* LayerNorm folding for one linear W [nout, k] (fp16, row stride ldw):
+ *   bias_out[i]   = (bias ? bias[i] : 0) + sum_j W[i, j] * beta[j]
+ *   colsum_out[i] = sum_j fp16(W[i, j] * gamma[j])       (colsum_out may be NULL) */
+cfb_status cfb_fold_bias(const void* w, int64_t ldw, int nout, int k, const float* gamma,
+                         const float* beta, const float* bias, float* bias_out, float* colsum_out,
+                         void* stream);
+
+/* out[s, :] = W2 silu(w1 * (s/steps) + b1) + b2 for s in [0, steps): the time embedding of
+ * every Euler step (the reference evaluates time_mlp at the same tau for every row) */
+cfb_status cfb_time_embed(const float* w1, const float* b1, const void* w2_f16, const float* b2,
+                          int D, int steps, float* out, void* stream);
+
+/* Plan = phase table + scratch for one (drafter, run) pair, laid out in a caller buffer. */
+cfb_status cfb_plan_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes);
+/* Synchronous set-up: validates shapes, writes the phase table into ws, zeroes counters. */
+cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes);
+/* Launch the persistent kernel on `stream` (no allocation, no host sync: capturable). */
+cfb_status cfb_plan_run(void* ws, void* stream);
+/* Synchronous: device error word of the last run (0 = ok, CFB_ERR_DEVICE_TIMEOUT, ...). */
+cfb_status cfb_plan_error(void* ws, int* device_error);
+/* Launch parameters the plan resolved (grid CTAs, threads, dynamic smem bytes, phases). */
+cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases);
+
+/* Device address and size of one intermediate buffer of a built plan (stage-by-stage checks):
+ * CFB_BUF_PATH_H16   fp16 [rows, D]      path offsets sum h (rows = B * beam width)
+ * CFB_BUF_PATH_MID   fp16 [rows, 2D]     gelu(LN(h) W_up^T + b)
+ * CFB_BUF_HEAD_IN    fp16 [rows, D + r]  [pred + residual | markov w1 row], the head input
+ * CFB_BUF_LASTP      int64 [rows, order] beam paths (last `order` tokens, -1 = none)
+ * CFB_BUF_CUM        fp32 [rows]         beam cumulative log-probs
+ * CFB_BUF_QKV0       fp32 [B*chunk, 3D]  expert 0 self-attention in-projection output
+ * CFB_BUF_X32_0      fp32 [B*chunk, D]   expert 0 residual stream (even Euler steps)
+ * CFB_BUF_KVC0       fp32 [L, B*ctx, 2D] expert 0 cross-attention K/V of every block
+ * Values hold what the last completed run left there. */
+enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
+       CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
+cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);
+
+/* Tree-aware Gated-DeltaNet verification over B independent trees of N nodes.
+ * q,k [B,N,H,Dk] fp16; v [B,N,H,Dv] fp16; g (log decay), beta [B,N,H] fp32;
+ * parent [B,N] int32 (parent < child; -1 = root, reads init); init [B,H,Dk,Dv] fp32;
+ * out o [B,N,H,Dv] fp32; states [B,N,H,Dk,Dv] fp32 (every node's state; also where a child
+ * reads its parent's state, so it is required).
+ * use_l2norm: q,k <- x / (||x|| + 1e-6); q is scaled by Dk**-0.5.
+ * Supported: Dk == 128; Dv a multiple of 32, and of 128 when above 128. */
+cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, const float* g,
+                        const float* beta, const int32_t* parent, const float* init,
+                        float* o, float* states, int B, int N, int H, int Dk, int Dv,
+                        int use_l2norm, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CFB_H_ */
