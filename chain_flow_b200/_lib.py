@@ -26,7 +26,8 @@ EXPORTED = [
     "cfb_fold_bias", "cfb_time_embed", "cfb_plan_workspace", "cfb_plan_build", "cfb_plan_run",
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn",
 ]
-BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0 = range(8)
+BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF = range(9)
+RUN_PROFILE = 1
 
 
 class CfbError(RuntimeError):
@@ -60,7 +61,7 @@ class Drafter(C.Structure):
 
 class Run(C.Structure):
     _fields_ = [("mode", C.c_int), ("batch", C.c_int), ("width", C.c_int), ("depth", C.c_int),
-                ("tree_keep", C.c_int), ("tree_topb", C.c_int), ("grid", C.c_int),
+                ("tree_keep", C.c_int), ("tree_topb", C.c_int), ("grid", C.c_int), ("flags", C.c_int),
                 ("ctx", C.c_void_p), ("z0", C.c_void_p), ("known0", C.c_void_p),
                 ("pred", C.c_void_p), ("tokens", C.c_void_p)]
 

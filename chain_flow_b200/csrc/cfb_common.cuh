@@ -76,6 +76,12 @@ CFB_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint
       :: "r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// Order earlier generic-proxy global accesses (made visible to this thread by an acquire) before
+// subsequent async-proxy (bulk copy) reads of global memory.
+CFB_DEV void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---- named barrier among the consumer warps ------------------------------------------------
 CFB_DEV void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" :: "r"(nthreads) : "memory");

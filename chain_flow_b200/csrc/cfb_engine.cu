@@ -7,14 +7,20 @@
 // (drafter, run) pair into a table of phases; the kernel walks the table with a bounded grid
 // barrier between phases.
 //
-// Per CTA: one producer thread streams the packed weight units of every GEMM phase through an
-// 8-stage shared-memory ring with cp.async.bulk (the TMA copy engine, no multicast) and runs
-// ahead across phase boundaries, since weights never depend on activations. 16 consumer warps
-// multiply each unit (64 output features x 128 k) with tensor-core MMAs against fp16 activation
-// fragments read from L2 one unit ahead, reduce across warps in a fixed order, and finish each
-// 64-feature tile with a fused epilogue. Work is split stream-K style: the units of a phase are
-// cut into equal contiguous ranges, one per CTA; a tile shared by two CTAs is completed by
-// whichever arrives last, summing the partials in k order (deterministic, no float atomics).
+// Each CTA is warp-specialised:
+//   * weight producer (1 thread): streams the CTA's packed weight units of every GEMM phase
+//     (64 output features x 128 k, 16 KiB) into a shared-memory ring with cp.async.bulk (the
+//     TMA copy engine, no multicast), running ahead across phase boundaries since weights never
+//     depend on activations;
+//   * activation producer (1 warp): once the grid barrier in front of a phase has passed,
+//     copies each unit's activation rows into the same ring slot with 16-byte cp.async;
+//   * 8 MMA warps: multiply each unit with tensor-core MMAs and, at the end of a 64-feature
+//     tile, hand their fp32 partials to a shared-memory slot and move on;
+//   * 4 epilogue warps: reduce the 8 partials in a fixed order, complete tiles split across
+//     CTAs (stream-K: whichever CTA arrives last sums the partials in k order -- deterministic,
+//     no float atomics), apply the fused epilogue (bias, LayerNorm correction, GELU, residual,
+//     Euler step, row statistics, attention of completed heads, head log-sum-exp + top-k) and
+//     take the beam step.
 //
 // A LayerNorm in front of a linear is folded at pack time (W <- W diag(gamma), b <- b + W beta);
 // the engine feeds the fp16 activation straight into the MMA and applies
@@ -42,22 +48,40 @@
 
 namespace cfb {
 
-constexpr int kConsumerWarps = 16;
-constexpr int kConsumers = kConsumerWarps * 32;     // 512
-constexpr int kThreads = kConsumers + 32;           // + 1 producer warp
+// ---- thread layout: [0,8) MMA warps, 8 weight producer, 9 activation producer, [10,14) epilogue.
+// 448 threads leave ~144 registers per thread, so accumulators never spill.
+constexpr int kMmaWarps = 8;
+constexpr int kMma = kMmaWarps * 32;                // 256
+constexpr int kKSlices = kMmaWarps / 4;             // k slices of a unit (4 m16 tiles per unit)
+constexpr int kWProdWarp = 8, kXProdWarp = 9, kEpiWarp0 = 10;
+constexpr int kEpiWarps = 4;
+constexpr int kEpi = kEpiWarps * 32;                // 128
+constexpr int kThreads = (kMmaWarps + 2 + kEpiWarps) * 32;   // 448
+constexpr int kWorkers = kMma + kEpi;               // threads that take part in phase-level work
+constexpr int kBarWorkers = 1, kBarEpi = 2;         // named barriers (0 is __syncthreads)
+
 constexpr int kTileRows = 64;                       // output features per tile (4 x m16)
 constexpr int kUnitK = 8;                           // 16-wide k blocks per streamed unit
 constexpr int kBlockBytes = 512;                    // one 16x16 fp16 fragment tile
 constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB
-constexpr int kStages = 8;
+constexpr int kMaxStages = 12;
+constexpr int kXRowBytes = 272;                     // activation row of a unit: 128 fp16 + 16 pad
+constexpr int kSmemBudget = 232448 - 1024;          // dynamic + static shared memory per CTA
 constexpr int kRowsMax = 64;                        // activation rows per job
 constexpr int kTopMax = 8;                          // top-k per beam row
 constexpr int kMaxExperts = 4;
 constexpr int kStatCols = 64;                       // columns per row-statistics part
 constexpr int kHeadPartFloats = 2 + 2 * kTopMax;
-constexpr int kSlices = 8;                          // epilogue threads per row
 
 enum XKind : int { XK_F16 = 0, XK_PATH = 1 };
+
+// fp16 activations the engine produces for its own GEMMs are stored unit-tiled: each 128-column
+// slice of all R rows is contiguous (one bulk copy per streamed unit), and within a row the
+// 16-byte chunks are XOR-swizzled by the row index so tensor-core fragment reads from shared
+// memory hit 32 distinct banks. Element (r, k) of an R-row buffer:
+CFB_DEV size_t tidx(int R, int r, int k) {
+  return ((size_t)(k >> 7) * R + r) * 128 + (size_t)((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7);
+}
 enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
 enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
                    EK_HEADIN = 5, EK_HEAD = 6 };
@@ -72,6 +96,7 @@ struct AttnTask {
   int rows_per_req, keys_per_req, B, hd, heads, causal, nsec, Dsec;
   float scale;
   unsigned* cnt;          // [heads]
+  int outR;               // tiled rows of `out`
 };
 
 struct ExpertRT {
@@ -84,16 +109,17 @@ struct Job {
   const uint4* w;
   int Mt, Kt, Kstride, nkc, rows, nout;
   int unit_base, tile_base;
-  // activation source (fp16 fragments)
+  // activation source (fp16 rows, or a gather of embedding rows by path token)
   int xkind;
-  const __half* x; int ldx;
+  const __half* x; int ldx;                // XK_F16: unit-tiled source with xR rows; XK_PATH: unused
+  int xR, xcopy;                           // tiled rows of the source; rows copied per unit
   int gin, gstride, goff;                  // source row = (r / gin) * gstride + goff + r % gin
   int ln; const float2* stats; int nparts; const float* colsum;
   const int64_t* lastp; int order; const __half* emb; int D;   // XK_PATH gather
   // epilogue
   int ekind;
   const float* bias;
-  float* out32; __half* out16; int ldo;
+  float* out32; __half* out16; int ldo; int oR;   // out32 row stride; out16 tiled rows
   float2* ostats; int onparts;
   int attn;                                // -1 or AttnTask index (trigger after the tile)
   int e_idx, step, last_step, wrows, nlive, R, topb;
@@ -104,12 +130,22 @@ struct Job {
 struct Phase {
   int kind;
   int job0, njobs, nunits, ntiles;
+  int whole;                // 1: each CTA gets whole tiles (no cross-CTA fixups); 0: stream-K
   int post;
   int side_markov;
   int step, rows, fr, keep, topb, base, base_prev, last;
 };
 
+// Dynamic shared memory, laid out per plan by the host: the ring of streamed units (each stage =
+// 16 KiB of packed weights + the unit's activation rows), mbarriers, the accumulator hand-off
+// slots, the epilogue's scratch (attention / merge ids), one reduced tile, row statistics.
+struct SmemLayout {
+  int nstages, stage_bytes, rows_pad, nbuf;
+  int off_bar, off_slots, off_scratch, off_red, off_rowstat, off_tile, off_misc, total;
+};
+
 struct Plan {
+  SmemLayout sm;
   int G, nphases, mode, B, D, DL, n_experts, chunk, C, steps, order, rank, vocab, R;
   int width, depth, keep, topb, Wmax, N;
   const Phase* phases;
@@ -121,23 +157,40 @@ struct Plan {
   unsigned* attncnt; int nattncnt;
   float* gpart;             // [G][2][kTileRows*kRowsMax]
   float* hpart;             // [G][kRowsMax][kHeadPartFloats]
-  const __half* ctx; const __half* z0; float* pred; float2* ctxstat;
+  const __half* ctx; const __half* z0; float* pred; float2* ctxstat; __half* ctx16;
   const int64_t* known0; int64_t* lastp; float* cum; int64_t* toks; int* bps; int64_t* tokens;
   const int64_t* shortlist; const __half* markov_w1; __half* xhead; int ldxhead;
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
+  unsigned long long* prof;                // [nphases][G][4] or NULL
 };
 
 struct Smem {
-  uint8_t ring[kStages][kUnitBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  float slots[kConsumerWarps * 16 * kRowsMax];     // warp partials; attention / merge scratch
-  float red[kTileRows * kRowsMax];                 // one reduced tile [feature][row]
-  float2 rowstat[kRowsMax];
-  int flag;
+  uint8_t* ring; int nstages, stage_bytes, rp, nbuf;
+  uint64_t* full; uint64_t* empty;         // per ring stage
+  uint64_t* accf; uint64_t* acce;          // per accumulator slot buffer
+  float* slots;                            // [nbuf][MMA warps][16][rp]
+  float* scratch;                          // attention / merge ids (epilogue only)
+  float* red;                              // [kTileRows][rp]
+  float2* rowstat;
+  float* tbias; float* tcsum;              // [kTileRows] bias / LayerNorm column sums of the tile
+  int* flag;
+  volatile int* phase_ready;               // the phase the workers have entered
+  __device__ uint8_t* stage(int s) const { return ring + (size_t)s * stage_bytes; }
+  __device__ float* slot(int b) const { return slots + (size_t)b * kMmaWarps * 16 * rp; }
 };
 
+// A cooperating thread group: index in group, size, named barrier.
+struct Grp { int t, n, bar; };
+CFB_DEV void gsync(const Grp& g) { asm volatile("bar.sync %0, %1;" :: "r"(g.bar), "r"(g.n) : "memory"); }
+
 struct HeadState { float m, s; float tv[kTopMax]; int ti[kTopMax]; };
+
+// Profiling (plans built with CFB_RUN_PROFILE): ns spent waiting, per role, reset every phase.
+struct WaitClock {
+  unsigned long long full = 0, slot = 0;
+  bool on = false;
+  CFB_DEV unsigned long long now() const { return on ? globaltimer() : 0ull; }
+};
 
 // ------------------------------------------------------------------------------------------
 CFB_DEV void set_err(const Plan& P, int code) { atomicCAS(P.err, 0, code); }
@@ -151,11 +204,11 @@ CFB_DEV int next_contributor(int c, long long U, int G) {
   return cta_of(cta_start(U, G, c + 1), U, G);
 }
 
-// grid barrier over the consumer threads of all CTAs; bounded; false once an error is set
-CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch) {
-  consumer_sync(kConsumers);
+// grid barrier over the worker threads of all CTAs; bounded; false once an error is set
+CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W) {
+  gsync(W);
   __shared__ int s_ok;
-  if (threadIdx.x == 0) {
+  if (W.t == 0) {
     ++epoch;
     __threadfence();
     atom_add_release(P.bar, 1u);
@@ -171,37 +224,11 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch) {
     if (ld_volatile_int(P.err) != 0) ok = 0;
     s_ok = ok;
   }
-  consumer_sync(kConsumers);
+  gsync(W);
   return s_ok != 0;
 }
 
-// ------------------------------------------------------------------------------------------
 CFB_DEV int src_row(const Job& J, int r) { return (r / J.gin) * J.gstride + J.goff + r % J.gin; }
-
-// B fragment (16 k x 8 rows) of k-block kb for n-tile nt: {X[row][2t..2t+1], X[row][2t+8..2t+9]}
-template <int NT>
-CFB_DEV void load_frag(const Job& J, int kb, int lane, uint32_t (&f)[NT][2]) {
-  const int g = lane >> 2, t = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int r = nt * 8 + g;
-    f[nt][0] = f[nt][1] = 0u;
-    if (r >= J.rows) continue;
-    const int sr = src_row(J, r);
-    const int k = kb * 16 + 2 * t;
-    const __half* p;
-    if (J.xkind == XK_PATH) {
-      const int j = k / J.D, d = k - j * J.D;
-      const int64_t tok = J.lastp[(size_t)sr * J.order + j];
-      if (tok < 0) continue;
-      p = J.emb + (size_t)tok * J.D + d;
-    } else {
-      p = J.x + (size_t)sr * J.ldx + k;
-    }
-    f[nt][0] = *reinterpret_cast<const uint32_t*>(p);
-    f[nt][1] = *reinterpret_cast<const uint32_t*>(p + 8);
-  }
-}
 
 // ------------------------------------------------------------------------------------------
 CFB_DEV void chan_merge(float& n, float& m, float& M2, float nb, float mb, float M2b) {
@@ -227,11 +254,11 @@ CFB_DEV void chan_group(float& n, float& m, float& M2, int width) {
   }
 }
 
-// row LayerNorm statistics of the job's source rows -> S.rowstat[r] = (mean, rstd)
-CFB_DEV void job_rowstats(const Job& J, Smem& S) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Row LayerNorm statistics of the job's source rows -> S.rowstat[r] = (mean, rstd) (epilogue).
+CFB_DEV void job_rowstats(const Job& J, Smem& S, const Grp& E) {
+  const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
   if (J.ln == LN_PARTS) {
-    for (int r = warp; r < J.rows; r += kConsumerWarps) {
+    for (int r = warp; r < J.rows; r += nw) {
       const int sr = src_row(J, r);
       float n = 0.f, m = 0.f, M2 = 0.f;
       for (int p = lane; p < J.nparts; p += 32) {
@@ -242,40 +269,61 @@ CFB_DEV void job_rowstats(const Job& J, Smem& S) {
       if (lane == 0) S.rowstat[r] = make_float2(m, rsqrtf(M2 / n + 1e-5f));
     }
   } else if (J.ln == LN_DIRECT) {
-    for (int r = tid; r < J.rows; r += kConsumers) S.rowstat[r] = __ldcg(J.stats + src_row(J, r));
+    for (int r = E.t; r < J.rows; r += E.n) S.rowstat[r] = __ldcg(J.stats + src_row(J, r));
   } else {
-    for (int r = tid; r < J.rows; r += kConsumers) S.rowstat[r] = make_float2(0.f, 1.f);
+    for (int r = E.t; r < J.rows; r += E.n) S.rowstat[r] = make_float2(0.f, 1.f);
   }
-  consumer_sync(kConsumers);
+  gsync(E);
 }
 
-CFB_DEV float epi_val(const Job& J, const Smem& S, int f, int r, int col) {
+// y = (acc - mean * colsum) * rstd + bias for feature f of the current tile, row r
+CFB_DEV float epi_val(const Smem& S, int f, int r) {
   const float2 rs = S.rowstat[r];
-  const float cs = J.colsum ? J.colsum[col] : 0.f;
-  return (S.red[f * kRowsMax + r] - rs.x * cs) * rs.y + (J.bias ? J.bias[col] : 0.f);
+  return (S.red[f * S.rp + r] - rs.x * S.tcsum[f]) * rs.y + S.tbias[f];
+}
+
+// Row/slice mapping of the epilogue threads for per-row work: `sl` threads per row (8, 4 or 2),
+// each owning 64 / sl consecutive features of a 64-feature tile; whole warps take part.
+struct RowMap { int r, q, sl, nf; };
+CFB_DEV RowMap row_map(int rows, int et) {
+  const int rp = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+  const int sl = kEpi / rp;
+  return {et / sl, et % sl, sl, kTileRows / sl};
 }
 
 // ------------------------------------------------------------------------------------------
-// attention of one head, run by the CTA that completes the last tile of that head's columns
-CFB_DEV void run_attention(const AttnTask& A, int h, Smem& S) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// attention of one head, run by the CTA whose epilogue completes the last tile of that head
+CFB_DEV void run_attention(const AttnTask& A, int h, Smem& S, const Grp& E) {
+  const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
   const int Sq = A.rows_per_req, Kn = A.keys_per_req, hd = A.hd;
-  float* qs = S.slots;
+  float* qs = S.scratch;
   float* ks = qs + Sq * hd;
   float* vs = ks + Kn * hd;
   float* sc = vs + Kn * hd;
+  const int cpr = hd / 4;                       // 16-byte chunks per head row
   for (int b = 0; b < A.B; ++b) {
-    for (int e = tid; e < Sq * hd; e += kConsumers) {
-      const int i = e / hd, d = e - i * hd;
-      qs[e] = __ldcg(A.q + (size_t)(b * Sq + i) * A.ldq + A.qoff + h * hd + d);
+    // every q/k/v row slice of this head in flight at once (L2 only), then one wait
+    for (int e = E.t; e < (Sq + 2 * Kn) * cpr; e += E.n) {
+      const int row = e / cpr, c = e - row * cpr;
+      const float* src;
+      float* dst;
+      if (row < Sq) {
+        src = A.q + (size_t)(b * Sq + row) * A.ldq + A.qoff + h * hd + c * 4;
+        dst = qs + row * hd + c * 4;
+      } else if (row < Sq + Kn) {
+        const int j = row - Sq;
+        src = A.k + (size_t)(b * Kn + j) * A.ldk + A.koff + h * hd + c * 4;
+        dst = ks + j * hd + c * 4;
+      } else {
+        const int j = row - Sq - Kn;
+        src = A.v + (size_t)(b * Kn + j) * A.ldv + A.voff + h * hd + c * 4;
+        dst = vs + j * hd + c * 4;
+      }
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
     }
-    for (int e = tid; e < Kn * hd; e += kConsumers) {
-      const int j = e / hd, d = e - j * hd;
-      ks[e] = __ldcg(A.k + (size_t)(b * Kn + j) * A.ldk + A.koff + h * hd + d);
-      vs[e] = __ldcg(A.v + (size_t)(b * Kn + j) * A.ldv + A.voff + h * hd + d);
-    }
-    consumer_sync(kConsumers);
-    for (int pr = warp; pr < Sq * Kn; pr += kConsumerWarps) {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    gsync(E);
+    for (int pr = warp; pr < Sq * Kn; pr += nw) {
       const int i = pr / Kn, j = pr - i * Kn;
       float s = 0.f;
       for (int d = lane; d < hd; d += 32) s += qs[i * hd + d] * ks[j * hd + d];
@@ -283,42 +331,43 @@ CFB_DEV void run_attention(const AttnTask& A, int h, Smem& S) {
       for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
       if (lane == 0) sc[pr] = (A.causal && j > i) ? -INFINITY : s * A.scale;
     }
-    consumer_sync(kConsumers);
-    if (tid < Sq) {
+    gsync(E);
+    if (E.t < Sq) {
       float mx = -INFINITY;
-      for (int j = 0; j < Kn; ++j) mx = fmaxf(mx, sc[tid * Kn + j]);
+      for (int j = 0; j < Kn; ++j) mx = fmaxf(mx, sc[E.t * Kn + j]);
       float sum = 0.f;
-      for (int j = 0; j < Kn; ++j) { const float e = __expf(sc[tid * Kn + j] - mx); sc[tid * Kn + j] = e; sum += e; }
+      for (int j = 0; j < Kn; ++j) { const float e = __expf(sc[E.t * Kn + j] - mx); sc[E.t * Kn + j] = e; sum += e; }
       const float inv = 1.f / sum;
-      for (int j = 0; j < Kn; ++j) sc[tid * Kn + j] *= inv;
+      for (int j = 0; j < Kn; ++j) sc[E.t * Kn + j] *= inv;
     }
-    consumer_sync(kConsumers);
-    for (int e = tid; e < Sq * hd; e += kConsumers) {
+    gsync(E);
+    for (int e = E.t; e < Sq * hd; e += E.n) {
       const int i = e / hd, d = e - i * hd;
       float o = 0.f;
       for (int j = 0; j < Kn; ++j) o += sc[i * Kn + j] * vs[j * hd + d];
-      A.out[(size_t)(b * Sq + i) * A.ldo + h * hd + d] = __float2half_rn(o);
+      A.out[tidx(A.outR, b * Sq + i, h * hd + d)] = __float2half_rn(o);
     }
-    consumer_sync(kConsumers);
+    gsync(E);
   }
 }
 
-CFB_DEV void attn_trigger(const Plan& P, const Job& J, int tile, Smem& S) {
+CFB_DEV void attn_trigger(const Plan& P, const Job& J, int tile, Smem& S, const Grp& E) {
   const AttnTask& A = P.attn[J.attn];
   const int c0 = (tile * kTileRows) % A.Dsec;
   const int h0 = c0 / A.hd, h1 = min((c0 + kTileRows - 1) / A.hd, A.heads - 1);
   for (int h = h0; h <= h1; ++h) {
-    if (threadIdx.x == 0) {
+    if (E.t == 0) {
       const unsigned expect = (unsigned)A.nsec *
           (unsigned)(((h + 1) * A.hd - 1) / kTileRows - (h * A.hd) / kTileRows + 1);
+      __threadfence();
       const unsigned old = atom_add_acqrel(A.cnt + h, 1u);
-      S.flag = (old + 1 == expect);
+      *S.flag = (old + 1 == expect);
       if (old + 1 == expect) A.cnt[h] = 0u;
     }
-    consumer_sync(kConsumers);
-    const int go = S.flag;
-    consumer_sync(kConsumers);
-    if (go) { __threadfence(); run_attention(A, h, S); }
+    gsync(E);
+    const int go = *S.flag;
+    gsync(E);
+    if (go) { __threadfence(); run_attention(A, h, S, E); }
   }
 }
 
@@ -368,108 +417,126 @@ CFB_DEV void head_group(HeadState& H, int K, int width) {
 }
 
 // ------------------------------------------------------------------------------------------
-CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadState& H) {
-  const int tid = threadIdx.x;
+// the fused epilogue of one completed 64-feature tile (S.red holds its [feature][row] sums);
+// per-row work loads its global operands in unrolled groups of 8 so the loads overlap
+CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadState& H, const Grp& E) {
   const int rows = J.rows;
   const int col0 = tile * kTileRows;
   switch (J.ekind) {
     case EK_STORE:
-    case EK_GELU16:
-    case EK_HEADIN: {
-      for (int e = tid; e < kTileRows * rows; e += kConsumers) {
-        const int f = e / rows, r = e - f * rows;
+    case EK_GELU16: {
+      for (int e = E.t; e < kTileRows * rows; e += E.n) {
+        const int r = e / kTileRows, f = e - r * kTileRows;      // consecutive threads: columns
         const int col = col0 + f;
         if (col >= J.nout) continue;
-        const float v = epi_val(J, S, f, r, col);
+        const float v = epi_val(S, f, r);
         if (J.ekind == EK_STORE) J.out32[(size_t)r * J.ldo + col] = v;
-        else if (J.ekind == EK_GELU16) J.out16[(size_t)r * J.ldo + col] = __float2half_rn(gelu_erf(v));
-        else {
-          const int b = r / J.wrows;
-          J.out16[(size_t)r * J.ldo + col] =
-              __float2half_rn(v + P.pred[((size_t)b * P.DL + J.step) * P.D + col]);
-        }
+        else J.out16[tidx(J.oR, r, col)] = __float2half_rn(gelu_erf(v));
+      }
+      break;
+    }
+    case EK_HEADIN: {
+      for (int e = E.t; e < kTileRows * rows; e += E.n) {
+        const int r = e / kTileRows, f = e - r * kTileRows;
+        const int col = col0 + f;
+        const int b = r / J.wrows;
+        J.out16[tidx(J.oR, r, col)] =
+            __float2half_rn(epi_val(S, f, r) + P.pred[((size_t)b * P.DL + J.step) * P.D + col]);
       }
       break;
     }
     case EK_RESID:
     case EK_PATHH: {
-      // thread (r, q): 8 consecutive columns of row r, statistics merged over the 8 slices
-      const int r = tid / kSlices, q = tid % kSlices;
-      if (r < ((rows + 3) / 4) * 4) {          // whole 32-lane groups enter the shuffles
-        float n = 0.f, m = 0.f, M2 = 0.f;
-        if (r < rows) {
-          for (int f = q * 8; f < q * 8 + 8; ++f) {
-            const int col = col0 + f;
-            float v = epi_val(J, S, f, r, col);
-            if (J.ekind == EK_RESID) {
-              v += J.out32[(size_t)r * J.ldo + col];
-              J.out32[(size_t)r * J.ldo + col] = v;
-            } else {
-              for (int j = 0; j < J.nlive; ++j)
-                if (J.lastp[(size_t)r * J.order + j] >= 0) v += J.p0[(size_t)j * J.D + col];
-            }
-            J.out16[(size_t)r * J.ldo + col] = __float2half_rn(v);
+      const RowMap M = row_map(rows, E.t);
+      float n = 0.f, m = 0.f, M2 = 0.f;
+      if (M.r < rows) {
+        for (int f0 = M.q * M.nf; f0 < (M.q + 1) * M.nf; f0 += 8) {
+          float add[8];
+          if (J.ekind == EK_RESID) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) add[i] = J.out32[(size_t)M.r * J.ldo + col0 + f0 + i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) add[i] = 0.f;
+            for (int j = 0; j < J.nlive; ++j)
+              if (J.lastp[(size_t)M.r * J.order + j] >= 0) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) add[i] += J.p0[(size_t)j * J.D + col0 + f0 + i];
+              }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int col = col0 + f0 + i;
+            const float v = epi_val(S, f0 + i, M.r) + add[i];
+            if (J.ekind == EK_RESID) J.out32[(size_t)M.r * J.ldo + col] = v;
+            J.out16[tidx(J.oR, M.r, col)] = __float2half_rn(v);
             n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
           }
         }
-        chan_group(n, m, M2, kSlices);
-        if (q == 0 && r < rows) J.ostats[(size_t)r * J.onparts + tile] = make_float2(m, M2);
       }
+      chan_group(n, m, M2, M.sl);
+      if (M.q == 0 && M.r < rows) J.ostats[(size_t)M.r * J.onparts + tile] = make_float2(m, M2);
       break;
     }
     case EK_EULER: {
-      const int r = tid / kSlices, q = tid % kSlices;
-      if (r < ((rows + 3) / 4) * 4) {
-        float n[kMaxExperts], m[kMaxExperts], M2[kMaxExperts];
+      const RowMap M = row_map(rows, E.t);
+      float n[kMaxExperts], m[kMaxExperts], M2[kMaxExperts];
 #pragma unroll
-        for (int e = 0; e < kMaxExperts; ++e) { n[e] = 0.f; m[e] = 0.f; M2[e] = 0.f; }
-        const int b = r / P.chunk, c = r - b * P.chunk;
-        const ExpertRT& E = P.ex[J.e_idx];
-        const int pos = E.start + c;
-        const int nx = (J.step + 1) & 1;
-        if (r < rows) {
-          for (int f = q * 8; f < q * 8 + 8; ++f) {
-            const int col = col0 + f;
-            const float v = epi_val(J, S, f, r, col);
-            float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col;
-            const float z = *zp + J.dt * v;
-            *zp = z;
-            if (!J.last_step) {
+      for (int e = 0; e < kMaxExperts; ++e) { n[e] = 0.f; m[e] = 0.f; M2[e] = 0.f; }
+      const int b = M.r / P.chunk, c = M.r - b * P.chunk;
+      const int pos = P.ex[J.e_idx].start + c;
+      const int nx = (J.step + 1) & 1;
+      if (M.r < rows) {
+        for (int f0 = M.q * M.nf; f0 < (M.q + 1) * M.nf; f0 += 8) {
+          float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f0;
+          float z[8];
 #pragma unroll
-              for (int e = 0; e < kMaxExperts; ++e) {
-                if (e >= P.n_experts) break;
-                const ExpertRT& X = P.ex[e];
-                if (pos >= X.S) continue;
-                float xv = z + X.pos[(size_t)pos * P.D + col];
-                if (pos >= X.start) xv += X.temb[(size_t)(J.step + 1) * P.D + col];
-                const size_t xi = ((size_t)b * X.S + pos) * P.D + col;
-                X.x32[nx][xi] = xv;
-                X.x16[nx][xi] = __float2half_rn(xv);
-                n[e] += 1.f; const float d = xv - m[e]; m[e] += d / n[e]; M2[e] += d * (xv - m[e]);
+          for (int i = 0; i < 8; ++i) z[i] = zp[i];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) { z[i] += J.dt * epi_val(S, f0 + i, M.r); zp[i] = z[i]; }
+          if (!J.last_step) {
+#pragma unroll
+            for (int e = 0; e < kMaxExperts; ++e) {
+              if (e >= P.n_experts) break;
+              const ExpertRT& X = P.ex[e];
+              if (pos >= X.S) continue;
+              const float* pe = X.pos + (size_t)pos * P.D + col0 + f0;
+              const float* te = X.temb + (size_t)(J.step + 1) * P.D + col0 + f0;
+              const bool cur = pos >= X.start;
+              float xv[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) xv[i] = z[i] + pe[i] + (cur ? te[i] : 0.f);
+              const int xrow = b * X.S + pos;
+              const size_t xi = (size_t)xrow * P.D + col0 + f0;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                X.x32[nx][xi + i] = xv[i];
+                X.x16[nx][tidx(P.B * X.S, xrow, col0 + f0 + i)] = __float2half_rn(xv[i]);
+                n[e] += 1.f; const float d = xv[i] - m[e]; m[e] += d / n[e]; M2[e] += d * (xv[i] - m[e]);
               }
             }
           }
         }
-        if (!J.last_step) {
+      }
+      if (!J.last_step) {
 #pragma unroll
-          for (int e = 0; e < kMaxExperts; ++e) {
-            if (e >= P.n_experts) break;
-            chan_group(n[e], m[e], M2[e], kSlices);
-            const ExpertRT& X = P.ex[e];
-            if (q == 0 && r < rows && pos < X.S)
-              X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m[e], M2[e]);
-          }
+        for (int e = 0; e < kMaxExperts; ++e) {
+          if (e >= P.n_experts) break;
+          chan_group(n[e], m[e], M2[e], M.sl);
+          const ExpertRT& X = P.ex[e];
+          if (M.q == 0 && M.r < rows && pos < X.S)
+            X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m[e], M2[e]);
         }
       }
       break;
     }
     case EK_HEAD: {
-      const int r = tid / kSlices, q = tid % kSlices;
-      if (r < rows) {
-        for (int f = q * 8; f < q * 8 + 8; ++f) {
+      const RowMap M = row_map(rows, E.t);
+      if (M.r < rows) {
+        for (int f = M.q * M.nf; f < (M.q + 1) * M.nf; ++f) {
           const int j = col0 + f;
           if (j >= J.R) break;
-          const float v = S.red[f * kRowsMax + r];
+          const float v = S.red[f * S.rp + M.r];
           if (v > H.m) { H.s = H.s * __expf(H.m - v) + 1.f; H.m = v; }
           else H.s += __expf(v - H.m);
           top_insert(H, J.topb, v, j);
@@ -478,41 +545,44 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
       break;
     }
   }
-  __threadfence();
-  consumer_sync(kConsumers);
-  if (J.attn >= 0) attn_trigger(P, J, tile, S);
+  gsync(E);
+  if (J.attn >= 0) attn_trigger(P, J, tile, S, E);
 }
 
 // ------------------------------------------------------------------------------------------
-// reduce the 16 warps' partials of one tile, then finish it (directly, or through the fixup)
-template <int NT>
-CFB_DEV void tile_end(const Plan& P, const Job& J, int tile, bool complete, long long U,
-                      long long ug_first, float (&acc)[NT][4], Smem& S, HeadState& H) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  constexpr int RP = NT * 8;
-  float* sl = S.slots + warp * 16 * RP;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int r0 = nt * 8 + 2 * t;
-    sl[g * RP + r0] = acc[nt][0];
-    sl[g * RP + r0 + 1] = acc[nt][1];
-    sl[(g + 8) * RP + r0] = acc[nt][2];
-    sl[(g + 8) * RP + r0 + 1] = acc[nt][3];
-    acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  }
-  consumer_sync(kConsumers);
+// Epilogue side of one tile: take the MMA warps' partials from slot buffer `b`, reduce them in a
+// fixed order, release the slot, then finish the tile directly or through the stream-K fixup.
+CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
+                      long long ug_first, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
+                      WaitClock& wc) {
   const int rows = J.rows;
-  // feature f = 16 i + ff comes from warps i, i+4, i+8, i+12 (one per k slice), summed in order
-  for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+  const int b = tseq % S.nbuf;
+  const unsigned long long w0 = wc.now();
+  if (!mbar_wait(&S.accf[b], (tseq / S.nbuf) & 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
+  wc.slot += wc.now() - w0;
+  const float* sl = S.slot(b);
+  {   // this tile's bias and LayerNorm column sums, one load per thread
+    const int col0 = tile * kTileRows;
+    if (E.t < kTileRows) {
+      const int col = col0 + E.t;
+      S.tbias[E.t] = (J.bias && col < J.nout) ? J.bias[col] : 0.f;
+    } else if (E.t < 2 * kTileRows) {
+      const int col = col0 + E.t - kTileRows;
+      S.tcsum[E.t - kTileRows] = (J.colsum && col < J.nout) ? J.colsum[col] : 0.f;
+    }
+  }
+  // feature f = 16 i + ff comes from MMA warps i, i+4, ... (one per k slice), summed in order
+  for (int e = E.t; e < kTileRows * rows; e += E.n) {
     const int f = e / rows, r = e - f * rows;
     const int i = f >> 4, ff = f & 15;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) s += S.slots[((i + 4 * w) * 16 + ff) * RP + r];
-    S.red[f * kRowsMax + r] = s;
+    for (int w = 0; w < kKSlices; ++w) s += sl[((i + 4 * w) * 16 + ff) * S.rp + r];
+    S.red[f * S.rp + r] = s;
   }
-  consumer_sync(kConsumers);
+  gsync(E);
+  if (E.t == 0) mbar_arrive(&S.acce[b]);
+  ++tseq;
   if (!complete) {
     // contributors: the CTAs whose ranges hold this tile's units, in k order; when a phase has
     // fewer units than CTAs, CTAs with empty ranges sit between them and are not counted
@@ -524,148 +594,303 @@ CFB_DEV void tile_end(const Plan& P, const Job& J, int tile, bool complete, long
       ++ncontrib;
     const int slot = (cta_start(U, P.G, c) >= ug_first) ? 0 : 1;
     float* mine = P.gpart + ((size_t)c * 2 + slot) * (kTileRows * kRowsMax);
-    for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+    for (int e = E.t; e < kTileRows * rows; e += E.n) {
       const int f = e / rows, r = e - f * rows;
-      __stcg(mine + f * kRowsMax + r, S.red[f * kRowsMax + r]);
+      __stcg(mine + f * kRowsMax + r, S.red[f * S.rp + r]);
     }
     __threadfence();
-    consumer_sync(kConsumers);
-    if (tid == 0) {
+    gsync(E);
+    if (E.t == 0) {
       unsigned* cnt = P.tilecnt + J.tile_base + tile;
       const unsigned old = atom_add_acqrel(cnt, 1u);
       const bool last = (old + 1 == (unsigned)ncontrib);
       if (last) *cnt = 0u;
-      S.flag = last;
+      *S.flag = last;
     }
-    consumer_sync(kConsumers);
-    const bool last = S.flag;
-    consumer_sync(kConsumers);
+    gsync(E);
+    const bool last = *S.flag;
+    gsync(E);
     if (!last) return;
     __threadfence();
-    for (int e = tid; e < kTileRows * rows; e += kConsumers) {
+    for (int e = E.t; e < kTileRows * rows; e += E.n) {
       const int f = e / rows, r = e - f * rows;
       float s = 0.f;
       for (int cc = c_first; cc < P.G && cta_start(U, P.G, cc) <= ug_last; cc = next_contributor(cc, U, P.G)) {
         const int sl2 = (cta_start(U, P.G, cc) >= ug_first) ? 0 : 1;
         s += __ldcg(P.gpart + ((size_t)cc * 2 + sl2) * (kTileRows * kRowsMax) + f * kRowsMax + r);
       }
-      S.red[f * kRowsMax + r] = s;
+      S.red[f * S.rp + r] = s;
     }
-    consumer_sync(kConsumers);
+    gsync(E);
   }
-  tile_epilogue(P, J, tile, S, H);
+  tile_epilogue(P, J, tile, S, H, E);
 }
 
 // ------------------------------------------------------------------------------------------
+// The units of a phase for this CTA: one contiguous range of the phase's linear unit space,
+// walked job by job. The weight producer, the activation producer, the MMA warps and the
+// epilogue warps all walk exactly this sequence, so ring slot i always holds the i-th unit and
+// slot buffer j the j-th tile.
+struct UnitRange { long long u0, u1; };
+// first unit of the phase's t-th tile (tiles are numbered across the phase's jobs)
+CFB_DEV long long tile_unit(const Plan& P, const Phase& ph, long long t) {
+  if (t >= ph.ntiles) return ph.nunits;
+  for (int jx = ph.njobs - 1; jx >= 0; --jx) {
+    const Job& J = P.jobs[ph.job0 + jx];
+    if (t >= J.tile_base) return J.unit_base + (t - J.tile_base) * J.nkc;
+  }
+  return 0;
+}
+CFB_DEV UnitRange cta_units(const Plan& P, const Phase& ph) {
+  if (ph.whole) {
+    const long long T = ph.ntiles;
+    return {tile_unit(P, ph, cta_start(T, P.G, blockIdx.x)), tile_unit(P, ph, cta_start(T, P.G, blockIdx.x + 1))};
+  }
+  const long long U = ph.nunits;
+  return {cta_start(U, P.G, blockIdx.x), cta_start(U, P.G, blockIdx.x + 1)};
+}
+CFB_DEV bool job_slice(const Job& J, const UnitRange& cu, int& ju0, int& ju1) {
+  const long long jb = J.unit_base, je = jb + (long long)J.Mt * J.nkc;
+  const long long a = max(cu.u0, jb), b = min(cu.u1, je);
+  if (a >= b) return false;
+  ju0 = (int)(a - jb); ju1 = (int)(b - jb);
+  return true;
+}
+
+// MMA warps: multiply the job's units; hand each finished tile's partials to a slot buffer.
 template <int NT>
-CFB_DEV void gemm_job(const Plan& P, const Job& J, long long U, int ju0, int ju1, uint32_t& ci,
-                      Smem& S, HeadState& H) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci, uint32_t& tseq, Smem& S,
+                     WaitClock& wc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice of a unit
-  job_rowstats(J, S);
+  const int g = lane >> 2, t = lane & 3;
+  // shared-memory row of each n-tile's activation row: tiled sources are 256 B per row with
+  // chunks swizzled by row; path gathers are 272 B per row, unswizzled
+  const bool tiled = J.xkind == XK_F16;
+  const int xrs = tiled ? 256 : kXRowBytes, xsw = tiled ? 7 : 0;
+  int xrow[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) { const int r = nt * 8 + g; xrow[nt] = r < J.rows ? src_row(J, r) : -1; }
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  uint32_t nx[2][NT][2];
-  auto prefetch = [&](int ju) {
-    const int kc = ju % J.nkc;
-    const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int blk = ks + 4 * i;
-      if (blk < nkb) load_frag<NT>(J, kc * kUnitK + blk, lane, nx[i]);
-    }
-  };
-  prefetch(ju0);
   for (int ju = ju0; ju < ju1; ++ju) {
     const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
     const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
-    uint32_t cx[2][NT][2];
+    const int stage = ci % S.nstages;
+    const unsigned long long w0 = wc.now();
+    if (!mbar_wait(&S.full[stage], (ci / S.nstages) & 1, P.err)) set_err(P, DEV_TIMEOUT_FULL);
+    wc.full += wc.now() - w0;
+    const uint8_t* st = S.stage(stage);
+    const uint8_t* xs = st + kUnitBytes;
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) { cx[i][nt][0] = nx[i][nt][0]; cx[i][nt][1] = nx[i][nt][1]; }
-    if (ju + 1 < ju1) prefetch(ju + 1);
-    const int stage = ci % kStages;
-    if (!mbar_wait(&S.full[stage], (ci / kStages) & 1, P.err)) set_err(P, DEV_TIMEOUT_FULL);
-    const uint8_t* st = S.ring[stage];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int blk = ks + 4 * i;
+    for (int i = 0; i < kUnitK / kKSlices; ++i) {
+      const int blk = ks + kKSlices * i;
       if (blk < nkb) {
         const uint4 a = *reinterpret_cast<const uint4*>(st + (blk * 4 + mi) * kBlockBytes + lane * 16);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma16816(acc[nt], a, cx[i][nt][0], cx[i][nt][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          uint32_t b0 = 0u, b1 = 0u;
+          const int sr = xrow[nt];
+          if (sr >= 0) {
+            const uint8_t* xr = xs + sr * xrs + 4 * t;
+            b0 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk) ^ (sr & xsw)) << 4));
+            b1 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk + 1) ^ (sr & xsw)) << 4));
+          }
+          mma16816(acc[nt], a, b0, b1);
+        }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.empty[stage]);
     ++ci;
     if (kc == J.nkc - 1 || ju == ju1 - 1) {
-      const bool complete = (ju0 <= tile * J.nkc) && (ju1 >= (tile + 1) * J.nkc);
-      tile_end<NT>(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, acc, S, H);
+      const int b = tseq % S.nbuf;
+      const unsigned long long w1 = wc.now();
+      if (!mbar_wait(&S.acce[b], ((tseq / S.nbuf) & 1) ^ 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
+      wc.slot += wc.now() - w1;
+      float* sl = S.slot(b) + warp * 16 * S.rp;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int r0 = nt * 8 + 2 * t;
+        if (r0 < S.rp) {
+          sl[g * S.rp + r0] = acc[nt][0];
+          sl[g * S.rp + r0 + 1] = acc[nt][1];
+          sl[(g + 8) * S.rp + r0] = acc[nt][2];
+          sl[(g + 8) * S.rp + r0 + 1] = acc[nt][3];
+        }
+        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.accf[b]);
+      ++tseq;
     }
   }
 }
 
-CFB_DEV void gemm_phase(const Plan& P, const Phase& ph, uint32_t& ci, Smem& S, HeadState& H) {
-  const long long U = ph.nunits;
-  const long long u0 = cta_start(U, P.G, blockIdx.x), u1 = cta_start(U, P.G, blockIdx.x + 1);
+CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& tseq, Smem& S, WaitClock& wc) {
+  const UnitRange cu = cta_units(P, ph);
   for (int jx = 0; jx < ph.njobs; ++jx) {
     const Job& J = P.jobs[ph.job0 + jx];
-    const long long jb = J.unit_base, je = jb + (long long)J.Mt * J.nkc;
-    const long long a = max(u0, jb), b = min(u1, je);
-    if (a >= b) continue;
-    const int ju0 = (int)(a - jb), ju1 = (int)(b - jb);
+    int ju0, ju1;
+    if (!job_slice(J, cu, ju0, ju1)) continue;
     switch ((J.rows + 7) / 8) {
-      case 1: gemm_job<1>(P, J, U, ju0, ju1, ci, S, H); break;
-      case 2: gemm_job<2>(P, J, U, ju0, ju1, ci, S, H); break;
-      case 3: case 4: gemm_job<4>(P, J, U, ju0, ju1, ci, S, H); break;
-      default: gemm_job<8>(P, J, U, ju0, ju1, ci, S, H); break;
+      case 1: mma_job<1>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 2: mma_job<2>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 3: mma_job<3>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 4: mma_job<4>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 5: case 6: mma_job<6>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      default: mma_job<8>(P, J, ju0, ju1, ci, tseq, S, wc); break;
     }
   }
 }
 
-// producer: stream this CTA's units of every GEMM phase, running ahead of the consumers
-CFB_DEV void producer(const Plan& P, Smem& S) {
+// Epilogue warps: the same tiles in the same order.
+CFB_DEV void epi_phase(const Plan& P, const Phase& ph, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
+                       WaitClock& wc) {
+  const long long U = ph.nunits;
+  const UnitRange cu = cta_units(P, ph);
+  for (int jx = 0; jx < ph.njobs; ++jx) {
+    const Job& J = P.jobs[ph.job0 + jx];
+    int ju0, ju1;
+    if (!job_slice(J, cu, ju0, ju1)) continue;
+    job_rowstats(J, S, E);
+    for (int tile = ju0 / J.nkc; tile <= (ju1 - 1) / J.nkc; ++tile) {
+      const bool complete = (ju0 <= tile * J.nkc) && (ju1 >= (tile + 1) * J.nkc);
+      epi_tile(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, tseq, S, H, E, wc);
+    }
+  }
+}
+
+// Weight producer (one thread): stream this CTA's packed weight units of every GEMM phase into
+// the ring with cp.async.bulk, running ahead of the consumers across phase boundaries.
+CFB_DEV void weight_producer(const Plan& P, Smem& S) {
   uint32_t pi = 0;
   bool ok = true;
   for (int p = 0; p < P.nphases && ok; ++p) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
-    const long long U = ph.nunits;
-    const long long u0 = cta_start(U, P.G, blockIdx.x), u1 = cta_start(U, P.G, blockIdx.x + 1);
+    unsigned long long waited = 0;
+    const UnitRange cu = cta_units(P, ph);
     for (int jx = 0; jx < ph.njobs && ok; ++jx) {
       const Job& J = P.jobs[ph.job0 + jx];
-      const long long jb = J.unit_base, je = jb + (long long)J.Mt * J.nkc;
-      const long long a = max(u0, jb), b = min(u1, je);
-      for (long long u = a; u < b; ++u) {
-        const int ju = (int)(u - jb);
+      int ju0, ju1;
+      if (!job_slice(J, cu, ju0, ju1)) continue;
+      for (int ju = ju0; ju < ju1; ++ju) {
         const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
         const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
         const uint8_t* src = reinterpret_cast<const uint8_t*>(J.w) +
             ((size_t)tile * J.Kstride + (size_t)kc * kUnitK) * 4 * kBlockBytes;
         const uint32_t bytes = (uint32_t)(nkb * 4 * kBlockBytes);
-        const int stage = pi % kStages;
-        if (!mbar_wait(&S.empty[stage], ((pi / kStages) & 1) ^ 1, P.err)) {
+        const int stage = pi % S.nstages;
+        const unsigned long long w0 = P.prof ? globaltimer() : 0ull;
+        if (!mbar_wait(&S.empty[stage], ((pi / S.nstages) & 1) ^ 1, P.err)) {
           set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
         }
+        if (P.prof) waited += globaltimer() - w0;
         mbar_arrive_expect_tx(&S.full[stage], bytes);
-        bulk_g2s(S.ring[stage], src, bytes, &S.full[stage]);
+        bulk_g2s(S.stage(stage), src, bytes, &S.full[stage]);
         ++pi;
       }
     }
+    if (P.prof) {
+      P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 8] = waited;
+      P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 9] = globaltimer();
+    }
   }
   // every issued copy must land before this CTA may exit (copies complete on their own)
-  const uint32_t first = pi > (uint32_t)kStages ? pi - kStages : 0u;
-  for (uint32_t i = first; i < pi; ++i) mbar_wait(&S.full[i % kStages], (i / kStages) & 1);
+  const uint32_t first = pi > (uint32_t)S.nstages ? pi - S.nstages : 0u;
+  for (uint32_t i = first; i < pi; ++i) mbar_wait(&S.full[i % S.nstages], (i / S.nstages) & 1);
+}
+
+// Activation producer (one thread): once the grid barrier in front of a phase has passed, copy
+// the activation rows each unit reads (rows x 128 fp16, or the embedding rows of a path gather)
+// into the unit's ring slot with 1-D bulk copies that complete on the slot's full barrier (the
+// same barrier the weight producer's copy completes on), so nothing here ever waits for data.
+// Absent path tokens are zero-filled with shared-memory stores before the arrive.
+CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
+  const int kc = ju % J.nkc;
+  const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
+  const int k0 = kc * kUnitK * 16;
+  const uint32_t rowbytes = (uint32_t)nkb * 32u;
+  uint32_t bytes = 0;
+  if (J.xkind == XK_PATH) {
+    // the unit's k range can span offsets when D is not a multiple of 128: split per offset
+    for (int r = 0; r < J.rows; ++r) {
+      const int sr = src_row(J, r);
+      for (int k = k0; k < k0 + nkb * 16;) {
+        const int j = k / J.D, d = k - j * J.D;
+        const int len = min(k0 + nkb * 16 - k, J.D - d);
+        const int64_t tok = J.lastp[(size_t)sr * J.order + j];
+        if (tok >= 0) bytes += (uint32_t)len * 2u;
+        k += len;
+      }
+    }
+    mbar_arrive_expect_tx(full, bytes);          // before the copies can complete
+    for (int r = 0; r < J.rows; ++r) {
+      const int sr = src_row(J, r);
+      for (int k = k0; k < k0 + nkb * 16;) {
+        const int j = k / J.D, d = k - j * J.D;
+        const int len = min(k0 + nkb * 16 - k, J.D - d);
+        const int64_t tok = J.lastp[(size_t)sr * J.order + j];
+        uint8_t* dst = xs + r * kXRowBytes + (k - k0) * 2;
+        if (tok >= 0) bulk_g2s(dst, J.emb + (size_t)tok * J.D + d, (uint32_t)len * 2u, full);
+        else for (int q = 0; q < len * 2; q += 16) *reinterpret_cast<uint4*>(dst + q) = make_uint4(0, 0, 0, 0);
+        k += len;
+      }
+    }
+  } else {
+    // the unit's 128-column slice of the first xcopy rows: one contiguous tiled block
+    const uint32_t bytes_t = (uint32_t)J.xcopy * 256u;
+    mbar_arrive_expect_tx(full, bytes_t);
+    bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes_t, full);
+    (void)rowbytes;
+  }
+}
+
+CFB_DEV void x_producer(const Plan& P, Smem& S) {
+  uint32_t xi = 0;            // units issued
+  bool ok = true;
+  for (int p = 0; p < P.nphases && ok; ++p) {
+    const Phase& ph = P.phases[p];
+    if (ph.kind != PK_GEMM) continue;
+    const UnitRange cu = cta_units(P, ph);
+    if (cu.u0 >= cu.u1) continue;
+    // wait until the workers have passed the grid barrier in front of phase p
+    const unsigned long long t0 = globaltimer();
+    while (*S.phase_ready < p) {
+      if (ld_volatile_int(P.err) != 0) { ok = false; break; }
+      if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_SLOT); ok = false; break; }
+    }
+    if (!ok) break;
+    // the rows were written by other SMs with ordinary stores; order them before the copy
+    // engine (async proxy) reads them
+    __threadfence();
+    fence_proxy_async_global();
+    for (int jx = 0; jx < ph.njobs && ok; ++jx) {
+      const Job& J = P.jobs[ph.job0 + jx];
+      int ju0, ju1;
+      if (!job_slice(J, cu, ju0, ju1)) continue;
+      for (int ju = ju0; ju < ju1; ++ju) {
+        const int stage = xi % S.nstages;
+        if (!mbar_wait(&S.empty[stage], ((xi / S.nstages) & 1) ^ 1, P.err)) {
+          set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
+        }
+        x_unit(J, ju, S.stage(stage) + kUnitBytes, &S.full[stage]);
+        ++xi;
+      }
+    }
+    if (P.prof) P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 7] = globaltimer();
+  }
+  // every issued copy must land before this CTA may exit (copies complete on their own)
+  const uint32_t first = xi > (uint32_t)S.nstages ? xi - S.nstages : 0u;
+  for (uint32_t i = first; i < xi; ++i) mbar_wait(&S.full[i % S.nstages], (i / S.nstages) & 1);
 }
 
 // ------------------------------------------------------------------------------------------
-CFB_DEV void prep_phase(const Plan& P) {
-  const int tid = threadIdx.x;
-  const long long gtid = (long long)blockIdx.x * kConsumers + tid;
-  const long long gthreads = (long long)P.G * kConsumers;
+CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
+  const long long gtid = (long long)blockIdx.x * W.n + W.t;
+  const long long gthreads = (long long)P.G * W.n;
   for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
   for (long long i = gtid; i < P.nattncnt; i += gthreads) P.attncnt[i] = 0u;
   if (gtid == 0) *P.headcnt = 0u;
@@ -688,14 +913,19 @@ CFB_DEV void prep_phase(const Plan& P) {
           float v = __half2float(P.z0[((size_t)b * P.DL + pos) * D + col]) + X.pos[(size_t)pos * D + col];
           if (pos >= X.start) v += X.temb[col];
           X.x32[0][(size_t)row * D + col] = v;
-          X.x16[0][(size_t)row * D + col] = __float2half_rn(v);
+          X.x16[0][tidx(P.B * X.S, (int)row, col)] = __float2half_rn(v);
           n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
         }
         X.xstat[0][(size_t)row * nparts + part] = make_float2(m, M2);
       }
     }
+    // the context rows, unit-tiled for the cross K/V projection's activation copies
+    for (long long i = gtid; i < (long long)P.B * P.C * D; i += gthreads) {
+      const int r = (int)(i / D), c = (int)(i % D);
+      P.ctx16[tidx(P.B * P.C, r, c)] = P.ctx[i];
+    }
     // context LayerNorm statistics (two-pass), one warp per row
-    const int lane = tid & 31;
+    const int lane = W.t & 31;
     const long long gw = gtid >> 5, nw = gthreads >> 5;
     const long long crows = (long long)P.B * P.C;
     for (long long r = gw; r < crows; r += nw) {
@@ -726,50 +956,48 @@ CFB_DEV void prep_phase(const Plan& P) {
 }
 
 // markov bias rows of the head input: xhead[r, D + j] = w1[lastp[r, 0], j]
-CFB_DEV void markov_side(const Plan& P, const Phase& ph) {
-  const long long gtid = (long long)blockIdx.x * kConsumers + threadIdx.x;
-  const long long gthreads = (long long)P.G * kConsumers;
+CFB_DEV void markov_side(const Plan& P, const Phase& ph, const Grp& W) {
+  const long long gtid = (long long)blockIdx.x * W.n + W.t;
+  const long long gthreads = (long long)P.G * W.n;
   const long long n = (long long)ph.rows * P.rank;
   for (long long i = gtid; i < n; i += gthreads) {
     const int r = (int)(i / P.rank), j = (int)(i % P.rank);
     const int64_t tok = P.lastp[(size_t)r * P.order];
-    P.xhead[(size_t)r * P.ldxhead + P.D + j] = P.markov_w1[(size_t)tok * P.rank + j];
+    P.xhead[tidx(ph.rows, r, P.D + j)] = P.markov_w1[(size_t)tok * P.rank + j];
   }
 }
 
 // ------------------------------------------------------------------------------------------
 // after the head GEMM: every CTA publishes (max, sumexp, top-k) per beam row; the last CTA to
-// arrive merges them in CTA order, finishes the log-softmax and takes the beam step
-CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// arrive merges them in CTA order, finishes the log-softmax and takes the beam step (epilogue)
+CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H, const Grp& E) {
+  const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
   const int rows = ph.rows, TB = ph.topb;
   {
-    const int r = tid / kSlices, q = tid % kSlices;
-    if (r < ((rows + 3) / 4) * 4) {
-      head_group(H, TB, kSlices);
-      if (q == 0 && r < rows) {
-        float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + r) * kHeadPartFloats;
-        __stcg(hp + 0, H.m); __stcg(hp + 1, H.s);
+    const RowMap M = row_map(rows, E.t);
+    head_group(H, TB, M.sl);
+    if (M.q == 0 && M.r < rows) {
+      float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + M.r) * kHeadPartFloats;
+      __stcg(hp + 0, H.m); __stcg(hp + 1, H.s);
 #pragma unroll
-        for (int i = 0; i < kTopMax; ++i) { __stcg(hp + 2 + i, H.tv[i]); __stcg(hp + 2 + kTopMax + i, __int_as_float(H.ti[i])); }
-      }
+      for (int i = 0; i < kTopMax; ++i) { __stcg(hp + 2 + i, H.tv[i]); __stcg(hp + 2 + kTopMax + i, __int_as_float(H.ti[i])); }
     }
   }
   __threadfence();
-  consumer_sync(kConsumers);
-  if (tid == 0) {
+  gsync(E);
+  if (E.t == 0) {
     const unsigned old = atom_add_acqrel(P.headcnt, 1u);
-    S.flag = (old + 1 == (unsigned)P.G);
+    *S.flag = (old + 1 == (unsigned)P.G);
     if (old + 1 == (unsigned)P.G) *P.headcnt = 0u;
   }
-  consumer_sync(kConsumers);
-  const bool last = S.flag;
-  consumer_sync(kConsumers);
+  gsync(E);
+  const bool last = *S.flag;
+  gsync(E);
   if (!last) return;
   __threadfence();
-  float* lp = S.red;                                  // [rows][kTopMax] log-probs
-  int* lid = reinterpret_cast<int*>(S.slots);         // [rows][kTopMax] shortlist-local ids
-  for (int r = warp; r < rows; r += kConsumerWarps) {
+  float* lp = S.scratch;                                       // [rows][kTopMax] log-probs
+  int* lid = reinterpret_cast<int*>(S.scratch + kRowsMax * kTopMax);   // shortlist-local ids
+  for (int r = warp; r < rows; r += nw) {
     HeadState A; head_reset(A);
     for (int c = lane; c < P.G; c += 32) {
       const float* hp = P.hpart + ((size_t)c * kRowsMax + r) * kHeadPartFloats;
@@ -792,7 +1020,7 @@ CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H) {
         }
     }
   }
-  consumer_sync(kConsumers);
+  gsync(E);
   // beam step, one thread per request: pick the survivors, then (after every thread has read
   // its old rows) write the new frontier; the tree frontier changes width, so rows move
   const int step = ph.step;
@@ -801,88 +1029,131 @@ CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H) {
   const int fr = treem ? ph.fr : P.width;
   const int TB2 = treem ? ph.topb : P.width;
   const int k = treem ? min(ph.keep, fr * TB2) : P.width;
-  HeadState C; head_reset(C);       // candidates: tv = cumulative log-prob, ti = w * TB2 + i
-  int64_t old[kTopMax][8];
-  const int b = tid;
-  if (b < P.B) {
-    for (int w = 0; w < fr; ++w)
-      for (int i = 0; i < TB2; ++i)
-        top_insert(C, k, P.cum[b * P.Wmax + w] + lp[(b * fr + w) * kTopMax + i], w * TB2 + i);
-    for (int w = 0; w < fr; ++w)
-      for (int j = 0; j < order; ++j) old[w][j] = P.lastp[((size_t)b * fr + w) * order + j];
-  }
-  consumer_sync(kConsumers);
-  if (b < P.B) {
+  for (int b0 = 0; b0 < P.B; b0 += E.n) {
+    const int b = b0 + E.t;
+    HeadState C; head_reset(C);     // candidates: tv = cumulative log-prob, ti = w * TB2 + i
+    int64_t old[kTopMax][8];
+    if (b < P.B) {
+      for (int w = 0; w < fr; ++w)
+        for (int i = 0; i < TB2; ++i)
+          top_insert(C, k, P.cum[b * P.Wmax + w] + lp[(b * fr + w) * kTopMax + i], w * TB2 + i);
+      for (int w = 0; w < fr; ++w)
+        for (int j = 0; j < order; ++j) old[w][j] = P.lastp[((size_t)b * fr + w) * order + j];
+    }
+    gsync(E);
+    if (b < P.B) {
 #pragma unroll
-    for (int i = 0; i < kTopMax; ++i) {
-      if (i >= k) break;
-      // candidate ids are < fr * TB2 by construction; clamp anyway so that no value read back
-      // from memory can ever become an out-of-range index
-      const int cid = min(max(C.ti[i], 0), fr * TB2 - 1);
-      const int src = cid / TB2, ii = cid % TB2;
-      const int loc = lid[(b * fr + src) * kTopMax + ii];
-      const int64_t tok = (loc >= 0 && loc < P.R) ? P.shortlist[loc] : (int64_t)0;
-      P.cum[b * P.Wmax + i] = C.tv[i];
-      int64_t* lpn = P.lastp + ((size_t)b * k + i) * order;
-      lpn[0] = tok;
-      for (int j = 1; j < order; ++j) lpn[j] = old[src][j - 1];
-      if (treem) {
-        P.tokens[(size_t)b * 2 * P.N + ph.base + i] = tok;
-        P.tokens[(size_t)b * 2 * P.N + P.N + ph.base + i] =
-            (step == 1) ? (int64_t)-1 : (int64_t)(ph.base_prev + src);
-      } else {
-        P.toks[((size_t)(step - 1) * P.B + b) * P.width + i] = tok;
-        P.bps[((size_t)(step - 1) * P.B + b) * P.width + i] = src;
+      for (int i = 0; i < kTopMax; ++i) {
+        if (i >= k) break;
+        // candidate ids are < fr * TB2 by construction; clamp anyway so that no value read back
+        // from memory can ever become an out-of-range index
+        const int cid = min(max(C.ti[i], 0), fr * TB2 - 1);
+        const int src = cid / TB2, ii = cid % TB2;
+        const int loc = lid[(b * fr + src) * kTopMax + ii];
+        const int64_t tok = (loc >= 0 && loc < P.R) ? P.shortlist[loc] : (int64_t)0;
+        P.cum[b * P.Wmax + i] = C.tv[i];
+        int64_t* lpn = P.lastp + ((size_t)b * k + i) * order;
+        lpn[0] = tok;
+        for (int j = 1; j < order; ++j) lpn[j] = old[src][j - 1];
+        if (treem) {
+          P.tokens[(size_t)b * 2 * P.N + ph.base + i] = tok;
+          P.tokens[(size_t)b * 2 * P.N + P.N + ph.base + i] =
+              (step == 1) ? (int64_t)-1 : (int64_t)(ph.base_prev + src);
+        } else {
+          P.toks[((size_t)(step - 1) * P.B + b) * P.width + i] = tok;
+          P.bps[((size_t)(step - 1) * P.B + b) * P.width + i] = src;
+        }
+      }
+      if (!treem && ph.last) {
+        // walk the best beam back (flow_proposer.py:1261-1267); argmax keeps the first maximum
+        const int W = P.width;
+        int idx = 0;
+        for (int i = 1; i < W; ++i) if (P.cum[b * W + i] > P.cum[b * W + idx]) idx = i;
+        for (int s2 = step; s2 >= 1; --s2) {
+          P.tokens[(size_t)b * P.depth + (s2 - 1)] = P.toks[((size_t)(s2 - 1) * P.B + b) * W + idx];
+          idx = P.bps[((size_t)(s2 - 1) * P.B + b) * W + idx];
+        }
       }
     }
-    if (!treem && ph.last) {
-      // walk the best beam back (flow_proposer.py:1261-1267); argmax keeps the first maximum
-      const int W = P.width;
-      int idx = 0;
-      for (int i = 1; i < W; ++i) if (P.cum[b * W + i] > P.cum[b * W + idx]) idx = i;
-      for (int s2 = step; s2 >= 1; --s2) {
-        P.tokens[(size_t)b * P.depth + (s2 - 1)] = P.toks[((size_t)(s2 - 1) * P.B + b) * W + idx];
-        idx = P.bps[((size_t)(s2 - 1) * P.B + b) * W + idx];
-      }
-    }
+    gsync(E);
   }
   __threadfence();
-  consumer_sync(kConsumers);
 }
 
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  Smem& S = *reinterpret_cast<Smem*>(smem_raw);
   const Plan& P = *Pp;
-  const int tid = threadIdx.x;
+  const SmemLayout L = P.sm;
+  Smem S;
+  S.ring = smem_raw; S.nstages = L.nstages; S.stage_bytes = L.stage_bytes; S.rp = L.rows_pad; S.nbuf = L.nbuf;
+  S.full = reinterpret_cast<uint64_t*>(smem_raw + L.off_bar);
+  S.empty = S.full + L.nstages;
+  S.accf = S.empty + L.nstages;
+  S.acce = S.accf + 2;
+  S.slots = reinterpret_cast<float*>(smem_raw + L.off_slots);
+  S.scratch = reinterpret_cast<float*>(smem_raw + L.off_scratch);
+  S.red = reinterpret_cast<float*>(smem_raw + L.off_red);
+  S.rowstat = reinterpret_cast<float2*>(smem_raw + L.off_rowstat);
+  S.tbias = reinterpret_cast<float*>(smem_raw + L.off_tile);
+  S.tcsum = S.tbias + kTileRows;
+  S.flag = reinterpret_cast<int*>(smem_raw + L.off_misc);
+  S.phase_ready = reinterpret_cast<volatile int*>(smem_raw + L.off_misc + 4);
+  const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) { mbar_init(&S.full[i], 1); mbar_init(&S.empty[i], kConsumerWarps); }
+    // full: the weight producer's expect_tx arrive + the activation producer's arrive
+    for (int i = 0; i < L.nstages; ++i) { mbar_init(&S.full[i], 2); mbar_init(&S.empty[i], kMmaWarps); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&S.accf[i], kMmaWarps); mbar_init(&S.acce[i], 1); }
+    *S.phase_ready = -1;
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid >= kConsumers) {
-    if (tid == kConsumers) producer(P, S);
+  if (warp == kWProdWarp) {
+    if ((tid & 31) == 0) weight_producer(P, S);
     return;
   }
-  uint32_t ci = 0;
+  if (warp == kXProdWarp) {
+    if ((tid & 31) == 0) x_producer(P, S);
+    return;
+  }
+  const bool is_epi = warp >= kEpiWarp0;
+  const Grp Wk{is_epi ? kMma + (tid - kEpiWarp0 * 32) : tid, kWorkers, kBarWorkers};
+  const Grp E{tid - kEpiWarp0 * 32, kEpi, kBarEpi};
+  uint32_t ci = 0, tseq = 0;
   unsigned epoch = 0;
   bool ok = true;
   HeadState H;
   head_reset(H);
+  WaitClock wc;
+  const bool rec = P.prof && ((!is_epi && tid == 0) || (is_epi && E.t == 0));
+  wc.on = rec;
   for (int p = 0; p < P.nphases && ok; ++p) {
     const Phase& ph = P.phases[p];
+    unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * 12 : nullptr;
+    unsigned long long* stamp = (P.prof && Wk.t == 0) ? prow : nullptr;
+    wc.full = wc.slot = 0;
+    if (stamp) stamp[0] = globaltimer();
+    if (Wk.t == 0) *S.phase_ready = p;
     if (ph.kind == PK_PREP) {
-      prep_phase(P);
+      prep_phase(P, Wk);
     } else {
-      if (ph.side_markov) markov_side(P, ph);
-      if (ph.post != PO_NONE) head_reset(H);
-      gemm_phase(P, ph, ci, S, H);
-      if (ph.post != PO_NONE) head_post(P, ph, S, H);
+      if (ph.side_markov) markov_side(P, ph, Wk);
+      if (is_epi) {
+        if (ph.post != PO_NONE) head_reset(H);
+        epi_phase(P, ph, tseq, S, H, E, wc);
+        if (ph.post != PO_NONE) head_post(P, ph, S, H, E);
+        if (rec) { prow[5] = wc.slot; prow[6] = globaltimer(); }
+      } else {
+        mma_phase(P, ph, ci, tseq, S, wc);
+        if (rec) { prow[3] = wc.full; prow[4] = wc.slot; }
+      }
     }
-    ok = grid_sync(P, epoch);
+    if (stamp) stamp[1] = globaltimer();
+    ok = grid_sync(P, epoch, Wk);
+    if (stamp) stamp[2] = globaltimer();
   }
-  if (tid == 0) {
+  if (Wk.t == 0) {
+    *S.phase_ready = 1 << 30;     // release the activation producer if the loop ended early
     __threadfence();
     const unsigned old = atomicAdd(P.exitcnt, 1u);
     if (old + 1 == (unsigned)P.G) { *P.bar = 0u; *P.exitcnt = 0u; __threadfence(); }
@@ -938,6 +1209,7 @@ struct Builder {
   cfb::Plan P{};
   size_t off_phases = 0, off_jobs = 0, off_attn = 0;
   int max_tiles = 0;
+  int G = 148;                   // persistent grid the phases are cut for
   template <class T> T* dptr(size_t off) { return reinterpret_cast<T*>(base + off); }
 };
 
@@ -955,6 +1227,7 @@ cfb::Job make_job(const cfb_linear& L, int rows) {
   J.nkc = (J.Kt + cfb::kUnitK - 1) / cfb::kUnitK;
   J.rows = rows;
   J.nout = L.nout;
+  J.xR = rows; J.xcopy = rows; J.oR = rows;
   J.gin = rows > 0 ? rows : 1; J.gstride = 0; J.goff = 0;
   J.bias = L.bias;
   J.colsum = L.colsum;
@@ -973,6 +1246,15 @@ void add_phase(Builder& B, cfb::Phase ph, const std::vector<cfb::Job>& js) {
     B.jobs.push_back(j);
   }
   ph.nunits = (int)u; ph.ntiles = t;
+  // Whole tiles per CTA (no cross-CTA fixup) unless splitting tiles finishes sooner even after
+  // paying for the fixup, which costs about as much as streaming kFixupUnits units.
+  constexpr long long kFixupUnits = 24;
+  long long nkc_max = 1;
+  for (const auto& j : js) nkc_max = std::max<long long>(nkc_max, j.nkc);
+  const long long G = B.G;
+  const long long whole_units = (t + G - 1) / G * nkc_max;
+  const long long split_units = (u + G - 1) / G + kFixupUnits;
+  ph.whole = whole_units <= split_units ? 1 : 0;
   B.max_tiles = std::max(B.max_tiles, t);
   B.phases.push_back(ph);
 }
@@ -994,7 +1276,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
       return CFB_ERR_INVALID_ARG;
     if (Bq * DL > cfb::kRowsMax || Bq * C > cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
     const int hd = D / d.heads, Kmax = std::max(DL, C);
-    if ((DL + 2 * Kmax) * hd + DL * Kmax > cfb::kConsumerWarps * 16 * cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
+    if (hd % 4 || (DL + 2 * Kmax) * hd + DL * Kmax > (cfb::kSmemBudget / 4) / 2) return CFB_ERR_UNSUPPORTED;
   }
   int Wmax = 0, K = 0;
   if (beam) {
@@ -1010,7 +1292,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
     }
     K = std::min(r.depth, DL - 1);
     if (K < 1 || (!tree && K != r.depth)) return CFB_ERR_UNSUPPORTED;
-    if (Bq * Wmax > cfb::kRowsMax || Bq > cfb::kConsumers) return CFB_ERR_UNSUPPORTED;
+    if (Bq * Wmax > cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
     if (!lin_ok(d.head, d.shortlist_rows, D + d.markov_rank)) return CFB_ERR_INVALID_ARG;
     if (!lin_ok(d.path_offsets, D, d.path_order * D) || !lin_ok(d.path_up, d.path_up.nout, D) ||
         !lin_ok(d.path_down, D, d.path_up.nout) || !d.path_offset_bias || !d.path_down.bias ||
@@ -1025,13 +1307,16 @@ cfb_status lower(Builder& B, size_t* bytes) {
       sms = 148;
     G = sms;
   }
+  B.G = G;
 
   Arena& A = B.A;
   A.off = 0;
   A.take(sizeof(cfb::Plan));
   const size_t o_bar = A.take(64);
   const int nparts = D / cfb::kStatCols;
+  auto k128 = [](int k) { return (size_t)((k + 127) / 128 * 128); };   // tiled buffers pad K
   std::vector<size_t> o_x32(2 * E), o_x16(2 * E), o_xs(2 * E), o_qkv(E), o_o(E), o_qc(E), o_u(E), o_kvc(E);
+  size_t o_ctx16 = 0;
   int FM = 0;
   if (flow) {
     FM = d.experts[0].blocks[0].ffn_up.nout / D;
@@ -1040,15 +1325,16 @@ cfb_status lower(Builder& B, size_t* bytes) {
       const int rows = Bq * (e + 1) * d.chunk;
       for (int q = 0; q < 2; ++q) {
         o_x32[2 * e + q] = A.take((size_t)rows * D * 4);
-        o_x16[2 * e + q] = A.take((size_t)rows * D * 2);
+        o_x16[2 * e + q] = A.take((size_t)rows * k128(D) * 2);
         o_xs[2 * e + q] = A.take((size_t)rows * nparts * 8);
       }
       o_qkv[e] = A.take((size_t)rows * 3 * D * 4);
-      o_o[e] = A.take((size_t)rows * D * 2);
+      o_o[e] = A.take((size_t)rows * k128(D) * 2);
       o_qc[e] = A.take((size_t)rows * D * 4);
-      o_u[e] = A.take((size_t)rows * FM * D * 2);
+      o_u[e] = A.take((size_t)rows * k128(FM * D) * 2);
       o_kvc[e] = A.take((size_t)d.layers * Bq * C * 2 * D * 4);
     }
+    o_ctx16 = A.take((size_t)Bq * C * k128(D) * 2);
   }
   const size_t o_ctxs = A.take((size_t)Bq * C * 8);
   const int rank = d.markov_rank, order = d.path_order;
@@ -1060,12 +1346,13 @@ cfb_status lower(Builder& B, size_t* bytes) {
     o_cum = A.take((size_t)rowsB * 4);
     o_toks = A.take((size_t)(K + 1) * rowsB * 8);
     o_bps = A.take((size_t)(K + 1) * rowsB * 4);
-    o_h16 = A.take((size_t)rowsB * D * 2);
+    o_h16 = A.take((size_t)rowsB * k128(D) * 2);
     o_hstat = A.take((size_t)rowsB * nparts * 8);
-    o_mpath = A.take((size_t)rowsB * P2 * 2);
-    o_xhead = A.take((size_t)rowsB * (D + rank) * 2);
+    o_mpath = A.take((size_t)rowsB * k128(P2) * 2);
+    o_xhead = A.take((size_t)rowsB * k128(D + rank) * 2);
   }
   const size_t o_gpart = A.take((size_t)G * 2 * cfb::kTileRows * cfb::kRowsMax * 4);
+  const bool profile = (r.flags & CFB_RUN_PROFILE) != 0;
   const size_t o_hpart = A.take((size_t)G * cfb::kRowsMax * cfb::kHeadPartFloats * 4);
 
   auto& ph = B.phases; ph.clear();
@@ -1085,7 +1372,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
           const cfb_linear& lin = d.experts[e].blocks[l].cross_kv;
           if (!lin_ok(lin, 2 * D, D)) return CFB_ERR_INVALID_ARG;
           cfb::Job J = make_job(lin, Bq * C);
-          J.xkind = cfb::XK_F16; J.x = static_cast<const __half*>(r.ctx); J.ldx = D;
+          J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_ctx16); J.ldx = D;
           J.ln = cfb::LN_DIRECT; J.stats = B.dptr<float2>(o_ctxs);
           J.ekind = cfb::EK_STORE;
           J.out32 = B.dptr<float>(o_kvc[e]) + (size_t)l * Bq * C * 2 * D; J.ldo = 2 * D;
@@ -1103,7 +1390,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
       a.v = a.q; a.ldv = 3 * D; a.voff = 2 * D;
       a.out = B.dptr<__half>(o_o[e]); a.ldo = D;
       a.rows_per_req = S; a.keys_per_req = S; a.B = Bq; a.hd = hd; a.heads = d.heads;
-      a.causal = 1; a.nsec = 3; a.Dsec = D; a.scale = 1.0f / std::sqrt((float)hd);
+      a.causal = 1; a.nsec = 3; a.Dsec = D; a.scale = 1.0f / std::sqrt((float)hd); a.outR = Bq * S;
       a.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
       at_self[e] = (int)at.size(); at.push_back(a);
       for (int l = 0; l < L; ++l) {
@@ -1113,7 +1400,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
         c.v = c.k; c.ldv = 2 * D; c.voff = D;
         c.out = B.dptr<__half>(o_o[e]); c.ldo = D;
         c.rows_per_req = S; c.keys_per_req = C; c.B = Bq; c.hd = hd; c.heads = d.heads;
-        c.causal = 0; c.nsec = 1; c.Dsec = D; c.scale = 1.0f / std::sqrt((float)hd);
+        c.causal = 0; c.nsec = 1; c.Dsec = D; c.scale = 1.0f / std::sqrt((float)hd); c.outR = Bq * S;
         c.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
         at_cross[e * L + l] = (int)at.size(); at.push_back(c);
       }
@@ -1190,7 +1477,8 @@ cfb_status lower(Builder& B, size_t* bytes) {
         const int S = (e + 1) * d.chunk;
         if (!lin_ok(ex.out_proj, D, D) || !ex.out_proj.bias) return CFB_ERR_INVALID_ARG;
         cfb::Job J = ln_job(ex.out_proj, e);
-        J.rows = Bq * d.chunk;
+        J.rows = Bq * d.chunk; J.oR = J.rows;
+        J.xR = Bq * S; J.xcopy = Bq * S;            // copy every row; the MMA picks the chunk's
         J.gin = d.chunk; J.gstride = S; J.goff = e * d.chunk;
         J.ekind = cfb::EK_EULER; J.e_idx = e; J.step = s; J.last_step = (s == T - 1);
         J.dt = 1.0f / (float)T;
@@ -1249,6 +1537,46 @@ cfb_status lower(Builder& B, size_t* bytes) {
     }
     B.P.N = base;
   }
+  // shared-memory layout: accumulator hand-off slots (double-buffered when that still leaves a
+  // deep ring), the epilogue's scratch (attention of one head of one request, merge ids), one
+  // reduced tile and row statistics; the rest of the budget goes to the ring, each stage = a
+  // 16 KiB weights unit + the unit's activation rows
+  {
+    int rows_max = 1, xrows_max = 1;
+    for (const auto& j : B.jobs) { rows_max = std::max(rows_max, j.rows); xrows_max = std::max(xrows_max, std::max(j.rows, j.xcopy)); }
+    const int ntb = (rows_max + 7) / 8;
+    const int bucket = ntb <= 4 ? ntb : ntb <= 6 ? 6 : 8;       // mma_job<NT> instantiations
+    const int RP = bucket * 8;
+    const size_t slot_bytes = (size_t)cfb::kMmaWarps * 16 * RP * 4;
+    size_t scratch = (size_t)2 * cfb::kRowsMax * cfb::kTopMax * 4;
+    if (flow) {
+      const int hd = D / d.heads, Kmax = std::max(DL, C);
+      scratch = std::max(scratch, (size_t)((DL + 2 * Kmax) * hd + DL * Kmax) * 4);
+    }
+    scratch = (scratch + 127) / 128 * 128;
+    const int red = cfb::kTileRows * RP * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
+    const int bars = (2 * cfb::kMaxStages + 4) * 8;
+    const int stage_bytes = (cfb::kUnitBytes + xrows_max * cfb::kXRowBytes + 127) / 128 * 128;
+    auto stages_for = [&](int nbuf) {
+      const long fixed = (long)nbuf * slot_bytes + scratch + red + rowstat + misc + bars + 512 +
+                       2 * cfb::kTileRows * 4;
+      return std::min<long>(cfb::kMaxStages, (cfb::kSmemBudget - fixed) / stage_bytes);
+    };
+    int nbuf = stages_for(2) >= 6 ? 2 : 1;
+    const int nst = (int)stages_for(nbuf);
+    if (nst < 3) return CFB_ERR_UNSUPPORTED;
+    cfb::SmemLayout& Lm = B.P.sm;
+    Lm.nstages = nst; Lm.stage_bytes = stage_bytes; Lm.rows_pad = RP; Lm.nbuf = nbuf;
+    Lm.off_bar = nst * stage_bytes;
+    Lm.off_slots = (Lm.off_bar + (2 * nst + 4) * 8 + 127) / 128 * 128;
+    Lm.off_scratch = Lm.off_slots + nbuf * (int)slot_bytes;
+    Lm.off_red = Lm.off_scratch + (int)scratch;
+    Lm.off_rowstat = Lm.off_red + red;
+    Lm.off_tile = Lm.off_rowstat + rowstat;
+    Lm.off_misc = Lm.off_tile + 2 * cfb::kTileRows * 4;
+    Lm.total = Lm.off_misc + misc;
+  }
+  const size_t o_prof = profile ? A.take(ph.size() * (size_t)G * 12 * 8) : 0;
   const size_t o_tilecnt = A.take((size_t)std::max(B.max_tiles, 1) * 4);
   const size_t o_attncnt = A.take((size_t)std::max(B.P.nattncnt, 1) * 4);
   B.off_phases = A.take(ph.size() * sizeof(cfb::Phase));
@@ -1278,6 +1606,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
       if (!X.pos || !X.temb) return CFB_ERR_INVALID_ARG;
     }
   }
+  if (profile) {
+    P.prof = B.dptr<unsigned long long>(o_prof);
+    P.buf[CFB_BUF_PROF] = P.prof; P.buf_bytes[CFB_BUF_PROF] = ph.size() * (size_t)G * 12 * 8;
+  }
   P.bar = B.dptr<unsigned>(o_bar); P.exitcnt = P.bar + 1; P.headcnt = P.bar + 2;
   P.err = reinterpret_cast<int*>(P.bar + 3);
   P.tilecnt = B.dptr<unsigned>(o_tilecnt); P.ntilecnt = B.max_tiles;
@@ -1285,13 +1617,14 @@ cfb_status lower(Builder& B, size_t* bytes) {
   P.gpart = B.dptr<float>(o_gpart); P.hpart = B.dptr<float>(o_hpart);
   P.ctx = static_cast<const __half*>(r.ctx); P.z0 = static_cast<const __half*>(r.z0);
   P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs);
+  if (flow) P.ctx16 = B.dptr<__half>(o_ctx16);
   P.known0 = r.known0; P.tokens = r.tokens;
   {
     auto expose = [&](int i, size_t off, size_t nbytes) { P.buf[i] = B.dptr<void>(off); P.buf_bytes[i] = nbytes; };
     if (beam) {
-      expose(CFB_BUF_PATH_H16, o_h16, (size_t)rowsB * D * 2);
-      expose(CFB_BUF_PATH_MID, o_mpath, (size_t)rowsB * P2 * 2);
-      expose(CFB_BUF_HEAD_IN, o_xhead, (size_t)rowsB * (D + rank) * 2);
+      expose(CFB_BUF_PATH_H16, o_h16, (size_t)rowsB * k128(D) * 2);
+      expose(CFB_BUF_PATH_MID, o_mpath, (size_t)rowsB * k128(P2) * 2);
+      expose(CFB_BUF_HEAD_IN, o_xhead, (size_t)rowsB * k128(D + rank) * 2);
       expose(CFB_BUF_LASTP, o_lastp, (size_t)rowsB * order * 8);
       expose(CFB_BUF_CUM, o_cum, (size_t)rowsB * 4);
     }
@@ -1312,11 +1645,11 @@ cfb_status lower(Builder& B, size_t* bytes) {
 }
 
 struct LaunchRecord { int G, phases, smem, pad; };
-struct LaunchRec { void* ws; int G; };
-std::vector<LaunchRec> g_launch;     // grid of the plan last built in each workspace
-void remember_grid(void* ws, int G) {
-  for (auto& l : g_launch) if (l.ws == ws) { l.G = G; return; }
-  g_launch.push_back({ws, G});
+struct LaunchRec { void* ws; int G, smem; };
+std::vector<LaunchRec> g_launch;     // launch shape of the plan last built in each workspace
+void remember_launch(void* ws, int G, int smem) {
+  for (auto& l : g_launch) if (l.ws == ws) { l.G = G; l.smem = smem; return; }
+  g_launch.push_back({ws, G, smem});
 }
 
 }  // namespace
@@ -1341,16 +1674,13 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   if (st != CFB_OK) return st;
   if (need > bytes) return CFB_ERR_WORKSPACE;
   cudaError_t e;
-  static bool attr_done = false;
-  if (!attr_done) {
-    if ((e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)sizeof(cfb::Smem))) != cudaSuccess)
-      return cuda_fail(e, "smem attribute");
-    attr_done = true;
-  }
+  const int smem = B.P.sm.total;
+  if ((e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+      cudaSuccess)
+    return cuda_fail(e, "smem attribute");
   int per_sm = 0, dev = 0, sms = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfb::engine_kernel, cfb::kThreads,
-                                                         sizeof(cfb::Smem))) != cudaSuccess)
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfb::engine_kernel, cfb::kThreads, smem)) !=
+      cudaSuccess)
     return cuda_fail(e, "occupancy");
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1367,11 +1697,11 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
     return cuda_fail(e, "copy plan");
   const size_t ob = off_barrier();
   if ((e = cudaMemset(B.base + ob, 0, 64)) != cudaSuccess) return cuda_fail(e, "zero barrier");
-  LaunchRecord h{B.P.G, B.P.nphases, (int)sizeof(cfb::Smem), 0};
+  LaunchRecord h{B.P.G, B.P.nphases, smem, B.P.sm.nstages};
   if ((e = cudaMemcpy(B.base + ob + 32, &h, sizeof(h), cudaMemcpyHostToDevice)) != cudaSuccess)
     return cuda_fail(e, "copy launch record");
   if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "plan build sync");
-  remember_grid(ws, B.P.G);
+  remember_launch(ws, B.P.G, smem);
   return CFB_OK;
 }
 
@@ -1390,17 +1720,19 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
 
 cfb_status cfb_plan_run(void* ws, void* stream) {
   if (!ws) return CFB_ERR_INVALID_ARG;
-  int G = -1;
-  for (auto& l : g_launch) if (l.ws == ws) G = l.G;
+  int G = -1, smem = 0;
+  for (auto& l : g_launch) if (l.ws == ws) { G = l.G; smem = l.smem; }
   if (G < 0) {
-    cfb_status st = cfb_plan_info(ws, &G, nullptr, nullptr, nullptr);
+    cfb_status st = cfb_plan_info(ws, &G, nullptr, &smem, nullptr);
     if (st != CFB_OK) return st;
-    remember_grid(ws, G);
+    cudaError_t ea = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (ea != cudaSuccess) return cuda_fail(ea, "smem attribute");
+    remember_launch(ws, G, smem);
   }
   const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
   void* args[] = {(void*)&P};
   cudaError_t e = cudaLaunchCooperativeKernel((const void*)cfb::engine_kernel, dim3(G), dim3(cfb::kThreads),
-                                              args, sizeof(cfb::Smem), static_cast<cudaStream_t>(stream));
+                                              args, (size_t)smem, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;
   if (e != cudaSuccess) return cuda_fail(e, "engine launch");
   return CFB_OK;

@@ -26,9 +26,20 @@ def tree_levels(keep: int, topb: int, depth: int) -> list[int]:
     return out
 
 
+def untile(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Row-major [rows, cols] view of a unit-tiled fp16 activation buffer (layout in cfb.h)."""
+    kp = (cols + 127) // 128 * 128
+    t = buf.reshape(-1)[: rows * kp].view(kp // 128, rows, 16, 8)      # [slice, r, chunk, 8]
+    r = torch.arange(rows, device=buf.device).view(1, rows, 1)
+    c = torch.arange(16, device=buf.device).view(1, 1, 16)
+    src = (c ^ (r & 7)).expand(kp // 128, rows, 16)                     # chunk holding logical c
+    t = torch.gather(t, 2, src.unsqueeze(-1).expand(-1, -1, -1, 8))
+    return t.permute(1, 0, 2, 3).reshape(rows, kp)[:, :cols]
+
+
 class Plan:
     def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
-                 tree_keep: int = 4, tree_topb: int = 8, grid: int = 0):
+                 tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False):
         self.w, self.mode, self.batch = w, mode, batch
         cfg, dev = w.cfg, w.dev
         D = cfg.hidden
@@ -49,6 +60,7 @@ class Plan:
         r = _lib.Run()
         r.mode, r.batch, r.width, r.depth = mode, batch, width, depth
         r.tree_keep, r.tree_topb, r.grid = tree_keep, tree_topb, grid
+        r.flags = _lib.RUN_PROFILE if profile else 0
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
         r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
         self.run_desc = r
@@ -82,6 +94,11 @@ class Plan:
         if off < 0 or off + n * elt > self.ws.numel() or n * elt > nbytes.value:
             raise _lib.CfbError("buffer view out of range")
         return self.ws[off:off + n * elt].view(dtype).view(*shape).clone()
+
+    def phase_times(self) -> torch.Tensor:
+        """[phases, grid, 12] int64 ns of the last profiled run (see CFB_BUF_PROF in cfb.h).
+        Needs a plan built with profile=True."""
+        return self.buffer(_lib.BUF_PROF, torch.int64, (self.phases, self.grid, 12))
 
     def device_error(self) -> int:
         """Synchronous read of the device error word (0 = the last run completed normally)."""

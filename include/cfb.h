@@ -116,6 +116,7 @@ typedef struct cfb_run {
   int tree_keep;       /* CF_TREE_KEEP */
   int tree_topb;       /* CF_TREE_TOPB */
   int grid;            /* persistent CTAs; 0 = one per SM */
+  int flags;           /* CFB_RUN_PROFILE: record per-phase %globaltimer stamps (CFB_BUF_PROF) */
   /* device I/O, bound at cfb_plan_build time (graph-stable addresses) */
   const void* ctx;     /* fp16 [B, ctx_rows, D] */
   const void* z0;      /* fp16 [B, draft_len, D] initial latents */
@@ -158,16 +159,26 @@ cfb_status cfb_plan_error(void* ws, int* device_error);
 /* Launch parameters the plan resolved (grid CTAs, threads, dynamic smem bytes, phases). */
 cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases);
 
-/* Device address and size of one intermediate buffer of a built plan (stage-by-stage checks):
- * CFB_BUF_PATH_H16   fp16 [rows, D]      path offsets sum h (rows = B * beam width)
- * CFB_BUF_PATH_MID   fp16 [rows, 2D]     gelu(LN(h) W_up^T + b)
- * CFB_BUF_HEAD_IN    fp16 [rows, D + r]  [pred + residual | markov w1 row], the head input
+/* Device address and size of one intermediate buffer of a built plan (stage-by-stage checks).
+ * fp16 activation buffers are unit-tiled: for R rows and K columns (K padded up to a multiple of
+ * 128), element (r, k) is at ((k >> 7) * R + r) * 128 + ((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7).
+ * CFB_BUF_PATH_H16   fp16 tiled [rows, D]     path offsets sum h (rows = B * frontier width)
+ * CFB_BUF_PATH_MID   fp16 tiled [rows, 2D]    gelu(LN(h) W_up^T + b)
+ * CFB_BUF_HEAD_IN    fp16 tiled [rows, D + r] [pred + residual | markov w1 row], the head input
  * CFB_BUF_LASTP      int64 [rows, order] beam paths (last `order` tokens, -1 = none)
  * CFB_BUF_CUM        fp32 [rows]         beam cumulative log-probs
  * CFB_BUF_QKV0       fp32 [B*chunk, 3D]  expert 0 self-attention in-projection output
  * CFB_BUF_X32_0      fp32 [B*chunk, D]   expert 0 residual stream (even Euler steps)
  * CFB_BUF_KVC0       fp32 [L, B*ctx, 2D] expert 0 cross-attention K/V of every block
  * Values hold what the last completed run left there. */
+#define CFB_RUN_PROFILE 1
+/* CFB_BUF_PROF        uint64 [phases, grid, 12] per CTA, %globaltimer ns: [0] phase start,
+ *                     [1] work done, [2] grid barrier passed, [3] MMA warps waiting for data,
+ *                     [4] MMA warps waiting for a free accumulator slot, [5] epilogue waiting for
+ *                     partials, [6] epilogue done, [7] activation copies all issued, [8] weight
+ *                     producer waiting for a free ring slot, [9] weight units all issued,
+ *                     [10..11] unused; written only by runs of plans built with CFB_RUN_PROFILE */
+enum { CFB_BUF_PROF = 8 };
 enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
        CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
 cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);

@@ -101,3 +101,18 @@ def test_plan_rejects_unsupported_shapes():
     assert lib.cfb_plan_workspace(C.byref(d2), C.byref(fake_run(_lib.MODE_FLOW, 1)), C.byref(n)) == 2
     r = fake_run(_lib.MODE_CHAIN, 1); r.pred = None
     assert lib.cfb_plan_workspace(C.byref(d), C.byref(r), C.byref(n)) == 1
+
+
+def test_untile_inverts_the_tiled_activation_layout():
+    """The unit-tiled fp16 activation layout documented in cfb.h, and engine.untile's inverse."""
+    import torch
+    from chain_flow_b200.engine import untile
+    for R, K in ((6, 2560), (4, 160), (3, 64), (8, 256)):
+        kp = (K + 127) // 128 * 128
+        x = torch.randn(R, K)
+        buf = torch.full((R * kp,), float("nan"))
+        for r in range(R):
+            for k in range(K):
+                idx = ((k >> 7) * R + r) * 128 + ((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7)
+                buf[idx] = x[r, k]
+        assert torch.equal(untile(buf, R, K), x)

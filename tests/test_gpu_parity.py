@@ -144,14 +144,16 @@ def test_path_residual_stages(gw):
     lastp[:, 0] = g["known0"].repeat_interleave(4)
     e = g["emb"][lastp[:, 0]]
     h = e @ W["path_head.offset_proj.0.weight"].T + W["path_head.offset_proj.0.bias"]
-    h16 = p.buffer(_lib.BUF_PATH_H16, torch.float16, (rows, D)).float().cpu()
+    from chain_flow_b200.engine import untile
+    kp = lambda k: (k + 127) // 128 * 128
+    h16 = untile(p.buffer(_lib.BUF_PATH_H16, torch.float16, (rows * kp(D),)), rows, D).float().cpu()
     assert _rel(h16, h) < 2e-3, ("h", _rel(h16, h))
     n = oracle.layer_norm(h, W["path_head.norm.weight"], W["path_head.norm.bias"])
     m = F.gelu(n @ W["path_head.mlp.0.weight"].T + W["path_head.mlp.0.bias"])
-    mid = p.buffer(_lib.BUF_PATH_MID, torch.float16, (rows, 2 * D)).float().cpu()
+    mid = untile(p.buffer(_lib.BUF_PATH_MID, torch.float16, (rows * kp(2 * D),)), rows, 2 * D).float().cpu()
     assert _rel(mid, m) < 1e-2, ("mid", _rel(mid, m))
     res = m @ W["path_head.mlp.3.weight"].T + W["path_head.mlp.3.bias"]
-    xin = p.buffer(_lib.BUF_HEAD_IN, torch.float16, (rows, D + g["rank"])).float().cpu()
+    xin = untile(p.buffer(_lib.BUF_HEAD_IN, torch.float16, (rows * kp(D + g["rank"]),)), rows, D + g["rank"]).float().cpu()
     want = g["pred"][:, 1].repeat_interleave(4, 0) + res
     assert _rel(xin[:, :D], want) < 1e-2, ("head input", _rel(xin[:, :D], want))
     assert torch.equal(xin[:, D:], W["markov.w1.weight"][lastp[:, 0]].half().float())
@@ -166,7 +168,9 @@ def test_head_topk_depth1(gw):
     B, D, W = g["B"], g["H"], g["W"]
     p = run_plan(w, _lib.MODE_BEAM_CHAIN, B, known0=g["known0"], pred=g["pred"], width=4, depth=1)
     rows = B * 4
-    xin = p.buffer(_lib.BUF_HEAD_IN, torch.float16, (rows, D + g["rank"])).float().cpu()
+    from chain_flow_b200.engine import untile
+    kp = (D + g["rank"] + 127) // 128 * 128
+    xin = untile(p.buffer(_lib.BUF_HEAD_IN, torch.float16, (rows * kp,)), rows, D + g["rank"]).float().cpu()
     sl = g["sl"]
     hw = torch.cat([g["lm_w"][sl], W["markov.w2.weight"][sl]], dim=1)
     logits = xin @ hw.T
