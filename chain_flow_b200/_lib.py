@@ -19,6 +19,8 @@ STATUS_NAMES = {
     4: "CFB_ERR_CUDA", 5: "CFB_ERR_COOP_LAUNCH", 6: "CFB_ERR_DEVICE_TIMEOUT",
 }
 MODE_FLOW, MODE_CHAIN, MODE_TREE, MODE_BEAM_CHAIN, MODE_BEAM_TREE = range(5)
+INIT_GIVEN, INIT_REPEAT_LAST, INIT_DELTA = range(3)
+INIT_MODES = {"noise": INIT_GIVEN, "repeat_last": INIT_REPEAT_LAST, "delta": INIT_DELTA}
 
 # every extern "C" symbol declared in include/cfb.h
 EXPORTED = [
@@ -60,7 +62,7 @@ class Drafter(C.Structure):
 
 
 class Run(C.Structure):
-    _fields_ = [("mode", C.c_int), ("batch", C.c_int), ("width", C.c_int), ("depth", C.c_int),
+    _fields_ = [("mode", C.c_int), ("init_mode", C.c_int), ("batch", C.c_int), ("width", C.c_int), ("depth", C.c_int),
                 ("tree_keep", C.c_int), ("tree_topb", C.c_int), ("grid", C.c_int), ("flags", C.c_int),
                 ("ctx", C.c_void_p), ("z0", C.c_void_p), ("known0", C.c_void_p),
                 ("pred", C.c_void_p), ("tokens", C.c_void_p)]

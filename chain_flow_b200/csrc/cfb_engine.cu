@@ -158,6 +158,7 @@ struct Plan {
   float* gpart;             // [G][2][kTileRows*kRowsMax]
   float* hpart;             // [G][kRowsMax][kHeadPartFloats]
   const __half* ctx; const __half* z0; float* pred; float2* ctxstat; __half* ctx16;
+  int init_mode;            // CFB_INIT_GIVEN / REPEAT_LAST / DELTA
   const int64_t* known0; int64_t* lastp; float* cum; int64_t* toks; int* bps; int64_t* tokens;
   const int64_t* shortlist; const __half* markov_w1; __half* xhead; int ldxhead;
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
@@ -658,30 +659,44 @@ CFB_DEV bool job_slice(const Job& J, const UnitRange& cu, int& ju0, int& ju1) {
 }
 
 // MMA warps: multiply the job's units; hand each finished tile's partials to a slot buffer.
+// Everything the per-unit loop needs is held in registers (job fields, ring stage and parity,
+// tile / k-chunk position): the mbarrier operations are compiler memory barriers, so anything
+// read through the Job reference would otherwise be reloaded on every unit.
 template <int NT>
 CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci, uint32_t& tseq, Smem& S,
                      WaitClock& wc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice of a unit
   const int g = lane >> 2, t = lane & 3;
+  const int nkc = J.nkc, Kt = J.Kt, rows = J.rows, nst = S.nstages, rp = S.rp, nbuf = S.nbuf;
+  const int* err = P.err;
   // shared-memory row of each n-tile's activation row: tiled sources are 256 B per row with
   // chunks swizzled by row; path gathers are 272 B per row, unswizzled
   const bool tiled = J.xkind == XK_F16;
   const int xrs = tiled ? 256 : kXRowBytes, xsw = tiled ? 7 : 0;
-  int xrow[NT];
+  int xoff[NT][2];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) { const int r = nt * 8 + g; xrow[nt] = r < J.rows ? src_row(J, r) : -1; }
+  for (int nt = 0; nt < NT; ++nt) {
+    const int r = nt * 8 + g;
+    const int sr = r < rows ? src_row(J, r) : -1;
+    // byte offsets of the two 16-byte chunks of k-block 0; k-block blk adds 32*blk before the swizzle
+    xoff[nt][0] = sr < 0 ? -1 : sr * xrs + 4 * t;
+    xoff[nt][1] = sr < 0 ? 0 : (sr & xsw);
+  }
   float acc[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+  int stage = (int)(ci % (uint32_t)nst);
+  uint32_t par = (ci / (uint32_t)nst) & 1u;
+  int tile = ju0 / nkc, kc = ju0 - tile * nkc;
+  int slot = (int)(tseq % (uint32_t)nbuf);
+  uint32_t spar = (tseq / (uint32_t)nbuf) & 1u;
   for (int ju = ju0; ju < ju1; ++ju) {
-    const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
-    const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
-    const int stage = ci % S.nstages;
+    const int nkb = min(kUnitK, Kt - kc * kUnitK);
     const unsigned long long w0 = wc.now();
-    if (!mbar_wait(&S.full[stage], (ci / S.nstages) & 1, P.err)) set_err(P, DEV_TIMEOUT_FULL);
+    if (!mbar_wait(&S.full[stage], par, err)) set_err(P, DEV_TIMEOUT_FULL);
     wc.full += wc.now() - w0;
-    const uint8_t* st = S.stage(stage);
+    const uint8_t* st = S.ring + (size_t)stage * S.stage_bytes;
     const uint8_t* xs = st + kUnitBytes;
 #pragma unroll
     for (int i = 0; i < kUnitK / kKSlices; ++i) {
@@ -691,11 +706,11 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           uint32_t b0 = 0u, b1 = 0u;
-          const int sr = xrow[nt];
-          if (sr >= 0) {
-            const uint8_t* xr = xs + sr * xrs + 4 * t;
-            b0 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk) ^ (sr & xsw)) << 4));
-            b1 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk + 1) ^ (sr & xsw)) << 4));
+          if (xoff[nt][0] >= 0) {
+            const uint8_t* xr = xs + xoff[nt][0];
+            const int sw = xoff[nt][1];
+            b0 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk) ^ sw) << 4));
+            b1 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk + 1) ^ sw) << 4));
           }
           mma16816(acc[nt], a, b0, b1);
         }
@@ -703,29 +718,32 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.empty[stage]);
+    if (++stage == nst) { stage = 0; par ^= 1u; }
     ++ci;
-    if (kc == J.nkc - 1 || ju == ju1 - 1) {
-      const int b = tseq % S.nbuf;
+    if (kc == nkc - 1 || ju == ju1 - 1) {
       const unsigned long long w1 = wc.now();
-      if (!mbar_wait(&S.acce[b], ((tseq / S.nbuf) & 1) ^ 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
+      if (!mbar_wait(&S.acce[slot], spar ^ 1u, err)) set_err(P, DEV_TIMEOUT_SLOT);
       wc.slot += wc.now() - w1;
-      float* sl = S.slot(b) + warp * 16 * S.rp;
+      float* sl = S.slots + ((size_t)slot * kMmaWarps + warp) * 16 * rp;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int r0 = nt * 8 + 2 * t;
-        if (r0 < S.rp) {
-          sl[g * S.rp + r0] = acc[nt][0];
-          sl[g * S.rp + r0 + 1] = acc[nt][1];
-          sl[(g + 8) * S.rp + r0] = acc[nt][2];
-          sl[(g + 8) * S.rp + r0 + 1] = acc[nt][3];
+        if (r0 < rp) {
+          sl[g * rp + r0] = acc[nt][0];
+          sl[g * rp + r0 + 1] = acc[nt][1];
+          sl[(g + 8) * rp + r0] = acc[nt][2];
+          sl[(g + 8) * rp + r0 + 1] = acc[nt][3];
         }
         acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.accf[b]);
+      if (lane == 0) mbar_arrive(&S.accf[slot]);
+      if (++slot == nbuf) { slot = 0; spar ^= 1u; }
       ++tseq;
     }
+    if (++kc == nkc) { kc = 0; ++tile; }
   }
+  (void)tile;
 }
 
 CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& tseq, Smem& S, WaitClock& wc) {
@@ -766,7 +784,12 @@ CFB_DEV void epi_phase(const Plan& P, const Phase& ph, uint32_t& tseq, Smem& S, 
 // the ring with cp.async.bulk, running ahead of the consumers across phase boundaries.
 CFB_DEV void weight_producer(const Plan& P, Smem& S) {
   uint32_t pi = 0;
+  int stage = 0;
+  uint32_t par = 1u;                 // a fresh mbarrier's previous phase counts as complete
   bool ok = true;
+  const int nst = S.nstages;
+  const int* err = P.err;
+  const bool prof = P.prof != nullptr;
   for (int p = 0; p < P.nphases && ok; ++p) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
@@ -776,21 +799,24 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S) {
       const Job& J = P.jobs[ph.job0 + jx];
       int ju0, ju1;
       if (!job_slice(J, cu, ju0, ju1)) continue;
+      const int nkc = J.nkc, Kt = J.Kt;
+      const uint8_t* wbase = reinterpret_cast<const uint8_t*>(J.w);
+      const size_t tile_bytes = (size_t)J.Kstride * 4 * kBlockBytes;
+      int tile = ju0 / nkc, kc = ju0 - tile * nkc;
       for (int ju = ju0; ju < ju1; ++ju) {
-        const int tile = ju / J.nkc, kc = ju - tile * J.nkc;
-        const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(J.w) +
-            ((size_t)tile * J.Kstride + (size_t)kc * kUnitK) * 4 * kBlockBytes;
+        const int nkb = min(kUnitK, Kt - kc * kUnitK);
+        const uint8_t* src = wbase + (size_t)tile * tile_bytes + (size_t)kc * kUnitK * 4 * kBlockBytes;
         const uint32_t bytes = (uint32_t)(nkb * 4 * kBlockBytes);
-        const int stage = pi % S.nstages;
-        const unsigned long long w0 = P.prof ? globaltimer() : 0ull;
-        if (!mbar_wait(&S.empty[stage], ((pi / S.nstages) & 1) ^ 1, P.err)) {
+        const unsigned long long w0 = prof ? globaltimer() : 0ull;
+        if (!mbar_wait(&S.empty[stage], par, err)) {
           set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
         }
-        if (P.prof) waited += globaltimer() - w0;
+        if (prof) waited += globaltimer() - w0;
         mbar_arrive_expect_tx(&S.full[stage], bytes);
-        bulk_g2s(S.stage(stage), src, bytes, &S.full[stage]);
+        bulk_g2s(S.ring + (size_t)stage * S.stage_bytes, src, bytes, &S.full[stage]);
         ++pi;
+        if (++stage == nst) { stage = 0; par ^= 1u; }
+        if (++kc == nkc) { kc = 0; ++tile; }
       }
     }
     if (P.prof) {
@@ -850,6 +876,8 @@ CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
 
 CFB_DEV void x_producer(const Plan& P, Smem& S) {
   uint32_t xi = 0;            // units issued
+  int xstage = 0;
+  uint32_t xpar = 1u;         // a fresh mbarrier's previous phase counts as complete
   bool ok = true;
   for (int p = 0; p < P.nphases && ok; ++p) {
     const Phase& ph = P.phases[p];
@@ -872,12 +900,12 @@ CFB_DEV void x_producer(const Plan& P, Smem& S) {
       int ju0, ju1;
       if (!job_slice(J, cu, ju0, ju1)) continue;
       for (int ju = ju0; ju < ju1; ++ju) {
-        const int stage = xi % S.nstages;
-        if (!mbar_wait(&S.empty[stage], ((xi / S.nstages) & 1) ^ 1, P.err)) {
+        if (!mbar_wait(&S.empty[xstage], xpar, P.err)) {
           set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
         }
-        x_unit(J, ju, S.stage(stage) + kUnitBytes, &S.full[stage]);
+        x_unit(J, ju, S.ring + (size_t)xstage * S.stage_bytes + kUnitBytes, &S.full[xstage]);
         ++xi;
+        if (++xstage == S.nstages) { xstage = 0; xpar ^= 1u; }
       }
     }
     if (P.prof) P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 7] = globaltimer();
@@ -888,6 +916,16 @@ CFB_DEV void x_producer(const Plan& P, Smem& S) {
 }
 
 // ------------------------------------------------------------------------------------------
+// initial latent z0[b, pos, col] (reference TreeFlowDrafter.init_latents, tree_flow.py:150-161):
+// given (noise drawn by the caller), the last context row, or last + (pos+1) * (last - previous)
+CFB_DEV float z0_at(const Plan& P, int b, int pos, int col) {
+  if (P.init_mode == CFB_INIT_GIVEN) return __half2float(P.z0[((size_t)b * P.DL + pos) * P.D + col]);
+  const float last = __half2float(P.ctx[((size_t)b * P.C + P.C - 1) * P.D + col]);
+  if (P.init_mode == CFB_INIT_REPEAT_LAST || P.C < 2) return last;
+  const float prev = __half2float(P.ctx[((size_t)b * P.C + P.C - 2) * P.D + col]);
+  return last + (float)(pos + 1) * (last - prev);
+}
+
 CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
   const long long gtid = (long long)blockIdx.x * W.n + W.t;
   const long long gthreads = (long long)P.G * W.n;
@@ -898,7 +936,8 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
   const int D = P.D, nparts = D / kStatCols;
   if (flow) {
     const long long nz = (long long)P.B * P.DL * D;
-    for (long long i = gtid; i < nz; i += gthreads) P.pred[i] = __half2float(P.z0[i]);
+    for (long long i = gtid; i < nz; i += gthreads)
+      P.pred[i] = z0_at(P, (int)(i / ((long long)P.DL * D)), (int)((i / D) % P.DL), (int)(i % D));
     // step-0 inputs of every expert: z0 + position embedding (+ time embedding on its chunk)
     for (int e = 0; e < P.n_experts; ++e) {
       const ExpertRT& X = P.ex[e];
@@ -910,7 +949,7 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
         float n = 0.f, m = 0.f, M2 = 0.f;
         for (int f = 0; f < kStatCols; ++f) {
           const int col = part * kStatCols + f;
-          float v = __half2float(P.z0[((size_t)b * P.DL + pos) * D + col]) + X.pos[(size_t)pos * D + col];
+          float v = z0_at(P, b, pos, col) + X.pos[(size_t)pos * D + col];
           if (pos >= X.start) v += X.temb[col];
           X.x32[0][(size_t)row * D + col] = v;
           X.x16[0][tidx(P.B * X.S, (int)row, col)] = __float2half_rn(v);
@@ -1272,7 +1311,9 @@ cfb_status lower(Builder& B, size_t* bytes) {
   if (E <= 0 || E > cfb::kMaxExperts || d.chunk <= 0 || E * d.chunk != DL) return CFB_ERR_UNSUPPORTED;
   if (!r.pred) return CFB_ERR_INVALID_ARG;
   if (flow) {
-    if (!r.ctx || !r.z0 || !d.experts || d.heads <= 0 || D % d.heads || d.layers <= 0 || d.steps <= 0)
+    if (!r.ctx || !d.experts || d.heads <= 0 || D % d.heads || d.layers <= 0 || d.steps <= 0)
+      return CFB_ERR_INVALID_ARG;
+    if (r.init_mode < CFB_INIT_GIVEN || r.init_mode > CFB_INIT_DELTA || (r.init_mode == CFB_INIT_GIVEN && !r.z0))
       return CFB_ERR_INVALID_ARG;
     if (Bq * DL > cfb::kRowsMax || Bq * C > cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
     const int hd = D / d.heads, Kmax = std::max(DL, C);
@@ -1616,7 +1657,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
   P.attncnt = B.dptr<unsigned>(o_attncnt);
   P.gpart = B.dptr<float>(o_gpart); P.hpart = B.dptr<float>(o_hpart);
   P.ctx = static_cast<const __half*>(r.ctx); P.z0 = static_cast<const __half*>(r.z0);
-  P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs);
+  P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs); P.init_mode = r.init_mode;
   if (flow) P.ctx16 = B.dptr<__half>(o_ctx16);
   P.known0 = r.known0; P.tokens = r.tokens;
   {

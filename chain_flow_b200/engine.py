@@ -39,7 +39,8 @@ def untile(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
 
 class Plan:
     def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
-                 tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False):
+                 tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False,
+                 init_mode: int = 0):
         self.w, self.mode, self.batch = w, mode, batch
         cfg, dev = w.cfg, w.dev
         D = cfg.hidden
@@ -59,6 +60,7 @@ class Plan:
             self.tokens = torch.zeros(batch, depth, dtype=torch.int64, device=dev)
         r = _lib.Run()
         r.mode, r.batch, r.width, r.depth = mode, batch, width, depth
+        r.init_mode = init_mode
         r.tree_keep, r.tree_topb, r.grid = tree_keep, tree_topb, grid
         r.flags = _lib.RUN_PROFILE if profile else 0
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()

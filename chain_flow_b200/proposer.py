@@ -1,0 +1,206 @@
+"""FlowDrafterProposer: the reference's drafting surface on the sm_100a engine.
+
+Mirrors ``chain_flow.vllm_plugin.flow_proposer.FlowDrafterProposer`` (reference
+src/chain_flow/vllm_plugin/flow_proposer.py:328-2569) where the drafting path is concerned:
+
+* ``_beam_chains(ctx[B,C,H], known0[B]) -> [B, K]`` int64 token ids (reference :1188-1269);
+* ``_beam_tree(ctx, known0) -> [B, 2N]``: N BFS-ordered tokens, then their parents (:1273-1332);
+* ``predict_hidden(ctx) -> [B, draft_length, H]`` (drafters/tree_flow.py:243);
+* the drafter checkpoint layout (``model.safetensors`` keys ``drafter.*`` +
+  ``chained_flow_tree_config.json``) and the shortlist file format and guard
+  (``CF_SHORTLIST`` -> ``<ckpt>/shortlist.pt``), with the declared-identity check (:1006-1016, :739-765);
+* the ``CF_*`` knobs of the path: ``CF_WIDTH``, ``CF_FLOW_STEPS``, ``CF_TREE_KEEP``, ``CF_TREE_TOPB``,
+  ``CF_TREE_DEPTH``, ``CF_TWOPASS_M`` (only 0 is implemented: the one-pass head), ``CF_PATH_TRIM``
+  (always on: it is exact).
+
+Every draft is ONE persistent kernel launch (flow + beam); there is no CPU fallback. The engine
+plans (and their graph-stable I/O buffers) are cached per (mode, batch).
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import torch
+
+from . import _lib, shortlist as _sl
+from .engine import Plan
+from .weights import DraftConfig, DrafterWeights
+
+
+def _env_int(name: str, default: int) -> int:
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+class FlowDrafterProposer:
+    """Drafting engine with the reference proposer's interface.
+
+    Build it with ``from_components`` (state dict + target embedding / lm_head tensors) or
+    ``from_checkpoint`` (a drafter directory); ``FlowDrafterProposer(vllm_config)`` reads the
+    speculative config and builds lazily from the loaded target model on first ``propose``.
+    """
+
+    def __init__(self, vllm_config=None, **kw):
+        self.vllm_config = vllm_config
+        self.width = _env_int("CF_WIDTH", 4)
+        self.tree_keep = _env_int("CF_TREE_KEEP", 4)
+        self.tree_topb = _env_int("CF_TREE_TOPB", 8)
+        self.tree_depth = _env_int("CF_TREE_DEPTH", 4)
+        self.tree = os.environ.get("VLLM_SPEC_TREE", "0") == "1"
+        if _env_int("CF_TWOPASS_M", 0) != 0:
+            raise _lib.CfbError("CF_TWOPASS_M > 0 (two-pass candidate head) is not implemented by this "
+                                "engine; set CF_TWOPASS_M=0 for the one-pass fused head")
+        self.K = 5
+        if vllm_config is not None:
+            spec = vllm_config.speculative_config
+            self.K = int(spec.num_speculative_tokens) - (1 if self.tree else 0)
+        self.weights: DrafterWeights | None = None
+        self._plans: dict = {}
+        self._gen = None
+        self.init_mode = "delta"
+        self.noise_scale = 1.0
+        for k, v in kw.items():
+            setattr(self, k, v)
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_components(cls, state_dict: dict, model_args: dict, embed: torch.Tensor, lm_head: torch.Tensor,
+                        shortlist_ids: torch.Tensor | None = None, *, width: int | None = None, K: int = 5,
+                        tree_keep: int | None = None, tree_topb: int | None = None,
+                        tree_depth: int | None = None, device=None, seed: int = 0) -> "FlowDrafterProposer":
+        self = cls()
+        hidden = int(embed.shape[1])
+        args = dict(model_args)
+        if os.environ.get("CF_FLOW_STEPS"):
+            steps = int(os.environ["CF_FLOW_STEPS"])
+            if steps < 1:
+                raise ValueError(f"CF_FLOW_STEPS must be >= 1, got {steps}")
+            args["num_flow_steps"] = steps
+        cfg = DraftConfig.from_model_args(args, hidden)
+        if shortlist_ids is None:
+            shortlist_ids = torch.arange(embed.shape[0])        # full head
+        self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device)
+        self.cfg = cfg
+        self.dev = self.weights.dev
+        self.init_mode = args.get("init_mode", "delta")
+        self.noise_scale = float(args.get("noise_scale", 1.0))
+        if self.init_mode not in _lib.INIT_MODES:
+            raise ValueError(f"init_mode {self.init_mode!r} is not one of {sorted(_lib.INIT_MODES)}")
+        if width is not None: self.width = width
+        if tree_keep is not None: self.tree_keep = tree_keep
+        if tree_topb is not None: self.tree_topb = tree_topb
+        if tree_depth is not None: self.tree_depth = tree_depth
+        self.K = K
+        if self.K > cfg.draft_length - 1:
+            raise ValueError(f"K={self.K} but this drafter can only emit {cfg.draft_length - 1} chain tokens "
+                             f"(draft_length={cfg.draft_length}; depth 0 reconstructs the committed token)")
+        if self.tree_keep > self.tree_topb:
+            raise ValueError(f"CF_TREE_KEEP={self.tree_keep} > CF_TREE_TOPB={self.tree_topb}: depth 1 "
+                             f"expands a single node and can hold at most {self.tree_topb} children")
+        self._gen = torch.Generator(device=self.dev).manual_seed(seed)
+        return self
+
+    @classmethod
+    def from_checkpoint(cls, drafter_dir: str, embed: torch.Tensor, lm_head: torch.Tensor, **kw):
+        """Load ``<dir>/model.safetensors`` (``drafter.*`` keys) and ``chained_flow_tree_config.json``
+        and resolve the shortlist (``CF_SHORTLIST``, else ``<dir>/shortlist.pt``, else the full head),
+        refusing a list built for another vocabulary or not matching the checkpoint's declaration."""
+        from safetensors.torch import load_file
+        with open(os.path.join(drafter_dir, "chained_flow_tree_config.json")) as f:
+            conf = json.load(f)
+        sd = load_file(os.path.join(drafter_dir, "model.safetensors"))
+        sub = {k[len("drafter."):]: v for k, v in sd.items() if k.startswith("drafter.")}
+        if not sub:
+            raise KeyError(f"{drafter_dir}/model.safetensors holds no 'drafter.' keys")
+        V = int(embed.shape[0])
+        ids = None
+        cands = []
+        if os.environ.get("CF_SHORTLIST"):
+            if not os.path.exists(os.environ["CF_SHORTLIST"]):
+                raise FileNotFoundError(f"CF_SHORTLIST={os.environ['CF_SHORTLIST']} does not exist")
+            cands.append(os.environ["CF_SHORTLIST"])
+        elif "CF_SHORTLIST" not in os.environ and os.path.exists(os.path.join(drafter_dir, "shortlist.pt")):
+            cands.append(os.path.join(drafter_dir, "shortlist.pt"))
+        for path in cands:
+            got, meta = _sl.load(path)
+            bad = _sl.check(got, meta, V)
+            if bad:
+                raise ValueError(f"shortlist {path} refused: {bad}")
+            got = got[(got >= 0) & (got < V)].unique()
+            decl = conf.get("shortlist") or {}
+            if decl:
+                sha = _sl.ids_content_sha(got)
+                if (decl.get("rows") and int(decl["rows"]) != got.numel()) or \
+                        (decl.get("ids_sha256") and decl["ids_sha256"] != sha):
+                    raise RuntimeError(f"shortlist {path} does not match what this drafter declares "
+                                       f"({decl}); got {got.numel()} rows, ids-sha256 {sha}")
+            ids = got
+            break
+        return cls.from_components(sub, conf["model_args"], embed, lm_head, ids, **kw)
+
+    # ------------------------------------------------------------------ engine plans
+    def _plan(self, mode: int, B: int) -> Plan:
+        key = (mode, B)
+        p = self._plans.get(key)
+        if p is None:
+            init = _lib.INIT_MODES[self.init_mode]
+            p = Plan(self.weights, mode, B, width=self.width,
+                     depth=self.tree_depth if mode == _lib.MODE_TREE else self.K,
+                     tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+            self._plans[key] = p
+        return p
+
+    def _load_inputs(self, p: Plan, ctx: torch.Tensor, known0: torch.Tensor | None):
+        _lib.require_cuda(ctx, "ctx")
+        p.ctx.copy_(ctx.to(torch.float16), non_blocking=True)
+        if known0 is not None:
+            p.known0.copy_(known0.view(-1).to(torch.int64), non_blocking=True)
+        if self.init_mode == "noise":
+            # the reference draws torch.randn at every draft (tree_flow.py:154-155); the
+            # generator here is seeded per proposer so drafts are reproducible
+            p.z0.normal_(generator=self._gen).mul_(self.noise_scale)
+
+    # ------------------------------------------------------------------ drafting interface
+    @torch.inference_mode()
+    def predict_hidden(self, ctx: torch.Tensor) -> torch.Tensor:
+        p = self._plan(_lib.MODE_FLOW, ctx.shape[0])
+        self._load_inputs(p, ctx, None)
+        p.run()
+        return p.pred
+
+    @torch.inference_mode()
+    def _beam_chains(self, ctx: torch.Tensor, known0: torch.Tensor) -> torch.Tensor:
+        """[B, K] int64 chain drafts; ``known0`` is the token vLLM just committed."""
+        p = self._plan(_lib.MODE_CHAIN, ctx.shape[0])
+        self._load_inputs(p, ctx, known0)
+        p.run()
+        return p.tokens
+
+    @torch.inference_mode()
+    def _beam_tree(self, ctx: torch.Tensor, known0: torch.Tensor) -> torch.Tensor:
+        """[B, 2N] int64: N BFS-ordered draft tokens followed by their N parent indices (-1 = root)."""
+        p = self._plan(_lib.MODE_TREE, ctx.shape[0])
+        self._load_inputs(p, ctx, known0)
+        p.run()
+        return p.tokens
+
+    def device_error(self) -> int:
+        """Synchronous: non-zero if a bounded device-side wait expired in any cached plan's last run."""
+        return max((p.device_error() for p in self._plans.values()), default=0)
+
+    # ------------------------------------------------------------------ vLLM entry point
+    def propose(self, sampled_token_ids, num_tokens_no_spec=None, token_ids_cpu=None, slot_mappings=None,
+                **kw):
+        """vLLM ``custom_class`` entry (reference flow_proposer.py:1699). The context window of each
+        request (its last ``context_size`` final hidden states, front-padded with the oldest one) is
+        taken from ``kw['context_hidden']`` [B, C, H] when the caller supplies it; the vLLM
+        runner-hook plumbing that assembles it inside a live engine is not part of this package."""
+        ctx = kw.get("context_hidden")
+        if ctx is None:
+            raise NotImplementedError(
+                "propose() needs context_hidden=[B, C, H]: the vLLM hidden-state hook and context ring "
+                "of the reference proposer are not implemented by this engine")
+        known0 = torch.as_tensor([int(t[-1]) for t in sampled_token_ids], device=ctx.device)
+        out = self._beam_tree(ctx, known0) if self.tree else self._beam_chains(ctx, known0)
+        return out.tolist()

@@ -108,8 +108,16 @@ typedef enum cfb_mode {
   CFB_MODE_BEAM_TREE = 4    /* tree beam over a given pred */
 } cfb_mode;
 
+/* initial latents z0 of the flow (reference TreeFlowDrafter.init_latents, tree_flow.py:150-161) */
+typedef enum cfb_init {
+  CFB_INIT_GIVEN = 0,        /* z0 supplied by the caller (init_mode='noise': the caller draws it) */
+  CFB_INIT_REPEAT_LAST = 1,  /* every position = the last context row */
+  CFB_INIT_DELTA = 2         /* position i = last + (i+1) * (last - previous context row) */
+} cfb_init;
+
 typedef struct cfb_run {
   int mode;            /* cfb_mode */
+  int init_mode;       /* cfb_init */
   int batch;           /* requests B */
   int width;           /* chain beam width (CF_WIDTH, reference flow_proposer.py:374) */
   int depth;           /* chain: emitted tokens K; tree: levels (CF_TREE_DEPTH) */
@@ -119,7 +127,7 @@ typedef struct cfb_run {
   int flags;           /* CFB_RUN_PROFILE: record per-phase %globaltimer stamps (CFB_BUF_PROF) */
   /* device I/O, bound at cfb_plan_build time (graph-stable addresses) */
   const void* ctx;     /* fp16 [B, ctx_rows, D] */
-  const void* z0;      /* fp16 [B, draft_len, D] initial latents */
+  const void* z0;      /* fp16 [B, draft_len, D] initial latents (CFB_INIT_GIVEN only) */
   const int64_t* known0;  /* int64 [B] committed token per request */
   float* pred;         /* fp32 [B, draft_len, D]: output of the flow, input of BEAM_* modes */
   int64_t* tokens;     /* int64 chain [B, depth]; tree [B, 2N] (N tokens, then N parents) */
