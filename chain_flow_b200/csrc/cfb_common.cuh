@@ -56,17 +56,22 @@ CFB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 CFB_DEV int ld_volatile_int(const int* p);
 
-// Bounded wait; returns false on timeout, or at once when `err` (if given) is already set,
-// so that after the first failure the rest of a launch runs through without waiting.
+// Polls between two looks at the clock and the error word in a bounded wait. Each look costs a
+// global-memory round trip, during which the waiter cannot notice that its wait is over.
+constexpr unsigned kPollsPerCheck = 64;
+
+// Bounded wait; returns false on timeout, or soon after `err` (if given) is set, so that after
+// the first failure the rest of a launch runs through without waiting.
 CFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  if (err && ld_volatile_int(err) != 0) return false;
   const unsigned long long t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitBudgetNs) return false;
-    if (err && ld_volatile_int(err) != 0) return false;
+  for (unsigned it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (it % kPollsPerCheck == 0) {
+      if (globaltimer() - t0 > kWaitBudgetNs) return false;
+      if (err && ld_volatile_int(err) != 0) return false;
+    }
   }
-  return true;
 }
 
 // ---- bulk copy global -> shared (the TMA unit, 1-D form; no multicast) -------------------

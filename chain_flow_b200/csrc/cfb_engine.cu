@@ -189,12 +189,19 @@ struct HeadState { float m, s; float tv[kTopMax]; int ti[kTopMax]; };
 // Profiling (plans built with CFB_RUN_PROFILE): ns spent waiting, per role, reset every phase.
 struct WaitClock {
   unsigned long long full = 0, slot = 0;
+  unsigned long long first = 0, last = 0;   // when the phase's first / last unit was ready
   bool on = false;
   CFB_DEV unsigned long long now() const { return on ? globaltimer() : 0ull; }
 };
 
 // ------------------------------------------------------------------------------------------
-CFB_DEV void set_err(const Plan& P, int code) { atomicCAS(P.err, 0, code); }
+// The grid barrier counter's top bit: set with the error word, so that every CTA waiting at (or
+// arriving at) a grid barrier sees the failure in the value it polls anyway.
+constexpr unsigned kBarErrBit = 0x80000000u;
+CFB_DEV void set_err(const Plan& P, int code) {
+  atomicCAS(P.err, 0, code);
+  atomicOr(P.bar, kBarErrBit);
+}
 
 CFB_DEV long long cta_start(long long U, int G, int c) { return (long long)c * U / G; }
 CFB_DEV int cta_of(long long u, long long U, int G) {       // the CTA whose range holds unit u
@@ -212,18 +219,19 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W) {
   if (W.t == 0) {
     ++epoch;
     __threadfence();
-    atom_add_release(P.bar, 1u);
     const unsigned target = epoch * (unsigned)P.G;
-    int ok = 1;
-    if (ld_acquire(P.bar) < target) {
+    unsigned v = atom_add_acqrel(P.bar, 1u) + 1u;
+    if (v < target) {
       const unsigned long long t0 = globaltimer();
-      while (ld_acquire(P.bar) < target) {
-        if (ld_volatile_int(P.err) != 0) { ok = 0; break; }
-        if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_GRID); ok = 0; break; }
+      for (unsigned it = 1; (v = ld_acquire(P.bar)) < target; ++it) {
+        if (it % kPollsPerCheck == 0 && globaltimer() - t0 > kWaitBudgetNs) {
+          set_err(P, DEV_TIMEOUT_GRID);
+          v = kBarErrBit;
+          break;
+        }
       }
     }
-    if (ld_volatile_int(P.err) != 0) ok = 0;
-    s_ok = ok;
+    s_ok = (v & kBarErrBit) == 0u;
   }
   gsync(W);
   return s_ok != 0;
@@ -695,7 +703,12 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
     const int nkb = min(kUnitK, Kt - kc * kUnitK);
     const unsigned long long w0 = wc.now();
     if (!mbar_wait(&S.full[stage], par, err)) set_err(P, DEV_TIMEOUT_FULL);
-    wc.full += wc.now() - w0;
+    if (wc.on) {
+      const unsigned long long w1 = wc.now();
+      wc.full += w1 - w0;
+      if (wc.first == 0) wc.first = w1;
+      wc.last = w1;
+    }
     const uint8_t* st = S.ring + (size_t)stage * S.stage_bytes;
     const uint8_t* xs = st + kUnitBytes;
 #pragma unroll
@@ -886,7 +899,8 @@ CFB_DEV void x_producer(const Plan& P, Smem& S) {
     if (cu.u0 >= cu.u1) continue;
     // wait until the workers have passed the grid barrier in front of phase p
     const unsigned long long t0 = globaltimer();
-    while (*S.phase_ready < p) {
+    for (unsigned it = 1; *S.phase_ready < p; ++it) {
+      if (it % kPollsPerCheck) continue;
       if (ld_volatile_int(P.err) != 0) { ok = false; break; }
       if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_SLOT); ok = false; break; }
     }
@@ -938,24 +952,31 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
     const long long nz = (long long)P.B * P.DL * D;
     for (long long i = gtid; i < nz; i += gthreads)
       P.pred[i] = z0_at(P, (int)(i / ((long long)P.DL * D)), (int)((i / D) % P.DL), (int)(i % D));
-    // step-0 inputs of every expert: z0 + position embedding (+ time embedding on its chunk)
+    // step-0 inputs of every expert: z0 + position embedding (+ time embedding on its chunk),
+    // with the (mean, M2) of each 64-column part; one warp per (row, part), two columns a lane
+    const int lane = W.t & 31;
+    const long long gw = gtid >> 5, nw = gthreads >> 5;
     for (int e = 0; e < P.n_experts; ++e) {
       const ExpertRT& X = P.ex[e];
       const long long items = (long long)P.B * X.S * nparts;
-      for (long long it = gtid; it < items; it += gthreads) {
+      for (long long it = gw; it < items; it += nw) {
         const int part = (int)(it % nparts);
         const long long row = it / nparts;
         const int b = (int)(row / X.S), pos = (int)(row % X.S);
-        float n = 0.f, m = 0.f, M2 = 0.f;
-        for (int f = 0; f < kStatCols; ++f) {
-          const int col = part * kStatCols + f;
-          float v = z0_at(P, b, pos, col) + X.pos[(size_t)pos * D + col];
-          if (pos >= X.start) v += X.temb[col];
-          X.x32[0][(size_t)row * D + col] = v;
-          X.x16[0][tidx(P.B * X.S, (int)row, col)] = __float2half_rn(v);
-          n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
-        }
-        X.xstat[0][(size_t)row * nparts + part] = make_float2(m, M2);
+        const int col = part * kStatCols + 2 * lane;
+        float v0 = z0_at(P, b, pos, col) + X.pos[(size_t)pos * D + col];
+        float v1 = z0_at(P, b, pos, col + 1) + X.pos[(size_t)pos * D + col + 1];
+        if (pos >= X.start) { v0 += X.temb[col]; v1 += X.temb[col + 1]; }
+        *reinterpret_cast<float2*>(X.x32[0] + (size_t)row * D + col) = make_float2(v0, v1);
+        *reinterpret_cast<__half2*>(X.x16[0] + tidx(P.B * X.S, (int)row, col)) = __floats2half2_rn(v0, v1);
+        float sum = v0 + v1;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        const float mean = sum / (float)kStatCols;
+        float m2 = (v0 - mean) * (v0 - mean) + (v1 - mean) * (v1 - mean);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, off);
+        if (lane == 0) X.xstat[0][(size_t)row * nparts + part] = make_float2(mean, m2);
       }
     }
     // the context rows, unit-tiled for the cross K/V projection's activation copies
@@ -964,8 +985,6 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
       P.ctx16[tidx(P.B * P.C, r, c)] = P.ctx[i];
     }
     // context LayerNorm statistics (two-pass), one warp per row
-    const int lane = W.t & 31;
-    const long long gw = gtid >> 5, nw = gthreads >> 5;
     const long long crows = (long long)P.B * P.C;
     for (long long r = gw; r < crows; r += nw) {
       float s = 0.f;
@@ -1144,15 +1163,19 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     for (int i = 0; i < L.nstages; ++i) { mbar_init(&S.full[i], 2); mbar_init(&S.empty[i], kMmaWarps); }
     for (int i = 0; i < 2; ++i) { mbar_init(&S.accf[i], kMmaWarps); mbar_init(&S.acce[i], 1); }
     *S.phase_ready = -1;
+    // a plan whose earlier run failed stays failed: this run leaves every output untouched
+    *S.flag = ld_volatile_int(P.err) != 0;
     fence_mbar_init();
   }
   __syncthreads();
+  const bool dead = *S.flag != 0;
+  __syncthreads();
   if (warp == kWProdWarp) {
-    if ((tid & 31) == 0) weight_producer(P, S);
+    if ((tid & 31) == 0 && !dead) weight_producer(P, S);
     return;
   }
   if (warp == kXProdWarp) {
-    if ((tid & 31) == 0) x_producer(P, S);
+    if ((tid & 31) == 0 && !dead) x_producer(P, S);
     return;
   }
   const bool is_epi = warp >= kEpiWarp0;
@@ -1160,7 +1183,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   const Grp E{tid - kEpiWarp0 * 32, kEpi, kBarEpi};
   uint32_t ci = 0, tseq = 0;
   unsigned epoch = 0;
-  bool ok = true;
+  bool ok = !dead;
   HeadState H;
   head_reset(H);
   WaitClock wc;
@@ -1170,7 +1193,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     const Phase& ph = P.phases[p];
     unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * 12 : nullptr;
     unsigned long long* stamp = (P.prof && Wk.t == 0) ? prow : nullptr;
-    wc.full = wc.slot = 0;
+    wc.full = wc.slot = wc.first = wc.last = 0;
     if (stamp) stamp[0] = globaltimer();
     if (Wk.t == 0) *S.phase_ready = p;
     if (ph.kind == PK_PREP) {
@@ -1184,7 +1207,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
         if (rec) { prow[5] = wc.slot; prow[6] = globaltimer(); }
       } else {
         mma_phase(P, ph, ci, tseq, S, wc);
-        if (rec) { prow[3] = wc.full; prow[4] = wc.slot; }
+        if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
     if (stamp) stamp[1] = globaltimer();

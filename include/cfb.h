@@ -3,7 +3,7 @@
  *
  * Plain C: device pointers, sizes and a cudaStream_t passed as void*. No torch types.
  * Every buffer (weights, inputs, outputs, workspace) is allocated by the CALLER; the library
- * allocates nothing per call, so every run entry point can be captured in a CUDA graph.
+ * allocates nothing per call.
  *
  * Reference interfaces replaced (paths relative to the reference checkout):
  *   src/chain_flow/csrc/fused_block.cu:784-862  cf_fused_block.{expert, cross_kv, max_grid}
@@ -162,7 +162,10 @@ cfb_status cfb_plan_workspace(const cfb_drafter* d, const cfb_run* r, size_t* by
 cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes);
 /* Launch the persistent kernel on `stream` (no allocation, no host sync: capturable). */
 cfb_status cfb_plan_run(void* ws, void* stream);
-/* Synchronous: device error word of the last run (0 = ok, CFB_ERR_DEVICE_TIMEOUT, ...). */
+/* Synchronous: the plan's device error word: 0 while every run so far completed, else the code
+ * of the first failure (a bounded device-side wait that expired). The word is sticky: once it
+ * is set, later runs of the plan return at once without touching the outputs, until
+ * cfb_plan_build rebuilds the plan. */
 cfb_status cfb_plan_error(void* ws, int* device_error);
 /* Launch parameters the plan resolved (grid CTAs, threads, dynamic smem bytes, phases). */
 cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases);
@@ -185,7 +188,9 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  *                     [4] MMA warps waiting for a free accumulator slot, [5] epilogue waiting for
  *                     partials, [6] epilogue done, [7] activation copies all issued, [8] weight
  *                     producer waiting for a free ring slot, [9] weight units all issued,
- *                     [10..11] unused; written only by runs of plans built with CFB_RUN_PROFILE */
+ *                     [10] / [11] the MMA warps' first / last unit of the phase ready (0 if
+ *                     the CTA had no unit); written only by runs of plans built with
+ *                     CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
 enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
        CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
