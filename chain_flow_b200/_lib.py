@@ -26,7 +26,7 @@ INIT_MODES = {"noise": INIT_GIVEN, "repeat_last": INIT_REPEAT_LAST, "delta": INI
 EXPORTED = [
     "cfb_abi_version", "cfb_last_cuda_error", "cfb_packed_bytes", "cfb_pack_linear",
     "cfb_fold_bias", "cfb_time_embed", "cfb_plan_workspace", "cfb_plan_build", "cfb_plan_run",
-    "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn",
+    "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
 ]
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF = range(9)
 RUN_PROFILE = 1
@@ -88,6 +88,7 @@ def _declare(lib):
     lib.cfb_plan_info.argtypes = [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]
     lib.cfb_plan_buffer.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(sz)]
     lib.cfb_tree_gdn.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
+    lib.cfb_tree_gdn_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
     return lib
 
 

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/cfb.h"
 #include "cfb_common.cuh"
@@ -102,4 +103,60 @@ extern "C" cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, 
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), g, beta,
       parent, init, o, states, N, H, Dv, use_l2norm);
   return cfb_launch_status("tree_gdn_kernel");
+}
+
+// ------------------------------------------------------------------------------------------
+// No-allocation variant: the same kernel, with the per-node states (which it needs as scratch:
+// every child re-reads its parent's state) held in a fixed device array of this library
+// instead of a caller buffer. Nothing in the array has to start at zero: every node state is
+// written before a child reads it, and the roots read `init`.
+static __device__ __align__(256) float cfb_gdn_scratch[CFB_TREE_GDN_NOALLOC_MAX_FLOATS];
+
+namespace {
+
+constexpr int kMaxDevices = 128;
+std::mutex g_scratch_mu;
+float* g_scratch_ptr[kMaxDevices] = {};
+
+// The device address of cfb_gdn_scratch on the current device, looked up once per device.
+cfb_status scratch_for_current_device(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cfb_launch_status("cudaGetDevice");
+    return CFB_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return CFB_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, cfb_gdn_scratch) != cudaSuccess) {
+      (void)cfb_launch_status("cudaGetSymbolAddress(cfb_gdn_scratch)");
+      return CFB_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return CFB_OK;
+}
+
+}  // namespace
+
+extern "C" cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, const float* g,
+                                           const float* beta, const int32_t* parent, const float* init,
+                                           float* o, int B, int N, int H, int Dk, int Dv, int use_l2norm,
+                                           void* stream) {
+  if (!q || !k || !v || !g || !beta || !parent || !init || !o) return CFB_ERR_INVALID_ARG;
+  if (B <= 0 || N <= 0 || H <= 0) return CFB_ERR_INVALID_ARG;
+  if (Dk != kDk || Dv <= 0 || Dv % 32 || (Dv > kColsPerBlock && Dv % kColsPerBlock)) return CFB_ERR_UNSUPPORTED;
+  const unsigned long long need = (unsigned long long)B * N * H * Dk * Dv;
+  if (need > (unsigned long long)CFB_TREE_GDN_NOALLOC_MAX_FLOATS) return CFB_ERR_WORKSPACE;
+  float* scratch = nullptr;
+  const cfb_status st = scratch_for_current_device(&scratch);
+  if (st != CFB_OK) return st;
+  const int cols = Dv < kColsPerBlock ? Dv : kColsPerBlock;
+  const dim3 grid(B * H, Dv / cols);
+  tree_gdn_kernel<<<grid, cols * kQ, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), g, beta,
+      parent, init, o, scratch, N, H, Dv, use_l2norm);
+  return cfb_launch_status("tree_gdn_kernel (no-alloc)");
 }

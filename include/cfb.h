@@ -208,6 +208,26 @@ cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, const float
                         float* o, float* states, int B, int N, int H, int Dk, int Dv,
                         int use_l2norm, void* stream);
 
+/* cfb_tree_gdn without the states buffer, allocating nothing. This entry point has no
+ * counterpart in the reference.
+ * It is for callers that cannot allocate device memory when they verify: the verify step runs
+ * inside the target model's forward pass, which serving engines record once into a CUDA graph
+ * and replay, and no cudaMalloc may happen there; a caller that only needs o would otherwise
+ * have to reserve a [B,N,H,Dk,Dv] fp32 states buffer for its largest batch up front.
+ * The node states (which the kernel re-reads as parents) live in one fixed device array of
+ * this library, CFB_TREE_GDN_NOALLOC_MAX_FLOATS fp32 (64 MiB), that every GPU which loads the
+ * library holds until the process exits. Calls with B*N*H*Dk*Dv above that return
+ * CFB_ERR_WORKSPACE. The first call on a device looks up the array's address on that device
+ * (cudaGetSymbolAddress, with that device current): make that first call before any stream
+ * capture. Every call shares the array and leaves its node states there; none of it needs to
+ * start at zero, but calls that overlap on the GPU (other streams, other host threads) race on
+ * it, so order them on one stream. Arguments and supported shapes are those of cfb_tree_gdn. */
+#define CFB_TREE_GDN_NOALLOC_MAX_FLOATS (16 * 1024 * 1024)
+cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, const float* g,
+                                const float* beta, const int32_t* parent, const float* init,
+                                float* o, int B, int N, int H, int Dk, int Dv, int use_l2norm,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif
