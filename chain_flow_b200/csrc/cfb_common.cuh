@@ -14,7 +14,7 @@ namespace cfb {
 
 // Device error word values (written into the workspace, read by cfb_plan_error).
 enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_GRID = 1, DEV_TIMEOUT_FULL = 2, DEV_TIMEOUT_EMPTY = 3,
-                    DEV_TIMEOUT_SLOT = 4, DEV_BAD_PHASE = 5 };
+                    DEV_TIMEOUT_SLOT = 4, DEV_BAD_PHASE = 5, DEV_TIMEOUT_FIXUP = 6 };
 
 // Every device-side wait is bounded by this many nanoseconds of %globaltimer. On expiry the
 // waiter records an error and returns, so a broken schedule ends the launch instead of hanging

@@ -65,7 +65,7 @@ constexpr int kUnitK = 8;                           // 16-wide k blocks per stre
 constexpr int kBlockBytes = 512;                    // one 16x16 fp16 fragment tile
 constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB
 constexpr int kMaxStages = 12;
-constexpr int kXRowBytes = 272;                     // activation row of a unit: 128 fp16 + 16 pad
+constexpr int kXRowBytes = 256;                     // activation row of a unit: 128 fp16
 constexpr int kSmemBudget = 232448 - 1024;          // dynamic + static shared memory per CTA
 constexpr int kRowsMax = 64;                        // activation rows per job
 constexpr int kTopMax = 8;                          // top-k per beam row
@@ -73,7 +73,7 @@ constexpr int kMaxExperts = 4;
 constexpr int kStatCols = 64;                       // columns per row-statistics part
 constexpr int kHeadPartFloats = 2 + 2 * kTopMax;
 
-enum XKind : int { XK_F16 = 0, XK_PATH = 1 };
+enum XKind : int { XK_F16 = 0 };
 
 // fp16 activations the engine produces for its own GEMMs are stored unit-tiled: each 128-column
 // slice of all R rows is contiguous (one bulk copy per streamed unit), and within a row the
@@ -85,17 +85,18 @@ CFB_DEV size_t tidx(int R, int r, int k) {
 enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
 enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
                    EK_HEADIN = 5, EK_HEAD = 6 };
-enum PKind : int { PK_PREP = 0, PK_GEMM = 1 };
-enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2 };
+enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3 };
+enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
+// Attention of one (expert, block): q rows [B*Sq] and k/v rows [B*Kn] (fp32, written by the
+// projection phase before it), output fp16 unit-tiled with outR rows. One task = (request, head).
 struct AttnTask {
   const float* q; int ldq, qoff;
   const float* k; int ldk, koff;
   const float* v; int ldv, voff;
-  __half* out; int ldo;
-  int rows_per_req, keys_per_req, B, hd, heads, causal, nsec, Dsec;
+  __half* out;
+  int rows_per_req, keys_per_req, B, hd, heads, causal;
   float scale;
-  unsigned* cnt;          // [heads]
   int outR;               // tiled rows of `out`
 };
 
@@ -111,17 +112,16 @@ struct Job {
   int unit_base, tile_base;
   // activation source (fp16 rows, or a gather of embedding rows by path token)
   int xkind;
-  const __half* x; int ldx;                // XK_F16: unit-tiled source with xR rows; XK_PATH: unused
+  const __half* x; int ldx;                // unit-tiled source with xR rows
   int xR, xcopy;                           // tiled rows of the source; rows copied per unit
   int gin, gstride, goff;                  // source row = (r / gin) * gstride + goff + r % gin
   int ln; const float2* stats; int nparts; const float* colsum;
-  const int64_t* lastp; int order; const __half* emb; int D;   // XK_PATH gather
+  int order; int D;                        // EK_PATHH: path order, hidden size
   // epilogue
   int ekind;
   const float* bias;
   float* out32; __half* out16; int ldo; int oR;   // out32 row stride; out16 tiled rows
   float2* ostats; int onparts;
-  int attn;                                // -1 or AttnTask index (trigger after the tile)
   int e_idx, step, last_step, wrows, nlive, R, topb;
   float dt;
   const float* p0;                         // EK_PATHH: offset biases [order][D]
@@ -129,10 +129,9 @@ struct Job {
 
 struct Phase {
   int kind;
-  int job0, njobs, nunits, ntiles;
+  int job0, njobs, nunits, ntiles;   // PK_ATTN: job0 / njobs index attention tasks, ntiles = tasks
   int whole;                // 1: each CTA gets whole tiles (no cross-CTA fixups); 0: stream-K
   int post;
-  int side_markov;
   int step, rows, fr, keep, topb, base, base_prev, last;
 };
 
@@ -152,15 +151,15 @@ struct Plan {
   const Job* jobs;
   const AttnTask* attn;
   ExpertRT ex[kMaxExperts];
-  unsigned* bar; unsigned* exitcnt; unsigned* headcnt; int* err;
+  unsigned* bar; unsigned* exitcnt; int* err;
   unsigned* tilecnt; int ntilecnt;
-  unsigned* attncnt; int nattncnt;
-  float* gpart;             // [G][2][kTileRows*kRowsMax]
+  float* gpart;             // [G][kTileRows*kRowsMax]: each CTA's one published split-tile partial
   float* hpart;             // [G][kRowsMax][kHeadPartFloats]
   const __half* ctx; const __half* z0; float* pred; float2* ctxstat; __half* ctx16;
   int init_mode;            // CFB_INIT_GIVEN / REPEAT_LAST / DELTA
   const int64_t* known0; int64_t* lastp; float* cum; int64_t* toks; int* bps; int64_t* tokens;
   const int64_t* shortlist; const __half* markov_w1; __half* xhead; int ldxhead;
+  const __half* emb; __half* pg;            // embeddings; tiled path-gather rows of the path GEMM
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
   unsigned long long* prof;                // [nphases][G][4] or NULL
 };
@@ -186,10 +185,13 @@ CFB_DEV void gsync(const Grp& g) { asm volatile("bar.sync %0, %1;" :: "r"(g.bar)
 
 struct HeadState { float m, s; float tv[kTopMax]; int ti[kTopMax]; };
 
-// Profiling (plans built with CFB_RUN_PROFILE): ns spent waiting, per role, reset every phase.
+// Profiling (plans built with CFB_RUN_PROFILE): ns spent waiting, per role, reset every phase,
+// and the times of a few events (the layout of a CFB_BUF_PROF record is documented in cfb.h).
+constexpr int kProfSlots = 20;
 struct WaitClock {
   unsigned long long full = 0, slot = 0;
   unsigned long long first = 0, last = 0;   // when the phase's first / last unit was ready
+  unsigned long long part = 0, atom = 0, fix = 0, tdone = 0;   // epilogue: last tile's events
   bool on = false;
   CFB_DEV unsigned long long now() const { return on ? globaltimer() : 0ull; }
 };
@@ -203,9 +205,12 @@ CFB_DEV void set_err(const Plan& P, int code) {
   atomicOr(P.bar, kBarErrBit);
 }
 
-CFB_DEV long long cta_start(long long U, int G, int c) { return (long long)c * U / G; }
+// 32-bit arithmetic: plans are only built when U * (G + 1) fits in 32 bits
+CFB_DEV long long cta_start(long long U, int G, int c) {
+  return (long long)((unsigned)c * (unsigned)U / (unsigned)G);
+}
 CFB_DEV int cta_of(long long u, long long U, int G) {       // the CTA whose range holds unit u
-  return (int)(((u + 1) * G + U - 1) / U - 1);
+  return (int)((((unsigned)u + 1u) * (unsigned)G + (unsigned)U - 1u) / (unsigned)U) - 1;
 }
 // the next CTA after c whose (non-empty) range holds units; CTAs with empty ranges are skipped
 CFB_DEV int next_contributor(int c, long long U, int G) {
@@ -218,7 +223,7 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W) {
   __shared__ int s_ok;
   if (W.t == 0) {
     ++epoch;
-    __threadfence();
+    // the CTA barrier above orders every thread's writes before this release (acq_rel) atomic
     const unsigned target = epoch * (unsigned)P.G;
     unsigned v = atom_add_acqrel(P.bar, 1u) + 1u;
     if (v < target) {
@@ -248,6 +253,18 @@ CFB_DEV void chan_merge(float& n, float& m, float& M2, float nb, float mb, float
   m = m + d * f;
   M2 = M2 + M2b + d * d * n * f;
   n = nn;
+}
+
+// Fold 8 values into a running (n, mean, M2): two-pass over the 8, then one Chan merge.
+CFB_DEV void stats8_merge(float& n, float& m, float& M2, const float (&v)[8]) {
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum += v[i];
+  const float mb = sum * 0.125f;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { const float d = v[i] - mb; q += d * d; }
+  chan_merge(n, m, M2, 8.f, mb, q);
 }
 
 // Merge (n, mean, M2) across `width` adjacent lanes; the lower lane is always the left operand,
@@ -301,82 +318,100 @@ CFB_DEV RowMap row_map(int rows, int et) {
 }
 
 // ------------------------------------------------------------------------------------------
-// attention of one head, run by the CTA whose epilogue completes the last tile of that head
-CFB_DEV void run_attention(const AttnTask& A, int h, Smem& S, const Grp& E) {
-  const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
+// Attention of request b, head h (reference nn.MultiheadAttention inside HiddenKVFlowBlock,
+// chunked_flow.py:185-197): softmax(q k^T * hd^-1/2 [+ causal mask]) v over the request's rows.
+// Run by all worker warps of one CTA; q/k/v slices go to shared memory with one cp.async batch.
+CFB_DEV void attn_task(const AttnTask& A, int b, int h, Smem& S, const Grp& W) {
   const int Sq = A.rows_per_req, Kn = A.keys_per_req, hd = A.hd;
   float* qs = S.scratch;
   float* ks = qs + Sq * hd;
   float* vs = ks + Kn * hd;
   float* sc = vs + Kn * hd;
   const int cpr = hd / 4;                       // 16-byte chunks per head row
-  for (int b = 0; b < A.B; ++b) {
-    // every q/k/v row slice of this head in flight at once (L2 only), then one wait
-    for (int e = E.t; e < (Sq + 2 * Kn) * cpr; e += E.n) {
-      const int row = e / cpr, c = e - row * cpr;
-      const float* src;
-      float* dst;
-      if (row < Sq) {
-        src = A.q + (size_t)(b * Sq + row) * A.ldq + A.qoff + h * hd + c * 4;
-        dst = qs + row * hd + c * 4;
-      } else if (row < Sq + Kn) {
-        const int j = row - Sq;
-        src = A.k + (size_t)(b * Kn + j) * A.ldk + A.koff + h * hd + c * 4;
-        dst = ks + j * hd + c * 4;
-      } else {
-        const int j = row - Sq - Kn;
-        src = A.v + (size_t)(b * Kn + j) * A.ldv + A.voff + h * hd + c * 4;
-        dst = vs + j * hd + c * 4;
-      }
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+  for (int e = W.t; e < (Sq + 2 * Kn) * cpr; e += W.n) {
+    const int row = e / cpr, c = e - row * cpr;
+    const float* src;
+    float* dst;
+    if (row < Sq) {
+      src = A.q + (size_t)(b * Sq + row) * A.ldq + A.qoff + h * hd + c * 4;
+      dst = qs + row * hd + c * 4;
+    } else if (row < Sq + Kn) {
+      const int j = row - Sq;
+      src = A.k + (size_t)(b * Kn + j) * A.ldk + A.koff + h * hd + c * 4;
+      dst = ks + j * hd + c * 4;
+    } else {
+      const int j = row - Sq - Kn;
+      src = A.v + (size_t)(b * Kn + j) * A.ldv + A.voff + h * hd + c * 4;
+      dst = vs + j * hd + c * 4;
     }
-    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-    gsync(E);
-    for (int pr = warp; pr < Sq * Kn; pr += nw) {
-      const int i = pr / Kn, j = pr - i * Kn;
-      float s = 0.f;
-      for (int d = lane; d < hd; d += 32) s += qs[i * hd + d] * ks[j * hd + d];
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      if (lane == 0) sc[pr] = (A.causal && j > i) ? -INFINITY : s * A.scale;
-    }
-    gsync(E);
-    if (E.t < Sq) {
-      float mx = -INFINITY;
-      for (int j = 0; j < Kn; ++j) mx = fmaxf(mx, sc[E.t * Kn + j]);
-      float sum = 0.f;
-      for (int j = 0; j < Kn; ++j) { const float e = __expf(sc[E.t * Kn + j] - mx); sc[E.t * Kn + j] = e; sum += e; }
-      const float inv = 1.f / sum;
-      for (int j = 0; j < Kn; ++j) sc[E.t * Kn + j] *= inv;
-    }
-    gsync(E);
-    for (int e = E.t; e < Sq * hd; e += E.n) {
-      const int i = e / hd, d = e - i * hd;
-      float o = 0.f;
-      for (int j = 0; j < Kn; ++j) o += sc[i * Kn + j] * vs[j * hd + d];
-      A.out[tidx(A.outR, b * Sq + i, h * hd + d)] = __float2half_rn(o);
-    }
-    gsync(E);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
   }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  gsync(W);
+  // scores: T adjacent lanes per (i, j) pair, each summing every T-th 4-column chunk
+  const int pairs = Sq * Kn;
+  int T = 32;
+  while (T > 1 && pairs * T > W.n) T >>= 1;
+  const int lane = W.t & 31, gl = lane & (T - 1);
+  for (int p0 = 0; p0 < pairs * T; p0 += W.n) {
+    const int pr = (p0 + W.t) / T;
+    float sum = 0.f;
+    if (pr < pairs) {
+      const int i = pr / Kn, j = pr - i * Kn;
+      const float4* q4 = reinterpret_cast<const float4*>(qs + i * hd);
+      const float4* k4 = reinterpret_cast<const float4*>(ks + j * hd);
+      for (int c = gl; c < cpr; c += T) {
+        const float4 a = q4[c], k = k4[c];
+        sum += a.x * k.x + a.y * k.y + a.z * k.z + a.w * k.w;
+      }
+    }
+    for (int off = T >> 1; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (pr < pairs && gl == 0) {
+      const int i = pr / Kn, j = pr - i * Kn;
+      sc[pr] = (A.causal && j > i) ? -INFINITY : sum * A.scale;
+    }
+  }
+  gsync(W);
+  if (W.t < Sq) {
+    float* row = sc + W.t * Kn;
+    float mx = -INFINITY;
+    for (int j = 0; j < Kn; ++j) mx = fmaxf(mx, row[j]);
+    float sum = 0.f;
+    for (int j = 0; j < Kn; ++j) { const float e = __expf(row[j] - mx); row[j] = e; sum += e; }
+    const float inv = 1.f / sum;
+    for (int j = 0; j < Kn; ++j) row[j] *= inv;
+  }
+  gsync(W);
+  // out[i, 4c..4c+3] = sum_j p[i, j] v[j, 4c..4c+3] -> four consecutive fp16 of the tiled output
+  for (int e = W.t; e < Sq * cpr; e += W.n) {
+    const int i = e / cpr, c = e - i * cpr;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < Kn; ++j) {
+      const float pj = sc[i * Kn + j];
+      const float4 v = reinterpret_cast<const float4*>(vs + j * hd)[c];
+      o.x += pj * v.x; o.y += pj * v.y; o.z += pj * v.z; o.w += pj * v.w;
+    }
+    uint2 pk;
+    pk.x = pack_half2(o.x, o.y);
+    pk.y = pack_half2(o.z, o.w);
+    *reinterpret_cast<uint2*>(A.out + tidx(A.outR, b * Sq + i, h * hd + 4 * c)) = pk;
+  }
+  gsync(W);
 }
 
-CFB_DEV void attn_trigger(const Plan& P, const Job& J, int tile, Smem& S, const Grp& E) {
-  const AttnTask& A = P.attn[J.attn];
-  const int c0 = (tile * kTileRows) % A.Dsec;
-  const int h0 = c0 / A.hd, h1 = min((c0 + kTileRows - 1) / A.hd, A.heads - 1);
-  for (int h = h0; h <= h1; ++h) {
-    if (E.t == 0) {
-      const unsigned expect = (unsigned)A.nsec *
-          (unsigned)(((h + 1) * A.hd - 1) / kTileRows - (h * A.hd) / kTileRows + 1);
-      __threadfence();
-      const unsigned old = atom_add_acqrel(A.cnt + h, 1u);
-      *S.flag = (old + 1 == expect);
-      if (old + 1 == expect) A.cnt[h] = 0u;
+// An attention phase: its (task, request, head) items spread over the CTAs, one at a time.
+CFB_DEV void attn_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
+  for (int t = blockIdx.x; t < ph.ntiles; t += P.G) {
+    int jx = 0, rem = t;
+    for (; jx < ph.njobs; ++jx) {
+      const AttnTask& A = P.attn[ph.job0 + jx];
+      const int n = A.B * A.heads;
+      if (rem < n) break;
+      rem -= n;
     }
-    gsync(E);
-    const int go = *S.flag;
-    gsync(E);
-    if (go) { __threadfence(); run_attention(A, h, S, E); }
+    if (jx >= ph.njobs) break;
+    const AttnTask& A = P.attn[ph.job0 + jx];
+    attn_task(A, rem / A.heads, rem % A.heads, S, W);
   }
 }
 
@@ -400,28 +435,35 @@ CFB_DEV void head_reset(HeadState& H) {
   for (int i = 0; i < kTopMax; ++i) { H.tv[i] = -INFINITY; H.ti[i] = 0x7fffffff; }
 }
 
-CFB_DEV void head_merge(HeadState& A, const HeadState& B, int K) {
-  const float M = fmaxf(A.m, B.m);
-  A.s = (M == -INFINITY) ? 0.f : A.s * __expf(A.m - M) + B.s * __expf(B.m - M);
-  A.m = M;
+// entry j of a sorted top list (-inf past its end), without indexing registers at run time
+CFB_DEV void list_at(const HeadState& H, int j, float& v, int& id) {
+  v = -INFINITY; id = 0x7fffffff;
 #pragma unroll
-  for (int i = 0; i < kTopMax; ++i) if (i < K) top_insert(A, K, B.tv[i], B.ti[i]);
+  for (int i = 0; i < kTopMax; ++i) if (i == j) { v = H.tv[i]; id = H.ti[i]; }
 }
 
-// merge across `width` adjacent lanes, lower lane on the left
-CFB_DEV void head_group(HeadState& H, int K, int width) {
+// better (value, id, owner) across the lanes of aligned groups of `width` lanes (xor tree)
+CFB_DEV void argmax_lanes(float& v, int& id, int& own, int width) {
+  for (int off = 1; off < width; off <<= 1) {
+    const float vo = __shfl_xor_sync(0xffffffffu, v, off);
+    const int io = __shfl_xor_sync(0xffffffffu, id, off), oo = __shfl_xor_sync(0xffffffffu, own, off);
+    if (better(vo, io, v, id) || (vo == v && io == id && oo < own)) { v = vo; id = io; own = oo; }
+  }
+}
+
+CFB_DEV void lse_merge(float& m, float& s, float mb, float sb) {
+  const float M = fmaxf(m, mb);
+  s = (M == -INFINITY) ? 0.f : s * __expf(m - M) + sb * __expf(mb - M);
+  m = M;
+}
+
+// (max, sumexp) across aligned groups of `width` lanes; the lower lane is the left operand
+CFB_DEV void lse_lanes(float& m, float& s, int width) {
   const int lane = threadIdx.x & 31;
   for (int off = 1; off < width; off <<= 1) {
-    HeadState O;
-    O.m = __shfl_xor_sync(0xffffffffu, H.m, off);
-    O.s = __shfl_xor_sync(0xffffffffu, H.s, off);
-#pragma unroll
-    for (int i = 0; i < kTopMax; ++i) {
-      O.tv[i] = __shfl_xor_sync(0xffffffffu, H.tv[i], off);
-      O.ti[i] = __shfl_xor_sync(0xffffffffu, H.ti[i], off);
-    }
-    if (lane & off) { HeadState T = H; H = O; head_merge(H, T, K); }
-    else head_merge(H, O, K);
+    const float mo = __shfl_xor_sync(0xffffffffu, m, off), so = __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane & off) { float m1 = mo, s1 = so; lse_merge(m1, s1, m, s); m = m1; s = s1; }
+    else lse_merge(m, s, mo, so);
   }
 }
 
@@ -467,20 +509,22 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) add[i] = 0.f;
+            const int64_t* lp = P.lastp + ((size_t)(M.r / J.wrows) * P.Wmax + M.r % J.wrows) * J.order;
             for (int j = 0; j < J.nlive; ++j)
-              if (J.lastp[(size_t)M.r * J.order + j] >= 0) {
+              if (lp[j] >= 0) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) add[i] += J.p0[(size_t)j * J.D + col0 + f0 + i];
               }
           }
+          float v[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int col = col0 + f0 + i;
-            const float v = epi_val(S, f0 + i, M.r) + add[i];
-            if (J.ekind == EK_RESID) J.out32[(size_t)M.r * J.ldo + col] = v;
-            J.out16[tidx(J.oR, M.r, col)] = __float2half_rn(v);
-            n += 1.f; const float d = v - m; m += d / n; M2 += d * (v - m);
+            v[i] = epi_val(S, f0 + i, M.r) + add[i];
+            if (J.ekind == EK_RESID) J.out32[(size_t)M.r * J.ldo + col] = v[i];
+            J.out16[tidx(J.oR, M.r, col)] = __float2half_rn(v[i]);
           }
+          stats8_merge(n, m, M2, v);
         }
       }
       chan_group(n, m, M2, M.sl);
@@ -489,53 +533,46 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     }
     case EK_EULER: {
       const RowMap M = row_map(rows, E.t);
-      float n[kMaxExperts], m[kMaxExperts], M2[kMaxExperts];
-#pragma unroll
-      for (int e = 0; e < kMaxExperts; ++e) { n[e] = 0.f; m[e] = 0.f; M2[e] = 0.f; }
       const int b = M.r / P.chunk, c = M.r - b * P.chunk;
       const int pos = P.ex[J.e_idx].start + c;
       const int nx = (J.step + 1) & 1;
-      if (M.r < rows) {
-        for (int f0 = M.q * M.nf; f0 < (M.q + 1) * M.nf; f0 += 8) {
-          float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f0;
-          float z[8];
+      const bool live = M.r < rows;
+      const int f0 = M.q * M.nf;
+      // z <- z + dt * v on this tile's columns of the chunk rows (reference tree_flow.py:229-235)
+      if (live) {
+        for (int f = f0; f < f0 + M.nf; f += 8) {
+          float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) z[i] = zp[i];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) { z[i] += J.dt * epi_val(S, f0 + i, M.r); zp[i] = z[i]; }
-          if (!J.last_step) {
-#pragma unroll
-            for (int e = 0; e < kMaxExperts; ++e) {
-              if (e >= P.n_experts) break;
-              const ExpertRT& X = P.ex[e];
-              if (pos >= X.S) continue;
-              const float* pe = X.pos + (size_t)pos * P.D + col0 + f0;
-              const float* te = X.temb + (size_t)(J.step + 1) * P.D + col0 + f0;
-              const bool cur = pos >= X.start;
-              float xv[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) xv[i] = z[i] + pe[i] + (cur ? te[i] : 0.f);
-              const int xrow = b * X.S + pos;
-              const size_t xi = (size_t)xrow * P.D + col0 + f0;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                X.x32[nx][xi + i] = xv[i];
-                X.x16[nx][tidx(P.B * X.S, xrow, col0 + f0 + i)] = __float2half_rn(xv[i]);
-                n[e] += 1.f; const float d = xv[i] - m[e]; m[e] += d / n[e]; M2[e] += d * (xv[i] - m[e]);
-              }
-            }
-          }
+          for (int i = 0; i < 8; ++i) zp[i] += J.dt * epi_val(S, f + i, M.r);
         }
       }
-      if (!J.last_step) {
+      if (J.last_step) break;
+      // next step's inputs of every expert that sees this position: z + pos (+ time on its chunk)
+#pragma unroll 1
+      for (int e = 0; e < P.n_experts; ++e) {
+        const ExpertRT& X = P.ex[e];
+        float n = 0.f, m = 0.f, M2 = 0.f;
+        const bool has = live && pos < X.S;
+        if (has) {
+          const bool cur = pos >= X.start;
+          const int xrow = b * X.S + pos;
+          for (int f = f0; f < f0 + M.nf; f += 8) {
+            const float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f;
+            const float* pe = X.pos + (size_t)pos * P.D + col0 + f;
+            const float* te = X.temb + (size_t)(J.step + 1) * P.D + col0 + f;
+            const size_t xi = (size_t)xrow * P.D + col0 + f;
+            float xv[8];
 #pragma unroll
-        for (int e = 0; e < kMaxExperts; ++e) {
-          if (e >= P.n_experts) break;
-          chan_group(n[e], m[e], M2[e], M.sl);
-          const ExpertRT& X = P.ex[e];
-          if (M.q == 0 && M.r < rows && pos < X.S)
-            X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m[e], M2[e]);
+            for (int i = 0; i < 8; ++i) {
+              xv[i] = zp[i] + pe[i] + (cur ? te[i] : 0.f);
+              X.x32[nx][xi + i] = xv[i];
+              X.x16[nx][tidx(P.B * X.S, xrow, col0 + f + i)] = __float2half_rn(xv[i]);
+            }
+            stats8_merge(n, m, M2, xv);
+          }
         }
+        chan_group(n, m, M2, M.sl);
+        if (M.q == 0 && has) X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m, M2);
       }
       break;
     }
@@ -555,10 +592,29 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     }
   }
   gsync(E);
-  if (J.attn >= 0) attn_trigger(P, J, tile, S, E);
 }
 
 // ------------------------------------------------------------------------------------------
+// While the MMA warps still work on a tile: pull the global operands of its epilogue (the rows it
+// adds to or updates, two 128-byte lines per row of 64 fp32 columns) into L1.
+CFB_DEV void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" :: "l"(p)); }
+CFB_DEV void epi_prefetch(const Plan& P, const Job& J, int tile, const Grp& E) {
+  const int col0 = tile * kTileRows;
+  for (int e = E.t; e < 2 * J.rows; e += E.n) {
+    const int r = e >> 1, c = col0 + 32 * (e & 1);
+    const float* p = nullptr;
+    if (J.ekind == EK_RESID) {
+      p = J.out32 + (size_t)r * J.ldo + c;
+    } else if (J.ekind == EK_HEADIN) {
+      p = P.pred + ((size_t)(r / J.wrows) * P.DL + J.step) * P.D + c;
+    } else if (J.ekind == EK_EULER) {
+      const int b = r / P.chunk, pos = P.ex[J.e_idx].start + (r - b * P.chunk);
+      p = P.pred + ((size_t)b * P.DL + pos) * P.D + c;
+    }
+    if (p) prefetch_l1(p);
+  }
+}
+
 // Epilogue side of one tile: take the MMA warps' partials from slot buffer `b`, reduce them in a
 // fixed order, release the slot, then finish the tile directly or through the stream-K fixup.
 CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
@@ -566,11 +622,9 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
                       WaitClock& wc) {
   const int rows = J.rows;
   const int b = tseq % S.nbuf;
-  const unsigned long long w0 = wc.now();
-  if (!mbar_wait(&S.accf[b], (tseq / S.nbuf) & 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
-  wc.slot += wc.now() - w0;
-  const float* sl = S.slot(b);
-  {   // this tile's bias and LayerNorm column sums, one load per thread
+  epi_prefetch(P, J, tile, E);
+  {   // this tile's bias and LayerNorm column sums, one load per thread, before the partials
+      // are ready (the previous tile's epilogue has finished with these arrays)
     const int col0 = tile * kTileRows;
     if (E.t < kTileRows) {
       const int col = col0 + E.t;
@@ -580,6 +634,10 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
       S.tcsum[E.t - kTileRows] = (J.colsum && col < J.nout) ? J.colsum[col] : 0.f;
     }
   }
+  const unsigned long long w0 = wc.now();
+  if (!mbar_wait(&S.accf[b], (tseq / S.nbuf) & 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
+  if (wc.on) { wc.part = wc.now(); wc.slot += wc.part - w0; wc.atom = wc.fix = 0; }
+  const float* sl = S.slot(b);
   // feature f = 16 i + ff comes from MMA warps i, i+4, ... (one per k slice), summed in order
   for (int e = E.t; e < kTileRows * rows; e += E.n) {
     const int f = e / rows, r = e - f * rows;
@@ -593,46 +651,79 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
   if (E.t == 0) mbar_arrive(&S.acce[b]);
   ++tseq;
   if (!complete) {
-    // contributors: the CTAs whose ranges hold this tile's units, in k order; when a phase has
-    // fewer units than CTAs, CTAs with empty ranges sit between them and are not counted
+    // A tile split across CTAs (stream-K). Its owner is the CTA whose range holds the tile's
+    // first unit; that unit range ends the owner's own range, so the owner reaches the tile last
+    // and finishes it. Every other contributor holds the tile's later units at the START of its
+    // range: it publishes its partial there (at most one per CTA and phase) and counts itself in.
+    // The owner waits (bounded) for the count, then adds the partials in k order to its own.
+    // Nobody else waits on anything, so the waits cannot form a cycle.
     const int c = blockIdx.x;
-    const long long ug_last = ug_first + J.nkc - 1;
-    const int c_first = cta_of(ug_first, U, P.G);
-    int ncontrib = 0;
-    for (int cc = c_first; cc < P.G && cta_start(U, P.G, cc) <= ug_last; cc = next_contributor(cc, U, P.G))
-      ++ncontrib;
-    const int slot = (cta_start(U, P.G, c) >= ug_first) ? 0 : 1;
-    float* mine = P.gpart + ((size_t)c * 2 + slot) * (kTileRows * kRowsMax);
-    for (int e = E.t; e < kTileRows * rows; e += E.n) {
-      const int f = e / rows, r = e - f * rows;
-      __stcg(mine + f * kRowsMax + r, S.red[f * S.rp + r]);
-    }
-    __threadfence();
-    gsync(E);
-    if (E.t == 0) {
-      unsigned* cnt = P.tilecnt + J.tile_base + tile;
-      const unsigned old = atom_add_acqrel(cnt, 1u);
-      const bool last = (old + 1 == (unsigned)ncontrib);
-      if (last) *cnt = 0u;
-      *S.flag = last;
-    }
-    gsync(E);
-    const bool last = *S.flag;
-    gsync(E);
-    if (!last) return;
-    __threadfence();
-    for (int e = E.t; e < kTileRows * rows; e += E.n) {
-      const int f = e / rows, r = e - f * rows;
-      float s = 0.f;
-      for (int cc = c_first; cc < P.G && cta_start(U, P.G, cc) <= ug_last; cc = next_contributor(cc, U, P.G)) {
-        const int sl2 = (cta_start(U, P.G, cc) >= ug_first) ? 0 : 1;
-        s += __ldcg(P.gpart + ((size_t)cc * 2 + sl2) * (kTileRows * kRowsMax) + f * kRowsMax + r);
+    unsigned* cnt = P.tilecnt + J.tile_base + tile;
+    if (cta_start(U, P.G, c) > ug_first) {
+      float* mine = P.gpart + (size_t)c * (kTileRows * kRowsMax);
+      for (int e = E.t; e < kTileRows * rows; e += E.n) {
+        const int f = e / rows, r = e - f * rows;
+        __stcg(mine + f * kRowsMax + r, S.red[f * S.rp + r]);
       }
-      S.red[f * S.rp + r] = s;
+      gsync(E);
+      // the barrier orders every thread's partial stores before thread 0's release count
+      if (E.t == 0) {
+        atom_add_release(cnt, 1u);
+        if (wc.on) wc.atom = wc.now();
+      }
+      return;
+    }
+    // owner: list the other contributors (CTA ids, in k order) in the epilogue scratch
+    int* clist = reinterpret_cast<int*>(S.scratch);
+    if (E.t == 0) {
+      const long long ug_last = ug_first + J.nkc - 1;
+      int n = 0;
+      for (int cc = next_contributor(c, U, P.G); cc < P.G && cta_start(U, P.G, cc) <= ug_last;
+           cc = next_contributor(cc, U, P.G))
+        clist[1 + n++] = cc;
+      clist[0] = n;
+      const unsigned want = (unsigned)n;
+      const unsigned long long t0 = globaltimer();
+      for (unsigned it = 1; ld_acquire(cnt) < want; ++it) {
+        if (it % kPollsPerCheck) continue;
+        if (ld_volatile_int(P.err) != 0) break;
+        if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_FIXUP); break; }
+      }
+      *cnt = 0u;               // reused by the same tile index of the next split phase
+      if (wc.on) wc.atom = wc.now();
     }
     gsync(E);
+    const int ncontrib = clist[0];
+    const int total = kTileRows * rows;
+    for (int e0 = E.t; e0 < total; e0 += 8 * E.n) {
+      int off[8];
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = e0 + k * E.n;
+        const int f = e / rows, r = e - f * rows;
+        off[k] = e < total ? f * kRowsMax + r : -1;
+        acc[k] = e < total ? S.red[f * S.rp + r] : 0.f;
+      }
+      for (int i = 0; i < ncontrib; ++i) {
+        const float* part = P.gpart + (size_t)clist[1 + i] * (kTileRows * kRowsMax);
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = off[k] >= 0 ? __ldcg(part + off[k]) : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = e0 + k * E.n;
+        if (e < total) { const int f = e / rows, r = e - f * rows; S.red[f * S.rp + r] = acc[k]; }
+      }
+    }
+    gsync(E);
+    if (wc.on) wc.fix = wc.now();
   }
   tile_epilogue(P, J, tile, S, H, E);
+  if (wc.on) wc.tdone = wc.now();
 }
 
 // ------------------------------------------------------------------------------------------
@@ -670,22 +761,26 @@ CFB_DEV bool job_slice(const Job& J, const UnitRange& cu, int& ju0, int& ju1) {
 // Everything the per-unit loop needs is held in registers (job fields, ring stage and parity,
 // tile / k-chunk position): the mbarrier operations are compiler memory barriers, so anything
 // read through the Job reference would otherwise be reloaded on every unit.
-template <int NT>
+// NSPLIT (jobs of 49-64 rows): instead of splitting a unit's k blocks between the two warps of an
+// m16 tile, each of them takes all k blocks for half of the n-tiles (NT each), which halves the
+// accumulators a thread holds; it writes zeros for the other half's rows so that the
+// epilogue's fixed two-slice sum is unchanged.
+template <int NT, bool NSPLIT>
 CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci, uint32_t& tseq, Smem& S,
                      WaitClock& wc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice of a unit
+  const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice (or n half) of a unit
+  const int nb = NSPLIT ? ks * NT : 0;         // first n-tile of this warp
   const int g = lane >> 2, t = lane & 3;
   const int nkc = J.nkc, Kt = J.Kt, rows = J.rows, nst = S.nstages, rp = S.rp, nbuf = S.nbuf;
   const int* err = P.err;
-  // shared-memory row of each n-tile's activation row: tiled sources are 256 B per row with
-  // chunks swizzled by row; path gathers are 272 B per row, unswizzled
-  const bool tiled = J.xkind == XK_F16;
-  const int xrs = tiled ? 256 : kXRowBytes, xsw = tiled ? 7 : 0;
+  // shared-memory row of each n-tile's activation row: 256 B per row, 16-byte chunks swizzled
+  // by the row index
+  const int xrs = kXRowBytes, xsw = 7;
   int xoff[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int r = nt * 8 + g;
+    const int r = (nb + nt) * 8 + g;
     const int sr = r < rows ? src_row(J, r) : -1;
     // byte offsets of the two 16-byte chunks of k-block 0; k-block blk adds 32*blk before the swizzle
     xoff[nt][0] = sr < 0 ? -1 : sr * xrs + 4 * t;
@@ -712,8 +807,8 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
     const uint8_t* st = S.ring + (size_t)stage * S.stage_bytes;
     const uint8_t* xs = st + kUnitBytes;
 #pragma unroll
-    for (int i = 0; i < kUnitK / kKSlices; ++i) {
-      const int blk = ks + kKSlices * i;
+    for (int i = 0; i < (NSPLIT ? kUnitK : kUnitK / kKSlices); ++i) {
+      const int blk = NSPLIT ? i : ks + kKSlices * i;
       if (blk < nkb) {
         const uint4 a = *reinterpret_cast<const uint4*>(st + (blk * 4 + mi) * kBlockBytes + lane * 16);
 #pragma unroll
@@ -740,12 +835,19 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
       float* sl = S.slots + ((size_t)slot * kMmaWarps + warp) * 16 * rp;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const int r0 = nt * 8 + 2 * t;
+        const int r0 = (nb + nt) * 8 + 2 * t;
         if (r0 < rp) {
           sl[g * rp + r0] = acc[nt][0];
           sl[g * rp + r0 + 1] = acc[nt][1];
           sl[(g + 8) * rp + r0] = acc[nt][2];
           sl[(g + 8) * rp + r0 + 1] = acc[nt][3];
+        }
+        if (NSPLIT) {
+          const int z0 = ((NT - nb) + nt) * 8 + 2 * t;     // the other half's rows
+          if (z0 < rp) {
+            sl[g * rp + z0] = 0.f; sl[g * rp + z0 + 1] = 0.f;
+            sl[(g + 8) * rp + z0] = 0.f; sl[(g + 8) * rp + z0 + 1] = 0.f;
+          }
         }
         acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
       }
@@ -766,12 +868,12 @@ CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& t
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
     switch ((J.rows + 7) / 8) {
-      case 1: mma_job<1>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 2: mma_job<2>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 3: mma_job<3>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 4: mma_job<4>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 5: case 6: mma_job<6>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      default: mma_job<8>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 1: mma_job<1, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 2: mma_job<2, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 3: mma_job<3, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 4: mma_job<4, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      case 5: case 6: mma_job<6, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
+      default: mma_job<4, true>(P, J, ju0, ju1, ci, tseq, S, wc); break;
     }
   }
 }
@@ -833,8 +935,8 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S) {
       }
     }
     if (P.prof) {
-      P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 8] = waited;
-      P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 9] = globaltimer();
+      P.prof[((size_t)p * P.G + blockIdx.x) * kProfSlots + 8] = waited;
+      P.prof[((size_t)p * P.G + blockIdx.x) * kProfSlots + 9] = globaltimer();
     }
   }
   // every issued copy must land before this CTA may exit (copies complete on their own)
@@ -843,48 +945,14 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S) {
 }
 
 // Activation producer (one thread): once the grid barrier in front of a phase has passed, copy
-// the activation rows each unit reads (rows x 128 fp16, or the embedding rows of a path gather)
-// into the unit's ring slot with 1-D bulk copies that complete on the slot's full barrier (the
-// same barrier the weight producer's copy completes on), so nothing here ever waits for data.
-// Absent path tokens are zero-filled with shared-memory stores before the arrive.
+// each unit's activation rows (its 128-column slice of the unit-tiled source: one contiguous
+// block) into the unit's ring slot with a 1-D bulk copy that completes on the slot's full
+// barrier (the same barrier the weight producer's copy completes on).
 CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
   const int kc = ju % J.nkc;
-  const int nkb = min(kUnitK, J.Kt - kc * kUnitK);
-  const int k0 = kc * kUnitK * 16;
-  const uint32_t rowbytes = (uint32_t)nkb * 32u;
-  uint32_t bytes = 0;
-  if (J.xkind == XK_PATH) {
-    // the unit's k range can span offsets when D is not a multiple of 128: split per offset
-    for (int r = 0; r < J.rows; ++r) {
-      const int sr = src_row(J, r);
-      for (int k = k0; k < k0 + nkb * 16;) {
-        const int j = k / J.D, d = k - j * J.D;
-        const int len = min(k0 + nkb * 16 - k, J.D - d);
-        const int64_t tok = J.lastp[(size_t)sr * J.order + j];
-        if (tok >= 0) bytes += (uint32_t)len * 2u;
-        k += len;
-      }
-    }
-    mbar_arrive_expect_tx(full, bytes);          // before the copies can complete
-    for (int r = 0; r < J.rows; ++r) {
-      const int sr = src_row(J, r);
-      for (int k = k0; k < k0 + nkb * 16;) {
-        const int j = k / J.D, d = k - j * J.D;
-        const int len = min(k0 + nkb * 16 - k, J.D - d);
-        const int64_t tok = J.lastp[(size_t)sr * J.order + j];
-        uint8_t* dst = xs + r * kXRowBytes + (k - k0) * 2;
-        if (tok >= 0) bulk_g2s(dst, J.emb + (size_t)tok * J.D + d, (uint32_t)len * 2u, full);
-        else for (int q = 0; q < len * 2; q += 16) *reinterpret_cast<uint4*>(dst + q) = make_uint4(0, 0, 0, 0);
-        k += len;
-      }
-    }
-  } else {
-    // the unit's 128-column slice of the first xcopy rows: one contiguous tiled block
-    const uint32_t bytes_t = (uint32_t)J.xcopy * 256u;
-    mbar_arrive_expect_tx(full, bytes_t);
-    bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes_t, full);
-    (void)rowbytes;
-  }
+  const uint32_t bytes = (uint32_t)J.xcopy * 256u;
+  mbar_arrive_expect_tx(full, bytes);
+  bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes, full);
 }
 
 CFB_DEV void x_producer(const Plan& P, Smem& S) {
@@ -922,7 +990,7 @@ CFB_DEV void x_producer(const Plan& P, Smem& S) {
         if (++xstage == S.nstages) { xstage = 0; xpar ^= 1u; }
       }
     }
-    if (P.prof) P.prof[((size_t)p * P.G + blockIdx.x) * 12 + 7] = globaltimer();
+    if (P.prof) P.prof[((size_t)p * P.G + blockIdx.x) * kProfSlots + 7] = globaltimer();
   }
   // every issued copy must land before this CTA may exit (copies complete on their own)
   const uint32_t first = xi > (uint32_t)S.nstages ? xi - S.nstages : 0u;
@@ -940,12 +1008,51 @@ CFB_DEV float z0_at(const Plan& P, int b, int pos, int col) {
   return last + (float)(pos + 1) * (last - prev);
 }
 
+// Head-input side rows of path-GEMM rows [row0, row0 + nrows) of a depth with R rows and `fr`
+// rows per request: the embedding rows of the last `nlive` path tokens side by side (zeros for
+// an absent token) into the path GEMM's tiled activation, and markov w1[last token] into the
+// head input's columns [D, D + rank) (reference tree_flow.py:434-450, markov_flow.py:72-74).
+// `from_known0`: depth 1, whose only path token is the committed one.
+CFB_DEV void path_gather(const Plan& P, int fr, int R, int row0, int nrows, int nlive, bool from_known0,
+                         long long t, long long nt) {
+  const int D = P.D, order = P.order, rank = P.rank;
+  const int cpe = D / 8;                         // 16-byte chunks per embedding row
+  const int cpr = nlive * cpe + rank / 8;        // chunks per gathered row
+  const long long total = (long long)nrows * cpr;
+  constexpr int kBatch = 4;                      // chunks per thread with their loads in flight together
+  for (long long it0 = t; it0 < total; it0 += kBatch * nt) {
+    uint4 val[kBatch];
+    __half* dst[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const long long it = it0 + u * nt;
+      val[u] = make_uint4(0u, 0u, 0u, 0u);
+      dst[u] = nullptr;
+      if (it >= total) continue;
+      const int i = (int)(it / cpr), q = (int)(it - (long long)i * cpr);
+      const int row = row0 + i, b = row / fr, w = row - b * fr;
+      const int64_t* lp = P.lastp + ((size_t)b * P.Wmax + w) * order;
+      if (q < nlive * cpe) {
+        const int j = q / cpe, c = q - j * cpe;
+        const int64_t tok = from_known0 ? (j == 0 ? P.known0[b] : (int64_t)-1) : lp[j];
+        if (tok >= 0 && tok < P.vocab) val[u] = *reinterpret_cast<const uint4*>(P.emb + (size_t)tok * D + c * 8);
+        dst[u] = P.pg + tidx(R, row, j * D + c * 8);
+      } else {
+        const int c = q - nlive * cpe;
+        const int64_t tok = from_known0 ? P.known0[b] : lp[0];
+        if (tok >= 0 && tok < P.vocab) val[u] = *reinterpret_cast<const uint4*>(P.markov_w1 + (size_t)tok * rank + c * 8);
+        dst[u] = P.xhead + tidx(R, row, D + c * 8);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) if (dst[u]) *reinterpret_cast<uint4*>(dst[u]) = val[u];
+  }
+}
+
 CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
   const long long gtid = (long long)blockIdx.x * W.n + W.t;
   const long long gthreads = (long long)P.G * W.n;
   for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
-  for (long long i = gtid; i < P.nattncnt; i += gthreads) P.attncnt[i] = 0u;
-  if (gtid == 0) *P.headcnt = 0u;
   const bool flow = (P.mode == CFB_MODE_FLOW || P.mode == CFB_MODE_CHAIN || P.mode == CFB_MODE_TREE);
   const int D = P.D, nparts = D / kStatCols;
   if (flow) {
@@ -1000,142 +1107,209 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
     }
   }
   if (P.mode != CFB_MODE_FLOW) {
-    // chain: W beams per request (rows b*W + w), cum = [0, -inf, ...] (flow_proposer.py:1220-1224)
-    // tree: a one-node frontier per request (row b), cum = 0 (flow_proposer.py:1289-1292)
+    // chain: W beams per request, cum = [0, -inf, ...] (flow_proposer.py:1220-1224)
+    // tree: a one-node frontier per request, cum = 0 (flow_proposer.py:1289-1292)
+    // lastp is request-major: beam w of request b is row b * Wmax + w
     const bool treem = (P.mode == CFB_MODE_TREE || P.mode == CFB_MODE_BEAM_TREE);
     const int Wm = P.Wmax, per = treem ? 1 : Wm;
     for (long long i = gtid; i < (long long)P.B * per; i += gthreads) {
-      const int b = (int)(i / per);
-      for (int j = 0; j < P.order; ++j) P.lastp[i * P.order + j] = (j == 0) ? P.known0[b] : -1;
+      const int b = (int)(i / per), w = (int)(i % per);
+      for (int j = 0; j < P.order; ++j)
+        P.lastp[((size_t)b * Wm + w) * P.order + j] = (j == 0) ? P.known0[b] : -1;
     }
     for (long long i = gtid; i < (long long)P.B * Wm; i += gthreads)
       P.cum[i] = (i % Wm == 0) ? 0.f : -INFINITY;
-  }
-}
-
-// markov bias rows of the head input: xhead[r, D + j] = w1[lastp[r, 0], j]
-CFB_DEV void markov_side(const Plan& P, const Phase& ph, const Grp& W) {
-  const long long gtid = (long long)blockIdx.x * W.n + W.t;
-  const long long gthreads = (long long)P.G * W.n;
-  const long long n = (long long)ph.rows * P.rank;
-  for (long long i = gtid; i < n; i += gthreads) {
-    const int r = (int)(i / P.rank), j = (int)(i % P.rank);
-    const int64_t tok = P.lastp[(size_t)r * P.order];
-    P.xhead[tidx(ph.rows, r, P.D + j)] = P.markov_w1[(size_t)tok * P.rank + j];
+    // depth-1 head-input side rows, straight from the committed token
+    path_gather(P, per, P.B * per, 0, P.B * per, 1, true, gtid, gthreads);
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// after the head GEMM: every CTA publishes (max, sumexp, top-k) per beam row; the last CTA to
-// arrive merges them in CTA order, finishes the log-softmax and takes the beam step (epilogue)
-CFB_DEV void head_post(const Plan& P, const Phase& ph, Smem& S, HeadState& H, const Grp& E) {
-  const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
+// after the head GEMM: every CTA publishes its (max, sumexp, top-TB) per beam row, merging the
+// row's slice lanes (their sorted lists) by TB rounds of a lane argmax
+CFB_DEV void head_post(const Plan& P, const Phase& ph, HeadState& H, const Grp& E) {
   const int rows = ph.rows, TB = ph.topb;
-  {
-    const RowMap M = row_map(rows, E.t);
-    head_group(H, TB, M.sl);
-    if (M.q == 0 && M.r < rows) {
-      float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + M.r) * kHeadPartFloats;
-      __stcg(hp + 0, H.m); __stcg(hp + 1, H.s);
-#pragma unroll
-      for (int i = 0; i < kTopMax; ++i) { __stcg(hp + 2 + i, H.tv[i]); __stcg(hp + 2 + kTopMax + i, __int_as_float(H.ti[i])); }
-    }
+  const RowMap M = row_map(rows, E.t);
+  float m = H.m, ssum = H.s;
+  lse_lanes(m, ssum, M.sl);
+  float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + M.r) * kHeadPartFloats;
+  const bool writer = M.q == 0 && M.r < rows;
+  if (writer) { __stcg(hp + 0, m); __stcg(hp + 1, ssum); }
+  int nxt = 0;
+#pragma unroll 1
+  for (int round = 0; round < TB; ++round) {
+    float v; int id;
+    list_at(H, nxt, v, id);
+    int own = M.q;
+    argmax_lanes(v, id, own, M.sl);
+    if (own == M.q) ++nxt;
+    if (writer) { __stcg(hp + 2 + round, v); __stcg(hp + 2 + kTopMax + round, __int_as_float(id)); }
   }
-  __threadfence();
-  gsync(E);
-  if (E.t == 0) {
-    const unsigned old = atom_add_acqrel(P.headcnt, 1u);
-    *S.flag = (old + 1 == (unsigned)P.G);
-    if (old + 1 == (unsigned)P.G) *P.headcnt = 0u;
-  }
-  gsync(E);
-  const bool last = *S.flag;
-  gsync(E);
-  if (!last) return;
-  __threadfence();
-  float* lp = S.scratch;                                       // [rows][kTopMax] log-probs
-  int* lid = reinterpret_cast<int*>(S.scratch + kRowsMax * kTopMax);   // shortlist-local ids
-  for (int r = warp; r < rows; r += nw) {
-    HeadState A; head_reset(A);
-    for (int c = lane; c < P.G; c += 32) {
-      const float* hp = P.hpart + ((size_t)c * kRowsMax + r) * kHeadPartFloats;
-      HeadState B;
-      B.m = __ldcg(hp); B.s = __ldcg(hp + 1);
-#pragma unroll
-      for (int i = 0; i < kTopMax; ++i) { B.tv[i] = __ldcg(hp + 2 + i); B.ti[i] = __float_as_int(__ldcg(hp + 2 + kTopMax + i)); }
-      head_merge(A, B, TB);
-    }
-    head_group(A, TB, 32);
-    if (lane == 0) {
-      const bool okrow = (A.s > 0.f) && isfinite(A.m) && isfinite(A.s);
-      const float lse = okrow ? A.m + logf(A.s) : 0.f;
-#pragma unroll
-      for (int i = 0; i < kTopMax; ++i)
-        if (i < TB) {
-          const bool ok = okrow && A.ti[i] >= 0 && A.ti[i] < P.R && !isnan(A.tv[i]);
-          lp[r * kTopMax + i] = ok ? A.tv[i] - lse : -INFINITY;
-          lid[r * kTopMax + i] = ok ? A.ti[i] : 0;
-        }
-    }
-  }
-  gsync(E);
-  // beam step, one thread per request: pick the survivors, then (after every thread has read
-  // its old rows) write the new frontier; the tree frontier changes width, so rows move
-  const int step = ph.step;
-  const int order = P.order;
+}
+
+// The beam phase: one CTA per request (reference flow_proposer.py:1234-1259 chain, :1295-1331
+// tree). Each frontier row of the request gets a group of warps; its threads follow up to
+// kMaxLists of the CTAs' published lists (sorted), the group combines their log-sum-exps in a
+// fixed order and takes the top-TB by TB rounds of a group argmax over the list heads (ties:
+// lower shortlist id). One thread then picks the survivors from shared memory; all threads
+// write the new frontier and gather the next depth's path and markov rows.
+constexpr int kMaxLists = 5;
+constexpr int kMaxDepth = 8;
+CFB_DEV void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, unsigned long long* prow) {
   const bool treem = (ph.post == PO_BEAM_TREE);
-  const int fr = treem ? ph.fr : P.width;
-  const int TB2 = treem ? ph.topb : P.width;
+  const int fr = ph.fr, TB = ph.topb, order = P.order, step = ph.step, Wm = P.Wmax;
+  const int TB2 = treem ? TB : P.width;
   const int k = treem ? min(ph.keep, fr * TB2) : P.width;
-  for (int b0 = 0; b0 < P.B; b0 += E.n) {
-    const int b = b0 + E.t;
-    HeadState C; head_reset(C);     // candidates: tv = cumulative log-prob, ti = w * TB2 + i
-    int64_t old[kTopMax][8];
-    if (b < P.B) {
-      for (int w = 0; w < fr; ++w)
-        for (int i = 0; i < TB2; ++i)
-          top_insert(C, k, P.cum[b * P.Wmax + w] + lp[(b * fr + w) * kTopMax + i], w * TB2 + i);
-      for (int w = 0; w < fr; ++w)
-        for (int j = 0; j < order; ++j) old[w][j] = P.lastp[((size_t)b * fr + w) * order + j];
-    }
-    gsync(E);
-    if (b < P.B) {
+  const int warp = W.t >> 5, lane = W.t & 31, nwarps = W.n >> 5;
+  const int wpg = max(1, nwarps / fr);              // warps per frontier row
+  const int grp = warp / wpg, gt = (warp - grp * wpg) * 32 + lane, gn = wpg * 32;
+  const bool active = grp < fr;
+  const int gbar = 3 + grp;                         // named barrier of this row group
+  // scratch (epilogue scratch is free during a beam phase)
+  float* lp = S.scratch;                                          // [row][kTopMax] log-probs
+  int* lid = reinterpret_cast<int*>(lp + kTopMax * kTopMax);      // shortlist-local ids
+  float* wv = reinterpret_cast<float*>(lid + kTopMax * kTopMax);  // per-warp argmax / lse parts
+  int* wid = reinterpret_cast<int*>(wv + 32);
+  int* wown = wid + 32;
+  float* wm = reinterpret_cast<float*>(wown + 32);
+  float* ws = wm + 32;
+  float* cumo = ws + 32;                                          // [kTopMax] cum before the step
+  float* selc = cumo + kTopMax;                                   // [kTopMax] cum after it
+  int* sel = reinterpret_cast<int*>(selc + kTopMax);              // [kTopMax] chosen candidate
+  int* hb = sel + kTopMax;                                        // [kMaxDepth][kTopMax] back-pointers
+  int64_t* oldp = reinterpret_cast<int64_t*>(hb + kMaxDepth * kTopMax);   // [kTopMax][order]
+  int64_t* ht = oldp + kTopMax * 8;                               // [kMaxDepth][kTopMax] tokens
+  for (int b = blockIdx.x; b < P.B; b += P.G) {
+    if (W.t < fr) cumo[W.t] = P.cum[b * Wm + W.t];
+    for (int e = W.t; e < fr * order; e += W.n)
+      oldp[e] = P.lastp[((size_t)b * Wm + e / order) * order + e % order];
+    if (active) {
+      const int row = b * fr + grp;
+      float hv[kMaxLists], nv[kMaxLists];
+      int hi[kMaxLists], ni[kMaxLists], pos[kMaxLists];
+      float m = -INFINITY, ssum = 0.f;
 #pragma unroll
-      for (int i = 0; i < kTopMax; ++i) {
-        if (i >= k) break;
+      for (int l = 0; l < kMaxLists; ++l) {
+        const int c = gt + l * gn;
+        hv[l] = nv[l] = -INFINITY; hi[l] = ni[l] = 0x7fffffff; pos[l] = 0;
+        if (c < P.G) {
+          const float* hp = P.hpart + ((size_t)c * kRowsMax + row) * kHeadPartFloats;
+          const float mb = __ldcg(hp), sb = __ldcg(hp + 1);
+          hv[l] = __ldcg(hp + 2); hi[l] = __float_as_int(__ldcg(hp + 2 + kTopMax));
+          if (TB > 1) { nv[l] = __ldcg(hp + 3); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax)); }
+          lse_merge(m, ssum, mb, sb);
+        }
+      }
+      if (prow && W.t == 0) prow[12] = globaltimer();
+      lse_lanes(m, ssum, 32);
+      if (lane == 0) { wm[warp] = m; ws[warp] = ssum; }
+      asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
+      m = wm[grp * wpg]; ssum = ws[grp * wpg];
+      for (int w = 1; w < wpg; ++w) lse_merge(m, ssum, wm[grp * wpg + w], ws[grp * wpg + w]);
+      const bool okrow = (ssum > 0.f) && isfinite(m) && isfinite(ssum);
+      const float lse = okrow ? m + logf(ssum) : 0.f;
+      if (prow && W.t == 0) prow[13] = globaltimer();
+#pragma unroll 1
+      for (int round = 0; round < TB; ++round) {
+        float v = -INFINITY; int id = 0x7fffffff, ol = 0;
+#pragma unroll
+        for (int l = 0; l < kMaxLists; ++l) if (better(hv[l], hi[l], v, id)) { v = hv[l]; id = hi[l]; ol = l; }
+        int own = gt;
+        argmax_lanes(v, id, own, 32);
+        asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");   // last round's reads done
+        if (lane == 0) { wv[warp] = v; wid[warp] = id; wown[warp] = own; }
+        asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
+        v = wv[grp * wpg]; id = wid[grp * wpg]; own = wown[grp * wpg];
+        for (int w = 1; w < wpg; ++w) {
+          const float vo = wv[grp * wpg + w]; const int io = wid[grp * wpg + w], oo = wown[grp * wpg + w];
+          if (better(vo, io, v, id) || (vo == v && io == id && oo < own)) { v = vo; id = io; own = oo; }
+        }
+        if (own == gt) {               // the winner moves on in the list it came from
+#pragma unroll
+          for (int l = 0; l < kMaxLists; ++l) {
+            if (l != ol) continue;
+            hv[l] = nv[l]; hi[l] = ni[l]; ++pos[l];
+            nv[l] = -INFINITY; ni[l] = 0x7fffffff;
+            if (pos[l] + 1 < TB) {
+              const float* hp = P.hpart + ((size_t)(gt + l * gn) * kRowsMax + row) * kHeadPartFloats;
+              nv[l] = __ldcg(hp + 3 + pos[l]); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax + pos[l]));
+            }
+          }
+        }
+        if (gt == 0) {
+          const bool ok = okrow && id >= 0 && id < P.R && !isnan(v) && v != -INFINITY;
+          lp[grp * kTopMax + round] = ok ? v - lse : -INFINITY;
+          lid[grp * kTopMax + round] = ok ? id : 0;
+        }
+      }
+      if (prow && W.t == 0) prow[14] = globaltimer();
+    }
+    gsync(W);
+    if (prow && W.t == 0) prow[16] = globaltimer();
+    // survivors: the best k of cum[w] + lp[w][i] (one thread, shared memory only)
+    if (W.t == 0) {
+      HeadState C; head_reset(C);     // tv = cumulative log-prob, ti = w * TB2 + i
+#pragma unroll 1
+      for (int w = 0; w < fr; ++w)
+#pragma unroll 1
+        for (int i = 0; i < TB2; ++i) top_insert(C, k, cumo[w] + lp[w * kTopMax + i], w * TB2 + i);
+#pragma unroll 1
+      for (int i = 0; i < k; ++i) {
+        float cv; int cid;
+        list_at(C, i, cv, cid);
         // candidate ids are < fr * TB2 by construction; clamp anyway so that no value read back
         // from memory can ever become an out-of-range index
-        const int cid = min(max(C.ti[i], 0), fr * TB2 - 1);
-        const int src = cid / TB2, ii = cid % TB2;
-        const int loc = lid[(b * fr + src) * kTopMax + ii];
-        const int64_t tok = (loc >= 0 && loc < P.R) ? P.shortlist[loc] : (int64_t)0;
-        P.cum[b * P.Wmax + i] = C.tv[i];
-        int64_t* lpn = P.lastp + ((size_t)b * k + i) * order;
-        lpn[0] = tok;
-        for (int j = 1; j < order; ++j) lpn[j] = old[src][j - 1];
+        sel[i] = min(max(cid, 0), fr * TB2 - 1);
+        selc[i] = cv;
+      }
+    }
+    gsync(W);
+    // the new frontier: path rows, cum, and this depth's tokens
+    for (int e = W.t; e < k * order; e += W.n) {
+      const int i = e / order, j = e - i * order;
+      const int src = sel[i] / TB2, ii = sel[i] - src * TB2;
+      int64_t v;
+      if (j == 0) {
+        const int loc = lid[src * kTopMax + ii];
+        v = (loc >= 0 && loc < P.R) ? P.shortlist[loc] : (int64_t)0;
+        P.cum[b * Wm + i] = selc[i];
         if (treem) {
-          P.tokens[(size_t)b * 2 * P.N + ph.base + i] = tok;
-          P.tokens[(size_t)b * 2 * P.N + P.N + ph.base + i] =
-              (step == 1) ? (int64_t)-1 : (int64_t)(ph.base_prev + src);
+          P.tokens[(size_t)b * 2 * P.N + ph.base + i] = v;
+          P.tokens[(size_t)b * 2 * P.N + P.N + ph.base + i] = (step == 1) ? (int64_t)-1 : (int64_t)(ph.base_prev + src);
         } else {
-          P.toks[((size_t)(step - 1) * P.B + b) * P.width + i] = tok;
+          P.toks[((size_t)(step - 1) * P.B + b) * P.width + i] = v;
           P.bps[((size_t)(step - 1) * P.B + b) * P.width + i] = src;
         }
+      } else {
+        v = oldp[src * order + j - 1];
       }
-      if (!treem && ph.last) {
-        // walk the best beam back (flow_proposer.py:1261-1267); argmax keeps the first maximum
-        const int W = P.width;
+      P.lastp[((size_t)b * Wm + i) * order + j] = v;
+    }
+    gsync(W);
+    if (prow && W.t == 0) prow[17] = globaltimer();
+    if (!treem && ph.last) {
+      // walk the best beam back (flow_proposer.py:1261-1267); argmax keeps the first maximum.
+      // Every depth's tokens and back-pointers are staged first, in parallel.
+      const int Wd = P.width;
+      for (int e = W.t; e < step * Wd; e += W.n) {
+        ht[e] = P.toks[((size_t)(e / Wd) * P.B + b) * Wd + e % Wd];
+        hb[e] = P.bps[((size_t)(e / Wd) * P.B + b) * Wd + e % Wd];
+      }
+      gsync(W);
+      if (W.t == 0) {
         int idx = 0;
-        for (int i = 1; i < W; ++i) if (P.cum[b * W + i] > P.cum[b * W + idx]) idx = i;
+        for (int i = 1; i < Wd; ++i) if (selc[i] > selc[idx]) idx = i;
         for (int s2 = step; s2 >= 1; --s2) {
-          P.tokens[(size_t)b * P.depth + (s2 - 1)] = P.toks[((size_t)(s2 - 1) * P.B + b) * W + idx];
-          idx = P.bps[((size_t)(s2 - 1) * P.B + b) * W + idx];
+          P.tokens[(size_t)b * P.depth + (s2 - 1)] = ht[(s2 - 1) * Wd + idx];
+          idx = min(max(hb[(s2 - 1) * Wd + idx], 0), Wd - 1);
         }
       }
     }
-    gsync(E);
+    // the next depth's path-GEMM and markov rows of this request
+    if (!ph.last) path_gather(P, k, P.B * k, b * k, k, min(step + 1, order), false, W.t, W.n);
+    gsync(W);
+    if (prow && W.t == 0) prow[18] = globaltimer();
   }
-  __threadfence();
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1191,20 +1365,27 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   wc.on = rec;
   for (int p = 0; p < P.nphases && ok; ++p) {
     const Phase& ph = P.phases[p];
-    unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * 12 : nullptr;
+    unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * kProfSlots : nullptr;
     unsigned long long* stamp = (P.prof && Wk.t == 0) ? prow : nullptr;
     wc.full = wc.slot = wc.first = wc.last = 0;
+    wc.part = wc.atom = wc.fix = wc.tdone = 0;
     if (stamp) stamp[0] = globaltimer();
     if (Wk.t == 0) *S.phase_ready = p;
     if (ph.kind == PK_PREP) {
       prep_phase(P, Wk);
+    } else if (ph.kind == PK_ATTN) {
+      attn_phase(P, ph, S, Wk);
+    } else if (ph.kind == PK_BEAM) {
+      beam_phase(P, ph, S, Wk, P.prof ? prow : nullptr);
     } else {
-      if (ph.side_markov) markov_side(P, ph, Wk);
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
         epi_phase(P, ph, tseq, S, H, E, wc);
-        if (ph.post != PO_NONE) head_post(P, ph, S, H, E);
-        if (rec) { prow[5] = wc.slot; prow[6] = globaltimer(); }
+        if (ph.post != PO_NONE) head_post(P, ph, H, E);
+        if (rec) {
+          prow[5] = wc.slot; prow[6] = globaltimer();
+          prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
+        }
       } else {
         mma_phase(P, ph, ci, tseq, S, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
@@ -1256,7 +1437,7 @@ struct Arena {
 };
 
 // fixed offsets at the start of every workspace: plan record, then the 64-byte barrier block
-// (bar, exitcnt, headcnt, err; launch record at +32)
+// (bar, exitcnt, spare, err; launch record at +32)
 constexpr size_t kOffPlan = 0;
 size_t off_barrier() { Arena A; A.take(sizeof(cfb::Plan)); return A.take(64); }
 
@@ -1271,6 +1452,7 @@ struct Builder {
   cfb::Plan P{};
   size_t off_phases = 0, off_jobs = 0, off_attn = 0;
   int max_tiles = 0;
+  bool too_big = false;          // a phase's units x grid overflows the kernel's 32-bit range math
   int G = 148;                   // persistent grid the phases are cut for
   template <class T> T* dptr(size_t off) { return reinterpret_cast<T*>(base + off); }
 };
@@ -1293,7 +1475,6 @@ cfb::Job make_job(const cfb_linear& L, int rows) {
   J.gin = rows > 0 ? rows : 1; J.gstride = 0; J.goff = 0;
   J.bias = L.bias;
   J.colsum = L.colsum;
-  J.attn = -1;
   return J;
 }
 
@@ -1308,9 +1489,10 @@ void add_phase(Builder& B, cfb::Phase ph, const std::vector<cfb::Job>& js) {
     B.jobs.push_back(j);
   }
   ph.nunits = (int)u; ph.ntiles = t;
+  if ((unsigned long long)u * (unsigned long long)(B.G + 1) >= (1ull << 32)) B.too_big = true;
   // Whole tiles per CTA (no cross-CTA fixup) unless splitting tiles finishes sooner even after
   // paying for the fixup, which costs about as much as streaming kFixupUnits units.
-  constexpr long long kFixupUnits = 24;
+  constexpr long long kFixupUnits = 6;
   long long nkc_max = 1;
   for (const auto& j : js) nkc_max = std::max<long long>(nkc_max, j.nkc);
   const long long G = B.G;
@@ -1372,6 +1554,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
     G = sms;
   }
   B.G = G;
+  // the beam merge: each thread follows at most kMaxLists of the G published lists per row
+  if (beam && (G + 32 * std::max(1, (cfb::kWorkers / 32) / Wmax) - 1) / (32 * std::max(1, (cfb::kWorkers / 32) / Wmax)) > cfb::kMaxLists)
+    return CFB_ERR_UNSUPPORTED;
+  if (beam && K > cfb::kMaxDepth) return CFB_ERR_UNSUPPORTED;
 
   Arena& A = B.A;
   A.off = 0;
@@ -1404,7 +1590,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
   const int rank = d.markov_rank, order = d.path_order;
   const int P2 = beam ? d.path_up.nout : 0;
   const int rowsB = Bq * std::max(Wmax, 1);
-  size_t o_lastp = 0, o_cum = 0, o_toks = 0, o_bps = 0, o_h16 = 0, o_hstat = 0, o_mpath = 0, o_xhead = 0;
+  size_t o_lastp = 0, o_cum = 0, o_toks = 0, o_bps = 0, o_h16 = 0, o_hstat = 0, o_mpath = 0, o_xhead = 0, o_pg = 0;
   if (beam) {
     o_lastp = A.take((size_t)rowsB * order * 8);
     o_cum = A.take((size_t)rowsB * 4);
@@ -1414,8 +1600,9 @@ cfb_status lower(Builder& B, size_t* bytes) {
     o_hstat = A.take((size_t)rowsB * nparts * 8);
     o_mpath = A.take((size_t)rowsB * k128(P2) * 2);
     o_xhead = A.take((size_t)rowsB * k128(D + rank) * 2);
+    o_pg = A.take((size_t)rowsB * k128(order * D) * 2);
   }
-  const size_t o_gpart = A.take((size_t)G * 2 * cfb::kTileRows * cfb::kRowsMax * 4);
+  const size_t o_gpart = A.take((size_t)G * cfb::kTileRows * cfb::kRowsMax * 4);
   const bool profile = (r.flags & CFB_RUN_PROFILE) != 0;
   const size_t o_hpart = A.take((size_t)G * cfb::kRowsMax * cfb::kHeadPartFloats * 4);
 
@@ -1423,7 +1610,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
   B.jobs.clear();
   auto& at = B.attn; at.clear();
   B.max_tiles = 0;
-  B.P.nattncnt = 0;
+  B.too_big = false;
 
   { cfb::Phase p{}; p.kind = cfb::PK_PREP; ph.push_back(p); }
 
@@ -1444,32 +1631,36 @@ cfb_status lower(Builder& B, size_t* bytes) {
         }
       add_phase(B, cfb::Phase{}, js);
     }
-    std::vector<int> at_self(E), at_cross(E * L);
-    int cntoff = 0;
+    // attention tasks: the E self-attentions first, then the cross-attentions by (block, expert),
+    // so that each attention phase covers one contiguous range of tasks
     for (int e = 0; e < E; ++e) {
       const int S = (e + 1) * d.chunk;
       cfb::AttnTask a{};
       a.q = B.dptr<float>(o_qkv[e]); a.ldq = 3 * D; a.qoff = 0;
       a.k = a.q; a.ldk = 3 * D; a.koff = D;
       a.v = a.q; a.ldv = 3 * D; a.voff = 2 * D;
-      a.out = B.dptr<__half>(o_o[e]); a.ldo = D;
+      a.out = B.dptr<__half>(o_o[e]);
       a.rows_per_req = S; a.keys_per_req = S; a.B = Bq; a.hd = hd; a.heads = d.heads;
-      a.causal = 1; a.nsec = 3; a.Dsec = D; a.scale = 1.0f / std::sqrt((float)hd); a.outR = Bq * S;
-      a.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
-      at_self[e] = (int)at.size(); at.push_back(a);
-      for (int l = 0; l < L; ++l) {
+      a.causal = 1; a.scale = 1.0f / std::sqrt((float)hd); a.outR = Bq * S;
+      at.push_back(a);
+    }
+    for (int l = 0; l < L; ++l)
+      for (int e = 0; e < E; ++e) {
+        const int S = (e + 1) * d.chunk;
         cfb::AttnTask c{};
         c.q = B.dptr<float>(o_qc[e]); c.ldq = D; c.qoff = 0;
         c.k = B.dptr<float>(o_kvc[e]) + (size_t)l * Bq * C * 2 * D; c.ldk = 2 * D; c.koff = 0;
         c.v = c.k; c.ldv = 2 * D; c.voff = D;
-        c.out = B.dptr<__half>(o_o[e]); c.ldo = D;
+        c.out = B.dptr<__half>(o_o[e]);
         c.rows_per_req = S; c.keys_per_req = C; c.B = Bq; c.hd = hd; c.heads = d.heads;
-        c.causal = 0; c.nsec = 1; c.Dsec = D; c.scale = 1.0f / std::sqrt((float)hd); c.outR = Bq * S;
-        c.cnt = reinterpret_cast<unsigned*>((uintptr_t)cntoff); cntoff += d.heads;
-        at_cross[e * L + l] = (int)at.size(); at.push_back(c);
+        c.causal = 0; c.scale = 1.0f / std::sqrt((float)hd); c.outR = Bq * S;
+        at.push_back(c);
       }
-    }
-    B.P.nattncnt = cntoff;
+    auto add_attn = [&](int first) {
+      cfb::Phase p{};
+      p.kind = cfb::PK_ATTN; p.job0 = first; p.njobs = E; p.ntiles = E * Bq * d.heads;
+      ph.push_back(p);
+    };
     for (int s = 0; s < T; ++s) {
       const int pb = s & 1;
       auto ln_job = [&](const cfb_linear& lin, int e) {
@@ -1495,10 +1686,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
           if (!lin_ok(bl.qkv, 3 * D, D)) return CFB_ERR_INVALID_ARG;
           cfb::Job J = ln_job(bl.qkv, e);
           J.ekind = cfb::EK_STORE; J.out32 = B.dptr<float>(o_qkv[e]); J.ldo = 3 * D;
-          J.attn = at_self[e];
           js.push_back(J);
         }
         add_phase(B, cfb::Phase{}, js); js.clear();
+        add_attn(0);
         for (int e = 0; e < E; ++e) {           // out-projection + residual
           const cfb_block& bl = d.experts[e].blocks[l];
           if (!lin_ok(bl.self_out, D, D)) return CFB_ERR_INVALID_ARG;
@@ -1510,10 +1701,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
           if (!lin_ok(bl.cross_q, D, D)) return CFB_ERR_INVALID_ARG;
           cfb::Job J = ln_job(bl.cross_q, e);
           J.ekind = cfb::EK_STORE; J.out32 = B.dptr<float>(o_qc[e]); J.ldo = D;
-          J.attn = at_cross[e * L + l];
           js.push_back(J);
         }
         add_phase(B, cfb::Phase{}, js); js.clear();
+        add_attn(E + l * E);
         for (int e = 0; e < E; ++e) {
           const cfb_block& bl = d.experts[e].blocks[l];
           if (!lin_ok(bl.cross_out, D, D)) return CFB_ERR_INVALID_ARG;
@@ -1558,16 +1749,17 @@ cfb_status lower(Builder& B, size_t* bytes) {
       const int rows = Bq * fr;
       const int nlive = std::min(step, order);
       {   // h = sum_j mask_j (W_j emb(lastp_j) + b_j) over the live offsets (CF_PATH_TRIM)
+        // over the embedding rows the previous beam phase (or prep, at depth 1) gathered
         cfb::Job J = make_job(d.path_offsets, rows);
         J.Kt = nlive * D / 16;
         J.nkc = (J.Kt + cfb::kUnitK - 1) / cfb::kUnitK;
-        J.xkind = cfb::XK_PATH; J.lastp = B.dptr<int64_t>(o_lastp); J.order = order;
-        J.emb = static_cast<const __half*>(d.embed); J.D = D;
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_pg); J.ldx = order * D;
+        J.order = order; J.D = D; J.wrows = fr;
         J.ekind = cfb::EK_PATHH; J.bias = nullptr; J.colsum = nullptr;
         J.p0 = d.path_offset_bias; J.nlive = nlive;
         J.out16 = B.dptr<__half>(o_h16); J.ldo = D;
         J.ostats = B.dptr<float2>(o_hstat); J.onparts = nparts;
-        cfb::Phase p{}; p.side_markov = 1; p.rows = rows; p.step = step;
+        cfb::Phase p{}; p.rows = rows; p.step = step;
         add_phase(B, p, {J});
       }
       {   // LayerNorm + Linear(D, 2D) + GELU
@@ -1584,15 +1776,21 @@ cfb_status lower(Builder& B, size_t* bytes) {
         J.step = step; J.wrows = fr;
         add_phase(B, cfb::Phase{}, {J});
       }
-      {   // shortlist head + markov bias with online LSE + top-k, then the beam step
+      {   // shortlist head + markov bias with online LSE + top-k per CTA
         cfb::Job J = make_job(d.head, rows);
         J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_xhead); J.ldx = D + rank;
         J.ekind = cfb::EK_HEAD; J.R = d.shortlist_rows; J.topb = TB; J.bias = nullptr; J.colsum = nullptr;
         cfb::Phase p{};
+        p.post = cfb::PO_PUBLISH; p.rows = rows; p.topb = TB;
+        add_phase(B, p, {J});
+      }
+      {   // merge the CTAs' lists, beam step, next depth's gather
+        cfb::Phase p{};
+        p.kind = cfb::PK_BEAM;
         p.post = tree ? cfb::PO_BEAM_TREE : cfb::PO_BEAM_CHAIN;
         p.rows = rows; p.step = step; p.fr = fr; p.keep = Wmax; p.topb = TB;
         p.base = base; p.base_prev = base_prev; p.last = (step == K);
-        add_phase(B, p, {J});
+        ph.push_back(p);
       }
       if (tree) {
         const int k = std::min(Wmax, fr * TB);
@@ -1640,14 +1838,13 @@ cfb_status lower(Builder& B, size_t* bytes) {
     Lm.off_misc = Lm.off_tile + 2 * cfb::kTileRows * 4;
     Lm.total = Lm.off_misc + misc;
   }
-  const size_t o_prof = profile ? A.take(ph.size() * (size_t)G * 12 * 8) : 0;
+  if (B.too_big) return CFB_ERR_UNSUPPORTED;
+  const size_t o_prof = profile ? A.take(ph.size() * (size_t)G * cfb::kProfSlots * 8) : 0;
   const size_t o_tilecnt = A.take((size_t)std::max(B.max_tiles, 1) * 4);
-  const size_t o_attncnt = A.take((size_t)std::max(B.P.nattncnt, 1) * 4);
   B.off_phases = A.take(ph.size() * sizeof(cfb::Phase));
   B.off_jobs = A.take(std::max<size_t>(B.jobs.size(), 1) * sizeof(cfb::Job));
   B.off_attn = A.take(std::max<size_t>(at.size(), 1) * sizeof(cfb::AttnTask));
   *bytes = A.take(0);
-  for (auto& a : at) a.cnt = B.dptr<unsigned>(o_attncnt) + reinterpret_cast<uintptr_t>(a.cnt);
 
   cfb::Plan& P = B.P;
   P.G = G; P.nphases = (int)ph.size(); P.mode = mode; P.B = Bq; P.D = D; P.DL = DL;
@@ -1672,12 +1869,11 @@ cfb_status lower(Builder& B, size_t* bytes) {
   }
   if (profile) {
     P.prof = B.dptr<unsigned long long>(o_prof);
-    P.buf[CFB_BUF_PROF] = P.prof; P.buf_bytes[CFB_BUF_PROF] = ph.size() * (size_t)G * 12 * 8;
+    P.buf[CFB_BUF_PROF] = P.prof; P.buf_bytes[CFB_BUF_PROF] = ph.size() * (size_t)G * cfb::kProfSlots * 8;
   }
-  P.bar = B.dptr<unsigned>(o_bar); P.exitcnt = P.bar + 1; P.headcnt = P.bar + 2;
+  P.bar = B.dptr<unsigned>(o_bar); P.exitcnt = P.bar + 1;
   P.err = reinterpret_cast<int*>(P.bar + 3);
   P.tilecnt = B.dptr<unsigned>(o_tilecnt); P.ntilecnt = B.max_tiles;
-  P.attncnt = B.dptr<unsigned>(o_attncnt);
   P.gpart = B.dptr<float>(o_gpart); P.hpart = B.dptr<float>(o_hpart);
   P.ctx = static_cast<const __half*>(r.ctx); P.z0 = static_cast<const __half*>(r.z0);
   P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs); P.init_mode = r.init_mode;
@@ -1704,6 +1900,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
     P.toks = B.dptr<int64_t>(o_toks); P.bps = B.dptr<int>(o_bps);
     P.shortlist = d.shortlist; P.markov_w1 = static_cast<const __half*>(d.markov_w1);
     P.xhead = B.dptr<__half>(o_xhead); P.ldxhead = D + rank;
+    P.emb = static_cast<const __half*>(d.embed); P.pg = B.dptr<__half>(o_pg);
   }
   return CFB_OK;
 }

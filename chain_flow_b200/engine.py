@@ -98,12 +98,12 @@ class Plan:
         return self.ws[off:off + n * elt].view(dtype).view(*shape).clone()
 
     def phase_times(self) -> torch.Tensor:
-        """[phases, grid, 12] int64 ns of the last profiled run (see CFB_BUF_PROF in cfb.h).
+        """[phases, grid, 20] int64 ns of the last profiled run (see CFB_BUF_PROF in cfb.h).
         Needs a plan built with profile=True."""
-        return self.buffer(_lib.BUF_PROF, torch.int64, (self.phases, self.grid, 12))
+        return self.buffer(_lib.BUF_PROF, torch.int64, (self.phases, self.grid, 20))
 
     def device_error(self) -> int:
-        """Synchronous read of the device error word (0 = the last run completed normally)."""
+        """Synchronous read of the plan's sticky device error word (0 = every run so far completed)."""
         v = C.c_int(0)
         self.lib.cfb_plan_error(C.c_void_p(self.ws_ptr), C.byref(v))
         return v.value

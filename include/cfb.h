@@ -183,14 +183,18 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  * CFB_BUF_KVC0       fp32 [L, B*ctx, 2D] expert 0 cross-attention K/V of every block
  * Values hold what the last completed run left there. */
 #define CFB_RUN_PROFILE 1
-/* CFB_BUF_PROF        uint64 [phases, grid, 12] per CTA, %globaltimer ns: [0] phase start,
+/* CFB_BUF_PROF        uint64 [phases, grid, 20] per CTA, %globaltimer ns: [0] phase start,
  *                     [1] work done, [2] grid barrier passed, [3] MMA warps waiting for data,
  *                     [4] MMA warps waiting for a free accumulator slot, [5] epilogue waiting for
  *                     partials, [6] epilogue done, [7] activation copies all issued, [8] weight
  *                     producer waiting for a free ring slot, [9] weight units all issued,
  *                     [10] / [11] the MMA warps' first / last unit of the phase ready (0 if
- *                     the CTA had no unit); written only by runs of plans built with
- *                     CFB_RUN_PROFILE */
+ *                     the CTA had no unit); for the epilogue's last tile of the phase: [12]
+ *                     partials ready, [13] split-tile counter updated, [14] split-tile partials
+ *                     summed (0 if not applicable), [15] tile finished; beam phases, in the
+ *                     CTAs that own a request: [16] lists merged, [17] beam step done, [18] next
+ *                     depth's rows gathered; [19] unused; written only by runs of plans built
+ *                     with CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
 enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
        CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
