@@ -42,7 +42,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-drafts", type=int, default=0, help="CPU baseline sample size (0 = auto)")
@@ -201,13 +201,14 @@ def run_ours(args, wl):
     ctx, known0 = make_inputs(wl, B, seed=1 + rank, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    # ---- device-resident throughput: K drafts, inputs in HBM
+    # ---- device-resident throughput: K drafts, inputs in HBM. The clock sampler starts first:
+    # nvidia-smi's start-up must not fall inside the timed region.
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(1.0)
     for _ in range(args.warmup):
         prop._beam_chains(ctx, known0)
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.2)
     barrier(); torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -264,12 +265,13 @@ def run_ours(args, wl):
         peak, peak_kind = measured_peaks()
         algo = wl.weight_bytes_per_draft()
         achieved = algo / (kernel_ms / 1e3) / 1e9
-        traffic = None
+        traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "engine_dram_traffic.json"
         if tf.exists():
             t = json.loads(tf.read_text()).get(wl.name)
             if t and int(t.get("batch", -1)) == B:
                 traffic = t.get("bytes_per_launch")
+                traffic_note = "measured" if t.get("measured") else f"scaled from {t.get('scaled_from')}"
         tokens = world * B * wl.draft_tokens
         line = {
             "metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
@@ -280,12 +282,14 @@ def run_ours(args, wl):
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
                        "beam_width": wl.width, "parallelism": f"requests split over {world} GPU(s)",
-                       "l2": "inputs larger than L2: 2.6 GB of weights stream from HBM every step"},
+                       "l2": f"inputs larger than L2: {prop.weights.packed_bytes / 1e9:.2f} GB of packed "
+                             f"weights stream from HBM every step"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
+                         "peak_source": peak_kind,
                          "kernel": "engine_kernel", "kernel_ms": kernel_ms,
                          "algorithmic_bytes_per_launch": algo},
             "clocks": clk,

@@ -65,6 +65,9 @@ WORKLOADS = {
     "4b": Workload("cfg2-4B-shaped", hidden=2560, layers=4, steps=8),
     # Qwen3.5-27B-shaped drafter
     "27b": Workload("cfg3-27B-shaped", hidden=5120, layers=4, steps=8),
+    # profiler-sized 4B-width case: one block, one Euler step, a 65,536-row vocabulary (about
+    # 1.3 GB on the device, still far larger than L2), for full hardware-counter captures
+    "4b-ncu": Workload("4B-width-ncu-case", hidden=2560, layers=1, steps=1, vocab=65536),
 }
 
 

@@ -192,5 +192,10 @@ class DrafterWeights:
                            colsum.data_ptr() if colsum is not None else None, nout, k)
 
     @property
+    def packed_bytes(self) -> int:
+        """Bytes of packed weight buffers (what the engine streams)."""
+        return sum(t.numel() for t in self._keep if t.dtype == torch.uint8)
+
+    @property
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self._keep) + self.embed.numel() * 2
