@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
     ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--head-shard", default="auto", choices=["auto", "on", "off"],
+                    help="row-shard the shortlist head across the GPUs (auto: the 27B shape on >1 GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-drafts", type=int, default=0, help="CPU baseline sample size (0 = auto)")
     return ap.parse_args()
@@ -193,12 +195,18 @@ def run_ours(args, wl):
         return float(t.item())
 
     B = args.batch
+    shard = world > 1 and (args.head_shard == "on" or (args.head_shard == "auto" and wl.hidden >= 5120))
     sd, emb, lm, sl = make_state(wl, seed=0, device=dev)
+    # sharded head: every rank drafts the same requests (same inputs and noise), each over its
+    # share of the head rows; otherwise each rank drafts its own requests
     prop = FlowDrafterProposer.from_components(sd, wl.model_args(), emb, lm, sl, width=wl.width,
-                                               K=wl.draft_tokens, device=dev, seed=1000 + rank)
+                                               K=wl.draft_tokens, device=dev,
+                                               seed=1000 + (0 if shard else rank),
+                                               head_shard=(rank, world) if shard else None,
+                                               group=dist.group.WORLD if shard else None)
     del sd, lm
     torch.cuda.empty_cache()
-    ctx, known0 = make_inputs(wl, B, seed=1 + rank, device=dev)
+    ctx, known0 = make_inputs(wl, B, seed=1 + (0 if shard else rank), device=dev)
     stream = torch.cuda.current_stream(dev)
 
     # ---- device-resident throughput: K drafts, inputs in HBM. The clock sampler starts first:
@@ -227,7 +235,7 @@ def run_ours(args, wl):
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0.record(stream)
     for _ in range(args.steps):
-        plan.run(stream)
+        plan.run(group=prop.group)
     k1.record(stream)
     torch.cuda.synchronize(dev)
     kernel_ms = max_over_ranks(k0.elapsed_time(k1) / args.steps)
@@ -263,7 +271,7 @@ def run_ours(args, wl):
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        algo = wl.weight_bytes_per_draft()
+        algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0)   # per GPU
         achieved = algo / (kernel_ms / 1e3) / 1e9
         traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "engine_dram_traffic.json"
@@ -272,21 +280,24 @@ def run_ours(args, wl):
             if t and int(t.get("batch", -1)) == B:
                 traffic = t.get("bytes_per_launch")
                 traffic_note = "measured" if t.get("measured") else f"scaled from {t.get('scaled_from')}"
-        tokens = world * B * wl.draft_tokens
+        tokens = (1 if shard else world) * B * wl.draft_tokens
         line = {
             "metric": METRIC, "value": tokens / (ms / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "scaling": "strong" if shard else "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init reference-architecture drafter, N(0,1) hidden states)",
             "config": {"workload": wl.name, "batch_per_gpu": B, "draft_tokens": wl.draft_tokens,
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
-                       "beam_width": wl.width, "parallelism": f"requests split over {world} GPU(s)",
+                       "beam_width": wl.width,
+                       "parallelism": (f"shortlist head rows sharded over {world} GPUs, flow replicated, "
+                                       f"one NCCL all_gather of merged top-k lists per depth") if shard
+                       else f"requests split over {world} GPU(s)",
                        "l2": f"inputs larger than L2: {prop.weights.packed_bytes / 1e9:.2f} GB of packed "
                              f"weights stream from HBM every step"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * plan.segments,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
                          "peak_source": peak_kind,

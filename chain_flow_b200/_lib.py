@@ -27,7 +27,10 @@ EXPORTED = [
     "cfb_abi_version", "cfb_last_cuda_error", "cfb_packed_bytes", "cfb_pack_linear",
     "cfb_fold_bias", "cfb_time_embed", "cfb_plan_workspace", "cfb_plan_build", "cfb_plan_run",
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
+    "cfb_plan_segments", "cfb_plan_run_segment",
 ]
+ABI_VERSION = 2
+XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF = range(9)
 RUN_PROFILE = 1
 
@@ -58,14 +61,16 @@ class Drafter(C.Structure):
                 ("path_order", C.c_int), ("markov_rank", C.c_int), ("vocab", C.c_int),
                 ("shortlist_rows", C.c_int), ("embed", C.c_void_p), ("path_offsets", Linear),
                 ("path_offset_bias", C.c_void_p), ("path_up", Linear), ("path_down", Linear),
-                ("markov_w1", C.c_void_p), ("head", Linear), ("shortlist", C.c_void_p)]
+                ("markov_w1", C.c_void_p), ("head", Linear), ("shortlist", C.c_void_p),
+                ("head_row0", C.c_int)]
 
 
 class Run(C.Structure):
     _fields_ = [("mode", C.c_int), ("init_mode", C.c_int), ("batch", C.c_int), ("width", C.c_int), ("depth", C.c_int),
                 ("tree_keep", C.c_int), ("tree_topb", C.c_int), ("grid", C.c_int), ("flags", C.c_int),
                 ("ctx", C.c_void_p), ("z0", C.c_void_p), ("known0", C.c_void_p),
-                ("pred", C.c_void_p), ("tokens", C.c_void_p)]
+                ("pred", C.c_void_p), ("tokens", C.c_void_p),
+                ("ranks", C.c_int), ("rank", C.c_int), ("xloc", C.c_void_p), ("xall", C.c_void_p)]
 
 
 _lock = threading.Lock()
@@ -84,6 +89,8 @@ def _declare(lib):
     lib.cfb_plan_workspace.argtypes = [C.POINTER(Drafter), C.POINTER(Run), C.POINTER(sz)]
     lib.cfb_plan_build.argtypes = [C.POINTER(Drafter), C.POINTER(Run), vp, sz]
     lib.cfb_plan_run.argtypes = [vp, vp]
+    lib.cfb_plan_segments.argtypes = [vp, C.POINTER(i32)]
+    lib.cfb_plan_run_segment.argtypes = [vp, i32, vp]
     lib.cfb_plan_error.argtypes = [vp, C.POINTER(i32)]
     lib.cfb_plan_info.argtypes = [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]
     lib.cfb_plan_buffer.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(sz)]
@@ -103,7 +110,7 @@ def load(build_if_missing: bool = True):
             if not LIB_PATH.exists():
                 raise CfbError(f"{LIB_PATH} is missing; build it with `python -m chain_flow_b200.build`")
             _lib = _declare(C.CDLL(str(LIB_PATH)))
-            if _lib.cfb_abi_version() != 1:
+            if _lib.cfb_abi_version() != ABI_VERSION:
                 raise CfbError("libcfb.so ABI version mismatch; rebuild it")
     return _lib
 

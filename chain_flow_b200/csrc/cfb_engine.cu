@@ -42,6 +42,7 @@
 #include <cstdio>
 #include <vector>
 #include <algorithm>
+#include <mutex>
 
 #include "cfb_common.cuh"
 #include "../../include/cfb.h"
@@ -72,6 +73,8 @@ constexpr int kTopMax = 8;                          // top-k per beam row
 constexpr int kMaxExperts = 4;
 constexpr int kStatCols = 64;                       // columns per row-statistics part
 constexpr int kHeadPartFloats = 2 + 2 * kTopMax;
+static_assert(kRowsMax == CFB_XROWS && kHeadPartFloats == CFB_XFLOATS, "xloc layout of cfb.h");
+constexpr int kMaxSeg = 16;                         // launch segments of a plan (sharded heads)
 
 enum XKind : int { XK_F16 = 0 };
 
@@ -85,7 +88,7 @@ CFB_DEV size_t tidx(int R, int r, int k) {
 enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
 enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
                    EK_HEADIN = 5, EK_HEAD = 6 };
-enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3 };
+enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4 };
 enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
 // Attention of one (expert, block): q rows [B*Sq] and k/v rows [B*Kn] (fp32, written by the
@@ -123,6 +126,7 @@ struct Job {
   float* out32; __half* out16; int ldo; int oR;   // out32 row stride; out16 tiled rows
   float2* ostats; int onparts;
   int e_idx, step, last_step, wrows, nlive, R, topb;
+  int rowoff;                              // EK_HEAD: shortlist row of the head's first row
   float dt;
   const float* p0;                         // EK_PATHH: offset biases [order][D]
 };
@@ -160,6 +164,8 @@ struct Plan {
   const int64_t* known0; int64_t* lastp; float* cum; int64_t* toks; int* bps; int64_t* tokens;
   const int64_t* shortlist; const __half* markov_w1; __half* xhead; int ldxhead;
   const __half* emb; __half* pg;            // embeddings; tiled path-gather rows of the path GEMM
+  int nranks; const float* xall; float* xloc;   // row-sharded head: gathered / local merged lists
+  int nseg; int seg[kMaxSeg + 1];           // launch segments: phases [seg[i], seg[i + 1])
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
   unsigned long long* prof;                // [nphases][G][4] or NULL
 };
@@ -585,7 +591,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
           const float v = S.red[f * S.rp + M.r];
           if (v > H.m) { H.s = H.s * __expf(H.m - v) + 1.f; H.m = v; }
           else H.s += __expf(v - H.m);
-          top_insert(H, J.topb, v, j);
+          top_insert(H, J.topb, v, j + J.rowoff);
         }
       }
       break;
@@ -897,7 +903,7 @@ CFB_DEV void epi_phase(const Plan& P, const Phase& ph, uint32_t& tseq, Smem& S, 
 
 // Weight producer (one thread): stream this CTA's packed weight units of every GEMM phase into
 // the ring with cp.async.bulk, running ahead of the consumers across phase boundaries.
-CFB_DEV void weight_producer(const Plan& P, Smem& S) {
+CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
   uint32_t pi = 0;
   int stage = 0;
   uint32_t par = 1u;                 // a fresh mbarrier's previous phase counts as complete
@@ -905,7 +911,7 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S) {
   const int nst = S.nstages;
   const int* err = P.err;
   const bool prof = P.prof != nullptr;
-  for (int p = 0; p < P.nphases && ok; ++p) {
+  for (int p = p0; p < p1 && ok; ++p) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
     unsigned long long waited = 0;
@@ -955,12 +961,12 @@ CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
   bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes, full);
 }
 
-CFB_DEV void x_producer(const Plan& P, Smem& S) {
+CFB_DEV void x_producer(const Plan& P, Smem& S, int p0, int p1) {
   uint32_t xi = 0;            // units issued
   int xstage = 0;
   uint32_t xpar = 1u;         // a fresh mbarrier's previous phase counts as complete
   bool ok = true;
-  for (int p = 0; p < P.nphases && ok; ++p) {
+  for (int p = p0; p < p1 && ok; ++p) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
     const UnitRange cu = cta_units(P, ph);
@@ -1147,105 +1153,150 @@ CFB_DEV void head_post(const Plan& P, const Phase& ph, HeadState& H, const Grp& 
   }
 }
 
-// The beam phase: one CTA per request (reference flow_proposer.py:1234-1259 chain, :1295-1331
-// tree). Each frontier row of the request gets a group of warps; its threads follow up to
-// kMaxLists of the CTAs' published lists (sorted), the group combines their log-sum-exps in a
-// fixed order and takes the top-TB by TB rounds of a group argmax over the list heads (ties:
-// lower shortlist id). One thread then picks the survivors from shared memory; all threads
-// write the new frontier and gather the next depth's path and markov rows.
+// Merging published (max, sumexp, sorted top-k) lists. Request b's `fr` frontier rows are each
+// given a group of warps. Each thread follows up to kMaxLists of the `nlists` lists of its row
+// (list c of row r at src + (c * kRowsMax + r) * kHeadPartFloats). The group combines the
+// log-sum-exps in a fixed order and takes the top-TB by TB rounds of a group argmax over the
+// list heads (ties: lower shortlist id). Per row it leaves (m, sumexp) in mbuf/sbuf and the
+// TB winners in vbuf/ibuf ([row][kTopMax]) in shared memory; the caller synchronises.
 constexpr int kMaxLists = 5;
 constexpr int kMaxDepth = 8;
+struct MergeBufs { float* vbuf; int* ibuf; float* mbuf; float* sbuf; float* wv; int* wid; int* wown; float* wm; float* ws; };
+CFB_DEV MergeBufs merge_bufs(Smem& S) {
+  MergeBufs M;
+  M.vbuf = S.scratch;
+  M.ibuf = reinterpret_cast<int*>(M.vbuf + kTopMax * kTopMax);
+  M.mbuf = reinterpret_cast<float*>(M.ibuf + kTopMax * kTopMax);
+  M.sbuf = M.mbuf + kTopMax;
+  M.wv = M.sbuf + kTopMax;
+  M.wid = reinterpret_cast<int*>(M.wv + 32);
+  M.wown = M.wid + 32;
+  M.wm = reinterpret_cast<float*>(M.wown + 32);
+  M.ws = M.wm + 32;
+  return M;
+}
+constexpr int kMergeFloats = 2 * kTopMax * kTopMax + 2 * kTopMax + 5 * 32;   // floats merge_bufs uses
+
+CFB_DEV void merge_rows(const Plan& P, const float* src, int nlists, int b, int fr, int TB, const MergeBufs& M,
+                        const Grp& W) {
+  const int warp = W.t >> 5, lane = W.t & 31, nwarps = W.n >> 5;
+  const int wpg = max(1, nwarps / fr);              // warps per frontier row
+  const int grp = warp / wpg, gt = (warp - grp * wpg) * 32 + lane, gn = wpg * 32;
+  if (grp >= fr) return;
+  const int gbar = 3 + grp;                         // named barrier of this row group
+  const int row = b * fr + grp;
+  float hv[kMaxLists], nv[kMaxLists];
+  int hi[kMaxLists], ni[kMaxLists], pos[kMaxLists];
+  float m = -INFINITY, ssum = 0.f;
+#pragma unroll
+  for (int l = 0; l < kMaxLists; ++l) {
+    const int c = gt + l * gn;
+    hv[l] = nv[l] = -INFINITY; hi[l] = ni[l] = 0x7fffffff; pos[l] = 0;
+    if (c < nlists) {
+      const float* hp = src + ((size_t)c * kRowsMax + row) * kHeadPartFloats;
+      const float mb = __ldcg(hp), sb = __ldcg(hp + 1);
+      hv[l] = __ldcg(hp + 2); hi[l] = __float_as_int(__ldcg(hp + 2 + kTopMax));
+      if (TB > 1) { nv[l] = __ldcg(hp + 3); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax)); }
+      lse_merge(m, ssum, mb, sb);
+    }
+  }
+  lse_lanes(m, ssum, 32);
+  if (lane == 0) { M.wm[warp] = m; M.ws[warp] = ssum; }
+  asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
+  m = M.wm[grp * wpg]; ssum = M.ws[grp * wpg];
+  for (int w = 1; w < wpg; ++w) lse_merge(m, ssum, M.wm[grp * wpg + w], M.ws[grp * wpg + w]);
+  if (gt == 0) { M.mbuf[grp] = m; M.sbuf[grp] = ssum; }
+#pragma unroll 1
+  for (int round = 0; round < TB; ++round) {
+    float v = -INFINITY; int id = 0x7fffffff, ol = 0;
+#pragma unroll
+    for (int l = 0; l < kMaxLists; ++l) if (better(hv[l], hi[l], v, id)) { v = hv[l]; id = hi[l]; ol = l; }
+    int own = gt;
+    argmax_lanes(v, id, own, 32);
+    asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");   // last round's reads done
+    if (lane == 0) { M.wv[warp] = v; M.wid[warp] = id; M.wown[warp] = own; }
+    asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
+    v = M.wv[grp * wpg]; id = M.wid[grp * wpg]; own = M.wown[grp * wpg];
+    for (int w = 1; w < wpg; ++w) {
+      const float vo = M.wv[grp * wpg + w]; const int io = M.wid[grp * wpg + w], oo = M.wown[grp * wpg + w];
+      if (better(vo, io, v, id) || (vo == v && io == id && oo < own)) { v = vo; id = io; own = oo; }
+    }
+    if (own == gt) {               // the winner moves on in the list it came from
+#pragma unroll
+      for (int l = 0; l < kMaxLists; ++l) {
+        if (l != ol) continue;
+        hv[l] = nv[l]; hi[l] = ni[l]; ++pos[l];
+        nv[l] = -INFINITY; ni[l] = 0x7fffffff;
+        if (pos[l] + 1 < TB) {
+          const float* hp = src + ((size_t)(gt + l * gn) * kRowsMax + row) * kHeadPartFloats;
+          nv[l] = __ldcg(hp + 3 + pos[l]); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax + pos[l]));
+        }
+      }
+    }
+    if (gt == 0) { M.vbuf[grp * kTopMax + round] = v; M.ibuf[grp * kTopMax + round] = id; }
+  }
+}
+
+// Rank-local merge of a row-sharded head (PK_RMERGE): request b's rows of this rank's CTA lists
+// merged into one list per row in xloc, for the caller to gather across ranks.
+CFB_DEV void rmerge_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
+  const MergeBufs M = merge_bufs(S);
+  const int fr = ph.fr, TB = ph.topb;
+  for (int b = blockIdx.x; b < P.B; b += P.G) {
+    merge_rows(P, P.hpart, P.G, b, fr, TB, M, W);
+    gsync(W);
+    for (int e = W.t; e < fr * kHeadPartFloats; e += W.n) {
+      const int r = e / kHeadPartFloats, f = e - r * kHeadPartFloats;
+      float v;
+      if (f == 0) v = M.mbuf[r];
+      else if (f == 1) v = M.sbuf[r];
+      else if (f < 2 + kTopMax) v = (f - 2 < TB) ? M.vbuf[r * kTopMax + f - 2] : -INFINITY;
+      else v = __int_as_float((f - 2 - kTopMax < TB) ? M.ibuf[r * kTopMax + f - 2 - kTopMax] : 0x7fffffff);
+      __stcg(P.xloc + (size_t)(b * fr + r) * kHeadPartFloats + f, v);
+    }
+    gsync(W);
+  }
+}
+
+// The beam phase: one CTA per request (reference flow_proposer.py:1234-1259 chain, :1295-1331
+// tree). The frontier rows' lists are merged (the CTAs' lists, or for a row-sharded head the
+// ranks' gathered lists), then one thread picks the survivors from shared memory and all
+// threads write the new frontier and gather the next depth's path and markov rows.
 CFB_DEV void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, unsigned long long* prow) {
   const bool treem = (ph.post == PO_BEAM_TREE);
   const int fr = ph.fr, TB = ph.topb, order = P.order, step = ph.step, Wm = P.Wmax;
   const int TB2 = treem ? TB : P.width;
   const int k = treem ? min(ph.keep, fr * TB2) : P.width;
-  const int warp = W.t >> 5, lane = W.t & 31, nwarps = W.n >> 5;
-  const int wpg = max(1, nwarps / fr);              // warps per frontier row
-  const int grp = warp / wpg, gt = (warp - grp * wpg) * 32 + lane, gn = wpg * 32;
-  const bool active = grp < fr;
-  const int gbar = 3 + grp;                         // named barrier of this row group
-  // scratch (epilogue scratch is free during a beam phase)
-  float* lp = S.scratch;                                          // [row][kTopMax] log-probs
-  int* lid = reinterpret_cast<int*>(lp + kTopMax * kTopMax);      // shortlist-local ids
-  float* wv = reinterpret_cast<float*>(lid + kTopMax * kTopMax);  // per-warp argmax / lse parts
-  int* wid = reinterpret_cast<int*>(wv + 32);
-  int* wown = wid + 32;
-  float* wm = reinterpret_cast<float*>(wown + 32);
-  float* ws = wm + 32;
-  float* cumo = ws + 32;                                          // [kTopMax] cum before the step
+  const MergeBufs M = merge_bufs(S);
+  float* lp = M.vbuf;                                             // merged values become log-probs
+  int* lid = M.ibuf;
+  float* cumo = S.scratch + kMergeFloats;                         // [kTopMax] cum before the step
   float* selc = cumo + kTopMax;                                   // [kTopMax] cum after it
   int* sel = reinterpret_cast<int*>(selc + kTopMax);              // [kTopMax] chosen candidate
   int* hb = sel + kTopMax;                                        // [kMaxDepth][kTopMax] back-pointers
   int64_t* oldp = reinterpret_cast<int64_t*>(hb + kMaxDepth * kTopMax);   // [kTopMax][order]
   int64_t* ht = oldp + kTopMax * 8;                               // [kMaxDepth][kTopMax] tokens
+  const bool sharded = P.nranks > 1;
   for (int b = blockIdx.x; b < P.B; b += P.G) {
     if (W.t < fr) cumo[W.t] = P.cum[b * Wm + W.t];
     for (int e = W.t; e < fr * order; e += W.n)
       oldp[e] = P.lastp[((size_t)b * Wm + e / order) * order + e % order];
-    if (active) {
-      const int row = b * fr + grp;
-      float hv[kMaxLists], nv[kMaxLists];
-      int hi[kMaxLists], ni[kMaxLists], pos[kMaxLists];
-      float m = -INFINITY, ssum = 0.f;
-#pragma unroll
-      for (int l = 0; l < kMaxLists; ++l) {
-        const int c = gt + l * gn;
-        hv[l] = nv[l] = -INFINITY; hi[l] = ni[l] = 0x7fffffff; pos[l] = 0;
-        if (c < P.G) {
-          const float* hp = P.hpart + ((size_t)c * kRowsMax + row) * kHeadPartFloats;
-          const float mb = __ldcg(hp), sb = __ldcg(hp + 1);
-          hv[l] = __ldcg(hp + 2); hi[l] = __float_as_int(__ldcg(hp + 2 + kTopMax));
-          if (TB > 1) { nv[l] = __ldcg(hp + 3); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax)); }
-          lse_merge(m, ssum, mb, sb);
-        }
-      }
-      if (prow && W.t == 0) prow[12] = globaltimer();
-      lse_lanes(m, ssum, 32);
-      if (lane == 0) { wm[warp] = m; ws[warp] = ssum; }
-      asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
-      m = wm[grp * wpg]; ssum = ws[grp * wpg];
-      for (int w = 1; w < wpg; ++w) lse_merge(m, ssum, wm[grp * wpg + w], ws[grp * wpg + w]);
-      const bool okrow = (ssum > 0.f) && isfinite(m) && isfinite(ssum);
-      const float lse = okrow ? m + logf(ssum) : 0.f;
-      if (prow && W.t == 0) prow[13] = globaltimer();
-#pragma unroll 1
-      for (int round = 0; round < TB; ++round) {
-        float v = -INFINITY; int id = 0x7fffffff, ol = 0;
-#pragma unroll
-        for (int l = 0; l < kMaxLists; ++l) if (better(hv[l], hi[l], v, id)) { v = hv[l]; id = hi[l]; ol = l; }
-        int own = gt;
-        argmax_lanes(v, id, own, 32);
-        asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");   // last round's reads done
-        if (lane == 0) { wv[warp] = v; wid[warp] = id; wown[warp] = own; }
-        asm volatile("bar.sync %0, %1;" :: "r"(gbar), "r"(gn) : "memory");
-        v = wv[grp * wpg]; id = wid[grp * wpg]; own = wown[grp * wpg];
-        for (int w = 1; w < wpg; ++w) {
-          const float vo = wv[grp * wpg + w]; const int io = wid[grp * wpg + w], oo = wown[grp * wpg + w];
-          if (better(vo, io, v, id) || (vo == v && io == id && oo < own)) { v = vo; id = io; own = oo; }
-        }
-        if (own == gt) {               // the winner moves on in the list it came from
-#pragma unroll
-          for (int l = 0; l < kMaxLists; ++l) {
-            if (l != ol) continue;
-            hv[l] = nv[l]; hi[l] = ni[l]; ++pos[l];
-            nv[l] = -INFINITY; ni[l] = 0x7fffffff;
-            if (pos[l] + 1 < TB) {
-              const float* hp = P.hpart + ((size_t)(gt + l * gn) * kRowsMax + row) * kHeadPartFloats;
-              nv[l] = __ldcg(hp + 3 + pos[l]); ni[l] = __float_as_int(__ldcg(hp + 3 + kTopMax + pos[l]));
-            }
-          }
-        }
-        if (gt == 0) {
-          const bool ok = okrow && id >= 0 && id < P.R && !isnan(v) && v != -INFINITY;
-          lp[grp * kTopMax + round] = ok ? v - lse : -INFINITY;
-          lid[grp * kTopMax + round] = ok ? id : 0;
-        }
-      }
-      if (prow && W.t == 0) prow[14] = globaltimer();
-    }
+    merge_rows(P, sharded ? P.xall : P.hpart, sharded ? P.nranks : P.G, b, fr, TB, M, W);
     gsync(W);
     if (prow && W.t == 0) prow[16] = globaltimer();
+    // log-probs of the merged top-TB per row
+    if (W.t < fr * TB) {
+      const int r = W.t / TB, i = W.t - r * TB;
+      const float mm = M.mbuf[r], ss = M.sbuf[r];
+      const bool okrow = (ss > 0.f) && isfinite(mm) && isfinite(ss);
+      const float lse = okrow ? mm + logf(ss) : 0.f;
+      const float v = lp[r * kTopMax + i];
+      const int id = lid[r * kTopMax + i];
+      const bool ok = okrow && id >= 0 && id < P.R && !isnan(v) && v != -INFINITY;
+      lp[r * kTopMax + i] = ok ? v - lse : -INFINITY;
+      lid[r * kTopMax + i] = ok ? id : 0;
+    }
+    gsync(W);
     // survivors: the best k of cum[w] + lp[w][i] (one thread, shared memory only)
     if (W.t == 0) {
       HeadState C; head_reset(C);     // tv = cumulative log-prob, ti = w * TB2 + i
@@ -1313,7 +1364,8 @@ CFB_DEV void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, u
 }
 
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp) {
+// Runs phases [p0, p1) of the plan: the whole table, or one segment of a sharded-head plan.
+__global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp, int p0, int p1) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const Plan& P = *Pp;
   const SmemLayout L = P.sm;
@@ -1345,11 +1397,11 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   const bool dead = *S.flag != 0;
   __syncthreads();
   if (warp == kWProdWarp) {
-    if ((tid & 31) == 0 && !dead) weight_producer(P, S);
+    if ((tid & 31) == 0 && !dead) weight_producer(P, S, p0, p1);
     return;
   }
   if (warp == kXProdWarp) {
-    if ((tid & 31) == 0 && !dead) x_producer(P, S);
+    if ((tid & 31) == 0 && !dead) x_producer(P, S, p0, p1);
     return;
   }
   const bool is_epi = warp >= kEpiWarp0;
@@ -1363,7 +1415,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   WaitClock wc;
   const bool rec = P.prof && ((!is_epi && tid == 0) || (is_epi && E.t == 0));
   wc.on = rec;
-  for (int p = 0; p < P.nphases && ok; ++p) {
+  for (int p = p0; p < p1 && ok; ++p) {
     const Phase& ph = P.phases[p];
     unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * kProfSlots : nullptr;
     unsigned long long* stamp = (P.prof && Wk.t == 0) ? prow : nullptr;
@@ -1377,6 +1429,8 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
       attn_phase(P, ph, S, Wk);
     } else if (ph.kind == PK_BEAM) {
       beam_phase(P, ph, S, Wk, P.prof ? prow : nullptr);
+    } else if (ph.kind == PK_RMERGE) {
+      rmerge_phase(P, ph, S, Wk);
     } else {
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
@@ -1449,6 +1503,7 @@ struct Builder {
   std::vector<cfb::Phase> phases;
   std::vector<cfb::Job> jobs;
   std::vector<cfb::AttnTask> attn;
+  std::vector<int> segs;         // first phase of every launch segment after the first
   cfb::Plan P{};
   size_t off_phases = 0, off_jobs = 0, off_attn = 0;
   int max_tiles = 0;
@@ -1539,7 +1594,16 @@ cfb_status lower(Builder& B, size_t* bytes) {
     K = std::min(r.depth, DL - 1);
     if (K < 1 || (!tree && K != r.depth)) return CFB_ERR_UNSUPPORTED;
     if (Bq * Wmax > cfb::kRowsMax) return CFB_ERR_UNSUPPORTED;
-    if (!lin_ok(d.head, d.shortlist_rows, D + d.markov_rank)) return CFB_ERR_INVALID_ARG;
+    // the head: every shortlist row, or (row-sharded across ranks) rows [head_row0, +nout)
+    if (d.head_row0 < 0 || d.head.nout < 1 || d.head_row0 + d.head.nout > d.shortlist_rows ||
+        !lin_ok(d.head, d.head.nout, D + d.markov_rank))
+      return CFB_ERR_INVALID_ARG;
+    if (r.ranks > 1) {
+      if (r.rank < 0 || r.rank >= r.ranks || !r.xloc || !r.xall) return CFB_ERR_INVALID_ARG;
+      if (r.ranks > cfb::kMaxLists * 32) return CFB_ERR_UNSUPPORTED;
+    } else if (d.head_row0 != 0 || d.head.nout != d.shortlist_rows) {
+      return CFB_ERR_INVALID_ARG;     // one GPU holds the whole head
+    }
     if (!lin_ok(d.path_offsets, D, d.path_order * D) || !lin_ok(d.path_up, d.path_up.nout, D) ||
         !lin_ok(d.path_down, D, d.path_up.nout) || !d.path_offset_bias || !d.path_down.bias ||
         d.path_up.nout % 16)
@@ -1608,6 +1672,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
 
   auto& ph = B.phases; ph.clear();
   B.jobs.clear();
+  B.segs.clear();
   auto& at = B.attn; at.clear();
   B.max_tiles = 0;
   B.too_big = false;
@@ -1779,10 +1844,17 @@ cfb_status lower(Builder& B, size_t* bytes) {
       {   // shortlist head + markov bias with online LSE + top-k per CTA
         cfb::Job J = make_job(d.head, rows);
         J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_xhead); J.ldx = D + rank;
-        J.ekind = cfb::EK_HEAD; J.R = d.shortlist_rows; J.topb = TB; J.bias = nullptr; J.colsum = nullptr;
+        J.ekind = cfb::EK_HEAD; J.R = d.head.nout; J.rowoff = d.head_row0; J.topb = TB;
+        J.bias = nullptr; J.colsum = nullptr;
         cfb::Phase p{};
         p.post = cfb::PO_PUBLISH; p.rows = rows; p.topb = TB;
         add_phase(B, p, {J});
+      }
+      if (r.ranks > 1) {   // merge this rank's CTA lists; the caller gathers them across ranks
+        cfb::Phase p{};
+        p.kind = cfb::PK_RMERGE; p.rows = rows; p.fr = fr; p.topb = TB;
+        ph.push_back(p);
+        B.segs.push_back((int)ph.size());
       }
       {   // merge the CTAs' lists, beam step, next depth's gather
         cfb::Phase p{};
@@ -1902,15 +1974,53 @@ cfb_status lower(Builder& B, size_t* bytes) {
     P.xhead = B.dptr<__half>(o_xhead); P.ldxhead = D + rank;
     P.emb = static_cast<const __half*>(d.embed); P.pg = B.dptr<__half>(o_pg);
   }
+  P.nranks = (beam && r.ranks > 1) ? r.ranks : 1;
+  P.xloc = r.xloc; P.xall = r.xall;
+  // launch segments: [0, s1), [s1, s2), ... [sk, nphases); the last boundary (after the final
+  // depth's merge) leaves only the last beam phase in the final segment
+  if ((int)B.segs.size() + 1 > cfb::kMaxSeg) return CFB_ERR_UNSUPPORTED;
+  P.nseg = (int)B.segs.size() + 1;
+  P.seg[0] = 0;
+  for (size_t i = 0; i < B.segs.size(); ++i) P.seg[i + 1] = B.segs[i];
+  P.seg[P.nseg] = (int)ph.size();
   return CFB_OK;
 }
 
 struct LaunchRecord { int G, phases, smem, pad; };
-struct LaunchRec { void* ws; int G, smem; };
+struct LaunchRec { void* ws; int G, smem, nseg; int seg[cfb::kMaxSeg + 1]; };
 std::vector<LaunchRec> g_launch;     // launch shape of the plan last built in each workspace
-void remember_launch(void* ws, int G, int smem) {
-  for (auto& l : g_launch) if (l.ws == ws) { l.G = G; l.smem = smem; return; }
-  g_launch.push_back({ws, G, smem});
+void remember_launch(void* ws, const cfb::Plan& P, int smem) {
+  LaunchRec r{ws, P.G, smem, P.nseg, {}};
+  for (int i = 0; i <= P.nseg; ++i) r.seg[i] = P.seg[i];
+  for (auto& l : g_launch) if (l.ws == ws) { l = r; return; }
+  g_launch.push_back(r);
+}
+// The kernel's dynamic shared-memory limit is a property of the function (per device), shared
+// by every plan: raise it to what this plan needs, never lower it under another plan.
+cfb_status ensure_smem_attr(int smem) {
+  static std::mutex mu;
+  static int attr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "get device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && attr[dev] >= smem) return CFB_OK;
+  e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "smem attribute");
+  if (dev >= 0 && dev < 64) attr[dev] = smem;
+  return CFB_OK;
+}
+
+// the launch record of workspace ws: the host copy, else read back from the device plan
+cfb_status launch_rec(void* ws, LaunchRec& out) {
+  for (auto& l : g_launch) if (l.ws == ws) { out = l; return CFB_OK; }
+  cfb::Plan P;
+  cudaError_t e = cudaMemcpy(&P, static_cast<uint8_t*>(ws) + kOffPlan, sizeof(P), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read plan record");
+  if (P.nseg < 1 || P.nseg > cfb::kMaxSeg) return CFB_ERR_INVALID_ARG;
+  remember_launch(ws, P, P.sm.total);
+  for (auto& l : g_launch) if (l.ws == ws) { out = l; return CFB_OK; }
+  return CFB_ERR_INVALID_ARG;
 }
 
 }  // namespace
@@ -1936,9 +2046,7 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   if (need > bytes) return CFB_ERR_WORKSPACE;
   cudaError_t e;
   const int smem = B.P.sm.total;
-  if ((e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
-      cudaSuccess)
-    return cuda_fail(e, "smem attribute");
+  if ((st = ensure_smem_attr(smem)) != CFB_OK) return st;
   int per_sm = 0, dev = 0, sms = 0;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfb::engine_kernel, cfb::kThreads, smem)) !=
       cudaSuccess)
@@ -1962,7 +2070,7 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   if ((e = cudaMemcpy(B.base + ob + 32, &h, sizeof(h), cudaMemcpyHostToDevice)) != cudaSuccess)
     return cuda_fail(e, "copy launch record");
   if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "plan build sync");
-  remember_launch(ws, B.P.G, smem);
+  remember_launch(ws, B.P, smem);
   return CFB_OK;
 }
 
@@ -1979,24 +2087,43 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
   return CFB_OK;
 }
 
-cfb_status cfb_plan_run(void* ws, void* stream) {
-  if (!ws) return CFB_ERR_INVALID_ARG;
-  int G = -1, smem = 0;
-  for (auto& l : g_launch) if (l.ws == ws) { G = l.G; smem = l.smem; }
-  if (G < 0) {
-    cfb_status st = cfb_plan_info(ws, &G, nullptr, &smem, nullptr);
-    if (st != CFB_OK) return st;
-    cudaError_t ea = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (ea != cudaSuccess) return cuda_fail(ea, "smem attribute");
-    remember_launch(ws, G, smem);
-  }
+static cfb_status launch_range(void* ws, const LaunchRec& L, int p0, int p1, void* stream) {
+  const cfb_status st = ensure_smem_attr(L.smem);
+  if (st != CFB_OK) return st;
   const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
-  void* args[] = {(void*)&P};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)cfb::engine_kernel, dim3(G), dim3(cfb::kThreads),
-                                              args, (size_t)smem, static_cast<cudaStream_t>(stream));
+  void* args[] = {(void*)&P, (void*)&p0, (void*)&p1};
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)cfb::engine_kernel, dim3(L.G), dim3(cfb::kThreads),
+                                              args, (size_t)L.smem, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;
   if (e != cudaSuccess) return cuda_fail(e, "engine launch");
   return CFB_OK;
+}
+
+cfb_status cfb_plan_run(void* ws, void* stream) {
+  if (!ws) return CFB_ERR_INVALID_ARG;
+  LaunchRec L;
+  cfb_status st = launch_rec(ws, L);
+  if (st != CFB_OK) return st;
+  if (L.nseg != 1) return CFB_ERR_INVALID_ARG;     // sharded heads run segment by segment
+  return launch_range(ws, L, 0, L.seg[1], stream);
+}
+
+cfb_status cfb_plan_segments(void* ws, int* nseg) {
+  if (!ws || !nseg) return CFB_ERR_INVALID_ARG;
+  LaunchRec L;
+  cfb_status st = launch_rec(ws, L);
+  if (st != CFB_OK) return st;
+  *nseg = L.nseg;
+  return CFB_OK;
+}
+
+cfb_status cfb_plan_run_segment(void* ws, int seg, void* stream) {
+  if (!ws) return CFB_ERR_INVALID_ARG;
+  LaunchRec L;
+  cfb_status st = launch_rec(ws, L);
+  if (st != CFB_OK) return st;
+  if (seg < 0 || seg >= L.nseg) return CFB_ERR_INVALID_ARG;
+  return launch_range(ws, L, L.seg[seg], L.seg[seg + 1], stream);
 }
 
 cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes) {

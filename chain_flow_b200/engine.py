@@ -38,6 +38,10 @@ def untile(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
 
 
 class Plan:
+    """With weights packed for a row-sharded head (DrafterWeights(head_shard=(rank, ranks))), every
+    rank builds the same plan; ``run(group=...)`` then runs it segment by segment and all-gathers
+    the ranks' merged top-k lists between segments (one small NCCL all_gather per beam depth)."""
+
     def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
                  tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False,
                  init_mode: int = 0):
@@ -65,6 +69,12 @@ class Plan:
         r.flags = _lib.RUN_PROFILE if profile else 0
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
         r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
+        self.ranks = w.head_ranks
+        if self.ranks > 1:
+            self.xloc = torch.zeros(_lib.XROWS * _lib.XFLOATS, dtype=torch.float32, device=dev)
+            self.xall = torch.zeros(self.ranks * _lib.XROWS * _lib.XFLOATS, dtype=torch.float32, device=dev)
+            r.ranks, r.rank = self.ranks, w.head_rank
+            r.xloc, r.xall = self.xloc.data_ptr(), self.xall.data_ptr()
         self.run_desc = r
         nbytes = C.c_size_t(0)
         _lib.check(self.lib.cfb_plan_workspace(C.byref(w.desc), C.byref(r), C.byref(nbytes)),
@@ -77,11 +87,24 @@ class Plan:
         _lib.check(self.lib.cfb_plan_info(C.c_void_p(self.ws_ptr), C.byref(g), C.byref(t), C.byref(s),
                                           C.byref(p)), "cfb_plan_info")
         self.grid, self.threads, self.smem, self.phases = g.value, t.value, s.value, p.value
+        n = C.c_int()
+        _lib.check(self.lib.cfb_plan_segments(C.c_void_p(self.ws_ptr), C.byref(n)), "cfb_plan_segments")
+        self.segments = n.value
 
-    def run(self, stream=None) -> None:
-        """One persistent launch on `stream` (default: torch's current stream)."""
-        _lib.check(self.lib.cfb_plan_run(C.c_void_p(self.ws_ptr), C.c_void_p(_lib.stream_ptr(stream))),
-                   "cfb_plan_run")
+    def run(self, stream=None, group=None) -> None:
+        """One persistent launch on `stream` (default: torch's current stream); a sharded-head plan
+        runs its segments with an all_gather over `group` (torch.distributed) between them."""
+        sp = C.c_void_p(_lib.stream_ptr(stream))
+        if self.segments == 1:
+            _lib.check(self.lib.cfb_plan_run(C.c_void_p(self.ws_ptr), sp), "cfb_plan_run")
+            return
+        import torch.distributed as dist
+        for seg in range(self.segments):
+            _lib.check(self.lib.cfb_plan_run_segment(C.c_void_p(self.ws_ptr), seg, sp), "cfb_plan_run_segment")
+            if seg + 1 < self.segments:
+                if stream is not None and stream != torch.cuda.current_stream():
+                    raise _lib.CfbError("a sharded-head plan runs on torch's current stream")
+                dist.all_gather_into_tensor(self.xall, self.xloc, group=group)
 
     def buffer(self, which: int, dtype, shape) -> torch.Tensor:
         """A copy of one intermediate buffer of this plan (CFB_BUF_*), for stage-by-stage checks."""

@@ -60,6 +60,7 @@ class FlowDrafterProposer:
         self._gen = None
         self.init_mode = "delta"
         self.noise_scale = 1.0
+        self.group = None
         for k, v in kw.items():
             setattr(self, k, v)
 
@@ -68,7 +69,11 @@ class FlowDrafterProposer:
     def from_components(cls, state_dict: dict, model_args: dict, embed: torch.Tensor, lm_head: torch.Tensor,
                         shortlist_ids: torch.Tensor | None = None, *, width: int | None = None, K: int = 5,
                         tree_keep: int | None = None, tree_topb: int | None = None,
-                        tree_depth: int | None = None, device=None, seed: int = 0) -> "FlowDrafterProposer":
+                        tree_depth: int | None = None, device=None, seed: int = 0,
+                        head_shard: tuple[int, int] | None = None, group=None) -> "FlowDrafterProposer":
+        """head_shard=(rank, ranks): this process packs only its share of the shortlist head rows
+        and every draft all-gathers the ranks' merged top-k lists over `group` (torch.distributed,
+        NCCL); all ranks must draft the same requests with the same inputs."""
         self = cls()
         hidden = int(embed.shape[1])
         args = dict(model_args)
@@ -80,7 +85,9 @@ class FlowDrafterProposer:
         cfg = DraftConfig.from_model_args(args, hidden)
         if shortlist_ids is None:
             shortlist_ids = torch.arange(embed.shape[0])        # full head
-        self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device)
+        self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device,
+                                      head_shard=head_shard)
+        self.group = group
         self.cfg = cfg
         self.dev = self.weights.dev
         self.init_mode = args.get("init_mode", "delta")
@@ -166,7 +173,7 @@ class FlowDrafterProposer:
     def predict_hidden(self, ctx: torch.Tensor) -> torch.Tensor:
         p = self._plan(_lib.MODE_FLOW, ctx.shape[0])
         self._load_inputs(p, ctx, None)
-        p.run()
+        p.run(group=self.group)
         return p.pred
 
     @torch.inference_mode()
@@ -174,7 +181,7 @@ class FlowDrafterProposer:
         """[B, K] int64 chain drafts; ``known0`` is the token vLLM just committed."""
         p = self._plan(_lib.MODE_CHAIN, ctx.shape[0])
         self._load_inputs(p, ctx, known0)
-        p.run()
+        p.run(group=self.group)
         return p.tokens
 
     @torch.inference_mode()
@@ -182,7 +189,7 @@ class FlowDrafterProposer:
         """[B, 2N] int64: N BFS-ordered draft tokens followed by their N parent indices (-1 = root)."""
         p = self._plan(_lib.MODE_TREE, ctx.shape[0])
         self._load_inputs(p, ctx, known0)
-        p.run()
+        p.run(group=self.group)
         return p.tokens
 
     def device_error(self) -> int:

@@ -42,19 +42,20 @@ class Workload:
                     path_order=c.path_order, path_ffn_multiplier=c.path_ffn_multiplier,
                     markov_rank=c.markov_rank, init_mode="noise", noise_scale=1.0)
 
-    def weight_bytes_per_draft(self) -> int:
+    def weight_bytes_per_draft(self, head_fraction: float = 1.0) -> int:
         """Packed fp16 weight bytes one draft streams (the algorithmic bytes of the engine):
         cross K/V once; per Euler step every block of both chunk experts plus their out_proj;
         per beam depth the live PathHead offsets, the PathHead MLP and the [lm_head | markov w2]
-        shortlist head (reference flow_proposer.py:1115-1117 counts the head the same way)."""
+        shortlist head (reference flow_proposer.py:1115-1117 counts the head the same way).
+        head_fraction: the share of the shortlist head one GPU holds when it is row-sharded."""
         D, L, T, FM = self.hidden, self.layers, self.steps, self.ffn
         E = 2
         crosskv = E * L * 2 * D * D
         per_step = E * L * (3 + 1 + 1 + 1 + FM + FM) * D * D + E * D * D
         head = 0
         for d in range(1, self.draft_tokens + 1):
-            head += min(d, 4) * D * D + 2 * (2 * D * D) + self.shortlist_rows * (D + self.markov_rank)
-        return 2 * (crosskv + T * per_step + head)
+            head += min(d, 4) * D * D + 2 * (2 * D * D) + head_fraction * self.shortlist_rows * (D + self.markov_rank)
+        return int(2 * (crosskv + T * per_step + head))
 
 
 WORKLOADS = {

@@ -53,9 +53,21 @@ def expert_prefix(e: int) -> str:
     return "expert." if e == 0 else f"extra_experts.{e - 1}."
 
 
+def shard_rows(rows: int, ranks: int, rank: int) -> tuple[int, int]:
+    """(first row, row count) of rank `rank`'s contiguous share of a `rows`-row head."""
+    if ranks < 1 or not 0 <= rank < ranks:
+        raise ValueError(f"rank {rank} of {ranks}")
+    r0, r1 = rank * rows // ranks, (rank + 1) * rows // ranks
+    return r0, r1 - r0
+
+
 class DrafterWeights:
+    """The drafter's weights packed for the engine. With head_shard=(rank, ranks) only that rank's
+    contiguous share of the shortlist head is packed (row-sharded head across GPUs); everything
+    else is replicated."""
+
     def __init__(self, sd: dict, cfg: DraftConfig, embed: torch.Tensor, lm_head: torch.Tensor,
-                 shortlist: torch.Tensor, device=None):
+                 shortlist: torch.Tensor, device=None, head_shard: tuple[int, int] | None = None):
         self.lib = _lib.load()
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if dev.type != "cuda":
@@ -127,12 +139,20 @@ class DrafterWeights:
                                    ln=(p32("path_head.norm.weight"), p32("path_head.norm.bias")))
         self.path_down = self.linear(self.sd16["path_head.mlp.3.weight"], p32("path_head.mlp.3.bias"))
         self.markov_w1 = self.sd16["markov.w1.weight"]
-        hb = self.pack_buffer(R, D + rank)
-        lm16 = f16(lm_head)
-        self._pack_into(lm16, hb, R, D, D + rank, 0, rows=sl)
-        self._pack_into(self.sd16["markov.w2.weight"], hb, R, rank, D + rank, D, rows=sl)
+        self.head_rank, self.head_ranks = head_shard if head_shard is not None else (0, 1)
+        self.head_row0, hrows = shard_rows(R, self.head_ranks, self.head_rank)
+        rows_sl = sl[self.head_row0:self.head_row0 + hrows].contiguous()
+        hb = self.pack_buffer(hrows, D + rank)
+        lm16 = lm_head if lm_head.device == dev and lm_head.dtype == torch.float16 else None
+        if lm16 is None:
+            # only the rows this rank packs travel to the device
+            lm16 = lm_head[rows_sl.to(lm_head.device)].to(device=dev, dtype=torch.float16).contiguous()
+            self._pack_into(lm16, hb, hrows, D, D + rank, 0)
+        else:
+            self._pack_into(lm16, hb, hrows, D, D + rank, 0, rows=rows_sl)
+        self._pack_into(self.sd16["markov.w2.weight"], hb, hrows, rank, D + rank, D, rows=rows_sl)
         del lm16
-        self.head = _lib.Linear(hb.data_ptr(), None, None, R, D + rank)
+        self.head = _lib.Linear(hb.data_ptr(), None, None, hrows, D + rank)
         self.R = R
 
         d = _lib.Drafter()
@@ -147,6 +167,7 @@ class DrafterWeights:
         d.markov_w1 = self.markov_w1.data_ptr()
         d.head = self.head
         d.shortlist = sl.data_ptr()
+        d.head_row0 = self.head_row0
         self.desc = d
         # the raw fp16 state dict is no longer needed except the tables the engine reads
         keep = {"markov.w1.weight"}

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define CFB_ABI_VERSION 1
+#define CFB_ABI_VERSION 2
 
 typedef enum cfb_status {
   CFB_OK = 0,
@@ -96,8 +96,10 @@ typedef struct cfb_drafter {
   cfb_linear path_up;          /* path_head.mlp.0, path_head.norm folded [2D, D] */
   cfb_linear path_down;        /* path_head.mlp.3 [D, 2D] */
   const void* markov_w1;       /* fp16 [vocab, rank] */
-  cfb_linear head;             /* [R, D + rank] = [lm_head.weight[sl] | markov.w2.weight[sl]] */
+  cfb_linear head;             /* [R, D + rank] = [lm_head.weight[sl] | markov.w2.weight[sl]],
+                                  or rows [head_row0, head_row0 + head.nout) of it (a row shard) */
   const int64_t* shortlist;    /* int64 [R] global token ids (sorted, unique) */
+  int head_row0;               /* first shortlist row `head` holds: 0 unless the head is sharded */
 } cfb_drafter;
 
 typedef enum cfb_mode {
@@ -131,7 +133,20 @@ typedef struct cfb_run {
   const int64_t* known0;  /* int64 [B] committed token per request */
   float* pred;         /* fp32 [B, draft_len, D]: output of the flow, input of BEAM_* modes */
   int64_t* tokens;     /* int64 chain [B, depth]; tree [B, 2N] (N tokens, then N parents) */
+  /* Row-sharded shortlist head across `ranks` GPUs (ranks > 1): every rank runs the same
+   * requests with the same inputs; the flow is computed on every rank, the head only over this
+   * rank's rows (cfb_drafter.head_row0 / head.nout). Per beam depth the plan merges its CTAs'
+   * lists into xloc [CFB_XROWS][CFB_XFLOATS] fp32 (max, sumexp, top-k values, top-k ids as
+   * float bits, per beam row), ends a segment, and expects the caller to gather every rank's
+   * xloc, in rank order, into xall [ranks][CFB_XROWS][CFB_XFLOATS] before the next segment. */
+  int ranks;           /* 0 or 1: no sharding */
+  int rank;
+  float* xloc;
+  const float* xall;
 } cfb_run;
+
+#define CFB_XROWS 64
+#define CFB_XFLOATS 18
 
 int cfb_abi_version(void);
 const char* cfb_last_cuda_error(void);
@@ -160,8 +175,13 @@ cfb_status cfb_time_embed(const float* w1, const float* b1, const void* w2_f16, 
 cfb_status cfb_plan_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes);
 /* Synchronous set-up: validates shapes, writes the phase table into ws, zeroes counters. */
 cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes);
-/* Launch the persistent kernel on `stream` (no allocation, no host sync: capturable). */
+/* Launch the persistent kernel on `stream` (no allocation, no host synchronisation) for the
+ * whole draft. Plans with a sharded head (cfb_run.ranks > 1) run segment by segment instead. */
 cfb_status cfb_plan_run(void* ws, void* stream);
+/* Segments of a built plan: 1, or K + 1 for a sharded head (the caller gathers xloc into xall
+ * after every segment but the last). cfb_plan_run_segment launches one of them. */
+cfb_status cfb_plan_segments(void* ws, int* nseg);
+cfb_status cfb_plan_run_segment(void* ws, int seg, void* stream);
 /* Synchronous: the plan's device error word: 0 while every run so far completed, else the code
  * of the first failure (a bounded device-side wait that expired). The word is sticky: once it
  * is set, later runs of the plan return at once without touching the outputs, until

@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.cfb_abi_version() == 1
+    assert lib.cfb_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_packed_bytes():
@@ -69,10 +69,13 @@ def fake_drafter(D=2560, L=4, T=8, FM=6, R=62642, rank=256, order=4):
     return d, (experts, blocks)
 
 
-def fake_run(mode, B, grid=148):
+def fake_run(mode, B, grid=148, ranks=1):
     r = _lib.Run()
     r.mode, r.batch, r.width, r.depth, r.tree_keep, r.tree_topb, r.grid = mode, B, 4, 5, 4, 8, grid
     r.ctx = r.z0 = r.known0 = r.pred = r.tokens = FAKE
+    r.ranks, r.rank = ranks, 0
+    if ranks > 1:
+        r.xloc = r.xall = FAKE
     return r
 
 
@@ -116,3 +119,23 @@ def test_untile_inverts_the_tiled_activation_layout():
                 idx = ((k >> 7) * R + r) * 128 + ((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7)
                 buf[idx] = x[r, k]
         assert torch.equal(untile(buf, R, K), x)
+
+
+@pytest.mark.parametrize("ranks", [2, 4, 8])
+def test_sharded_head_plans(ranks):
+    """A row-sharded 27B-shaped head: each rank packs rows [row0, row0 + n) of the shortlist;
+    the plan needs the exchange buffers, and refuses a shard on a single GPU."""
+    lib = _lib.load()
+    R = 62642
+    n = C.c_size_t(0)
+    for rank in range(ranks):
+        row0, rows = rank * R // ranks, (rank + 1) * R // ranks - rank * R // ranks
+        d, keep = fake_drafter(D=5120, R=R)
+        d.head = fake_linear(rows, 5120 + 256)
+        d.head_row0 = row0
+        r = fake_run(_lib.MODE_CHAIN, 1, ranks=ranks)
+        r.rank = rank
+        assert lib.cfb_plan_workspace(C.byref(d), C.byref(r), C.byref(n)) == 0
+        r.xall = None
+        assert lib.cfb_plan_workspace(C.byref(d), C.byref(r), C.byref(n)) == 1      # no exchange buffer
+        assert lib.cfb_plan_workspace(C.byref(d), C.byref(fake_run(_lib.MODE_CHAIN, 1)), C.byref(n)) == 1
