@@ -42,8 +42,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "gdn"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
+                    help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
+                         "eager PyTorch fp16 on the GPU (the reference's eager GPU draft)")
     ap.add_argument("--head-shard", default="auto", choices=["auto", "on", "off"],
                     help="row-shard the shortlist head across the GPUs (auto: the 27B shape on >1 GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -146,11 +149,61 @@ def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float =
         f"{len(times)} drafts of the {wl.name} chain at b=1, fp32 torch on CPU (after 1 warm-up draft)"
 
 
+def eager_gpu_reference_rate(wl, n_drafts: int, warmup: int, seed: int = 0):
+    """The reference algorithm (oracle/ restatement of its eager PyTorch drafter and one-pass beam)
+    in eager fp16 on cuda:0: (tok/s, seconds per draft, sample description)."""
+    import oracle
+    from chain_flow_b200.synthetic import make_state, make_inputs
+    dev = torch.device("cuda", 0)
+    sd, emb, lm, sl = make_state(wl, seed=seed, device=dev)
+    sl = sl.to(dev)
+    hw = lm[sl].contiguous()
+    w2 = sd["markov.w2.weight"][sl].contiguous()
+    del lm
+    ctx, known0 = make_inputs(wl, 1, device=dev)
+    cfg = oracle.FlowConfig(hidden=wl.hidden, ffn_multiplier=wl.ffn, num_layers=wl.layers,
+                            num_flow_steps=wl.steps, markov_rank=wl.markov_rank)
+    g = torch.Generator(device=dev).manual_seed(seed)
+
+    def draft():
+        z0 = torch.randn(1, 6, wl.hidden, generator=g, device=dev, dtype=torch.float16)
+        pred = oracle.integrate(sd, cfg, ctx, z0)
+        return oracle.beam_chains(sd, cfg, emb, hw, w2, sl, pred, known0, wl.width, wl.draft_tokens)
+
+    with torch.inference_mode():
+        for _ in range(max(1, warmup)):
+            draft()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n_drafts):
+            draft()
+        e1.record()
+        torch.cuda.synchronize(dev)
+    spd = e0.elapsed_time(e1) / 1e3 / n_drafts
+    return wl.draft_tokens / spd, spd, (f"{n_drafts} drafts of the {wl.name} chain at b=1: the reference algorithm "
+                                       f"in eager PyTorch fp16 on the GPU (no CUDA graph, no compile)")
+
+
 def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     n = max(1, args.steps)
+    if args.ref_device == "cuda":
+        rate, spd, sample = eager_gpu_reference_rate(wl, n, args.warmup)
+        line = {
+            "metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": 1, "steps": n,
+            "warmup": args.warmup, "ms_per_step": spd * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random weights and inputs)",
+            "config": {"workload": wl.name, "batch_per_gpu": 1, "draft_tokens": wl.draft_tokens,
+                       "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
+                       "shortlist_rows": wl.shortlist_rows, "beam_width": wl.width, "device": "cuda"},
+            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_sample": sample,
+        }
+        print(json.dumps(line), flush=True)
+        return
     rate, spd, threads, sample = cpu_reference_draft_rate(wl, n)
     line = {
         "metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
@@ -312,8 +365,73 @@ def run_ours(args, wl):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------
+def run_gdn(args):
+    """tree-aware Gated-DeltaNet verification of one layer, 16 heads,
+    Dk = Dv = 128, fp32 state, a 16-node tree of depth 5 and branching <= 4 per request, at
+    B = 1, 8 and 64 (one JSON line per B). A step is one cfb_tree_gdn launch over B requests.
+    Algorithmic bytes per request: the prefix state read and the 16 node states written (fp32),
+    q/k/v (fp16), g/beta (fp32), o (fp32)."""
+    from chain_flow_b200.gdn import make_tree, tree_gdn_batched
+    import oracle
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    N, H, Dk, Dv = 16, 16, 128, 128
+    peak, peak_kind = measured_peaks()
+    per_req = H * Dk * Dv * 4 * (1 + N) + N * H * ((2 * Dk + Dv) * 2 + 8 + Dv * 4)
+    for B in (1, 8, 64):
+        g = torch.Generator(device=dev).manual_seed(B)
+        q = torch.nn.functional.normalize(torch.randn(B, N, H, Dk, device=dev, generator=g), dim=-1).half()
+        k = torch.nn.functional.normalize(torch.randn(B, N, H, Dk, device=dev, generator=g), dim=-1).half()
+        v = torch.randn(B, N, H, Dv, device=dev, generator=g).half()
+        gl = torch.log(torch.sigmoid(torch.randn(B, N, H, device=dev, generator=g)))
+        beta = torch.sigmoid(torch.randn(B, N, H, device=dev, generator=g))
+        par = torch.stack([make_tree(N, 5, 4, seed=b)[0] for b in range(B)]).to(dev)
+        init = torch.randn(B, H, Dk, Dv, device=dev, generator=g) * 0.1
+        states = torch.empty(B, N, H, Dk, Dv, device=dev)
+        for _ in range(max(3, args.warmup)):
+            tree_gdn_batched(q, k, v, gl, beta, par, init, states=states)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            tree_gdn_batched(q, k, v, gl, beta, par, init, states=states)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        achieved = B * per_req / (ms / 1e3) / 1e9
+        # CPU baseline: the reference recurrence (oracle) on the host cores, one request
+        torch.set_num_threads(os.cpu_count() or 1)
+        qc, kc, vc = q[0].cpu(), k[0].cpu(), v[0].cpu()
+        gc, bc, ic = gl[0].cpu(), beta[0].cpu(), init[0].cpu()
+        pc = par[0].cpu()
+        dep = make_tree(N, 5, 4, seed=0)[1]
+        oracle.tree_gdn_scan(qc, kc, vc, gc, bc, pc, dep, ic)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            oracle.tree_gdn_scan(qc, kc, vc, gc, bc, pc, dep, ic)
+        cpu_s = (time.perf_counter() - t0) / reps
+        line = {"metric": "tree GDN verification: requests/s (16-node trees, 16 heads, Dk=Dv=128)",
+                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded q,k,v,alpha,beta,trees)",
+                "config": {"workload": "cfg4-tree-gdn", "batch": B, "nodes": N, "heads": H, "dk": Dk, "dv": Dv},
+                "gpu_launches": args.steps,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                             "kernel": "tree_gdn_kernel", "algorithmic_bytes_per_launch": B * per_req},
+                "cpu_baseline": {"value": 1.0 / cpu_s, "unit": "req/s", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": f"{reps} single-request scans, oracle fp32 on CPU"}}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "gdn":
+        run_gdn(args)
+        return
     from chain_flow_b200.synthetic import WORKLOADS
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

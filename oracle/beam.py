@@ -15,7 +15,8 @@ def head_logprobs(W, emb, hw, w2_sl, h, lastp, order, nlive):
     """log_softmax over the shortlist of (h + path residual) @ hw^T + markov bias
     (reference flow_proposer.py:1021-1025, 1247-1249). Returns (logits, logprobs) [N, R]."""
     res = path_residual(W, emb, lastp, order, nlive)
-    logits = (h.float() + res) @ hw.float().T + markov_bias(W, w2_sl, lastp[:, 0])
+    # the reference's dtypes: head and bias in the weights' dtype, log_softmax in fp32
+    logits = ((h.to(res.dtype) + res).to(hw.dtype) @ hw.T + markov_bias(W, w2_sl, lastp[:, 0]).to(hw.dtype)).float()
     return logits, torch.log_softmax(logits, dim=-1)
 
 
@@ -27,11 +28,11 @@ def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int
     extensions of the width x width candidates, then the best path is walked back.
     Returns [B, K] int64 global token ids.
     """
-    B = pred.shape[0]
+    B, dev = pred.shape[0], pred.device
     Wd, order = width, cfg.path_order
-    lastp = torch.full((B, Wd, order), -1, dtype=torch.long)
+    lastp = torch.full((B, Wd, order), -1, dtype=torch.long, device=dev)
     lastp[:, :, 0] = known0.view(B, 1)
-    cum = torch.full((B, Wd), float("-inf"))
+    cum = torch.full((B, Wd), float("-inf"), device=dev)
     cum[:, 0] = 0.0
     steps = min(K + 1, pred.shape[1])
     toks, bps = [], []
@@ -60,13 +61,13 @@ def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, t
               depth: int):
     """Tree draft: every surviving extension becomes a BFS-ordered node. Returns [B, 2N]
     = N global token ids followed by N parent node indices (-1 for depth-1 nodes)."""
-    B = pred.shape[0]
+    B, dev = pred.shape[0], pred.device
     order = cfg.path_order
     fr = 1
-    lastp = torch.full((B, fr, order), -1, dtype=torch.long)
+    lastp = torch.full((B, fr, order), -1, dtype=torch.long, device=dev)
     lastp[:, :, 0] = known0.view(B, 1)
-    cum = torch.zeros(B, fr)
-    prev_ids = torch.full((B, fr), -1, dtype=torch.long)
+    cum = torch.zeros(B, fr, device=dev)
+    prev_ids = torch.full((B, fr), -1, dtype=torch.long, device=dev)
     toks, pars = [], []
     base = 0
     nstep = min(depth, pred.shape[1] - 1)
@@ -84,7 +85,7 @@ def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, t
         pars.append(prev_ids.gather(1, src))
         lastp = lastp.gather(1, src.unsqueeze(-1).expand(B, k, order))
         lastp = torch.cat([newtok.unsqueeze(-1), lastp[:, :, :-1]], dim=-1)
-        prev_ids = base + torch.arange(k).expand(B, k)
+        prev_ids = base + torch.arange(k, device=dev).expand(B, k)
         base += k
         fr = k
     return torch.cat(toks + pars, dim=1)

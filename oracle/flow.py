@@ -107,7 +107,7 @@ def expert_velocity(W, cfg: FlowConfig, e: int, ctx, z, tau: float):
     S = x.shape[1]
     x = x + W[p + "position_embedding.weight"][:S]
     x[:, start:] = x[:, start:] + time_embedding(W, p, tau)
-    mask = torch.triu(torch.full((S, S), float("-inf")), diagonal=1)
+    mask = torch.triu(torch.full((S, S), float("-inf"), device=z.device, dtype=z.dtype), diagonal=1)
     for i in range(cfg.num_layers):
         x = flow_block(x, ctx, W, f"{p}blocks.{i}.", cfg.num_heads, mask)
     cur = layer_norm(x[:, start:], W[p + "out_norm.weight"], W[p + "out_norm.bias"])
@@ -117,9 +117,10 @@ def expert_velocity(W, cfg: FlowConfig, e: int, ctx, z, tau: float):
 def integrate(W, cfg: FlowConfig, ctx, z0):
     """Explicit Euler over tau = s/T, s = 0..T-1 (reference tree_flow.py:229-235). Every chunk
     expert reads the same iterate z (reference tree_flow.py:163-174), so the experts of one step
-    are independent."""
-    z = z0.float()
-    ctx = ctx.float()
+    are independent. Computes in the dtype of the expert weights (fp32 for the CPU checks)."""
+    wd = W[cfg.expert_prefix(0) + "out_proj.weight"].dtype
+    z = z0.to(wd)
+    ctx = ctx.to(wd)
     T = cfg.num_flow_steps
     dt = 1.0 / T
     for s in range(T):
@@ -139,9 +140,10 @@ def path_residual(W, emb, lastp, order: int, nlive: int | None = None):
     h = sum_j mask_j * (W_j emb(lastp_j) + b_j);  res = W_m2 gelu(W_m1 LN(h) + b_m1) + b_m2.
     """
     o = order if nlive is None else min(nlive, order)
+    wd = W["path_head.offset_proj.0.weight"].dtype
     lp = lastp[:, :o]
-    mask = (lp >= 0).float()
-    e = emb[lp.clamp_min(0)].float()                          # [N, o, D]
+    mask = (lp >= 0).to(wd)
+    e = emb[lp.clamp_min(0)].to(wd)                           # [N, o, D]
     h = None
     for j in range(o):
         t = (e[:, j] @ W[f"path_head.offset_proj.{j}.weight"].T
@@ -155,4 +157,4 @@ def path_residual(W, emb, lastp, order: int, nlive: int | None = None):
 def markov_bias(W, w2_sl, prev):
     """MarkovHead bias on the shortlist rows: w1[prev] @ w2[sl]^T (reference
     markov_flow.py:72-74, flow_proposer.py:1024-1025)."""
-    return W["markov.w1.weight"][prev].float() @ w2_sl.float().T
+    return W["markov.w1.weight"][prev].to(w2_sl.dtype) @ w2_sl.T
