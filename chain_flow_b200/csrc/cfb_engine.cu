@@ -166,6 +166,7 @@ struct Plan {
   const __half* emb; __half* pg;            // embeddings; tiled path-gather rows of the path GEMM
   int nranks; const float* xall; float* xloc;   // row-sharded head: gathered / local merged lists
   int nseg; int seg[kMaxSeg + 1];           // launch segments: phases [seg[i], seg[i + 1])
+  int maxnt;                                // engine_kernel<maxnt> runs this plan
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
   unsigned long long* prof;                // [nphases][G][4] or NULL
 };
@@ -406,7 +407,7 @@ CFB_DEV void attn_task(const AttnTask& A, int b, int h, Smem& S, const Grp& W) {
 }
 
 // An attention phase: its (task, request, head) items spread over the CTAs, one at a time.
-CFB_DEV void attn_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
+__device__ __noinline__ void attn_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
   for (int t = blockIdx.x; t < ph.ntiles; t += P.G) {
     int jx = 0, rem = t;
     for (; jx < ph.njobs; ++jx) {
@@ -867,20 +868,22 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
   (void)tile;
 }
 
+// MAXNT: the widest job of the plan in 8-row n-tiles (1, 2, 4 or 8). Each engine_kernel
+// instantiation carries only the MMA loops its plans can need: wider variants cost registers
+// (spills) and instruction-cache room in every phase.
+template <int MAXNT>
 CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& tseq, Smem& S, WaitClock& wc) {
   const UnitRange cu = cta_units(P, ph);
   for (int jx = 0; jx < ph.njobs; ++jx) {
     const Job& J = P.jobs[ph.job0 + jx];
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
-    switch ((J.rows + 7) / 8) {
-      case 1: mma_job<1, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 2: mma_job<2, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 3: mma_job<3, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 4: mma_job<4, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      case 5: case 6: mma_job<6, false>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-      default: mma_job<4, true>(P, J, ju0, ju1, ci, tseq, S, wc); break;
-    }
+    const int nt = (J.rows + 7) / 8;
+    if (MAXNT <= 1 || nt <= 1) mma_job<1, false>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (MAXNT <= 2 || nt <= 2) mma_job<2, false>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (MAXNT <= 4 || nt <= 4) mma_job<4, false>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (nt <= 6) mma_job<6, false>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else mma_job<4, true>(P, J, ju0, ju1, ci, tseq, S, wc);
   }
 }
 
@@ -1019,7 +1022,7 @@ CFB_DEV float z0_at(const Plan& P, int b, int pos, int col) {
 // an absent token) into the path GEMM's tiled activation, and markov w1[last token] into the
 // head input's columns [D, D + rank) (reference tree_flow.py:434-450, markov_flow.py:72-74).
 // `from_known0`: depth 1, whose only path token is the committed one.
-CFB_DEV void path_gather(const Plan& P, int fr, int R, int row0, int nrows, int nlive, bool from_known0,
+__device__ __noinline__ void path_gather(const Plan& P, int fr, int R, int row0, int nrows, int nlive, bool from_known0,
                          long long t, long long nt) {
   const int D = P.D, order = P.order, rank = P.rank;
   const int cpe = D / 8;                         // 16-byte chunks per embedding row
@@ -1055,7 +1058,7 @@ CFB_DEV void path_gather(const Plan& P, int fr, int R, int row0, int nrows, int 
   }
 }
 
-CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
+__device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
   const long long gtid = (long long)blockIdx.x * W.n + W.t;
   const long long gthreads = (long long)P.G * W.n;
   for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
@@ -1133,7 +1136,7 @@ CFB_DEV void prep_phase(const Plan& P, const Grp& W) {
 // ------------------------------------------------------------------------------------------
 // after the head GEMM: every CTA publishes its (max, sumexp, top-TB) per beam row, merging the
 // row's slice lanes (their sorted lists) by TB rounds of a lane argmax
-CFB_DEV void head_post(const Plan& P, const Phase& ph, HeadState& H, const Grp& E) {
+__device__ __noinline__ void head_post(const Plan& P, const Phase& ph, HeadState& H, const Grp& E) {
   const int rows = ph.rows, TB = ph.topb;
   const RowMap M = row_map(rows, E.t);
   float m = H.m, ssum = H.s;
@@ -1239,7 +1242,7 @@ CFB_DEV void merge_rows(const Plan& P, const float* src, int nlists, int b, int 
 
 // Rank-local merge of a row-sharded head (PK_RMERGE): request b's rows of this rank's CTA lists
 // merged into one list per row in xloc, for the caller to gather across ranks.
-CFB_DEV void rmerge_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
+__device__ __noinline__ void rmerge_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
   const MergeBufs M = merge_bufs(S);
   const int fr = ph.fr, TB = ph.topb;
   for (int b = blockIdx.x; b < P.B; b += P.G) {
@@ -1262,7 +1265,7 @@ CFB_DEV void rmerge_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W)
 // tree). The frontier rows' lists are merged (the CTAs' lists, or for a row-sharded head the
 // ranks' gathered lists), then one thread picks the survivors from shared memory and all
 // threads write the new frontier and gather the next depth's path and markov rows.
-CFB_DEV void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, unsigned long long* prow) {
+__device__ __noinline__ void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, unsigned long long* prow) {
   const bool treem = (ph.post == PO_BEAM_TREE);
   const int fr = ph.fr, TB = ph.topb, order = P.order, step = ph.step, Wm = P.Wmax;
   const int TB2 = treem ? TB : P.width;
@@ -1365,6 +1368,9 @@ CFB_DEV void beam_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W, u
 
 // ------------------------------------------------------------------------------------------
 // Runs phases [p0, p1) of the plan: the whole table, or one segment of a sharded-head plan.
+// The phases that run once per draft or per depth (prep, attention, beam, gathers) are out of
+// line, so the GEMM path stays compact in the instruction cache.
+template <int MAXNT>
 __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp, int p0, int p1) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const Plan& P = *Pp;
@@ -1441,7 +1447,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
           prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
         }
       } else {
-        mma_phase(P, ph, ci, tseq, S, wc);
+        mma_phase<MAXNT>(P, ph, ci, tseq, S, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
@@ -1879,7 +1885,8 @@ cfb_status lower(Builder& B, size_t* bytes) {
     int rows_max = 1, xrows_max = 1;
     for (const auto& j : B.jobs) { rows_max = std::max(rows_max, j.rows); xrows_max = std::max(xrows_max, std::max(j.rows, j.xcopy)); }
     const int ntb = (rows_max + 7) / 8;
-    const int bucket = ntb <= 4 ? ntb : ntb <= 6 ? 6 : 8;       // mma_job<NT> instantiations
+    const int bucket = ntb <= 2 ? ntb : ntb <= 4 ? 4 : ntb <= 6 ? 6 : 8;   // mma_job<NT> widths
+    B.P.maxnt = ntb <= 1 ? 1 : ntb <= 2 ? 2 : ntb <= 4 ? 4 : 8;
     const int RP = bucket * 8;
     const size_t slot_bytes = (size_t)cfb::kMmaWarps * 16 * RP * 4;
     size_t scratch = (size_t)2 * cfb::kRowsMax * cfb::kTopMax * 4;
@@ -1987,27 +1994,39 @@ cfb_status lower(Builder& B, size_t* bytes) {
 }
 
 struct LaunchRecord { int G, phases, smem, pad; };
-struct LaunchRec { void* ws; int G, smem, nseg; int seg[cfb::kMaxSeg + 1]; };
+struct LaunchRec { void* ws; int G, smem, nseg, maxnt; int seg[cfb::kMaxSeg + 1]; };
 std::vector<LaunchRec> g_launch;     // launch shape of the plan last built in each workspace
+using EngineFn = void (*)(const cfb::Plan*, int, int);
+// the engine_kernel instantiation for plans whose widest job has `maxnt` 8-row n-tiles
+EngineFn engine_for(int maxnt) {
+  switch (maxnt) {
+    case 1: return cfb::engine_kernel<1>;
+    case 2: return cfb::engine_kernel<2>;
+    case 4: return cfb::engine_kernel<4>;
+    default: return cfb::engine_kernel<8>;
+  }
+}
+int kernel_slot(int maxnt) { return maxnt == 1 ? 0 : maxnt == 2 ? 1 : maxnt == 4 ? 2 : 3; }
 void remember_launch(void* ws, const cfb::Plan& P, int smem) {
-  LaunchRec r{ws, P.G, smem, P.nseg, {}};
+  LaunchRec r{ws, P.G, smem, P.nseg, P.maxnt, {}};
   for (int i = 0; i <= P.nseg; ++i) r.seg[i] = P.seg[i];
   for (auto& l : g_launch) if (l.ws == ws) { l = r; return; }
   g_launch.push_back(r);
 }
 // The kernel's dynamic shared-memory limit is a property of the function (per device), shared
 // by every plan: raise it to what this plan needs, never lower it under another plan.
-cfb_status ensure_smem_attr(int smem) {
+cfb_status ensure_smem_attr(int maxnt, int smem) {
   static std::mutex mu;
-  static int attr[64] = {};
+  static int attr[64][4] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "get device");
+  const int k = kernel_slot(maxnt);
   std::lock_guard<std::mutex> lock(mu);
-  if (dev >= 0 && dev < 64 && attr[dev] >= smem) return CFB_OK;
-  e = cudaFuncSetAttribute(cfb::engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (dev >= 0 && dev < 64 && attr[dev][k] >= smem) return CFB_OK;
+  e = cudaFuncSetAttribute(engine_for(maxnt), cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "smem attribute");
-  if (dev >= 0 && dev < 64) attr[dev] = smem;
+  if (dev >= 0 && dev < 64) attr[dev][k] = smem;
   return CFB_OK;
 }
 
@@ -2046,9 +2065,9 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   if (need > bytes) return CFB_ERR_WORKSPACE;
   cudaError_t e;
   const int smem = B.P.sm.total;
-  if ((st = ensure_smem_attr(smem)) != CFB_OK) return st;
+  if ((st = ensure_smem_attr(B.P.maxnt, smem)) != CFB_OK) return st;
   int per_sm = 0, dev = 0, sms = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfb::engine_kernel, cfb::kThreads, smem)) !=
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, engine_for(B.P.maxnt), cfb::kThreads, smem)) !=
       cudaSuccess)
     return cuda_fail(e, "occupancy");
   cudaGetDevice(&dev);
@@ -2088,11 +2107,11 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
 }
 
 static cfb_status launch_range(void* ws, const LaunchRec& L, int p0, int p1, void* stream) {
-  const cfb_status st = ensure_smem_attr(L.smem);
+  const cfb_status st = ensure_smem_attr(L.maxnt, L.smem);
   if (st != CFB_OK) return st;
   const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
   void* args[] = {(void*)&P, (void*)&p0, (void*)&p1};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)cfb::engine_kernel, dim3(L.G), dim3(cfb::kThreads),
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)engine_for(L.maxnt), dim3(L.G), dim3(cfb::kThreads),
                                               args, (size_t)L.smem, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;
   if (e != cudaSuccess) return cuda_fail(e, "engine launch");
