@@ -43,6 +43,7 @@
 #include <vector>
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "cfb_common.cuh"
 #include "../../include/cfb.h"
@@ -195,12 +196,20 @@ struct HeadState { float m, s; float tv[kTopMax]; int ti[kTopMax]; };
 // Profiling (plans built with CFB_RUN_PROFILE): ns spent waiting, per role, reset every phase,
 // and the times of a few events (the layout of a CFB_BUF_PROF record is documented in cfb.h).
 constexpr int kProfSlots = 20;
-struct WaitClock {
+// Two clock types: plans built with CFB_RUN_PROFILE run the engine instantiation with ProfClock;
+// every other plan gets NoClock, whose fields are never touched (every use sits under `if
+// (wc.on)`), so unprofiled kernels spend no registers on profiling.
+struct ProfClock {
   unsigned long long full = 0, slot = 0;
   unsigned long long first = 0, last = 0;   // when the phase's first / last unit was ready
   unsigned long long part = 0, atom = 0, fix = 0, tdone = 0;   // epilogue: last tile's events
   bool on = false;
   CFB_DEV unsigned long long now() const { return on ? globaltimer() : 0ull; }
+};
+struct NoClock {
+  unsigned long long full, slot, first, last, part, atom, fix, tdone;
+  static constexpr bool on = false;
+  CFB_DEV unsigned long long now() const { return 0ull; }
 };
 
 // ------------------------------------------------------------------------------------------
@@ -525,12 +534,15 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
           }
           float v[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int col = col0 + f0 + i;
-            v[i] = epi_val(S, f0 + i, M.r) + add[i];
-            if (J.ekind == EK_RESID) J.out32[(size_t)M.r * J.ldo + col] = v[i];
-            J.out16[tidx(J.oR, M.r, col)] = __float2half_rn(v[i]);
+          for (int i = 0; i < 8; ++i) v[i] = epi_val(S, f0 + i, M.r) + add[i];
+          if (J.ekind == EK_RESID) {
+            float4* o32 = reinterpret_cast<float4*>(J.out32 + (size_t)M.r * J.ldo + col0 + f0);
+            o32[0] = make_float4(v[0], v[1], v[2], v[3]);
+            o32[1] = make_float4(v[4], v[5], v[6], v[7]);
           }
+          // 8 consecutive columns from a multiple of 8 are 16 contiguous bytes of the tiled layout
+          *reinterpret_cast<uint4*>(J.out16 + tidx(J.oR, M.r, col0 + f0)) =
+              make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
           stats8_merge(n, m, M2, v);
         }
       }
@@ -624,6 +636,7 @@ CFB_DEV void epi_prefetch(const Plan& P, const Job& J, int tile, const Grp& E) {
 
 // Epilogue side of one tile: take the MMA warps' partials from slot buffer `b`, reduce them in a
 // fixed order, release the slot, then finish the tile directly or through the stream-K fixup.
+template <class WaitClock>
 CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
                       long long ug_first, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
                       WaitClock& wc) {
@@ -772,7 +785,7 @@ CFB_DEV bool job_slice(const Job& J, const UnitRange& cu, int& ju0, int& ju1) {
 // m16 tile, each of them takes all k blocks for half of the n-tiles (NT each), which halves the
 // accumulators a thread holds; it writes zeros for the other half's rows so that the
 // epilogue's fixed two-slice sum is unchanged.
-template <int NT, bool NSPLIT>
+template <int NT, bool NSPLIT, class WaitClock>
 CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci, uint32_t& tseq, Smem& S,
                      WaitClock& wc) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -838,7 +851,7 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
     if (kc == nkc - 1 || ju == ju1 - 1) {
       const unsigned long long w1 = wc.now();
       if (!mbar_wait(&S.acce[slot], spar ^ 1u, err)) set_err(P, DEV_TIMEOUT_SLOT);
-      wc.slot += wc.now() - w1;
+      if (wc.on) wc.slot += wc.now() - w1;
       float* sl = S.slots + ((size_t)slot * kMmaWarps + warp) * 16 * rp;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -871,7 +884,7 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
 // MAXNT: the widest job of the plan in 8-row n-tiles (1, 2, 4 or 8). Each engine_kernel
 // instantiation carries only the MMA loops its plans can need: wider variants cost registers
 // (spills) and instruction-cache room in every phase.
-template <int MAXNT>
+template <int MAXNT, class WaitClock>
 CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& tseq, Smem& S, WaitClock& wc) {
   const UnitRange cu = cta_units(P, ph);
   for (int jx = 0; jx < ph.njobs; ++jx) {
@@ -879,15 +892,16 @@ CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& t
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
     const int nt = (J.rows + 7) / 8;
-    if (MAXNT <= 1 || nt <= 1) mma_job<1, false>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (MAXNT <= 2 || nt <= 2) mma_job<2, false>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (MAXNT <= 4 || nt <= 4) mma_job<4, false>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (nt <= 6) mma_job<6, false>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else mma_job<4, true>(P, J, ju0, ju1, ci, tseq, S, wc);
+    if (MAXNT <= 1 || nt <= 1) mma_job<1, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (MAXNT <= 2 || nt <= 2) mma_job<2, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (MAXNT <= 4 || nt <= 4) mma_job<4, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else if (nt <= 6) mma_job<6, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
+    else mma_job<4, true, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
   }
 }
 
 // Epilogue warps: the same tiles in the same order.
+template <class WaitClock>
 CFB_DEV void epi_phase(const Plan& P, const Phase& ph, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
                        WaitClock& wc) {
   const long long U = ph.nunits;
@@ -1372,6 +1386,12 @@ __device__ __noinline__ void beam_phase(const Plan& P, const Phase& ph, Smem& S,
 // line, so the GEMM path stays compact in the instruction cache.
 template <int MAXNT>
 __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp, int p0, int p1) {
+  // The narrow classes (jobs of <= 16 rows) measured faster with the per-phase profiling
+  // switched at run time (CFB_RUN_PROFILE); the wider ones with the profiling compiled out
+  // (their plans record no stamps), which frees registers. Results are the same.
+  constexpr bool kLean = MAXNT > 2;
+  constexpr bool kProf = !kLean;                  // profiling code present in this instantiation
+  using WaitClock = typename std::conditional<kProf, ProfClock, NoClock>::type;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const Plan& P = *Pp;
   const SmemLayout L = P.sm;
@@ -1416,17 +1436,19 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   uint32_t ci = 0, tseq = 0;
   unsigned epoch = 0;
   bool ok = !dead;
-  HeadState H;
+  const bool rec = kProf && P.prof && ((!is_epi && tid == 0) || (is_epi && E.t == 0));
+  HeadState H;                   // the head phases' per-row (max, sumexp, top-k) of this thread
   head_reset(H);
-  WaitClock wc;
-  const bool rec = P.prof && ((!is_epi && tid == 0) || (is_epi && E.t == 0));
-  wc.on = rec;
   for (int p = p0; p < p1 && ok; ++p) {
     const Phase& ph = P.phases[p];
-    unsigned long long* prow = P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * kProfSlots : nullptr;
-    unsigned long long* stamp = (P.prof && Wk.t == 0) ? prow : nullptr;
-    wc.full = wc.slot = wc.first = wc.last = 0;
-    wc.part = wc.atom = wc.fix = wc.tdone = 0;
+    unsigned long long* prow = kProf && P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * kProfSlots : nullptr;
+    unsigned long long* stamp = (kProf && P.prof && Wk.t == 0) ? prow : nullptr;
+    WaitClock wc;
+    if constexpr (kProf) {
+      wc.on = rec;
+      wc.full = wc.slot = wc.first = wc.last = 0;
+      wc.part = wc.atom = wc.fix = wc.tdone = 0;
+    }
     if (stamp) stamp[0] = globaltimer();
     if (Wk.t == 0) *S.phase_ready = p;
     if (ph.kind == PK_PREP) {
@@ -1447,7 +1469,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
           prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
         }
       } else {
-        mma_phase<MAXNT>(P, ph, ci, tseq, S, wc);
+        mma_phase<MAXNT, WaitClock>(P, ph, ci, tseq, S, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
@@ -1894,6 +1916,8 @@ cfb_status lower(Builder& B, size_t* bytes) {
       const int hd = D / d.heads, Kmax = std::max(DL, C);
       scratch = std::max(scratch, (size_t)((DL + 2 * Kmax) * hd + DL * Kmax) * 4);
     }
+    // a split tile's owner lists the other contributors (at most G) in the scratch
+    scratch = std::max(scratch, (size_t)(G + 1) * 4);
     scratch = (scratch + 127) / 128 * 128;
     const int red = cfb::kTileRows * RP * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
     const int bars = (2 * cfb::kMaxStages + 4) * 8;
@@ -1994,11 +2018,12 @@ cfb_status lower(Builder& B, size_t* bytes) {
 }
 
 struct LaunchRecord { int G, phases, smem, pad; };
-struct LaunchRec { void* ws; int G, smem, nseg, maxnt; int seg[cfb::kMaxSeg + 1]; };
+struct LaunchRec { void* ws; int G, smem, nseg, maxnt; bool prof; int seg[cfb::kMaxSeg + 1]; };
 std::vector<LaunchRec> g_launch;     // launch shape of the plan last built in each workspace
 using EngineFn = void (*)(const cfb::Plan*, int, int);
-// the engine_kernel instantiation for plans whose widest job has `maxnt` 8-row n-tiles
-EngineFn engine_for(int maxnt) {
+// the engine_kernel instantiation for plans whose widest job has `maxnt` 8-row n-tiles, with or
+// without the per-phase profiling stamps
+EngineFn engine_for(int maxnt, bool) {
   switch (maxnt) {
     case 1: return cfb::engine_kernel<1>;
     case 2: return cfb::engine_kernel<2>;
@@ -2006,25 +2031,25 @@ EngineFn engine_for(int maxnt) {
     default: return cfb::engine_kernel<8>;
   }
 }
-int kernel_slot(int maxnt) { return maxnt == 1 ? 0 : maxnt == 2 ? 1 : maxnt == 4 ? 2 : 3; }
+int kernel_slot(int maxnt, bool) { return maxnt == 1 ? 0 : maxnt == 2 ? 1 : maxnt == 4 ? 2 : 3; }
 void remember_launch(void* ws, const cfb::Plan& P, int smem) {
-  LaunchRec r{ws, P.G, smem, P.nseg, P.maxnt, {}};
+  LaunchRec r{ws, P.G, smem, P.nseg, P.maxnt, P.prof != nullptr, {}};
   for (int i = 0; i <= P.nseg; ++i) r.seg[i] = P.seg[i];
   for (auto& l : g_launch) if (l.ws == ws) { l = r; return; }
   g_launch.push_back(r);
 }
 // The kernel's dynamic shared-memory limit is a property of the function (per device), shared
 // by every plan: raise it to what this plan needs, never lower it under another plan.
-cfb_status ensure_smem_attr(int maxnt, int smem) {
+cfb_status ensure_smem_attr(int maxnt, bool prof, int smem) {
   static std::mutex mu;
-  static int attr[64][4] = {};
+  static int attr[64][8] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "get device");
-  const int k = kernel_slot(maxnt);
+  const int k = kernel_slot(maxnt, prof);
   std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < 64 && attr[dev][k] >= smem) return CFB_OK;
-  e = cudaFuncSetAttribute(engine_for(maxnt), cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  e = cudaFuncSetAttribute(engine_for(maxnt, prof), cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "smem attribute");
   if (dev >= 0 && dev < 64) attr[dev][k] = smem;
   return CFB_OK;
@@ -2065,9 +2090,10 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   if (need > bytes) return CFB_ERR_WORKSPACE;
   cudaError_t e;
   const int smem = B.P.sm.total;
-  if ((st = ensure_smem_attr(B.P.maxnt, smem)) != CFB_OK) return st;
+  const bool prof = B.P.prof != nullptr;
+  if ((st = ensure_smem_attr(B.P.maxnt, prof, smem)) != CFB_OK) return st;
   int per_sm = 0, dev = 0, sms = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, engine_for(B.P.maxnt), cfb::kThreads, smem)) !=
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, engine_for(B.P.maxnt, prof), cfb::kThreads, smem)) !=
       cudaSuccess)
     return cuda_fail(e, "occupancy");
   cudaGetDevice(&dev);
@@ -2107,11 +2133,11 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
 }
 
 static cfb_status launch_range(void* ws, const LaunchRec& L, int p0, int p1, void* stream) {
-  const cfb_status st = ensure_smem_attr(L.maxnt, L.smem);
+  const cfb_status st = ensure_smem_attr(L.maxnt, L.prof, L.smem);
   if (st != CFB_OK) return st;
   const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
   void* args[] = {(void*)&P, (void*)&p0, (void*)&p1};
-  cudaError_t e = cudaLaunchCooperativeKernel((const void*)engine_for(L.maxnt), dim3(L.G), dim3(cfb::kThreads),
+  cudaError_t e = cudaLaunchCooperativeKernel((const void*)engine_for(L.maxnt, L.prof), dim3(L.G), dim3(cfb::kThreads),
                                               args, (size_t)L.smem, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;
   if (e != cudaSuccess) return cuda_fail(e, "engine launch");
