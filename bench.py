@@ -282,8 +282,10 @@ def run_ours(args, wl):
     if prop.device_error():
         raise SystemExit(f"device-side wait timed out (code {prop.device_error()})")
 
-    # ---- the engine kernel alone (roofline): back-to-back launches of the bound plan
-    plan = prop._plan(_lib.MODE_CHAIN, B)
+    # ---- the engine kernel alone (roofline): back-to-back launches of the bound plan (batches
+    # above one plan's capacity run as several plans; the roofline is that of one plan)
+    from chain_flow_b200.proposer import MAX_PLAN_BATCH
+    plan = prop._plan(_lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH))
     torch.cuda.synchronize(dev)
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0.record(stream)
@@ -324,7 +326,7 @@ def run_ours(args, wl):
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0)   # per GPU
+        algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0)   # per GPU, per plan
         achieved = algo / (kernel_ms / 1e3) / 1e9
         traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "engine_dram_traffic.json"
@@ -342,7 +344,7 @@ def run_ours(args, wl):
             "config": {"workload": wl.name, "batch_per_gpu": B, "draft_tokens": wl.draft_tokens,
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
-                       "beam_width": wl.width,
+                       "beam_width": wl.width, "plans_per_step": (B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH,
                        "parallelism": (f"shortlist head rows sharded over {world} GPUs, flow replicated, "
                                        f"one NCCL all_gather of merged top-k lists per depth") if shard
                        else f"requests split over {world} GPU(s)",
@@ -350,7 +352,7 @@ def run_ours(args, wl):
                              f"weights stream from HBM every step"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * plan.segments,
+            "gpu_launches": args.steps * plan.segments * ((B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
                          "peak_source": peak_kind,

@@ -28,6 +28,11 @@ from .engine import Plan
 from .weights import DraftConfig, DrafterWeights
 
 
+# requests one engine plan drafts at once: its jobs hold at most 64 activation rows
+# (B x context rows, B x draft_length, B x beam width); larger batches run as several plans
+MAX_PLAN_BATCH = 8
+
+
 def _env_int(name: str, default: int) -> int:
     v = os.environ.get(name)
     return int(v) if v not in (None, "") else default
@@ -169,28 +174,36 @@ class FlowDrafterProposer:
             p.z0.normal_(generator=self._gen).mul_(self.noise_scale)
 
     # ------------------------------------------------------------------ drafting interface
+    def _run(self, mode: int, ctx: torch.Tensor, known0: torch.Tensor | None, out: str) -> torch.Tensor:
+        """One plan launch per chunk of at most MAX_PLAN_BATCH requests."""
+        B = ctx.shape[0]
+        if B <= MAX_PLAN_BATCH:
+            p = self._plan(mode, B)
+            self._load_inputs(p, ctx, known0)
+            p.run(group=self.group)
+            return getattr(p, out)
+        parts = []
+        for b0 in range(0, B, MAX_PLAN_BATCH):
+            b1 = min(B, b0 + MAX_PLAN_BATCH)
+            p = self._plan(mode, b1 - b0)
+            self._load_inputs(p, ctx[b0:b1], None if known0 is None else known0[b0:b1])
+            p.run(group=self.group)
+            parts.append(getattr(p, out).clone())
+        return torch.cat(parts, dim=0)
+
     @torch.inference_mode()
     def predict_hidden(self, ctx: torch.Tensor) -> torch.Tensor:
-        p = self._plan(_lib.MODE_FLOW, ctx.shape[0])
-        self._load_inputs(p, ctx, None)
-        p.run(group=self.group)
-        return p.pred
+        return self._run(_lib.MODE_FLOW, ctx, None, "pred")
 
     @torch.inference_mode()
     def _beam_chains(self, ctx: torch.Tensor, known0: torch.Tensor) -> torch.Tensor:
         """[B, K] int64 chain drafts; ``known0`` is the token vLLM just committed."""
-        p = self._plan(_lib.MODE_CHAIN, ctx.shape[0])
-        self._load_inputs(p, ctx, known0)
-        p.run(group=self.group)
-        return p.tokens
+        return self._run(_lib.MODE_CHAIN, ctx, known0.view(-1), "tokens")
 
     @torch.inference_mode()
     def _beam_tree(self, ctx: torch.Tensor, known0: torch.Tensor) -> torch.Tensor:
         """[B, 2N] int64: N BFS-ordered draft tokens followed by their N parent indices (-1 = root)."""
-        p = self._plan(_lib.MODE_TREE, ctx.shape[0])
-        self._load_inputs(p, ctx, known0)
-        p.run(group=self.group)
-        return p.tokens
+        return self._run(_lib.MODE_TREE, ctx, known0.view(-1), "tokens")
 
     def device_error(self) -> int:
         """Synchronous: non-zero if a bounded device-side wait expired in any cached plan's last run."""

@@ -143,3 +143,38 @@ def test_batch8_flow_and_chain_match_oracle():
     assert _rel(p.pred, want) < HIDDEN_RTOL, _rel(p.pred, want)
     ch = oracle.beam_chains(sd, ocfg, emb, lm[sl], sd["markov.w2.weight"][sl], sl, p.pred.cpu(), known0, 4, 5)
     assert torch.equal(p.tokens.cpu(), ch), (p.tokens.cpu(), ch)
+
+
+def test_batches_above_one_plan_run_as_several_plans():
+    """B = 11 > MAX_PLAN_BATCH: the proposer drafts requests [0, 8) and [8, 11) as two plans. The
+    hiddens stay within tolerance of the oracle for all 11, and the drafts equal those of the two
+    chunks drafted on their own (same plans, same inputs)."""
+    from chain_flow_b200.proposer import MAX_PLAN_BATCH, FlowDrafterProposer
+    from chain_flow_b200.weights import DraftConfig
+    from gpu_util import random_state_dict
+    D, V, R, B = 256, 2000, 512, MAX_PLAN_BATCH + 3
+    margs = dict(context_size=8, draft_length=6, chunk_size=3, num_heads=8, ffn_multiplier=2,
+                 num_drafter_layers=2, num_flow_steps=2, path_order=4, path_ffn_multiplier=2, markov_rank=32,
+                 init_mode="delta", noise_scale=1.0)
+    cfg = DraftConfig.from_model_args(margs, D)
+    sd = random_state_dict(cfg, V, seed=7)
+    g = torch.Generator().manual_seed(8)
+    emb = (torch.randn(V, D, generator=g) * 0.5).half().float()
+    lm = (torch.randn(V, D, generator=g) * 0.02).half().float()
+    sl = torch.randperm(V, generator=g)[:R].sort().values
+    p = FlowDrafterProposer.from_components(sd, margs, emb, lm, sl, width=4, K=5, tree_keep=4, tree_topb=4,
+                                            tree_depth=5, device="cuda")
+    ctx = torch.randn(B, 8, D, generator=g).half().cuda()
+    known0 = torch.randint(0, V, (B,), generator=g).cuda()
+    pred = p.predict_hidden(ctx).clone()
+    assert pred.shape[0] == B
+    ocfg = oracle.FlowConfig(hidden=D, num_heads=8, ffn_multiplier=2, num_layers=2, num_flow_steps=2,
+                             markov_rank=32)
+    c = ctx.float().cpu()
+    want = oracle.integrate(sd, ocfg, c, _delta_z0(c).half().float())
+    assert _rel(pred, want) < HIDDEN_RTOL, _rel(pred, want)
+    for fn in (p._beam_chains, p._beam_tree):
+        whole = fn(ctx, known0).clone()
+        parts = [fn(ctx[a:b], known0[a:b]).clone() for a, b in ((0, MAX_PLAN_BATCH), (MAX_PLAN_BATCH, B))]
+        assert torch.equal(whole, torch.cat(parts)), fn.__name__
+    assert p.device_error() == 0
