@@ -27,12 +27,14 @@ EXPORTED = [
     "cfb_abi_version", "cfb_last_cuda_error", "cfb_packed_bytes", "cfb_pack_linear",
     "cfb_fold_bias", "cfb_time_embed", "cfb_plan_workspace", "cfb_plan_build", "cfb_plan_run",
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
-    "cfb_plan_segments", "cfb_plan_run_segment",
+    "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_workspace",
+    "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
 ]
 ABI_VERSION = 2
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF = range(9)
 RUN_PROFILE = 1
+EPI_F32, EPI_F16, EPI_GELU16, EPI_PART = 0, 1, 2, 3      # cfb_wide_gemm epilogues
 
 
 class CfbError(RuntimeError):
@@ -96,6 +98,14 @@ def _declare(lib):
     lib.cfb_plan_buffer.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(sz)]
     lib.cfb_tree_gdn.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
     lib.cfb_tree_gdn_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
+    lib.cfb_wide_gemm.argtypes = [vp, i64, vp, i64, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]
+    lib.cfb_wide_workspace.argtypes = [C.POINTER(Drafter), C.POINTER(Run), C.POINTER(sz)]
+    lib.cfb_wide_create.argtypes = [C.POINTER(Drafter), C.POINTER(Run), vp, sz, C.POINTER(vp)]
+    lib.cfb_wide_run.argtypes = [vp, vp]
+    lib.cfb_wide_error.argtypes = [vp, C.POINTER(i32)]
+    lib.cfb_wide_info.argtypes = [vp, C.POINTER(i32)]
+    lib.cfb_wide_destroy.argtypes = [vp]
+    lib.cfb_wide_destroy.restype = None
     return lib
 
 

@@ -1,0 +1,130 @@
+// cfb_wide_gemm.cuh -- the batched ("wide") drafting path's GEMM: C = A · Wᵀ on the 5th-generation
+// tensor cores of sm_100a.
+//
+// A is an fp16 activation matrix [M, K] and W an fp16 weight matrix [N, K], both row-major
+// (K-major). One CTA computes one 128 × 128 output tile (128 activation rows × 128 weight rows)
+// over one k range (split-K). 192 threads in three roles:
+//   warp 0, one lane   TMA producer: 2-D tiled bulk tensor copies of a 128 × 64 A tile and a
+//                      128 × 64 W tile per stage (128-byte swizzle) into a kStages-deep ring;
+//   warp 1             allocates 128 TMEM columns (the fp32 accumulator); one lane issues
+//                      tcgen05.mma (M = 128, N = 128, K = 16, four per stage) and returns each
+//                      stage to the producer with tcgen05.commit;
+//   warps 2..5         epilogue: each thread owns one accumulator row (its TMEM lane), reads it
+//                      16 columns at a time with tcgen05.ld and applies the fused epilogue.
+// Every wait is bounded (kWaitBudgetNs); a wait that expires records an error and the CTA
+// winds down (the producer first waits, bounded, for its copies in flight; TMEM is always freed).
+#pragma once
+#include <cuda.h>
+#include "cfb_common.cuh"
+
+namespace cfb {
+namespace wide {
+
+constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int kStages = 6;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTileBytes = BM * BK * 2;             // 16 KiB, A and W tiles alike
+constexpr uint32_t kStageBytes = 2 * kTileBytes;
+constexpr size_t kGemmSmem = kStages * kStageBytes + 1024 /* 1 KiB alignment slack */ + 256;
+constexpr int kTopMaxW = 8;                              // head epilogue: longest top list
+
+enum EpiKind : int {
+  EPI_F32 = 0,      // out32[r, c] = acc + bias                      (tests, partials)
+  EPI_F16 = 1,      // out16[r, c] = fp16(acc + bias)
+  EPI_GELU16 = 2,   // out16[r, c] = fp16(gelu(acc + bias))
+  EPI_PART = 3,     // part[split][r, c] = acc                       (split-K residual GEMMs)
+  EPI_EULER = 4,    // z[b, start + r % chunk, c] += dt * (acc + bias), b = r / chunk
+  EPI_PATH = 5,     // out32[r, c] = acc + sum_{j < nlive, lastp[r][j] >= 0} pbias[j, c]
+  EPI_HEADIN = 6,   // out16[r, c] = fp16(acc + bias + pred[r / beams, step, c])
+  EPI_HEAD = 7      // per (row, tile): online (max, sum exp) and top-`topb` (value, id)
+};
+
+struct GemmProb {
+  CUtensorMap ta;                 // A [M, K]: box 64 × 128
+  CUtensorMap tw;                 // W [N, K]: box 64 × 128
+  int M, N, kblocks;              // kblocks = K / 64 actually multiplied
+  int m_tiles, n_tiles, splits, kb_per_split;
+  int cta0;                       // first CTA of this problem in the grouped launch
+  int epi;
+  const float* bias;              // [N] or null
+  void* out;                      // epilogue target (see EpiKind)
+  long long ldo;                  // row stride of `out` in elements
+  long long split_stride;         // EPI_PART: elements between two splits' partials
+  // EPI_EULER
+  float dt; int chunk, zrows, zstart;
+  // EPI_PATH
+  const int64_t* lastp; int order, nlive; const float* pbias;
+  // EPI_HEADIN
+  const float* pred; int beams, pred_rows, step;
+  // EPI_HEAD
+  int topb, rowoff;
+};
+
+constexpr int kMaxProbs = 8;
+struct GemmLaunch {
+  GemmProb p[kMaxProbs];
+  int nprob;
+  int* err;                       // sticky device error word
+};
+static_assert(sizeof(GemmLaunch) <= 4000, "kernel parameter space");
+
+// ---- PTX wrappers: TMA, tcgen05 ---------------------------------------------------------------
+CFB_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+CFB_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+CFB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CFB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// whole warp; writes the allocated TMEM address to *slot
+CFB_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+CFB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[smem] · B[smem]ᵀ, kind::f16 (fp16 × fp16 -> fp32)
+CFB_DEV void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on `bar` once every tcgen05 op this thread issued before has completed
+CFB_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(bar)) : "memory");
+}
+// 32 lanes × 16 consecutive fp32 columns of TMEM (lane = row of the accumulator)
+CFB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the 128-byte swizzle:
+// 128-byte rows, 8-row groups 1024 bytes apart (SBO), leading offset unused (1), version 1,
+// layout SWIZZLE_128B (2). The tile base must be 1024-byte aligned; stepping K by 16 elements
+// inside the 64-element swizzle row adds 32 bytes to the start address.
+CFB_DEV uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+CFB_DEV bool better_w(float v, int i, float w, int j) { return v > w || (v == w && i < j); }
+
+}  // namespace wide
+}  // namespace cfb

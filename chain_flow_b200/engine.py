@@ -135,3 +135,69 @@ class Plan:
         err = self.device_error()
         if err:
             raise _lib.CfbError(f"device-side wait timed out (code {err}); outputs are invalid")
+
+
+class WidePlan:
+    """The wide (batched) plan over WideWeights: same inputs and outputs as ``Plan`` (ctx, z0,
+    known0 -> pred, tokens), run as a fixed list of tcgen05 GEMM and row-kernel launches on one
+    stream (capturable in a CUDA graph). For batches above what one persistent launch holds."""
+
+    def __init__(self, w, mode: int, batch: int, *, width: int = 4, depth: int = 5, tree_keep: int = 4,
+                 tree_topb: int = 8, init_mode: int = 0):
+        self.w, self.mode, self.batch = w, mode, batch
+        cfg, dev = w.cfg, w.dev
+        D = cfg.hidden
+        self.lib = w.lib
+        self.ctx = torch.zeros(batch, cfg.context_size, D, dtype=torch.float16, device=dev)
+        self.z0 = torch.zeros(batch, cfg.draft_length, D, dtype=torch.float16, device=dev)
+        self.known0 = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.pred = torch.zeros(batch, cfg.draft_length, D, dtype=torch.float32, device=dev)
+        self.tree = mode in (_lib.MODE_TREE, _lib.MODE_BEAM_TREE)
+        if self.tree:
+            depth = min(depth, cfg.draft_length - 1)
+            self.levels = tree_levels(tree_keep, tree_topb, depth)
+            self.N = sum(self.levels)
+            self.tokens = torch.zeros(batch, 2 * self.N, dtype=torch.int64, device=dev)
+        else:
+            self.N = depth
+            self.tokens = torch.zeros(batch, depth, dtype=torch.int64, device=dev)
+        r = _lib.Run()
+        r.mode, r.batch, r.width, r.depth = mode, batch, width, depth
+        r.init_mode = init_mode
+        r.tree_keep, r.tree_topb = tree_keep, tree_topb
+        r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
+        r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
+        self.run_desc = r
+        nbytes = C.c_size_t(0)
+        _lib.check(self.lib.cfb_wide_workspace(C.byref(w.desc), C.byref(r), C.byref(nbytes)), "cfb_wide_workspace")
+        self.ws = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=dev)
+        self.ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        h = C.c_void_p()
+        _lib.check(self.lib.cfb_wide_create(C.byref(w.desc), C.byref(r), C.c_void_p(self.ws_ptr),
+                                            C.c_size_t(int(nbytes.value)), C.byref(h)), "cfb_wide_create")
+        self._h = h
+        n = C.c_int()
+        _lib.check(self.lib.cfb_wide_info(h, C.byref(n)), "cfb_wide_info")
+        self.launches = n.value
+        self.segments = 1
+
+    def run(self, stream=None, group=None) -> None:
+        if group is not None and self.w is not None and getattr(self.w, "head_ranks", 1) > 1:
+            raise _lib.CfbError("the wide plan has no row-sharded head")
+        _lib.check(self.lib.cfb_wide_run(self._h, C.c_void_p(_lib.stream_ptr(stream))), "cfb_wide_run")
+
+    def device_error(self) -> int:
+        v = C.c_int(0)
+        _lib.check(self.lib.cfb_wide_error(self._h, C.byref(v)), "cfb_wide_error")
+        return v.value
+
+    def check(self) -> None:
+        err = self.device_error()
+        if err:
+            raise _lib.CfbError(f"device-side wait timed out (code {err}); outputs are invalid")
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            self.lib.cfb_wide_destroy(h)
+            self._h = None

@@ -220,3 +220,110 @@ class DrafterWeights:
     @property
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in self._keep) + self.embed.numel() * 2
+
+
+class WideWeights:
+    """The drafter's weights for the wide (batched, tcgen05) plan: every Linear as a row-major fp16
+    [nout, k] matrix with the LayerNorm that feeds it folded in (w = fp16(W16 * gamma),
+    bias = b + W16 beta, the same folding as the persistent engine's packing), the time MLP
+    evaluated at every Euler step, the path offsets side by side as [D, order * D], and the
+    shortlist head [lm_head[sl] | markov.w2[sl]] as one [R, D + rank] matrix."""
+
+    def __init__(self, sd: dict, cfg: DraftConfig, embed: torch.Tensor, lm_head: torch.Tensor,
+                 shortlist: torch.Tensor, device=None):
+        self.lib = _lib.load()
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if dev.type != "cuda":
+            raise _lib.CfbError("WideWeights needs a CUDA device: the wide path has no CPU path")
+        self.dev, self.cfg = dev, cfg
+        D = cfg.hidden
+        if D % 64 or cfg.draft_length % cfg.chunk_size:
+            raise _lib.CfbError(f"unsupported drafter shape: hidden={D} must be a multiple of 64")
+        self._keep = []
+        stream = torch.cuda.current_stream(dev)
+        f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
+        f16 = lambda t: t.to(device=dev, dtype=torch.float16).contiguous()
+
+        def linear(w, b, ln=None):
+            w16 = f16(w)
+            bias = f32(b) if b is not None else torch.zeros(w16.shape[0], device=dev)
+            if ln is not None:
+                g, beta = f32(ln[0]), f32(ln[1])
+                bias = bias + w16.float() @ beta
+                w16 = (w16.float() * g).to(torch.float16).contiguous()
+            bias = bias.contiguous()
+            self._keep += [w16, bias]
+            return _lib.Linear(w16.data_ptr(), bias.data_ptr(), None, w16.shape[0], w16.shape[1])
+
+        self.embed = f16(embed)
+        self.vocab = self.embed.shape[0]
+        sl = shortlist.to(device=dev, dtype=torch.int64).contiguous()
+        self.shortlist = sl
+        R, rank = sl.numel(), cfg.markov_rank
+        self.experts = (_lib.Expert * cfg.n_experts)()
+        self._blocks = []
+        for e in range(cfg.n_experts):
+            p = expert_prefix(e)
+            blocks = (_lib.Block * cfg.num_drafter_layers)()
+            for l in range(cfg.num_drafter_layers):
+                b = f"{p}blocks.{l}."
+                cw, cb = sd[b + "cross_attn.in_proj_weight"], sd[b + "cross_attn.in_proj_bias"]
+                blocks[l].qkv = linear(sd[b + "self_attn.in_proj_weight"], sd[b + "self_attn.in_proj_bias"],
+                                       ln=(sd[b + "self_norm.weight"], sd[b + "self_norm.bias"]))
+                blocks[l].self_out = linear(sd[b + "self_attn.out_proj.weight"], sd[b + "self_attn.out_proj.bias"])
+                blocks[l].cross_q = linear(cw[:D], cb[:D], ln=(sd[b + "cross_norm.weight"], sd[b + "cross_norm.bias"]))
+                blocks[l].cross_kv = linear(cw[D:], cb[D:], ln=(sd[b + "context_norm.weight"], sd[b + "context_norm.bias"]))
+                blocks[l].cross_out = linear(sd[b + "cross_attn.out_proj.weight"], sd[b + "cross_attn.out_proj.bias"])
+                blocks[l].ffn_up = linear(sd[b + "ffn.1.weight"], sd[b + "ffn.1.bias"],
+                                          ln=(sd[b + "ffn.0.weight"], sd[b + "ffn.0.bias"]))
+                blocks[l].ffn_down = linear(sd[b + "ffn.4.weight"], sd[b + "ffn.4.bias"])
+            self._blocks.append(blocks)
+            ex = self.experts[e]
+            pos = f32(sd[p + "position_embedding.weight"])
+            temb = torch.empty(cfg.num_flow_steps, D, device=dev, dtype=torch.float32)
+            w1t, b1t = f32(sd[p + "time_mlp.0.weight"][:, 0]), f32(sd[p + "time_mlp.0.bias"])
+            w2t, b2t = f16(sd[p + "time_mlp.2.weight"]), f32(sd[p + "time_mlp.2.bias"])
+            _lib.check(self.lib.cfb_time_embed(w1t.data_ptr(), b1t.data_ptr(), w2t.data_ptr(), b2t.data_ptr(),
+                                               D, cfg.num_flow_steps, temb.data_ptr(), stream.cuda_stream),
+                       "cfb_time_embed")
+            self._keep += [pos, temb, w1t, b1t, w2t, b2t]
+            ex.pos_emb, ex.temb = pos.data_ptr(), temb.data_ptr()
+            ex.out_proj = linear(sd[p + "out_proj.weight"], sd[p + "out_proj.bias"],
+                                 ln=(sd[p + "out_norm.weight"], sd[p + "out_norm.bias"]))
+            ex.blocks = C.cast(blocks, C.POINTER(_lib.Block))
+        order = cfg.path_order
+        po = torch.cat([f16(sd[f"path_head.offset_proj.{j}.weight"]) for j in range(order)], dim=1).contiguous()
+        pb = torch.stack([f32(sd[f"path_head.offset_proj.{j}.bias"]) for j in range(order)]).contiguous()
+        self._keep += [po, pb]
+        self.path_offsets = _lib.Linear(po.data_ptr(), None, None, D, order * D)
+        self.path_up = linear(sd["path_head.mlp.0.weight"], sd["path_head.mlp.0.bias"],
+                              ln=(sd["path_head.norm.weight"], sd["path_head.norm.bias"]))
+        self.path_down = linear(sd["path_head.mlp.3.weight"], sd["path_head.mlp.3.bias"])
+        self.markov_w1 = f16(sd["markov.w1.weight"])
+        rows = sl.to(lm_head.device)
+        kh = (D + rank + 63) // 64 * 64          # zero columns pad the head's K to a multiple of 64
+        head = torch.zeros(R, kh, dtype=torch.float16, device=dev)
+        head[:, :D] = lm_head[rows].to(device=dev, dtype=torch.float16)
+        head[:, D:D + rank] = f16(sd["markov.w2.weight"])[sl]
+        self._keep += [self.markov_w1, head]
+        self.head = _lib.Linear(head.data_ptr(), None, None, R, kh)
+        self.R = R
+        d = _lib.Drafter()
+        d.hidden, d.heads, d.layers, d.steps = D, cfg.num_heads, cfg.num_drafter_layers, cfg.num_flow_steps
+        d.draft_len, d.chunk, d.ctx_rows, d.n_experts = cfg.draft_length, cfg.chunk_size, cfg.context_size, cfg.n_experts
+        d.experts = C.cast(self.experts, C.POINTER(_lib.Expert))
+        d.path_order, d.markov_rank, d.vocab, d.shortlist_rows = order, rank, self.vocab, R
+        d.embed = self.embed.data_ptr()
+        d.path_offsets = self.path_offsets
+        d.path_offset_bias = pb.data_ptr()
+        d.path_up, d.path_down = self.path_up, self.path_down
+        d.markov_w1 = self.markov_w1.data_ptr()
+        d.head = self.head
+        d.shortlist = sl.data_ptr()
+        d.head_row0 = 0
+        self.desc = d
+        torch.cuda.synchronize(dev)
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self._keep) + self.embed.numel() * 2

@@ -252,6 +252,48 @@ cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, con
                                 float* o, int B, int N, int H, int Dk, int Dv, int use_l2norm,
                                 void* stream);
 
+/* ---- the wide (batched) drafting path ------------------------------------------------------
+ * C = A · Wᵀ on the sm_100a tensor cores (tcgen05.mma, fp16 in, fp32 accumulate in TMEM), fed by
+ * 2-D TMA copies: the GEMM of the wide path, exported on its own for tests and for callers that
+ * batch their own rows. This entry point has no counterpart in the reference.
+ * a fp16 [M, K] with row stride lda; w fp16 [N, K] with row stride ldw; bias fp32 [N] or NULL.
+ * epi: CFB_EPI_F32    out fp32 [M, ldo] = A·Wᵀ + bias
+ *      CFB_EPI_F16    out fp16 [M, ldo] = fp16(A·Wᵀ + bias)
+ *      CFB_EPI_GELU16 out fp16 [M, ldo] = fp16(gelu(A·Wᵀ + bias))   (exact erf GELU)
+ *      CFB_EPI_PART   out fp32 [s][M, ldo]: split-K partials (bias ignored); s = ceil(K/64 /
+ *                     ceil(K/64 / splits)) splits, each over a contiguous range of 64-column blocks.
+ * Supported: K a multiple of 64, N a multiple of 16, a/w/out/bias 16-byte aligned, lda and ldw
+ * multiples of 8, ldo a multiple of 4. err: a device int that becomes non-zero if a bounded
+ * device-side wait expired (outputs then invalid); it is never cleared by the library. */
+enum { CFB_EPI_F32 = 0, CFB_EPI_F16 = 1, CFB_EPI_GELU16 = 2, CFB_EPI_PART = 3 };
+cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias,
+                         void* out, int64_t ldo, int M, int N, int K, int epi, int splits, int* err,
+                         void* stream);
+
+/* The wide plan: a draft of many requests at once (the batch-throughput shape) as a fixed list
+ * of kernel launches: tcgen05 GEMMs for every Linear (grouped over the chunk experts, split-K for
+ * the residual projections), and row kernels for LayerNorm + residual updates, attention, the
+ * path-token gather and the beam step. Same drafter description and run description as the
+ * persistent plan, except that every cfb_linear.w is a ROW-MAJOR fp16 [nout, k] matrix (row
+ * stride k) with the LayerNorm in front of it folded in (w = fp16(W * gamma), bias = b + W beta);
+ * cfb_linear.colsum is unused. path_offsets is [D, order * D] (column block j = offset_proj.j),
+ * head is [R, Kh] = [lm_head[sl] | markov.w2[sl] | 0], Kh >= D + markov_rank a multiple of 64
+ * (zero columns pad it). Modes and outputs are those of
+ * cfb_run; the row-sharded head (ranks > 1) is not supported here. The library keeps the launch
+ * list in host memory (cfb_wide_destroy frees it); all device memory is the caller's workspace.
+ * cfb_wide_run only enqueues kernels on `stream` (capturable in a CUDA graph).
+ * These entry points have no counterpart in the reference, whose batched drafts run its
+ * per-layer PyTorch modules (reference cuda_block.py:382-431 for the fused expert). */
+typedef struct cfb_wide_plan cfb_wide_plan;
+cfb_status cfb_wide_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes);
+cfb_status cfb_wide_create(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes,
+                           cfb_wide_plan** plan);
+cfb_status cfb_wide_run(cfb_wide_plan* plan, void* stream);
+/* synchronous read of the sticky device error word (0 = every run so far completed) */
+cfb_status cfb_wide_error(cfb_wide_plan* plan, int* device_error);
+cfb_status cfb_wide_info(cfb_wide_plan* plan, int* launches);
+void cfb_wide_destroy(cfb_wide_plan* plan);
+
 #ifdef __cplusplus
 }
 #endif
