@@ -6,7 +6,8 @@
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 A step is one 5-token chain draft (flow integrator + shortlist head + top-4 beam) of B
-independent requests per GPU, as one persistent kernel launch. Requests are partitioned across
+independent requests per GPU: one persistent kernel launch up to 8 requests, above that the wide
+plan (tcgen05 GEMMs over the whole batch plus row kernels). Requests are partitioned across
 GPUs with no collective on the data path (weak scaling). The timed region holds inputs already
 resident in HBM; the drafter's weights (2.6 GB at the 4B shape) exceed the 126 MB L2, so every
 step streams them from HBM. `e2e` repeats the measurement through the proposer API with host
@@ -60,6 +61,17 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d.get("hbm_gbs", 6650.0)), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense fp16/bf16 tensor peak in TFLOP/s: the sustained cuBLAS figure (the wide plan is timed
+    over a multi-millisecond step under the power cap)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured (sustained)"
+    return 1400.0, "fallback (sustained)"
 
 
 class ClockSampler:
@@ -282,10 +294,13 @@ def run_ours(args, wl):
     if prop.device_error():
         raise SystemExit(f"device-side wait timed out (code {prop.device_error()})")
 
-    # ---- the engine kernel alone (roofline): back-to-back launches of the bound plan (batches
-    # above one plan's capacity run as several plans; the roofline is that of one plan)
+    # ---- the plan alone (roofline): back-to-back runs of the bound plan. Up to MAX_PLAN_BATCH
+    # requests that is one persistent-engine launch; above it, the wide plan's launch list
+    # (tcgen05 GEMMs and row kernels); a sharded head runs engine plans of MAX_PLAN_BATCH.
     from chain_flow_b200.proposer import MAX_PLAN_BATCH
-    plan = prop._plan(_lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH))
+    wide = B > MAX_PLAN_BATCH and not shard
+    plan = prop._wide_plan(_lib.MODE_CHAIN, B) if wide else prop._plan(_lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH))
+    plans_per_step = 1 if wide else (B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH
     torch.cuda.synchronize(dev)
     k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k0.record(stream)
@@ -328,6 +343,9 @@ def run_ours(args, wl):
         peak, peak_kind = measured_peaks()
         algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0)   # per GPU, per plan
         achieved = algo / (kernel_ms / 1e3) / 1e9
+        flops = wl.flops_per_draft(B if wide else min(B, MAX_PLAN_BATCH))
+        tpeak, tpeak_kind = measured_tensor_peak()
+        tensor_bound = wide and flops / (tpeak * 1e12) > algo / (peak * 1e9)
         traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "engine_dram_traffic.json"
         if tf.exists():
@@ -344,20 +362,29 @@ def run_ours(args, wl):
             "config": {"workload": wl.name, "batch_per_gpu": B, "draft_tokens": wl.draft_tokens,
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
-                       "beam_width": wl.width, "plans_per_step": (B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH,
+                       "beam_width": wl.width, "plans_per_step": plans_per_step,
+                       "path": ("wide plan: tcgen05 GEMMs + row kernels, one launch list per step" if wide
+                                else "persistent engine: one cooperative launch per plan"),
                        "parallelism": (f"shortlist head rows sharded over {world} GPUs, flow replicated, "
                                        f"one NCCL all_gather of merged top-k lists per depth") if shard
                        else f"requests split over {world} GPU(s)",
-                       "l2": f"inputs larger than L2: {prop.weights.packed_bytes / 1e9:.2f} GB of packed "
-                             f"weights stream from HBM every step"},
+                       "l2": f"inputs larger than L2: {algo / 1e9:.2f} GB of fp16 weights stream from HBM "
+                             f"every step"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * plan.segments * ((B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_note,
-                         "peak_source": peak_kind,
-                         "kernel": "engine_kernel", "kernel_ms": kernel_ms,
-                         "algorithmic_bytes_per_launch": algo},
+            "gpu_launches": args.steps * (plan.launches if wide else plan.segments * plans_per_step),
+            "roofline": ({"bound": "tensor", "achieved": flops / (kernel_ms / 1e3) / 1e12, "peak": tpeak,
+                          "unit": "TFLOP/s", "frac": flops / (kernel_ms / 1e3) / 1e12 / tpeak, "traffic": None,
+                          "peak_source": tpeak_kind, "kernel": "wide plan (all launches; tcgen05 GEMMs dominate)",
+                          "kernel_ms": kernel_ms, "algorithmic_flops_per_step": flops,
+                          "hbm_gbs": achieved} if tensor_bound else
+                         {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "traffic": traffic if not wide else None,
+                          "traffic_source": traffic_note if not wide else None,
+                          "peak_source": peak_kind,
+                          "kernel": "wide plan (all launches; tcgen05 GEMMs dominate)" if wide else "engine_kernel",
+                          "kernel_ms": kernel_ms, "algorithmic_bytes_per_launch": algo,
+                          "tflops": flops / (kernel_ms / 1e3) / 1e12}),
             "clocks": clk,
             "cpu_baseline": cpu,
         }

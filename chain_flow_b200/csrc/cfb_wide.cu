@@ -207,6 +207,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
         for (int q = 0; q < kTopMaxW; ++q)
           if (q < P.topb) { o[2 + q] = tv[q]; o[2 + P.topb + q] = __int_as_float(ti[q]); }
       }
+    } else if (P.splits > 1 && P.epi != EPI_PART) {
+      const int tile = mt + P.m_tiles * nt;
+      const int rl = lg * 32 + lane;
+      float* mine = P.fix_ws + (((long long)tile * P.splits + sp) * BM + rl) * BN;
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tb + c0, v);
+        float4* o4 = reinterpret_cast<float4*>(mine + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+      consumer_sync(4 * 32);
+      volatile int* s_last = sflag + 1;
+      if (threadIdx.x == 2 * 32) {
+        __threadfence();
+        const int prev = atomicAdd(P.fix_cnt + tile, 1);
+        const int last = prev == P.splits - 1;
+        if (last) { P.fix_cnt[tile] = 0; __threadfence(); }
+        *s_last = last;
+      }
+      consumer_sync(4 * 32);
+      if (*s_last && live) {
+        const float* base = P.fix_ws + ((long long)tile * P.splits * BM + rl) * BN;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          const int col = nt * BN + c0;
+          if (col >= P.N) break;
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          for (int q = 0; q < P.splits; ++q) {
+            const float4* src = reinterpret_cast<const float4*>(base + (long long)q * BM * BN + c0);
+#pragma unroll
+            for (int z = 0; z < 4; ++z) {
+              const float4 t4 = __ldcg(src + z);
+              v[4 * z] += t4.x; v[4 * z + 1] += t4.y; v[4 * z + 2] += t4.z; v[4 * z + 3] += t4.w;
+            }
+          }
+          epi_slice(P, sp, row, col, v);
+        }
+      }
     } else {
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
@@ -334,25 +374,33 @@ struct LnSeg {
 constexpr int kMaxLnSegs = 4;
 struct LnLaunch { LnSeg s[kMaxLnSegs]; int nseg, D, rows; };
 
-// One warp per row; the row lives in registers (VPL float4 per lane) between the passes:
-// residual update, mean, centred variance, normalised fp16 output (nn.LayerNorm without its
-// affine part, which is folded into the next Linear).
-template <int VPL>
-__global__ void __launch_bounds__(256) wide_ln_kernel(const __grid_constant__ LnLaunch L) {
+// One CTA (128 threads) per row; the row lives in registers (up to kLnMaxV float4 per thread)
+// between the passes: residual update (bias + every split-K partial, loads all in flight),
+// mean, centred variance, normalised fp16 output (nn.LayerNorm without its affine part, which
+// is folded into the next Linear).
+constexpr int kLnThreads = 128, kLnMaxV = 10, kLnMaxSplit = 8;
+__device__ __forceinline__ float ln_block_sum(float v, float* red) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gr = blockIdx.x * 8 + warp;
-  if (gr >= L.rows) return;
+  __syncthreads();                                    // red[] free from a previous use
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+__global__ void __launch_bounds__(kLnThreads) wide_ln_kernel(const __grid_constant__ LnLaunch L) {
+  __shared__ float red[kLnThreads / 32];
+  const int gr = blockIdx.x;
   int si = 0;
   while (si + 1 < L.nseg && gr >= L.s[si + 1].row0) ++si;
   const LnSeg& S = L.s[si];
   const int r = gr - S.row0;
   const int D = L.D;
-  float4 x[VPL];
-  float sum = 0.f;
   const int b = S.S > 0 ? r / S.S : 0, i = S.S > 0 ? r - b * S.S : 0;
+  float4 x[kLnMaxV];
+  float sum = 0.f;
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    const int c = (v * 32 + lane) * 4;
+  for (int v = 0; v < kLnMaxV; ++v) {
+    const int c = (v * kLnThreads + threadIdx.x) * 4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     if (c < D) {
       if (S.mode == LN_PREP) {
@@ -363,18 +411,16 @@ __global__ void __launch_bounds__(256) wide_ln_kernel(const __grid_constant__ Ln
           const float4 t = *reinterpret_cast<const float4*>(S.temb + c);
           a.x += t.x; a.y += t.y; a.z += t.z; a.w += t.w;
         }
-        *reinterpret_cast<float4*>(S.x32 + (long long)r * D + c) = a;
       } else if (S.mode == LN_RESID) {
-        float4* xp = reinterpret_cast<float4*>(S.x32 + (long long)r * D + c);
-        a = *xp;
-        const float4 bb = *reinterpret_cast<const float4*>(S.bias + c);
-        float4 acc = bb;
-        for (int sp = 0; sp < S.nsplit; ++sp) {
-          const float4 q = *reinterpret_cast<const float4*>(S.part + sp * S.split_stride + (long long)r * D + c);
-          acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
-        }
+        a = *reinterpret_cast<const float4*>(S.x32 + (long long)r * D + c);
+        float4 acc = *reinterpret_cast<const float4*>(S.bias + c);
+#pragma unroll
+        for (int sp = 0; sp < kLnMaxSplit; ++sp)
+          if (sp < S.nsplit) {
+            const float4 q = *reinterpret_cast<const float4*>(S.part + sp * S.split_stride + (long long)r * D + c);
+            acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+          }
         a.x += acc.x; a.y += acc.y; a.z += acc.z; a.w += acc.w;
-        *xp = a;
       } else if (S.mode == LN_PLAIN32) {
         a = *reinterpret_cast<const float4*>(S.x32 + (long long)r * D + c);
       } else {
@@ -382,28 +428,27 @@ __global__ void __launch_bounds__(256) wide_ln_kernel(const __grid_constant__ Ln
         const float2 lo = unpack_half2(h.x), hi = unpack_half2(h.y);
         a = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
+      if (S.mode == LN_PREP || S.mode == LN_RESID) *reinterpret_cast<float4*>(S.x32 + (long long)r * D + c) = a;
     }
     x[v] = a;
     sum += (a.x + a.y) + (a.z + a.w);
   }
-  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  const float mean = sum / (float)D;
+  const float mean = ln_block_sum(sum, red) / (float)D;
   float var = 0.f;
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    const int c = (v * 32 + lane) * 4;
+  for (int v = 0; v < kLnMaxV; ++v) {
+    const int c = (v * kLnThreads + threadIdx.x) * 4;
     if (c < D) {
       const float dx = x[v].x - mean, dy = x[v].y - mean, dz = x[v].z - mean, dw = x[v].w - mean;
       var += (dx * dx + dy * dy) + (dz * dz + dw * dw);
     }
   }
-  for (int off = 16; off > 0; off >>= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
-  const float rstd = rsqrtf(var / (float)D + kLnEps);
+  const float rstd = rsqrtf(ln_block_sum(var, red) / (float)D + kLnEps);
   if (S.cur_only && i < S.start) return;
   const long long orow = S.cur_only ? (long long)b * S.chunk + (i - S.start) : r;
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) {
-    const int c = (v * 32 + lane) * 4;
+  for (int v = 0; v < kLnMaxV; ++v) {
+    const int c = (v * kLnThreads + threadIdx.x) * 4;
     if (c < D)
       *reinterpret_cast<uint2*>(S.out + orow * D + c) =
           make_uint2(pack_half2((x[v].x - mean) * rstd, (x[v].y - mean) * rstd),
@@ -411,63 +456,102 @@ __global__ void __launch_bounds__(256) wide_ln_kernel(const __grid_constant__ Ln
   }
 }
 
-// ---- attention: one CTA per (request, head, segment) ---------------------------------------------
+// ---- attention: one CTA (4 warps) per (request, head, segment), one warp per query row -------------
+// Lane l holds head-dimension chunks c = l + 32 t (8 halves each) of q, and of each key / value
+// row as it streams past; the scores of the (at most kAttnMaxKeys) keys stay in registers.
+constexpr int kAttnMaxKeys = 16, kAttnMaxChunks = 4;     // head dim <= 32 * 4 * 8 = 1024
 struct AttnSeg {
   const __half* q; long long ldq; int qoff;
   const __half* k; const __half* v; long long ldkv; int koff, voff;
   int S, SK, causal;
   __half* out; long long ldo;
 };
-struct AttnLaunch { AttnSeg s[kMaxLnSegs]; int nseg, H, hd, maxS, maxSK; float scale; };
+struct AttnLaunch { AttnSeg s[kMaxLnSegs]; int nseg, H, hd; float scale; };
+
+__device__ __forceinline__ void h8_to_f(const uint4& u, float (&f)[8]) {
+  const float2 a = unpack_half2(u.x), b = unpack_half2(u.y), c = unpack_half2(u.z), d = unpack_half2(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
 
 __global__ void __launch_bounds__(128) wide_attn_kernel(const __grid_constant__ AttnLaunch L) {
-  extern __shared__ float asm_[];
   const AttnSeg& A = L.s[blockIdx.y];
-  const int b = blockIdx.x / L.H, h = blockIdx.x % L.H, hd = L.hd;
-  const int S = A.S, SK = A.SK;
-  float* qs = asm_;                         // [S][hd]
-  float* ks = qs + L.maxS * hd;             // [SK][hd]
-  float* vs = ks + L.maxSK * hd;            // [SK][hd]
-  float* ps = vs + L.maxSK * hd;            // [S][SK]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int e = tid; e < S * hd; e += blockDim.x) {
-    const int i = e / hd, d = e - i * hd;
-    qs[e] = __half2float(A.q[((long long)b * S + i) * A.ldq + A.qoff + h * hd + d]);
-  }
-  for (int e = tid; e < SK * hd; e += blockDim.x) {
-    const int j = e / hd, d = e - j * hd;
-    const long long row = ((long long)b * SK + j) * A.ldkv + h * hd + d;
-    ks[e] = __half2float(A.k[row + A.koff]);
-    vs[e] = __half2float(A.v[row + A.voff]);
-  }
-  __syncthreads();
-  for (int pidx = warp; pidx < S * SK; pidx += blockDim.x >> 5) {
-    const int i = pidx / SK, j = pidx - i * SK;
-    float acc = 0.f;
-    if (!(A.causal && j > i))
-      for (int d = lane; d < hd; d += 32) acc += qs[i * hd + d] * ks[j * hd + d];
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) ps[pidx] = (A.causal && j > i) ? -INFINITY : acc * L.scale;
-  }
-  __syncthreads();
-  if (tid < S) {
-    float m = -INFINITY;
-    for (int j = 0; j < SK; ++j) m = fmaxf(m, ps[tid * SK + j]);
-    float sum = 0.f;
-    for (int j = 0; j < SK; ++j) {
-      const float e = ps[tid * SK + j] == -INFINITY ? 0.f : expf(ps[tid * SK + j] - m);
-      ps[tid * SK + j] = e;
-      sum += e;
+  const int b = blockIdx.x / L.H, h = blockIdx.x % L.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = L.hd / 8;
+  for (int i = warp; i < A.S; i += 4) {
+    float q[kAttnMaxChunks][8];
+    const __half* qrow = A.q + ((long long)b * A.S + i) * A.ldq + A.qoff + h * L.hd;
+#pragma unroll
+    for (int t = 0; t < kAttnMaxChunks; ++t) {
+      const int c = lane + 32 * t;
+      if (c < nch) h8_to_f(*reinterpret_cast<const uint4*>(qrow + c * 8), q[t]);
+      else {
+#pragma unroll
+        for (int z = 0; z < 8; ++z) q[t][z] = 0.f;
+      }
     }
-    const float inv = 1.f / sum;
-    for (int j = 0; j < SK; ++j) ps[tid * SK + j] *= inv;
-  }
-  __syncthreads();
-  for (int e = tid; e < S * hd; e += blockDim.x) {
-    const int i = e / hd, d = e - i * hd;
-    float acc = 0.f;
-    for (int j = 0; j < SK; ++j) acc += ps[i * SK + j] * vs[j * hd + d];
-    A.out[((long long)b * S + i) * A.ldo + h * hd + d] = __float2half_rn(acc);
+    const int nk = A.causal ? min(i + 1, A.SK) : A.SK;
+    float sc[kAttnMaxKeys];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kAttnMaxKeys; ++j) {
+      sc[j] = -INFINITY;
+      if (j < nk) {
+        const __half* krow = A.k + ((long long)b * A.SK + j) * A.ldkv + A.koff + h * L.hd;
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < kAttnMaxChunks; ++t) {
+          const int c = lane + 32 * t;
+          if (c < nch) {
+            float kf[8];
+            h8_to_f(*reinterpret_cast<const uint4*>(krow + c * 8), kf);
+#pragma unroll
+            for (int z = 0; z < 8; ++z) acc += q[t][z] * kf[z];
+          }
+        }
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        sc[j] = acc * L.scale;
+        m = fmaxf(m, sc[j]);
+      }
+    }
+    float den = 0.f;
+#pragma unroll
+    for (int j = 0; j < kAttnMaxKeys; ++j) {
+      sc[j] = j < nk ? expf(sc[j] - m) : 0.f;
+      den += sc[j];
+    }
+    const float inv = 1.f / den;
+    float o[kAttnMaxChunks][8];
+#pragma unroll
+    for (int t = 0; t < kAttnMaxChunks; ++t)
+#pragma unroll
+      for (int z = 0; z < 8; ++z) o[t][z] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kAttnMaxKeys; ++j) {
+      if (j < nk) {
+        const __half* vrow = A.v + ((long long)b * A.SK + j) * A.ldkv + A.voff + h * L.hd;
+        const float p = sc[j] * inv;
+#pragma unroll
+        for (int t = 0; t < kAttnMaxChunks; ++t) {
+          const int c = lane + 32 * t;
+          if (c < nch) {
+            float vf[8];
+            h8_to_f(*reinterpret_cast<const uint4*>(vrow + c * 8), vf);
+#pragma unroll
+            for (int z = 0; z < 8; ++z) o[t][z] += p * vf[z];
+          }
+        }
+      }
+    }
+    __half* orow = A.out + ((long long)b * A.S + i) * A.ldo + h * L.hd;
+#pragma unroll
+    for (int t = 0; t < kAttnMaxChunks; ++t) {
+      const int c = lane + 32 * t;
+      if (c < nch)
+        *reinterpret_cast<uint4*>(orow + c * 8) =
+            make_uint4(pack_half2(o[t][0], o[t][1]), pack_half2(o[t][2], o[t][3]), pack_half2(o[t][4], o[t][5]),
+                       pack_half2(o[t][6], o[t][7]));
+    }
   }
 }
 
@@ -668,10 +752,6 @@ extern "C" cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, i
 // The wide plan: the whole draft as a fixed list of launches over caller-owned buffers.
 namespace {
 
-template <int VPL>
-void ln_launch(const LnLaunch& L, cudaStream_t st) {
-  wide_ln_kernel<VPL><<<(L.rows + 7) / 8, 256, 0, st>>>(L);
-}
 
 struct Bump {
   char* base;
@@ -688,16 +768,13 @@ struct Bump {
 enum StepKind { S_INIT, S_HEADINIT, S_LN, S_GEMM, S_ATTN, S_GATHER, S_BEAM };
 struct Step { int kind, idx; };
 
-// residual GEMMs: the split count that minimises waves x (k blocks per split + a fixed cost)
+// Split-K only for launches with fewer output tiles than SMs: a split of at least 4 k blocks,
+// at most 8 splits, and no more CTAs than SMs (one resident CTA per SM).
 int choose_splits(int tiles, int kblocks, int nsm) {
-  int best = 1;
-  long long bestc = -1;
-  for (int s = 1; s <= std::min(8, kblocks); ++s) {
-    const long long waves = ((long long)tiles * s + nsm - 1) / nsm;
-    const long long c = waves * ((kblocks + s - 1) / s + 4);
-    if (bestc < 0 || c < bestc) { bestc = c; best = s; }
-  }
-  return best;
+  if (tiles >= nsm) return 1;
+  int s = std::max(1, nsm / tiles);
+  s = std::min(s, std::max(1, kblocks / 4));
+  return std::min(s, 8);
 }
 
 }  // namespace
@@ -705,7 +782,6 @@ int choose_splits(int tiles, int kblocks, int nsm) {
 struct cfb_wide_plan {
   int dev = 0, nsm = 148;
   int* err = nullptr;
-  int vpl = 0;                 // LayerNorm register bucket (float4 per lane)
   std::vector<Step> steps;
   std::vector<GemmLaunch> gemms;
   std::vector<LnLaunch> lns;
@@ -714,7 +790,9 @@ struct cfb_wide_plan {
   std::vector<BeamArgs> beams;
   InitArgs init{};
   HeadInitArgs hinit{};
-  int batch = 0, attn_smem = 0, head_rows = 0;
+  int batch = 0, head_rows = 0;
+  int* fix_cnt = nullptr;      // split-K arrival counters: zero between launches
+  size_t fix_cnt_bytes = 0;
   __half* hin = nullptr;       // head input: its padding columns stay zero
   size_t hin_bytes = 0;
   int kernel_launches = 0;
@@ -732,7 +810,8 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   const bool head = r->mode != CFB_MODE_FLOW;
   if (r->mode < CFB_MODE_FLOW || r->mode > CFB_MODE_BEAM_TREE) return CFB_ERR_INVALID_ARG;
   if (D <= 0 || D % 64 || H <= 0 || D % H || Lb <= 0 || T <= 0 || CH <= 0 || E <= 0 || E * CH != DL ||
-      C <= 0 || B <= 0 || D > 5120)
+      C <= 0 || B <= 0 || D > 4 * kLnThreads * kLnMaxV || (D / H) % 8 || D / H > 32 * 8 * kAttnMaxChunks ||
+      C > kAttnMaxKeys || DL > kAttnMaxKeys)
     return CFB_ERR_UNSUPPORTED;
   if (r->ranks > 1) return CFB_ERR_UNSUPPORTED;           // the row-sharded head is engine-only
   if (flow && (r->init_mode < CFB_INIT_GIVEN || r->init_mode > CFB_INIT_DELTA || (r->init_mode == CFB_INIT_GIVEN && !r->z0)))
@@ -758,8 +837,6 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
     int fr = 1;
     for (int i = 0; i < K; ++i) { const int k = min(r->tree_keep, fr * TB); levels.push_back(k); Ntree += k; fr = k; }
   }
-  const int VPL = (D + 127) / 128;
-  if (P) P->vpl = VPL <= 8 ? 8 : VPL <= 16 ? 16 : VPL <= 24 ? 24 : 40;
 
   int* err = bm.take<int>(64);
   // ---- flow buffers
@@ -778,6 +855,35 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
     splits[2] = choose_splits(tiles, FM * D / BK, nsm);
   }
   const int SPL = std::max(splits[0], splits[2]);
+  // split-K fixup scratch, shared by the plan's launches (they run one after another): partial
+  // tiles and per-tile arrival counters (zeroed once at creation; each launch leaves them zero)
+  const size_t kFixFloats = (size_t)16 << 20;          // 64 MiB of partial tiles
+  const int kFixTiles = 4096;
+  float* fix_ws = bm.take<float>(kFixFloats);
+  int* fix_cnt = bm.take<int>(kFixTiles);
+  // split-K for a non-partial epilogue: enough CTAs to fill the SMs, within the scratch
+  auto fix_splits = [&](GemmLaunch& G) {
+    int tiles = 0;
+    for (int i = 0; i < G.nprob; ++i) tiles += G.p[i].m_tiles * G.p[i].n_tiles;
+    size_t used = 0;
+    int ctile = 0;
+    for (int i = 0; i < G.nprob; ++i) {
+      GemmProb& p = G.p[i];
+      if (p.epi == EPI_PART || p.epi == EPI_HEAD) continue;
+      int s = choose_splits(tiles, p.kblocks, nsm);
+      const size_t per = (size_t)p.m_tiles * p.n_tiles * BM * BN;
+      while (s > 1 && used + per * s > kFixFloats) --s;
+      if (s > 1 && ctile + p.m_tiles * p.n_tiles > kFixTiles) s = 1;
+      p.kb_per_split = (p.kblocks + s - 1) / s;
+      p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+      if (p.splits > 1) {
+        p.fix_ws = fix_ws + used;
+        p.fix_cnt = fix_cnt + ctile;
+        used += per * p.splits;
+        ctile += p.m_tiles * p.n_tiles;
+      }
+    }
+  };
   if (flow) {
     for (int i = 0; i < E * Lb; ++i) kvc[i] = bm.take<__half>((size_t)B * C * 2 * D);
     for (int e = 0; e < E; ++e) {
@@ -817,7 +923,14 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   P->err = err;
   P->batch = B;
   cfb_status st;
-  auto add_gemm = [&](GemmLaunch& L) { L.err = err; P->gemms.push_back(L); P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1}); };
+  auto add_gemm = [&](GemmLaunch& L) {
+    L.err = err;
+    fix_splits(L);
+    P->gemms.push_back(L);
+    P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1});
+  };
+  P->fix_cnt = fix_cnt;
+  P->fix_cnt_bytes = kFixTiles * sizeof(int);
   auto add_ln = [&](LnLaunch& L) {
     L.D = D;
     L.rows = 0;
@@ -847,8 +960,6 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
         if (++G.nprob == kMaxProbs) { add_gemm(G); G = GemmLaunch{}; }
       }
     if (G.nprob) add_gemm(G);
-    const int amax = std::max(C, DL);
-    P->attn_smem = (int)((size_t)(amax + 2 * amax) * hd * 4 + (size_t)amax * amax * 4);
     for (int s = 0; s < T; ++s) {
       {
         LnLaunch L{};
@@ -893,7 +1004,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
         };
         auto attn = [&](bool self_, int l_) {
           AttnLaunch A{};
-          A.nseg = E; A.H = H; A.hd = hd; A.maxS = amax; A.maxSK = amax; A.scale = 1.f / sqrtf((float)hd);
+          A.nseg = E; A.H = H; A.hd = hd; A.scale = 1.f / sqrtf((float)hd);
           for (int e = 0; e < E; ++e) {
             AttnSeg& g = A.s[e];
             g.S = (e + 1) * CH; g.out = ao[e]; g.ldo = D;
@@ -1030,10 +1141,7 @@ cfb_status wide_run_steps(cfb_wide_plan* P, cudaStream_t st) {
         break;
       case S_LN: {
         const LnLaunch& L = P->lns[s.idx];
-        if (P->vpl == 8) ln_launch<8>(L, st);
-        else if (P->vpl == 16) ln_launch<16>(L, st);
-        else if (P->vpl == 24) ln_launch<24>(L, st);
-        else ln_launch<40>(L, st);
+        wide_ln_kernel<<<L.rows, kLnThreads, 0, st>>>(L);
         break;
       }
       case S_GEMM: {
@@ -1043,7 +1151,7 @@ cfb_status wide_run_steps(cfb_wide_plan* P, cudaStream_t st) {
       }
       case S_ATTN: {
         const AttnLaunch& A = P->attns[s.idx];
-        wide_attn_kernel<<<dim3((unsigned)(P->batch * A.H), (unsigned)A.nseg), 128, P->attn_smem, st>>>(A);
+        wide_attn_kernel<<<dim3((unsigned)(P->batch * A.H), (unsigned)A.nseg), 128, 0, st>>>(A);
         break;
       }
       case S_GATHER: {
@@ -1088,11 +1196,9 @@ extern "C" cfb_status cfb_wide_create(const cfb_drafter* d, const cfb_run* r, vo
   cudaDeviceGetAttribute(&P->nsm, cudaDevAttrMultiProcessorCount, P->dev);
   Bump bm{static_cast<char*>(ws)};
   st = wide_layout(d, r, bm, P);
-  if (st == CFB_OK && P->attn_smem > 48 * 1024 &&
-      cudaFuncSetAttribute(wide_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P->attn_smem) != cudaSuccess)
-    st = cfb_launch_status("cudaFuncSetAttribute(wide_attn_kernel)");
   if (st == CFB_OK && cudaMemset(P->err, 0, sizeof(int)) != cudaSuccess) st = cfb_launch_status("cudaMemset");
   if (st == CFB_OK && P->hin && cudaMemset(P->hin, 0, P->hin_bytes) != cudaSuccess) st = cfb_launch_status("cudaMemset");
+  if (st == CFB_OK && cudaMemset(P->fix_cnt, 0, P->fix_cnt_bytes) != cudaSuccess) st = cfb_launch_status("cudaMemset");
   if (st != CFB_OK) { delete P; return st; }
   *out = P;
   return CFB_OK;

@@ -58,6 +58,10 @@ struct GemmProb {
   const float* pred; int beams, pred_rows, step;
   // EPI_HEAD
   int topb, rowoff;
+  // split-K of a non-partial epilogue: each split stores its fp32 tile to fix_ws
+  // [tile][split][BM][BN]; the split that arrives last at fix_cnt[tile] adds them in split order,
+  // applies the epilogue and resets the counter (nobody waits)
+  float* fix_ws; int* fix_cnt;
 };
 
 constexpr int kMaxProbs = 8;

@@ -24,12 +24,13 @@ import os
 import torch
 
 from . import _lib, shortlist as _sl
-from .engine import Plan
-from .weights import DraftConfig, DrafterWeights
+from .engine import Plan, WidePlan
+from .weights import DraftConfig, DrafterWeights, WideWeights
 
 
-# requests one engine plan drafts at once: its jobs hold at most 64 activation rows
-# (B x context rows, B x draft_length, B x beam width); larger batches run as several plans
+# requests one persistent-engine plan drafts at once: its jobs hold at most 64 activation rows
+# (B x context rows, B x draft_length, B x beam width). Larger batches run on the wide plan
+# (tcgen05 GEMMs over all requests at once), or, with a row-sharded head, as several engine plans.
 MAX_PLAN_BATCH = 8
 
 
@@ -92,6 +93,9 @@ class FlowDrafterProposer:
             shortlist_ids = torch.arange(embed.shape[0])        # full head
         self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device,
                                       head_shard=head_shard)
+        # the wide plan's row-major weights are built on first use by a batch above MAX_PLAN_BATCH
+        self._wide_src = None if head_shard is not None else (state_dict, embed, lm_head, shortlist_ids)
+        self._wide_weights = None
         self.group = group
         self.cfg = cfg
         self.dev = self.weights.dev
@@ -163,6 +167,22 @@ class FlowDrafterProposer:
             self._plans[key] = p
         return p
 
+    def _wide_plan(self, mode: int, B: int) -> WidePlan:
+        key = ("wide", mode, B)
+        p = self._plans.get(key)
+        if p is None:
+            if self._wide_weights is None:
+                sd, embed, lm_head, ids = self._wide_src
+                if ids is None:
+                    ids = torch.arange(embed.shape[0])
+                self._wide_weights = WideWeights(sd, self.cfg, embed, lm_head, ids, device=self.dev)
+            init = _lib.INIT_MODES[self.init_mode]
+            p = WidePlan(self._wide_weights, mode, B, width=self.width,
+                         depth=self.tree_depth if mode == _lib.MODE_TREE else self.K,
+                         tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+            self._plans[key] = p
+        return p
+
     def _load_inputs(self, p: Plan, ctx: torch.Tensor, known0: torch.Tensor | None):
         _lib.require_cuda(ctx, "ctx")
         p.ctx.copy_(ctx.to(torch.float16), non_blocking=True)
@@ -175,10 +195,11 @@ class FlowDrafterProposer:
 
     # ------------------------------------------------------------------ drafting interface
     def _run(self, mode: int, ctx: torch.Tensor, known0: torch.Tensor | None, out: str) -> torch.Tensor:
-        """One plan launch per chunk of at most MAX_PLAN_BATCH requests."""
+        """Up to MAX_PLAN_BATCH requests: one persistent-engine launch. More: one wide plan over
+        the whole batch (a row-sharded head instead runs engine plans of MAX_PLAN_BATCH requests)."""
         B = ctx.shape[0]
-        if B <= MAX_PLAN_BATCH:
-            p = self._plan(mode, B)
+        if B <= MAX_PLAN_BATCH or self._wide_src is not None:
+            p = self._plan(mode, B) if B <= MAX_PLAN_BATCH else self._wide_plan(mode, B)
             self._load_inputs(p, ctx, known0)
             p.run(group=self.group)
             return getattr(p, out)

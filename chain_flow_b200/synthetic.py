@@ -57,6 +57,24 @@ class Workload:
             head += min(d, 4) * D * D + 2 * (2 * D * D) + head_fraction * self.shortlist_rows * (D + self.markov_rank)
         return int(2 * (crosskv + T * per_step + head))
 
+    def flops_per_draft(self, batch: int) -> int:
+        """Multiply-add FLOPs (2 per MAC) of the Linear layers of one draft of `batch` requests:
+        every Euler step runs each block of chunk expert e over batch x 3(e+1) rows and out_proj
+        over batch x 3 rows; cross K/V runs once over batch x 8 context rows; each beam depth runs
+        the path head and the shortlist head over batch x width beam rows. Attention and the
+        row kernels are not counted (under 1%)."""
+        D, L, T, FM = self.hidden, self.layers, self.steps, self.ffn
+        flow = 0
+        for e in range(2):
+            rows = batch * 3 * (e + 1)
+            flow += rows * L * (6 + 2 * FM) * D * D + batch * 3 * D * D
+        cross = batch * 8 * 2 * L * 2 * D * D
+        head = 0
+        bw = batch * self.width
+        for d in range(1, self.draft_tokens + 1):
+            head += bw * (min(d, 4) * D * D + 4 * D * D + self.shortlist_rows * (D + self.markov_rank))
+        return int(2 * (T * flow + cross + head))
+
 
 WORKLOADS = {
     # BASELINE config 1 (CPU plumbing) at flow width = hidden (no VAE)

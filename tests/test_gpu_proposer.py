@@ -145,10 +145,11 @@ def test_batch8_flow_and_chain_match_oracle():
     assert torch.equal(p.tokens.cpu(), ch), (p.tokens.cpu(), ch)
 
 
-def test_batches_above_one_plan_run_as_several_plans():
-    """B = 11 > MAX_PLAN_BATCH: the proposer drafts requests [0, 8) and [8, 11) as two plans. The
-    hiddens stay within tolerance of the oracle for all 11, and the drafts equal those of the two
-    chunks drafted on their own (same plans, same inputs)."""
+def test_batches_above_one_engine_plan_run_on_the_wide_plan():
+    """B = 11 > MAX_PLAN_BATCH: the proposer drafts the whole batch with one wide plan (tcgen05
+    GEMMs). The hiddens stay within tolerance of the oracle, and the chain and tree drafts are the
+    oracle beam over the wide plan's own hiddens."""
+    from chain_flow_b200 import _lib
     from chain_flow_b200.proposer import MAX_PLAN_BATCH, FlowDrafterProposer
     from chain_flow_b200.weights import DraftConfig
     from gpu_util import random_state_dict
@@ -167,14 +168,20 @@ def test_batches_above_one_plan_run_as_several_plans():
     ctx = torch.randn(B, 8, D, generator=g).half().cuda()
     known0 = torch.randint(0, V, (B,), generator=g).cuda()
     pred = p.predict_hidden(ctx).clone()
-    assert pred.shape[0] == B
+    assert pred.shape[0] == B and ("wide", _lib.MODE_FLOW, B) in p._plans
     ocfg = oracle.FlowConfig(hidden=D, num_heads=8, ffn_multiplier=2, num_layers=2, num_flow_steps=2,
                              markov_rank=32)
     c = ctx.float().cpu()
     want = oracle.integrate(sd, ocfg, c, _delta_z0(c).half().float())
     assert _rel(pred, want) < HIDDEN_RTOL, _rel(pred, want)
-    for fn in (p._beam_chains, p._beam_tree):
-        whole = fn(ctx, known0).clone()
-        parts = [fn(ctx[a:b], known0[a:b]).clone() for a, b in ((0, MAX_PLAN_BATCH), (MAX_PLAN_BATCH, B))]
-        assert torch.equal(whole, torch.cat(parts)), fn.__name__
+    hw, w2 = lm[sl], sd["markov.w2.weight"][sl]
+    ch = p._beam_chains(ctx, known0).cpu()
+    cp = p._plans[("wide", _lib.MODE_CHAIN, B)].pred.cpu()
+    assert torch.equal(ch, oracle.beam_chains(sd, ocfg, emb, hw, w2, sl, cp, known0.cpu(), 4, 5))
+    tr = p._beam_tree(ctx, known0).cpu()
+    tp = p._plans[("wide", _lib.MODE_TREE, B)].pred.cpu()
+    want_tr = oracle.beam_tree(sd, ocfg, emb, hw, w2, sl, tp, known0.cpu(), 4, 4, 5)
+    if not torch.equal(tr, want_tr):
+        from beam_check import check_tree
+        check_tree(tr, sd, ocfg, emb, hw, w2, sl, tp, known0.cpu(), 4, 4, 5)
     assert p.device_error() == 0
