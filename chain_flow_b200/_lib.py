@@ -27,7 +27,7 @@ EXPORTED = [
     "cfb_abi_version", "cfb_last_cuda_error", "cfb_packed_bytes", "cfb_pack_linear",
     "cfb_fold_bias", "cfb_time_embed", "cfb_plan_workspace", "cfb_plan_build", "cfb_plan_run",
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
-    "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_workspace",
+    "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_packed_bytes", "cfb_wide_pack", "cfb_wide_workspace",
     "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
 ]
 ABI_VERSION = 2
@@ -99,6 +99,9 @@ def _declare(lib):
     lib.cfb_tree_gdn.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
     lib.cfb_tree_gdn_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp]
     lib.cfb_wide_gemm.argtypes = [vp, i64, vp, i64, vp, vp, i64, i32, i32, i32, i32, i32, vp, vp]
+    lib.cfb_wide_packed_bytes.argtypes = [i32, i32]
+    lib.cfb_wide_packed_bytes.restype = sz
+    lib.cfb_wide_pack.argtypes = [vp, i64, i32, i32, vp, vp]
     lib.cfb_wide_workspace.argtypes = [C.POINTER(Drafter), C.POINTER(Run), C.POINTER(sz)]
     lib.cfb_wide_create.argtypes = [C.POINTER(Drafter), C.POINTER(Run), vp, sz, C.POINTER(vp)]
     lib.cfb_wide_run.argtypes = [vp, vp]

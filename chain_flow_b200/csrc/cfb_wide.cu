@@ -21,17 +21,22 @@ __device__ __forceinline__ void wide_err(int* err, int code) {
 }
 
 // ---- the epilogue of one 16-column slice of one accumulator row -------------------------------
-__device__ __forceinline__ void store_half16(__half* dst, const float (&v)[16]) {
+template <int NV>
+__device__ __forceinline__ void store_halves(__half* dst, const float (&v)[NV]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
-  d[0] = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
-  d[1] = make_uint4(pack_half2(v[8], v[9]), pack_half2(v[10], v[11]), pack_half2(v[12], v[13]), pack_half2(v[14], v[15]));
+#pragma unroll
+  for (int q = 0; q < NV / 8; ++q)
+    d[q] = make_uint4(pack_half2(v[8 * q], v[8 * q + 1]), pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                      pack_half2(v[8 * q + 4], v[8 * q + 5]), pack_half2(v[8 * q + 6], v[8 * q + 7]));
 }
 
-__device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, int col, float (&v)[16]) {
+// NV consecutive columns [col, col + NV) of one output row (NV a multiple of 4)
+template <int NV>
+__device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, int col, float (&v)[NV]) {
   if (P.bias && P.epi != EPI_PART && P.epi != EPI_PATH) {
     const float4* b4 = reinterpret_cast<const float4*>(P.bias + col);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NV / 4; ++q) {
       const float4 b = b4[q];
       v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
     }
@@ -43,16 +48,16 @@ __device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, in
                  (long long)row * P.ldo + col;
       float4* o4 = reinterpret_cast<float4*>(o);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < NV / 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       break;
     }
     case EPI_F16:
-      store_half16(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
+      store_halves(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
       break;
     case EPI_GELU16: {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i]);
-      store_half16(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
+      for (int i = 0; i < NV; ++i) v[i] = gelu_erf(v[i]);
+      store_halves(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
       break;
     }
     case EPI_EULER: {
@@ -60,7 +65,7 @@ __device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, in
       float* z = static_cast<float*>(P.out) + ((long long)b * P.zrows + P.zstart + c) * P.ldo + col;
       float4* z4 = reinterpret_cast<float4*>(z);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NV / 4; ++q) {
         float4 a = z4[q];
         a.x += P.dt * v[4 * q]; a.y += P.dt * v[4 * q + 1]; a.z += P.dt * v[4 * q + 2]; a.w += P.dt * v[4 * q + 3];
         z4[q] = a;
@@ -73,25 +78,25 @@ __device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, in
         if (lp[j] < 0) continue;
         const float4* b4 = reinterpret_cast<const float4*>(P.pbias + (long long)j * P.N + col);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NV / 4; ++q) {
           const float4 b = b4[q];
           v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
         }
       }
       float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(P.out) + (long long)row * P.ldo + col);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < NV / 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       break;
     }
     case EPI_HEADIN: {
       const int b = row / P.beams;
       const float4* p4 = reinterpret_cast<const float4*>(P.pred + ((long long)b * P.pred_rows + P.step) * P.N + col);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NV / 4; ++q) {
         const float4 a = p4[q];
         v[4 * q] += a.x; v[4 * q + 1] += a.y; v[4 * q + 2] += a.z; v[4 * q + 3] += a.w;
       }
-      store_half16(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
+      store_halves(static_cast<__half*>(P.out) + (long long)row * P.ldo + col, v);
       break;
     }
     default:
@@ -100,34 +105,107 @@ __device__ __forceinline__ void epi_slice(const GemmProb& P, int sp, int row, in
 }
 
 // ---- the GEMM kernel ----------------------------------------------------------------------------
+// The fp32 logits of one accumulator row [col0, col0 + BN): online (max, sum exp) and the sorted
+// top-`topb` (value, id) list, written to the row's list slot of this n tile. Per 16 columns: one
+// max, 16 independent exponentials, and a list insertion only for a value that beats the list's
+// current last entry (rare after the first columns).
+__device__ __forceinline__ void head_row(const GemmProb& P, uint32_t tb, int nt, int row, bool live) {
+  float m = -INFINITY, s = 0.f;
+  float tv[kTopMaxW];
+  int ti[kTopMaxW];
+#pragma unroll
+  for (int i = 0; i < kTopMaxW; ++i) { tv[i] = -INFINITY; ti[i] = 0x7fffffff; }
+  float thr = -INFINITY;
+  int thr_i = 0x7fffffff;
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    float v[16];
+    tmem_ld16(tb + c0, v);                                    // every lane: .sync.aligned
+    const int cb = nt * BN + c0;
+    float cm = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (cb + i >= P.N) v[i] = -INFINITY;
+      cm = fmaxf(cm, v[i]);
+    }
+    if (cm > m) { s *= __expf(m - cm); m = cm; }
+    if (m > -INFINITY) {
+      float cs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) cs += __expf(v[i] - m);
+      s += cs;
+    }
+    unsigned cand = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (better_w(v[i], cb + i + P.rowoff, thr, thr_i)) cand |= 1u << i;
+    while (cand) {
+      const int i = __ffs(cand) - 1;
+      cand &= cand - 1;
+      float xv = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) if (j == i) xv = v[j];
+      int xi = cb + i + P.rowoff;
+      if (!better_w(xv, xi, thr, thr_i)) continue;            // the list's last entry may have risen
+#pragma unroll
+      for (int q = 0; q < kTopMaxW; ++q) {
+        if (q < P.topb && better_w(xv, xi, tv[q], ti[q])) {
+          const float a = tv[q]; const int b = ti[q];
+          tv[q] = xv; ti[q] = xi; xv = a; xi = b;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kTopMaxW; ++q)
+        if (q == P.topb - 1) { thr = tv[q]; thr_i = ti[q]; }
+    }
+  }
+  if (live) {
+    const int lw = 2 + 2 * P.topb;
+    float* o = static_cast<float*>(P.out) + ((long long)row * P.n_tiles + nt) * lw;
+    o[0] = m; o[1] = s;
+#pragma unroll
+    for (int q = 0; q < kTopMaxW; ++q)
+      if (q < P.topb) { o[2 + q] = tv[q]; o[2 + P.topb + q] = __int_as_float(ti[q]); }
+  }
+}
+
+// NH: 128-row M tiles per CTA (1, or 2 sharing each weight block; every problem of a launch
+// must then have pair = 1), fixed at compile time so that the ring arithmetic is static.
+template <int NH>
 __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid_constant__ GemmLaunch L) {
+  constexpr uint32_t abytes = NH * kTileBytes;
+  constexpr uint32_t stage = abytes + kWTileBytes;                       // 48 or 64 KiB
+  constexpr int nst = (int)(kRingBytes / stage);                         // 4 or 3 stages
+  constexpr uint32_t tcols = NH * BN;
   extern __shared__ uint8_t smraw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kStages * kStageBytes);
-  uint64_t* empty = full + kStages;
-  uint64_t* accf = empty + kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kRingBytes);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
   volatile int* sflag = reinterpret_cast<volatile int*>(tslot + 1);      // this CTA failed a wait
+  volatile int* s_last = sflag + 1;                                      // split-K: this split is last
 
   int pi = 0;
   while (pi + 1 < L.nprob && (int)blockIdx.x >= L.p[pi + 1].cta0) ++pi;
   const GemmProb& P = L.p[pi];
   int t = (int)blockIdx.x - P.cta0;
-  const int mt = t % P.m_tiles;
-  t /= P.m_tiles;
+  const int mp = t % P.m_pairs;
+  t /= P.m_pairs;
   const int nt = t % P.n_tiles;
   const int sp = t / P.n_tiles;
   const int kb0 = sp * P.kb_per_split;
   const int nk = min(P.kblocks, kb0 + P.kb_per_split) - kb0;            // >= 1 (host guarantees)
+  const int mt0 = NH * mp;                                              // first 128-row M tile
+  const int nh = (NH == 2 && mt0 + 1 < P.m_tiles) ? 2 : 1;              // M tiles holding rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < kMaxStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(accf, 1);
     *sflag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tslot, BN);
+  if (warp == 1) tmem_alloc(tslot, tcols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -136,31 +214,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&P.ta);
-      prefetch_tmap(&P.tw);
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % kStages;
-        if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) - 1) & 1)) { *sflag = 1; break; }
+        const int s = i % nst;
+        if (i >= nst && !mbar_wait(&empty[s], ((i / nst) - 1) & 1)) { *sflag = 1; break; }
         if (*sflag) break;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        uint8_t* st = sm + s * kStageBytes;
-        tma_load_2d(st, &P.ta, (kb0 + i) * BK, mt * BM, &full[s]);
-        tma_load_2d(st + kTileBytes, &P.tw, (kb0 + i) * BK, nt * BN, &full[s]);
+        mbar_arrive_expect_tx(&full[s], stage);
+        uint8_t* st = sm + s * stage;
+        const int kb = kb0 + i;
+        tma_load_2d(st, &P.ta, kb * BK, mt0 * BM, &full[s]);
+        if (NH == 2) tma_load_2d(st + kTileBytes, &P.ta, kb * BK, (mt0 + 1) * BM, &full[s]);
+        bulk_g2s(st + abytes, P.wt + ((long long)nt * P.kbt + kb) * (BN * BK), kWTileBytes, &full[s]);
         ++issued;
       }
       if (*sflag)   // copies still in flight land before the CTA may exit (bounded)
-        for (int i = max(0, issued - kStages); i < issued; ++i) mbar_wait(&full[i % kStages], (i / kStages) & 1);
+        for (int i = max(0, issued - nst); i < issued; ++i) mbar_wait(&full[i % nst], (i / nst) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       for (int i = 0; i < nk; ++i) {
-        const int s = i % kStages;
-        if (!mbar_wait(&full[s], (i / kStages) & 1)) { *sflag = 1; break; }
+        const int s = i % nst;
+        if (!mbar_wait(&full[s], (i / nst) & 1)) { *sflag = 1; break; }
         tc_fence_after();
-        const uint32_t a = smem_u32(sm + s * kStageBytes), w = a + kTileBytes;
+        const uint32_t a = smem_u32(sm + s * stage), w = a + abytes;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          tc_mma_f16(tmem, sw128_desc(a + k * 32), sw128_desc(w + k * 32), kIdesc, (uint32_t)((i | k) != 0));
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t wd = sw128_desc(w + k * 32);
+          const uint32_t acc = (uint32_t)((i | k) != 0);
+          tc_mma_f16(tmem, sw128_desc(a + k * 32), wd, kIdesc, acc);
+          if (NH == 2) tc_mma_f16(tmem + BN, sw128_desc(a + kTileBytes + k * 32), wd, kIdesc, acc);
+        }
         tc_commit(&empty[s]);
       }
       tc_commit(accf);       // arrives once every MMA issued above has completed
@@ -170,56 +253,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
     const bool ok = mbar_wait(accf, 0);
     tc_fence_after();
     if (!ok) *sflag = 1;
-    const int row = mt * BM + lg * 32 + lane;
-    const bool live = ok && *sflag == 0 && row < P.M;
-    const uint32_t tb = tmem + ((uint32_t)(lg * 32) << 16);
+    const bool good = ok && *sflag == 0;
     if (P.epi == EPI_HEAD) {
-      float m = -INFINITY, s = 0.f;
-      float tv[kTopMaxW];
-      int ti[kTopMaxW];
-#pragma unroll
-      for (int i = 0; i < kTopMaxW; ++i) { tv[i] = -INFINITY; ti[i] = 0x7fffffff; }
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tb + c0, v);                                // every lane: .sync.aligned
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = nt * BN + c0 + i;
-          if (col >= P.N) break;
-          const float x = v[i];
-          if (x > m) { s = s * __expf(m - x) + 1.f; m = x; } else { s += __expf(x - m); }
-          float xv = x;
-          int xi = col + P.rowoff;
-#pragma unroll
-          for (int q = 0; q < kTopMaxW; ++q) {
-            if (q < P.topb && better_w(xv, xi, tv[q], ti[q])) {
-              const float a = tv[q]; const int b = ti[q];
-              tv[q] = xv; ti[q] = xi; xv = a; xi = b;
-            }
-          }
-        }
-      }
-      if (live) {
-        const int lw = 2 + 2 * P.topb;
-        float* o = static_cast<float*>(P.out) + ((long long)row * P.n_tiles + nt) * lw;
-        o[0] = m; o[1] = s;
-#pragma unroll
-        for (int q = 0; q < kTopMaxW; ++q)
-          if (q < P.topb) { o[2 + q] = tv[q]; o[2 + P.topb + q] = __int_as_float(ti[q]); }
+      for (int h = 0; h < nh; ++h) {
+        const int row = (mt0 + h) * BM + lg * 32 + lane;
+        head_row(P, tmem + ((uint32_t)(lg * 32) << 16) + h * BN, nt, row, good && row < P.M);
       }
     } else if (P.splits > 1 && P.epi != EPI_PART) {
-      const int tile = mt + P.m_tiles * nt;
-      const int rl = lg * 32 + lane;
-      float* mine = P.fix_ws + (((long long)tile * P.splits + sp) * BM + rl) * BN;
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tb + c0, v);
-        float4* o4 = reinterpret_cast<float4*>(mine + c0);
+      // split-K of a non-partial epilogue: publish this split's tile; the split that arrives last
+      // adds every split's tile in split order and applies the epilogue (nobody waits)
+      const int tile = mp + P.m_pairs * nt;
+      for (int h = 0; h < nh; ++h) {
+        const int rl = h * BM + lg * 32 + lane;
+        float* mine = P.fix_ws + (((long long)tile * P.splits + sp) * 2 * BM + rl) * BN;
+        const uint32_t tb = tmem + ((uint32_t)(lg * 32) << 16) + h * BN;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tb + c0, v);
+          float4* o4 = reinterpret_cast<float4*>(mine + c0);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          for (int q = 0; q < 4; ++q) o4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
       }
       consumer_sync(4 * 32);
-      volatile int* s_last = sflag + 1;
       if (threadIdx.x == 2 * 32) {
         __threadfence();
         const int prev = atomicAdd(P.fix_cnt + tile, 1);
@@ -228,31 +284,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
         *s_last = last;
       }
       consumer_sync(4 * 32);
-      if (*s_last && live) {
-        const float* base = P.fix_ws + ((long long)tile * P.splits * BM + rl) * BN;
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          const int col = nt * BN + c0;
-          if (col >= P.N) break;
-          float v[16];
+      if (*s_last && good) {
+        for (int h = 0; h < nh; ++h) {
+          const int rl = h * BM + lg * 32 + lane;
+          const int row = mt0 * BM + rl;
+          if (row >= P.M) continue;
+          const float* base = P.fix_ws + ((long long)tile * P.splits * 2 * BM + rl) * BN;
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            const int col = nt * BN + c0;
+            if (col >= P.N) break;
+            float v[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.f;
-          for (int q = 0; q < P.splits; ++q) {
-            const float4* src = reinterpret_cast<const float4*>(base + (long long)q * BM * BN + c0);
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            for (int q = 0; q < P.splits; ++q) {
+              const float4* src = reinterpret_cast<const float4*>(base + (long long)q * 2 * BM * BN + c0);
 #pragma unroll
-            for (int z = 0; z < 4; ++z) {
-              const float4 t4 = __ldcg(src + z);
-              v[4 * z] += t4.x; v[4 * z + 1] += t4.y; v[4 * z + 2] += t4.z; v[4 * z + 3] += t4.w;
+              for (int z = 0; z < 4; ++z) {
+                const float4 t4 = __ldcg(src + z);
+                v[4 * z] += t4.x; v[4 * z + 1] += t4.y; v[4 * z + 2] += t4.z; v[4 * z + 3] += t4.w;
+              }
             }
+            epi_slice<16>(P, sp, row, col, v);
           }
-          epi_slice(P, sp, row, col, v);
         }
       }
     } else {
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tb + c0, v);
-        const int col = nt * BN + c0;
-        if (live && col < P.N) epi_slice(P, sp, row, col, v);
+      for (int h = 0; h < nh; ++h) {
+        const int row = (mt0 + h) * BM + lg * 32 + lane;
+        const bool live = good && row < P.M;
+        const uint32_t tb = tmem + ((uint32_t)(lg * 32) << 16) + h * BN;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tb + c0, v);
+          const int col = nt * BN + c0;
+          if (live && col < P.N) epi_slice<16>(P, sp, row, col, v);
+        }
       }
     }
   }
@@ -260,7 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, tcols);
   }
   if (threadIdx.x == 0 && *sflag) wide_err(L.err, DEV_TIMEOUT_FULL);
 }
@@ -282,7 +348,8 @@ cfb_status wide_init(int dev) {
   }
   if ((int)g_gemm_attr_done.size() <= dev) g_gemm_attr_done.resize(dev + 1, 0);
   if (!g_gemm_attr_done[dev]) {
-    if (cudaFuncSetAttribute(wide_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(wide_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(wide_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem) != cudaSuccess)
       return cfb_launch_status("cudaFuncSetAttribute(wide_gemm_kernel)");
     g_gemm_attr_done[dev] = 1;
   }
@@ -310,15 +377,21 @@ namespace wide {
 
 // Fill the shape part of one problem. K (the multiplied extent) must be a multiple of 64; every
 // split gets at least one 64-column k block.
+// W: tiled by cfb_wide_pack from a [N, ldw] matrix (ldw a multiple of 64); the GEMM multiplies its
+// first K columns.
 cfb_status gemm_prob(GemmProb& p, const void* A, long long lda, int M, const void* W, long long ldw, int N,
                      int K, int epi, int splits) {
-  if (M <= 0 || N <= 0 || K <= 0 || K % BK) return CFB_ERR_UNSUPPORTED;
+  if (M <= 0 || N <= 0 || K <= 0 || K % BK || ldw % BK || K > ldw) return CFB_ERR_UNSUPPORTED;
   if (epi != EPI_HEAD && N % 16) return CFB_ERR_UNSUPPORTED;
+  if (!W || (reinterpret_cast<uintptr_t>(W) & 15)) return CFB_ERR_INVALID_ARG;
   cfb_status st = make_map(&p.ta, A, M, K, lda);
   if (st != CFB_OK) return st;
-  if ((st = make_map(&p.tw, W, N, K, ldw)) != CFB_OK) return st;
+  p.wt = static_cast<const __half*>(W);
+  p.kbt = (int)(ldw / BK);
   p.M = M; p.N = N; p.kblocks = K / BK;
   p.m_tiles = (M + BM - 1) / BM;
+  p.pair = 0;
+  p.m_pairs = p.m_tiles;
   p.n_tiles = (N + BN - 1) / BN;
   splits = std::max(1, std::min(splits, p.kblocks));
   p.kb_per_split = (p.kblocks + splits - 1) / splits;
@@ -331,10 +404,11 @@ cfb_status gemm_launch(GemmLaunch& L, cudaStream_t stream) {
   int total = 0;
   for (int i = 0; i < L.nprob; ++i) {
     L.p[i].cta0 = total;
-    total += L.p[i].m_tiles * L.p[i].n_tiles * L.p[i].splits;
+    total += L.p[i].m_pairs * L.p[i].n_tiles * L.p[i].splits;
   }
   if (total <= 0) return CFB_OK;
-  wide_gemm_kernel<<<total, kGemmThreads, kGemmSmem, stream>>>(L);
+  if (L.p[0].pair) wide_gemm_kernel<2><<<total, kGemmThreads, kGemmSmem, stream>>>(L);
+  else wide_gemm_kernel<1><<<total, kGemmThreads, kGemmSmem, stream>>>(L);
   return cfb_launch_status("wide_gemm_kernel");
 }
 
@@ -358,7 +432,8 @@ enum LnMode : int {
   LN_PREP = 0,     // x32[b*S + i] = z[b, i] + pos[i] + (i >= start ? temb : 0), then LN
   LN_RESID = 1,    // x32 += bias + sum_s part[s], then LN
   LN_PLAIN32 = 2,  // LN of an fp32 matrix
-  LN_PLAIN16 = 3   // LN of an fp16 matrix
+  LN_PLAIN16 = 3,  // LN of an fp16 matrix
+  LN_PATH = 4      // x = sum_s part[s] + sum_{j < nlive, lastp[r][j] >= 0} pbias[j] (PathHead offsets)
 };
 
 struct LnSeg {
@@ -370,6 +445,7 @@ struct LnSeg {
   const float* z; int zrows, S, start; const float* pos; const float* temb;
   __half* out;
   int cur_only, chunk;     // cur_only: write only rows i >= start, to out[b*chunk + i - start]
+  const int64_t* lastp; int order, nlive; const float* pbias;    // LN_PATH
 };
 constexpr int kMaxLnSegs = 4;
 struct LnLaunch { LnSeg s[kMaxLnSegs]; int nseg, D, rows; };
@@ -423,6 +499,19 @@ __global__ void __launch_bounds__(kLnThreads) wide_ln_kernel(const __grid_consta
         a.x += acc.x; a.y += acc.y; a.z += acc.z; a.w += acc.w;
       } else if (S.mode == LN_PLAIN32) {
         a = *reinterpret_cast<const float4*>(S.x32 + (long long)r * D + c);
+      } else if (S.mode == LN_PATH) {
+#pragma unroll
+        for (int sp = 0; sp < kLnMaxSplit; ++sp)
+          if (sp < S.nsplit) {
+            const float4 q = *reinterpret_cast<const float4*>(S.part + sp * S.split_stride + (long long)r * D + c);
+            a.x += q.x; a.y += q.y; a.z += q.z; a.w += q.w;
+          }
+        const int64_t* lp = S.lastp + (long long)r * S.order;
+        for (int j = 0; j < S.nlive; ++j)
+          if (lp[j] >= 0) {
+            const float4 q = *reinterpret_cast<const float4*>(S.pbias + (long long)j * D + c);
+            a.x += q.x; a.y += q.y; a.z += q.z; a.w += q.w;
+          }
       } else {
         const uint2 h = *reinterpret_cast<const uint2*>(S.x16 + (long long)r * D + c);
         const float2 lo = unpack_half2(h.x), hi = unpack_half2(h.y);
@@ -727,6 +816,45 @@ __global__ void __launch_bounds__(128) wide_beam_kernel(BeamArgs a) {
 
 }  // namespace
 
+// ---- weight packing for the wide GEMM ------------------------------------------------------------
+namespace {
+// one thread per 16-byte chunk of the packed matrix: block (nt, kb), row r, stored chunk c' holds
+// source chunk c = c' ^ (r & 7) of row nt*128 + r, columns kb*64 + 8c .. +8 (zero past nout)
+__global__ void wide_pack_kernel(const __half* __restrict__ w, long long ldw, int nout, int kbt, __half* __restrict__ dst,
+                                 long long nchunks) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < nchunks; e += (long long)gridDim.x * blockDim.x) {
+    const int cs = (int)(e & 7);
+    const long long rowblk = e >> 3;                // (nt, kb, r)
+    const int r = (int)(rowblk % BN);
+    const long long blk = rowblk / BN;              // nt * kbt + kb
+    const int kb = (int)(blk % kbt);
+    const long long nt = blk / kbt;
+    const long long n = nt * BN + r;
+    const int c = cs ^ (r & 7);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n < nout) v = *reinterpret_cast<const uint4*>(w + n * ldw + (long long)kb * BK + c * 8);
+    *reinterpret_cast<uint4*>(dst + e * 8) = v;
+  }
+}
+}  // namespace
+
+extern "C" size_t cfb_wide_packed_bytes(int nout, int k) {
+  if (nout <= 0 || k <= 0 || k % BK) return 0;
+  return (size_t)((nout + BN - 1) / BN) * BN * (size_t)k * sizeof(__half);
+}
+
+extern "C" cfb_status cfb_wide_pack(const void* w, int64_t ldw, int nout, int k, void* dst, void* stream) {
+  if (!w || !dst || nout <= 0 || k <= 0 || ldw < k || (ldw % 8) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(dst) & 15))
+    return CFB_ERR_INVALID_ARG;
+  if (k % BK) return CFB_ERR_UNSUPPORTED;
+  const long long nchunks = (long long)((nout + BN - 1) / BN) * BN * (k / 8);
+  const int blocks = (int)std::min<long long>((nchunks + 255) / 256, 1 << 16);
+  wide_pack_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(w), ldw, nout,
+                                                                        k / BK, static_cast<__half*>(dst), nchunks);
+  return cfb_launch_status("wide_pack_kernel");
+}
+
 extern "C" cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias,
                                     void* out, int64_t ldo, int M, int N, int K, int epi, int splits, int* err,
                                     void* stream) {
@@ -768,14 +896,6 @@ struct Bump {
 enum StepKind { S_INIT, S_HEADINIT, S_LN, S_GEMM, S_ATTN, S_GATHER, S_BEAM };
 struct Step { int kind, idx; };
 
-// Split-K only for launches with fewer output tiles than SMs: a split of at least 4 k blocks,
-// at most 8 splits, and no more CTAs than SMs (one resident CTA per SM).
-int choose_splits(int tiles, int kblocks, int nsm) {
-  if (tiles >= nsm) return 1;
-  int s = std::max(1, nsm / tiles);
-  s = std::min(s, std::max(1, kblocks / 4));
-  return std::min(s, 8);
-}
 
 }  // namespace
 
@@ -845,42 +965,53 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   std::vector<float*> x32(E), part(E);
   std::vector<__half*> xh(E), qkv(E), ao(E), qx(E), u(E), xc(E);
   const int nsm = P ? P->nsm : 148;
-  // split counts of the three residual GEMMs of a block (same for every block)
-  int splits[3];
-  {
-    int tiles = 0;
-    for (int e = 0; e < E; ++e) tiles += ((B * (e + 1) * CH + BM - 1) / BM) * ((D + BN - 1) / BN);
-    splits[0] = choose_splits(tiles, D / BK, nsm);
-    splits[1] = splits[0];
-    splits[2] = choose_splits(tiles, FM * D / BK, nsm);
-  }
-  const int SPL = std::max(splits[0], splits[2]);
+  const int SPL = 8;                                    // partial buffers: the largest split count
   // split-K fixup scratch, shared by the plan's launches (they run one after another): partial
   // tiles and per-tile arrival counters (zeroed once at creation; each launch leaves them zero)
   const size_t kFixFloats = (size_t)16 << 20;          // 64 MiB of partial tiles
   const int kFixTiles = 4096;
   float* fix_ws = bm.take<float>(kFixFloats);
   int* fix_cnt = bm.take<int>(kFixTiles);
-  // split-K for a non-partial epilogue: enough CTAs to fill the SMs, within the scratch
-  auto fix_splits = [&](GemmLaunch& G) {
-    int tiles = 0;
-    for (int i = 0; i < G.nprob; ++i) tiles += G.p[i].m_tiles * G.p[i].n_tiles;
+  // The launch shape of a grouped GEMM (the same for every problem of the group): split-K only
+  // when the group has fewer output tiles than SMs (one resident CTA per SM): as many splits as
+  // fill the SMs, each of at least 4 k blocks, at most 8, and at most 4 for a non-partial
+  // epilogue (whose last split reads every split's tile back). A CTA covers one M tile; the
+  // kernel's two-tile mode (each weight block feeding two M tiles) measured slower on these
+  // shapes, where it halves an already short grid.
+  auto shape = [&](GemmLaunch& G) {
+    bool part = true, fix_ok = true;
+    int tiles = 0, kmin = 1 << 30;
+    for (int i = 0; i < G.nprob; ++i) {
+      if (G.p[i].epi == EPI_HEAD) fix_ok = false;
+      if (G.p[i].epi != EPI_PART) part = false;
+      tiles += G.p[i].m_tiles * G.p[i].n_tiles;
+      kmin = std::min(kmin, G.p[i].kblocks);
+    }
+    int bs = 1;
+    if (tiles < nsm && (part || fix_ok)) {
+      bs = std::min(std::max(1, nsm / tiles), std::max(1, kmin / 4));
+      bs = std::min(bs, part ? 8 : 4);
+    }
+    const int bpair = 0;
     size_t used = 0;
     int ctile = 0;
     for (int i = 0; i < G.nprob; ++i) {
       GemmProb& p = G.p[i];
-      if (p.epi == EPI_PART || p.epi == EPI_HEAD) continue;
-      int s = choose_splits(tiles, p.kblocks, nsm);
-      const size_t per = (size_t)p.m_tiles * p.n_tiles * BM * BN;
-      while (s > 1 && used + per * s > kFixFloats) --s;
-      if (s > 1 && ctile + p.m_tiles * p.n_tiles > kFixTiles) s = 1;
-      p.kb_per_split = (p.kblocks + s - 1) / s;
+      p.pair = bpair;
+      p.m_pairs = bpair ? (p.m_tiles + 1) / 2 : p.m_tiles;
+      int s_ = std::min(bs, p.kblocks);
+      const size_t per = (size_t)p.m_pairs * p.n_tiles * 2 * BM * BN;
+      if (p.epi != EPI_PART) {
+        while (s_ > 1 && used + per * s_ > kFixFloats) --s_;
+        if (s_ > 1 && ctile + p.m_pairs * p.n_tiles > kFixTiles) s_ = 1;
+      }
+      p.kb_per_split = (p.kblocks + s_ - 1) / s_;
       p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
-      if (p.splits > 1) {
+      if (p.epi != EPI_PART && p.splits > 1) {
         p.fix_ws = fix_ws + used;
         p.fix_cnt = fix_cnt + ctile;
         used += per * p.splits;
-        ctile += p.m_tiles * p.n_tiles;
+        ctile += p.m_pairs * p.n_tiles;
       }
     }
   };
@@ -902,14 +1033,14 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   const int BW = B * Wmax;
   const int ntiles = head ? (d->head.nout + BN - 1) / BN : 0;
   const int lw = 2 + 2 * TB;
-  int64_t* lastp = nullptr; float* cum = nullptr; int* prev = nullptr; __half* apath = nullptr; float* hp32 = nullptr;
+  int64_t* lastp = nullptr; float* cum = nullptr; int* prev = nullptr; __half* apath = nullptr; float* hpart = nullptr;
   __half *hph = nullptr, *pm = nullptr, *hin = nullptr; float* lists = nullptr; int64_t* toks = nullptr; int* bps = nullptr;
   if (head) {
     lastp = bm.take<int64_t>((size_t)BW * order);
     cum = bm.take<float>(BW);
     prev = bm.take<int>(BW);
     apath = bm.take<__half>((size_t)BW * order * D);
-    hp32 = bm.take<float>((size_t)BW * D);
+    hpart = bm.take<float>((size_t)8 * BW * D);           // split-K partials of the path offsets
     hph = bm.take<__half>((size_t)BW * D);
     pm = bm.take<__half>((size_t)BW * P2);
     hin = bm.take<__half>((size_t)BW * Kh);
@@ -925,7 +1056,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   cfb_status st;
   auto add_gemm = [&](GemmLaunch& L) {
     L.err = err;
-    fix_splits(L);
+    shape(L);
     P->gemms.push_back(L);
     P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1});
   };
@@ -1023,11 +1154,11 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
         for (int e = 0; e < E; ++e) { o_qkv[e] = qkv[e]; o_part[e] = part[e]; o_qx[e] = qx[e]; o_u[e] = u[e]; }
         if ((st = gemm_e(&cfb_block::qkv, xh.data(), D, 3 * D, D, EPI_F16, o_qkv, 3 * D, 1)) != CFB_OK) return st;
         attn(true, l);
-        if ((st = gemm_e(&cfb_block::self_out, ao.data(), D, D, D, EPI_PART, o_part, D, splits[0])) != CFB_OK) return st;
+        if ((st = gemm_e(&cfb_block::self_out, ao.data(), D, D, D, EPI_PART, o_part, D, 1)) != CFB_OK) return st;
         resid_ln(&cfb_block::self_out, false);
         if ((st = gemm_e(&cfb_block::cross_q, xh.data(), D, D, D, EPI_F16, o_qx, D, 1)) != CFB_OK) return st;
         attn(false, l);
-        if ((st = gemm_e(&cfb_block::cross_out, ao.data(), D, D, D, EPI_PART, o_part, D, splits[1])) != CFB_OK) return st;
+        if ((st = gemm_e(&cfb_block::cross_out, ao.data(), D, D, D, EPI_PART, o_part, D, 1)) != CFB_OK) return st;
         resid_ln(&cfb_block::cross_out, false);
         if ((st = gemm_e(&cfb_block::ffn_up, xh.data(), D, FM * D, D, EPI_GELU16, o_u, FM * D, 1)) != CFB_OK) return st;
         {
@@ -1036,7 +1167,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
           for (int e = 0; e < E; ++e) {
             const cfb_linear& w = d->experts[e].blocks[l].ffn_down;
             GemmProb& p = G2.p[e];
-            if ((st = gemm_prob(p, u[e], FM * D, B * (e + 1) * CH, w.w, FM * D, D, FM * D, EPI_PART, splits[2])) != CFB_OK)
+            if ((st = gemm_prob(p, u[e], FM * D, B * (e + 1) * CH, w.w, FM * D, D, FM * D, EPI_PART, 1)) != CFB_OK)
               return st;
             p.out = part[e]; p.ldo = D; p.split_stride = (long long)B * (e + 1) * CH * D;
           }
@@ -1073,16 +1204,15 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
         G.nprob = 1;
         GemmProb& p = G.p[0];
         if ((st = gemm_prob(p, apath, (long long)order * D, BW, d->path_offsets.w, (long long)order * D, D, nlive * D,
-                            EPI_PATH, 1)) != CFB_OK)
+                            EPI_PART, 1)) != CFB_OK)
           return st;
-        p.out = hp32; p.ldo = D; p.lastp = lastp; p.order = order; p.nlive = nlive; p.pbias = d->path_offset_bias;
+        p.out = hpart; p.ldo = D; p.split_stride = (long long)BW * D;
         add_gemm(G);
-      }
-      {
         LnLaunch L{};
         L.nseg = 1;
         LnSeg& g = L.s[0];
-        g.rows = BW; g.mode = LN_PLAIN32; g.x32 = hp32; g.out = hph;
+        g.rows = BW; g.mode = LN_PATH; g.part = hpart; g.nsplit = p.splits; g.split_stride = (long long)BW * D;
+        g.lastp = lastp; g.order = order; g.nlive = nlive; g.pbias = d->path_offset_bias; g.out = hph;
         add_ln(L);
       }
       {

@@ -1,14 +1,19 @@
 // cfb_wide_gemm.cuh -- the batched ("wide") drafting path's GEMM: C = A · Wᵀ on the 5th-generation
 // tensor cores of sm_100a.
 //
-// A is an fp16 activation matrix [M, K] and W an fp16 weight matrix [N, K], both row-major
-// (K-major). One CTA computes one 128 × 128 output tile (128 activation rows × 128 weight rows)
-// over one k range (split-K). 192 threads in three roles:
-//   warp 0, one lane   TMA producer: 2-D tiled bulk tensor copies of a 128 × 64 A tile and a
-//                      128 × 64 W tile per stage (128-byte swizzle) into a kStages-deep ring;
-//   warp 1             allocates 128 TMEM columns (the fp32 accumulator); one lane issues
-//                      tcgen05.mma (M = 128, N = 128, K = 16, four per stage) and returns each
-//                      stage to the producer with tcgen05.commit;
+// A is an fp16 activation matrix [M, K], row-major (K-major). W, an fp16 weight matrix [N, K], is
+// stored tiled (cfb_wide_pack): [N/256][K/64] blocks of 256 rows x 64 columns, 32 KiB each,
+// contiguous, every block already in the 128-byte-swizzled shared-memory image the tensor cores
+// read, so a CTA streams its weights as consecutive 32 KiB bulk copies, while the activations,
+// re-read from L2 by every CTA of a row of tiles, come in through 2-D TMA.
+// One CTA computes a 256 × 256 output tile (two 128-row M tiles of activations × 256 weight
+// rows; one M tile where M ends) over one k range (split-K): each weight block it streams feeds
+// both M tiles, so the weights are read once per 256 activation rows. 192 threads in three roles:
+//   warp 0, one lane   producer: per stage one 2-D tiled TMA copy of each 128 × 64 A tile (128-byte
+//                      swizzle) and one 32 KiB bulk copy of the W block into the stage ring;
+//   warp 1             allocates 512 TMEM columns (two fp32 accumulators); one lane issues
+//                      tcgen05.mma (M = 128, N = 256, K = 16, four per stage and M tile) and
+//                      returns each stage to the producer with tcgen05.commit;
 //   warps 2..5         epilogue: each thread owns one accumulator row (its TMEM lane), reads it
 //                      16 columns at a time with tcgen05.ld and applies the fused epilogue.
 // Every wait is bounded (kWaitBudgetNs); a wait that expires records an error and the CTA
@@ -20,12 +25,15 @@
 namespace cfb {
 namespace wide {
 
-constexpr int BM = 128, BN = 128, BK = 64;
-constexpr int kStages = 6;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int kGemmThreads = 192;
-constexpr uint32_t kTileBytes = BM * BK * 2;             // 16 KiB, A and W tiles alike
-constexpr uint32_t kStageBytes = 2 * kTileBytes;
-constexpr size_t kGemmSmem = kStages * kStageBytes + 1024 /* 1 KiB alignment slack */ + 256;
+constexpr uint32_t kTileBytes = BM * BK * 2;             // 16 KiB A tile (128 rows)
+constexpr uint32_t kWTileBytes = BN * BK * 2;            // 32 KiB W block
+// a CTA covers one or two 128-row M tiles: stages of 2 x 16 + 32 = 64 KiB (3 deep) or
+// 16 + 32 = 48 KiB (4 deep); two fp32 accumulators of 256 columns fill the 512 TMEM columns
+constexpr int kMaxStages = 4;
+constexpr uint32_t kRingBytes = 192 * 1024;
+constexpr size_t kGemmSmem = kRingBytes + 1024 /* 1 KiB alignment slack */ + 256;
 constexpr int kTopMaxW = 8;                              // head epilogue: longest top list
 
 enum EpiKind : int {
@@ -41,9 +49,12 @@ enum EpiKind : int {
 
 struct GemmProb {
   CUtensorMap ta;                 // A [M, K]: box 64 × 128
-  CUtensorMap tw;                 // W [N, K]: box 64 × 128
+  const __half* wt;               // W, tiled: block (n tile, k block) at (nt * kbt + kb) * BN * BK
+  int kbt;                        // k blocks of the packed W (its full K / 64)
   int M, N, kblocks;              // kblocks = K / 64 actually multiplied
   int m_tiles, n_tiles, splits, kb_per_split;
+  int pair;                       // 1: a CTA covers M tiles 2 mp and 2 mp + 1; 0: M tile mp only
+  int m_pairs;                    // CTAs along M
   int cta0;                       // first CTA of this problem in the grouped launch
   int epi;
   const float* bias;              // [N] or null
@@ -125,7 +136,7 @@ CFB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 CFB_DEV uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = 128.
+// Instruction descriptor: fp32 accumulator, fp16 A and B, both K-major, M = 128, N = 256.
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 
 CFB_DEV bool better_w(float v, int i, float w, int j) { return v > w || (v == w && i < j); }

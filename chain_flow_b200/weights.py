@@ -223,8 +223,8 @@ class DrafterWeights:
 
 
 class WideWeights:
-    """The drafter's weights for the wide (batched, tcgen05) plan: every Linear as a row-major fp16
-    [nout, k] matrix with the LayerNorm that feeds it folded in (w = fp16(W16 * gamma),
+    """The drafter's weights for the wide (batched, tcgen05) plan: every Linear as an fp16 [nout, k]
+    matrix in the wide GEMM's tiled layout (cfb_wide_pack), with the LayerNorm that feeds it folded in (w = fp16(W16 * gamma),
     bias = b + W16 beta, the same folding as the persistent engine's packing), the time MLP
     evaluated at every Euler step, the path offsets side by side as [D, order * D], and the
     shortlist head [lm_head[sl] | markov.w2[sl]] as one [R, D + rank] matrix."""
@@ -244,6 +244,15 @@ class WideWeights:
         f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
         f16 = lambda t: t.to(device=dev, dtype=torch.float16).contiguous()
 
+        def pack(w16):
+            """row-major fp16 [nout, k] -> the wide GEMM's tiled layout (cfb_wide_pack)"""
+            nout, k = w16.shape
+            buf = torch.empty(self.lib.cfb_wide_packed_bytes(nout, k), dtype=torch.uint8, device=dev)
+            _lib.check(self.lib.cfb_wide_pack(w16.data_ptr(), w16.stride(0), nout, k, buf.data_ptr(),
+                                              stream.cuda_stream), "cfb_wide_pack")
+            self._keep.append(buf)
+            return buf
+
         def linear(w, b, ln=None):
             w16 = f16(w)
             bias = f32(b) if b is not None else torch.zeros(w16.shape[0], device=dev)
@@ -252,8 +261,9 @@ class WideWeights:
                 bias = bias + w16.float() @ beta
                 w16 = (w16.float() * g).to(torch.float16).contiguous()
             bias = bias.contiguous()
-            self._keep += [w16, bias]
-            return _lib.Linear(w16.data_ptr(), bias.data_ptr(), None, w16.shape[0], w16.shape[1])
+            self._keep.append(bias)
+            buf = pack(w16)          # w16 may be freed after this: the allocator orders reuse on the stream
+            return _lib.Linear(buf.data_ptr(), bias.data_ptr(), None, w16.shape[0], w16.shape[1])
 
         self.embed = f16(embed)
         self.vocab = self.embed.shape[0]
@@ -292,9 +302,9 @@ class WideWeights:
                                  ln=(sd[p + "out_norm.weight"], sd[p + "out_norm.bias"]))
             ex.blocks = C.cast(blocks, C.POINTER(_lib.Block))
         order = cfg.path_order
-        po = torch.cat([f16(sd[f"path_head.offset_proj.{j}.weight"]) for j in range(order)], dim=1).contiguous()
+        po = pack(torch.cat([f16(sd[f"path_head.offset_proj.{j}.weight"]) for j in range(order)], dim=1).contiguous())
         pb = torch.stack([f32(sd[f"path_head.offset_proj.{j}.bias"]) for j in range(order)]).contiguous()
-        self._keep += [po, pb]
+        self._keep.append(pb)
         self.path_offsets = _lib.Linear(po.data_ptr(), None, None, D, order * D)
         self.path_up = linear(sd["path_head.mlp.0.weight"], sd["path_head.mlp.0.bias"],
                               ln=(sd["path_head.norm.weight"], sd["path_head.norm.bias"]))
@@ -305,8 +315,10 @@ class WideWeights:
         head = torch.zeros(R, kh, dtype=torch.float16, device=dev)
         head[:, :D] = lm_head[rows].to(device=dev, dtype=torch.float16)
         head[:, D:D + rank] = f16(sd["markov.w2.weight"])[sl]
-        self._keep += [self.markov_w1, head]
-        self.head = _lib.Linear(head.data_ptr(), None, None, R, kh)
+        hp = pack(head)
+        self._keep.append(self.markov_w1)
+        self.head = _lib.Linear(hp.data_ptr(), None, None, R, kh)
+        del head
         self.R = R
         d = _lib.Drafter()
         d.hidden, d.heads, d.layers, d.steps = D, cfg.num_heads, cfg.num_drafter_layers, cfg.num_flow_steps

@@ -256,16 +256,24 @@ cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, con
  * C = A · Wᵀ on the sm_100a tensor cores (tcgen05.mma, fp16 in, fp32 accumulate in TMEM), fed by
  * 2-D TMA copies: the GEMM of the wide path, exported on its own for tests and for callers that
  * batch their own rows. This entry point has no counterpart in the reference.
- * a fp16 [M, K] with row stride lda; w fp16 [N, K] with row stride ldw; bias fp32 [N] or NULL.
+ * a fp16 [M, K] with row stride lda; w: an fp16 [N, ldw] matrix tiled by cfb_wide_pack (ldw a
+ * multiple of 64, K <= ldw: the first K columns are multiplied); bias fp32 [N] or NULL.
  * epi: CFB_EPI_F32    out fp32 [M, ldo] = A·Wᵀ + bias
  *      CFB_EPI_F16    out fp16 [M, ldo] = fp16(A·Wᵀ + bias)
  *      CFB_EPI_GELU16 out fp16 [M, ldo] = fp16(gelu(A·Wᵀ + bias))   (exact erf GELU)
  *      CFB_EPI_PART   out fp32 [s][M, ldo]: split-K partials (bias ignored); s = ceil(K/64 /
  *                     ceil(K/64 / splits)) splits, each over a contiguous range of 64-column blocks.
- * Supported: K a multiple of 64, N a multiple of 16, a/w/out/bias 16-byte aligned, lda and ldw
- * multiples of 8, ldo a multiple of 4. err: a device int that becomes non-zero if a bounded
+ * Supported: K a multiple of 64, N a multiple of 16, a/w/out/bias 16-byte aligned, lda a
+ * multiple of 8, ldo a multiple of 4. err: a device int that becomes non-zero if a bounded
  * device-side wait expired (outputs then invalid); it is never cleared by the library. */
 enum { CFB_EPI_F32 = 0, CFB_EPI_F16 = 1, CFB_EPI_GELU16 = 2, CFB_EPI_PART = 3 };
+/* The wide path's weight layout: an fp16 [nout, k] matrix (row stride ldw elements, k a multiple
+ * of 64) as ceil(nout/256) x (k/64) blocks of 256 rows x 64 columns, block (n, j) at element
+ * (n * k/64 + j) * 16384, each block the 128-byte-swizzled image the tensor cores read from shared
+ * memory (16-byte chunk c of block row r stored at chunk c ^ (r mod 8)); rows past nout are zero.
+ * One 32 KiB block per pipeline stage is one contiguous bulk copy. */
+size_t cfb_wide_packed_bytes(int nout, int k);
+cfb_status cfb_wide_pack(const void* w, int64_t ldw, int nout, int k, void* dst, void* stream);
 cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, const float* bias,
                          void* out, int64_t ldo, int M, int N, int K, int epi, int splits, int* err,
                          void* stream);
@@ -274,9 +282,10 @@ cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, int64_t ldw,
  * of kernel launches: tcgen05 GEMMs for every Linear (grouped over the chunk experts, split-K for
  * the residual projections), and row kernels for LayerNorm + residual updates, attention, the
  * path-token gather and the beam step. Same drafter description and run description as the
- * persistent plan, except that every cfb_linear.w is a ROW-MAJOR fp16 [nout, k] matrix (row
- * stride k) with the LayerNorm in front of it folded in (w = fp16(W * gamma), bias = b + W beta);
- * cfb_linear.colsum is unused. path_offsets is [D, order * D] (column block j = offset_proj.j),
+ * persistent plan, except that every cfb_linear.w is an fp16 [nout, k] matrix packed by
+ * cfb_wide_pack, with the LayerNorm in front of it folded in (w = fp16(W * gamma),
+ * bias = b + W beta); cfb_linear.colsum is unused. path_offsets is [D, order * D] (column block j
+ * = offset_proj.j),
  * head is [R, Kh] = [lm_head[sl] | markov.w2[sl] | 0], Kh >= D + markov_rank a multiple of 64
  * (zero columns pad it). Modes and outputs are those of
  * cfb_run; the row-sharded head (ranks > 1) is not supported here. The library keeps the launch

@@ -1,5 +1,6 @@
 """The wide path's tcgen05 GEMM (cfb_wide_gemm) against a torch fp32 matmul of the same fp16
-operands: every epilogue, ragged M and N (TMA zero fill past the edges), split-K partials."""
+operands: every epilogue, ragged M (TMA zero fill past the edge) and N (zero rows of the packed
+weights), split-K partials; and the weight packing (cfb_wide_pack) against its layout rule."""
 import ctypes as C
 
 import pytest
@@ -8,14 +9,24 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+def _pack(w):
+    from chain_flow_b200 import _lib
+    lib = _lib.load()
+    buf = torch.empty(lib.cfb_wide_packed_bytes(w.shape[0], w.shape[1]), dtype=torch.uint8, device=w.device)
+    _lib.check(lib.cfb_wide_pack(w.data_ptr(), w.stride(0), w.shape[0], w.shape[1], buf.data_ptr(),
+                                 _lib.stream_ptr()), "cfb_wide_pack")
+    return buf
+
+
 def _gemm(a, w, bias, epi, splits=1, out_dtype=torch.float32, nsplit=1):
     from chain_flow_b200 import _lib
     lib = _lib.load()
     M, K = a.shape
     N = w.shape[0]
+    wp = _pack(w)
     out = torch.zeros(nsplit, M, N, dtype=out_dtype, device=a.device).squeeze(0)
     err = torch.zeros(1, dtype=torch.int32, device=a.device)
-    _lib.check(lib.cfb_wide_gemm(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+    _lib.check(lib.cfb_wide_gemm(a.data_ptr(), a.stride(0), wp.data_ptr(), K,
                                  bias.data_ptr() if bias is not None else None, out.data_ptr(), N,
                                  M, N, K, epi, splits, err.data_ptr(), _lib.stream_ptr()), "cfb_wide_gemm")
     torch.cuda.synchronize()
@@ -68,3 +79,18 @@ def test_wide_gemm_split_k_partials_sum_to_the_product():
         ks = slice(s * 192, (s + 1) * 192)
         want = a[:, ks].float() @ w[:, ks].float().T
         assert float((parts[s] - want).abs().max() / want.abs().max()) < 1e-4
+
+
+def test_wide_pack_layout():
+    """Block (n, j) of 256 rows x 64 columns at element (n * K/64 + j) * 16384; row r's 16-byte
+    chunk c stored at chunk c ^ (r mod 8); rows past N zero."""
+    N, K = 300, 192
+    w = torch.arange(N * K, device="cuda", dtype=torch.float32).remainder(2039).half().view(N, K)
+    got = _pack(w).view(torch.float16).view(2, K // 64, 256, 8, 8).cpu()
+    wp = torch.zeros(512, K, dtype=torch.float16)
+    wp[:N] = w.cpu()
+    want = wp.view(2, 256, K // 64, 8, 8).permute(0, 2, 1, 3, 4)          # [nt, kb, r, chunk, 8]
+    r = torch.arange(256).view(256, 1)
+    c = torch.arange(8).view(1, 8)
+    src = (c ^ (r % 8)).view(1, 1, 256, 8, 1).expand(2, K // 64, 256, 8, 8)
+    assert torch.equal(got, torch.gather(want, 3, src))
