@@ -332,6 +332,42 @@ def run_ours(args, wl):
     h2d = h_ctx.numel() * h_ctx.element_size() + h_k0.numel() * h_k0.element_size()
     d2h = h_out.numel() * h_out.element_size()
 
+    # ---- the shortlist head alone (engine plans): a profiled run of the same plan. Each beam
+    # depth's head phase is the GEMM phase whose post-op publishes the head lists (the plan's
+    # phase table); its wall is from the previous phase's last grid-barrier pass to its own.
+    head = None
+    peak_hbm = measured_peaks()[0]
+    if not wide and not shard and rank == 0:
+        from chain_flow_b200.engine import Plan
+        pp = Plan(prop.weights, _lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH), width=wl.width, depth=wl.draft_tokens,
+                  profile=True, init_mode=_lib.INIT_MODES[prop.init_mode])
+        pp.ctx.copy_(plan.ctx); pp.z0.copy_(plan.z0); pp.known0.copy_(plan.known0)
+        for _ in range(2):
+            pp.run()
+        torch.cuda.synchronize(dev)
+        pp.check()
+        t = pp.phase_times().double()                       # [phases, grid, 20] ns
+        kinds = pp.phase_table()
+        ends = t[:, :, 2].max(dim=1).values
+        walls, streams = [], []
+        for i in range(1, t.shape[0]):
+            if int(kinds[i, 0]) == _lib.PK_GEMM and int(kinds[i, 6]) == _lib.PO_PUBLISH:
+                walls.append(float(ends[i] - ends[i - 1]) / 1e3)
+                has = t[i, :, 10] > 0
+                streams.append(float(t[i, has, 11].max() - ends[i - 1]) / 1e3)
+        hbytes = wl.shortlist_rows * (wl.hidden + wl.markov_rank) * 2
+        # plans of more than 2 requests run an engine build without the profiling stamps
+        if walls and min(walls) > 0 and min(streams) > 0:
+            w_us = statistics.median(walls)
+            s_us = statistics.median(streams)
+            head = {"depths": len(walls), "bytes_per_depth": hbytes, "us_per_depth": w_us,
+                    "achieved_gbs": hbytes / (w_us * 1e3), "frac": hbytes / (w_us * 1e3) / peak_hbm,
+                    "stream_us": s_us, "stream_gbs": hbytes / (s_us * 1e3),
+                    "how": "median over beam depths of the head phase's wall (previous phase's last barrier "
+                           "pass to its own), from a CFB_RUN_PROFILE run of the same plan; stream = to the "
+                           "last weight unit ready"}
+        del pp
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         n = args.cpu_drafts or (3 if wl.hidden >= 2560 else 20)
@@ -386,6 +422,7 @@ def run_ours(args, wl):
                           "kernel_ms": kernel_ms, "algorithmic_bytes_per_launch": algo,
                           "tflops": flops / (kernel_ms / 1e3) / 1e12}),
             "clocks": clk,
+            "shortlist_head": head,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

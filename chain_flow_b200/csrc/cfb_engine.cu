@@ -132,6 +132,7 @@ struct Job {
   const float* p0;                         // EK_PATHH: offset biases [order][D]
 };
 
+// a CFB_BUF_PHASES record (layout documented in cfb.h): int fields only
 struct Phase {
   int kind;
   int job0, njobs, nunits, ntiles;   // PK_ATTN: job0 / njobs index attention tasks, ntiles = tasks
@@ -139,6 +140,7 @@ struct Phase {
   int post;
   int step, rows, fr, keep, topb, base, base_prev, last;
 };
+static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
 
 // Dynamic shared memory, laid out per plan by the host: the ring of streamed units (each stage =
 // 16 KiB of packed weights + the unit's activation rows), mbarriers, the accumulator hand-off
@@ -1970,6 +1972,8 @@ cfb_status lower(Builder& B, size_t* bytes) {
       if (!X.pos || !X.temb) return CFB_ERR_INVALID_ARG;
     }
   }
+  P.buf[CFB_BUF_PHASES] = const_cast<cfb::Phase*>(P.phases);
+  P.buf_bytes[CFB_BUF_PHASES] = ph.size() * sizeof(cfb::Phase);
   if (profile) {
     P.prof = B.dptr<unsigned long long>(o_prof);
     P.buf[CFB_BUF_PROF] = P.prof; P.buf_bytes[CFB_BUF_PROF] = ph.size() * (size_t)G * cfb::kProfSlots * 8;

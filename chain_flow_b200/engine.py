@@ -125,6 +125,11 @@ class Plan:
         Needs a plan built with profile=True."""
         return self.buffer(_lib.BUF_PROF, torch.int64, (self.phases, self.grid, 20))
 
+    def phase_table(self) -> torch.Tensor:
+        """[phases, 15] int32 copy of the plan's phase table (CFB_BUF_PHASES in cfb.h): [:, 0] kind,
+        [:, 6] post-op."""
+        return self.buffer(_lib.BUF_PHASES, torch.int32, (self.phases, 15))
+
     def device_error(self) -> int:
         """Synchronous read of the plan's sticky device error word (0 = every run so far completed)."""
         v = C.c_int(0)

@@ -216,6 +216,13 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  *                     depth's rows gathered; [19] unused; written only by runs of plans built
  *                     with CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
+/* CFB_BUF_PHASES      int32 [phases, 15] the phase table: [0] kind (0 prep, 1 GEMM, 2 attention,
+ *                     3 beam, 4 rank merge), [1..5] first job, jobs, units, tiles, whole-tile flag,
+ *                     [6] post-op (0 none, 1 chain beam, 2 tree beam, 3 head lists published:
+ *                     the shortlist head GEMM of a beam depth), [7..14] step, rows, frontier,
+ *                     kept beams, top list length, node base, previous node base, last-depth
+ *                     flag. Read-only for the caller. */
+enum { CFB_BUF_PHASES = 9 };
 enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
        CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
 cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);

@@ -185,3 +185,17 @@ def test_batches_above_one_engine_plan_run_on_the_wide_plan():
         from beam_check import check_tree
         check_tree(tr, sd, ocfg, emb, hw, w2, sl, tp, known0.cpu(), 4, 4, 5)
     assert p.device_error() == 0
+
+
+def test_phase_table_marks_one_head_phase_per_depth():
+    """CFB_BUF_PHASES: a chain plan of depth K has K shortlist-head GEMM phases (post-op: lists
+    published), each followed by the beam phase of its depth."""
+    from chain_flow_b200 import _lib
+    from gpu_util import golden_weights, run_plan
+    g = load_golden("g64")
+    p = run_plan(golden_weights(g), _lib.MODE_CHAIN, g["B"], ctx=g["ctx"], z0=g["z0"], known0=g["known0"],
+                 width=4, depth=5)
+    t = p.phase_table()
+    heads = [i for i in range(t.shape[0]) if int(t[i, 0]) == _lib.PK_GEMM and int(t[i, 6]) == _lib.PO_PUBLISH]
+    assert len(heads) == 5
+    assert all(int(t[i + 1, 0]) == _lib.PK_BEAM for i in heads)
