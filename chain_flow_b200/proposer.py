@@ -25,6 +25,7 @@ import torch
 
 from . import _lib, shortlist as _sl
 from .engine import Plan, WidePlan
+from .ring import ContextRing
 from .weights import DraftConfig, DrafterWeights, WideWeights
 
 
@@ -58,9 +59,14 @@ class FlowDrafterProposer:
             raise _lib.CfbError("CF_TWOPASS_M > 0 (two-pass candidate head) is not implemented by this "
                                 "engine; set CF_TWOPASS_M=0 for the one-pass fused head")
         self.K = 5
+        self.max_reqs = 256                 # context-ring slots (the scheduler's max_num_seqs)
+        self._ring = None
         if vllm_config is not None:
             spec = vllm_config.speculative_config
             self.K = int(spec.num_speculative_tokens) - (1 if self.tree else 0)
+            sched = getattr(vllm_config, "scheduler_config", None)
+            if sched is not None and getattr(sched, "max_num_seqs", None):
+                self.max_reqs = int(sched.max_num_seqs)
         self.weights: DrafterWeights | None = None
         self._plans: dict = {}
         self._gen = None
@@ -76,7 +82,8 @@ class FlowDrafterProposer:
                         shortlist_ids: torch.Tensor | None = None, *, width: int | None = None, K: int = 5,
                         tree_keep: int | None = None, tree_topb: int | None = None,
                         tree_depth: int | None = None, device=None, seed: int = 0,
-                        head_shard: tuple[int, int] | None = None, group=None) -> "FlowDrafterProposer":
+                        head_shard: tuple[int, int] | None = None, group=None,
+                        max_reqs: int | None = None) -> "FlowDrafterProposer":
         """head_shard=(rank, ranks): this process packs only its share of the shortlist head rows
         and every draft all-gathers the ranks' merged top-k lists over `group` (torch.distributed,
         NCCL); all ranks must draft the same requests with the same inputs."""
@@ -104,6 +111,7 @@ class FlowDrafterProposer:
         if self.init_mode not in _lib.INIT_MODES:
             raise ValueError(f"init_mode {self.init_mode!r} is not one of {sorted(_lib.INIT_MODES)}")
         if width is not None: self.width = width
+        if max_reqs is not None: self.max_reqs = max_reqs
         if tree_keep is not None: self.tree_keep = tree_keep
         if tree_topb is not None: self.tree_topb = tree_topb
         if tree_depth is not None: self.tree_depth = tree_depth
@@ -225,6 +233,29 @@ class FlowDrafterProposer:
     def _beam_tree(self, ctx: torch.Tensor, known0: torch.Tensor) -> torch.Tensor:
         """[B, 2N] int64: N BFS-ordered draft tokens followed by their N parent indices (-1 = root)."""
         return self._run(_lib.MODE_TREE, ctx, known0.view(-1), "tokens")
+
+    # ------------------------------------------------------------------ context ring
+    def _init_ring(self, H: int):
+        """One ring slot of ctx_size hidden states per request slot (reference
+        flow_proposer.py:881-889), on the GPU kernels of chain_flow_b200.ring."""
+        self._ring = ContextRing(self.max_reqs, self.cfg.context_size, H, device=self.dev)
+
+    def _ring_write(self, sh, rows_g, starts_g, cnt_g, wmask_g, path_g, Kmax: int):
+        """Append each request's newly accepted hidden states to its slot (reference
+        flow_proposer.py:916-945): row j is sh[start + j] on a chain step, or the committed
+        token's row then the accepted path's rows (start + 1 + path[j - 1]) on a tree step."""
+        self._ring.write(sh, rows_g, starts_g, cnt_g, wmask_g, path_g, Kmax)
+
+    def _ring_gather(self, rows_g) -> torch.Tensor:
+        """[B, ctx_size, H] fp16 windows, oldest first, front-padded by repeating the oldest row
+        (reference flow_proposer.py:947-961)."""
+        return self._ring.gather(rows_g)
+
+    @torch.inference_mode()
+    def _draft_from_ring(self, rows_g, k0_g) -> torch.Tensor:
+        """The whole draft from the ring: gather the windows, then the chain or tree beam."""
+        ctx = self._ring_gather(rows_g)
+        return self._beam_tree(ctx, k0_g) if self.tree else self._beam_chains(ctx, k0_g)
 
     def device_error(self) -> int:
         """Synchronous: non-zero if a bounded device-side wait expired in any cached plan's last run."""

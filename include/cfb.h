@@ -259,6 +259,26 @@ cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, con
                                 float* o, int B, int N, int H, int Dk, int Dv, int use_l2norm,
                                 void* stream);
 
+/* ---- the per-request context ring -------------------------------------------------------------
+ * The window of the last C target hidden states each request's draft is conditioned on
+ * (reference FlowDrafterProposer._init_ring / _ring_write / _ring_gather,
+ * flow_proposer.py:881-961). ring fp16 [slots, C + 1, H] (row C: trash row), rpos / nval int64
+ * [slots] (next write position; valid rows <= C), all caller-owned, zero at start.
+ * cfb_ring_write appends, for each of B requests (ring slot rows[b]), rows j < kmax taken from
+ * the harvested hidden states sh fp16 [nsh, H]: sh[starts[b] + j] on a chain step (path NULL),
+ * or sh[starts[b]] then sh[starts[b] + 1 + path[rows[b] * path_ld + j - 1]] on a tree step
+ * (source rows clamped into sh); rows j >= cnt[b], and all rows of a request with wmask[b] == 0,
+ * go to the trash row; rpos advances by cnt[b] mod C and nval saturates at C.
+ * cfb_ring_gather writes out fp16 [B, C, H]: each slot's rows oldest first, front-padded by
+ * repeating the oldest row when fewer than C exist. Both only move fp16 rows; the slots of one
+ * call must be distinct. */
+cfb_status cfb_ring_write(void* ring, int64_t* rpos, int64_t* nval, int slots, int C, int H,
+                          const void* sh, int64_t nsh, const int64_t* rows, const int64_t* starts,
+                          const int64_t* cnt, const uint8_t* wmask, const int64_t* path,
+                          int64_t path_ld, int B, int kmax, void* stream);
+cfb_status cfb_ring_gather(const void* ring, const int64_t* rpos, const int64_t* nval, int slots,
+                           int C, int H, const int64_t* rows, int B, void* out, void* stream);
+
 /* ---- the wide (batched) drafting path ------------------------------------------------------
  * C = A · Wᵀ on the sm_100a tensor cores (tcgen05.mma, fp16 in, fp32 accumulate in TMEM), fed by
  * 2-D TMA copies: the GEMM of the wide path, exported on its own for tests and for callers that
