@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "gdn"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "gdn", "gdn-verify"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
@@ -493,10 +493,86 @@ def run_gdn(args):
         print(json.dumps(line), flush=True)
 
 
+def run_gdn_verify(args):
+    """The in-engine tree GDN verify of the reference's vLLM patch at its own shapes: one GDN
+    layer of the 4B target (16 key heads, 32 value heads, K = V = 128, fp32 state of 2 MiB per
+    slot), a 41-node draft tree per request (the reference's 40 + root) walked path-parallel from
+    the request's prefix slot, bf16 q/k/v. One JSON line per B in (1, 8). Algorithmic bytes per
+    request: its prefix state read once and 41 node states written (fp32), plus q/k/v/a/b/o."""
+    from chain_flow_b200.gdn import ancestor_chains, gdn_verify, make_tree
+    import oracle
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    N, H, HV, K, V, MAXD = 41, 16, 32, 128, 128, 6
+    peak, peak_kind = measured_peaks()
+    slot = HV * V * K * 4
+    per_req = slot * (1 + N) + N * (H * K * 2 * 2 + HV * V * 2 * 2 + HV * 8)
+    for B in (1, 8):
+        g = torch.Generator(device=dev).manual_seed(B)
+        T = B * N
+        q = torch.randn(T, H, K, device=dev, generator=g).bfloat16()
+        k = torch.randn(T, H, K, device=dev, generator=g).bfloat16()
+        v = torch.randn(T, HV, V, device=dev, generator=g).bfloat16()
+        a = torch.randn(T, HV, device=dev, generator=g)
+        b = torch.randn(T, HV, device=dev, generator=g)
+        A_log = torch.randn(HV, device=dev, generator=g) * 0.5
+        dt_bias = torch.randn(HV, device=dev, generator=g) * 0.5
+        chains, depths = [], []
+        for r in range(B):
+            par, _ = make_tree(N, MAXD, 4, seed=r)
+            ch, dp = ancestor_chains(par, MAXD)
+            chains.append(ch + r * N); depths.append(dp)
+        chain = torch.cat(chains).to(dev); depth = torch.cat(depths).to(dev)
+        init_slot = (torch.arange(T, device=dev) // N).to(torch.int32)            # request r's prefix: slot r
+        out_slot = (B + torch.arange(T, device=dev)).to(torch.int32)
+        state = torch.randn(B + T, HV, V, K, device=dev, generator=g) * 0.1
+        o = torch.empty(T, HV, V, device=dev, dtype=torch.bfloat16)
+        run = lambda: gdn_verify(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, out_slot, init_slot,
+                                 scale=K ** -0.5)
+        for _ in range(max(3, args.warmup)):
+            run()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        achieved = B * per_req / (ms / 1e3) / 1e9
+        # CPU baseline: the oracle's restatement of the reference kernel, one request, all threads
+        torch.set_num_threads(os.cpu_count() or 1)
+        sl = slice(0, N)
+        args_c = [t.cpu() for t in (A_log, dt_bias, a[sl], b[sl], q[sl], k[sl], v[sl])]
+        st_c = state[:1].cpu()
+        t0 = time.perf_counter()
+        oracle.tree_gdn_verify(*args_c, st_c, chain[sl].cpu(), depth[sl].cpu(), torch.zeros(N, dtype=torch.int32),
+                               torch.zeros(N, dtype=torch.int32), K ** -0.5, write_state=False)
+        cpu_s = time.perf_counter() - t0
+        line = {"metric": "in-engine tree GDN verify: requests/s (41-row trees, 32 value heads, K=V=128)",
+                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 state, bf16 q/k/v",
+                "data": "synthetic (seeded q,k,v,a,b,A_log,dt_bias,trees)",
+                "config": {"workload": "gdn-verify (reference in-engine shape)", "batch": B, "rows_per_request": N,
+                           "heads": H, "value_heads": HV, "dk": K, "dv": V},
+                "gpu_launches": args.steps,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                             "kernel": "tree_gdn_verify_kernel", "algorithmic_bytes_per_launch": B * per_req},
+                "cpu_baseline": {"value": 1.0 / cpu_s, "unit": "req/s", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": "1 request (41 rows), oracle fp32 on CPU"}}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.workload == "gdn":
         run_gdn(args)
+        return
+    if args.workload == "gdn-verify":
+        run_gdn_verify(args)
         return
     from chain_flow_b200.synthetic import WORKLOADS
     wl = WORKLOADS[args.workload]

@@ -29,7 +29,7 @@ EXPORTED = [
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
     "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_packed_bytes", "cfb_wide_pack", "cfb_wide_workspace",
     "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
-    "cfb_ring_write", "cfb_ring_gather",
+    "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify",
 ]
 ABI_VERSION = 2
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
@@ -114,6 +114,8 @@ def _declare(lib):
     lib.cfb_wide_destroy.restype = None
     lib.cfb_ring_write.argtypes = [vp, vp, vp, i32, i32, i32, vp, i64, vp, vp, vp, vp, vp, i64, i32, i32, vp]
     lib.cfb_ring_gather.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, vp, vp]
+    lib.cfb_tree_gdn_verify.argtypes = [vp, i32, vp, i32, vp, i32, vp, i32, vp, vp, vp, vp, i32, vp, i64, vp, i32,
+                                        vp, vp, vp, vp, C.c_float, i32, i32, i32, i32, i32, i32, i32, vp]
     return lib
 
 

@@ -14,6 +14,7 @@
 // coalesced along j) and re-read from there as a parent: the same thread wrote it.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
+#include <cuda_bf16.h>
 #include <cstdint>
 #include <mutex>
 
@@ -220,4 +221,212 @@ extern "C" cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const v
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), g, beta,
       parent, init, o, scratch, N, H, Dv, use_l2norm);
   return cfb_launch_status("tree_gdn_kernel (no-alloc)");
+}
+
+// =================================================================================================
+// The in-engine tree GDN verify: the contract of the reference's vLLM-patch kernel
+// (gdn_verify_kernel, src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4401-4562). The gate
+// comes from the model's raw parameters (decay exp(-exp(A_log) softplus(a + dt_bias)),
+// beta = sigmoid(b)), states live in slots [slots, HV, V, K] (K = 128 contiguous), and every
+// query row t re-walks its ancestor chain chain[t, depth[t]] .. chain[t, 0] from its initial
+// slot, then writes its output row and its state to its own slot.
+//
+// One CTA per (query row, value head, 128 value rows), one thread per value row holding the
+// row's 128 state values in registers: the walk needs no barrier and no cross-thread sum (and
+// two CTAs of 255 registers share an SM). Before it, the CTA stages the ancestor chain (at most
+// kMaxChain nodes) in shared memory: the node ids first, then, all loads at once, each node's
+// normalised key (fp32), decay and beta, the value column of every row, and the query. The
+// state rows move between global and shared memory as 512-byte rows (a warp per row), and
+// between shared memory and registers per thread (rows padded so the accesses spread over banks).
+namespace {
+
+enum { GV_F32 = 0, GV_F16 = 1, GV_BF16 = 2 };
+constexpr int kMaxChain = 16;              // nodes on one row's chain (tree depth + 1)
+constexpr int kVerifyRows = 128;           // value rows per CTA
+constexpr int kVerifyThreads = kVerifyRows;
+constexpr int kTileLd = kDk + 4;           // a staged row + 4 floats of padding
+constexpr int kVerifySmem = kVerifyRows * kTileLd * 4;
+
+__device__ __forceinline__ float ld_code(const void* p, int code, long long i) {
+  if (code == GV_F32) return static_cast<const float*>(p)[i];
+  if (code == GV_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ void from_f(__half& d, float x) { d = __float2half_rn(x); }
+__device__ __forceinline__ void from_f(__nv_bfloat16& d, float x) { d = __float2bfloat16_rn(x); }
+
+struct VerifyArgs {
+  const void* A_log; int c_alog;
+  const void* dt_bias; int c_dtb;
+  const void* a; int c_a;
+  const void* b; int c_b;
+  const void* q; const void* k; const void* v; void* o;
+  float* state; long long slot_stride;
+  const int* chain; int chain_stride;
+  const int* depth; const int* out_slot; const int* init_slot; const int* rows;
+  float scale, threshold;
+  int H, HV, V, write_out, write_state;
+};
+
+// shared-memory offset of state element (row r, key c)
+__device__ __forceinline__ int tile_off(int r, int c) { return r * kTileLd + c; }
+
+template <typename T>
+__global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const VerifyArgs A) {
+  __shared__ float4 ks[kMaxChain][kDk / 4];   // normalised keys, processing order (root first)
+  __shared__ float vs[kMaxChain][kVerifyRows];
+  __shared__ float egs[kMaxChain], bts[kMaxChain];
+  __shared__ float4 qs[kDk / 4];
+  __shared__ int chs[kMaxChain];              // the chain's node ids, processing order
+  extern __shared__ float st_tile[];          // [kVerifyRows][kTileLd]
+  const int tt = blockIdx.x, hv = blockIdx.y;
+  const int t = A.rows ? A.rows[tt] : tt;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = tid;                                      // value row of the CTA
+  const int vrow = blockIdx.z * kVerifyRows + r;
+  const int h = hv / (A.HV / A.H);
+  const T* q = static_cast<const T*>(A.q);
+  const T* k = static_cast<const T*>(A.k);
+  const T* v = static_cast<const T*>(A.v);
+  const int nd = min(A.depth[t] + 1, kMaxChain);
+  const float negA = -expf(ld_code(A.A_log, A.c_alog, hv));
+  const float dtb = ld_code(A.dt_bias, A.c_dtb, hv);
+  const long long crow = (long long)t * A.chain_stride;
+  const int vrows = min(kVerifyRows, A.V - (int)blockIdx.z * kVerifyRows);
+  constexpr int kWarps = kVerifyThreads / 32;
+  // the state rows of this CTA, row-contiguous from global memory (a warp per row)
+  {
+    const float4* src = reinterpret_cast<const float4*>(
+        A.state + (long long)A.init_slot[t] * A.slot_stride + ((long long)hv * A.V + blockIdx.z * kVerifyRows) * kDk);
+    for (int rr = warp; rr < vrows; rr += kWarps)
+      *reinterpret_cast<float4*>(&st_tile[tile_off(rr, lane * 4)]) = src[rr * (kDk / 4) + lane];
+  }
+  // the chain's node ids first, so that every later load of the CTA issues at once
+  if (tid < nd) chs[tid] = A.chain[crow + (nd - 1 - tid)];   // j = 0: the root end of the chain
+  __syncthreads();
+  // warp w takes nodes j = w, w + kWarps, ...; lane l holds key columns 4l .. 4l+3
+  for (int j = warp; j < nd; j += kWarps) {
+    const int n = chs[j];
+    const T* kr = k + ((long long)n * A.H + h) * kDk + lane * 4;
+    const float k0 = to_f(kr[0]), k1 = to_f(kr[1]), k2 = to_f(kr[2]), k3 = to_f(kr[3]);
+    float ss = (k0 * k0 + k1 * k1) + (k2 * k2 + k3 * k3);
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss + 1e-6f);
+    ks[j][lane] = make_float4(k0 * inv, k1 * inv, k2 * inv, k3 * inv);
+    if (lane == 0) {
+      const float x = ld_code(A.a, A.c_a, (long long)n * A.HV + hv) + dtb;
+      const float sp = x <= A.threshold ? log1pf(expf(x)) : x;
+      egs[j] = expf(negA * sp);
+      bts[j] = 1.f / (1.f + expf(-ld_code(A.b, A.c_b, (long long)n * A.HV + hv)));
+    }
+  }
+  for (int e = tid; e < nd * kVerifyRows; e += kVerifyThreads) {
+    const int j = e / kVerifyRows, rr = e - j * kVerifyRows;
+    const int n = chs[j];
+    const int vr = blockIdx.z * kVerifyRows + rr;
+    vs[j][rr] = vr < A.V ? to_f(v[((long long)n * A.HV + hv) * A.V + vr]) : 0.f;
+  }
+  if (A.write_out && warp == kWarps - 1) {
+    const T* qr = q + ((long long)t * A.H + h) * kDk + lane * 4;
+    const float q0 = to_f(qr[0]), q1 = to_f(qr[1]), q2 = to_f(qr[2]), q3 = to_f(qr[3]);
+    float ss = (q0 * q0 + q1 * q1) + (q2 * q2 + q3 * q3);
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss + 1e-6f) * A.scale;
+    qs[lane] = make_float4(q0 * inv, q1 * inv, q2 * inv, q3 * inv);
+  }
+  __syncthreads();
+  const bool live = vrow < A.V;
+  float S[kDk];
+  float* mine = &st_tile[r * kTileLd];
+#pragma unroll
+  for (int i = 0; i < kDk / 4; ++i) {
+    const float4 f = *reinterpret_cast<const float4*>(mine + 4 * i);
+    S[4 * i] = f.x; S[4 * i + 1] = f.y; S[4 * i + 2] = f.z; S[4 * i + 3] = f.w;
+  }
+  for (int j = 0; j < nd; ++j) {
+    const float eg = egs[j];
+    float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kDk / 4; ++i) {
+      const float4 kk = ks[j][i];
+      S[4 * i] *= eg; S[4 * i + 1] *= eg; S[4 * i + 2] *= eg; S[4 * i + 3] *= eg;
+      p0 += S[4 * i] * kk.x; p1 += S[4 * i + 1] * kk.y; p2 += S[4 * i + 2] * kk.z; p3 += S[4 * i + 3] * kk.w;
+    }
+    const float d = (vs[j][r] - ((p0 + p1) + (p2 + p3))) * bts[j];
+#pragma unroll
+    for (int i = 0; i < kDk / 4; ++i) {
+      const float4 kk = ks[j][i];
+      S[4 * i] += d * kk.x; S[4 * i + 1] += d * kk.y; S[4 * i + 2] += d * kk.z; S[4 * i + 3] += d * kk.w;
+    }
+  }
+  if (A.write_out) {
+    float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kDk / 4; ++i) {
+      const float4 qq = qs[i];
+      r0 += S[4 * i] * qq.x; r1 += S[4 * i + 1] * qq.y; r2 += S[4 * i + 2] * qq.z; r3 += S[4 * i + 3] * qq.w;
+    }
+    const float o = (r0 + r1) + (r2 + r3);
+    if (live) from_f(static_cast<T*>(A.o)[((long long)t * A.HV + hv) * A.V + vrow], o);
+  }
+  if (A.write_state) {
+    // own row into shared memory (each thread only ever touches its own row there after the
+    // barrier above), then every row back out row-contiguously
+#pragma unroll
+    for (int i = 0; i < kDk / 4; ++i)
+      *reinterpret_cast<float4*>(mine + 4 * i) = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    __syncthreads();
+    float4* dst = reinterpret_cast<float4*>(
+        A.state + (long long)A.out_slot[t] * A.slot_stride + ((long long)hv * A.V + blockIdx.z * kVerifyRows) * kDk);
+    for (int rr = warp; rr < vrows; rr += kWarps)
+      dst[rr * (kDk / 4) + lane] = *reinterpret_cast<const float4*>(&st_tile[tile_off(rr, lane * 4)]);
+  }
+}
+
+}  // namespace
+
+extern "C" cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, const void* dt_bias, int dt_bias_dtype,
+                                          const void* a, int a_dtype, const void* b, int b_dtype, const void* q,
+                                          const void* k, const void* v, void* o, int qkv_dtype, float* state,
+                                          int64_t slot_stride, const int32_t* chain, int chain_stride,
+                                          const int32_t* depth, const int32_t* out_slot, const int32_t* init_slot,
+                                          const int32_t* rows, float scale, int T_rows, int H, int HV, int K, int V,
+                                          int write_out, int write_state, void* stream) {
+  if (!A_log || !dt_bias || !a || !b || !q || !k || !v || !state || !chain || !depth || !out_slot || !init_slot ||
+      (write_out && !o) || T_rows < 0 || H <= 0 || HV <= 0 || chain_stride <= 0)
+    return CFB_ERR_INVALID_ARG;
+  for (int c : {A_log_dtype, dt_bias_dtype, a_dtype, b_dtype})
+    if (c < GV_F32 || c > GV_BF16) return CFB_ERR_INVALID_ARG;
+  if (K != kDk || V <= 0 || V % 32 || HV % H || chain_stride > kMaxChain ||
+      (qkv_dtype != GV_F16 && qkv_dtype != GV_BF16))
+    return CFB_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(state) & 15) || slot_stride < (int64_t)HV * V * K || slot_stride % 4)
+    return CFB_ERR_INVALID_ARG;
+  if (T_rows == 0) return CFB_OK;
+  VerifyArgs A{A_log, A_log_dtype, dt_bias, dt_bias_dtype, a, a_dtype, b, b_dtype, q, k, v, o, state,
+               slot_stride, chain, chain_stride, depth, out_slot, init_slot, rows, scale, 20.0f,
+               H, HV, V, write_out, write_state};
+  const dim3 grid((unsigned)T_rows, (unsigned)HV, (unsigned)((V + kVerifyRows - 1) / kVerifyRows));
+  {
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 64 && !done[dev]) {
+      if (cudaFuncSetAttribute(tree_gdn_verify_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kVerifySmem) != cudaSuccess ||
+          cudaFuncSetAttribute(tree_gdn_verify_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kVerifySmem) != cudaSuccess)
+        return cfb_launch_status("cudaFuncSetAttribute(tree_gdn_verify_kernel)");
+      done[dev] = true;
+    }
+  }
+  if (qkv_dtype == GV_F16)
+    tree_gdn_verify_kernel<__half><<<grid, kVerifyThreads, kVerifySmem, static_cast<cudaStream_t>(stream)>>>(A);
+  else
+    tree_gdn_verify_kernel<__nv_bfloat16><<<grid, kVerifyThreads, kVerifySmem, static_cast<cudaStream_t>(stream)>>>(A);
+  return cfb_launch_status("tree_gdn_verify_kernel");
 }

@@ -3,7 +3,9 @@
 ``tree_gated_delta_scan`` keeps the reference's signature and semantics
 (src/chain_flow/kernels/tree_scan.py:43-78) for a single tree, and ``tree_gdn_batched`` runs B
 independent trees in one launch. ``make_tree`` builds the seeded BFS parent arrays the
-benchmarks use (parent < child, bounded depth and branching).
+benchmarks use (parent < child, bounded depth and branching). ``gdn_verify`` is the in-engine
+variant of the reference's vLLM patch (gate from the model's raw parameters, slot-addressed
+states, a path-parallel walk of each row's ancestor chain; cfb_tree_gdn_verify).
 """
 from __future__ import annotations
 
@@ -69,3 +71,58 @@ def tree_gated_delta_scan(query, key, value, g, beta, parent, depth, initial_sta
     o, st = tree_gdn_batched(query[None], key[None], value[None], g[None], beta[None], par,
                              initial_state[None], use_qk_l2norm=use_qk_l2norm)
     return o[0], st[0]
+
+
+_DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def ancestor_chains(parent: torch.Tensor, max_depth: int):
+    """(chain [N, max_depth + 1] int32, depth [N] int32) from a parent array (parent < child,
+    -1 = root): chain[t, kk] is the ancestor kk levels above node t (chain[t, 0] = t), the layout
+    the in-engine verify walks from chain[t, depth[t]] (the root) down to t."""
+    p = parent.tolist()
+    N = len(p)
+    chain = torch.zeros(N, max_depth + 1, dtype=torch.int32)
+    depth = torch.zeros(N, dtype=torch.int32)
+    for t in range(N):
+        n, kk = t, 0
+        while True:
+            chain[t, kk] = n
+            if p[n] < 0:
+                break
+            n, kk = p[n], kk + 1
+        depth[t] = kk
+    return chain, depth
+
+
+def gdn_verify(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, out_slot, init_slot, rows=None, *,
+               scale: float, write_out: bool = True, write_state: bool = True) -> None:
+    """The in-engine tree GDN verify (reference vLLM patch ``gdn_verify``,
+    src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4606) on cfb_tree_gdn_verify: for
+    each query row (``rows``, default all), walk its ancestor chain from ``state[init_slot]``,
+    write o and ``state[out_slot]`` in place. q, k [T, H, 128] and v, o [T, HV, V] fp16 or
+    bf16; a, b [T, HV] and A_log, dt_bias [HV] fp32 / fp16 / bf16; state fp32
+    [slots, HV, V, 128]; chain, depth, slots, rows int32, all on one CUDA device."""
+    lib = _lib.load()
+    for t_, n in ((q, "q"), (k, "k"), (v, "v"), (state, "state"), (chain, "chain")):
+        _lib.require_cuda(t_, n)
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise _lib.CfbError("gdn_verify: q, k, v must share one dtype, fp16 or bf16")
+    if state.dtype != torch.float32 or state.stride(-1) != 1 or not state[0].is_contiguous():
+        raise _lib.CfbError("gdn_verify: state must be fp32 [slots, HV, V, K] with contiguous slots")
+    for t_ in (q, k, v, a, b, A_log, dt_bias):
+        if not t_.is_contiguous():
+            raise _lib.CfbError("gdn_verify: q, k, v, a, b, A_log, dt_bias must be contiguous")
+    ints = [t_.to(torch.int32).contiguous() for t_ in (chain, depth, out_slot, init_slot)]
+    rows_i = rows.to(torch.int32).contiguous() if rows is not None else None
+    T_rows = rows_i.numel() if rows_i is not None else q.shape[0]
+    H, K = q.shape[1], q.shape[2]
+    HV, V = v.shape[1], v.shape[2]
+    _lib.check(lib.cfb_tree_gdn_verify(
+        A_log.data_ptr(), _DTYPE_CODE[A_log.dtype], dt_bias.data_ptr(), _DTYPE_CODE[dt_bias.dtype],
+        a.data_ptr(), _DTYPE_CODE[a.dtype], b.data_ptr(), _DTYPE_CODE[b.dtype],
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr() if o is not None else None,
+        _DTYPE_CODE[q.dtype], state.data_ptr(), state.stride(0), ints[0].data_ptr(), ints[0].stride(0),
+        ints[1].data_ptr(), ints[2].data_ptr(), ints[3].data_ptr(),
+        rows_i.data_ptr() if rows_i is not None else None, float(scale), T_rows, H, HV, K, V,
+        int(write_out), int(write_state), _lib.stream_ptr()), "cfb_tree_gdn_verify")

@@ -239,6 +239,28 @@ cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, const float
                         float* o, float* states, int B, int N, int H, int Dk, int Dv,
                         int use_l2norm, void* stream);
 
+/* The in-engine tree GDN verify (the contract of the reference's vLLM-patch kernel,
+ * src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4401-4562 / gdn_verify :4606): every
+ * query row t re-walks its ancestor chain n = chain[t * chain_stride + kk], kk = depth[t] .. 0,
+ * from state slot init_slot[t]:
+ *   S <- S * exp(-exp(A_log[hv]) * softplus(a[n, hv] + dt_bias[hv]))   (softplus(x) = x above 20)
+ *   S <- S + sigmoid(b[n, hv]) * (v[n, hv] - S kn) (x) kn,   kn = k[n, h] * rsqrt(|k[n, h]|^2 + 1e-6)
+ * then o[t, hv] = S (q[t, h] * rsqrt(|q[t, h]|^2 + 1e-6) * scale) (write_out) and
+ * state[out_slot[t], hv] = S (write_state), h = hv / (HV / H).
+ * q, k [*, H, K] and v, o [*, HV, V] fp16 (qkv_dtype 1) or bf16 (2); a, b [*, HV] and A_log,
+ * dt_bias [HV] of dtype code 0 (fp32), 1 (fp16) or 2 (bf16); state fp32 [slots, HV, V, K] with
+ * slot stride slot_stride floats; chain, depth, out_slot, init_slot, rows int32; rows (may be
+ * NULL) selects the T_rows query rows. Out slots must not be read as init slots by other rows
+ * of the same call. Supported: K == 128, V a multiple of 32, HV a multiple of H. */
+cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, const void* dt_bias,
+                               int dt_bias_dtype, const void* a, int a_dtype, const void* b,
+                               int b_dtype, const void* q, const void* k, const void* v, void* o,
+                               int qkv_dtype, float* state, int64_t slot_stride,
+                               const int32_t* chain, int chain_stride, const int32_t* depth,
+                               const int32_t* out_slot, const int32_t* init_slot,
+                               const int32_t* rows, float scale, int T_rows, int H, int HV, int K,
+                               int V, int write_out, int write_state, void* stream);
+
 /* cfb_tree_gdn without the states buffer, allocating nothing. This entry point has no
  * counterpart in the reference.
  * It is for callers that cannot allocate device memory when they verify: the verify step runs

@@ -63,3 +63,53 @@ def path_gdn_output(q, k, v, g, beta, path, init, use_qk_l2norm=True):
     for n in path:
         S, o = _step(S, q[n:n + 1], k[n:n + 1], v[n:n + 1], g[n:n + 1], beta[n:n + 1])
     return o[0]
+
+
+def tree_gdn_verify(A_log, dt_bias, a, b, q, k, v, state, chain, depth, out_slot, init_slot, scale,
+                    rows=None, write_out=True, write_state=True, threshold=20.0):
+    """The in-engine tree GDN verify of the reference's vLLM patch (``gdn_verify_kernel``,
+    src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4401-4562, and the Triton
+    ``_tree_gdn_kernel`` it replaces, :3285-3385). Path-parallel: every query row t re-walks its
+    ancestor chain from its initial state slot:
+
+        S = state[init_slot[t], hv]                        (V x K, fp32)
+        for kk = depth[t] .. 0:  n = chain[t, kk]
+            kn = k[n, h] * rsqrt(||k[n, h]||^2 + 1e-6)
+            S  = S * exp(-exp(A_log[hv]) * softplus(a[n, hv] + dt_bias[hv]))   (softplus = x
+                                                                      above `threshold`)
+            S  = S + beta_n * (v[n, hv] - S kn) (x) kn,   beta_n = sigmoid(b[n, hv])
+        o[t, hv]  = S (q[t, h] * rsqrt(||q[t, h]||^2 + 1e-6) * scale)
+        state[out_slot[t], hv] = S
+
+    with h = hv // (HV // H). q, k [T, H, K]; v, o [T, HV, V]; a, b [T, HV]; A_log, dt_bias
+    [HV]; state [slots, HV, V, K]; chain [T, >= MAXD + 1]; depth, slots [T]; rows: the query
+    rows to run (default all). Returns (o [T, HV, V] fp32, new state); states are read from the
+    input `state` only."""
+    q, k, v, a, b = (t.float() for t in (q, k, v, a, b))
+    A_log, dt_bias = A_log.float(), dt_bias.float()
+    T, H, K = q.shape
+    HV, V = v.shape[1], v.shape[2]
+    rep = HV // H
+    st = state.float().clone()
+    o = torch.zeros(T, HV, V)
+    negA = -A_log.exp()
+    rr = range(T) if rows is None else [int(r) for r in rows]
+    for t in rr:
+        for hv in range(HV):
+            h = hv // rep
+            S = state[int(init_slot[t]), hv].float().clone()            # [V, K]
+            for kk in range(int(depth[t]), -1, -1):
+                n = int(chain[t, kk])
+                kn = k[n, h] * torch.rsqrt((k[n, h] * k[n, h]).sum() + 1e-6)
+                x = a[n, hv] + dt_bias[hv]
+                sp = torch.log1p(torch.exp(x)) if x <= threshold else x
+                S = S * torch.exp(negA[hv] * sp)
+                part = S @ kn                                              # [V]
+                beta = torch.sigmoid(b[n, hv])
+                S = S + ((v[n, hv] - part) * beta)[:, None] * kn[None, :]
+            if write_out:
+                qn = q[t, h] * torch.rsqrt((q[t, h] * q[t, h]).sum() + 1e-6) * scale
+                o[t, hv] = S @ qn
+            if write_state:
+                st[int(out_slot[t]), hv] = S
+    return o, st
