@@ -142,6 +142,12 @@ struct Phase {
 };
 static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
 
+// The cost of a cross-CTA split-tile fixup (publish, owner's bounded wait, sum), in streamed
+// units, for the whole-tiles-or-split choice of each GEMM phase.
+#ifndef CFB_FIXUP_UNITS
+#define CFB_FIXUP_UNITS 12
+#endif
+
 // Dynamic shared memory, laid out per plan by the host: the ring of streamed units (each stage =
 // 16 KiB of packed weights + the unit's activation rows), mbarriers, the accumulator hand-off
 // slots, the epilogue's scratch (attention / merge ids), one reduced tile, row statistics.
@@ -1577,7 +1583,7 @@ void add_phase(Builder& B, cfb::Phase ph, const std::vector<cfb::Job>& js) {
   if ((unsigned long long)u * (unsigned long long)(B.G + 1) >= (1ull << 32)) B.too_big = true;
   // Whole tiles per CTA (no cross-CTA fixup) unless splitting tiles finishes sooner even after
   // paying for the fixup, which costs about as much as streaming kFixupUnits units.
-  constexpr long long kFixupUnits = 6;
+  constexpr long long kFixupUnits = CFB_FIXUP_UNITS;
   long long nkc_max = 1;
   for (const auto& j : js) nkc_max = std::max<long long>(nkc_max, j.nkc);
   const long long G = B.G;
