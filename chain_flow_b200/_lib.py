@@ -29,7 +29,7 @@ EXPORTED = [
     "cfb_plan_error", "cfb_plan_info", "cfb_plan_buffer", "cfb_tree_gdn", "cfb_tree_gdn_noalloc",
     "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_packed_bytes", "cfb_wide_pack", "cfb_wide_workspace",
     "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
-    "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify",
+    "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify", "cfb_vae_workspace", "cfb_vae_create",
 ]
 ABI_VERSION = 2
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
@@ -78,6 +78,16 @@ class Run(C.Structure):
                 ("ranks", C.c_int), ("rank", C.c_int), ("xloc", C.c_void_p), ("xall", C.c_void_p)]
 
 
+class VaeLayer(C.Structure):
+    _fields_ = [("qkv", Linear), ("attn_out", Linear), ("ffn_up", Linear), ("ffn_down", Linear)]
+
+
+class VaeSide(C.Structure):
+    _fields_ = [("in_dim", C.c_int), ("width", C.c_int), ("out_dim", C.c_int), ("layers", C.c_int),
+                ("heads", C.c_int), ("max_len", C.c_int), ("in_proj", Linear), ("pos", C.c_void_p),
+                ("layer", C.POINTER(VaeLayer)), ("out_proj", Linear)]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -116,6 +126,8 @@ def _declare(lib):
     lib.cfb_ring_gather.argtypes = [vp, vp, vp, i32, i32, i32, vp, i32, vp, vp]
     lib.cfb_tree_gdn_verify.argtypes = [vp, i32, vp, i32, vp, i32, vp, i32, vp, vp, vp, vp, i32, vp, i64, vp, i32,
                                         vp, vp, vp, vp, C.c_float, i32, i32, i32, i32, i32, i32, i32, vp]
+    lib.cfb_vae_workspace.argtypes = [C.POINTER(VaeSide), i32, i32, i32, C.POINTER(sz)]
+    lib.cfb_vae_create.argtypes = [C.POINTER(VaeSide), i32, i32, i32, vp, vp, vp, sz, C.POINTER(vp)]
     return lib
 
 

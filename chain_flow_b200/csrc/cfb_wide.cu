@@ -433,7 +433,9 @@ enum LnMode : int {
   LN_RESID = 1,    // x32 += bias + sum_s part[s], then LN
   LN_PLAIN32 = 2,  // LN of an fp32 matrix
   LN_PLAIN16 = 3,  // LN of an fp16 matrix
-  LN_PATH = 4      // x = sum_s part[s] + sum_{j < nlive, lastp[r][j] >= 0} pbias[j] (PathHead offsets)
+  LN_PATH = 4,     // x = sum_s part[s] + sum_{j < nlive, lastp[r][j] >= 0} pbias[j] (PathHead offsets)
+  LN_POS = 5,      // x32[r] += pos[r % S] (learned positions after an in-projection), then LN
+  LN_CAST = 6      // out = fp16(x32), no normalisation (an fp32 input of a GEMM)
 };
 
 struct LnSeg {
@@ -497,8 +499,13 @@ __global__ void __launch_bounds__(kLnThreads) wide_ln_kernel(const __grid_consta
             acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
           }
         a.x += acc.x; a.y += acc.y; a.z += acc.z; a.w += acc.w;
-      } else if (S.mode == LN_PLAIN32) {
+      } else if (S.mode == LN_PLAIN32 || S.mode == LN_CAST) {
         a = *reinterpret_cast<const float4*>(S.x32 + (long long)r * D + c);
+      } else if (S.mode == LN_POS) {
+        a = *reinterpret_cast<const float4*>(S.x32 + (long long)r * D + c);
+        const float4 p = *reinterpret_cast<const float4*>(S.pos + (long long)(r % S.S) * D + c);
+        a.x += p.x; a.y += p.y; a.z += p.z; a.w += p.w;
+        *reinterpret_cast<float4*>(S.x32 + (long long)r * D + c) = a;
       } else if (S.mode == LN_PATH) {
 #pragma unroll
         for (int sp = 0; sp < kLnMaxSplit; ++sp)
@@ -521,6 +528,16 @@ __global__ void __launch_bounds__(kLnThreads) wide_ln_kernel(const __grid_consta
     }
     x[v] = a;
     sum += (a.x + a.y) + (a.z + a.w);
+  }
+  if (S.mode == LN_CAST) {
+#pragma unroll
+    for (int v = 0; v < kLnMaxV; ++v) {
+      const int c = (v * kLnThreads + threadIdx.x) * 4;
+      if (c < D)
+        *reinterpret_cast<uint2*>(S.out + (long long)r * D + c) =
+            make_uint2(pack_half2(x[v].x, x[v].y), pack_half2(x[v].z, x[v].w));
+    }
+    return;
   }
   const float mean = ln_block_sum(sum, red) / (float)D;
   float var = 0.f;
@@ -920,6 +937,50 @@ struct cfb_wide_plan {
 
 namespace {
 
+// The launch shape of a grouped GEMM (the same for every problem of the group): split-K only
+// when the group has fewer output tiles than SMs (one resident CTA per SM): as many splits as
+// fill the SMs, each of at least 4 k blocks, at most 8, and at most 4 for a non-partial
+// epilogue (whose last split reads every split's tile back from the fixup scratch fix_ws
+// [fix_floats] with arrival counters fix_cnt [fix_tiles], shared by a plan's launches, which run
+// one after another). A CTA covers one M tile; the kernel's two-tile mode (each weight block
+// feeding two M tiles) measured slower on these shapes, where it halves an already short grid.
+void shape_gemm(GemmLaunch& G, int nsm, float* fix_ws, size_t fix_floats, int* fix_cnt, int fix_tiles) {
+  bool part = true, fix_ok = true;
+  int tiles = 0, kmin = 1 << 30;
+  for (int i = 0; i < G.nprob; ++i) {
+    if (G.p[i].epi == EPI_HEAD) fix_ok = false;
+    if (G.p[i].epi != EPI_PART) part = false;
+    tiles += G.p[i].m_tiles * G.p[i].n_tiles;
+    kmin = std::min(kmin, G.p[i].kblocks);
+  }
+  int bs = 1;
+  if (tiles < nsm && (part || fix_ok)) {
+    bs = std::min(std::max(1, nsm / tiles), std::max(1, kmin / 4));
+    bs = std::min(bs, part ? 8 : 4);
+  }
+  size_t used = 0;
+  int ctile = 0;
+  for (int i = 0; i < G.nprob; ++i) {
+    GemmProb& p = G.p[i];
+    p.pair = 0;
+    p.m_pairs = p.m_tiles;
+    int s_ = std::min(bs, p.kblocks);
+    const size_t per = (size_t)p.m_pairs * p.n_tiles * 2 * BM * BN;
+    if (p.epi != EPI_PART) {
+      while (s_ > 1 && used + per * s_ > fix_floats) --s_;
+      if (s_ > 1 && ctile + p.m_pairs * p.n_tiles > fix_tiles) s_ = 1;
+    }
+    p.kb_per_split = (p.kblocks + s_ - 1) / s_;
+    p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
+    if (p.epi != EPI_PART && p.splits > 1) {
+      p.fix_ws = fix_ws + used;
+      p.fix_cnt = fix_cnt + ctile;
+      used += per * p.splits;
+      ctile += p.m_pairs * p.n_tiles;
+    }
+  }
+}
+
 cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wide_plan* P) {
   using std::min;
   if (!d || !r) return CFB_ERR_INVALID_ARG;
@@ -937,7 +998,8 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   if (flow && (r->init_mode < CFB_INIT_GIVEN || r->init_mode > CFB_INIT_DELTA || (r->init_mode == CFB_INIT_GIVEN && !r->z0)))
     return CFB_ERR_INVALID_ARG;
   if (!r->pred || (flow && !r->ctx) || (head && (!r->known0 || !r->tokens))) return CFB_ERR_INVALID_ARG;
-  const int hd = D / H, P2 = head ? d->path_up.nout : 0, FM = d->experts[0].blocks[0].ffn_up.nout / D;
+  if (flow && (!d->experts || !d->experts[0].blocks)) return CFB_ERR_INVALID_ARG;
+  const int hd = D / H, P2 = head ? d->path_up.nout : 0, FM = flow ? d->experts[0].blocks[0].ffn_up.nout / D : 0;
   const int Kh = head ? d->head.k : 0;     // head K: D + rank, padded with zero columns to a multiple of 64
   const int Wmax = tree ? std::max(1, r->tree_keep) : r->width;
   const int TB = tree ? r->tree_topb : r->width;
@@ -972,49 +1034,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   const int kFixTiles = 4096;
   float* fix_ws = bm.take<float>(kFixFloats);
   int* fix_cnt = bm.take<int>(kFixTiles);
-  // The launch shape of a grouped GEMM (the same for every problem of the group): split-K only
-  // when the group has fewer output tiles than SMs (one resident CTA per SM): as many splits as
-  // fill the SMs, each of at least 4 k blocks, at most 8, and at most 4 for a non-partial
-  // epilogue (whose last split reads every split's tile back). A CTA covers one M tile; the
-  // kernel's two-tile mode (each weight block feeding two M tiles) measured slower on these
-  // shapes, where it halves an already short grid.
-  auto shape = [&](GemmLaunch& G) {
-    bool part = true, fix_ok = true;
-    int tiles = 0, kmin = 1 << 30;
-    for (int i = 0; i < G.nprob; ++i) {
-      if (G.p[i].epi == EPI_HEAD) fix_ok = false;
-      if (G.p[i].epi != EPI_PART) part = false;
-      tiles += G.p[i].m_tiles * G.p[i].n_tiles;
-      kmin = std::min(kmin, G.p[i].kblocks);
-    }
-    int bs = 1;
-    if (tiles < nsm && (part || fix_ok)) {
-      bs = std::min(std::max(1, nsm / tiles), std::max(1, kmin / 4));
-      bs = std::min(bs, part ? 8 : 4);
-    }
-    const int bpair = 0;
-    size_t used = 0;
-    int ctile = 0;
-    for (int i = 0; i < G.nprob; ++i) {
-      GemmProb& p = G.p[i];
-      p.pair = bpair;
-      p.m_pairs = bpair ? (p.m_tiles + 1) / 2 : p.m_tiles;
-      int s_ = std::min(bs, p.kblocks);
-      const size_t per = (size_t)p.m_pairs * p.n_tiles * 2 * BM * BN;
-      if (p.epi != EPI_PART) {
-        while (s_ > 1 && used + per * s_ > kFixFloats) --s_;
-        if (s_ > 1 && ctile + p.m_pairs * p.n_tiles > kFixTiles) s_ = 1;
-      }
-      p.kb_per_split = (p.kblocks + s_ - 1) / s_;
-      p.splits = (p.kblocks + p.kb_per_split - 1) / p.kb_per_split;
-      if (p.epi != EPI_PART && p.splits > 1) {
-        p.fix_ws = fix_ws + used;
-        p.fix_cnt = fix_cnt + ctile;
-        used += per * p.splits;
-        ctile += p.m_pairs * p.n_tiles;
-      }
-    }
-  };
+  auto shape = [&](GemmLaunch& G) { shape_gemm(G, nsm, fix_ws, kFixFloats, fix_cnt, kFixTiles); };
   if (flow) {
     for (int i = 0; i < E * Lb; ++i) kvc[i] = bm.take<__half>((size_t)B * C * 2 * D);
     for (int e = 0; e < E; ++e) {
@@ -1302,6 +1322,179 @@ cfb_status wide_run_steps(cfb_wide_plan* P, cudaStream_t st) {
 }
 
 }  // namespace
+
+// ---- the VAE bridge of the production drafter -----------------------------------------------------
+// One side of the reference's TransformerHiddenVAE (encode: hidden -> mu; decode: latent ->
+// hidden; transformer_hidden.py:51-67) as a launch list on the wide kernels: in-projection
+// (+ bias, + learned positions), `layers` pre-LN encoder layers (bidirectional self-attention,
+// GELU FFN), the final LayerNorm folded into the out-projection.
+namespace {
+
+cfb_status vae_layout(const cfb_vae_side* v, int B, int rows, int decode, const void* in, void* out, Bump& bm,
+                      cfb_wide_plan* P) {
+  if (!v || B <= 0 || rows <= 0) return CFB_ERR_INVALID_ARG;
+  const int Hin = v->in_dim, Dw = v->width, Hout = v->out_dim, NL = v->layers, heads = v->heads;
+  if (Hin % 64 || Dw % 64 || Hout % 16 || NL < 0 || heads <= 0 || Dw % heads || (Dw / heads) % 8 ||
+      Dw / heads > 32 * 8 * kAttnMaxChunks || rows > kAttnMaxKeys || rows > v->max_len || Dw > 4 * kLnThreads * kLnMaxV ||
+      (decode && Hin > 4 * kLnThreads * kLnMaxV))
+    return CFB_ERR_UNSUPPORTED;
+  if (!in || !out || !v->pos || !v->in_proj.w || !v->out_proj.w || (NL > 0 && !v->layer)) return CFB_ERR_INVALID_ARG;
+  const int M = B * rows;
+  const int FF = NL > 0 ? v->layer[0].ffn_up.nout : 0;
+  int* err = bm.take<int>(64);
+  const size_t kFixFloats = (size_t)8 << 20;           // 32 MiB of split-K fixup tiles
+  const int kFixTiles = 1024;
+  float* fix_ws = bm.take<float>(kFixFloats);
+  int* fix_cnt = bm.take<int>(kFixTiles);
+  __half* inh = decode ? bm.take<__half>((size_t)M * Hin) : nullptr;
+  float* x32 = bm.take<float>((size_t)M * Dw);
+  __half* xh = bm.take<__half>((size_t)M * Dw);
+  __half* qkv = bm.take<__half>((size_t)M * 3 * Dw);
+  __half* ao = bm.take<__half>((size_t)M * Dw);
+  __half* u = bm.take<__half>((size_t)M * std::max(FF, 64));
+  float* part = bm.take<float>((size_t)8 * M * Dw);
+  if (!P) return CFB_OK;
+  P->err = err;
+  P->batch = B;
+  cfb_status st;
+  P->fix_cnt = fix_cnt;
+  P->fix_cnt_bytes = kFixTiles * sizeof(int);
+  auto add_gemm = [&](GemmLaunch& L, bool) {
+    L.err = err;
+    shape_gemm(L, P->nsm, fix_ws, kFixFloats, fix_cnt, kFixTiles);
+    P->gemms.push_back(L);
+    P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1});
+  };
+  auto add_ln = [&](LnLaunch& L, int D) {
+    L.D = D;
+    L.rows = 0;
+    for (int i = 0; i < L.nseg; ++i) { L.s[i].row0 = L.rows; L.rows += L.s[i].rows; }
+    P->lns.push_back(L);
+    P->steps.push_back({S_LN, (int)P->lns.size() - 1});
+  };
+  const __half* A0 = static_cast<const __half*>(in);
+  if (decode) {               // the latent arrives in fp32: an fp16 copy is the GEMM's input
+    LnLaunch L{};
+    L.nseg = 1;
+    LnSeg& g = L.s[0];
+    g.rows = M; g.mode = LN_CAST; g.x32 = const_cast<float*>(static_cast<const float*>(in)); g.out = inh;
+    add_ln(L, Hin);
+    A0 = inh;
+  }
+  {
+    GemmLaunch G{};
+    G.nprob = 1;
+    GemmProb& p = G.p[0];
+    if ((st = gemm_prob(p, A0, Hin, M, v->in_proj.w, v->in_proj.k, Dw, Hin, EPI_F32, 1)) != CFB_OK) return st;
+    p.bias = v->in_proj.bias; p.out = x32; p.ldo = Dw;
+    add_gemm(G, false);
+    LnLaunch L{};
+    L.nseg = 1;
+    LnSeg& g = L.s[0];
+    g.rows = M; g.mode = LN_POS; g.x32 = x32; g.pos = v->pos; g.S = rows; g.out = xh;
+    add_ln(L, Dw);
+  }
+  auto resid = [&](const float* bias, int nsplit) {
+    LnLaunch L{};
+    L.nseg = 1;
+    LnSeg& g = L.s[0];
+    g.rows = M; g.mode = LN_RESID; g.x32 = x32; g.part = part; g.nsplit = nsplit; g.split_stride = (long long)M * Dw;
+    g.bias = bias; g.out = xh;
+    add_ln(L, Dw);
+  };
+  for (int l = 0; l < NL; ++l) {
+    const cfb_vae_layer& ly = v->layer[l];
+    {
+      GemmLaunch G{};
+      G.nprob = 1;
+      GemmProb& p = G.p[0];
+      if ((st = gemm_prob(p, xh, Dw, M, ly.qkv.w, ly.qkv.k, 3 * Dw, Dw, EPI_F16, 1)) != CFB_OK) return st;
+      p.bias = ly.qkv.bias; p.out = qkv; p.ldo = 3 * Dw;
+      add_gemm(G, false);
+    }
+    {
+      AttnLaunch A{};
+      A.nseg = 1; A.H = heads; A.hd = Dw / heads; A.scale = 1.f / sqrtf((float)(Dw / heads));
+      AttnSeg& g = A.s[0];
+      g.S = rows; g.SK = rows; g.causal = 0;
+      g.q = qkv; g.ldq = 3 * Dw; g.qoff = 0; g.k = g.v = qkv; g.ldkv = 3 * Dw; g.koff = Dw; g.voff = 2 * Dw;
+      g.out = ao; g.ldo = Dw;
+      P->attns.push_back(A);
+      P->steps.push_back({S_ATTN, (int)P->attns.size() - 1});
+    }
+    {
+      GemmLaunch G{};
+      G.nprob = 1;
+      GemmProb& p = G.p[0];
+      if ((st = gemm_prob(p, ao, Dw, M, ly.attn_out.w, ly.attn_out.k, Dw, Dw, EPI_PART, 1)) != CFB_OK) return st;
+      p.out = part; p.ldo = Dw; p.split_stride = (long long)M * Dw;
+      add_gemm(G, true);
+      resid(ly.attn_out.bias, P->gemms.back().p[0].splits);
+    }
+    {
+      GemmLaunch G{};
+      G.nprob = 1;
+      GemmProb& p = G.p[0];
+      if ((st = gemm_prob(p, xh, Dw, M, ly.ffn_up.w, ly.ffn_up.k, FF, Dw, EPI_GELU16, 1)) != CFB_OK) return st;
+      p.bias = ly.ffn_up.bias; p.out = u; p.ldo = FF;
+      add_gemm(G, false);
+    }
+    {
+      GemmLaunch G{};
+      G.nprob = 1;
+      GemmProb& p = G.p[0];
+      if ((st = gemm_prob(p, u, FF, M, ly.ffn_down.w, ly.ffn_down.k, Dw, FF, EPI_PART, 1)) != CFB_OK) return st;
+      p.out = part; p.ldo = Dw; p.split_stride = (long long)M * Dw;
+      add_gemm(G, true);
+      resid(ly.ffn_down.bias, P->gemms.back().p[0].splits);
+    }
+  }
+  {
+    GemmLaunch G{};
+    G.nprob = 1;
+    GemmProb& p = G.p[0];
+    if ((st = gemm_prob(p, xh, Dw, M, v->out_proj.w, v->out_proj.k, Hout, Dw, decode ? EPI_F32 : EPI_F16, 1)) != CFB_OK)
+      return st;
+    p.bias = v->out_proj.bias; p.out = out; p.ldo = Hout;
+    add_gemm(G, false);
+  }
+  P->kernel_launches = (int)P->steps.size();
+  return CFB_OK;
+}
+
+}  // namespace
+
+extern "C" cfb_status cfb_vae_workspace(const cfb_vae_side* v, int batch, int rows, int decode, size_t* bytes) {
+  if (!bytes) return CFB_ERR_INVALID_ARG;
+  Bump bm{nullptr};
+  // shape checks need non-null I/O pointers: any non-null value serves the sizing pass
+  cfb_status st = vae_layout(v, batch, rows, decode, reinterpret_cast<void*>(16), reinterpret_cast<void*>(16), bm,
+                             nullptr);
+  if (st != CFB_OK) return st;
+  *bytes = bm.off + 256;
+  return CFB_OK;
+}
+
+extern "C" cfb_status cfb_vae_create(const cfb_vae_side* v, int batch, int rows, int decode, const void* in, void* out,
+                                     void* ws, size_t bytes, cfb_wide_plan** plan) {
+  if (!ws || !plan || (reinterpret_cast<uintptr_t>(ws) & 255)) return CFB_ERR_INVALID_ARG;
+  *plan = nullptr;
+  size_t need = 0;
+  cfb_status st = cfb_vae_workspace(v, batch, rows, decode, &need);
+  if (st != CFB_OK) return st;
+  if (bytes < need) return CFB_ERR_WORKSPACE;
+  if ((st = cfb::wide::init_device()) != CFB_OK) return st;
+  cfb_wide_plan* P = new cfb_wide_plan();
+  cudaGetDevice(&P->dev);
+  cudaDeviceGetAttribute(&P->nsm, cudaDevAttrMultiProcessorCount, P->dev);
+  Bump bm{static_cast<char*>(ws)};
+  st = vae_layout(v, batch, rows, decode, in, out, bm, P);
+  if (st == CFB_OK && cudaMemset(P->err, 0, sizeof(int)) != cudaSuccess) st = cfb_launch_status("cudaMemset");
+  if (st == CFB_OK && cudaMemset(P->fix_cnt, 0, P->fix_cnt_bytes) != cudaSuccess) st = cfb_launch_status("cudaMemset");
+  if (st != CFB_OK) { delete P; return st; }
+  *plan = P;
+  return CFB_OK;
+}
 
 extern "C" cfb_status cfb_wide_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes) {
   if (!bytes) return CFB_ERR_INVALID_ARG;

@@ -14,7 +14,9 @@ src/chain_flow/vllm_plugin/flow_proposer.py:328-2569) where the drafting path is
   (always on: it is exact).
 
 Every draft is ONE persistent kernel launch (flow + beam); there is no CPU fallback. The engine
-plans (and their graph-stable I/O buffers) are cached per (mode, batch).
+plans (and their graph-stable I/O buffers) are cached per (mode, batch). A production drafter
+(``TreeVAEFlowDrafter``: ``latent_size`` in the model args, ``vae.*`` weights) drafts as VAE
+encode -> latent flow -> VAE decode -> hidden-width beam (chain_flow_b200.vae).
 """
 from __future__ import annotations
 
@@ -26,6 +28,7 @@ import torch
 from . import _lib, shortlist as _sl
 from .engine import Plan, WidePlan
 from .ring import ContextRing
+from .vae import VaeConfig, VaeDraft, VaeWeights, is_vae_drafter
 from .weights import DraftConfig, DrafterWeights, WideWeights
 
 
@@ -68,6 +71,8 @@ class FlowDrafterProposer:
             if sched is not None and getattr(sched, "max_num_seqs", None):
                 self.max_reqs = int(sched.max_num_seqs)
         self.weights: DrafterWeights | None = None
+        self.vae: VaeWeights | None = None          # production (TreeVAEFlowDrafter) drafters only
+        self.flow_weights: DrafterWeights | None = None
         self._plans: dict = {}
         self._gen = None
         self.init_mode = "delta"
@@ -98,11 +103,23 @@ class FlowDrafterProposer:
         cfg = DraftConfig.from_model_args(args, hidden)
         if shortlist_ids is None:
             shortlist_ids = torch.arange(embed.shape[0])        # full head
+        self.vae = None
+        self.flow_weights = None
+        self.flow_cfg = cfg
+        if is_vae_drafter(state_dict, args):
+            # TreeVAEFlowDrafter (reference drafters/tree_vae_flow.py:91-175): the flow runs at the
+            # VAE's latent width (expert_dim is forced to latent_size), the beam at the hidden width
+            vcfg = VaeConfig.from_model_args(args, hidden)
+            self.flow_cfg = DraftConfig.from_model_args(args, vcfg.latent)
+            self.vae = VaeWeights(state_dict, vcfg, device=device)
+            self.flow_weights = DrafterWeights(state_dict, self.flow_cfg, None, None, None, device=device,
+                                               parts="flow")
         self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device,
-                                      head_shard=head_shard)
+                                      head_shard=head_shard, parts="head" if self.vae is not None else "all")
         # the wide plan's row-major weights are built on first use by a batch above MAX_PLAN_BATCH
         self._wide_src = None if head_shard is not None else (state_dict, embed, lm_head, shortlist_ids)
         self._wide_weights = None
+        self._wide_flow_weights = None
         self.group = group
         self.cfg = cfg
         self.dev = self.weights.dev
@@ -169,9 +186,13 @@ class FlowDrafterProposer:
         p = self._plans.get(key)
         if p is None:
             init = _lib.INIT_MODES[self.init_mode]
-            p = Plan(self.weights, mode, B, width=self.width,
-                     depth=self.tree_depth if mode == _lib.MODE_TREE else self.K,
-                     tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+            depth = self.tree_depth if mode == _lib.MODE_TREE else self.K
+            if self.vae is not None:
+                p = VaeDraft(self.vae, self.flow_weights, self.weights, mode, B, width=self.width, depth=depth,
+                             tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+            else:
+                p = Plan(self.weights, mode, B, width=self.width, depth=depth,
+                         tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
             self._plans[key] = p
         return p
 
@@ -183,11 +204,21 @@ class FlowDrafterProposer:
                 sd, embed, lm_head, ids = self._wide_src
                 if ids is None:
                     ids = torch.arange(embed.shape[0])
-                self._wide_weights = WideWeights(sd, self.cfg, embed, lm_head, ids, device=self.dev)
+                vae = self.vae is not None
+                self._wide_weights = WideWeights(sd, self.cfg, embed, lm_head, ids, device=self.dev,
+                                                 parts="head" if vae else "all")
+                if vae:
+                    self._wide_flow_weights = WideWeights(sd, self.flow_cfg, None, None, None, device=self.dev,
+                                                          parts="flow")
             init = _lib.INIT_MODES[self.init_mode]
-            p = WidePlan(self._wide_weights, mode, B, width=self.width,
-                         depth=self.tree_depth if mode == _lib.MODE_TREE else self.K,
-                         tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+            depth = self.tree_depth if mode == _lib.MODE_TREE else self.K
+            if self.vae is not None:
+                p = VaeDraft(self.vae, self._wide_flow_weights, self._wide_weights, mode, B, wide=True,
+                             width=self.width, depth=depth, tree_keep=self.tree_keep, tree_topb=self.tree_topb,
+                             init_mode=init)
+            else:
+                p = WidePlan(self._wide_weights, mode, B, width=self.width, depth=depth,
+                             tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
             self._plans[key] = p
         return p
 

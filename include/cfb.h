@@ -343,6 +343,32 @@ cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, int64_t ldw,
  * These entry points have no counterpart in the reference, whose batched drafts run its
  * per-layer PyTorch modules (reference cuda_block.py:382-431 for the fused expert). */
 typedef struct cfb_wide_plan cfb_wide_plan;
+
+/* The VAE bridge of the production drafter (reference TransformerHiddenVAE,
+ * src/chain_flow/vae/transformer_hidden.py:51-67, as TreeVAEFlowDrafter._encode / _decode use
+ * it, drafters/tree_vae_flow.py:163-175): one side (encoder or decoder) as a wide launch list.
+ * in_proj [width, in_dim] (+ bias) then learned positions pos fp32 [max_len, width]; `layers`
+ * pre-LN nn.TransformerEncoderLayer: qkv = self_attn.in_proj with norm1 folded in, attn_out =
+ * self_attn.out_proj, ffn_up = linear1 with norm2 folded in (GELU), ffn_down = linear2; out_proj
+ * with the side's final LayerNorm folded in (mu for the encoder, decoder_out for the decoder).
+ * Every cfb_linear.w is packed by cfb_wide_pack (k = the packed inner dimension). */
+typedef struct cfb_vae_layer { cfb_linear qkv, attn_out, ffn_up, ffn_down; } cfb_vae_layer;
+typedef struct cfb_vae_side {
+  int in_dim, width, out_dim, layers, heads, max_len;
+  cfb_linear in_proj;
+  const float* pos;
+  const cfb_vae_layer* layer;
+  cfb_linear out_proj;
+} cfb_vae_side;
+/* A plan of one side over `batch` requests of `rows` positions: encode (decode = 0) reads
+ * fp16 [batch, rows, in_dim] and writes fp16 [batch, rows, out_dim] (mu, the flow's context);
+ * decode (decode = 1) reads fp32 [batch, rows, in_dim] (the integrated latent) and writes fp32
+ * [batch, rows, out_dim] (the hidden states the head scores). The plan is run, checked and freed
+ * with cfb_wide_run / cfb_wide_error / cfb_wide_destroy. Supported: in_dim and width multiples of
+ * 64, out_dim a multiple of 16, width / heads a multiple of 8, rows <= 16 and <= max_len. */
+cfb_status cfb_vae_workspace(const cfb_vae_side* v, int batch, int rows, int decode, size_t* bytes);
+cfb_status cfb_vae_create(const cfb_vae_side* v, int batch, int rows, int decode, const void* in,
+                          void* out, void* ws, size_t bytes, cfb_wide_plan** plan);
 cfb_status cfb_wide_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes);
 cfb_status cfb_wide_create(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes,
                            cfb_wide_plan** plan);
