@@ -30,6 +30,7 @@ EXPORTED = [
     "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_packed_bytes", "cfb_wide_pack", "cfb_wide_workspace",
     "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
     "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify", "cfb_vae_workspace", "cfb_vae_create",
+    "cfb_vae_plan_workspace", "cfb_vae_plan_build",
 ]
 ABI_VERSION = 2
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
@@ -128,6 +129,8 @@ def _declare(lib):
                                         vp, vp, vp, vp, C.c_float, i32, i32, i32, i32, i32, i32, i32, vp]
     lib.cfb_vae_workspace.argtypes = [C.POINTER(VaeSide), i32, i32, i32, C.POINTER(sz)]
     lib.cfb_vae_create.argtypes = [C.POINTER(VaeSide), i32, i32, i32, vp, vp, vp, sz, C.POINTER(vp)]
+    lib.cfb_vae_plan_workspace.argtypes = [C.POINTER(VaeSide), i32, i32, i32, C.POINTER(sz)]
+    lib.cfb_vae_plan_build.argtypes = [C.POINTER(VaeSide), i32, i32, i32, vp, vp, vp, sz]
     return lib
 
 

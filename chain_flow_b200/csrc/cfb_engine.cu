@@ -68,14 +68,18 @@ constexpr int kBlockBytes = 512;                    // one 16x16 fp16 fragment t
 constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB
 constexpr int kMaxStages = 12;
 constexpr int kXRowBytes = 256;                     // activation row of a unit: 128 fp16
-constexpr int kSmemBudget = 232448 - 1024;          // dynamic + static shared memory per CTA
+constexpr int kSmemBudget = 232448 - 1024 - 2048;   // dynamic + static shared memory per CTA
 constexpr int kRowsMax = 64;                        // activation rows per job
 constexpr int kTopMax = 8;                          // top-k per beam row
 constexpr int kMaxExperts = 4;
 constexpr int kStatCols = 64;                       // columns per row-statistics part
 constexpr int kHeadPartFloats = 2 + 2 * kTopMax;
 static_assert(kRowsMax == CFB_XROWS && kHeadPartFloats == CFB_XFLOATS, "xloc layout of cfb.h");
-constexpr int kMaxSeg = 16;                         // launch segments of a plan (sharded heads)
+constexpr int kMaxSeg = 16;
+// Descriptor cache: the activation producer copies each phase's record and (up to kJobCache)
+// jobs into one of kDescBufs shared-memory slots a phase ahead, so that the roles do not wait on
+// the job table in global memory after a grid barrier (whose acquire leaves the L1 cold).
+constexpr int kJobCache = 4, kDescBufs = 3, kPhaseSlot = 64;                         // launch segments of a plan (sharded heads)
 
 enum XKind : int { XK_F16 = 0 };
 
@@ -88,7 +92,9 @@ CFB_DEV size_t tidx(int R, int r, int k) {
 }
 enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
 enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
-                   EK_HEADIN = 5, EK_HEAD = 6 };
+                   EK_HEADIN = 5, EK_HEAD = 6, EK_STORE16 = 7 };
+// the plan mode of a VAE side (cfb_vae_plan_build): not a cfb_mode the caller can ask for
+constexpr int kModeVae = 16;
 enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4 };
 enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
@@ -110,7 +116,7 @@ struct ExpertRT {
   const float* pos; const float* temb;
 };
 
-struct Job {
+struct alignas(16) Job {
   const uint4* w;
   int Mt, Kt, Kstride, nkc, rows, nout;
   int unit_base, tile_base;
@@ -141,6 +147,8 @@ struct Phase {
   int step, rows, fr, keep, topb, base, base_prev, last;
 };
 static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
+static_assert(sizeof(Phase) <= kPhaseSlot, "descriptor cache slot");
+static_assert(sizeof(Job) % 16 == 0 && kJobCache * sizeof(Job) / 16 <= 64, "descriptor cache copy");
 
 // The cost of a cross-CTA split-tile fixup (publish, owner's bounded wait, sum), in streamed
 // units, for the whole-tiles-or-split choice of each GEMM phase.
@@ -153,7 +161,7 @@ static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
 // slots, the epilogue's scratch (attention / merge ids), one reduced tile, row statistics.
 struct SmemLayout {
   int nstages, stage_bytes, rows_pad, nbuf;
-  int off_bar, off_slots, off_scratch, off_red, off_rowstat, off_tile, off_misc, total;
+  int off_bar, off_slots, off_scratch, off_red, off_rowstat, off_tile, off_misc, off_desc, total;
 };
 
 struct Plan {
@@ -178,6 +186,10 @@ struct Plan {
   int maxnt;                                // engine_kernel<maxnt> runs this plan
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
   unsigned long long* prof;                // [nphases][G][4] or NULL
+  // a VAE side (mode kModeVae): input rows [B * vS, vDin] (fp32 when vin32, else fp16), unit-
+  // tiled into vin16 by prep; the residual stream vx32 [B * vS, D] starts at pos[row % vS]
+  const void* vin; int vin32, vS, vDin;
+  __half* vin16; float* vx32; const float* vpos;
 };
 
 struct Smem {
@@ -191,6 +203,14 @@ struct Smem {
   float* tbias; float* tcsum;              // [kTileRows] bias / LayerNorm column sums of the tile
   int* flag;
   volatile int* phase_ready;               // the phase the workers have entered
+  volatile int* desc_ready;                // the last phase whose descriptors are cached
+  uint8_t* desc;                           // kDescBufs x (phase record slot + kJobCache jobs)
+  __device__ const Phase& dphase(int p) const {
+    return *reinterpret_cast<const Phase*>(desc + (size_t)(p % kDescBufs) * (kPhaseSlot + kJobCache * sizeof(Job)));
+  }
+  __device__ const Job* djobs(int p) const {
+    return reinterpret_cast<const Job*>(desc + (size_t)(p % kDescBufs) * (kPhaseSlot + kJobCache * sizeof(Job)) + kPhaseSlot);
+  }
   __device__ uint8_t* stage(int s) const { return ring + (size_t)s * stage_bytes; }
   __device__ float* slot(int b) const { return slots + (size_t)b * kMmaWarps * 16 * rp; }
 };
@@ -211,11 +231,12 @@ struct ProfClock {
   unsigned long long full = 0, slot = 0;
   unsigned long long first = 0, last = 0;   // when the phase's first / last unit was ready
   unsigned long long part = 0, atom = 0, fix = 0, tdone = 0;   // epilogue: last tile's events
+  unsigned long long rstat = 0;                                // epilogue: row statistics loaded
   bool on = false;
   CFB_DEV unsigned long long now() const { return on ? globaltimer() : 0ull; }
 };
 struct NoClock {
-  unsigned long long full, slot, first, last, part, atom, fix, tdone;
+  unsigned long long full, slot, first, last, part, atom, fix, tdone, rstat;
   static constexpr bool on = false;
   CFB_DEV unsigned long long now() const { return 0ull; }
 };
@@ -242,7 +263,22 @@ CFB_DEV int next_contributor(int c, long long U, int G) {
 }
 
 // grid barrier over the worker threads of all CTAs; bounded; false once an error is set
-CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W) {
+// Thread-0 side of waiting for phase `next`'s cached descriptors (filled by the activation
+// producer warp); false if the wait gave up or the plan failed.
+CFB_DEV bool desc_wait1(const Plan& P, volatile int* desc_ready, int next) {
+  if (*desc_ready >= next) { __threadfence_block(); return true; }
+  const unsigned long long t0 = globaltimer();
+  for (unsigned it = 1; *desc_ready < next; ++it) {
+    if (it % kPollsPerCheck) continue;
+    if (ld_volatile_int(P.err) != 0) return false;
+    if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_SLOT); return false; }
+  }
+  __threadfence_block();
+  return true;
+}
+
+// Grid barrier of the worker threads; then (next >= 0) phase `next`'s descriptors are cached.
+CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W, volatile int* desc_ready, int next) {
   gsync(W);
   __shared__ int s_ok;
   if (W.t == 0) {
@@ -260,7 +296,9 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W) {
         }
       }
     }
-    s_ok = (v & kBarErrBit) == 0u;
+    bool good = (v & kBarErrBit) == 0u;
+    if (good && next >= 0) good = desc_wait1(P, desc_ready, next);
+    s_ok = good;
   }
   gsync(W);
   return s_ok != 0;
@@ -499,6 +537,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
   const int col0 = tile * kTileRows;
   switch (J.ekind) {
     case EK_STORE:
+    case EK_STORE16:
     case EK_GELU16: {
       for (int e = E.t; e < kTileRows * rows; e += E.n) {
         const int r = e / kTileRows, f = e - r * kTileRows;      // consecutive threads: columns
@@ -506,6 +545,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
         if (col >= J.nout) continue;
         const float v = epi_val(S, f, r);
         if (J.ekind == EK_STORE) J.out32[(size_t)r * J.ldo + col] = v;
+        else if (J.ekind == EK_STORE16) J.out16[(size_t)r * J.ldo + col] = __float2half_rn(v);   // row-major
         else J.out16[tidx(J.oR, r, col)] = __float2half_rn(gelu_erf(v));
       }
       break;
@@ -761,18 +801,18 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
 // slot buffer j the j-th tile.
 struct UnitRange { long long u0, u1; };
 // first unit of the phase's t-th tile (tiles are numbered across the phase's jobs)
-CFB_DEV long long tile_unit(const Plan& P, const Phase& ph, long long t) {
+CFB_DEV long long tile_unit(const Phase& ph, const Job* jt, long long t) {
   if (t >= ph.ntiles) return ph.nunits;
   for (int jx = ph.njobs - 1; jx >= 0; --jx) {
-    const Job& J = P.jobs[ph.job0 + jx];
+    const Job& J = jt[jx];
     if (t >= J.tile_base) return J.unit_base + (t - J.tile_base) * J.nkc;
   }
   return 0;
 }
-CFB_DEV UnitRange cta_units(const Plan& P, const Phase& ph) {
+CFB_DEV UnitRange cta_units(const Plan& P, const Phase& ph, const Job* jt) {
   if (ph.whole) {
     const long long T = ph.ntiles;
-    return {tile_unit(P, ph, cta_start(T, P.G, blockIdx.x)), tile_unit(P, ph, cta_start(T, P.G, blockIdx.x + 1))};
+    return {tile_unit(ph, jt, cta_start(T, P.G, blockIdx.x)), tile_unit(ph, jt, cta_start(T, P.G, blockIdx.x + 1))};
   }
   const long long U = ph.nunits;
   return {cta_start(U, P.G, blockIdx.x), cta_start(U, P.G, blockIdx.x + 1)};
@@ -893,10 +933,11 @@ CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci
 // instantiation carries only the MMA loops its plans can need: wider variants cost registers
 // (spills) and instruction-cache room in every phase.
 template <int MAXNT, class WaitClock>
-CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& tseq, Smem& S, WaitClock& wc) {
-  const UnitRange cu = cta_units(P, ph);
+CFB_DEV void mma_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& ci, uint32_t& tseq, Smem& S,
+                       WaitClock& wc) {
+  const UnitRange cu = cta_units(P, ph, jt);
   for (int jx = 0; jx < ph.njobs; ++jx) {
-    const Job& J = P.jobs[ph.job0 + jx];
+    const Job& J = jt[jx];
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
     const int nt = (J.rows + 7) / 8;
@@ -910,15 +951,16 @@ CFB_DEV void mma_phase(const Plan& P, const Phase& ph, uint32_t& ci, uint32_t& t
 
 // Epilogue warps: the same tiles in the same order.
 template <class WaitClock>
-CFB_DEV void epi_phase(const Plan& P, const Phase& ph, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
-                       WaitClock& wc) {
+CFB_DEV void epi_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& tseq, Smem& S, HeadState& H,
+                       const Grp& E, WaitClock& wc) {
   const long long U = ph.nunits;
-  const UnitRange cu = cta_units(P, ph);
+  const UnitRange cu = cta_units(P, ph, jt);
   for (int jx = 0; jx < ph.njobs; ++jx) {
-    const Job& J = P.jobs[ph.job0 + jx];
+    const Job& J = jt[jx];
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
     job_rowstats(J, S, E);
+    if (wc.on) wc.rstat = wc.now();
     for (int tile = ju0 / J.nkc; tile <= (ju1 - 1) / J.nkc; ++tile) {
       const bool complete = (ju0 <= tile * J.nkc) && (ju1 >= (tile + 1) * J.nkc);
       epi_tile(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, tseq, S, H, E, wc);
@@ -940,9 +982,10 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
     unsigned long long waited = 0;
-    const UnitRange cu = cta_units(P, ph);
+    const Job* jt = P.jobs + ph.job0;
+    const UnitRange cu = cta_units(P, ph, jt);
     for (int jx = 0; jx < ph.njobs && ok; ++jx) {
-      const Job& J = P.jobs[ph.job0 + jx];
+      const Job& J = jt[jx];
       int ju0, ju1;
       if (!job_slice(J, cu, ju0, ju1)) continue;
       const int nkc = J.nkc, Kt = J.Kt;
@@ -986,16 +1029,54 @@ CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
   bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes, full);
 }
 
+// The descriptor cache slot of phase p (one thread): the phase record, then, for a GEMM phase of
+// at most kJobCache jobs, its jobs, 16 loads in flight at a time; published through
+// S.desc_ready.
+CFB_DEV void desc_fill(const Plan& P, Smem& S, int p) {
+  uint8_t* slot = S.desc + (size_t)(p % kDescBufs) * (kPhaseSlot + kJobCache * sizeof(Job));
+  constexpr int kPhInts = (int)(sizeof(Phase) / sizeof(int));
+  const int* ps = reinterpret_cast<const int*>(P.phases + p);
+  int v[kPhInts];
+#pragma unroll
+  for (int i = 0; i < kPhInts; ++i) v[i] = __ldcg(ps + i);
+#pragma unroll
+  for (int i = 0; i < kPhInts; ++i) reinterpret_cast<int*>(slot)[i] = v[i];
+  const int kind = v[0], job0 = v[1], njobs = v[2];
+  if (kind == PK_GEMM && njobs <= kJobCache) {
+    const int n16 = njobs * (int)(sizeof(Job) / 16);
+    const uint4* src = reinterpret_cast<const uint4*>(P.jobs + job0);
+    uint4* dst = reinterpret_cast<uint4*>(slot + kPhaseSlot);
+    for (int i0 = 0; i0 < n16; i0 += 16) {
+      uint4 t[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i0 + i < n16) t[i] = __ldcg(src + i0 + i);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i0 + i < n16) dst[i0 + i] = t[i];
+    }
+  }
+  __threadfence_block();
+  *S.desc_ready = p;
+}
+
+// The jobs of cached phase p (the descriptor cache, or the global table beyond kJobCache jobs).
+CFB_DEV const Job* phase_jobs(const Plan& P, const Smem& S, const Phase& ph, int p) {
+  return ph.njobs <= kJobCache ? S.djobs(p) : P.jobs + ph.job0;
+}
+
+// Activation producer (one thread): copies the activation rows of this CTA's units, and fills
+// the descriptor cache a phase ahead of the workers. At the top of iteration p it fills phase
+// p + 1's slot, which last held phase p - 2: the workers are past it, since iteration p - 1
+// waited for them to enter phase p - 1.
 CFB_DEV void x_producer(const Plan& P, Smem& S, int p0, int p1) {
   uint32_t xi = 0;            // units issued
   int xstage = 0;
   uint32_t xpar = 1u;         // a fresh mbarrier's previous phase counts as complete
   bool ok = true;
+  desc_fill(P, S, p0);
   for (int p = p0; p < p1 && ok; ++p) {
-    const Phase& ph = P.phases[p];
-    if (ph.kind != PK_GEMM) continue;
-    const UnitRange cu = cta_units(P, ph);
-    if (cu.u0 >= cu.u1) continue;
+    if (p + 1 < p1) desc_fill(P, S, p + 1);
     // wait until the workers have passed the grid barrier in front of phase p
     const unsigned long long t0 = globaltimer();
     for (unsigned it = 1; *S.phase_ready < p; ++it) {
@@ -1003,13 +1084,17 @@ CFB_DEV void x_producer(const Plan& P, Smem& S, int p0, int p1) {
       if (ld_volatile_int(P.err) != 0) { ok = false; break; }
       if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_SLOT); ok = false; break; }
     }
-    if (!ok) break;
+    const Phase& ph = S.dphase(p);
+    if (!ok || ph.kind != PK_GEMM) continue;
+    const Job* jt = phase_jobs(P, S, ph, p);
+    const UnitRange cu = cta_units(P, ph, jt);
+    if (cu.u0 >= cu.u1) continue;
     // the rows were written by other SMs with ordinary stores; order them before the copy
     // engine (async proxy) reads them
     __threadfence();
     fence_proxy_async_global();
     for (int jx = 0; jx < ph.njobs && ok; ++jx) {
-      const Job& J = P.jobs[ph.job0 + jx];
+      const Job& J = jt[jx];
       int ju0, ju1;
       if (!job_slice(J, cu, ju0, ju1)) continue;
       for (int ju = ju0; ju < ju1; ++ju) {
@@ -1084,6 +1169,21 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
   const long long gtid = (long long)blockIdx.x * W.n + W.t;
   const long long gthreads = (long long)P.G * W.n;
   for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
+  if (P.mode == kModeVae) {
+    // the input rows, unit-tiled for the in-projection's activation copies; the residual stream
+    // starts at the learned position rows (the in-projection adds to it)
+    const int Din = P.vDin, D = P.D, M = P.B * P.vS;
+    for (long long i = gtid; i < (long long)M * Din; i += gthreads) {
+      const int r = (int)(i / Din), c = (int)(i % Din);
+      const __half h = P.vin32 ? __float2half_rn(static_cast<const float*>(P.vin)[i]) : static_cast<const __half*>(P.vin)[i];
+      P.vin16[tidx(M, r, c)] = h;
+    }
+    for (long long i = gtid; i < (long long)M * D; i += gthreads) {
+      const int r = (int)(i / D), c = (int)(i % D);
+      P.vx32[i] = P.vpos[(size_t)(r % P.vS) * D + c];
+    }
+    return;
+  }
   const bool flow = (P.mode == CFB_MODE_FLOW || P.mode == CFB_MODE_CHAIN || P.mode == CFB_MODE_TREE);
   const int D = P.D, nparts = D / kStatCols;
   if (flow) {
@@ -1394,6 +1494,16 @@ __device__ __noinline__ void beam_phase(const Plan& P, const Phase& ph, Smem& S,
 // line, so the GEMM path stays compact in the instruction cache.
 template <int MAXNT>
 __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restrict__ Pp, int p0, int p1) {
+  // The plan record stays in global memory: passed by value (a __grid_constant__ parameter) it
+  // measured slower on the head phase (75 vs 68 us a depth at the 4B shape). Each CTA keeps a
+  // copy in shared memory instead: a grid barrier's acquire leaves the L1 cold, and every role
+  // reads plan fields right after one.
+  __shared__ __align__(16) Plan s_plan;
+  static_assert(sizeof(Plan) % 8 == 0 && sizeof(Plan) <= 2048, "plan copy");
+  for (int i = threadIdx.x; i < (int)(sizeof(Plan) / 8); i += blockDim.x)
+    reinterpret_cast<uint64_t*>(&s_plan)[i] = __ldcg(reinterpret_cast<const unsigned long long*>(Pp) + i);
+  __syncthreads();
+  const Plan& P = s_plan;
   // The narrow classes (jobs of <= 16 rows) measured faster with the per-phase profiling
   // switched at run time (CFB_RUN_PROFILE); the wider ones with the profiling compiled out
   // (their plans record no stamps), which frees registers. Results are the same.
@@ -1401,7 +1511,6 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   constexpr bool kProf = !kLean;                  // profiling code present in this instantiation
   using WaitClock = typename std::conditional<kProf, ProfClock, NoClock>::type;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const Plan& P = *Pp;
   const SmemLayout L = P.sm;
   Smem S;
   S.ring = smem_raw; S.nstages = L.nstages; S.stage_bytes = L.stage_bytes; S.rp = L.rows_pad; S.nbuf = L.nbuf;
@@ -1417,12 +1526,15 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   S.tcsum = S.tbias + kTileRows;
   S.flag = reinterpret_cast<int*>(smem_raw + L.off_misc);
   S.phase_ready = reinterpret_cast<volatile int*>(smem_raw + L.off_misc + 4);
+  S.desc_ready = reinterpret_cast<volatile int*>(smem_raw + L.off_misc + 8);
+  S.desc = smem_raw + L.off_desc;
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
     // full: the weight producer's expect_tx arrive + the activation producer's arrive
     for (int i = 0; i < L.nstages; ++i) { mbar_init(&S.full[i], 2); mbar_init(&S.empty[i], kMmaWarps); }
     for (int i = 0; i < 2; ++i) { mbar_init(&S.accf[i], kMmaWarps); mbar_init(&S.acce[i], 1); }
     *S.phase_ready = -1;
+    *S.desc_ready = -1;
     // a plan whose earlier run failed stays failed: this run leaves every output untouched
     *S.flag = ld_volatile_int(P.err) != 0;
     fence_mbar_init();
@@ -1447,15 +1559,22 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   const bool rec = kProf && P.prof && ((!is_epi && tid == 0) || (is_epi && E.t == 0));
   HeadState H;                   // the head phases' per-row (max, sumexp, top-k) of this thread
   head_reset(H);
+  if (ok) {                      // the first phase's descriptors
+    __shared__ int s_first;
+    if (Wk.t == 0) s_first = desc_wait1(P, S.desc_ready, p0);
+    gsync(Wk);
+    ok = s_first != 0;
+  }
   for (int p = p0; p < p1 && ok; ++p) {
-    const Phase& ph = P.phases[p];
+    const Phase& ph = S.dphase(p);
+    const Job* jt = ph.kind == PK_GEMM ? phase_jobs(P, S, ph, p) : nullptr;
     unsigned long long* prow = kProf && P.prof ? P.prof + ((size_t)p * P.G + blockIdx.x) * kProfSlots : nullptr;
     unsigned long long* stamp = (kProf && P.prof && Wk.t == 0) ? prow : nullptr;
     WaitClock wc;
     if constexpr (kProf) {
       wc.on = rec;
       wc.full = wc.slot = wc.first = wc.last = 0;
-      wc.part = wc.atom = wc.fix = wc.tdone = 0;
+      wc.part = wc.atom = wc.fix = wc.tdone = wc.rstat = 0;
     }
     if (stamp) stamp[0] = globaltimer();
     if (Wk.t == 0) *S.phase_ready = p;
@@ -1470,19 +1589,20 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     } else {
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
-        epi_phase(P, ph, tseq, S, H, E, wc);
+        epi_phase(P, ph, jt, tseq, S, H, E, wc);
         if (ph.post != PO_NONE) head_post(P, ph, H, E);
         if (rec) {
           prow[5] = wc.slot; prow[6] = globaltimer();
           prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
+          prow[19] = wc.rstat;
         }
       } else {
-        mma_phase<MAXNT, WaitClock>(P, ph, ci, tseq, S, wc);
+        mma_phase<MAXNT, WaitClock>(P, ph, jt, ci, tseq, S, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
     if (stamp) stamp[1] = globaltimer();
-    ok = grid_sync(P, epoch, Wk);
+    ok = grid_sync(P, epoch, Wk, S.desc_ready, p + 1 < p1 ? p + 1 : -1);
     if (stamp) stamp[2] = globaltimer();
   }
   if (Wk.t == 0) {
@@ -1545,6 +1665,10 @@ struct Builder {
   int max_tiles = 0;
   bool too_big = false;          // a phase's units x grid overflows the kernel's 32-bit range math
   int G = 148;                   // persistent grid the phases are cut for
+  // a VAE side plan (cfb_vae_plan_build): d / r are stand-ins carrying D, batch and rows
+  const cfb_vae_side* vae = nullptr;
+  int vrows = 0, vdecode = 0;
+  const void* vin = nullptr; void* vout = nullptr;
   template <class T> T* dptr(size_t off) { return reinterpret_cast<T*>(base + off); }
 };
 
@@ -1599,10 +1723,30 @@ cfb_status lower(Builder& B, size_t* bytes) {
   const cfb_run& r = *B.r;
   const int D = d.hidden, Bq = r.batch, C = d.ctx_rows, DL = d.draft_len, E = d.n_experts;
   const int mode = r.mode;
-  if (mode < CFB_MODE_FLOW || mode > CFB_MODE_BEAM_TREE) return CFB_ERR_INVALID_ARG;
-  const bool flow = mode == CFB_MODE_FLOW || mode == CFB_MODE_CHAIN || mode == CFB_MODE_TREE;
-  const bool beam = mode != CFB_MODE_FLOW;
-  const bool tree = mode == CFB_MODE_TREE || mode == CFB_MODE_BEAM_TREE;
+  const bool vae = B.vae != nullptr;
+  if (vae ? mode != cfb::kModeVae : (mode < CFB_MODE_FLOW || mode > CFB_MODE_BEAM_TREE)) return CFB_ERR_INVALID_ARG;
+  const bool flow = !vae && (mode == CFB_MODE_FLOW || mode == CFB_MODE_CHAIN || mode == CFB_MODE_TREE);
+  const bool beam = !vae && mode != CFB_MODE_FLOW;
+  const bool tree = !vae && (mode == CFB_MODE_TREE || mode == CFB_MODE_BEAM_TREE);
+  if (vae) {
+    const cfb_vae_side& v = *B.vae;
+    const int S = B.vrows, FF = v.layers > 0 ? v.layer[0].ffn_up.nout : 64;
+    if (!B.vin || !B.vout || !v.pos || (v.layers > 0 && !v.layer)) return CFB_ERR_INVALID_ARG;
+    if (v.in_dim <= 0 || v.in_dim % 16 || v.width != D || v.out_dim <= 0 || v.out_dim % 16 || v.layers < 0 ||
+        v.heads <= 0 || D % v.heads || (D / v.heads) % 4 || S <= 0 || S > v.max_len || Bq * S > cfb::kRowsMax ||
+        FF % cfb::kStatCols)
+      return CFB_ERR_UNSUPPORTED;
+    if (3 * S * (D / v.heads) + S * S > (cfb::kSmemBudget / 4) / 2) return CFB_ERR_UNSUPPORTED;
+    if (!lin_ok(v.in_proj, D, v.in_dim) || !v.in_proj.bias || !lin_ok(v.out_proj, v.out_dim, D) ||
+        !v.out_proj.bias || !v.out_proj.colsum)
+      return CFB_ERR_INVALID_ARG;
+    for (int l = 0; l < v.layers; ++l) {
+      const cfb_vae_layer& ly = v.layer[l];
+      if (!lin_ok(ly.qkv, 3 * D, D) || !ly.qkv.colsum || !lin_ok(ly.attn_out, D, D) || !lin_ok(ly.ffn_up, FF, D) ||
+          !ly.ffn_up.colsum || !lin_ok(ly.ffn_down, D, FF))
+        return CFB_ERR_INVALID_ARG;
+    }
+  }
   if (D <= 0 || D % cfb::kStatCols || Bq <= 0) return CFB_ERR_UNSUPPORTED;
   if (E <= 0 || E > cfb::kMaxExperts || d.chunk <= 0 || E * d.chunk != DL) return CFB_ERR_UNSUPPORTED;
   if (!r.pred) return CFB_ERR_INVALID_ARG;
@@ -1687,6 +1831,18 @@ cfb_status lower(Builder& B, size_t* bytes) {
     o_ctx16 = A.take((size_t)Bq * C * k128(D) * 2);
   }
   const size_t o_ctxs = A.take((size_t)Bq * C * 8);
+  size_t o_vin16 = 0, o_vx32 = 0, o_vx16 = 0, o_vxs = 0, o_vqkv = 0, o_vo = 0, o_vu = 0;
+  if (vae) {
+    const size_t M = (size_t)Bq * B.vrows;
+    const int FF = B.vae->layers > 0 ? B.vae->layer[0].ffn_up.nout : 64;
+    o_vin16 = A.take(M * k128(B.vae->in_dim) * 2);
+    o_vx32 = A.take(M * D * 4);
+    o_vx16 = A.take(M * k128(D) * 2);
+    o_vxs = A.take(M * nparts * 8);
+    o_vqkv = A.take(M * 3 * D * 4);
+    o_vo = A.take(M * k128(D) * 2);
+    o_vu = A.take(M * k128(FF) * 2);
+  }
   const int rank = d.markov_rank, order = d.path_order;
   const int P2 = beam ? d.path_up.nout : 0;
   const int rowsB = Bq * std::max(Wmax, 1);
@@ -1714,6 +1870,53 @@ cfb_status lower(Builder& B, size_t* bytes) {
   B.too_big = false;
 
   { cfb::Phase p{}; p.kind = cfb::PK_PREP; ph.push_back(p); }
+
+  if (vae) {   // TransformerHiddenVAE encode_sequence / decode_sequence (transformer_hidden.py:51-67)
+    const cfb_vae_side& v = *B.vae;
+    const int S = B.vrows, M = Bq * S, hd = D / v.heads;
+    const int FF = v.layers > 0 ? v.layer[0].ffn_up.nout : 64;
+    auto resid_job = [&](const cfb_linear& lin, size_t o_in, int ldin) {
+      cfb::Job J = make_job(lin, M);
+      J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_in); J.ldx = ldin;
+      J.ekind = cfb::EK_RESID; J.out32 = B.dptr<float>(o_vx32); J.out16 = B.dptr<__half>(o_vx16); J.ldo = D;
+      J.ostats = B.dptr<float2>(o_vxs); J.onparts = nparts;
+      return J;
+    };
+    auto ln_job = [&](const cfb_linear& lin) {
+      cfb::Job J = make_job(lin, M);
+      J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_vx16); J.ldx = D;
+      J.ln = cfb::LN_PARTS; J.stats = B.dptr<float2>(o_vxs); J.nparts = nparts;
+      return J;
+    };
+    add_phase(B, cfb::Phase{}, {resid_job(v.in_proj, o_vin16, v.in_dim)});   // x = pos + in_proj(h)
+    cfb::AttnTask a{};
+    a.q = B.dptr<float>(o_vqkv); a.ldq = 3 * D; a.qoff = 0;
+    a.k = a.q; a.ldk = 3 * D; a.koff = D;
+    a.v = a.q; a.ldv = 3 * D; a.voff = 2 * D;
+    a.out = B.dptr<__half>(o_vo);
+    a.rows_per_req = S; a.keys_per_req = S; a.B = Bq; a.hd = hd; a.heads = v.heads;
+    a.causal = 0; a.scale = 1.0f / std::sqrt((float)hd); a.outR = M;
+    at.push_back(a);
+    for (int l = 0; l < v.layers; ++l) {       // pre-LN encoder layers (norm_first, GELU)
+      const cfb_vae_layer& ly = v.layer[l];
+      cfb::Job J = ln_job(ly.qkv);
+      J.ekind = cfb::EK_STORE; J.out32 = B.dptr<float>(o_vqkv); J.ldo = 3 * D;
+      add_phase(B, cfb::Phase{}, {J});
+      cfb::Phase pa{};
+      pa.kind = cfb::PK_ATTN; pa.job0 = 0; pa.njobs = 1; pa.ntiles = Bq * v.heads;
+      ph.push_back(pa);
+      add_phase(B, cfb::Phase{}, {resid_job(ly.attn_out, o_vo, D)});
+      J = ln_job(ly.ffn_up);
+      J.ekind = cfb::EK_GELU16; J.out16 = B.dptr<__half>(o_vu); J.ldo = FF;
+      add_phase(B, cfb::Phase{}, {J});
+      add_phase(B, cfb::Phase{}, {resid_job(ly.ffn_down, o_vu, FF)});
+    }
+    cfb::Job J = ln_job(v.out_proj);          // final LayerNorm folded in; mu or decoder_out
+    J.ldo = v.out_dim;
+    if (B.vdecode) { J.ekind = cfb::EK_STORE; J.out32 = static_cast<float*>(B.vout); }
+    else { J.ekind = cfb::EK_STORE16; J.out16 = static_cast<__half*>(B.vout); }
+    add_phase(B, cfb::Phase{}, {J});
+  }
 
   if (flow) {
     const int L = d.layers, T = d.steps, hd = D / d.heads;
@@ -1924,15 +2127,20 @@ cfb_status lower(Builder& B, size_t* bytes) {
       const int hd = D / d.heads, Kmax = std::max(DL, C);
       scratch = std::max(scratch, (size_t)((DL + 2 * Kmax) * hd + DL * Kmax) * 4);
     }
+    if (vae) {
+      const int hd = D / B.vae->heads, S = B.vrows;
+      scratch = std::max(scratch, (size_t)(3 * S * hd + S * S) * 4);
+    }
     // a split tile's owner lists the other contributors (at most G) in the scratch
     scratch = std::max(scratch, (size_t)(G + 1) * 4);
     scratch = (scratch + 127) / 128 * 128;
     const int red = cfb::kTileRows * RP * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
+    const int desc = cfb::kDescBufs * (cfb::kPhaseSlot + cfb::kJobCache * (int)sizeof(cfb::Job));
     const int bars = (2 * cfb::kMaxStages + 4) * 8;
     const int stage_bytes = (cfb::kUnitBytes + xrows_max * cfb::kXRowBytes + 127) / 128 * 128;
     auto stages_for = [&](int nbuf) {
       const long fixed = (long)nbuf * slot_bytes + scratch + red + rowstat + misc + bars + 512 +
-                       2 * cfb::kTileRows * 4;
+                       2 * cfb::kTileRows * 4 + desc + 16;
       return std::min<long>(cfb::kMaxStages, (cfb::kSmemBudget - fixed) / stage_bytes);
     };
     int nbuf = stages_for(2) >= 6 ? 2 : 1;
@@ -1947,7 +2155,8 @@ cfb_status lower(Builder& B, size_t* bytes) {
     Lm.off_rowstat = Lm.off_red + red;
     Lm.off_tile = Lm.off_rowstat + rowstat;
     Lm.off_misc = Lm.off_tile + 2 * cfb::kTileRows * 4;
-    Lm.total = Lm.off_misc + misc;
+    Lm.off_desc = (Lm.off_misc + misc + 15) / 16 * 16;
+    Lm.total = Lm.off_desc + desc;
   }
   if (B.too_big) return CFB_ERR_UNSUPPORTED;
   const size_t o_prof = profile ? A.take(ph.size() * (size_t)G * cfb::kProfSlots * 8) : 0;
@@ -1992,6 +2201,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
   P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs); P.init_mode = r.init_mode;
   if (flow) P.ctx16 = B.dptr<__half>(o_ctx16);
   P.known0 = r.known0; P.tokens = r.tokens;
+  if (vae) {
+    P.vin = B.vin; P.vin32 = B.vdecode; P.vS = B.vrows; P.vDin = B.vae->in_dim;
+    P.vin16 = B.dptr<__half>(o_vin16); P.vx32 = B.dptr<float>(o_vx32); P.vpos = B.vae->pos;
+  }
   {
     auto expose = [&](int i, size_t off, size_t nbytes) { P.buf[i] = B.dptr<void>(off); P.buf_bytes[i] = nbytes; };
     if (beam) {
@@ -2090,10 +2303,11 @@ cfb_status cfb_plan_workspace(const cfb_drafter* d, const cfb_run* r, size_t* by
   return lower(B, bytes);
 }
 
-cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes) {
-  if (!d || !r || !ws) return CFB_ERR_INVALID_ARG;
-  if (reinterpret_cast<uintptr_t>(ws) % 256) return CFB_ERR_INVALID_ARG;
-  Builder B; B.d = d; B.r = r; B.base = static_cast<uint8_t*>(ws);
+}  // extern "C"
+
+namespace {
+// Lower B into the workspace and record the launch shape (cfb_plan_build, cfb_vae_plan_build).
+cfb_status build_into(Builder& B, void* ws, size_t bytes) {
   size_t need = 0;
   cfb_status st = lower(B, &need);
   if (st != CFB_OK) return st;
@@ -2129,6 +2343,47 @@ cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size
   return CFB_OK;
 }
 
+// The stand-in drafter / run of a VAE side plan: D = the VAE width, one "expert" of `rows`
+// rows so that the shared validation holds, the output bound as pred.
+void vae_standins(const cfb_vae_side* v, int batch, int rows, void* out, cfb_drafter& d, cfb_run& r) {
+  d = cfb_drafter{};
+  r = cfb_run{};
+  d.hidden = v->width; d.heads = v->heads; d.layers = v->layers; d.steps = 1;
+  d.draft_len = rows; d.chunk = rows; d.ctx_rows = rows; d.n_experts = 1;
+  r.mode = cfb::kModeVae; r.batch = batch; r.pred = static_cast<float*>(out);
+}
+}  // namespace
+
+extern "C" {
+
+cfb_status cfb_plan_build(const cfb_drafter* d, const cfb_run* r, void* ws, size_t bytes) {
+  if (!d || !r || !ws) return CFB_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return CFB_ERR_INVALID_ARG;
+  Builder B; B.d = d; B.r = r; B.base = static_cast<uint8_t*>(ws);
+  return build_into(B, ws, bytes);
+}
+
+cfb_status cfb_vae_plan_workspace(const cfb_vae_side* v, int batch, int rows, int decode, size_t* bytes) {
+  if (!v || !bytes || batch <= 0 || rows <= 0) return CFB_ERR_INVALID_ARG;
+  cfb_drafter d; cfb_run r;
+  void* any = reinterpret_cast<void*>(256);           // sizing pass: any non-null I/O address
+  vae_standins(v, batch, rows, any, d, r);
+  Builder B; B.d = &d; B.r = &r; B.base = nullptr;
+  B.vae = v; B.vrows = rows; B.vdecode = decode != 0; B.vin = any; B.vout = any;
+  return lower(B, bytes);
+}
+
+cfb_status cfb_vae_plan_build(const cfb_vae_side* v, int batch, int rows, int decode, const void* in, void* out,
+                              void* ws, size_t bytes) {
+  if (!v || !ws || !in || !out || batch <= 0 || rows <= 0) return CFB_ERR_INVALID_ARG;
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return CFB_ERR_INVALID_ARG;
+  cfb_drafter d; cfb_run r;
+  vae_standins(v, batch, rows, out, d, r);
+  Builder B; B.d = &d; B.r = &r; B.base = static_cast<uint8_t*>(ws);
+  B.vae = v; B.vrows = rows; B.vdecode = decode != 0; B.vin = in; B.vout = out;
+  return build_into(B, ws, bytes);
+}
+
 cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases) {
   if (!ws) return CFB_ERR_INVALID_ARG;
   LaunchRecord h{};
@@ -2145,8 +2400,8 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
 static cfb_status launch_range(void* ws, const LaunchRec& L, int p0, int p1, void* stream) {
   const cfb_status st = ensure_smem_attr(L.maxnt, L.prof, L.smem);
   if (st != CFB_OK) return st;
-  const cfb::Plan* P = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
-  void* args[] = {(void*)&P, (void*)&p0, (void*)&p1};
+  const cfb::Plan* Pd = reinterpret_cast<const cfb::Plan*>(static_cast<uint8_t*>(ws) + kOffPlan);
+  void* args[] = {(void*)&Pd, (void*)&p0, (void*)&p1};
   cudaError_t e = cudaLaunchCooperativeKernel((const void*)engine_for(L.maxnt, L.prof), dim3(L.G), dim3(cfb::kThreads),
                                               args, (size_t)L.smem, static_cast<cudaStream_t>(stream));
   if (e == cudaErrorCooperativeLaunchTooLarge) return CFB_ERR_COOP_LAUNCH;

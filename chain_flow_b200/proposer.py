@@ -111,7 +111,9 @@ class FlowDrafterProposer:
             # VAE's latent width (expert_dim is forced to latent_size), the beam at the hidden width
             vcfg = VaeConfig.from_model_args(args, hidden)
             self.flow_cfg = DraftConfig.from_model_args(args, vcfg.latent)
-            self.vae = VaeWeights(state_dict, vcfg, device=device)
+            self.vae = VaeWeights(state_dict, vcfg, device=device, layout="engine")
+            self._vae_cfg = vcfg
+            self._wide_vae = None
             self.flow_weights = DrafterWeights(state_dict, self.flow_cfg, None, None, None, device=device,
                                                parts="flow")
         self.weights = DrafterWeights(state_dict, cfg, embed, lm_head, shortlist_ids, device=device,
@@ -213,7 +215,9 @@ class FlowDrafterProposer:
             init = _lib.INIT_MODES[self.init_mode]
             depth = self.tree_depth if mode == _lib.MODE_TREE else self.K
             if self.vae is not None:
-                p = VaeDraft(self.vae, self._wide_flow_weights, self._wide_weights, mode, B, wide=True,
+                if self._wide_vae is None:
+                    self._wide_vae = VaeWeights(self._wide_src[0], self._vae_cfg, device=self.dev, layout="wide")
+                p = VaeDraft(self._wide_vae, self._wide_flow_weights, self._wide_weights, mode, B, wide=True,
                              width=self.width, depth=depth, tree_keep=self.tree_keep, tree_topb=self.tree_topb,
                              init_mode=init)
             else:

@@ -28,52 +28,88 @@ class Workload:
     markov_rank: int = 256
     width: int = 4
     draft_tokens: int = 5
+    draft_length: int = 6
+    chunk: int = 3
+    path_order: int = 4
+    # latent > 0: a production TreeVAEFlowDrafter (reference drafters/tree_vae_flow.py:91-175), the
+    # flow at this latent width between a TransformerHiddenVAE encode and decode
+    latent: int = 0
+    vae_inter: int = 1920
+    vae_layers: int = 2
+    vae_heads: int = 8
 
-    def config(self) -> DraftConfig:
-        return DraftConfig(hidden=self.hidden, context_size=8, draft_length=6, chunk_size=3, num_heads=8,
-                           ffn_multiplier=self.ffn, num_drafter_layers=self.layers, num_flow_steps=self.steps,
-                           path_order=4, path_ffn_multiplier=2, markov_rank=self.markov_rank)
+    @property
+    def flow_width(self) -> int:
+        return self.latent or self.hidden
+
+    @property
+    def n_experts(self) -> int:
+        return self.draft_length // self.chunk
+
+    def config(self, hidden: int | None = None) -> DraftConfig:
+        return DraftConfig(hidden=hidden or self.hidden, context_size=8, draft_length=self.draft_length,
+                           chunk_size=self.chunk, num_heads=8, ffn_multiplier=self.ffn,
+                           num_drafter_layers=self.layers, num_flow_steps=self.steps, path_order=self.path_order,
+                           path_ffn_multiplier=2, markov_rank=self.markov_rank)
 
     def model_args(self) -> dict:
         c = self.config()
-        return dict(context_size=c.context_size, draft_length=c.draft_length, chunk_size=c.chunk_size,
-                    num_heads=c.num_heads, ffn_multiplier=c.ffn_multiplier,
-                    num_drafter_layers=c.num_drafter_layers, num_flow_steps=c.num_flow_steps,
-                    path_order=c.path_order, path_ffn_multiplier=c.path_ffn_multiplier,
-                    markov_rank=c.markov_rank, init_mode="noise", noise_scale=1.0)
+        a = dict(context_size=c.context_size, draft_length=c.draft_length, chunk_size=c.chunk_size,
+                 num_heads=c.num_heads, ffn_multiplier=c.ffn_multiplier,
+                 num_drafter_layers=c.num_drafter_layers, num_flow_steps=c.num_flow_steps,
+                 path_order=c.path_order, path_ffn_multiplier=c.path_ffn_multiplier,
+                 markov_rank=c.markov_rank, init_mode="noise", noise_scale=1.0)
+        if self.latent:
+            a.update(expert_dim=self.latent, latent_size=self.latent, vae_intermediate_size=self.vae_inter,
+                     vae_num_layers=self.vae_layers, vae_num_heads=self.vae_heads, vae_max_sequence_length=16)
+        return a
+
+    def vae_macs_per_row(self) -> tuple[int, int]:
+        """(encoder, decoder) multiply-adds per sequence row of the VAE's Linear layers: in-projection,
+        per layer in_proj 3I^2 + out_proj I^2 + FFN 2 * 4I^2, then mu / decoder_out."""
+        if not self.latent:
+            return 0, 0
+        H, I, Z, nl = self.hidden, self.vae_inter, self.latent, self.vae_layers
+        body = nl * 12 * I * I
+        return H * I + body + I * Z, Z * I + body + I * H
 
     def weight_bytes_per_draft(self, head_fraction: float = 1.0) -> int:
         """Packed fp16 weight bytes one draft streams (the algorithmic bytes of the engine):
-        cross K/V once; per Euler step every block of both chunk experts plus their out_proj;
+        cross K/V once; per Euler step every block of every chunk expert plus its out_proj;
         per beam depth the live PathHead offsets, the PathHead MLP and the [lm_head | markov w2]
-        shortlist head (reference flow_proposer.py:1115-1117 counts the head the same way).
+        shortlist head (reference flow_proposer.py:1115-1117 counts the head the same way); for a
+        production drafter the VAE encoder and decoder once each.
         head_fraction: the share of the shortlist head one GPU holds when it is row-sharded."""
-        D, L, T, FM = self.hidden, self.layers, self.steps, self.ffn
-        E = 2
-        crosskv = E * L * 2 * D * D
-        per_step = E * L * (3 + 1 + 1 + 1 + FM + FM) * D * D + E * D * D
+        Df, Dh, L, T, FM, E = self.flow_width, self.hidden, self.layers, self.steps, self.ffn, self.n_experts
+        crosskv = E * L * 2 * Df * Df
+        per_step = E * L * (3 + 1 + 1 + 1 + FM + FM) * Df * Df + E * Df * Df
         head = 0
         for d in range(1, self.draft_tokens + 1):
-            head += min(d, 4) * D * D + 2 * (2 * D * D) + head_fraction * self.shortlist_rows * (D + self.markov_rank)
-        return int(2 * (crosskv + T * per_step + head))
+            head += min(d, self.path_order) * Dh * Dh + 2 * (2 * Dh * Dh) + \
+                head_fraction * self.shortlist_rows * (Dh + self.markov_rank)
+        enc, dec = self.vae_macs_per_row()
+        return int(2 * (crosskv + T * per_step + head + enc + dec))
 
     def flops_per_draft(self, batch: int) -> int:
         """Multiply-add FLOPs (2 per MAC) of the Linear layers of one draft of `batch` requests:
-        every Euler step runs each block of chunk expert e over batch x 3(e+1) rows and out_proj
-        over batch x 3 rows; cross K/V runs once over batch x 8 context rows; each beam depth runs
-        the path head and the shortlist head over batch x width beam rows. Attention and the
+        every Euler step runs each block of chunk expert e over batch x chunk (e+1) rows and
+        out_proj over batch x chunk rows; cross K/V runs once over batch x 8 context rows; each
+        beam depth runs the path head and the shortlist head over batch x width beam rows; the VAE
+        encodes batch x 8 context rows and decodes batch x draft_length rows. Attention and the
         row kernels are not counted (under 1%)."""
-        D, L, T, FM = self.hidden, self.layers, self.steps, self.ffn
+        Df, Dh, L, T, FM, E, CH = self.flow_width, self.hidden, self.layers, self.steps, self.ffn, self.n_experts, self.chunk
         flow = 0
-        for e in range(2):
-            rows = batch * 3 * (e + 1)
-            flow += rows * L * (6 + 2 * FM) * D * D + batch * 3 * D * D
-        cross = batch * 8 * 2 * L * 2 * D * D
+        for e in range(E):
+            rows = batch * CH * (e + 1)
+            flow += rows * L * (6 + 2 * FM) * Df * Df + batch * CH * Df * Df
+        cross = batch * 8 * E * L * 2 * Df * Df
         head = 0
         bw = batch * self.width
         for d in range(1, self.draft_tokens + 1):
-            head += bw * (min(d, 4) * D * D + 4 * D * D + self.shortlist_rows * (D + self.markov_rank))
-        return int(2 * (T * flow + cross + head))
+            head += bw * (min(d, self.path_order) * Dh * Dh + 4 * Dh * Dh + self.shortlist_rows * (Dh + self.markov_rank))
+        enc, dec = self.vae_macs_per_row()
+        vae = batch * 8 * enc + batch * self.draft_length * dec
+        return int(2 * (T * flow + cross + head + vae))
 
 
 WORKLOADS = {
@@ -87,6 +123,11 @@ WORKLOADS = {
     # profiler-sized 4B-width case: one block, one Euler step, a 65,536-row vocabulary (about
     # 1.3 GB on the device, still far larger than L2), for full hardware-counter captures
     "4b-ncu": Workload("4B-width-ncu-case", hidden=2560, layers=1, steps=1, vocab=65536),
+    # the shipped 4B production drafter (the reference's published draft timings are for this
+    # shape): VAE 2560 -> 640 (intermediate 1920, 2 layers, 8 heads), 8 blocks, 2 Euler steps,
+    # draft_length 8 in chunks of 4, path order 8
+    "4b-prod": Workload("4B-production-vae", hidden=2560, layers=8, steps=2, draft_length=8, chunk=4,
+                        path_order=8, latent=640),
 }
 
 
@@ -96,7 +137,7 @@ def make_state(w: Workload, seed: int = 0, device="cuda"):
     cfg = w.config()
     dev = torch.device(device)
     g = torch.Generator(device=dev).manual_seed(seed)
-    D, FM, L, V, rank = w.hidden, w.ffn, w.layers, w.vocab, w.markov_rank
+    D, FM, L, V, rank = w.flow_width, w.ffn, w.layers, w.vocab, w.markov_rank
 
     def r(*shape, std=0.02, mean=0.0):
         return (torch.randn(*shape, generator=g, device=dev) * std + mean).to(torch.float16)
@@ -127,6 +168,7 @@ def make_state(w: Workload, seed: int = 0, device="cuda"):
         sd[p + "out_norm.bias"] = r(D, std=0.1)
         sd[p + "out_proj.weight"] = r(D, D)
         sd[p + "out_proj.bias"] = r(D)
+    D = w.hidden                     # the path head, markov head and shortlist head: hidden width
     sd["markov.w1.weight"] = r(V, rank, std=0.5)
     sd["markov.w2.weight"] = r(V, rank)
     for j in range(cfg.path_order):
@@ -139,6 +181,30 @@ def make_state(w: Workload, seed: int = 0, device="cuda"):
     sd["path_head.mlp.0.bias"] = r(P2)
     sd["path_head.mlp.3.weight"] = r(D, P2)
     sd["path_head.mlp.3.bias"] = r(D)
+    if w.latent:
+        I, Z = w.vae_inter, w.latent
+        for side, din, dout, inp, out in (("encoder", D, Z, "encoder_in", "mu"),
+                                          ("decoder", Z, D, "decoder_in", "decoder_out")):
+            sd[f"vae.{inp}.weight"] = r(I, din, std=din ** -0.5)
+            sd[f"vae.{inp}.bias"] = r(I)
+            sd[f"vae.{side}_pos.weight"] = r(16, I, std=0.1)
+            for i in range(w.vae_layers):
+                q = f"vae.{side}.layers.{i}."
+                for n in ("norm1", "norm2"):
+                    sd[f"{q}{n}.weight"] = r(I, std=0.1, mean=1.0)
+                    sd[f"{q}{n}.bias"] = r(I, std=0.1)
+                sd[q + "self_attn.in_proj_weight"] = r(3 * I, I)
+                sd[q + "self_attn.in_proj_bias"] = r(3 * I)
+                sd[q + "self_attn.out_proj.weight"] = r(I, I)
+                sd[q + "self_attn.out_proj.bias"] = r(I)
+                sd[q + "linear1.weight"] = r(4 * I, I)
+                sd[q + "linear1.bias"] = r(4 * I)
+                sd[q + "linear2.weight"] = r(I, 4 * I)
+                sd[q + "linear2.bias"] = r(I)
+            sd[f"vae.{side}_norm.weight"] = r(I, std=0.1, mean=1.0)
+            sd[f"vae.{side}_norm.bias"] = r(I, std=0.1)
+            sd[f"vae.{out}.weight"] = r(dout, I, std=I ** -0.5)
+            sd[f"vae.{out}.bias"] = r(dout)
     embed = r(V, D, std=0.5)
     lm_head = r(V, D)
     sl = torch.randperm(V, generator=torch.Generator().manual_seed(seed + 7))[: w.shortlist_rows].sort().values

@@ -9,10 +9,13 @@ width exactly as for ``TreeFlowDrafter``.
 
 Here one draft is four stages on one stream, each bound to the next one's input buffer:
 
-  encode (VaePlan, wide kernels)   ctx fp16 [B, C, H]       -> mu fp16 [B, C, latent] = flow ctx
-  flow   (engine Plan / WidePlan)  MODE_FLOW at the latent width -> z fp32 [B, DL, latent]
-  decode (VaePlan, wide kernels)   z                        -> pred fp32 [B, DL, H]   = beam pred
-  beam   (engine Plan / WidePlan)  MODE_BEAM_CHAIN / _TREE at the hidden width -> tokens
+  encode  ctx fp16 [B, C, H]       -> mu fp16 [B, C, latent] = the flow's ctx
+  flow    MODE_FLOW at the latent width -> z fp32 [B, DL, latent]
+  decode  z                        -> pred fp32 [B, DL, H]   = the beam's pred
+  beam    MODE_BEAM_CHAIN / _TREE at the hidden width -> tokens
+
+Up to 8 requests every stage is one persistent-engine launch (VaeEnginePlan, Plan); above that
+the VAE sides are wide launch lists (VaePlan) and the flow and beam wide plans.
 
 No stage allocates or synchronises; the whole draft can be captured in a CUDA graph.
 """
@@ -25,7 +28,7 @@ import torch
 
 from . import _lib
 from .engine import Plan, WidePlan
-from .weights import WidePacker
+from .weights import EnginePacker, WidePacker
 
 
 @dataclass
@@ -57,20 +60,24 @@ def is_vae_drafter(state_dict: dict, model_args: dict) -> bool:
 
 
 class VaeWeights:
-    """Both sides of the VAE in the wide GEMM's layout, every pre-LN folded into the Linear after
-    it: norm1 into self_attn.in_proj, norm2 into linear1, the encoder's final LayerNorm into
-    ``mu``, the decoder's into ``decoder_out``. ``logvar`` is not needed (the drafter uses mu)."""
+    """Both sides of the VAE, every pre-LN folded into the Linear after it: norm1 into
+    self_attn.in_proj, norm2 into linear1, the encoder's final LayerNorm into ``mu``, the
+    decoder's into ``decoder_out``. ``logvar`` is not needed (the drafter uses mu).
+    layout "engine": the persistent engine's stream layout (cfb_pack_linear, with LayerNorm
+    column sums); "wide": the wide GEMM's tiled layout (cfb_wide_pack)."""
 
-    def __init__(self, sd: dict, cfg: VaeConfig, device=None):
+    def __init__(self, sd: dict, cfg: VaeConfig, device=None, layout: str = "engine"):
         self.lib = _lib.load()
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if dev.type != "cuda":
             raise _lib.CfbError("VaeWeights needs a CUDA device: the VAE has no CPU path")
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
-        self.dev, self.cfg = dev, cfg
+        if layout not in ("engine", "wide"):
+            raise ValueError(f"layout={layout!r}")
+        self.dev, self.cfg, self.layout = dev, cfg, layout
         self._keep = []
-        pk = WidePacker(self.lib, dev, self._keep)
+        pk = WidePacker(self.lib, dev, self._keep) if layout == "wide" else EnginePacker(self.lib, dev, self._keep)
         f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
         self._layers = {}
 
@@ -150,6 +157,40 @@ class VaePlan:
             self._h = None
 
 
+class VaeEnginePlan:
+    """One VAE side as a persistent-engine plan (batch * rows <= 64), same I/O as VaePlan; runs
+    and reports like a drafting ``Plan`` (cfb_plan_run / cfb_plan_error)."""
+
+    def __init__(self, vw: VaeWeights, decode: bool, batch: int, rows: int, inp: torch.Tensor, out: torch.Tensor):
+        if vw.layout != "engine":
+            raise _lib.CfbError("VaeEnginePlan needs VaeWeights(layout='engine')")
+        self.vw, self.lib = vw, vw.lib
+        side = vw.decoder if decode else vw.encoder
+        want_in = (torch.float32 if decode else torch.float16, (batch, rows, side.in_dim))
+        want_out = (torch.float32 if decode else torch.float16, (batch, rows, side.out_dim))
+        for t, (dt, shape), what in ((inp, want_in, "input"), (out, want_out, "output")):
+            if t.dtype != dt or tuple(t.shape) != shape or not t.is_contiguous() or t.device != vw.dev:
+                raise _lib.CfbError(f"VAE {what}: want a contiguous {dt} {shape} tensor on {vw.dev}")
+        self.side, self.inp, self.out = side, inp, out
+        nbytes = C.c_size_t(0)
+        _lib.check(self.lib.cfb_vae_plan_workspace(C.byref(side), batch, rows, int(decode), C.byref(nbytes)),
+                   "cfb_vae_plan_workspace")
+        self.ws = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=vw.dev)
+        self.ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        _lib.check(self.lib.cfb_vae_plan_build(C.byref(side), batch, rows, int(decode), inp.data_ptr(), out.data_ptr(),
+                                               C.c_void_p(self.ws_ptr), C.c_size_t(int(nbytes.value))),
+                   "cfb_vae_plan_build")
+        self.launches = 1
+
+    def run(self, stream=None) -> None:
+        _lib.check(self.lib.cfb_plan_run(C.c_void_p(self.ws_ptr), C.c_void_p(_lib.stream_ptr(stream))), "cfb_plan_run")
+
+    def device_error(self) -> int:
+        v = C.c_int(0)
+        self.lib.cfb_plan_error(C.c_void_p(self.ws_ptr), C.byref(v))
+        return v.value
+
+
 _BEAM_MODE = {_lib.MODE_CHAIN: _lib.MODE_BEAM_CHAIN, _lib.MODE_TREE: _lib.MODE_BEAM_TREE}
 
 
@@ -158,7 +199,7 @@ class VaeDraft:
     as ``Plan``: write ``ctx`` (fp16 [B, C, hidden]), ``z0`` (fp16 [B, DL, latent], init_mode
     'noise') and ``known0``; ``run()``; read ``pred`` (fp32 [B, DL, hidden]) and ``tokens``.
     ``wide`` selects the wide (tcgen05, batched) plans for the flow and the beam instead of the
-    persistent engine."""
+    persistent engine; the VAE sides follow the layout of ``vw`` (engine plans or wide lists)."""
 
     def __init__(self, vw: VaeWeights, flow_w, head_w, mode: int, batch: int, *, wide: bool = False,
                  width: int = 4, depth: int = 5, tree_keep: int = 4, tree_topb: int = 8, init_mode: int = 0):
@@ -188,8 +229,9 @@ class VaeDraft:
             self.known0 = torch.zeros(batch, dtype=torch.int64, device=dev)
             self.pred = torch.zeros(batch, DL, vc.hidden, dtype=torch.float32, device=dev)
             self.tokens = None
-        self.encode = VaePlan(vw, False, batch, C_, self.ctx, self.flow.ctx)
-        self.decode = VaePlan(vw, True, batch, DL, self.flow.pred, self.pred)
+        side = VaeEnginePlan if vw.layout == "engine" else VaePlan
+        self.encode = side(vw, False, batch, C_, self.ctx, self.flow.ctx)
+        self.decode = side(vw, True, batch, DL, self.flow.pred, self.pred)
         self.segments = 1 + (self.head.segments if self.head is not None else 0)
         self.launches = self.encode.launches + getattr(self.flow, "launches", 1) + self.decode.launches + \
             (getattr(self.head, "launches", 1) if self.head is not None else 0)

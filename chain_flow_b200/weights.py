@@ -61,6 +61,56 @@ def shard_rows(rows: int, ranks: int, rank: int) -> tuple[int, int]:
     return r0, r1 - r0
 
 
+class EnginePacker:
+    """Packs fp16 weights into the persistent engine's stream layout (cfb_pack_linear) on `dev`,
+    folding the LayerNorm that feeds a Linear into it (gamma into the columns, beta into the bias,
+    column sums for the mean correction: cfb_fold_bias). Every device buffer is appended to
+    `keep`."""
+
+    def __init__(self, lib, dev, keep: list, stream=None):
+        self.lib, self.dev, self.keep = lib, dev, keep
+        self.stream = stream if stream is not None else torch.cuda.current_stream(dev)
+
+    def pack_buffer(self, nout: int, k: int) -> torch.Tensor:
+        nbytes = self.lib.cfb_packed_bytes(nout, k)
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
+        self.keep.append(buf)
+        return buf
+
+    def pack_into(self, w16: torch.Tensor, buf: torch.Tensor, nout: int, k: int, ktotal: int, kofs: int,
+                  rows: torch.Tensor | None = None, gamma: torch.Tensor | None = None):
+        _lib.check(self.lib.cfb_pack_linear(
+            w16.data_ptr(), w16.stride(0), rows.data_ptr() if rows is not None else None, nout, k,
+            gamma.data_ptr() if gamma is not None else None, buf.data_ptr(), ktotal, kofs,
+            self.stream.cuda_stream), "cfb_pack_linear")
+
+    def linear(self, w16: torch.Tensor, bias32: torch.Tensor | None, ln=None) -> "_lib.Linear":
+        """Pack one nn.Linear (optionally with the LayerNorm (gamma, beta) that feeds it)."""
+        w16 = w16.to(device=self.dev, dtype=torch.float16).contiguous()
+        if bias32 is not None:
+            bias32 = bias32.to(device=self.dev, dtype=torch.float32).contiguous()
+        if ln is not None:
+            ln = tuple(t.to(device=self.dev, dtype=torch.float32).contiguous() for t in ln)
+        nout, k = w16.shape
+        buf = self.pack_buffer(nout, k)
+        gamma = ln[0] if ln is not None else None
+        self.pack_into(w16, buf, nout, k, k, 0, gamma=gamma)
+        colsum = None
+        if ln is not None:
+            b_out = torch.empty(nout, device=self.dev, dtype=torch.float32)
+            colsum = torch.empty(nout, device=self.dev, dtype=torch.float32)
+            _lib.check(self.lib.cfb_fold_bias(
+                w16.data_ptr(), w16.stride(0), nout, k, ln[0].data_ptr(), ln[1].data_ptr(),
+                bias32.data_ptr() if bias32 is not None else None, b_out.data_ptr(), colsum.data_ptr(),
+                self.stream.cuda_stream), "cfb_fold_bias")
+            bias32 = b_out
+            self.keep.append(colsum)
+        if bias32 is not None:
+            self.keep.append(bias32)
+        return _lib.Linear(buf.data_ptr(), bias32.data_ptr() if bias32 is not None else None,
+                           colsum.data_ptr() if colsum is not None else None, nout, k)
+
+
 class DrafterWeights:
     """The drafter's weights packed for the engine. With head_shard=(rank, ranks) only that rank's
     contiguous share of the shortlist head is packed (row-sharded head across GPUs); everything
@@ -84,6 +134,7 @@ class DrafterWeights:
             raise _lib.CfbError(f"unsupported drafter shape: hidden={D} must be a multiple of 64")
         self._keep = []            # every device tensor the packed structs point at
         self.stream = torch.cuda.current_stream(dev)
+        self._pk = EnginePacker(self.lib, dev, self._keep, self.stream)
         f16 = lambda t: t.to(device=dev, dtype=torch.float16).contiguous()
         f32 = lambda t: t.to(device=dev, dtype=torch.float32).contiguous()
         want = {"all": None, "flow": ("expert.", "extra_experts."), "head": ("path_head.", "markov.")}[parts]
@@ -191,40 +242,14 @@ class DrafterWeights:
 
     # ------------------------------------------------------------------------------------------
     def pack_buffer(self, nout: int, k: int) -> torch.Tensor:
-        nbytes = self.lib.cfb_packed_bytes(nout, k)
-        buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.dev)
-        self._keep.append(buf)
-        return buf
+        return self._pk.pack_buffer(nout, k)
 
-    def _pack_into(self, w16: torch.Tensor, buf: torch.Tensor, nout: int, k: int, ktotal: int, kofs: int,
-                   rows: torch.Tensor | None = None, gamma: torch.Tensor | None = None):
-        _lib.check(self.lib.cfb_pack_linear(
-            w16.data_ptr(), w16.stride(0), rows.data_ptr() if rows is not None else None, nout, k,
-            gamma.data_ptr() if gamma is not None else None, buf.data_ptr(), ktotal, kofs,
-            self.stream.cuda_stream), "cfb_pack_linear")
+    def _pack_into(self, w16, buf, nout, k, ktotal, kofs, rows=None, gamma=None):
+        self._pk.pack_into(w16, buf, nout, k, ktotal, kofs, rows=rows, gamma=gamma)
 
     def linear(self, w16: torch.Tensor, bias32: torch.Tensor | None, ln=None) -> "_lib.Linear":
         """Pack one nn.Linear (optionally with the LayerNorm (gamma, beta) that feeds it)."""
-        w16 = w16.contiguous()
-        nout, k = w16.shape
-        buf = self.pack_buffer(nout, k)
-        gamma = ln[0] if ln is not None else None
-        self._pack_into(w16, buf, nout, k, k, 0, gamma=gamma)
-        colsum = None
-        if ln is not None:
-            b_out = torch.empty(nout, device=self.dev, dtype=torch.float32)
-            colsum = torch.empty(nout, device=self.dev, dtype=torch.float32)
-            _lib.check(self.lib.cfb_fold_bias(
-                w16.data_ptr(), w16.stride(0), nout, k, ln[0].data_ptr(), ln[1].data_ptr(),
-                bias32.data_ptr() if bias32 is not None else None, b_out.data_ptr(), colsum.data_ptr(),
-                self.stream.cuda_stream), "cfb_fold_bias")
-            bias32 = b_out
-            self._keep.append(colsum)
-        if bias32 is not None:
-            bias32 = bias32.contiguous()
-            self._keep.append(bias32)
-        return _lib.Linear(buf.data_ptr(), bias32.data_ptr() if bias32 is not None else None,
-                           colsum.data_ptr() if colsum is not None else None, nout, k)
+        return self._pk.linear(w16, bias32, ln)
 
     @property
     def packed_bytes(self) -> int:

@@ -213,7 +213,8 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  *                     partials ready, [13] split-tile counter updated, [14] split-tile partials
  *                     summed (0 if not applicable), [15] tile finished; beam phases, in the
  *                     CTAs that own a request: [16] lists merged, [17] beam step done, [18] next
- *                     depth's rows gathered; [19] unused; written only by runs of plans built
+ *                     depth's rows gathered; [19] epilogue: the last job's row statistics
+ *                     loaded (GEMM phases); written only by runs of plans built
  *                     with CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
 /* CFB_BUF_PHASES      int32 [phases, 15] the phase table: [0] kind (0 prep, 1 GEMM, 2 attention,
@@ -367,6 +368,14 @@ typedef struct cfb_vae_side {
  * with cfb_wide_run / cfb_wide_error / cfb_wide_destroy. Supported: in_dim and width multiples of
  * 64, out_dim a multiple of 16, width / heads a multiple of 8, rows <= 16 and <= max_len. */
 cfb_status cfb_vae_workspace(const cfb_vae_side* v, int batch, int rows, int decode, size_t* bytes);
+/* The same side as a persistent-engine plan (batch * rows <= 64: the small batches, where one
+ * cooperative launch beats a launch list): every cfb_linear packed by cfb_pack_linear, the
+ * LayerNorms folded by cfb_fold_bias (colsum set for qkv, ffn_up and out_proj). I/O as for
+ * cfb_vae_create; the plan lives in the caller's workspace and runs with cfb_plan_run /
+ * cfb_plan_error like a drafting plan. */
+cfb_status cfb_vae_plan_workspace(const cfb_vae_side* v, int batch, int rows, int decode, size_t* bytes);
+cfb_status cfb_vae_plan_build(const cfb_vae_side* v, int batch, int rows, int decode, const void* in,
+                              void* out, void* ws, size_t bytes);
 cfb_status cfb_vae_create(const cfb_vae_side* v, int batch, int rows, int decode, const void* in,
                           void* out, void* ws, size_t bytes, cfb_wide_plan** plan);
 cfb_status cfb_wide_workspace(const cfb_drafter* d, const cfb_run* r, size_t* bytes);

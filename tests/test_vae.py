@@ -74,26 +74,30 @@ def gvae_weights():
     from chain_flow_b200.weights import DrafterWeights, WideWeights
     g = load_gvae()
     W = g["W"]
-    vw = VaeWeights(W, _vae_cfg(g), device="cuda")
+    vw = VaeWeights(W, _vae_cfg(g), device="cuda", layout="wide")
+    ve = VaeWeights(W, _vae_cfg(g), device="cuda", layout="engine")
     fl = DrafterWeights(W, _draft_cfg(g, g["latent"]), None, None, None, device="cuda", parts="flow")
     hd = DrafterWeights(W, _draft_cfg(g, g["H"]), g["emb"], g["lm_w"], g["sl"], device="cuda", parts="head")
     wfl = WideWeights(W, _draft_cfg(g, g["latent"]), None, None, None, device="cuda", parts="flow")
     whd = WideWeights(W, _draft_cfg(g, g["H"]), g["emb"], g["lm_w"], g["sl"], device="cuda", parts="head")
-    return g, vw, fl, hd, wfl, whd
+    return g, vw, fl, hd, wfl, whd, ve
 
 
 @pytest.mark.gpu
-def test_gpu_vae_encode_decode_match_reference(gvae_weights):
-    from chain_flow_b200.vae import VaePlan
-    g, vw, *_ = gvae_weights
+@pytest.mark.parametrize("layout", ["wide", "engine"])
+def test_gpu_vae_encode_decode_match_reference(gvae_weights, layout):
+    from chain_flow_b200.vae import VaeEnginePlan, VaePlan
+    g, vw, fl, hd, wfl, whd, ve = gvae_weights
+    side = VaePlan if layout == "wide" else VaeEnginePlan
+    vw = vw if layout == "wide" else ve
     B = g["B"]
     ctx = g["ctx"].half().cuda().contiguous()
     mu = torch.zeros(B, 8, g["latent"], dtype=torch.float16, device="cuda")
-    enc = VaePlan(vw, False, B, 8, ctx, mu)
+    enc = side(vw, False, B, 8, ctx, mu)
     enc.run()
     zf = g["zflow"].float().cuda().contiguous()
     dec = torch.zeros(B, g["DL"], g["H"], dtype=torch.float32, device="cuda")
-    dp = VaePlan(vw, True, B, g["DL"], zf, dec)
+    dp = side(vw, True, B, g["DL"], zf, dec)
     dp.run()
     torch.cuda.synchronize()
     assert enc.device_error() == 0 and dp.device_error() == 0
@@ -108,8 +112,9 @@ def test_gpu_vae_draft_matches_reference(gvae_weights, wide):
     states within tolerance, chain ids equal to the reference's, tree equal or tie-explained."""
     from chain_flow_b200 import _lib
     from chain_flow_b200.vae import VaeDraft
-    g, vw, fl, hd, wfl, whd = gvae_weights
+    g, vw, fl, hd, wfl, whd, ve = gvae_weights
     f, h = (wfl, whd) if wide else (fl, hd)
+    vw = vw if wide else ve
     sl = g["sl"]
     W = g["W"]
     for mode in (_lib.MODE_CHAIN, _lib.MODE_TREE):
