@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "gdn", "gdn-verify"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
@@ -126,6 +126,23 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------
+def oracle_flow_config(oracle, wl):
+    """The flow's configuration (at the latent width for a production VAE drafter)."""
+    return oracle.FlowConfig(hidden=wl.flow_width, draft_length=wl.draft_length, chunk_size=wl.chunk,
+                             ffn_multiplier=wl.ffn, num_layers=wl.layers, num_flow_steps=wl.steps,
+                             path_order=wl.path_order, markov_rank=wl.markov_rank)
+
+
+def oracle_draft(oracle, wl, cfg, W, emb, hw, w2, sl, ctx, z0, known0):
+    """One draft of the reference algorithm (oracle/ restatement): predict_hidden (with the VAE
+    encode / decode around the flow for a production drafter), then the one-pass chain beam."""
+    if wl.latent:
+        pred = oracle.predict_hidden_vae(W, cfg, wl.vae_layers, wl.vae_heads, ctx, z0)
+    else:
+        pred = oracle.integrate(W, cfg, ctx, z0)
+    return oracle.beam_chains(W, cfg, emb, hw, w2, sl, pred, known0, wl.width, wl.draft_tokens)
+
+
 def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float = 30.0):
     """The reference algorithm on the host cores (oracle/ restatement, fp32, all threads):
     returns (tok/s, seconds per draft, threads, sample description). Stops after `n_drafts`
@@ -142,16 +159,14 @@ def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float =
     del lm, sd
     ctx, known0 = make_inputs(wl, 1, device=dev)
     ctx, known0 = ctx.float().cpu(), known0.cpu()
-    cfg = oracle.FlowConfig(hidden=wl.hidden, ffn_multiplier=wl.ffn, num_layers=wl.layers,
-                            num_flow_steps=wl.steps, markov_rank=wl.markov_rank)
+    cfg = oracle_flow_config(oracle, wl)
     g = torch.Generator().manual_seed(seed)
     times = []
     with torch.inference_mode():
         for i in range(n_drafts + 1):
-            z0 = torch.randn(1, 6, wl.hidden, generator=g)
+            z0 = torch.randn(1, wl.draft_length, wl.flow_width, generator=g)
             t0 = time.perf_counter()
-            pred = oracle.integrate(W, cfg, ctx, z0)
-            oracle.beam_chains(W, cfg, emb, hw, w2, sl, pred, known0, wl.width, wl.draft_tokens)
+            oracle_draft(oracle, wl, cfg, W, emb, hw, w2, sl, ctx, z0, known0)
             if i > 0:                      # the first draft warms caches and threads
                 times.append(time.perf_counter() - t0)
                 if len(times) >= 2 and sum(times) > budget_s:
@@ -173,14 +188,12 @@ def eager_gpu_reference_rate(wl, n_drafts: int, warmup: int, seed: int = 0):
     w2 = sd["markov.w2.weight"][sl].contiguous()
     del lm
     ctx, known0 = make_inputs(wl, 1, device=dev)
-    cfg = oracle.FlowConfig(hidden=wl.hidden, ffn_multiplier=wl.ffn, num_layers=wl.layers,
-                            num_flow_steps=wl.steps, markov_rank=wl.markov_rank)
+    cfg = oracle_flow_config(oracle, wl)
     g = torch.Generator(device=dev).manual_seed(seed)
 
     def draft():
-        z0 = torch.randn(1, 6, wl.hidden, generator=g, device=dev, dtype=torch.float16)
-        pred = oracle.integrate(sd, cfg, ctx, z0)
-        return oracle.beam_chains(sd, cfg, emb, hw, w2, sl, pred, known0, wl.width, wl.draft_tokens)
+        z0 = torch.randn(1, wl.draft_length, wl.flow_width, generator=g, device=dev, dtype=torch.float16)
+        return oracle_draft(oracle, wl, cfg, sd, emb, hw, w2, sl, ctx, z0, known0)
 
     with torch.inference_mode():
         for _ in range(max(1, warmup)):
@@ -339,9 +352,14 @@ def run_ours(args, wl):
     peak_hbm = measured_peaks()[0]
     if not wide and not shard and rank == 0:
         from chain_flow_b200.engine import Plan
-        pp = Plan(prop.weights, _lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH), width=wl.width, depth=wl.draft_tokens,
-                  profile=True, init_mode=_lib.INIT_MODES[prop.init_mode])
-        pp.ctx.copy_(plan.ctx); pp.z0.copy_(plan.z0); pp.known0.copy_(plan.known0)
+        if prop.vae is not None:        # the beam plan of a production draft, on that draft's hidden states
+            pp = Plan(prop.weights, _lib.MODE_BEAM_CHAIN, min(B, MAX_PLAN_BATCH), width=wl.width,
+                      depth=wl.draft_tokens, profile=True)
+            pp.pred.copy_(plan.pred); pp.known0.copy_(plan.known0)
+        else:
+            pp = Plan(prop.weights, _lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH), width=wl.width, depth=wl.draft_tokens,
+                      profile=True, init_mode=_lib.INIT_MODES[prop.init_mode])
+            pp.ctx.copy_(plan.ctx); pp.z0.copy_(plan.z0); pp.known0.copy_(plan.known0)
         for _ in range(2):
             pp.run()
         torch.cuda.synchronize(dev)
@@ -399,7 +417,14 @@ def run_ours(args, wl):
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
                        "beam_width": wl.width, "plans_per_step": plans_per_step,
-                       "path": ("wide plan: tcgen05 GEMMs + row kernels, one launch list per step" if wide
+                       **({"vae": {"latent": wl.latent, "intermediate": wl.vae_inter, "layers": wl.vae_layers,
+                                   "heads": wl.vae_heads},
+                           "draft_length": wl.draft_length, "chunk": wl.chunk, "path_order": wl.path_order}
+                          if wl.latent else {}),
+                       "path": (("VAE encode (wide launches) -> latent flow -> VAE decode (wide launches) -> beam, "
+                                 + ("wide plans" if wide else "flow and beam as persistent-engine launches"))
+                                if wl.latent else
+                                "wide plan: tcgen05 GEMMs + row kernels, one launch list per step" if wide
                                 else "persistent engine: one cooperative launch per plan"),
                        "parallelism": (f"shortlist head rows sharded over {world} GPUs, flow replicated, "
                                        f"one NCCL all_gather of merged top-k lists per depth") if shard
@@ -408,7 +433,7 @@ def run_ours(args, wl):
                              f"every step"},
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": args.steps * (plan.launches if wide else plan.segments * plans_per_step),
+            "gpu_launches": args.steps * plans_per_step * getattr(plan, "launches", plan.segments),
             "roofline": ({"bound": "tensor", "achieved": flops / (kernel_ms / 1e3) / 1e12, "peak": tpeak,
                           "unit": "TFLOP/s", "frac": flops / (kernel_ms / 1e3) / 1e12 / tpeak, "traffic": None,
                           "peak_source": tpeak_kind, "kernel": "wide plan (all launches; tcgen05 GEMMs dominate)",
@@ -418,7 +443,8 @@ def run_ours(args, wl):
                           "frac": achieved / peak, "traffic": traffic if not wide else None,
                           "traffic_source": traffic_note if not wide else None,
                           "peak_source": peak_kind,
-                          "kernel": "wide plan (all launches; tcgen05 GEMMs dominate)" if wide else "engine_kernel",
+                          "kernel": ("whole production draft (VAE launches + flow + beam)" if wl.latent else
+                                     "wide plan (all launches; tcgen05 GEMMs dominate)" if wide else "engine_kernel"),
                           "kernel_ms": kernel_ms, "algorithmic_bytes_per_launch": algo,
                           "tflops": flops / (kernel_ms / 1e3) / 1e12}),
             "clocks": clk,
