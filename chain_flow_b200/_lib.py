@@ -35,7 +35,7 @@ EXPORTED = [
 ABI_VERSION = 2
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF, BUF_PHASES = range(10)
-PK_PREP, PK_GEMM, PK_ATTN, PK_BEAM, PK_RMERGE = range(5)          # CFB_BUF_PHASES [0]
+PK_PREP, PK_GEMM, PK_ATTN, PK_BEAM, PK_RMERGE, PK_GATHER = range(6)   # CFB_BUF_PHASES [0]
 PO_NONE, PO_BEAM_CHAIN, PO_BEAM_TREE, PO_PUBLISH = range(4)        # CFB_BUF_PHASES [6]
 RUN_PROFILE = 1
 EPI_F32, EPI_F16, EPI_GELU16, EPI_PART = 0, 1, 2, 3      # cfb_wide_gemm epilogues

@@ -95,12 +95,12 @@ enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_P
                    EK_HEADIN = 5, EK_HEAD = 6, EK_STORE16 = 7 };
 // the plan mode of a VAE side (cfb_vae_plan_build): not a cfb_mode the caller can ask for
 constexpr int kModeVae = 16;
-enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4 };
+enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4, PK_GATHER = 5 };
 enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
 // Attention of one (expert, block): q rows [B*Sq] and k/v rows [B*Kn] (fp32, written by the
 // projection phase before it), output fp16 unit-tiled with outR rows. One task = (request, head).
-struct AttnTask {
+struct alignas(16) AttnTask {
   const float* q; int ldq, qoff;
   const float* k; int ldk, koff;
   const float* v; int ldv, voff;
@@ -149,6 +149,9 @@ struct Phase {
 static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
 static_assert(sizeof(Phase) <= kPhaseSlot, "descriptor cache slot");
 static_assert(sizeof(Job) % 16 == 0 && kJobCache * sizeof(Job) / 16 <= 64, "descriptor cache copy");
+static_assert(sizeof(AttnTask) % 16 == 0, "descriptor cache copy");
+// attention tasks a descriptor cache slot holds (in the room of its jobs)
+constexpr int kAttnCache = (int)(kJobCache * sizeof(Job) / sizeof(AttnTask));
 
 // The cost of a cross-CTA split-tile fixup (publish, owner's bounded wait, sum), in streamed
 // units, for the whole-tiles-or-split choice of each GEMM phase.
@@ -307,54 +310,74 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W, volatile in
 CFB_DEV int src_row(const Job& J, int r) { return (r / J.gin) * J.gstride + J.goff + r % J.gin; }
 
 // ------------------------------------------------------------------------------------------
-CFB_DEV void chan_merge(float& n, float& m, float& M2, float nb, float mb, float M2b) {
-  const float nn = n + nb;
-  if (nn == 0.f) return;
-  const float d = mb - m;
-  const float f = nb / nn;
-  m = m + d * f;
-  M2 = M2 + M2b + d * d * n * f;
-  n = nn;
-}
+// LayerNorm statistics as (mean, M2 = sum of squared deviations) of equal-count groups, merged
+// without divisions: for k groups of c values each, mean = avg(mean_g) and
+// M2 = sum(M2_g) + c * sum((mean_g - mean)^2) (the pairwise form of Chan et al. with equal counts).
 
-// Fold 8 values into a running (n, mean, M2): two-pass over the 8, then one Chan merge.
-CFB_DEV void stats8_merge(float& n, float& m, float& M2, const float (&v)[8]) {
+// (mean, M2) of 8 values, two-pass.
+CFB_DEV void stats8(const float (&v)[8], float& mean, float& M2) {
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) sum += v[i];
-  const float mb = sum * 0.125f;
+  mean = sum * 0.125f;
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) { const float d = v[i] - mb; q += d * d; }
-  chan_merge(n, m, M2, 8.f, mb, q);
+  for (int i = 0; i < 8; ++i) { const float d = v[i] - mean; q += d * d; }
+  M2 = q;
 }
 
-// Merge (n, mean, M2) across `width` adjacent lanes; the lower lane is always the left operand,
-// so the result does not depend on scheduling.
-CFB_DEV void chan_group(float& n, float& m, float& M2, int width) {
-  const int lane = threadIdx.x & 31;
-  for (int off = 1; off < width; off <<= 1) {
-    const float nb = __shfl_xor_sync(0xffffffffu, n, off);
-    const float mb = __shfl_xor_sync(0xffffffffu, m, off);
-    const float M2b = __shfl_xor_sync(0xffffffffu, M2, off);
-    if (lane & off) { float tn = n, tm = m, tM = M2; n = nb; m = mb; M2 = M2b; chan_merge(n, m, M2, tn, tm, tM); }
-    else chan_merge(n, m, M2, nb, mb, M2b);
-  }
+// Fold group k (0-based; 8 values: mean mb, M2 qb) into the running statistics of groups 0..k-1.
+CFB_DEV void stats8_add(float& m, float& M2, int k, float mb, float qb) {
+  if (k == 0) { m = mb; M2 = qb; return; }
+  const float r = k == 1 ? 0.5f : k == 2 ? (1.f / 3.f) : k == 3 ? 0.25f : 1.f / (float)(k + 1);
+  const float d = mb - m;
+  m += d * r;
+  M2 += qb + d * d * (8.f * (float)k) * r;
+}
+
+// Merge equal-count statistics (cnt values each) held by `width` adjacent lanes (a power of two);
+// every lane of the group ends with the same result (butterfly sums are order-independent here:
+// each stage adds two identical partial values). Out of line, like job_rowstats: inlined, these
+// measured 2-3 % slower weight streaming in the large phases (register allocation of the loop).
+__device__ __noinline__ void eq_group(float& m, float& M2, float cnt, int width) {
+  float s = m;
+  for (int off = 1; off < width; off <<= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  const float mean = s * (1.f / (float)width);
+  const float d = m - mean;
+  float q = M2 + cnt * d * d;
+  for (int off = 1; off < width; off <<= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+  m = mean; M2 = q;
 }
 
 // Row LayerNorm statistics of the job's source rows -> S.rowstat[r] = (mean, rstd) (epilogue).
-CFB_DEV void job_rowstats(const Job& J, Smem& S, const Grp& E) {
+__device__ __noinline__ void job_rowstats(const Job& J, Smem& S, const Grp& E) {
   const int warp = E.t >> 5, lane = E.t & 31, nw = E.n >> 5;
   if (J.ln == LN_PARTS) {
+    // the row's parts are kStatCols columns each: mean = avg(part means), then
+    // M2 = sum(part M2 + kStatCols * (part mean - mean)^2); parts lane, lane + 32, ... per lane
+    constexpr int kPL = 4;                                  // parts per lane (<= 128 parts)
+    const int np = J.nparts;
+    const float inv = 1.f / (float)np;
     for (int r = warp; r < J.rows; r += nw) {
       const int sr = src_row(J, r);
-      float n = 0.f, m = 0.f, M2 = 0.f;
-      for (int p = lane; p < J.nparts; p += 32) {
-        const float2 st = __ldcg(J.stats + (size_t)sr * J.nparts + p);
-        chan_merge(n, m, M2, (float)kStatCols, st.x, st.y);
+      float2 st[kPL];
+      float ms = 0.f;
+#pragma unroll
+      for (int j = 0; j < kPL; ++j) {
+        const int p = lane + 32 * j;
+        st[j] = p < np ? __ldcg(J.stats + (size_t)sr * np + p) : make_float2(0.f, 0.f);
+        ms += st[j].x;
       }
-      chan_group(n, m, M2, 32);
-      if (lane == 0) S.rowstat[r] = make_float2(m, rsqrtf(M2 / n + 1e-5f));
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ms += __shfl_xor_sync(0xffffffffu, ms, off);
+      const float mean = ms * inv;
+      float q = 0.f;
+#pragma unroll
+      for (int j = 0; j < kPL; ++j)
+        if (lane + 32 * j < np) { const float d = st[j].x - mean; q += st[j].y + (float)kStatCols * d * d; }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(0xffffffffu, q, off);
+      if (lane == 0) S.rowstat[r] = make_float2(mean, rsqrtf(q * inv * (1.f / (float)kStatCols) + 1e-5f));
     }
   } else if (J.ln == LN_DIRECT) {
     for (int r = E.t; r < J.rows; r += E.n) S.rowstat[r] = __ldcg(J.stats + src_row(J, r));
@@ -462,17 +485,17 @@ CFB_DEV void attn_task(const AttnTask& A, int b, int h, Smem& S, const Grp& W) {
 }
 
 // An attention phase: its (task, request, head) items spread over the CTAs, one at a time.
-__device__ __noinline__ void attn_phase(const Plan& P, const Phase& ph, Smem& S, const Grp& W) {
+__device__ __noinline__ void attn_phase(const Plan& P, const Phase& ph, const AttnTask* at, Smem& S, const Grp& W) {
   for (int t = blockIdx.x; t < ph.ntiles; t += P.G) {
     int jx = 0, rem = t;
     for (; jx < ph.njobs; ++jx) {
-      const AttnTask& A = P.attn[ph.job0 + jx];
+      const AttnTask& A = at[jx];
       const int n = A.B * A.heads;
       if (rem < n) break;
       rem -= n;
     }
     if (jx >= ph.njobs) break;
-    const AttnTask& A = P.attn[ph.job0 + jx];
+    const AttnTask& A = at[jx];
     attn_task(A, rem / A.heads, rem % A.heads, S, W);
   }
 }
@@ -563,7 +586,8 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     case EK_RESID:
     case EK_PATHH: {
       const RowMap M = row_map(rows, E.t);
-      float n = 0.f, m = 0.f, M2 = 0.f;
+      float m = 0.f, M2 = 0.f;
+      int ng = 0;
       if (M.r < rows) {
         for (int f0 = M.q * M.nf; f0 < (M.q + 1) * M.nf; f0 += 8) {
           float add[8];
@@ -591,10 +615,12 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
           // 8 consecutive columns from a multiple of 8 are 16 contiguous bytes of the tiled layout
           *reinterpret_cast<uint4*>(J.out16 + tidx(J.oR, M.r, col0 + f0)) =
               make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
-          stats8_merge(n, m, M2, v);
+          float mb, qb;
+          stats8(v, mb, qb);
+          stats8_add(m, M2, ng++, mb, qb);
         }
       }
-      chan_group(n, m, M2, M.sl);
+      eq_group(m, M2, (float)M.nf, M.sl);
       if (M.q == 0 && M.r < rows) J.ostats[(size_t)M.r * J.onparts + tile] = make_float2(m, M2);
       break;
     }
@@ -618,7 +644,8 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
 #pragma unroll 1
       for (int e = 0; e < P.n_experts; ++e) {
         const ExpertRT& X = P.ex[e];
-        float n = 0.f, m = 0.f, M2 = 0.f;
+        float m = 0.f, M2 = 0.f;
+        int ng = 0;
         const bool has = live && pos < X.S;
         if (has) {
           const bool cur = pos >= X.start;
@@ -635,10 +662,12 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
               X.x32[nx][xi + i] = xv[i];
               X.x16[nx][tidx(P.B * X.S, xrow, col0 + f + i)] = __float2half_rn(xv[i]);
             }
-            stats8_merge(n, m, M2, xv);
+            float mb, qb;
+            stats8(xv, mb, qb);
+            stats8_add(m, M2, ng++, mb, qb);
           }
         }
-        chan_group(n, m, M2, M.sl);
+        eq_group(m, M2, (float)M.nf, M.sl);
         if (M.q == 0 && has) X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m, M2);
       }
       break;
@@ -1042,9 +1071,10 @@ CFB_DEV void desc_fill(const Plan& P, Smem& S, int p) {
 #pragma unroll
   for (int i = 0; i < kPhInts; ++i) reinterpret_cast<int*>(slot)[i] = v[i];
   const int kind = v[0], job0 = v[1], njobs = v[2];
-  if (kind == PK_GEMM && njobs <= kJobCache) {
-    const int n16 = njobs * (int)(sizeof(Job) / 16);
-    const uint4* src = reinterpret_cast<const uint4*>(P.jobs + job0);
+  const bool gemm = kind == PK_GEMM && njobs <= kJobCache, attn = kind == PK_ATTN && njobs <= kAttnCache;
+  if (gemm || attn) {
+    const int n16 = gemm ? njobs * (int)(sizeof(Job) / 16) : njobs * (int)(sizeof(AttnTask) / 16);
+    const uint4* src = gemm ? reinterpret_cast<const uint4*>(P.jobs + job0) : reinterpret_cast<const uint4*>(P.attn + job0);
     uint4* dst = reinterpret_cast<uint4*>(slot + kPhaseSlot);
     for (int i0 = 0; i0 < n16; i0 += 16) {
       uint4 t[16];
@@ -1063,6 +1093,10 @@ CFB_DEV void desc_fill(const Plan& P, Smem& S, int p) {
 // The jobs of cached phase p (the descriptor cache, or the global table beyond kJobCache jobs).
 CFB_DEV const Job* phase_jobs(const Plan& P, const Smem& S, const Phase& ph, int p) {
   return ph.njobs <= kJobCache ? S.djobs(p) : P.jobs + ph.job0;
+}
+// The attention tasks of cached phase p.
+CFB_DEV const AttnTask* phase_tasks(const Plan& P, const Smem& S, const Phase& ph, int p) {
+  return ph.njobs <= kAttnCache ? reinterpret_cast<const AttnTask*>(S.djobs(p)) : P.attn + ph.job0;
 }
 
 // Activation producer (one thread): copies the activation rows of this CTA's units, and fills
@@ -1481,11 +1515,17 @@ __device__ __noinline__ void beam_phase(const Plan& P, const Phase& ph, Smem& S,
         }
       }
     }
-    // the next depth's path-GEMM and markov rows of this request
-    if (!ph.last) path_gather(P, k, P.B * k, b * k, k, min(step + 1, order), false, W.t, W.n);
     gsync(W);
     if (prow && W.t == 0) prow[18] = globaltimer();
   }
+}
+
+// The next depth's path-GEMM and markov rows of every request (the embedding rows of the live
+// path tokens the beam phase just wrote), spread over the whole grid: one request's rows are
+// about 100 KB of scattered embedding rows, too slow for the one CTA that ran its beam step.
+__device__ __noinline__ void gather_phase(const Plan& P, const Phase& ph, const Grp& W) {
+  const long long t = (long long)blockIdx.x * W.n + W.t, nt = (long long)P.G * W.n;
+  path_gather(P, ph.fr, P.B * ph.fr, 0, P.B * ph.fr, min(ph.step, P.order), false, t, nt);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -1581,9 +1621,11 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     if (ph.kind == PK_PREP) {
       prep_phase(P, Wk);
     } else if (ph.kind == PK_ATTN) {
-      attn_phase(P, ph, S, Wk);
+      attn_phase(P, ph, phase_tasks(P, S, ph, p), S, Wk);
     } else if (ph.kind == PK_BEAM) {
       beam_phase(P, ph, S, Wk, P.prof ? prow : nullptr);
+    } else if (ph.kind == PK_GATHER) {
+      gather_phase(P, ph, Wk);
     } else if (ph.kind == PK_RMERGE) {
       rmerge_phase(P, ph, S, Wk);
     } else {
@@ -2102,6 +2144,13 @@ cfb_status lower(Builder& B, size_t* bytes) {
         p.rows = rows; p.step = step; p.fr = fr; p.keep = Wmax; p.topb = TB;
         p.base = base; p.base_prev = base_prev; p.last = (step == K);
         ph.push_back(p);
+      }
+      if (step < K) {   // the next depth's gathered rows, over the whole grid
+        cfb::Phase g{};
+        g.kind = cfb::PK_GATHER;
+        g.fr = tree ? std::min(Wmax, fr * TB) : Wmax;
+        g.step = step + 1;
+        ph.push_back(g);
       }
       if (tree) {
         const int k = std::min(Wmax, fr * TB);

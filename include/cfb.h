@@ -218,7 +218,7 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  *                     with CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
 /* CFB_BUF_PHASES      int32 [phases, 15] the phase table: [0] kind (0 prep, 1 GEMM, 2 attention,
- *                     3 beam, 4 rank merge), [1..5] first job, jobs, units, tiles, whole-tile flag,
+ *                     3 beam, 4 rank merge, 5 next depth's path-row gather), [1..5] first job, jobs, units, tiles, whole-tile flag,
  *                     [6] post-op (0 none, 1 chain beam, 2 tree beam, 3 head lists published:
  *                     the shortlist head GEMM of a beam depth), [7..14] step, rows, frontier,
  *                     kept beams, top list length, node base, previous node base, last-depth
