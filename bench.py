@@ -421,8 +421,8 @@ def run_ours(args, wl):
                                    "heads": wl.vae_heads},
                            "draft_length": wl.draft_length, "chunk": wl.chunk, "path_order": wl.path_order}
                           if wl.latent else {}),
-                       "path": (("VAE encode (wide launches) -> latent flow -> VAE decode (wide launches) -> beam, "
-                                 + ("wide plans" if wide else "flow and beam as persistent-engine launches"))
+                       "path": (("VAE encode -> latent flow -> VAE decode -> beam: "
+                                 + ("wide launch lists and wide plans" if wide else "four persistent-engine launches"))
                                 if wl.latent else
                                 "wide plan: tcgen05 GEMMs + row kernels, one launch list per step" if wide
                                 else "persistent engine: one cooperative launch per plan"),
