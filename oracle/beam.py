@@ -2,7 +2,10 @@
 
 Restates ``FlowDrafterProposer._beam_chains`` (reference
 ``src/chain_flow/vllm_plugin/flow_proposer.py:1188-1269``) and ``_beam_tree`` (``:1273-1332``)
-with the one-pass head (``CF_TWOPASS_M=0``), ``CF_FEEDBACK=0`` and ``CF_PATH_TRIM=1``.
+with ``CF_FEEDBACK=0`` and ``CF_PATH_TRIM=1``: the one-pass head (``CF_TWOPASS_M=0``), or the
+two-pass candidate head with one candidate set shared by every depth (``CF_TWOPASS_M=M``,
+``CF_TWOPASS_SHARED=1``, ``CF_TWOPASS_SEED=0``; ``_candidates`` / ``_gather_cand`` /
+``_rescore``, ``flow_proposer.py:1142-1184``).
 """
 from __future__ import annotations
 
@@ -20,7 +23,32 @@ def head_logprobs(W, emb, hw, w2_sl, h, lastp, order, nlive):
     return logits, torch.log_softmax(logits, dim=-1)
 
 
-def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int, K: int):
+def twopass_candidates(hw, pred, lo: int, hi: int, M: int):
+    """Pass A of the two-pass head, shared mode (flow_proposer.py:1142-1165): one GEMM of the
+    marginal hiddens pred[:, lo:hi] against the whole shortlist head, log_softmax per depth (fp32),
+    the best log-prob of each row over the depths, and its top M -> [B, M] shortlist-local ids
+    (sorted by score, as torch.topk returns them)."""
+    B, n = pred.shape[0], hi - lo
+    hm = pred[:, lo:hi].reshape(B * n, -1)
+    logits = (hm.to(hw.dtype) @ hw.T).float()
+    lp = torch.log_softmax(logits.view(B, n, -1), dim=-1).amax(dim=1)
+    return lp.topk(M, dim=-1).indices
+
+
+def twopass_logprobs(W, emb, hw, w2_sl, cd, h, lastp, order, nlive, B: int):
+    """Pass B (flow_proposer.py:1167-1184): the rows of this depth rescored against the
+    gathered candidate rows only; log_softmax over the M candidates. h, lastp [B*F, ...] ->
+    [B, F, M]."""
+    res = path_residual(W, emb, lastp, order, nlive)
+    x = (h.to(res.dtype) + res).view(B, -1, res.shape[-1])
+    wc, w2c = hw[cd], w2_sl[cd]                                        # [B, M, D], [B, M, rank]
+    mb = W["markov.w1.weight"][lastp[:, 0]].view(B, x.shape[1], -1)
+    logits = torch.bmm(x.to(wc.dtype), wc.transpose(1, 2)) + torch.bmm(mb.to(w2c.dtype), w2c.transpose(1, 2))
+    return torch.log_softmax(logits.float(), dim=-1)
+
+
+def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int, K: int,
+                twopass_m: int = 0):
     """Chain beam over the integrated hiddens ``pred`` [B, draft_length, D].
 
     Depth 0 is seeded with the committed token (one live beam, cum = [0, -inf, ...]); depths
@@ -36,11 +64,18 @@ def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int
     cum[:, 0] = 0.0
     steps = min(K + 1, pred.shape[1])
     toks, bps = [], []
+    cd = twopass_candidates(hw, pred, 1, steps, twopass_m) if twopass_m and steps > 1 else None
     for step in range(1, steps):
         h = pred[:, step].float().unsqueeze(1).expand(B, Wd, -1).reshape(B * Wd, -1)
-        _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * Wd, order), order, step)
-        cv, ci = lp.topk(Wd, dim=-1)                                    # [B*W, W]
-        ci = ci.reshape(B, Wd * Wd)
+        if cd is not None:
+            lp = twopass_logprobs(W, emb, hw, w2_sl, cd, h, lastp.reshape(B * Wd, order), order, step, B)
+            cv, ii = lp.topk(Wd, dim=-1)                                # [B, W, W]
+            cv = cv.reshape(B * Wd, Wd)
+            ci = cd.gather(1, ii.reshape(B, Wd * Wd))
+        else:
+            _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * Wd, order), order, step)
+            cv, ci = lp.topk(Wd, dim=-1)                                # [B*W, W]
+            ci = ci.reshape(B, Wd * Wd)
         cand = (cum.reshape(B * Wd, 1) + cv).reshape(B, Wd * Wd)
         cum, flat = cand.topk(Wd, dim=-1)
         src = flat // Wd
@@ -58,7 +93,7 @@ def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int
 
 
 def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, topb: int,
-              depth: int):
+              depth: int, twopass_m: int = 0):
     """Tree draft: every surviving extension becomes a BFS-ordered node. Returns [B, 2N]
     = N global token ids followed by N parent node indices (-1 for depth-1 nodes)."""
     B, dev = pred.shape[0], pred.device
@@ -71,11 +106,18 @@ def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, t
     toks, pars = [], []
     base = 0
     nstep = min(depth, pred.shape[1] - 1)
+    cd = twopass_candidates(hw, pred, 1, nstep + 1, twopass_m) if twopass_m and nstep > 0 else None
     for step in range(1, nstep + 1):
         h = pred[:, step].float().unsqueeze(1).expand(B, fr, -1).reshape(B * fr, -1)
-        _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * fr, order), order, step)
-        cv, ci = lp.topk(topb, dim=-1)                                  # [B*fr, TB]
-        ci = ci.reshape(B, fr * topb)
+        if cd is not None:
+            lp = twopass_logprobs(W, emb, hw, w2_sl, cd, h, lastp.reshape(B * fr, order), order, step, B)
+            cv, ii = lp.topk(topb, dim=-1)                              # [B, fr, TB]
+            cv = cv.reshape(B * fr, topb)
+            ci = cd.gather(1, ii.reshape(B, fr * topb))
+        else:
+            _, lp = head_logprobs(W, emb, hw, w2_sl, h, lastp.reshape(B * fr, order), order, step)
+            cv, ci = lp.topk(topb, dim=-1)                              # [B*fr, TB]
+            ci = ci.reshape(B, fr * topb)
         cand = (cum.reshape(B * fr, 1) + cv).reshape(B, fr * topb)
         k = min(keep, fr * topb)
         cum, flat = cand.topk(k, dim=-1)
