@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
                          "eager PyTorch fp16 on the GPU (the reference's eager GPU draft)")
+    ap.add_argument("--twopass", type=int, default=0, metavar="M",
+                    help="the two-pass candidate head with M candidates (the reference's CF_TWOPASS_M; "
+                         "its default is 8192); 0 = the one-pass head BASELINE specifies")
     ap.add_argument("--head-shard", default="auto", choices=["auto", "on", "off"],
                     help="row-shard the shortlist head across the GPUs (auto: the 27B shape on >1 GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -274,6 +277,10 @@ def run_ours(args, wl):
 
     B = args.batch
     shard = world > 1 and (args.head_shard == "on" or (args.head_shard == "auto" and wl.hidden >= 5120))
+    if args.twopass:
+        if shard:
+            raise SystemExit("--twopass runs on unsharded heads only")
+        os.environ["CF_TWOPASS_M"] = str(args.twopass)
     sd, emb, lm, sl = make_state(wl, seed=0, device=dev)
     # sharded head: every rank drafts the same requests (same inputs and noise), each over its
     # share of the head rows; otherwise each rank drafts its own requests
@@ -311,7 +318,7 @@ def run_ours(args, wl):
     # requests that is one persistent-engine launch; above it, the wide plan's launch list
     # (tcgen05 GEMMs and row kernels); a sharded head runs engine plans of MAX_PLAN_BATCH.
     from chain_flow_b200.proposer import MAX_PLAN_BATCH
-    wide = B > MAX_PLAN_BATCH and not shard
+    wide = B > MAX_PLAN_BATCH and not shard and not args.twopass
     plan = prop._wide_plan(_lib.MODE_CHAIN, B) if wide else prop._plan(_lib.MODE_CHAIN, min(B, MAX_PLAN_BATCH))
     plans_per_step = 1 if wide else (B + MAX_PLAN_BATCH - 1) // MAX_PLAN_BATCH
     torch.cuda.synchronize(dev)
@@ -350,7 +357,7 @@ def run_ours(args, wl):
     # phase table); its wall is from the previous phase's last grid-barrier pass to its own.
     head = None
     peak_hbm = measured_peaks()[0]
-    if not wide and not shard and rank == 0:
+    if not wide and not shard and rank == 0 and not args.twopass:
         from chain_flow_b200.engine import Plan
         if prop.vae is not None:        # the beam plan of a production draft, on that draft's hidden states
             pp = Plan(prop.weights, _lib.MODE_BEAM_CHAIN, min(B, MAX_PLAN_BATCH), width=wl.width,
@@ -395,7 +402,8 @@ def run_ours(args, wl):
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0)   # per GPU, per plan
+        algo = wl.weight_bytes_per_draft(head_fraction=1.0 / world if shard else 1.0, twopass_m=args.twopass,
+                                         batch=min(B, MAX_PLAN_BATCH))   # per GPU, per plan
         achieved = algo / (kernel_ms / 1e3) / 1e9
         flops = wl.flops_per_draft(B if wide else min(B, MAX_PLAN_BATCH))
         tpeak, tpeak_kind = measured_tensor_peak()
@@ -417,6 +425,8 @@ def run_ours(args, wl):
                        "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
                        "ffn_multiplier": wl.ffn, "shortlist_rows": wl.shortlist_rows,
                        "beam_width": wl.width, "plans_per_step": plans_per_step,
+                       "head": (f"two-pass, {args.twopass} shared candidates (CF_TWOPASS_M)" if args.twopass
+                                else "one-pass fused top-k (CF_TWOPASS_M=0)"),
                        **({"vae": {"latent": wl.latent, "intermediate": wl.vae_inter, "layers": wl.vae_layers,
                                    "heads": wl.vae_heads},
                            "draft_length": wl.draft_length, "chunk": wl.chunk, "path_order": wl.path_order}

@@ -32,10 +32,11 @@ EXPORTED = [
     "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify", "cfb_vae_workspace", "cfb_vae_create",
     "cfb_vae_plan_workspace", "cfb_vae_plan_build",
 ]
-ABI_VERSION = 2
+ABI_VERSION = 3
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
-BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF, BUF_PHASES = range(10)
-PK_PREP, PK_GEMM, PK_ATTN, PK_BEAM, PK_RMERGE, PK_GATHER = range(6)   # CFB_BUF_PHASES [0]
+BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF, BUF_PHASES, \
+    BUF_TP_CAND, BUF_TP_CHEAD = range(12)
+PK_PREP, PK_GEMM, PK_ATTN, PK_BEAM, PK_RMERGE, PK_GATHER, PK_TPXA, PK_TPSEL, PK_TPGATH = range(9)  # CFB_BUF_PHASES [0]
 PO_NONE, PO_BEAM_CHAIN, PO_BEAM_TREE, PO_PUBLISH = range(4)        # CFB_BUF_PHASES [6]
 RUN_PROFILE = 1
 EPI_F32, EPI_F16, EPI_GELU16, EPI_PART = 0, 1, 2, 3      # cfb_wide_gemm epilogues
@@ -76,7 +77,8 @@ class Run(C.Structure):
                 ("tree_keep", C.c_int), ("tree_topb", C.c_int), ("grid", C.c_int), ("flags", C.c_int),
                 ("ctx", C.c_void_p), ("z0", C.c_void_p), ("known0", C.c_void_p),
                 ("pred", C.c_void_p), ("tokens", C.c_void_p),
-                ("ranks", C.c_int), ("rank", C.c_int), ("xloc", C.c_void_p), ("xall", C.c_void_p)]
+                ("ranks", C.c_int), ("rank", C.c_int), ("xloc", C.c_void_p), ("xall", C.c_void_p),
+                ("twopass_m", C.c_int)]
 
 
 class VaeLayer(C.Structure):

@@ -95,7 +95,9 @@ enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_P
                    EK_HEADIN = 5, EK_HEAD = 6, EK_STORE16 = 7 };
 // the plan mode of a VAE side (cfb_vae_plan_build): not a cfb_mode the caller can ask for
 constexpr int kModeVae = 16;
-enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4, PK_GATHER = 5 };
+enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE = 4, PK_GATHER = 5,
+                   PK_TPXA = 6, PK_TPSEL = 7, PK_TPGATH = 8, PK_TPKEY = 9, PK_TPRAD = 10,
+                   PK_TPCNT = 11 };   // 6-11: the two-pass head
 enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
 // Attention of one (expert, block): q rows [B*Sq] and k/v rows [B*Kn] (fp32, written by the
@@ -134,6 +136,10 @@ struct alignas(16) Job {
   float2* ostats; int onparts;
   int e_idx, step, last_step, wrows, nlive, R, topb;
   int rowoff;                              // EK_HEAD: shortlist row of the head's first row
+  // EK_HEAD of the two-pass head: pass A stores the raw scores [rows, R] (logits); pass B maps
+  // column c to shortlist row cand[c] and scores row r only against the columns of its own
+  // request (c / cmask == r / wrows)
+  float* logits; const int* cand; int cmask;
   float dt;
   const float* p0;                         // EK_PATHH: offset biases [order][D]
 };
@@ -147,6 +153,10 @@ struct Phase {
   int step, rows, fr, keep, topb, base, base_prev, last;
 };
 static_assert(sizeof(Phase) == 15 * sizeof(int), "CFB_BUF_PHASES record");
+// Phase.last of a GEMM phase (unused by GEMM phases otherwise): its weights are written by an
+// earlier phase of the same launch, so the weight producer may stream them only once the workers
+// have entered the phase
+constexpr int kWeightsWritten = 2;
 static_assert(sizeof(Phase) <= kPhaseSlot, "descriptor cache slot");
 static_assert(sizeof(Job) % 16 == 0 && kJobCache * sizeof(Job) / 16 <= 64, "descriptor cache copy");
 static_assert(sizeof(AttnTask) % 16 == 0, "descriptor cache copy");
@@ -193,6 +203,14 @@ struct Plan {
   // tiled into vin16 by prep; the residual stream vx32 [B * vS, D] starts at pos[row % vS]
   const void* vin; int vin32, vS, vDin;
   __half* vin16; float* vx32; const float* vpos;
+  // the two-pass head (tp_m > 0): tp_n marginal rows per request (depths 1..tp_n), their fp16
+  // head input txa, pass A's scores tlog [B * tp_n, R], the candidates' keys tkeys [B, R], the
+  // candidate set tcd [B, tp_m] (shortlist rows, ascending) and its packed head rows tchead
+  int tp_m, tp_n, tp_rs;    // tp_rs: the key rows' stride (R rounded up to 4)
+  unsigned* thist;          // [4][B][256] radix histograms of the keys, one byte per pass
+  int* tcnt;                // [B][G][2] per-CTA counts of keys above / at the threshold
+  const uint4* tp_head;     // the packed full shortlist head the candidates are read from
+  __half* txa; float* tlog; unsigned* tkeys; int* tcd; uint4* tchead;
 };
 
 struct Smem {
@@ -675,12 +693,17 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     case EK_HEAD: {
       const RowMap M = row_map(rows, E.t);
       if (M.r < rows) {
+        const int rq = J.cmask ? M.r / J.wrows : 0;
         for (int f = M.q * M.nf; f < (M.q + 1) * M.nf; ++f) {
           const int j = col0 + f;
           if (j >= J.R) break;
           const float v = S.red[f * S.rp + M.r];
+          if (J.logits) J.logits[(size_t)M.r * J.R + j] = v;
+          if (J.cmask && j / J.cmask != rq) continue;
           if (v > H.m) { H.s = H.s * __expf(H.m - v) + 1.f; H.m = v; }
           else H.s += __expf(v - H.m);
+          // pass B: a candidate column; the candidates of a request are in ascending shortlist
+          // order, so ties still go to the lower shortlist id (mapped when the lists are published)
           top_insert(H, J.topb, v, j + J.rowoff);
         }
       }
@@ -1010,6 +1033,19 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
   for (int p = p0; p < p1 && ok; ++p) {
     const Phase& ph = P.phases[p];
     if (ph.kind != PK_GEMM) continue;
+    if (ph.last == kWeightsWritten) {
+      // these weights are written by an earlier phase of this launch (the two-pass head's
+      // gathered candidate rows): stream them only once the workers have entered this phase
+      const unsigned long long t0 = globaltimer();
+      for (unsigned it = 1; *S.phase_ready < p; ++it) {
+        if (it % kPollsPerCheck) continue;
+        if (ld_volatile_int(P.err) != 0) { ok = false; break; }
+        if (globaltimer() - t0 > kWaitBudgetNs) { set_err(P, DEV_TIMEOUT_SLOT); ok = false; break; }
+      }
+      if (!ok) break;
+      __threadfence();
+      fence_proxy_async_global();
+    }
     unsigned long long waited = 0;
     const Job* jt = P.jobs + ph.job0;
     const UnitRange cu = cta_units(P, ph, jt);
@@ -1203,6 +1239,10 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
   const long long gtid = (long long)blockIdx.x * W.n + W.t;
   const long long gthreads = (long long)P.G * W.n;
   for (long long i = gtid; i < P.ntilecnt; i += gthreads) P.tilecnt[i] = 0u;
+  if (P.tp_m) {   // the two-pass head's radix histograms and per-CTA counts start at zero
+    for (long long i = gtid; i < 4LL * P.B * 256; i += gthreads) P.thist[i] = 0u;
+    for (long long i = gtid; i < 2LL * P.B * P.G; i += gthreads) P.tcnt[i] = 0;
+  }
   if (P.mode == kModeVae) {
     // the input rows, unit-tiled for the in-projection's activation copies; the residual stream
     // starts at the learned position rows (the in-projection adds to it)
@@ -1292,7 +1332,7 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
 // ------------------------------------------------------------------------------------------
 // after the head GEMM: every CTA publishes its (max, sumexp, top-TB) per beam row, merging the
 // row's slice lanes (their sorted lists) by TB rounds of a lane argmax
-__device__ __noinline__ void head_post(const Plan& P, const Phase& ph, HeadState& H, const Grp& E) {
+__device__ __noinline__ void head_post(const Plan& P, const Phase& ph, const Job* jt, HeadState& H, const Grp& E) {
   const int rows = ph.rows, TB = ph.topb;
   const RowMap M = row_map(rows, E.t);
   float m = H.m, ssum = H.s;
@@ -1308,7 +1348,12 @@ __device__ __noinline__ void head_post(const Plan& P, const Phase& ph, HeadState
     int own = M.q;
     argmax_lanes(v, id, own, M.sl);
     if (own == M.q) ++nxt;
-    if (writer) { __stcg(hp + 2 + round, v); __stcg(hp + 2 + kTopMax + round, __int_as_float(id)); }
+    if (writer) {
+      // pass B of the two-pass head: candidate column -> shortlist row
+      const int* cand = jt ? jt[0].cand : nullptr;
+      const int gid = (cand && id >= 0 && id < jt[0].R) ? __ldcg(cand + id) : id;
+      __stcg(hp + 2 + round, v); __stcg(hp + 2 + kTopMax + round, __int_as_float(gid));
+    }
   }
 }
 
@@ -1528,6 +1573,293 @@ __device__ __noinline__ void gather_phase(const Plan& P, const Phase& ph, const 
   path_gather(P, ph.fr, P.B * ph.fr, 0, P.B * ph.fr, min(ph.step, P.order), false, t, nt);
 }
 
+// ---- the two-pass candidate head (reference CF_TWOPASS_M with a shared candidate set,
+// flow_proposer.py:1142-1184) --------------------------------------------------------------
+// Pass A input: the marginal hiddens pred[b, 1 + j] (j < tp_n) as fp16 head-input rows, zero in
+// the markov columns (pass A has no markov bias).
+__device__ __noinline__ void tpxa_phase(const Plan& P, const Grp& W) {
+  const int D = P.D, K = D + P.rank, n = P.tp_n, rows = P.B * n;
+  const long long nt = (long long)P.G * W.n;
+  for (long long i = (long long)blockIdx.x * W.n + W.t; i < (long long)rows * K; i += nt) {
+    const int r = (int)(i / K), c = (int)(i - (long long)r * K);
+    const int b = r / n, j = r - b * n;
+    const float v = c < D ? P.pred[((size_t)b * P.DL + 1 + j) * D + c] : 0.f;
+    P.txa[tidx(rows, r, c)] = __float2half_rn(v);
+  }
+}
+
+// Histogram increment aggregated over the lanes of a warp that hit the same bin (the keys of
+// one request crowd into few bins, and same-address shared atomics serialise). All lanes of the
+// warp must call it; `live` = false contributes nothing.
+CFB_DEV void hist_add(unsigned* hist, unsigned bin, bool live) {
+  const unsigned act = __ballot_sync(0xffffffffu, live);
+  if (!act) return;
+  const int lane = threadIdx.x & 31, first = __ffs(act) - 1;
+  const unsigned b0 = __shfl_sync(0xffffffffu, bin, first);
+  if (__all_sync(0xffffffffu, !live || bin == b0)) {          // the common case: one bin
+    if (lane == first) atomicAdd(&hist[b0], (unsigned)__popc(act));
+    return;
+  }
+  const unsigned same = __match_any_sync(0xffffffffu, live ? bin : 0xffffffffu) & act;
+  if (live && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned)__popc(same));
+}
+
+// order-preserving map of a float to uint32 (larger float -> larger key)
+CFB_DEV unsigned float_key(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---- pass A's top-tp_m selection, over the whole grid: keys, then a byte-wise radix select ----
+// Each CTA owns a contiguous range of the B x tp_rs keys (at most two requests, since G >= B).
+struct KeyRange { long long e0, e1; int b0, b1; };
+CFB_DEV KeyRange key_range(const Plan& P) {
+  const long long total = (long long)P.B * P.tp_rs, per = (total + P.G - 1) / P.G;
+  KeyRange kr;
+  kr.e0 = min(total, (long long)blockIdx.x * per);
+  kr.e1 = min(total, kr.e0 + per);
+  kr.b0 = (int)(kr.e0 / P.tp_rs);
+  kr.b1 = kr.e1 > kr.e0 ? (int)((kr.e1 - 1) / P.tp_rs) : kr.b0 - 1;
+  return kr;
+}
+
+// The select state after `passes` radix passes of request b (one warp, every lane gets it):
+// the key prefix so far, its mask, and how many keys equal to the prefix are still needed.
+// cnt(>= bin) is a suffix sum over the lanes' 8 bins each; the digit is the bin where the count
+// from the top first reaches `need`.
+CFB_DEV void radix_state(const Plan& P, int b, int passes, unsigned& prefix, unsigned& pmask, int& need) {
+  const int lane = threadIdx.x & 31;
+  prefix = 0u; pmask = 0u; need = P.tp_m;
+  for (int p = 0; p < passes; ++p) {
+    const int shift = 24 - 8 * p;
+    const uint4* hp = reinterpret_cast<const uint4*>(P.thist + ((size_t)p * P.B + b) * 256) + 2 * lane;
+    const uint4 h0 = __ldcg(hp), h1 = __ldcg(hp + 1);
+    const unsigned h[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    int c = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c += (int)h[i];
+    int suf = c;                                         // keys in bins >= 8 * lane
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_down_sync(0xffffffffu, suf, off);
+      if (lane + off < 32) suf += o;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, suf >= need);
+    const int L = hit ? 31 - __clz(hit) : 0;             // the highest lane whose suffix reaches need
+    const int above = __shfl_sync(0xffffffffu, suf - c, L);   // keys in bins above lane L's
+    int d = 0, nd = 0;
+    if (lane == L) {
+      int cum = above, i = 7;
+      for (; i > 0; --i) {
+        if (cum + (int)h[i] >= need) break;
+        cum += (int)h[i];
+      }
+      d = 8 * L + i; nd = need - cum;
+    }
+    d = __shfl_sync(0xffffffffu, d, L);
+    nd = __shfl_sync(0xffffffffu, nd, L);
+    prefix |= (unsigned)d << shift;
+    pmask |= 255u << shift;
+    need = nd;
+  }
+}
+
+// Keys of this CTA's range (and, for pass 0, the histogram of their top byte): the log-sum-exp
+// of each marginal row from the head phase's per-CTA (max, sumexp), each shortlist row's best
+// log-prob over the depths as an order-preserving uint32 (row stride padded to 4 with zeros).
+// pass > 0 (PK_TPRAD): the histogram of byte `pass` of the keys that match the prefix so far.
+__device__ __noinline__ void tprad_phase(const Plan& P, Smem& S, const Grp& W, int pass) {
+  const KeyRange kr = key_range(P);
+  if (kr.e0 >= kr.e1) return;
+  const int n = P.tp_n, R = P.R, Rs = P.tp_rs, nb = kr.b1 - kr.b0 + 1;
+  const int warp = W.t >> 5, lane = W.t & 31, nw = W.n >> 5;
+  unsigned* hist = reinterpret_cast<unsigned*>(S.scratch);                 // [2][256]
+  float* lse = reinterpret_cast<float*>(hist + 512);                        // [2][kMaxDepth]
+  unsigned* st = reinterpret_cast<unsigned*>(lse + 2 * kMaxDepth);        // [2][2]: prefix, mask
+  for (int i = W.t; i < 512; i += W.n) hist[i] = 0u;
+  if (pass == 0) {
+    for (int q = warp; q < nb * n; q += nw) {
+      const int row = (kr.b0 + q / n) * n + q % n;
+      float m = -INFINITY, s = 0.f;
+      for (int c = lane; c < P.G; c += 32) {
+        const float* hp = P.hpart + ((size_t)c * kRowsMax + row) * kHeadPartFloats;
+        lse_merge(m, s, __ldcg(hp), __ldcg(hp + 1));
+      }
+      lse_lanes(m, s, 32);
+      if (lane == 0) lse[q] = m + logf(s);
+    }
+  } else if (warp < nb) {
+    unsigned pre, msk; int need;
+    radix_state(P, kr.b0 + warp, pass, pre, msk, need);
+    if (lane == 0) { st[2 * warp] = pre; st[2 * warp + 1] = msk; }
+  }
+  gsync(W);
+  const int shift = 24 - 8 * pass;
+  for (long long e0 = kr.e0 + warp * 32; e0 < kr.e1; e0 += W.n) {   // whole warps
+    const long long e = e0 + lane;
+    const bool in = e < kr.e1;
+    const int b = in ? (int)(e / Rs) : kr.b0, r = in ? (int)(e - (long long)b * Rs) : 0;
+    const int bl = b - kr.b0;
+    unsigned k = 0u;
+    if (pass == 0) {
+      if (in && r < R) {
+        const float* lg = P.tlog + (size_t)b * n * R + r;
+        float v[kMaxDepth];
+#pragma unroll
+        for (int j = 0; j < kMaxDepth; ++j) v[j] = j < n ? __ldcg(lg + (size_t)j * R) : -INFINITY;
+        float best = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kMaxDepth; ++j) if (j < n) best = fmaxf(best, v[j] - lse[bl * n + j]);
+        k = float_key(best);
+      }
+      if (in) P.tkeys[e] = k;
+    } else if (in) {
+      k = __ldcg(P.tkeys + e);
+    }
+    const bool live = in && r < R && (pass == 0 || (k & st[2 * bl + 1]) == st[2 * bl]);
+    hist_add(hist + 256 * bl, (k >> shift) & 255u, live);
+  }
+  gsync(W);
+  for (int i = W.t; i < nb * 256; i += W.n)
+    if (hist[i]) atomicAdd(P.thist + ((size_t)pass * P.B + kr.b0 + i / 256) * 256 + (i & 255), hist[i]);
+}
+
+// After the four passes: the threshold key T (the tp_m-th largest) and `need` keys equal to it.
+// PK_TPCNT: this CTA's counts of keys above and at T, per request. PK_TPSEL: each CTA writes its
+// picks at the offset the counts of the CTAs before it give, in ascending shortlist order (ties
+// at T go to the lower rows); threads own contiguous sub-ranges placed by one block scan.
+__device__ __noinline__ void tpsel_phase(const Plan& P, Smem& S, const Grp& W, bool write) {
+  const KeyRange kr = key_range(P);
+  if (kr.e0 >= kr.e1) return;
+  const int R = P.R, Rs = P.tp_rs, M = P.tp_m, nb = kr.b1 - kr.b0 + 1;
+  const int warp = W.t >> 5, lane = W.t & 31, nw = W.n >> 5;
+  int* sc = reinterpret_cast<int*>(S.scratch);              // [2][8]: T, need, gbase, ebase; [2 * 32 + 2] scan
+  if (warp < nb) {
+    const int b = kr.b0 + warp;
+    unsigned pre, msk; int need;
+    radix_state(P, b, 4, pre, msk, need);
+    int gb = 0, eb = 0;
+    if (write) {                                            // counts of the CTAs before this one
+      for (int c = lane; c < (int)blockIdx.x; c += 32) {
+        gb += __ldcg(P.tcnt + ((size_t)b * P.G + c) * 2);
+        eb += __ldcg(P.tcnt + ((size_t)b * P.G + c) * 2 + 1);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        gb += __shfl_xor_sync(0xffffffffu, gb, off);
+        eb += __shfl_xor_sync(0xffffffffu, eb, off);
+      }
+    }
+    if (lane == 0) { sc[8 * warp] = (int)pre; sc[8 * warp + 1] = need; sc[8 * warp + 2] = gb; sc[8 * warp + 3] = eb; }
+  }
+  gsync(W);
+  int* scan = sc + 16;
+  for (int bl = 0; bl < nb; ++bl) {
+    const int b = kr.b0 + bl;
+    const long long lo = max(kr.e0, (long long)b * Rs), hi = min(kr.e1, (long long)(b + 1) * Rs);
+    const unsigned T = (unsigned)sc[8 * bl];
+    const int need = sc[8 * bl + 1];
+    const long long chunk = (hi - lo + W.n - 1) / W.n;
+    const long long t0 = min(hi, lo + W.t * chunk), t1 = min(hi, t0 + chunk);
+    int gt = 0, eq = 0;
+    for (long long e = t0; e < t1; ++e) {
+      const int r = (int)(e - (long long)b * Rs);
+      const unsigned k = __ldcg(P.tkeys + e);
+      if (r < R) { gt += k > T; eq += k == T; }
+    }
+    int ag = gt, ae = eq;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int ug = __shfl_up_sync(0xffffffffu, ag, off), ue = __shfl_up_sync(0xffffffffu, ae, off);
+      if (lane >= off) { ag += ug; ae += ue; }
+    }
+    if (lane == 31) { scan[2 + 2 * warp] = ag; scan[3 + 2 * warp] = ae; }
+    gsync(W);
+    if (W.t == 0) {
+      int sg = 0, se = 0;
+      for (int w = 0; w < nw; ++w) {
+        const int tg = scan[2 + 2 * w], te = scan[3 + 2 * w];
+        scan[2 + 2 * w] = sg; scan[3 + 2 * w] = se;
+        sg += tg; se += te;
+      }
+      scan[0] = sg; scan[1] = se;
+    }
+    gsync(W);
+    if (!write) {
+      if (W.t == 0) {
+        P.tcnt[((size_t)b * P.G + blockIdx.x) * 2] = scan[0];
+        P.tcnt[((size_t)b * P.G + blockIdx.x) * 2 + 1] = scan[1];
+      }
+    } else {
+      const int gbase = sc[8 * bl + 2] + scan[2 + 2 * warp] + ag - gt;
+      const int ebase = sc[8 * bl + 3] + scan[3 + 2 * warp] + ae - eq;
+      int pos = gbase + min(ebase, need), seen = ebase;
+      int* out = P.tcd + (size_t)b * M;
+      for (long long e = t0; e < t1; ++e) {
+        const int r = (int)(e - (long long)b * Rs);
+        if (r >= R) continue;
+        const unsigned k = __ldcg(P.tkeys + e);
+        // (pos < M always holds: the picks are the rows above T plus `need` rows at T)
+        if (k > T) { if (pos < M) out[pos] = r; ++pos; }
+        else if (k == T) { if (seen < need && pos < M) out[pos++] = r; ++seen; }
+      }
+    }
+    gsync(W);
+  }
+}
+
+// The candidate head: the rows tcd of the packed shortlist head, packed in the same layout (cfb_pack.cu)
+// as one [B * tp_m, D + rank] matrix, read from the packed full head: a 16 x 16 block of a
+// packed matrix holds row g's (and g + 8's) column pairs 2t and 2t + 8 in lane 4g + t. A warp
+// takes one 16-row group and a range of 16-column blocks: the two source rows of each lane are
+// looked up once, then 4 blocks' loads are in flight at a time.
+__device__ __noinline__ void tpgath_phase(const Plan& P, const Grp& W, const uint4* head) {
+  const int Kt = (P.D + P.rank) / 16;
+  const int nout = P.B * P.tp_m, Mt = (nout + 63) / 64 * 4;
+  constexpr int kKbChunk = 22, kU = 8;
+  const int nkc = (Kt + kKbChunk - 1) / kKbChunk;
+  const int lane = W.t & 31, g = lane >> 2, t = lane & 3;
+  const long long tasks = (long long)Mt * nkc;
+  const long long wg = (long long)blockIdx.x * (W.n >> 5) + (W.t >> 5), nwg = (long long)P.G * (W.n >> 5);
+  const uint32_t* hw = reinterpret_cast<const uint32_t*>(head);
+  for (long long task = wg; task < tasks; task += nwg) {
+    const int m = (int)(task / nkc), c = (int)(task - (long long)m * nkc);
+    size_t base[2];
+    int hs[2];
+    bool live[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = m * 16 + g + 8 * h;
+      live[h] = row < nout;
+      int s = live[h] ? __ldcg(P.tcd + row) : 0;
+      s = min(max(s, 0), P.R - 1);                       // (always in range; never read outside)
+      const int ms = s >> 4, rs = s & 15;
+      hs[h] = rs >> 3;
+      base[h] = ((size_t)(ms >> 2) * Kt * 4 + (ms & 3)) * 32 + (rs & 7) * 4 + t;   // uint4 index at kb = 0
+    }
+    const int kb0 = c * kKbChunk, kb1 = min(Kt, kb0 + kKbChunk);
+    for (int kb = kb0; kb < kb1; kb += kU) {
+      uint32_t w[kU][4];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int k = kb + u;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int h = q & 1;
+          w[u][q] = (k < kb1 && live[h]) ? __ldg(hw + (base[h] + (size_t)k * 128) * 4 + hs[h] + (q & 2)) : 0u;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int k = kb + u;
+        if (k < kb1)
+          P.tchead[(((long long)(m >> 2) * Kt + k) * 4 + (m & 3)) * 32 + lane] =
+              make_uint4(w[u][0], w[u][1], w[u][2], w[u][3]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // Runs phases [p0, p1) of the plan: the whole table, or one segment of a sharded-head plan.
 // The phases that run once per draft or per depth (prep, attention, beam, gathers) are out of
@@ -1626,13 +1958,25 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
       beam_phase(P, ph, S, Wk, P.prof ? prow : nullptr);
     } else if (ph.kind == PK_GATHER) {
       gather_phase(P, ph, Wk);
+    } else if (ph.kind == PK_TPXA) {
+      tpxa_phase(P, Wk);
+    } else if (ph.kind == PK_TPKEY) {
+      tprad_phase(P, S, Wk, 0);
+    } else if (ph.kind == PK_TPRAD) {
+      tprad_phase(P, S, Wk, ph.step);
+    } else if (ph.kind == PK_TPCNT) {
+      tpsel_phase(P, S, Wk, false);
+    } else if (ph.kind == PK_TPSEL) {
+      tpsel_phase(P, S, Wk, true);
+    } else if (ph.kind == PK_TPGATH) {
+      tpgath_phase(P, Wk, P.tp_head);
     } else if (ph.kind == PK_RMERGE) {
       rmerge_phase(P, ph, S, Wk);
     } else {
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
         epi_phase(P, ph, jt, tseq, S, H, E, wc);
-        if (ph.post != PO_NONE) head_post(P, ph, H, E);
+        if (ph.post != PO_NONE) head_post(P, ph, jt, H, E);
         if (rec) {
           prow[5] = wc.slot; prow[6] = globaltimer();
           prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
@@ -1830,7 +2174,16 @@ cfb_status lower(Builder& B, size_t* bytes) {
         !lin_ok(d.path_down, D, d.path_up.nout) || !d.path_offset_bias || !d.path_down.bias ||
         d.path_up.nout % 16)
       return CFB_ERR_INVALID_ARG;
+    // the two-pass head: candidates from the whole head, on one GPU; every request's marginal
+    // rows fit one head job
+    if (r.twopass_m < 0) return CFB_ERR_INVALID_ARG;
+    if (r.twopass_m > 0 && (r.ranks > 1 || r.twopass_m >= d.shortlist_rows || Bq * K > cfb::kRowsMax ||
+                            (long long)Bq * r.twopass_m > (1LL << 30)))
+      return CFB_ERR_UNSUPPORTED;
+  } else if (r.twopass_m != 0) {
+    return CFB_ERR_INVALID_ARG;
   }
+  const int TPM = beam ? r.twopass_m : 0;
   int G = r.grid;
   if (G <= 0) {
     int dev = 0, sms = 0;
@@ -1840,6 +2193,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
     G = sms;
   }
   B.G = G;
+  if (TPM && G < Bq) return CFB_ERR_UNSUPPORTED;          // a CTA's key range spans <= 2 requests
   // the beam merge: each thread follows at most kMaxLists of the G published lists per row
   if (beam && (G + 32 * std::max(1, (cfb::kWorkers / 32) / Wmax) - 1) / (32 * std::max(1, (cfb::kWorkers / 32) / Wmax)) > cfb::kMaxLists)
     return CFB_ERR_UNSUPPORTED;
@@ -1899,6 +2253,17 @@ cfb_status lower(Builder& B, size_t* bytes) {
     o_mpath = A.take((size_t)rowsB * k128(P2) * 2);
     o_xhead = A.take((size_t)rowsB * k128(D + rank) * 2);
     o_pg = A.take((size_t)rowsB * k128(order * D) * 2);
+  }
+  size_t o_txa = 0, o_tlog = 0, o_tkeys = 0, o_tcd = 0, o_tchead = 0, o_thist = 0, o_tcnt = 0;
+  if (TPM) {
+    const size_t rowsA = (size_t)Bq * K, nc = (size_t)Bq * TPM;
+    o_txa = A.take(rowsA * k128(D + rank) * 2);
+    o_tlog = A.take(rowsA * d.shortlist_rows * 4);
+    o_tkeys = A.take((size_t)Bq * ((d.shortlist_rows + 3) / 4 * 4) * 4);
+    o_tcd = A.take(nc * 4);
+    o_thist = A.take((size_t)4 * Bq * 256 * 4);
+    o_tcnt = A.take((size_t)Bq * G * 2 * 4);
+    o_tchead = A.take((nc + 63) / 64 * 64 * (size_t)(D + rank) * 2);
   }
   const size_t o_gpart = A.take((size_t)G * cfb::kTileRows * cfb::kRowsMax * 4);
   const bool profile = (r.flags & CFB_RUN_PROFILE) != 0;
@@ -2090,6 +2455,23 @@ cfb_status lower(Builder& B, size_t* bytes) {
   }
   if (beam) {
     int fr = tree ? 1 : Wmax, base = 0, base_prev = 0;
+    if (TPM) {   // pass A of the two-pass head: candidates for every depth from one head GEMM
+      { cfb::Phase p{}; p.kind = cfb::PK_TPXA; ph.push_back(p); }
+      {
+        cfb::Job J = make_job(d.head, Bq * K);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_txa); J.ldx = D + rank;
+        J.ekind = cfb::EK_HEAD; J.R = d.head.nout; J.rowoff = 0; J.topb = 1;
+        J.bias = nullptr; J.colsum = nullptr; J.logits = B.dptr<float>(o_tlog);
+        cfb::Phase p{};
+        p.post = cfb::PO_PUBLISH; p.rows = Bq * K; p.topb = 1;
+        add_phase(B, p, {J});
+      }
+      { cfb::Phase p{}; p.kind = cfb::PK_TPKEY; ph.push_back(p); }
+      for (int pass = 1; pass < 4; ++pass) { cfb::Phase p{}; p.kind = cfb::PK_TPRAD; p.step = pass; ph.push_back(p); }
+      { cfb::Phase p{}; p.kind = cfb::PK_TPCNT; ph.push_back(p); }
+      { cfb::Phase p{}; p.kind = cfb::PK_TPSEL; ph.push_back(p); }
+      { cfb::Phase p{}; p.kind = cfb::PK_TPGATH; ph.push_back(p); }
+    }
     const int TB = tree ? r.tree_topb : r.width;
     for (int step = 1; step <= K; ++step) {
       const int rows = Bq * fr;
@@ -2122,7 +2504,18 @@ cfb_status lower(Builder& B, size_t* bytes) {
         J.step = step; J.wrows = fr;
         add_phase(B, cfb::Phase{}, {J});
       }
-      {   // shortlist head + markov bias with online LSE + top-k per CTA
+      if (TPM) {   // pass B: every beam row against its own request's candidate rows only
+        cfb_linear cl{B.dptr<void>(o_tchead), nullptr, nullptr, Bq * TPM, D + rank};
+        cfb::Job J = make_job(cl, rows);
+        J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_xhead); J.ldx = D + rank;
+        J.ekind = cfb::EK_HEAD; J.R = Bq * TPM; J.rowoff = 0; J.topb = TB;
+        J.bias = nullptr; J.colsum = nullptr;
+        J.cand = B.dptr<int>(o_tcd); J.cmask = TPM; J.wrows = fr;
+        cfb::Phase p{};
+        p.post = cfb::PO_PUBLISH; p.rows = rows; p.topb = TB;
+        if (step == 1) p.last = cfb::kWeightsWritten;
+        add_phase(B, p, {J});
+      } else {   // shortlist head + markov bias with online LSE + top-k per CTA
         cfb::Job J = make_job(d.head, rows);
         J.xkind = cfb::XK_F16; J.x = B.dptr<__half>(o_xhead); J.ldx = D + rank;
         J.ekind = cfb::EK_HEAD; J.R = d.head.nout; J.rowoff = d.head_row0; J.topb = TB;
@@ -2276,6 +2669,16 @@ cfb_status lower(Builder& B, size_t* bytes) {
     P.shortlist = d.shortlist; P.markov_w1 = static_cast<const __half*>(d.markov_w1);
     P.xhead = B.dptr<__half>(o_xhead); P.ldxhead = D + rank;
     P.emb = static_cast<const __half*>(d.embed); P.pg = B.dptr<__half>(o_pg);
+    P.tp_m = TPM; P.tp_n = TPM ? K : 0; P.tp_rs = (d.shortlist_rows + 3) / 4 * 4;
+    if (TPM) {
+      P.tp_head = static_cast<const uint4*>(d.head.w);
+      P.txa = B.dptr<__half>(o_txa); P.tlog = B.dptr<float>(o_tlog); P.tkeys = B.dptr<unsigned>(o_tkeys);
+      P.tcd = B.dptr<int>(o_tcd); P.tchead = B.dptr<uint4>(o_tchead);
+      P.thist = B.dptr<unsigned>(o_thist); P.tcnt = B.dptr<int>(o_tcnt);
+      P.buf[CFB_BUF_TP_CAND] = P.tcd; P.buf_bytes[CFB_BUF_TP_CAND] = (size_t)Bq * TPM * 4;
+      P.buf[CFB_BUF_TP_CHEAD] = P.tchead;
+      P.buf_bytes[CFB_BUF_TP_CHEAD] = ((size_t)Bq * TPM + 63) / 64 * 64 * (size_t)(D + rank) * 2;
+    }
   }
   P.nranks = (beam && r.ranks > 1) ? r.ranks : 1;
   P.xloc = r.xloc; P.xall = r.xall;

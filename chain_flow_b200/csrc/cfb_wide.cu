@@ -995,6 +995,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
       C > kAttnMaxKeys || DL > kAttnMaxKeys)
     return CFB_ERR_UNSUPPORTED;
   if (r->ranks > 1) return CFB_ERR_UNSUPPORTED;           // the row-sharded head is engine-only
+  if (r->twopass_m != 0) return CFB_ERR_UNSUPPORTED;      // so is the two-pass head
   if (flow && (r->init_mode < CFB_INIT_GIVEN || r->init_mode > CFB_INIT_DELTA || (r->init_mode == CFB_INIT_GIVEN && !r->z0)))
     return CFB_ERR_INVALID_ARG;
   if (!r->pred || (flow && !r->ctx) || (head && (!r->known0 || !r->tokens))) return CFB_ERR_INVALID_ARG;

@@ -44,7 +44,7 @@ class Plan:
 
     def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
                  tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False,
-                 init_mode: int = 0):
+                 init_mode: int = 0, twopass_m: int = 0):
         self.w, self.mode, self.batch = w, mode, batch
         cfg, dev = w.cfg, w.dev
         D = cfg.hidden
@@ -67,6 +67,8 @@ class Plan:
         r.init_mode = init_mode
         r.tree_keep, r.tree_topb, r.grid = tree_keep, tree_topb, grid
         r.flags = _lib.RUN_PROFILE if profile else 0
+        r.twopass_m = twopass_m if mode != _lib.MODE_FLOW else 0
+        self.twopass_m = r.twopass_m
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
         r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
         self.ranks = w.head_ranks
@@ -124,6 +126,11 @@ class Plan:
         """[phases, grid, 20] int64 ns of the last profiled run (see CFB_BUF_PROF in cfb.h).
         Needs a plan built with profile=True."""
         return self.buffer(_lib.BUF_PROF, torch.int64, (self.phases, self.grid, 20))
+
+    def candidates(self) -> torch.Tensor:
+        """[B, twopass_m] int32 copy of the two-pass head's candidate shortlist rows of the last
+        run (CFB_BUF_TP_CAND), ascending per request."""
+        return self.buffer(_lib.BUF_TP_CAND, torch.int32, (self.batch, self.twopass_m))
 
     def phase_table(self) -> torch.Tensor:
         """[phases, 15] int32 copy of the plan's phase table (CFB_BUF_PHASES in cfb.h): [:, 0] kind,

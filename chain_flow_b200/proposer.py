@@ -10,7 +10,8 @@ src/chain_flow/vllm_plugin/flow_proposer.py:328-2569) where the drafting path is
   ``chained_flow_tree_config.json``) and the shortlist file format and guard
   (``CF_SHORTLIST`` -> ``<ckpt>/shortlist.pt``), with the declared-identity check (:1006-1016, :739-765);
 * the ``CF_*`` knobs of the path: ``CF_WIDTH``, ``CF_FLOW_STEPS``, ``CF_TREE_KEEP``, ``CF_TREE_TOPB``,
-  ``CF_TREE_DEPTH``, ``CF_TWOPASS_M`` (only 0 is implemented: the one-pass head), ``CF_PATH_TRIM``
+  ``CF_TREE_DEPTH``, ``CF_TWOPASS_M`` (0: the one-pass head; M > 0: the two-pass candidate head
+  with one candidate set for every depth, ``CF_TWOPASS_SHARED=1``, ``CF_TWOPASS_SEED=0``), ``CF_PATH_TRIM``
   (always on: it is exact).
 
 Every draft is ONE persistent kernel launch (flow + beam); there is no CPU fallback. The engine
@@ -58,9 +59,16 @@ class FlowDrafterProposer:
         self.tree_topb = _env_int("CF_TREE_TOPB", 8)
         self.tree_depth = _env_int("CF_TREE_DEPTH", 4)
         self.tree = os.environ.get("VLLM_SPEC_TREE", "0") == "1"
-        if _env_int("CF_TWOPASS_M", 0) != 0:
-            raise _lib.CfbError("CF_TWOPASS_M > 0 (two-pass candidate head) is not implemented by this "
-                                "engine; set CF_TWOPASS_M=0 for the one-pass fused head")
+        # the two-pass candidate head (reference flow_proposer.py:1142-1184): only its shared,
+        # unseeded form (the reference's defaults CF_TWOPASS_SHARED=1, CF_TWOPASS_SEED=0)
+        self.twopass_m = _env_int("CF_TWOPASS_M", 0)
+        if self.twopass_m < 0:
+            raise ValueError(f"CF_TWOPASS_M={self.twopass_m} must be >= 0")
+        if self.twopass_m and os.environ.get("CF_TWOPASS_SHARED", "1") in ("0", "false", "no"):
+            raise _lib.CfbError("CF_TWOPASS_SHARED=0 (a candidate set per depth) is not implemented; "
+                                "the shared candidate set (CF_TWOPASS_SHARED=1) is")
+        if self.twopass_m and os.environ.get("CF_TWOPASS_SEED", "0") == "1":
+            raise _lib.CfbError("CF_TWOPASS_SEED=1 is not implemented (the reference measured it worse)")
         self.K = 5
         self.max_reqs = 256                 # context-ring slots (the scheduler's max_num_seqs)
         self._ring = None
@@ -189,12 +197,13 @@ class FlowDrafterProposer:
         if p is None:
             init = _lib.INIT_MODES[self.init_mode]
             depth = self.tree_depth if mode == _lib.MODE_TREE else self.K
+            tp = self.twopass_m if mode != _lib.MODE_FLOW else 0
             if self.vae is not None:
                 p = VaeDraft(self.vae, self.flow_weights, self.weights, mode, B, width=self.width, depth=depth,
-                             tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+                             tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init, twopass_m=tp)
             else:
                 p = Plan(self.weights, mode, B, width=self.width, depth=depth,
-                         tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init)
+                         tree_keep=self.tree_keep, tree_topb=self.tree_topb, init_mode=init, twopass_m=tp)
             self._plans[key] = p
         return p
 
@@ -239,9 +248,11 @@ class FlowDrafterProposer:
     # ------------------------------------------------------------------ drafting interface
     def _run(self, mode: int, ctx: torch.Tensor, known0: torch.Tensor | None, out: str) -> torch.Tensor:
         """Up to MAX_PLAN_BATCH requests: one persistent-engine launch. More: one wide plan over
-        the whole batch (a row-sharded head instead runs engine plans of MAX_PLAN_BATCH requests)."""
+        the whole batch (a row-sharded head, or the two-pass head, instead runs engine plans of
+        MAX_PLAN_BATCH requests)."""
         B = ctx.shape[0]
-        if B <= MAX_PLAN_BATCH or self._wide_src is not None:
+        wide_ok = self._wide_src is not None and not (self.twopass_m and mode != _lib.MODE_FLOW)
+        if B <= MAX_PLAN_BATCH or wide_ok:
             p = self._plan(mode, B) if B <= MAX_PLAN_BATCH else self._wide_plan(mode, B)
             self._load_inputs(p, ctx, known0)
             p.run(group=self.group)

@@ -73,20 +73,25 @@ class Workload:
         body = nl * 12 * I * I
         return H * I + body + I * Z, Z * I + body + I * H
 
-    def weight_bytes_per_draft(self, head_fraction: float = 1.0) -> int:
+    def weight_bytes_per_draft(self, head_fraction: float = 1.0, twopass_m: int = 0, batch: int = 1) -> int:
         """Packed fp16 weight bytes one draft streams (the algorithmic bytes of the engine):
         cross K/V once; per Euler step every block of every chunk expert plus its out_proj;
         per beam depth the live PathHead offsets, the PathHead MLP and the [lm_head | markov w2]
         shortlist head (reference flow_proposer.py:1115-1117 counts the head the same way); for a
         production drafter the VAE encoder and decoder once each.
-        head_fraction: the share of the shortlist head one GPU holds when it is row-sharded."""
+        head_fraction: the share of the shortlist head one GPU holds when it is row-sharded.
+        twopass_m > 0: the two-pass head instead streams the whole head once (pass A), reads and
+        writes each request's twopass_m candidate rows once, and reads them at every depth."""
         Df, Dh, L, T, FM, E = self.flow_width, self.hidden, self.layers, self.steps, self.ffn, self.n_experts
         crosskv = E * L * 2 * Df * Df
         per_step = E * L * (3 + 1 + 1 + 1 + FM + FM) * Df * Df + E * Df * Df
         head = 0
+        row = Dh + self.markov_rank
         for d in range(1, self.draft_tokens + 1):
-            head += min(d, self.path_order) * Dh * Dh + 2 * (2 * Dh * Dh) + \
-                head_fraction * self.shortlist_rows * (Dh + self.markov_rank)
+            head += min(d, self.path_order) * Dh * Dh + 2 * (2 * Dh * Dh)
+            head += (batch * twopass_m * row) if twopass_m else head_fraction * self.shortlist_rows * row
+        if twopass_m:
+            head += self.shortlist_rows * row + 2 * batch * twopass_m * row
         enc, dec = self.vae_macs_per_row()
         return int(2 * (crosskv + T * per_step + head + enc + dec))
 

@@ -202,7 +202,8 @@ class VaeDraft:
     persistent engine; the VAE sides follow the layout of ``vw`` (engine plans or wide lists)."""
 
     def __init__(self, vw: VaeWeights, flow_w, head_w, mode: int, batch: int, *, wide: bool = False,
-                 width: int = 4, depth: int = 5, tree_keep: int = 4, tree_topb: int = 8, init_mode: int = 0):
+                 width: int = 4, depth: int = 5, tree_keep: int = 4, tree_topb: int = 8, init_mode: int = 0,
+                 twopass_m: int = 0):
         self.mode, self.batch = mode, batch
         vc = vw.cfg
         kind = WidePlan if wide else Plan
@@ -218,8 +219,9 @@ class VaeDraft:
         if mode != _lib.MODE_FLOW:
             if head_w is None or head_w.cfg.hidden != vc.hidden:
                 raise _lib.CfbError("a beam draft needs head weights at the VAE's hidden width")
+            extra = {"twopass_m": twopass_m} if twopass_m else {}
             self.head = kind(head_w, _BEAM_MODE[mode], batch, width=width, depth=depth, tree_keep=tree_keep,
-                             tree_topb=tree_topb)
+                             tree_topb=tree_topb, **extra)
         self.ctx = torch.zeros(batch, C_, vc.hidden, dtype=torch.float16, device=dev)
         self.z0 = self.flow.z0
         if self.head is not None:

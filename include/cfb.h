@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define CFB_ABI_VERSION 2
+#define CFB_ABI_VERSION 3
 
 typedef enum cfb_status {
   CFB_OK = 0,
@@ -143,6 +143,13 @@ typedef struct cfb_run {
   int rank;
   float* xloc;
   const float* xall;
+  /* The two-pass candidate head (reference CF_TWOPASS_M with CF_TWOPASS_SHARED=1 and
+   * CF_TWOPASS_SEED=0, flow_proposer.py:1142-1184); 0 = the one-pass head. Pass A scores the
+   * marginal hiddens of depths 1..K against the whole shortlist head in one GEMM and keeps, per
+   * request, the twopass_m shortlist rows with the best log-prob over those depths; every depth
+   * then rescores its beam rows against those rows only (log-softmax over the candidates).
+   * Engine plans on one GPU (ranks <= 1); 0 < twopass_m < shortlist_rows. */
+  int twopass_m;
 } cfb_run;
 
 #define CFB_XROWS 64
@@ -218,12 +225,19 @@ cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phas
  *                     with CFB_RUN_PROFILE */
 enum { CFB_BUF_PROF = 8 };
 /* CFB_BUF_PHASES      int32 [phases, 15] the phase table: [0] kind (0 prep, 1 GEMM, 2 attention,
- *                     3 beam, 4 rank merge, 5 next depth's path-row gather), [1..5] first job, jobs, units, tiles, whole-tile flag,
+ *                     3 beam, 4 rank merge, 5 next depth's path-row gather, 6-8 the two-pass
+ *                     head's pass-A input, candidate selection and candidate-row gather), [1..5] first job, jobs, units, tiles, whole-tile flag,
  *                     [6] post-op (0 none, 1 chain beam, 2 tree beam, 3 head lists published:
  *                     the shortlist head GEMM of a beam depth), [7..14] step, rows, frontier,
  *                     kept beams, top list length, node base, previous node base, last-depth
  *                     flag. Read-only for the caller. */
 enum { CFB_BUF_PHASES = 9 };
+/* CFB_BUF_TP_CAND     int32 [B, twopass_m]: the two-pass head's candidate shortlist rows per
+ *                     request, ascending (plans built with twopass_m > 0). */
+enum { CFB_BUF_TP_CAND = 10 };
+/* CFB_BUF_TP_CHEAD    the candidates' head rows [lm_head[sl] | markov.w2[sl]] of CFB_BUF_TP_CAND,
+ *                     request-major, packed like cfb_pack_linear ([B * twopass_m, D + rank]). */
+enum { CFB_BUF_TP_CHEAD = 11 };
 enum { CFB_BUF_PATH_H16 = 0, CFB_BUF_PATH_MID = 1, CFB_BUF_HEAD_IN = 2, CFB_BUF_LASTP = 3,
        CFB_BUF_CUM = 4, CFB_BUF_QKV0 = 5, CFB_BUF_X32_0 = 6, CFB_BUF_KVC0 = 7 };
 cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);

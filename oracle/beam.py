@@ -48,7 +48,7 @@ def twopass_logprobs(W, emb, hw, w2_sl, cd, h, lastp, order, nlive, B: int):
 
 
 def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int, K: int,
-                twopass_m: int = 0):
+                twopass_m: int = 0, cand=None, return_beams: bool = False):
     """Chain beam over the integrated hiddens ``pred`` [B, draft_length, D].
 
     Depth 0 is seeded with the committed token (one live beam, cum = [0, -inf, ...]); depths
@@ -64,7 +64,8 @@ def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int
     cum[:, 0] = 0.0
     steps = min(K + 1, pred.shape[1])
     toks, bps = [], []
-    cd = twopass_candidates(hw, pred, 1, steps, twopass_m) if twopass_m and steps > 1 else None
+    cd = cand if cand is not None else (
+        twopass_candidates(hw, pred, 1, steps, twopass_m) if twopass_m and steps > 1 else None)
     for step in range(1, steps):
         h = pred[:, step].float().unsqueeze(1).expand(B, Wd, -1).reshape(B * Wd, -1)
         if cd is not None:
@@ -89,11 +90,23 @@ def beam_chains(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, width: int
     for step in range(len(toks) - 1, -1, -1):
         seq[step] = toks[step].gather(1, idx.unsqueeze(1)).squeeze(1)
         idx = bps[step].gather(1, idx.unsqueeze(1)).squeeze(1)
-    return torch.stack(seq, dim=1)
+    best = torch.stack(seq, dim=1)
+    if not return_beams:
+        return best
+    # every final beam's path and cumulative log-prob (for checks of near-tied final beams)
+    beams = []
+    for w0 in range(Wd):
+        idx = torch.full((B,), w0, dtype=torch.long, device=dev)
+        sq = [None] * len(toks)
+        for step in range(len(toks) - 1, -1, -1):
+            sq[step] = toks[step].gather(1, idx.unsqueeze(1)).squeeze(1)
+            idx = bps[step].gather(1, idx.unsqueeze(1)).squeeze(1)
+        beams.append(torch.stack(sq, dim=1))
+    return best, torch.stack(beams, dim=1), cum
 
 
 def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, topb: int,
-              depth: int, twopass_m: int = 0):
+              depth: int, twopass_m: int = 0, cand=None):
     """Tree draft: every surviving extension becomes a BFS-ordered node. Returns [B, 2N]
     = N global token ids followed by N parent node indices (-1 for depth-1 nodes)."""
     B, dev = pred.shape[0], pred.device
@@ -106,7 +119,8 @@ def beam_tree(W, cfg: FlowConfig, emb, hw, w2_sl, sl, pred, known0, keep: int, t
     toks, pars = [], []
     base = 0
     nstep = min(depth, pred.shape[1] - 1)
-    cd = twopass_candidates(hw, pred, 1, nstep + 1, twopass_m) if twopass_m and nstep > 0 else None
+    cd = cand if cand is not None else (
+        twopass_candidates(hw, pred, 1, nstep + 1, twopass_m) if twopass_m and nstep > 0 else None)
     for step in range(1, nstep + 1):
         h = pred[:, step].float().unsqueeze(1).expand(B, fr, -1).reshape(B * fr, -1)
         if cd is not None:

@@ -15,8 +15,9 @@ import torch
 import oracle
 
 
-def check_tree(tokens, W, cfg, emb, hw, w2, sl, pred, known0, keep, topb, depth, eps=5e-3):
-    """tokens [B, 2N] from the engine; raises AssertionError with the first violation."""
+def check_tree(tokens, W, cfg, emb, hw, w2, sl, pred, known0, keep, topb, depth, eps=5e-3, tp_cand=None):
+    """tokens [B, 2N] from the engine; raises AssertionError with the first violation. tp_cand [B, M]:
+    the two-pass head's candidate rows (log-probs normalised over them), else the one-pass head."""
     B = pred.shape[0]
     order = cfg.path_order
     N = tokens.shape[1] // 2
@@ -28,7 +29,12 @@ def check_tree(tokens, W, cfg, emb, hw, w2, sl, pred, known0, keep, topb, depth,
         for step in range(1, min(depth, pred.shape[1] - 1) + 1):
             k = min(keep, fr * topb)
             h = pred[b, step].float().unsqueeze(0).expand(fr, -1)
-            _, lp = oracle.head_logprobs(W, emb, hw, w2, h, lastp, order, step)
+            if tp_cand is None:
+                _, lp = oracle.head_logprobs(W, emb, hw, w2, h, lastp, order, step)
+            else:   # scores of the candidates, scattered back to shortlist rows (-inf elsewhere)
+                lpc = oracle.twopass_logprobs(W, emb, hw, w2, tp_cand[b:b + 1], h, lastp, order, step, 1)[0]
+                lp = torch.full((fr, sl.numel()), float("-inf"))
+                lp[:, tp_cand[b]] = lpc
             cv, ci = lp.topk(topb, dim=-1)                                  # [fr, topb]
             cand = (cum.view(fr, 1) + cv).reshape(-1)
             kth = cand.topk(k).values[-1]

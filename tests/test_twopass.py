@@ -29,3 +29,69 @@ def test_twopass_oracle_matches_reference(name, M):
     assert torch.equal(ch, t[f"{name}.m{M}.chains"])
     tr = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5, twopass_m=M)
     assert torch.equal(tr, t[f"{name}.m{M}.tree"])
+
+
+def _scores(hw, pred, lo, hi):
+    """pass A's per-row best log-prob over the depths (the selection key), fp16 hiddens"""
+    B, n = pred.shape[0], hi - lo
+    lg = (pred[:, lo:hi].reshape(B * n, -1).half().float() @ hw.T).view(B, n, -1)
+    return torch.log_softmax(lg, dim=-1).amax(dim=1)
+
+
+def _check_set(cand, want, sc, M):
+    """Equal candidate sets, or differences only between rows whose keys tie at the threshold
+    within the fp32 rounding of the GPU's GEMM."""
+    for b in range(cand.shape[0]):
+        got, ref = set(cand[b].tolist()), set(want[b].tolist())
+        if got == ref:
+            continue
+        thr = sc[b].topk(M).values[-1]
+        for r in got ^ ref:
+            assert abs(float(sc[b, r] - thr)) < 1e-4, (b, r, float(sc[b, r]), float(thr))
+
+
+def _check_chain(tokens, W, cfg, g, hw, w2, sl, pred, cand, tol=5e-3):
+    """Chain drafts equal to the oracle's on the same candidate set, or, where they differ, the
+    engine's path is one of the oracle's final beams whose cumulative log-prob ties the best
+    within tol (the engine's fp16 head inputs against the oracle's fp32)."""
+    best, beams, cum = oracle.beam_chains(W, cfg, g["emb"], hw, w2, sl, pred, g["known0"], 4, 5, cand=cand,
+                                          return_beams=True)
+    for b in range(tokens.shape[0]):
+        if torch.equal(tokens[b], best[b]):
+            continue
+        hit = [w for w in range(beams.shape[1]) if torch.equal(beams[b, w], tokens[b])]
+        assert hit, (b, tokens[b], best[b])
+        assert float(cum[b].max() - cum[b, hit[0]]) < tol, (b, cum[b].tolist(), hit)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,M", CASES)
+def test_gpu_twopass_engine(name, M):
+    """The engine's two-pass head: candidate sets equal to the reference's, chain and tree drafts
+    equal to the reference's (on the reference's own hiddens and end to end from the flow)."""
+    from chain_flow_b200 import _lib
+    from gpu_util import golden_weights, run_plan
+    g, t = load_golden(name), _gtp()
+    W, sl, B = g["W"], g["sl"], g["B"]
+    hw, w2 = g["lm_w"][sl], W["markov.w2.weight"][sl]
+    cfg = golden_flow_config(g)
+    w = golden_weights(g)
+    sc = _scores(hw, g["pred"], 1, 6)
+    p = run_plan(w, _lib.MODE_BEAM_CHAIN, B, known0=g["known0"], pred=g["pred"], width=4, depth=5, twopass_m=M)
+    cand = p.candidates().long().cpu()
+    assert bool((cand[:, 1:] > cand[:, :-1]).all())               # ascending shortlist rows
+    _check_set(cand, t[f"{name}.m{M}.cand"], sc, M)
+    _check_chain(p.tokens.cpu(), W, cfg, g, hw, w2, sl, g["pred"], cand)
+    p = run_plan(w, _lib.MODE_BEAM_TREE, B, known0=g["known0"], pred=g["pred"], depth=5, tree_keep=4,
+                 tree_topb=4, twopass_m=M)
+    cand = p.candidates().long().cpu()
+    want = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5, cand=cand)
+    if not torch.equal(p.tokens.cpu(), want):
+        # only where candidates tie within the engine's fp16 head inputs
+        from beam_check import check_tree
+        check_tree(p.tokens.cpu(), W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5, tp_cand=cand)
+    # end to end: flow, then the two-pass beam
+    p = run_plan(w, _lib.MODE_CHAIN, B, ctx=g["ctx"], z0=g["z0"], known0=g["known0"], width=4, depth=5, twopass_m=M)
+    pred = p.pred.cpu()
+    _check_chain(p.tokens.cpu(), W, cfg, g, hw, w2, sl, pred, p.candidates().long().cpu())
+    assert p.device_error() == 0
