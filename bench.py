@@ -394,7 +394,7 @@ def run_ours(args, wl):
         del pp
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the host baseline: N=1 only
         n = args.cpu_drafts or (3 if wl.hidden >= 2560 else 20)
         if wl.hidden <= 2560:
             rate, spd, threads, sample = cpu_reference_draft_rate(wl, n)
