@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify", "ring"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
@@ -602,8 +602,87 @@ def run_gdn_verify(args):
         print(json.dumps(line), flush=True)
 
 
+def run_ring(args):
+    """The context ring (reference _ring_write / _ring_gather, flow_proposer.py:916-961) at the 4B
+    hidden size: 256 request slots of C=8 rows, each step appends K+1 = 6 accepted rows per request
+    (a chain step) and gathers every request's window, at B = 1, 8, 64 and 256 requests. A step is
+    one cfb_ring_write and one cfb_ring_gather launch. Algorithmic bytes per request: the appended
+    rows read and written, the window read and written (fp16)."""
+    from chain_flow_b200.ring import ContextRing
+    import oracle
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    slots, C, H, K1 = 256, 8, 2560, 6
+    peak, peak_kind = measured_peaks()
+    per_req = 2 * K1 * H * 2 + 2 * C * H * 2
+    for B in (1, 8, 64, 256):
+        g = torch.Generator(device=dev).manual_seed(B)
+        ring = ContextRing(slots, C, H, device=dev)
+        rows = torch.randperm(slots, generator=g, device=dev)[:B]
+        sh = torch.randn(B * K1, H, generator=g, device=dev).half()
+        starts = torch.arange(B, device=dev) * K1
+        cnt = torch.full((B,), K1, dtype=torch.long, device=dev)
+        wmask = torch.ones(B, dtype=torch.bool, device=dev)
+        out = torch.empty(B, C, H, dtype=torch.float16, device=dev)
+        for _ in range(max(3, args.warmup)):
+            ring.write(sh, rows, starts, cnt, wmask, None, K1)
+            ring.gather(rows, out=out)
+        torch.cuda.synchronize(dev)
+        # the two launches take a few microseconds; issued one by one from Python the host is the
+        # bottleneck, so the timed steps replay a CUDA graph of `per_graph` steps (no allocation
+        # or host sync happens inside either call)
+        per_graph = 20
+        side = torch.cuda.Stream(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(per_graph):
+                    ring.write(sh, rows, starts, cnt, wmask, None, K1, stream=side)
+                    ring.gather(rows, out=out, stream=side)
+        torch.cuda.synchronize(dev)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        reps_g = max(1, args.steps // per_graph)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps_g):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / (reps_g * per_graph)
+        achieved = B * per_req / (ms / 1e3) / 1e9
+        # CPU baseline: the reference's ring semantics (oracle) on the host cores
+        torch.set_num_threads(os.cpu_count() or 1)
+        rc, rp, nv = ring.ring.cpu(), ring.rpos.cpu(), ring.nval.cpu()
+        args_c = (sh.cpu(), rows.cpu(), starts.cpu(), cnt.cpu(), wmask.cpu(), None, K1)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            oracle.ring_write(rc, rp, nv, *args_c)
+            oracle.ring_gather(rc, rp, nv, rows.cpu())
+        cpu_s = (time.perf_counter() - t0) / reps
+        line = {"metric": "context ring: requests/s (append 6 rows + gather the 8-row window, H=2560)",
+                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": reps_g * per_graph,
+                "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded hidden states and slots)",
+                "config": {"workload": "a1-context-ring", "batch": B, "slots": slots, "rows": C, "hidden": H,
+                           "appended": K1, "timing": f"CUDA graph of {per_graph} steps, replayed {reps_g} times"},
+                "gpu_launches": 2 * per_graph * reps_g,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
+                             "kernel": "ring_write_kernel + ring_gather_kernel",
+                             "algorithmic_bytes_per_launch": B * per_req},
+                "cpu_baseline": {"value": B / cpu_s, "unit": "req/s", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": f"{reps} steps of {B} requests, oracle on CPU"}}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload == "ring":
+        run_ring(args)
+        return
     if args.workload == "gdn":
         run_gdn(args)
         return

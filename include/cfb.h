@@ -308,7 +308,7 @@ cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, con
  * go to the trash row; rpos advances by cnt[b] mod C and nval saturates at C.
  * cfb_ring_gather writes out fp16 [B, C, H]: each slot's rows oldest first, front-padded by
  * repeating the oldest row when fewer than C exist. Both only move fp16 rows; the slots of one
- * call must be distinct. */
+ * call must be distinct. Supported: kmax <= 64 and C <= 64 (CFB_ERR_UNSUPPORTED beyond). */
 cfb_status cfb_ring_write(void* ring, int64_t* rpos, int64_t* nval, int slots, int C, int H,
                           const void* sh, int64_t nsh, const int64_t* rows, const int64_t* starts,
                           const int64_t* cnt, const uint8_t* wmask, const int64_t* path,
