@@ -736,6 +736,7 @@ CFB_DEV void epi_prefetch(const Plan& P, const Job& J, int tile, const Grp& E) {
 
 // Epilogue side of one tile: take the MMA warps' partials from slot buffer `b`, reduce them in a
 // fixed order, release the slot, then finish the tile directly or through the stream-K fixup.
+constexpr int kFixBatch = 3;   // contributors whose partials one fixup step loads at once
 template <class WaitClock>
 CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
                       long long ug_first, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
@@ -825,13 +826,22 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
         off[k] = e < total ? f * kRowsMax + r : -1;
         acc[k] = e < total ? S.red[f * S.rp + r] : 0.f;
       }
-      for (int i = 0; i < ncontrib; ++i) {
-        const float* part = P.gpart + (size_t)clist[1 + i] * (kTileRows * kRowsMax);
-        float v[8];
+      // the partials are added in k order, but the loads of kFixBatch contributors are all
+      // issued before the first add, so their L2 round trips overlap instead of queueing
+      for (int i0 = 0; i0 < ncontrib; i0 += kFixBatch) {
+        float v[kFixBatch][8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = off[k] >= 0 ? __ldcg(part + off[k]) : 0.f;
+        for (int j = 0; j < kFixBatch; ++j) {
+          const bool on = i0 + j < ncontrib;
+          const float* part = P.gpart + (size_t)clist[1 + (on ? i0 + j : i0)] * (kTileRows * kRowsMax);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] += v[k];
+          for (int k = 0; k < 8; ++k) v[j][k] = (on && off[k] >= 0) ? __ldcg(part + off[k]) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < kFixBatch; ++j) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[k] += v[j][k];
+        }
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
