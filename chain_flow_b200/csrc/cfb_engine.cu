@@ -420,6 +420,14 @@ CFB_DEV RowMap row_map(int rows, int et) {
   return {et / sl, et % sl, sl, kTileRows / sl};
 }
 
+// the head epilogue's map: a row gets kEpi / rows lanes (at least 2 features each), so small
+// row counts keep every epilogue thread busy
+CFB_DEV RowMap head_map(int rows, int et) {
+  const int rp = rows <= 4 ? 4 : rows <= 8 ? 8 : rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+  const int sl = kEpi / rp;
+  return {et / sl, et % sl, sl, kTileRows / sl};
+}
+
 // ------------------------------------------------------------------------------------------
 // Attention of request b, head h (reference nn.MultiheadAttention inside HiddenKVFlowBlock,
 // chunked_flow.py:185-197): softmax(q k^T * hd^-1/2 [+ causal mask]) v over the request's rows.
@@ -691,7 +699,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
       break;
     }
     case EK_HEAD: {
-      const RowMap M = row_map(rows, E.t);
+      const RowMap M = head_map(rows, E.t);
       if (M.r < rows) {
         const int rq = J.cmask ? M.r / J.wrows : 0;
         for (int f = M.q * M.nf; f < (M.q + 1) * M.nf; ++f) {
@@ -1344,7 +1352,7 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
 // row's slice lanes (their sorted lists) by TB rounds of a lane argmax
 __device__ __noinline__ void head_post(const Plan& P, const Phase& ph, const Job* jt, HeadState& H, const Grp& E) {
   const int rows = ph.rows, TB = ph.topb;
-  const RowMap M = row_map(rows, E.t);
+  const RowMap M = head_map(rows, E.t);
   float m = H.m, ssum = H.s;
   lse_lanes(m, ssum, M.sl);
   float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + M.r) * kHeadPartFloats;
