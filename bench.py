@@ -146,10 +146,11 @@ def oracle_draft(oracle, wl, cfg, W, emb, hw, w2, sl, ctx, z0, known0):
     return oracle.beam_chains(W, cfg, emb, hw, w2, sl, pred, known0, wl.width, wl.draft_tokens)
 
 
-def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float = 30.0):
+def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float = 30.0, warmup: int = 1):
     """The reference algorithm on the host cores (oracle/ restatement, fp32, all threads):
-    returns (tok/s, seconds per draft, threads, sample description). Stops after `n_drafts`
-    timed drafts or once `budget_s` seconds of drafting have been timed (at least 2 drafts)."""
+    returns (tok/s, seconds per draft, threads, sample description, timed drafts). Runs `warmup`
+    untimed drafts (at least 1), then stops after `n_drafts` timed drafts or once `budget_s`
+    seconds of drafting have been timed (at least 2 drafts)."""
     import oracle
     from chain_flow_b200.synthetic import make_state, make_inputs
     torch.set_num_threads(os.cpu_count() or 1)
@@ -165,18 +166,20 @@ def cpu_reference_draft_rate(wl, n_drafts: int, seed: int = 0, budget_s: float =
     cfg = oracle_flow_config(oracle, wl)
     g = torch.Generator().manual_seed(seed)
     times = []
+    nw = max(1, warmup)
     with torch.inference_mode():
-        for i in range(n_drafts + 1):
+        for i in range(n_drafts + nw):
             z0 = torch.randn(1, wl.draft_length, wl.flow_width, generator=g)
             t0 = time.perf_counter()
             oracle_draft(oracle, wl, cfg, W, emb, hw, w2, sl, ctx, z0, known0)
-            if i > 0:                      # the first draft warms caches and threads
+            if i >= nw:                    # the warm-up drafts warm caches and threads
                 times.append(time.perf_counter() - t0)
                 if len(times) >= 2 and sum(times) > budget_s:
                     break
     spd = sum(times) / len(times)
     return wl.draft_tokens / spd, spd, torch.get_num_threads(), \
-        f"{len(times)} drafts of the {wl.name} chain at b=1, fp32 torch on CPU (after 1 warm-up draft)"
+        f"{len(times)} drafts of the {wl.name} chain at b=1, fp32 torch on CPU (after {nw} warm-up draft{'s' if nw > 1 else ''})", \
+        len(times)
 
 
 def eager_gpu_reference_rate(wl, n_drafts: int, warmup: int, seed: int = 0):
@@ -232,10 +235,10 @@ def run_reference(args, wl):
         }
         print(json.dumps(line), flush=True)
         return
-    rate, spd, threads, sample = cpu_reference_draft_rate(wl, n)
+    rate, spd, threads, sample, timed = cpu_reference_draft_rate(wl, n, warmup=args.warmup)
     line = {
         "metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-        "steps": n, "warmup": 1, "ms_per_step": spd * 1e3, "higher_is_better": True, "scaling": "weak",
+        "steps": timed, "warmup": max(1, args.warmup), "ms_per_step": spd * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights and inputs)",
         "config": {"workload": wl.name, "batch_per_gpu": 1, "draft_tokens": wl.draft_tokens,
                    "hidden": wl.hidden, "blocks": wl.layers, "euler_steps": wl.steps,
@@ -397,7 +400,7 @@ def run_ours(args, wl):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:   # the host baseline: N=1 only
         n = args.cpu_drafts or (3 if wl.hidden >= 2560 else 20)
         if wl.hidden <= 2560:
-            rate, spd, threads, sample = cpu_reference_draft_rate(wl, n)
+            rate, spd, threads, sample, _ = cpu_reference_draft_rate(wl, n)
             cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
     if rank == 0:
