@@ -9,7 +9,6 @@ in latent space, decode). Weights use the reference's state-dict names under ``v
 """
 from __future__ import annotations
 
-import torch
 import torch.nn.functional as F
 
 from .flow import FlowConfig, integrate, layer_norm, mha

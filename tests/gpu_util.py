@@ -4,7 +4,6 @@ from __future__ import annotations
 
 import torch
 
-from chain_flow_b200 import _lib
 from chain_flow_b200.engine import Plan
 from chain_flow_b200.weights import DraftConfig, DrafterWeights
 

@@ -1,8 +1,6 @@
 """The wide path's tcgen05 GEMM (cfb_wide_gemm) against a torch fp32 matmul of the same fp16
 operands: every epilogue, ragged M (TMA zero fill past the edge) and N (zero rows of the packed
 weights), split-K partials; and the weight packing (cfb_wide_pack) against its layout rule."""
-import ctypes as C
-
 import pytest
 import torch
 
