@@ -95,3 +95,20 @@ def test_gpu_twopass_engine(name, M):
     pred = p.pred.cpu()
     _check_chain(p.tokens.cpu(), W, cfg, g, hw, w2, sl, pred, p.candidates().long().cpu())
     assert p.device_error() == 0
+
+
+@pytest.mark.parametrize("name", ["g64", "g128"])
+def test_twopass_over_the_whole_shortlist_is_the_one_pass_head(name):
+    """With every shortlist row a candidate, pass B is the full head: the two-pass oracle's
+    chains and trees equal the one-pass oracle's."""
+    g = load_golden(name)
+    W, sl = g["W"], g["sl"]
+    hw, w2 = g["lm_w"][sl], W["markov.w2.weight"][sl]
+    R = hw.shape[0]
+    cfg = golden_flow_config(g)
+    one = oracle.beam_chains(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 5)
+    two = oracle.beam_chains(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 5, twopass_m=R)
+    assert torch.equal(one, two)
+    one_t = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5)
+    two_t = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5, twopass_m=R)
+    assert torch.equal(one_t, two_t)
