@@ -32,13 +32,17 @@ EXPORTED = [
     "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify", "cfb_vae_workspace", "cfb_vae_create",
     "cfb_vae_plan_workspace", "cfb_vae_plan_build",
 ]
-ABI_VERSION = 3
+ABI_VERSION = 4
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF, BUF_PHASES, \
     BUF_TP_CAND, BUF_TP_CHEAD = range(12)
 PK_PREP, PK_GEMM, PK_ATTN, PK_BEAM, PK_RMERGE, PK_GATHER, PK_TPXA, PK_TPSEL, PK_TPGATH = range(9)  # CFB_BUF_PHASES [0]
 PO_NONE, PO_BEAM_CHAIN, PO_BEAM_TREE, PO_PUBLISH = range(4)        # CFB_BUF_PHASES [6]
 RUN_PROFILE = 1
+# device error word codes (cfb_plan_error / cfb_wide_error)
+DEV_ERRORS = {1: "grid barrier wait expired", 2: "loaded-stage wait expired", 3: "free-stage wait expired",
+              4: "slot or descriptor wait expired", 5: "bad phase", 6: "split-tile wait expired",
+              7: "token or row id outside its table"}
 EPI_F32, EPI_F16, EPI_GELU16, EPI_PART = 0, 1, 2, 3      # cfb_wide_gemm epilogues
 
 
@@ -78,7 +82,7 @@ class Run(C.Structure):
                 ("ctx", C.c_void_p), ("z0", C.c_void_p), ("known0", C.c_void_p),
                 ("pred", C.c_void_p), ("tokens", C.c_void_p),
                 ("ranks", C.c_int), ("rank", C.c_int), ("xloc", C.c_void_p), ("xall", C.c_void_p),
-                ("twopass_m", C.c_int)]
+                ("twopass_m", C.c_int), ("wait_budget_ns", C.c_uint64)]
 
 
 class VaeLayer(C.Structure):

@@ -14,7 +14,8 @@ namespace cfb {
 
 // Device error word values (written into the workspace, read by cfb_plan_error).
 enum DevErr : int { DEV_OK = 0, DEV_TIMEOUT_GRID = 1, DEV_TIMEOUT_FULL = 2, DEV_TIMEOUT_EMPTY = 3,
-                    DEV_TIMEOUT_SLOT = 4, DEV_BAD_PHASE = 5, DEV_TIMEOUT_FIXUP = 6 };
+                    DEV_TIMEOUT_SLOT = 4, DEV_BAD_PHASE = 5, DEV_TIMEOUT_FIXUP = 6,
+                    DEV_BAD_INDEX = 7 };   // a token / row id outside its table: never dereferenced
 
 // Every device-side wait is bounded by this many nanoseconds of %globaltimer. On expiry the
 // waiter records an error and returns, so a broken schedule ends the launch instead of hanging
@@ -54,21 +55,52 @@ CFB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
+// non-suspending form: reports at once whether the phase has completed
+CFB_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.b32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
 CFB_DEV int ld_volatile_int(const int* p);
 
 // Polls between two looks at the clock and the error word in a bounded wait. Each look costs a
 // global-memory round trip, during which the waiter cannot notice that its wait is over.
 constexpr unsigned kPollsPerCheck = 64;
 
+// A wait budget below the default is a caller forcing waits to expire, to test the failure path:
+// such a wait looks at the clock at every poll (polls_per_check), and a budget of n ns expires
+// once n - 1 ns have passed (wait_expired), so a budget of 1 ns gives up at the first poll that
+// finds the wait unfinished, whatever the resolution of %globaltimer.
+CFB_DEV unsigned polls_per_check(unsigned long long budget) {
+  return budget < kWaitBudgetNs ? 1u : kPollsPerCheck;
+}
+CFB_DEV bool wait_expired(unsigned long long t0, unsigned long long budget) {
+  return globaltimer() - t0 + 1ull >= budget;
+}
+
 // Bounded wait; returns false on timeout, or soon after `err` (if given) is set, so that after
-// the first failure the rest of a launch runs through without waiting.
-CFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr) {
+// the first failure the rest of a launch runs through without waiting. A forced short budget
+// polls with the non-suspending test_wait (try_wait may suspend the thread until the phase
+// completes, which would hide the expiry).
+CFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr,
+                       unsigned long long budget = kWaitBudgetNs) {
+  if (budget < kWaitBudgetNs) {
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+      if (mbar_test_wait(bar, parity)) return true;
+      if (wait_expired(t0, budget)) return false;
+      if (err && ld_volatile_int(err) != 0) return false;
+    }
+  }
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (unsigned it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if (it % kPollsPerCheck == 0) {
-      if (globaltimer() - t0 > kWaitBudgetNs) return false;
+      if (wait_expired(t0, budget)) return false;
       if (err && ld_volatile_int(err) != 0) return false;
     }
   }

@@ -199,6 +199,7 @@ struct Plan {
   int maxnt;                                // engine_kernel<maxnt> runs this plan
   void* buf[16]; size_t buf_bytes[16];     // intermediate buffers exposed by cfb_plan_buffer
   unsigned long long* prof;                // [nphases][G][4] or NULL
+  unsigned long long wait_ns;              // the grid barrier's wait budget (cfb_run.wait_budget_ns)
   // a VAE side (mode kModeVae): input rows [B * vS, vDin] (fp32 when vin32, else fp16), unit-
   // tiled into vin16 by prep; the residual stream vx32 [B * vS, D] starts at pos[row % vS]
   const void* vin; int vin32, vS, vDin;
@@ -309,8 +310,9 @@ CFB_DEV bool grid_sync(const Plan& P, unsigned& epoch, const Grp& W, volatile in
     unsigned v = atom_add_acqrel(P.bar, 1u) + 1u;
     if (v < target) {
       const unsigned long long t0 = globaltimer();
+      const unsigned every = polls_per_check(P.wait_ns);
       for (unsigned it = 1; (v = ld_acquire(P.bar)) < target; ++it) {
-        if (it % kPollsPerCheck == 0 && globaltimer() - t0 > kWaitBudgetNs) {
+        if (it % every == 0 && wait_expired(t0, P.wait_ns)) {
           set_err(P, DEV_TIMEOUT_GRID);
           v = kBarErrBit;
           break;
@@ -2659,6 +2661,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
   P.gpart = B.dptr<float>(o_gpart); P.hpart = B.dptr<float>(o_hpart);
   P.ctx = static_cast<const __half*>(r.ctx); P.z0 = static_cast<const __half*>(r.z0);
   P.pred = r.pred; P.ctxstat = B.dptr<float2>(o_ctxs); P.init_mode = r.init_mode;
+  P.wait_ns = r.wait_budget_ns ? r.wait_budget_ns : cfb::kWaitBudgetNs;
   if (flow) P.ctx16 = B.dptr<__half>(o_ctx16);
   P.known0 = r.known0; P.tokens = r.tokens;
   if (vae) {

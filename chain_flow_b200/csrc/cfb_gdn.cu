@@ -102,11 +102,19 @@ tree_gdn_kernel(const __half* __restrict__ q, const __half* __restrict__ k, cons
     const size_t nh = ((size_t)b * N + n) * H + h;
     const int p = pr[n], par = n & 1;
     const float vj = live ? __half2float(v[nh * Dv + j]) : 0.f;
-    if (p != held && live) {
-      const float* src = (p < 0) ? init + ((size_t)b * H + h) * kDk * Dv
-                                 : states + (((size_t)b * N + p) * H + h) * kDk * Dv;
+    // a parent must be -1 (the prefix state) or an earlier node of the same tree; any other
+    // value is never dereferenced: the node (and every descendant) gets NaN state and output
+    const bool bad = p >= n || p < -1;
+    if ((p != held || bad) && live) {
+      if (bad) {
 #pragma unroll
-      for (int i = 0; i < kRowsPerThread; ++i) S[i] = src[(size_t)(k0 + i) * Dv + j];
+        for (int i = 0; i < kRowsPerThread; ++i) S[i] = __int_as_float(0x7fc00000);
+      } else {
+        const float* src = (p < 0) ? init + ((size_t)b * H + h) * kDk * Dv
+                                   : states + (((size_t)b * N + p) * H + h) * kDk * Dv;
+#pragma unroll
+        for (int i = 0; i < kRowsPerThread; ++i) S[i] = src[(size_t)(k0 + i) * Dv + j];
+      }
     }
     const float decay = gd[n], kn = nk[n], qn = nq[n];
     float kv = 0.f;

@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
         const int s = i % nst;
-        if (i >= nst && !mbar_wait(&empty[s], ((i / nst) - 1) & 1)) { *sflag = 1; break; }
+        if (i >= nst && !mbar_wait(&empty[s], ((i / nst) - 1) & 1, nullptr, L.wait_ns)) { *sflag = 1; break; }
         if (*sflag) break;
         mbar_arrive_expect_tx(&full[s], stage);
         uint8_t* st = sm + s * stage;
@@ -227,14 +227,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
         bulk_g2s(st + abytes, P.wt + ((long long)nt * P.kbt + kb) * (BN * BK), kWTileBytes, &full[s]);
         ++issued;
       }
-      if (*sflag)   // copies still in flight land before the CTA may exit (bounded)
-        for (int i = max(0, issued - nst); i < issued; ++i) mbar_wait(&full[i % nst], (i / nst) & 1);
+      // copies still in flight land before the CTA may exit (bounded): after a failed wait the
+      // MMA issuer may have stopped consuming them; the last nst copies are each stage's last use
+      for (int i = max(0, issued - nst); i < issued; ++i) mbar_wait(&full[i % nst], (i / nst) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       for (int i = 0; i < nk; ++i) {
         const int s = i % nst;
-        if (!mbar_wait(&full[s], (i / nst) & 1)) { *sflag = 1; break; }
+        if (!mbar_wait(&full[s], (i / nst) & 1, nullptr, L.wait_ns)) { *sflag = 1; break; }
         tc_fence_after();
         const uint32_t a = smem_u32(sm + s * stage), w = a + abytes;
 #pragma unroll
@@ -250,6 +251,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) wide_gemm_kernel(const __grid
     }
   } else {
     const int lg = warp & 3;                                  // TMEM lanes 32*lg .. 32*lg+31
+    // the issuer commits accf whether or not its loop completed, so this wait (default budget)
+    // also keeps TMEM allocated until every MMA it issued has finished
     const bool ok = mbar_wait(accf, 0);
     tc_fence_after();
     if (!ok) *sflag = 1;
@@ -704,8 +707,12 @@ struct GatherArgs {
   const int64_t* lastp; int order, nlive, rows, D, rank;
   const __half* emb; __half* apath; long long lda;
   const __half* w1; __half* hin; long long ldh;
+  int vocab; int* err;
 };
+// After a failed launch of the plan (err set) the path tokens may be stale or unset, so this
+// kernel then does nothing; a token outside [0, vocab) is never dereferenced (it sets err).
 __global__ void __launch_bounds__(128) wide_gather_kernel(GatherArgs a) {
+  if (ld_volatile_int(a.err) != 0) return;
   const int r = blockIdx.x;
   const int64_t* lp = a.lastp + (long long)r * a.order;
   const int d8 = a.D / 8;
@@ -713,10 +720,15 @@ __global__ void __launch_bounds__(128) wide_gather_kernel(GatherArgs a) {
     const int j = e / d8, c = (e - j * d8) * 8;
     const int64_t tok = lp[j];
     uint4 val = make_uint4(0, 0, 0, 0);
-    if (tok >= 0) val = *reinterpret_cast<const uint4*>(a.emb + tok * a.D + c);
+    if (tok >= a.vocab) wide_err(a.err, DEV_BAD_INDEX);
+    else if (tok >= 0) val = *reinterpret_cast<const uint4*>(a.emb + tok * a.D + c);
     *reinterpret_cast<uint4*>(a.apath + (long long)r * a.lda + (long long)j * a.D + c) = val;
   }
   const int64_t t0 = lp[0];
+  if (t0 < 0 || t0 >= a.vocab) {
+    if (threadIdx.x == 0) wide_err(a.err, DEV_BAD_INDEX);
+    return;
+  }
   for (int c = threadIdx.x * 8; c < a.rank; c += blockDim.x * 8)
     *reinterpret_cast<uint4*>(a.hin + (long long)r * a.ldh + a.D + c) =
         *reinterpret_cast<const uint4*>(a.w1 + t0 * a.rank + c);
@@ -731,8 +743,12 @@ struct BeamArgs {
   const int64_t* sl;
   int64_t* toks; int* bps;                     // chain: [K][B * Wmax]
   int64_t* tokens;                             // chain [B, K]; tree [B, 2N]
+  int R; int* err;                             // shortlist rows; the plan's error word
 };
+// Like the gather, the beam step does nothing after a failed launch of the plan (its lists are
+// then unset), and a list id outside the shortlist is never dereferenced (it sets err).
 __global__ void __launch_bounds__(128) wide_beam_kernel(BeamArgs a) {
+  if (ld_volatile_int(a.err) != 0) return;
   __shared__ float cv[kBeamMaxRows][kBeamMaxTop];
   __shared__ int ci[kBeamMaxRows][kBeamMaxTop];
   __shared__ int64_t oldlp[kBeamMaxRows][8];
@@ -805,7 +821,9 @@ __global__ void __launch_bounds__(128) wide_beam_kernel(BeamArgs a) {
     }
     taken |= 1ull << best;
     const int src = best / a.topb;
-    const int64_t tok = a.sl[ci[src][best % a.topb]];
+    const int sid = ci[src][best % a.topb];
+    if (sid < 0 || sid >= a.R) { wide_err(a.err, DEV_BAD_INDEX); return; }
+    const int64_t tok = a.sl[sid];
     const int row = b * a.Wmax + k;
     a.cum[row] = bv;
     int64_t* lp = a.lastp + (long long)row * a.order;
@@ -884,6 +902,7 @@ extern "C" cfb_status cfb_wide_gemm(const void* a, int64_t lda, const void* w, i
   GemmLaunch L{};
   L.nprob = 1;
   L.err = err;
+  L.wait_ns = cfb::kWaitBudgetNs;
   GemmProb& p = L.p[0];
   if ((st = cfb::wide::gemm_prob(p, a, lda, M, w, ldw, N, K, epi, epi == EPI_PART ? splits : 1)) != CFB_OK) return st;
   p.bias = bias;
@@ -1077,6 +1096,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
   cfb_status st;
   auto add_gemm = [&](GemmLaunch& L) {
     L.err = err;
+    L.wait_ns = r->wait_budget_ns ? r->wait_budget_ns : kWaitBudgetNs;
     shape(L);
     P->gemms.push_back(L);
     P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1});
@@ -1218,7 +1238,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
       const int keep = tree ? levels[dd] : Wmax;
       P->gathers.push_back(GatherArgs{lastp, order, nlive, BW, D, rank, static_cast<const __half*>(d->embed), apath,
                                       (long long)order * D, static_cast<const __half*>(d->markov_w1), hin,
-                                      (long long)Kh});
+                                      (long long)Kh, d->vocab, err});
       P->steps.push_back({S_GATHER, (int)P->gathers.size() - 1});
       {
         GemmLaunch G{};
@@ -1266,6 +1286,7 @@ cfb_status wide_layout(const cfb_drafter* d, const cfb_run* r, Bump& bm, cfb_wid
       a.lists = lists; a.ntiles = ntiles; a.topb = TB; a.Wmax = Wmax; a.fr = fr; a.keep = keep; a.order = order;
       a.depth = dd; a.K = K; a.tree = tree ? 1 : 0; a.N = Ntree; a.base = base; a.cum = cum; a.lastp = lastp; a.prev = prev;
       a.sl = d->shortlist; a.toks = toks; a.bps = bps; a.tokens = r->tokens;
+      a.R = d->shortlist_rows; a.err = err;
       P->beams.push_back(a);
       P->steps.push_back({S_BEAM, (int)P->beams.size() - 1});
       base += keep;
@@ -1362,6 +1383,7 @@ cfb_status vae_layout(const cfb_vae_side* v, int B, int rows, int decode, const 
   P->fix_cnt_bytes = kFixTiles * sizeof(int);
   auto add_gemm = [&](GemmLaunch& L, bool) {
     L.err = err;
+    L.wait_ns = kWaitBudgetNs;
     shape_gemm(L, P->nsm, fix_ws, kFixFloats, fix_cnt, kFixTiles);
     P->gemms.push_back(L);
     P->steps.push_back({S_GEMM, (int)P->gemms.size() - 1});

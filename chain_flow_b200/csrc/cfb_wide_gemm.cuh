@@ -16,8 +16,10 @@
 //                      returns each stage to the producer with tcgen05.commit;
 //   warps 2..5         epilogue: each thread owns one accumulator row (its TMEM lane), reads it
 //                      16 columns at a time with tcgen05.ld and applies the fused epilogue.
-// Every wait is bounded (kWaitBudgetNs); a wait that expires records an error and the CTA
-// winds down (the producer first waits, bounded, for its copies in flight; TMEM is always freed).
+// Every wait is bounded: the ring waits by the launch's budget (default kWaitBudgetNs), the waits
+// that let the CTA wind down by kWaitBudgetNs. A ring wait that expires records an error and the
+// CTA winds down: the accumulator wait still lets every issued MMA finish, the producer waits for
+// its copies in flight, and TMEM is always freed.
 #pragma once
 #include <cuda.h>
 #include "cfb_common.cuh"
@@ -80,6 +82,7 @@ struct GemmLaunch {
   GemmProb p[kMaxProbs];
   int nprob;
   int* err;                       // sticky device error word
+  unsigned long long wait_ns;     // budget of the ring waits (cfb_run.wait_budget_ns; default 1 s)
 };
 static_assert(sizeof(GemmLaunch) <= 4000, "kernel parameter space");
 

@@ -44,7 +44,7 @@ class Plan:
 
     def __init__(self, w: DrafterWeights, mode: int, batch: int, *, width: int = 4, depth: int = 5,
                  tree_keep: int = 4, tree_topb: int = 8, grid: int = 0, profile: bool = False,
-                 init_mode: int = 0, twopass_m: int = 0):
+                 init_mode: int = 0, twopass_m: int = 0, wait_ns: int = 0):
         self.w, self.mode, self.batch = w, mode, batch
         cfg, dev = w.cfg, w.dev
         D = cfg.hidden
@@ -68,6 +68,7 @@ class Plan:
         r.tree_keep, r.tree_topb, r.grid = tree_keep, tree_topb, grid
         r.flags = _lib.RUN_PROFILE if profile else 0
         r.twopass_m = twopass_m if mode != _lib.MODE_FLOW else 0
+        r.wait_budget_ns = wait_ns
         self.twopass_m = r.twopass_m
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
         r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
@@ -83,8 +84,9 @@ class Plan:
                    "cfb_plan_workspace")
         self.ws = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=dev)
         self.ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        self.ws_bytes = int(nbytes.value)
         _lib.check(self.lib.cfb_plan_build(C.byref(w.desc), C.byref(r), C.c_void_p(self.ws_ptr),
-                                           C.c_size_t(int(nbytes.value))), "cfb_plan_build")
+                                           C.c_size_t(self.ws_bytes)), "cfb_plan_build")
         g, t, s, p = C.c_int(), C.c_int(), C.c_int(), C.c_int()
         _lib.check(self.lib.cfb_plan_info(C.c_void_p(self.ws_ptr), C.byref(g), C.byref(t), C.byref(s),
                                           C.byref(p)), "cfb_plan_info")
@@ -92,6 +94,14 @@ class Plan:
         n = C.c_int()
         _lib.check(self.lib.cfb_plan_segments(C.c_void_p(self.ws_ptr), C.byref(n)), "cfb_plan_segments")
         self.segments = n.value
+
+    def rebuild(self, wait_ns: int = 0) -> None:
+        """Rebuild the plan in its own workspace (cfb_plan_build), with the given wait budget
+        (0 = the default): clears the sticky device error word after a failed run."""
+        torch.cuda.synchronize(self.ws.device)
+        self.run_desc.wait_budget_ns = wait_ns
+        _lib.check(self.lib.cfb_plan_build(C.byref(self.w.desc), C.byref(self.run_desc), C.c_void_p(self.ws_ptr),
+                                           C.c_size_t(self.ws_bytes)), "cfb_plan_build")
 
     def run(self, stream=None, group=None) -> None:
         """One persistent launch on `stream` (default: torch's current stream); a sharded-head plan
@@ -146,7 +156,8 @@ class Plan:
     def check(self) -> None:
         err = self.device_error()
         if err:
-            raise _lib.CfbError(f"device-side wait timed out (code {err}); outputs are invalid")
+            raise _lib.CfbError(f"device-side failure (code {err}: {_lib.DEV_ERRORS.get(err, '?')}); "
+                                f"outputs are invalid")
 
 
 class WidePlan:
@@ -155,7 +166,7 @@ class WidePlan:
     stream (capturable in a CUDA graph). For batches above what one persistent launch holds."""
 
     def __init__(self, w, mode: int, batch: int, *, width: int = 4, depth: int = 5, tree_keep: int = 4,
-                 tree_topb: int = 8, init_mode: int = 0):
+                 tree_topb: int = 8, init_mode: int = 0, wait_ns: int = 0):
         self.w, self.mode, self.batch = w, mode, batch
         cfg, dev = w.cfg, w.dev
         D = cfg.hidden
@@ -177,6 +188,7 @@ class WidePlan:
         r.mode, r.batch, r.width, r.depth = mode, batch, width, depth
         r.init_mode = init_mode
         r.tree_keep, r.tree_topb = tree_keep, tree_topb
+        r.wait_budget_ns = wait_ns
         r.ctx, r.z0, r.known0 = self.ctx.data_ptr(), self.z0.data_ptr(), self.known0.data_ptr()
         r.pred, r.tokens = self.pred.data_ptr(), self.tokens.data_ptr()
         self.run_desc = r
@@ -184,14 +196,29 @@ class WidePlan:
         _lib.check(self.lib.cfb_wide_workspace(C.byref(w.desc), C.byref(r), C.byref(nbytes)), "cfb_wide_workspace")
         self.ws = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=dev)
         self.ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        self.ws_bytes = int(nbytes.value)
+        self._h = None
+        self._create()
+
+    def _create(self) -> None:
         h = C.c_void_p()
-        _lib.check(self.lib.cfb_wide_create(C.byref(w.desc), C.byref(r), C.c_void_p(self.ws_ptr),
-                                            C.c_size_t(int(nbytes.value)), C.byref(h)), "cfb_wide_create")
+        _lib.check(self.lib.cfb_wide_create(C.byref(self.w.desc), C.byref(self.run_desc), C.c_void_p(self.ws_ptr),
+                                            C.c_size_t(self.ws_bytes), C.byref(h)), "cfb_wide_create")
         self._h = h
         n = C.c_int()
         _lib.check(self.lib.cfb_wide_info(h, C.byref(n)), "cfb_wide_info")
         self.launches = n.value
         self.segments = 1
+
+    def rebuild(self, wait_ns: int = 0) -> None:
+        """Re-create the plan in its own workspace with the given wait budget (0 = the default):
+        clears the sticky device error word after a failed run."""
+        torch.cuda.synchronize(self.ws.device)
+        if self._h is not None and self._h.value:
+            self.lib.cfb_wide_destroy(self._h)
+            self._h = None
+        self.run_desc.wait_budget_ns = wait_ns
+        self._create()
 
     def run(self, stream=None, group=None) -> None:
         if group is not None and self.w is not None and getattr(self.w, "head_ranks", 1) > 1:
@@ -206,7 +233,8 @@ class WidePlan:
     def check(self) -> None:
         err = self.device_error()
         if err:
-            raise _lib.CfbError(f"device-side wait timed out (code {err}); outputs are invalid")
+            raise _lib.CfbError(f"device-side failure (code {err}: {_lib.DEV_ERRORS.get(err, '?')}); "
+                                f"outputs are invalid")
 
     def __del__(self):
         h = getattr(self, "_h", None)

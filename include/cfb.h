@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define CFB_ABI_VERSION 3
+#define CFB_ABI_VERSION 4
 
 typedef enum cfb_status {
   CFB_OK = 0,
@@ -150,6 +150,14 @@ typedef struct cfb_run {
    * then rescores its beam rows against those rows only (log-softmax over the candidates).
    * Engine plans on one GPU (ranks <= 1); 0 < twopass_m < shortlist_rows. */
   int twopass_m;
+  /* Budget in ns of the waits that order the work of a draft (0 = the default, 1 s): the grid
+   * barrier between the phases of an engine plan, and in the wide plan's GEMMs the producer's
+   * wait for a free ring stage and the MMA issuer's wait for a loaded one. A wait that outlasts it
+   * ends the run with the plan's device error word set (cfb_plan_error / cfb_wide_error), and
+   * the run after a rebuild is clean. A budget below the default is checked at every poll, so a
+   * tiny one (1 ns) makes those waits expire on purpose: that is how the failure path is
+   * tested. Waits for copies already in flight (before a CTA may exit) always get the default. */
+  uint64_t wait_budget_ns;
 } cfb_run;
 
 #define CFB_XROWS 64
@@ -244,7 +252,9 @@ cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);
 
 /* Tree-aware Gated-DeltaNet verification over B independent trees of N nodes.
  * q,k [B,N,H,Dk] fp16; v [B,N,H,Dv] fp16; g (log decay), beta [B,N,H] fp32;
- * parent [B,N] int32 (parent < child; -1 = root, reads init); init [B,H,Dk,Dv] fp32;
+ * parent [B,N] int32 (parent < child; -1 = root, reads init; a node whose parent is neither
+ * -1 nor an earlier node gets NaN output and state, as do its descendants, and the bad index is
+ * never dereferenced); init [B,H,Dk,Dv] fp32;
  * out o [B,N,H,Dv] fp32; states [B,N,H,Dk,Dv] fp32 (every node's state; also where a child
  * reads its parent's state, so it is required).
  * use_l2norm: q,k <- x / (||x|| + 1e-6); q is scaled by Dk**-0.5.

@@ -60,3 +60,37 @@ def check_tree(tokens, W, cfg, emb, hw, w2, sl, pred, known0, keep, topb, depth,
             cum = torch.tensor(scores)
             prev_base, base, fr = base, base + k, k
         assert base == N, (b, base, N)
+
+
+def chain_logprob(W, cfg, emb, hw, w2, sl, pred_b, known0_b, toks):
+    """The oracle's cumulative log-prob of one chain (tokens at depths 1..K) of one request: the
+    sum over depths of log_softmax((h + path residual) @ hw^T + markov bias) at the chain's token,
+    with the path built from the chain itself (reference flow_proposer.py:1234-1259)."""
+    order = cfg.path_order
+    lastp = torch.full((1, order), -1, dtype=torch.long)
+    lastp[0, 0] = int(known0_b)
+    total = 0.0
+    for d, t in enumerate(toks.tolist(), start=1):
+        _, lp = oracle.head_logprobs(W, emb, hw, w2, pred_b[d].float().unsqueeze(0), lastp, order, d)
+        loc = int(torch.searchsorted(sl, torch.tensor(t)))
+        assert loc < sl.numel() and int(sl[loc]) == t, (d, t, "not a shortlist id")
+        total += float(lp[0, loc])
+        lastp = torch.cat([torch.tensor([[t]]), lastp[:, :-1]], dim=1)
+    return total
+
+
+def check_chain(tokens, W, cfg, emb, hw, w2, sl, pred, known0, width, K, eps=5e-3):
+    """tokens [B, K] from the engine against the oracle's chain beam over the same hiddens `pred`.
+    A request must match exactly, or else (a near-tie the engine's fp16 head inputs can flip) its
+    chain must score, under the oracle, within `eps` of the oracle's best final beam. Returns the
+    number of requests that matched exactly."""
+    want, _, cum = oracle.beam_chains(W, cfg, emb, hw, w2, sl, pred, known0, width, K, return_beams=True)
+    exact = 0
+    for b in range(tokens.shape[0]):
+        if torch.equal(tokens[b], want[b]):
+            exact += 1
+            continue
+        s = chain_logprob(W, cfg, emb, hw, w2, sl, pred[b], known0[b], tokens[b])
+        best = float(cum[b].max())
+        assert s >= best - eps, (b, tokens[b].tolist(), want[b].tolist(), s, best)
+    return exact

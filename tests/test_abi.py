@@ -25,7 +25,7 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.cfb_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.cfb_abi_version() == _lib.ABI_VERSION == 4
 
 
 def test_packed_bytes():

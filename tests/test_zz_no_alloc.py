@@ -80,3 +80,30 @@ def test_noalloc_rejects_sizes_beyond_its_array():
     st = lib.cfb_tree_gdn_noalloc(_ptr(q), _ptr(k), _ptr(v), _ptr(gl), _ptr(beta), _ptr(par), _ptr(init),
                                   _ptr(o), 5, 16, 16, 128, 128, 1, stream)
     assert st == 3                                   # CFB_ERR_WORKSPACE
+
+
+def test_noalloc_malformed_parent_is_nan_not_leftover_state():
+    """A call after a larger one leaves node states of the first call in the shared array. A node
+    whose parent index points past its own position (p == n) must not read them: its output, and
+    its descendants' outputs, are NaN; every other node equals the existing entry point's."""
+    from chain_flow_b200 import _lib
+    lib = _lib.load()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    _call_noalloc(lib, stream, *_inputs(4, 16, 16, 128, 303))        # fills the array
+    q, k, v, gl, beta, par, init = _inputs(1, 16, 16, 128, 404)
+    bad = 9
+    par[0, bad] = bad                                                 # parent == self
+    got = _call_noalloc(lib, stream, q, k, v, gl, beta, par, init)
+    want = _call_existing(lib, stream, q, k, v, gl, beta, par, init)
+    torch.cuda.synchronize()
+    p = par[0].tolist()
+    tainted = set()
+    for n in range(16):
+        if n == bad or p[n] in tainted:
+            tainted.add(n)
+    for n in range(16):
+        if n in tainted:
+            assert torch.isnan(got[0, n]).all() and torch.isnan(want[0, n]).all(), n
+        else:
+            assert torch.isfinite(got[0, n]).all(), n
+            assert _rel(got[0, n], want[0, n]) <= GDN_RTOL, (n, _rel(got[0, n], want[0, n]))
