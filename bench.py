@@ -43,7 +43,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify", "ring"])
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify", "ring",
+                                                         "tree-attn", "tree-verify", "4b-head"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="--impl reference: the reference algorithm on the host cores (default, fp32) or in "
@@ -603,6 +604,43 @@ def run_gdn_verify(args):
                 "cpu_baseline": {"value": 1.0 / cpu_s, "unit": "req/s", "cores": torch.get_num_threads(),
                                  "kind": "port", "sample": "1 request (41 rows), oracle fp32 on CPU"}}
         print(json.dumps(line), flush=True)
+        # the same outputs by the shared-root factorisation (reference fork gdn_factor): the root
+        # state is read once per (request, head) and no state is written
+        from chain_flow_b200.gdn import gdn_factor
+        row_start = (torch.arange(B, device=dev) * N).to(torch.int32)
+        row_count = torch.full((B,), N, dtype=torch.int32, device=dev)
+        fac = lambda: gdn_factor(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, init_slot, row_start,
+                                 row_count, scale=K ** -0.5, n_max=N)
+        for _ in range(max(3, args.warmup)):
+            fac()
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(args.steps):
+            fac()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        fms = e0.elapsed_time(e1) / args.steps
+        fbytes = B * (slot + N * (H * K * 2 * 2 + HV * V * 2 * 2 + HV * 8))
+        t0 = time.perf_counter()
+        oracle.tree_gdn_factor(*args_c, st_c, chain[sl].cpu(), depth[sl].cpu(), torch.zeros(N, dtype=torch.int32),
+                               torch.zeros(1, dtype=torch.int32), torch.full((1,), N, dtype=torch.int32), K ** -0.5)
+        fcpu = time.perf_counter() - t0
+        line = {"metric": "tree GDN verify outputs, shared-root factorisation: requests/s (41-row trees, 32 value heads)",
+                "value": B / (fms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": max(3, args.warmup), "ms_per_step": fms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 state, bf16 q/k/v",
+                "data": "synthetic (seeded q,k,v,a,b,A_log,dt_bias,trees)",
+                "config": {"workload": "gdn-factor (reference in-engine shape)", "batch": B, "rows_per_request": N,
+                           "heads": H, "value_heads": HV, "dk": K, "dv": V,
+                           "note": "outputs only; the accepted leaf's state is materialised afterwards by the verify"},
+                "gpu_launches": args.steps,
+                "roofline": {"bound": "latency (hbm figure for context)", "achieved": fbytes / (fms / 1e3) / 1e9,
+                             "peak": peak, "unit": "GB/s", "frac": fbytes / (fms / 1e3) / 1e9 / peak, "traffic": None,
+                             "peak_source": peak_kind, "kernel": "tree_gdn_factor_kernel",
+                             "algorithmic_bytes_per_launch": fbytes},
+                "cpu_baseline": {"value": 1.0 / fcpu, "unit": "req/s", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": "1 request (41 rows), factor oracle fp32 on CPU"}}
+        print(json.dumps(line), flush=True)
 
 
 def run_ring(args):
@@ -681,8 +719,205 @@ def run_ring(args):
         print(json.dumps(line), flush=True)
 
 
+def _graph_time_ms(fn, steps: int, per_graph: int = 20) -> tuple[float, int]:
+    """Mean device time of one fn() call, from a CUDA graph of per_graph calls replayed until
+    `steps` calls have been timed (CUDA events around the replays): the kernels are a few
+    microseconds long, so launched one by one from Python the host would be the bound."""
+    dev = torch.device("cuda", 0)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(per_graph):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(1, steps // per_graph)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    del graph
+    return e0.elapsed_time(e1) / (reps * per_graph), reps * per_graph
+
+
+def run_tree_attn(args):
+    """The tree-attention fix-up of one full-attention layer of the target (the reference fork's
+    suffix_merge, vllm-0.25.1-chain-flow-tree.patch:5235-5540): every node of a 40-node draft tree
+    attends to its ancestors and is merged with the paged-prefix result. The reference measures
+    5.33 us per layer at 4B (H=16, HKV=4, D=256) and 5.74 us at 27B (H=24) on its RTX PRO 6000,
+    under CUDA-graph replay (patch:2819-2824). A step is one cfb_tree_attn_merge launch; one JSON
+    line per shape. Algorithmic bytes per launch: the q, k, v, prefix and output rows, the prefix
+    log-sum-exps, the node table and the ancestor mask."""
+    from chain_flow_b200.gdn import make_tree
+    from chain_flow_b200.tree import ancestor_mask, tree_attn_merge
+    import oracle
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = measured_peaks()
+    N, D = 40, 256
+    for S, H, HKV, shape in ((1, 16, 4, "4B"), (1, 24, 4, "27B"), (8, 16, 4, "4B")):
+        g = torch.Generator(device=dev).manual_seed(S * H)
+        T = S * N
+        dt = torch.bfloat16
+        q = torch.randn(T, H, D, device=dev, generator=g).to(dt)
+        k = torch.randn(T, HKV, D, device=dev, generator=g).to(dt)
+        v = torch.randn(T, HKV, D, device=dev, generator=g).to(dt)
+        po = torch.randn(T, H, D, device=dev, generator=g).to(dt)
+        plse = torch.randn(H, T, device=dev, generator=g)
+        idx = torch.arange(T, device=dev).view(S, N)
+        par = torch.stack([make_tree(N, 5, 4, seed=s)[0] for s in range(S)]).to(dev)
+        mask = ancestor_mask(par)
+        out = torch.empty(T, H, D, device=dev, dtype=dt)
+        scale = D ** -0.5
+        ms, n = _graph_time_ms(lambda: tree_attn_merge(q, k, v, out, po, plse, idx, mask, scale), max(args.steps, 20))
+        nbytes = T * H * D * 2 * 3 + T * HKV * D * 2 * 2 + H * T * 4 + T * 8 + S * N * N
+        torch.set_num_threads(os.cpu_count() or 1)
+        args_c = [t.cpu() for t in (q, k, v, out, po, plse, idx, mask)]
+        t0 = time.perf_counter()
+        oracle.tree_attn_merge(*args_c, scale)
+        cpu_s = time.perf_counter() - t0
+        line = {"metric": "tree-attention suffix + LSE merge: us per full-attention layer (40-node tree)",
+                "value": ms * 1e3, "unit": "us", "n_gpus": 1, "steps": n, "warmup": 3, "ms_per_step": ms,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 math)",
+                "data": "synthetic (seeded q,k,v,prefix rows, BFS trees of depth 5)",
+                "config": {"workload": f"tree-attn ({shape} target layer)", "requests": S, "nodes": N, "heads": H,
+                           "kv_heads": HKV, "head_dim": D,
+                           "timing": "CUDA graph of 20 launches (the reference's figure is under graph replay)",
+                           "reference_us_per_layer": 5.33 if H == 16 else 5.74},
+                "gpu_launches": n,
+                "roofline": {"bound": "latency (hbm figure for context)", "achieved": nbytes / (ms / 1e3) / 1e9,
+                             "peak": peak, "unit": "GB/s", "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                             "peak_source": peak_kind, "kernel": "tree_attn_merge_kernel",
+                             "algorithmic_bytes_per_launch": nbytes},
+                "cpu_baseline": {"value": cpu_s * 1e6, "unit": "us", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": "1 layer, oracle fp32 on CPU"}}
+        print(json.dumps(line), flush=True)
+
+
+def run_tree_verify(args):
+    """Greedy verification of a draft tree (the reference fork's tree_rejection_sample,
+    vllm-0.25.1-chain-flow-tree.patch:640-723): the argmax of every logits row (41 rows per request:
+    the committed token and 40 tree nodes, over the 248,320-token vocabulary) and the walk down the
+    tree, in one launch. A step is one cfb_tree_verify_greedy launch; one JSON line per batch.
+    Algorithmic bytes: the logits rows."""
+    from chain_flow_b200.gdn import make_tree
+    from chain_flow_b200.tree import TreeVerifier
+    import oracle
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = measured_peaks()
+    N, V = 40, 248320
+    for B, dt in ((1, torch.bfloat16), (8, torch.bfloat16), (8, torch.float32)):
+        g = torch.Generator(device=dev).manual_seed(B)
+        rows = B * (N + 1)
+        logits = torch.randn(rows, V, device=dev, generator=g).to(dt)
+        pars = torch.cat([make_tree(N, 5, 4, seed=b)[0] for b in range(B)]).to(dev)
+        toks = torch.randint(0, V, (B * N,), device=dev, generator=g)
+        cu_d = torch.arange(1, B + 1, device=dev) * N
+        cu_s = torch.arange(1, B + 1, device=dev) * (N + 1)
+        ver = TreeVerifier(rows, B, N, device=dev)
+        ms, n = _graph_time_ms(lambda: ver(logits, cu_d, cu_s, toks, pars), max(args.steps, 20))
+        nbytes = rows * V * logits.element_size()
+        torch.set_num_threads(os.cpu_count() or 1)
+        lc = logits.cpu()
+        t0 = time.perf_counter()
+        oracle.tree_verify_greedy(lc, cu_d.cpu(), cu_s.cpu(), toks.cpu(), pars.cpu(), N)
+        cpu_s = time.perf_counter() - t0
+        line = {"metric": "greedy tree verification: us per verify (argmax of 41 logits rows per request + descent)",
+                "value": ms * 1e3, "unit": "us", "n_gpus": 1, "steps": n, "warmup": 3, "ms_per_step": ms,
+                "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16 logits" if dt == torch.bfloat16 else "f32 logits",
+                "data": "synthetic (seeded logits, BFS trees of depth 5)",
+                "config": {"workload": "tree-verify", "requests": B, "nodes": N, "vocab": V,
+                           "timing": "CUDA graph of 20 launches; logits larger than L2 at 8 requests"},
+                "gpu_launches": n,
+                "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "peak_source": peak_kind,
+                             "kernel": "tree_verify_greedy_kernel", "algorithmic_bytes_per_launch": nbytes},
+                "cpu_baseline": {"value": cpu_s * 1e6, "unit": "us", "cores": torch.get_num_threads(),
+                                 "kind": "port", "sample": f"1 verify of {B} requests, oracle on CPU"}}
+        print(json.dumps(line), flush=True)
+
+
+def run_head(args):
+    """The beam half of a cfg 2 (4B) draft alone: a CFB_MODE_BEAM_CHAIN engine plan over given
+    integrated hidden states, b=1 and 8, i.e. per depth the path residual, the shortlist head (62,642
+    rows of [lm_head | markov w2], 352.8 MB) with its fused log-sum-exp / top-k, and the beam step.
+    Here the head is the dominant traffic, so the plan's HBM fraction is the head's (north_star: >=
+    0.70 of HBM on the shortlist head). Timed with CUDA events over back-to-back launches; the
+    2 GB of head and path weights a draft streams exceed L2."""
+    from chain_flow_b200 import _lib
+    from chain_flow_b200.engine import Plan
+    from chain_flow_b200.proposer import FlowDrafterProposer
+    from chain_flow_b200.synthetic import WORKLOADS, make_state
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    wl = WORKLOADS["4b"]
+    peak, peak_kind = measured_peaks()
+    sd, emb, lm, sl = make_state(wl, seed=0, device=dev)
+    prop = FlowDrafterProposer.from_components(sd, wl.model_args(), emb, lm, sl, width=wl.width, K=wl.draft_tokens,
+                                               device=dev, seed=1000)
+    del sd, lm
+    torch.cuda.empty_cache()
+    row = wl.hidden + wl.markov_rank
+    for B in (1, 8):
+        p = Plan(prop.weights, _lib.MODE_BEAM_CHAIN, B, width=wl.width, depth=wl.draft_tokens)
+        g = torch.Generator(device=dev).manual_seed(B)
+        p.pred.copy_(torch.randn(p.pred.shape, device=dev, generator=g))
+        p.known0.copy_(torch.randint(0, wl.vocab, (B,), device=dev, generator=g))
+        for _ in range(max(3, args.warmup)):
+            p.run()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            p.run()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        p.check()
+        ms = e0.elapsed_time(e1) / args.steps
+        head = wl.draft_tokens * wl.shortlist_rows * row * 2
+        path = sum(2 * (min(d, wl.path_order) * wl.hidden ** 2 + 4 * wl.hidden ** 2)
+                   for d in range(1, wl.draft_tokens + 1))
+        nbytes = head + path
+        line = {"metric": "beam half of a 4B draft (path residual + shortlist head + beam, 5 depths): ms per draft",
+                "value": ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+                "ms_per_step": ms, "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded random-init head, N(0,1) hidden states)",
+                "config": {"workload": "cfg2-4B beam plan (CFB_MODE_BEAM_CHAIN)", "batch": B, "depths": wl.draft_tokens,
+                           "shortlist_rows": wl.shortlist_rows, "head_bytes_per_depth": wl.shortlist_rows * row * 2,
+                           "l2": "inputs larger than L2: 1.76 GB of head weights stream from HBM every step"},
+                "gpu_launches": args.steps,
+                "roofline": {"bound": "hbm", "achieved": nbytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                             "frac": nbytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "peak_source": peak_kind,
+                             "kernel": "engine_kernel (beam plan)", "algorithmic_bytes_per_launch": nbytes,
+                             "head_share_of_bytes": head / nbytes}}
+        print(json.dumps(line), flush=True)
+        del p
+
+
 def main():
     args = parse()
+    if args.workload == "4b-head":
+        run_head(args)
+        return
+    if args.workload == "tree-attn":
+        run_tree_attn(args)
+        return
+    if args.workload == "tree-verify":
+        run_tree_verify(args)
+        return
     if args.workload == "ring":
         run_ring(args)
         return

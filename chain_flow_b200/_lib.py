@@ -30,7 +30,8 @@ EXPORTED = [
     "cfb_plan_segments", "cfb_plan_run_segment", "cfb_wide_gemm", "cfb_wide_packed_bytes", "cfb_wide_pack", "cfb_wide_workspace",
     "cfb_wide_create", "cfb_wide_run", "cfb_wide_error", "cfb_wide_info", "cfb_wide_destroy",
     "cfb_ring_write", "cfb_ring_gather", "cfb_tree_gdn_verify", "cfb_vae_workspace", "cfb_vae_create",
-    "cfb_vae_plan_workspace", "cfb_vae_plan_build",
+    "cfb_vae_plan_workspace", "cfb_vae_plan_build", "cfb_tree_attn_merge", "cfb_tree_verify_workspace",
+    "cfb_tree_verify_greedy", "cfb_tree_gdn_factor",
 ]
 ABI_VERSION = 4
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
@@ -137,6 +138,14 @@ def _declare(lib):
     lib.cfb_vae_create.argtypes = [C.POINTER(VaeSide), i32, i32, i32, vp, vp, vp, sz, C.POINTER(vp)]
     lib.cfb_vae_plan_workspace.argtypes = [C.POINTER(VaeSide), i32, i32, i32, C.POINTER(sz)]
     lib.cfb_vae_plan_build.argtypes = [C.POINTER(VaeSide), i32, i32, i32, vp, vp, vp, sz]
+    lib.cfb_tree_attn_merge.argtypes = [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64,
+                                        vp, vp, vp, C.c_float, i32, i32, i32, i32, i32, i32, vp]
+    lib.cfb_tree_gdn_factor.argtypes = [vp, i32, vp, i32, vp, i32, vp, i32, vp, vp, vp, vp, i32, vp, i64, vp, i32,
+                                        vp, vp, vp, vp, i32, i32, C.c_float, i32, i32, i32, i32, vp]
+    lib.cfb_tree_verify_workspace.argtypes = [i32, i32]
+    lib.cfb_tree_verify_workspace.restype = sz
+    lib.cfb_tree_verify_greedy.argtypes = [vp, i64, i32, i32, i32, vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, vp,
+                                           sz, vp, vp]
     return lib
 
 

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB = PKG / "libcfb.so"
-SOURCES = ["cfb_engine.cu", "cfb_pack.cu", "cfb_gdn.cu", "cfb_wide.cu", "cfb_ring.cu"]
+SOURCES = ["cfb_engine.cu", "cfb_pack.cu", "cfb_gdn.cu", "cfb_wide.cu", "cfb_ring.cu", "cfb_tree.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -438,3 +438,257 @@ extern "C" cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, co
     tree_gdn_verify_kernel<__nv_bfloat16><<<grid, kVerifyThreads, kVerifySmem, static_cast<cudaStream_t>(stream)>>>(A);
   return cfb_launch_status("tree_gdn_verify_kernel");
 }
+
+// =================================================================================================
+// Shared-root factorisation of the tree GDN verify (the contract of the reference fork's
+// gdn_factor, src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4664-5094): the outputs of
+// every row of a request whose rows all start from ONE state slot H, with no per-node state read
+// or written. Every update along a path is rank 1, so (k^ = k * rsqrt(|k|^2 + 1e-6),
+// q^ = q * rsqrt(|q|^2 + 1e-6) * scale, g the decay, beta the gate)
+//   h_t = D_t H + sum_{m on t's path} w_{m,t} u_m k^_m^T,  D_t = g_t D_p,  w_{m,t} = g_t w_{m,p},
+//   w_{t,t} = 1,  u_t = beta_t (v_t - g_t S_t),
+//   S_t = h_p k^_t = D_p (H k^_t) + sum_{m on p's path} w_{m,p} (k^_m . k^_t) u_m,
+//   o_t = h_t q^_t = D_t (H q^_t) + sum_{m on t's path} w_{m,t} (k^_m . q^_t) u_m.
+// H is touched only through the matrix-vector products H k^_t and H q^_t; the rest is dot products
+// of the small k / q vectors and a level-by-level solve for the u_t.
+//
+// One CTA per (32 value rows, value head, request), 8 warps. The CTA stages the request's
+// normalised keys and queries, gates, values and chains, and its 32 rows of H (padded rows in
+// shared memory, then each warp holds them in registers, one row per lane); warp w forms the
+// products H k^_j / H q^_j for j = w, w + 8, ... with the vectors broadcast from shared memory.
+// The ancestor dot products take a warp each. Then the nodes are solved level by level (a warp per
+// node, a lane per value row) and every node's output is contracted.
+namespace {
+
+constexpr int kFacWarps = 8;
+constexpr int kFacThreads = kFacWarps * 32;
+constexpr int kFacBV = 32;                 // value rows per CTA
+constexpr int kFacMaxN = 64;               // rows per request
+constexpr int kFacMaxW = kMaxChain;        // chain entries per row (depth + 1)
+constexpr int kFacHLd = kDk + 4;           // padded row of the staged H block
+
+struct FactorArgs {
+  const void* A_log; int c_alog;
+  const void* dt_bias; int c_dtb;
+  const void* a; int c_a;
+  const void* b; int c_b;
+  const void* q; const void* k; const void* v; void* o;
+  const float* state; long long slot_stride;
+  const int* chain; int chain_stride;
+  const int* depth; const int* init_slot; const int* row_start; const int* row_count;
+  float scale, threshold;
+  int H, HV, V, n_max;
+};
+
+// shared memory of one CTA for requests of up to n rows (floats, then ints)
+inline size_t factor_smem(int n) {
+  const size_t f = (size_t)2 * n * kDk            // k^, q^
+                   + (size_t)kFacBV * kFacHLd      // H block
+                   + (size_t)4 * n * kFacBV        // H k^, H q^, u, v
+                   + (size_t)3 * n                 // g, beta, D
+                   + (size_t)3 * n * kFacMaxW;     // w, (k^_m . k^_t), (k^_m . q^_t)
+  const size_t i = (size_t)n * kFacMaxW + 3 * (size_t)n + kFacMaxW;   // chains, depths, levels, flags
+  return (f + i) * 4;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFacThreads) tree_gdn_factor_kernel(const FactorArgs A) {
+  extern __shared__ __align__(16) float fsm[];
+  const int vb = blockIdx.x, hv = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = hv / (A.HV / A.H);
+  const int base = A.row_start[s], n = A.row_count[s];
+  const int NM = A.n_max;
+  float* xk = fsm;                                   // [NM][kDk]
+  float* xq = xk + (size_t)NM * kDk;                 // [NM][kDk]
+  float* sH = xq + (size_t)NM * kDk;                 // [kFacBV][kFacHLd]
+  float* sP = sH + (size_t)kFacBV * kFacHLd;         // [NM][kFacBV]  H k^
+  float* sQ = sP + (size_t)NM * kFacBV;              //               H q^
+  float* sU = sQ + (size_t)NM * kFacBV;
+  float* sV = sU + (size_t)NM * kFacBV;
+  float* sg = sV + (size_t)NM * kFacBV;
+  float* sb = sg + NM;
+  float* sD = sb + NM;
+  float* sW = sD + NM;                               // [NM][kFacMaxW]
+  float* sC = sW + (size_t)NM * kFacMaxW;            // C[t][j] = k^_{m_j} . k^_t
+  float* sR = sC + (size_t)NM * kFacMaxW;            // R[t][j] = k^_{m_j} . q^_t
+  int* sCh = reinterpret_cast<int*>(sR + (size_t)NM * kFacMaxW);   // [NM][kFacMaxW] local ids
+  int* sDep = sCh + (size_t)NM * kFacMaxW;
+  int* sLev = sDep + NM;                             // nodes sorted by depth
+  int* sLevN = sLev + NM;                            // [kFacMaxW] first index of each depth
+  int* sbad = sLevN + kFacMaxW;                      // [NM] rows with an unusable chain
+  if (n <= 0) return;
+  const T* q = static_cast<const T*>(A.q);
+  const T* k = static_cast<const T*>(A.k);
+  const T* v = static_cast<const T*>(A.v);
+  const int v0 = vb * kFacBV;
+  // chains (local ids), depths, gates, values, and the H block
+  for (int t = tid; t < n; t += kFacThreads) {
+    // a depth past the chain row, or a chain entry outside this request's rows, is never used
+    // as an index: the row is computed as a root-level node and its output is NaN
+    const int dep = A.depth[base + t];
+    bool bad = dep < 0 || dep >= A.chain_stride;
+    const int d = bad ? 0 : dep;
+    for (int j = 0; j <= d; ++j) {
+      const int m = A.chain[(long long)(base + t) * A.chain_stride + j] - base;
+      const bool ok = m >= 0 && m < n && (j > 0 || m == t);
+      bad |= !ok;
+      sCh[t * kFacMaxW + j] = ok ? m : t;
+    }
+    sDep[t] = bad ? 0 : d;
+    sbad[t] = bad;
+    const float x = ld_code(A.a, A.c_a, (long long)(base + t) * A.HV + hv) + ld_code(A.dt_bias, A.c_dtb, hv);
+    const float sp = x <= A.threshold ? log1pf(expf(x)) : x;
+    sg[t] = expf(-expf(ld_code(A.A_log, A.c_alog, hv)) * sp);
+    sb[t] = 1.f / (1.f + expf(-ld_code(A.b, A.c_b, (long long)(base + t) * A.HV + hv)));
+  }
+  for (int e = tid; e < n * kFacBV; e += kFacThreads) {
+    const int t = e / kFacBV, vl = e - t * kFacBV;
+    sV[t * kFacBV + vl] = to_f(v[((long long)(base + t) * A.HV + hv) * A.V + v0 + vl]);
+  }
+  {
+    const float4* src = reinterpret_cast<const float4*>(
+        A.state + (long long)A.init_slot[base] * A.slot_stride + ((long long)hv * A.V + v0) * kDk);
+    for (int e = tid; e < kFacBV * (kDk / 4); e += kFacThreads) {
+      const int r = e / (kDk / 4), c4 = e - r * (kDk / 4);
+      *reinterpret_cast<float4*>(&sH[r * kFacHLd + 4 * c4]) = src[e];
+    }
+  }
+  // normalised keys and queries: a warp per row, lane l holds columns 4l .. 4l+3
+  for (int rr = warp; rr < 2 * n; rr += kFacWarps) {
+    const bool isq = rr >= n;
+    const int t = isq ? rr - n : rr;
+    const T* src = (isq ? q : k) + ((long long)(base + t) * A.H + h) * kDk + lane * 4;
+    const float e0 = to_f(src[0]), e1 = to_f(src[1]), e2 = to_f(src[2]), e3 = to_f(src[3]);
+    float ss = (e0 * e0 + e1 * e1) + (e2 * e2 + e3 * e3);
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss + 1e-6f) * (isq ? A.scale : 1.f);
+    *reinterpret_cast<float4*>((isq ? xq : xk) + (size_t)t * kDk + lane * 4) =
+        make_float4(e0 * inv, e1 * inv, e2 * inv, e3 * inv);
+  }
+  __syncthreads();
+  if (tid == 0) {                                    // level lists: nodes ordered by depth
+    int cnt[kFacMaxW] = {};
+    for (int t = 0; t < n; ++t) ++cnt[sDep[t]];
+    int acc = 0;
+    for (int d = 0; d < kFacMaxW; ++d) { sLevN[d] = acc; acc += cnt[d]; cnt[d] = sLevN[d]; }
+    for (int t = 0; t < n; ++t) sLev[cnt[sDep[t]]++] = t;
+  }
+  // H k^_j and H q^_j: lane = value row, the row in registers
+  {
+    float hr[kDk];
+#pragma unroll
+    for (int c = 0; c < kDk / 4; ++c) {
+      const float4 f = *reinterpret_cast<const float4*>(&sH[lane * kFacHLd + 4 * c]);
+      hr[4 * c] = f.x; hr[4 * c + 1] = f.y; hr[4 * c + 2] = f.z; hr[4 * c + 3] = f.w;
+    }
+    for (int j = warp; j < 2 * n; j += kFacWarps) {
+      const float* x = j < n ? xk + (size_t)j * kDk : xq + (size_t)(j - n) * kDk;
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+      for (int c = 0; c < kDk / 4; ++c) {
+        const float4 xx = *reinterpret_cast<const float4*>(x + 4 * c);
+        p0 = fmaf(hr[4 * c], xx.x, p0); p1 = fmaf(hr[4 * c + 1], xx.y, p1);
+        p2 = fmaf(hr[4 * c + 2], xx.z, p2); p3 = fmaf(hr[4 * c + 3], xx.w, p3);
+      }
+      (j < n ? sP : sQ)[(size_t)(j < n ? j : j - n) * kFacBV + lane] = (p0 + p1) + (p2 + p3);
+    }
+  }
+  // the ancestor dot products: pair (t, j) -> C[t][j] (j >= 1) and R[t][j] (j >= 0)
+  for (int t = warp; t < n; t += kFacWarps) {
+    const float4 kt = *reinterpret_cast<const float4*>(xk + (size_t)t * kDk + lane * 4);
+    const float4 qt = *reinterpret_cast<const float4*>(xq + (size_t)t * kDk + lane * 4);
+    for (int j = 0; j <= sDep[t]; ++j) {
+      const int m = sCh[t * kFacMaxW + j];
+      const float4 km = *reinterpret_cast<const float4*>(xk + (size_t)m * kDk + lane * 4);
+      float c = (km.x * kt.x + km.y * kt.y) + (km.z * kt.z + km.w * kt.w);
+      float r = (km.x * qt.x + km.y * qt.y) + (km.z * qt.z + km.w * qt.w);
+      for (int off = 16; off > 0; off >>= 1) {
+        c += __shfl_xor_sync(0xffffffffu, c, off);
+        r += __shfl_xor_sync(0xffffffffu, r, off);
+      }
+      if (lane == 0) { sC[t * kFacMaxW + j] = c; sR[t * kFacMaxW + j] = r; }
+    }
+  }
+  __syncthreads();
+  // level by level: u_t, D_t and the path weights w_{m,t}
+  for (int d = 0; d < kFacMaxW; ++d) {
+    const int l0 = sLevN[d], l1 = d + 1 < kFacMaxW ? sLevN[d + 1] : n;
+    if (l0 >= l1) continue;
+    for (int i = l0 + warp; i < l1; i += kFacWarps) {
+      const int t = sLev[i];
+      const int par = d > 0 ? sCh[t * kFacMaxW + 1] : -1;
+      const float Dp = d > 0 ? sD[par] : 1.f;
+      float S = Dp * sP[t * kFacBV + lane];
+      for (int j = 1; j <= d; ++j) {
+        const int m = sCh[t * kFacMaxW + j];
+        S = fmaf(sW[par * kFacMaxW + j - 1] * sC[t * kFacMaxW + j], sU[m * kFacBV + lane], S);
+      }
+      const float g = sg[t];
+      sU[t * kFacBV + lane] = sb[t] * (sV[t * kFacBV + lane] - g * S);
+      if (lane <= d) sW[t * kFacMaxW + lane] = lane == 0 ? 1.f : sW[par * kFacMaxW + lane - 1] * g;
+      if (lane == 0) sD[t] = Dp * g;
+    }
+    __syncthreads();
+  }
+  // outputs
+  for (int t = warp; t < n; t += kFacWarps) {
+    const int d = sDep[t];
+    float acc = sD[t] * sQ[t * kFacBV + lane];
+    for (int j = 0; j <= d; ++j) {
+      const int m = sCh[t * kFacMaxW + j];
+      acc = fmaf(sW[t * kFacMaxW + j] * sR[t * kFacMaxW + j], sU[m * kFacBV + lane], acc);
+    }
+    from_f(static_cast<T*>(A.o)[((long long)(base + t) * A.HV + hv) * A.V + v0 + lane],
+           sbad[t] ? __int_as_float(0x7fc00000) : acc);
+  }
+}
+
+cfb_status factor_smem_attr(size_t bytes) {
+  static std::mutex mu;
+  static size_t done[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return cfb_launch_status("cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return CFB_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev] >= bytes) return CFB_OK;
+  if (cudaFuncSetAttribute(tree_gdn_factor_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(tree_gdn_factor_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)bytes) != cudaSuccess)
+    return cfb_launch_status("tree_gdn_factor_kernel shared-memory attribute");
+  done[dev] = bytes;
+  return CFB_OK;
+}
+
+}  // namespace
+
+extern "C" cfb_status cfb_tree_gdn_factor(const void* A_log, int A_log_dtype, const void* dt_bias, int dt_bias_dtype,
+                                          const void* a, int a_dtype, const void* b, int b_dtype, const void* q,
+                                          const void* k, const void* v, void* o, int qkv_dtype, const float* state,
+                                          int64_t slot_stride, const int32_t* chain, int chain_stride,
+                                          const int32_t* depth, const int32_t* init_slot, const int32_t* row_start,
+                                          const int32_t* row_count, int S, int n_max, float scale, int H, int HV,
+                                          int K, int V, void* stream) {
+  if (!A_log || !dt_bias || !a || !b || !q || !k || !v || !o || !state || !chain || !depth || !init_slot ||
+      !row_start || !row_count || S < 0 || H <= 0 || HV <= 0 || chain_stride <= 0 || n_max <= 0)
+    return CFB_ERR_INVALID_ARG;
+  for (int c : {A_log_dtype, dt_bias_dtype, a_dtype, b_dtype})
+    if (c < GV_F32 || c > GV_BF16) return CFB_ERR_INVALID_ARG;
+  if (K != kDk || V <= 0 || V % kFacBV || HV % H || n_max > kFacMaxN || chain_stride > kFacMaxW ||
+      (qkv_dtype != GV_F16 && qkv_dtype != GV_BF16))
+    return CFB_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(state) & 15) || slot_stride < (int64_t)HV * V * K || slot_stride % 4)
+    return CFB_ERR_INVALID_ARG;
+  if (S == 0) return CFB_OK;
+  const size_t smem = factor_smem(n_max);
+  const cfb_status sa = factor_smem_attr(smem);
+  if (sa != CFB_OK) return sa;
+  FactorArgs A{A_log, A_log_dtype, dt_bias, dt_bias_dtype, a, a_dtype, b, b_dtype, q, k, v, o, state, slot_stride,
+               chain, chain_stride, depth, init_slot, row_start, row_count, scale, 20.0f, H, HV, V, n_max};
+  const dim3 grid((unsigned)(V / kFacBV), (unsigned)HV, (unsigned)S);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (qkv_dtype == GV_F16) tree_gdn_factor_kernel<__half><<<grid, kFacThreads, smem, st>>>(A);
+  else tree_gdn_factor_kernel<__nv_bfloat16><<<grid, kFacThreads, smem, st>>>(A);
+  return cfb_launch_status("tree_gdn_factor_kernel");
+}

@@ -64,10 +64,10 @@ def tree_gated_delta_scan(query, key, value, g, beta, parent, depth, initial_sta
                           use_qk_l2norm: bool = True):
     """Reference-signature single tree: query,key [N,H,Dk]; value [N,H,Dv]; g,beta [N,H];
     parent [N] (-1 = root); depth [N] (accepted for signature parity: nodes must be in BFS order,
-    parent < child, which the kernel relies on instead); initial_state [H,Dk,Dv]."""
+    parent < child, which the kernel relies on instead); initial_state [H,Dk,Dv]. No host sync: a
+    node whose parent is neither -1 nor an earlier node gets NaN output and state (so do its
+    descendants), and the bad index is never dereferenced."""
     par = parent.view(1, -1)
-    if par.numel() and bool((par >= torch.arange(par.shape[1], device=par.device)).any()):
-        raise ValueError("tree nodes must be ordered so that parent < child")
     o, st = tree_gdn_batched(query[None], key[None], value[None], g[None], beta[None], par,
                              initial_state[None], use_qk_l2norm=use_qk_l2norm)
     return o[0], st[0]
@@ -78,21 +78,21 @@ _DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 def ancestor_chains(parent: torch.Tensor, max_depth: int):
     """(chain [N, max_depth + 1] int32, depth [N] int32) from a parent array (parent < child,
-    -1 = root): chain[t, kk] is the ancestor kk levels above node t (chain[t, 0] = t), the layout
-    the in-engine verify walks from chain[t, depth[t]] (the root) down to t."""
-    p = parent.tolist()
-    N = len(p)
-    chain = torch.zeros(N, max_depth + 1, dtype=torch.int32)
-    depth = torch.zeros(N, dtype=torch.int32)
-    for t in range(N):
-        n, kk = t, 0
-        while True:
-            chain[t, kk] = n
-            if p[n] < 0:
-                break
-            n, kk = p[n], kk + 1
-        depth[t] = kk
-    return chain, depth
+    -1 = root) on the parent's device: chain[t, kk] is the ancestor kk levels above node t
+    (chain[t, 0] = t; entries past depth[t] repeat the top ancestor), the layout the in-engine
+    verify walks from chain[t, depth[t]] (the root) down to t. Pointer jumping with device ops
+    only: no host sync, so it can be captured in a CUDA graph."""
+    p = parent.to(torch.int64).view(-1)
+    N = p.numel()
+    cur = torch.arange(N, device=p.device)
+    cols, depth = [cur], torch.zeros(N, dtype=torch.int64, device=p.device)
+    for _ in range(max_depth):
+        up = p[cur] if N else cur
+        has = up >= 0
+        depth = depth + has.to(torch.int64)
+        cur = torch.where(has, up, cur)
+        cols.append(cur)
+    return torch.stack(cols, dim=1).to(torch.int32), depth.to(torch.int32)
 
 
 def gdn_verify(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, out_slot, init_slot, rows=None, *,
@@ -126,3 +126,32 @@ def gdn_verify(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, out_slot, 
         ints[1].data_ptr(), ints[2].data_ptr(), ints[3].data_ptr(),
         rows_i.data_ptr() if rows_i is not None else None, float(scale), T_rows, H, HV, K, V,
         int(write_out), int(write_state), _lib.stream_ptr()), "cfb_tree_gdn_verify")
+
+
+def gdn_factor(A_log, dt_bias, a, b, q, k, v, o, state, chain, depth, init_slot, row_start, row_count, *,
+               scale: float, n_max: int) -> None:
+    """The shared-root factorisation of the in-engine verify (reference fork ``gdn_factor``,
+    src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4664-5094) on cfb_tree_gdn_factor:
+    the outputs ``o`` of ``gdn_verify`` for requests whose rows [row_start[s], + row_count[s]) all
+    start from the state slot ``init_slot[row_start[s]]``, reading that state once per (request,
+    head) and writing no state. ``chain`` rows hold global row ids. Same dtypes as ``gdn_verify``;
+    n_max >= every row_count (<= 64)."""
+    lib = _lib.load()
+    for t_, n in ((q, "q"), (k, "k"), (v, "v"), (o, "o"), (state, "state"), (chain, "chain")):
+        _lib.require_cuda(t_, n)
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype or v.dtype != q.dtype or o.dtype != q.dtype:
+        raise _lib.CfbError("gdn_factor: q, k, v, o must share one dtype, fp16 or bf16")
+    if state.dtype != torch.float32 or state.stride(-1) != 1 or not state[0].is_contiguous():
+        raise _lib.CfbError("gdn_factor: state must be fp32 [slots, HV, V, K] with contiguous slots")
+    for t_ in (q, k, v, o, a, b, A_log, dt_bias):
+        if not t_.is_contiguous():
+            raise _lib.CfbError("gdn_factor: q, k, v, o, a, b, A_log, dt_bias must be contiguous")
+    ch, dp, isl, rs, rc = (t_.to(torch.int32).contiguous() for t_ in (chain, depth, init_slot, row_start, row_count))
+    H, K = q.shape[1], q.shape[2]
+    HV, V = v.shape[1], v.shape[2]
+    _lib.check(lib.cfb_tree_gdn_factor(
+        A_log.data_ptr(), _DTYPE_CODE[A_log.dtype], dt_bias.data_ptr(), _DTYPE_CODE[dt_bias.dtype],
+        a.data_ptr(), _DTYPE_CODE[a.dtype], b.data_ptr(), _DTYPE_CODE[b.dtype], q.data_ptr(), k.data_ptr(),
+        v.data_ptr(), o.data_ptr(), _DTYPE_CODE[q.dtype], state.data_ptr(), state.stride(0), ch.data_ptr(),
+        ch.stride(0), dp.data_ptr(), isl.data_ptr(), rs.data_ptr(), rc.data_ptr(), rs.numel(), int(n_max),
+        float(scale), H, HV, K, V, _lib.stream_ptr()), "cfb_tree_gdn_factor")

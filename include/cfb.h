@@ -286,6 +286,27 @@ cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, const void* d
                                const int32_t* rows, float scale, int T_rows, int H, int HV, int K,
                                int V, int write_out, int write_state, void* stream);
 
+/* The shared-root factorisation of the in-engine tree GDN verify (the contract of the reference
+ * fork's gdn_factor, src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4664-5094): the
+ * outputs o of cfb_tree_gdn_verify, for S requests whose rows [row_start[s], +row_count[s]) all
+ * start from the one state slot init_slot[row_start[s]], computed without reading or writing any
+ * per-node state: every update is rank 1, so a node's state is the root state decayed plus one
+ * rank-1 term per ancestor, and the root state is only used through H k and H q. The root state is
+ * read once per (request, head). chain rows hold GLOBAL row ids (chain[t, 0] = t, chain[t, j] the
+ * j-th ancestor, j <= depth[t]); a row whose chain leaves its request, or whose depth does not fit
+ * the chain row, gets NaN. Other arguments as cfb_tree_gdn_verify. Supported: K == 128, V a multiple
+ * of 32, row_count <= n_max <= 64, chain_stride <= 16. No state is written: the state that
+ * survives verification (the accepted leaf's) is materialised afterwards with
+ * cfb_tree_gdn_verify(write_out = 0, rows = the leaf). */
+cfb_status cfb_tree_gdn_factor(const void* A_log, int A_log_dtype, const void* dt_bias,
+                               int dt_bias_dtype, const void* a, int a_dtype, const void* b,
+                               int b_dtype, const void* q, const void* k, const void* v, void* o,
+                               int qkv_dtype, const float* state, int64_t slot_stride,
+                               const int32_t* chain, int chain_stride, const int32_t* depth,
+                               const int32_t* init_slot, const int32_t* row_start,
+                               const int32_t* row_count, int S, int n_max, float scale, int H,
+                               int HV, int K, int V, void* stream);
+
 /* cfb_tree_gdn without the states buffer, allocating nothing. This entry point has no
  * counterpart in the reference.
  * It is for callers that cannot allocate device memory when they verify: the verify step runs
@@ -305,6 +326,50 @@ cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const void* v, con
                                 const float* beta, const int32_t* parent, const float* init,
                                 float* o, int B, int N, int H, int Dk, int Dv, int use_l2norm,
                                 void* stream);
+
+/* ---- tree verification around the draft (the target model's side of a tree step) -------------
+ * The tree-attention fix-up of one full-attention layer (the contract of the reference fork's
+ * suffix_merge, src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:5516-5537, whose eager
+ * form is _tree_suffix_eager :529-575 + vLLM's merge_attn_states): for request s and tree node m
+ * (query row r = idx[s * N + m]) and query head h (key/value head h / (H / HKV)),
+ *   suffix = softmax_n(scale * q[r, h] . k[idx[s, n], kh]) v[idx[s, n], kh] over the ancestors n
+ *            of m (not_anc[(s * N + m) * N + n] == 0, m itself included), lse its log-sum-exp;
+ *   o[r, h] = prefix_out[s * N + m, h] * ps / (ps + ss) + fp(suffix) * ss / (ps + ss),
+ *            ps = exp(plse - M), ss = exp(lse - M), M = max(plse, lse), plse = prefix_lse[h, s*N + m]
+ *            (a +inf lse counts as -inf), fp() = rounding to the I/O dtype.
+ * q, k, v, o, prefix_out: fp16 (dtype 1) or bf16 (2) rows [*, heads, D] with the given strides in
+ * elements (rows 16-byte aligned); prefix_lse fp32 [H, S * N]; idx int64 [S, N]; not_anc uint8
+ * [S, N, N]. Only the tree rows of o are written. Supported: D in {64, 128, 256}, N <= 128,
+ * H a multiple of HKV. */
+cfb_status cfb_tree_attn_merge(const void* q, int64_t sq_t, int64_t sq_h, const void* k, int64_t sk_t,
+                               int64_t sk_h, const void* v, int64_t sv_t, int64_t sv_h, void* o,
+                               int64_t so_t, int64_t so_h, const void* prefix_out, int64_t spo_t,
+                               int64_t spo_h, const float* prefix_lse, const int64_t* idx,
+                               const uint8_t* not_anc, float scale, int S, int N, int H, int HKV,
+                               int D, int dtype, void* stream);
+
+/* Greedy tree verification (the contract of the reference fork's tree_rejection_sample and
+ * tree_greedy_descent_kernel, src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:640-723):
+ * the argmax of every logits row and the walk down each request's draft tree, in one launch.
+ * Request r owns n = cu_num_draft[r] - cu_num_draft[r - 1] draft nodes (flat draft_tokens /
+ * parents entries; parents are local node indices, -1 = the root) and logits rows [s0, s0 + n],
+ * s0 = cu_num_sampled[r] - (n + 1): row s0 scores the committed token, row s0 + 1 + i node i.
+ * From the root, the walk takes the row's argmax token (first maximum; NaN counts as the maximum,
+ * as torch.argmax) and moves to the first child (node order) whose draft token equals it.
+ * Outputs: output_tokens int32 [batch, max_spec_len + 1] = the accepted tokens then the bonus
+ * token, -1 after; accepted_path int32 [batch, max_spec_len] = the accepted node indices, -1 after;
+ * accepted_len int32 [batch]; row_argmax int32 [num_rows] (rows of the requests).
+ * logits [num_rows, V] with row stride ld elements: fp32 (dtype 0), fp16 (1) or bf16 (2).
+ * ws: cfb_tree_verify_workspace(num_rows, batch) bytes, 256-byte aligned, ZERO before its first
+ * use (each launch leaves it zeroed again). err (may be NULL): set non-zero when a request's
+ * offsets do not fit the logits rows or max_spec_len (that request then emits nothing). */
+size_t cfb_tree_verify_workspace(int num_rows, int batch);
+cfb_status cfb_tree_verify_greedy(const void* logits, int64_t ld, int num_rows, int V, int dtype,
+                                  const int32_t* cu_num_draft, const int32_t* cu_num_sampled,
+                                  const int32_t* draft_tokens, const int32_t* parents, int batch,
+                                  int max_spec_len, int32_t* output_tokens, int32_t* accepted_path,
+                                  int32_t* accepted_len, int32_t* row_argmax, void* ws,
+                                  size_t ws_bytes, int* err, void* stream);
 
 /* ---- the per-request context ring -------------------------------------------------------------
  * The window of the last C target hidden states each request's draft is conditioned on

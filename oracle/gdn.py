@@ -113,3 +113,58 @@ def tree_gdn_verify(A_log, dt_bias, a, b, q, k, v, state, chain, depth, out_slot
             if write_state:
                 st[int(out_slot[t]), hv] = S
     return o, st
+
+
+def tree_gdn_factor(A_log, dt_bias, a, b, q, k, v, state, chain, depth, init_slot, row_start, row_count, scale,
+                    threshold=20.0):
+    """The shared-root factorisation of the verify (reference fork ``gdn_factor``,
+    src/chain_flow/patches/vllm-0.25.1-chain-flow-tree.patch:4664-5094): every row of request s
+    starts from H = state[init_slot[row_start[s]], hv]; a node's state is
+    h_t = D_t H + sum_{m on its path} w_{m,t} u_m kn_m^T (every update is rank 1), so with
+    S_t = h_parent kn_t = D_p (H kn_t) + sum_{m on the parent's path} w_{m,p} (kn_m . kn_t) u_m,
+    u_t = beta_t (v_t - g_t S_t), D_t = g_t D_p, w_{m,t} = g_t w_{m,p}, w_{t,t} = 1, and
+    o_t = D_t (H qn_t) + sum_{m on t's path} w_{m,t} (kn_m . qn_t) u_m. Returns o [T, HV, V] fp32
+    (rows outside the requests stay zero). Equal to tree_gdn_verify's o up to rounding."""
+    q, k, v, a, b = (t.float() for t in (q, k, v, a, b))
+    A_log, dt_bias = A_log.float(), dt_bias.float()
+    T, H, K = q.shape
+    HV, V = v.shape[1], v.shape[2]
+    rep = HV // H
+    o = torch.zeros(T, HV, V)
+    kn = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    qn = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * scale
+    x = a + dt_bias[None, :]
+    sp = torch.where(x <= threshold, torch.log1p(torch.exp(x)), x)
+    g = torch.exp(-A_log.exp()[None, :] * sp)                          # [T, HV]
+    beta = torch.sigmoid(b)
+    for s in range(len(row_start)):
+        base, n = int(row_start[s]), int(row_count[s])
+        rows = range(base, base + n)
+        order = sorted(rows, key=lambda t: int(depth[t]))              # parents before children
+        for hv in range(HV):
+            h = hv // rep
+            Hs = state[int(init_slot[base]), hv].float()                # [V, K]
+            u, D, w = {}, {}, {}
+            for t in order:
+                d = int(depth[t])
+                path = [int(chain[t, j]) for j in range(d + 1)]         # t, parent, ..., top
+                if d > 0:
+                    p = path[1]
+                    S = D[p] * (Hs @ kn[t, h])
+                    for j, m in enumerate(path[1:]):                    # w_{m,p} = w[p][j]
+                        S = S + w[p][j] * (kn[m, h] @ kn[t, h]) * u[m]
+                    D[t] = D[p] * g[t, hv]
+                    w[t] = [1.0] + [w[p][j] * g[t, hv] for j in range(d)]
+                else:
+                    S = Hs @ kn[t, h]
+                    D[t] = g[t, hv]
+                    w[t] = [1.0]
+                u[t] = beta[t, hv] * (v[t, hv] - g[t, hv] * S)
+            for t in rows:
+                d = int(depth[t])
+                acc = D[t] * (Hs @ qn[t, h])
+                for j in range(d + 1):
+                    m = int(chain[t, j])
+                    acc = acc + w[t][j] * (kn[m, h] @ qn[t, h]) * u[m]
+                o[t, hv] = acc
+    return o

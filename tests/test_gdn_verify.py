@@ -79,3 +79,74 @@ def test_verify_kernel_matches_oracle(dtype, codes):
     torch.cuda.synchronize()
     assert torch.equal(st2.cpu(), c["state"])
     assert _rel(o2.cpu()[rows.long()], want_o[rows.long()]) < GDN_RTOL
+
+
+def _batched_case(seed, S=2, N=20, H=2, HV=4, V=64, K=128, max_depth=5):
+    """S requests of N rows each, request s's rows starting from state slot s (the shared root)."""
+    from chain_flow_b200.gdn import ancestor_chains, make_tree
+    g = torch.Generator().manual_seed(seed)
+    chains, depths = [], []
+    for s in range(S):
+        par, _ = make_tree(N, max_depth, 4, seed + s)
+        ch, dp = ancestor_chains(par, max_depth)
+        chains.append(ch + s * N); depths.append(dp)
+    T = S * N
+    return dict(
+        A_log=torch.randn(HV, generator=g) * 0.5, dt_bias=torch.randn(HV, generator=g) * 0.5,
+        a=torch.randn(T, HV, generator=g), b=torch.randn(T, HV, generator=g),
+        q=torch.randn(T, H, K, generator=g).half(), k=torch.randn(T, H, K, generator=g).half(),
+        v=torch.randn(T, HV, V, generator=g).half(), state=torch.randn(S, HV, V, K, generator=g) * 0.1,
+        chain=torch.cat(chains), depth=torch.cat(depths),
+        init_slot=torch.arange(S, dtype=torch.int32).repeat_interleave(N),
+        row_start=torch.arange(S, dtype=torch.int32) * N, row_count=torch.full((S,), N, dtype=torch.int32))
+
+
+def test_ancestor_chains_walk_to_the_root():
+    from chain_flow_b200.gdn import ancestor_chains, make_tree
+    par, dep = make_tree(30, 6, 3, seed=9)
+    chain, depth = ancestor_chains(par, 5)
+    assert torch.equal(depth.long(), dep)
+    for t in range(30):
+        n = t
+        for kk in range(int(depth[t]) + 1):
+            assert int(chain[t, kk]) == n
+            n = int(par[n])
+        assert n == -1
+
+
+def test_factor_oracle_equals_the_verify_oracle():
+    """The factorised algebra is a different expression of the same outputs: pinned to the
+    path-parallel verify oracle (itself pinned to the reference's tree_scan goldens)."""
+    c = _batched_case(11)
+    K = c["q"].shape[2]
+    want, _ = oracle.tree_gdn_verify(c["A_log"], c["dt_bias"], c["a"], c["b"], c["q"], c["k"], c["v"], c["state"],
+                                     c["chain"], c["depth"], torch.zeros_like(c["init_slot"]), c["init_slot"],
+                                     K ** -0.5, write_state=False)
+    got = oracle.tree_gdn_factor(c["A_log"], c["dt_bias"], c["a"], c["b"], c["q"], c["k"], c["v"], c["state"],
+                                 c["chain"], c["depth"], c["init_slot"], c["row_start"], c["row_count"], K ** -0.5)
+    assert _rel(got, want) < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_factor_kernel_matches_the_verify_oracle(dtype):
+    from chain_flow_b200.gdn import gdn_factor
+    c = _batched_case(13, S=3, N=41, H=4, HV=8, V=128)
+    K = c["q"].shape[2]
+    dev = "cuda"
+    q, k, v = (c[n].to(dtype) for n in ("q", "k", "v"))
+    want, _ = oracle.tree_gdn_verify(c["A_log"], c["dt_bias"], c["a"], c["b"], q, k, v, c["state"], c["chain"],
+                                     c["depth"], torch.zeros_like(c["init_slot"]), c["init_slot"], K ** -0.5,
+                                     write_state=False)
+    o = torch.zeros(q.shape[0], v.shape[1], v.shape[2], dtype=dtype, device=dev)
+    gdn_factor(c["A_log"].to(dev), c["dt_bias"].to(dev), c["a"].to(dev), c["b"].to(dev), q.to(dev), k.to(dev),
+               v.to(dev), o, c["state"].to(dev), c["chain"].to(dev), c["depth"].to(dev), c["init_slot"].to(dev),
+               c["row_start"].to(dev), c["row_count"].to(dev), scale=K ** -0.5, n_max=41)
+    torch.cuda.synchronize()
+    assert _rel(o.cpu(), want) < GDN_RTOL, _rel(o.cpu(), want)
+    # chains computed on the device (no host sync) give the same walk
+    from chain_flow_b200.gdn import ancestor_chains, make_tree
+    par, _ = make_tree(41, 5, 4, 13)
+    ch_d, dp_d = ancestor_chains(par.cuda(), 5)
+    ch_h, dp_h = ancestor_chains(par, 5)
+    assert torch.equal(ch_d.cpu(), ch_h) and torch.equal(dp_d.cpu(), dp_h)

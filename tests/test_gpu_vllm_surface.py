@@ -67,20 +67,19 @@ def window(hist, C=8):
 
 def run_steps(p, g, stash, tree=False):
     """Prefill (2 requests of 5 and 11 prompt tokens), a decode step with 3 and 1 accepted tokens,
-    then a step after the input batch swapped the two requests' rows (slot migration). Returns
-    the list of (out, expected) pairs."""
+    then a step after the input batch swapped the two requests' rows (slot migration). Yields
+    (out, expected context windows, committed tokens) right after each propose()."""
     H, dev = g["H"], "cuda"
     gen = torch.Generator(device=dev).manual_seed(5)
     hs = torch.randn(16, H, device=dev, generator=gen).half()
     hist = {"a": list(hs[0:5]), "b": list(hs[5:16])}
     stash.update(runner=runner_for(g, ["a", "b"], qsl=[0, 5, 16]), hidden_states=hs,
                  sample_hidden_states=hs[[4, 15]], spec_meta=None)
-    steps = []
     toks = [[11], [22]]
     out = p.propose(toks, None, None)
     k0 = torch.tensor([11, 22], device=dev)
     ctx = torch.stack([window(hist["a"]), window(hist["b"])])
-    steps.append((out, ctx, k0))
+    yield out, ctx, k0
     # decode: every request carried num_draft rows + 1; a accepted 3 tokens, b one
     nd = 5
     sh = torch.randn(2 * (nd + 1), H, device=dev, generator=gen).half()
@@ -89,7 +88,7 @@ def run_steps(p, g, stash, tree=False):
     hist["b"] += list(sh[6:7])
     toks = [[31, 32, 33], [44]]
     out = p.propose(toks, None, None)
-    steps.append((out, torch.stack([window(hist["a"]), window(hist["b"])]), torch.tensor([33, 44], device=dev)))
+    yield out, torch.stack([window(hist["a"]), window(hist["b"])]), torch.tensor([33, 44], device=dev)
     # the input batch swapped the requests' rows: each slot's history moves with its request
     sh = torch.randn(2 * (nd + 1), H, device=dev, generator=gen).half()
     stash.update(runner=runner_for(g, ["b", "a"]), sample_hidden_states=sh)
@@ -97,8 +96,7 @@ def run_steps(p, g, stash, tree=False):
     hist["a"] += list(sh[6:7])
     toks = [[51, 52], [61]]
     out = p.propose(toks, None, None)
-    steps.append((out, torch.stack([window(hist["b"]), window(hist["a"])]), torch.tensor([52, 61], device=dev)))
-    return steps
+    yield out, torch.stack([window(hist["b"]), window(hist["a"])]), torch.tensor([52, 61], device=dev)
 
 
 def test_chain_proposer_from_vllm_config(g64_dir, monkeypatch):
