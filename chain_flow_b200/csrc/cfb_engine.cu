@@ -38,6 +38,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <cstring>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <vector>
@@ -1041,7 +1042,10 @@ CFB_DEV void epi_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& 
 }
 
 // Weight producer (one thread): stream this CTA's packed weight units of every GEMM phase into
-// the ring with cp.async.bulk, running ahead of the consumers across phase boundaries.
+// the ring with cp.async.bulk, running ahead of the consumers across phase boundaries. (An L2
+// prefetch running further ahead than the ring was measured and not kept: with 8 to 32 units
+// per CTA ahead, DRAM reads grew by up to 1.75x, the prefetched lines being evicted before use,
+// and the 4B draft slowed from 5.35 to 5.8-6.8 ms.)
 CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
   uint32_t pi = 0;
   int stage = 0;

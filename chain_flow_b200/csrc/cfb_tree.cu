@@ -281,6 +281,7 @@ namespace {
 
 constexpr int kVerifyThreads = 256;
 constexpr int kVerifyChunks = 8;           // CTAs per logits row
+constexpr int kVerifyMaxNodes = 1024;      // draft nodes per request (max_spec_len)
 
 // torch.argmax order: larger value first, NaN above everything, ties to the lower index
 __device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
@@ -381,41 +382,55 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_verify_greedy_kernel(cons
     if (s_last) { __threadfence(); A.counter[r] = 0u; }
   }
   __syncthreads();
-  if (!s_last || threadIdx.x != 0) return;
+  if (!s_last) return;
+  // the request's last arriver: the whole CTA reduces the rows' chunks (a thread per row, chunks
+  // in column order), stages the request's parents and draft tokens, then one warp walks the tree
   __threadfence();
+  __shared__ int s_am[kVerifyMaxNodes + 1], s_par[kVerifyMaxNodes], s_tok[kVerifyMaxNodes];
   int32_t* ot = A.out_tokens + (long long)r * (A.max_spec + 1);
   int32_t* op = A.out_path + (long long)r * A.max_spec;
-  for (int p = 0; p <= A.max_spec; ++p) ot[p] = -1;
-  for (int p = 0; p < A.max_spec; ++p) op[p] = -1;
+  for (int p = threadIdx.x; p <= A.max_spec; p += kVerifyThreads) ot[p] = -1;
+  for (int p = threadIdx.x; p < A.max_spec; p += kVerifyThreads) op[p] = -1;
   if (!sane) {                            // inconsistent offsets: emit nothing, flag it
-    A.out_len[r] = 0;
-    if (A.err) atomicCAS(A.err, 0, cfb::DEV_BAD_INDEX);
+    if (threadIdx.x == 0) {
+      A.out_len[r] = 0;
+      if (A.err) atomicCAS(A.err, 0, cfb::DEV_BAD_INDEX);
+    }
     return;
   }
-  for (int jj = 0; jj <= n; ++jj) {
+  for (int jj = threadIdx.x; jj <= n; jj += kVerifyThreads) {
     const long long row = s0 + jj;
     float bv = __ldcg(A.part_v + row * kVerifyChunks);
     int bi = __ldcg(A.part_i + row * kVerifyChunks);
+#pragma unroll
     for (int c = 1; c < kVerifyChunks; ++c) {
       const float v = __ldcg(A.part_v + row * kVerifyChunks + c);
       const int i = __ldcg(A.part_i + row * kVerifyChunks + c);
       if (argmax_better(v, i, bv, bi)) { bv = v; bi = i; }
     }
     A.row_argmax[row] = bi;
+    s_am[jj] = bi;
   }
+  for (int i = threadIdx.x; i < n; i += kVerifyThreads) { s_par[i] = A.parents[d0 + i]; s_tok[i] = A.draft_tokens[d0 + i]; }
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
   int cur = -1, pos = 0;
   for (;;) {
-    const int tok = A.row_argmax[s0 + cur + 1];
-    ot[pos] = tok;
-    int nxt = -1;
-    for (int i = 0; i < n && nxt < 0; ++i)
-      if (A.parents[d0 + i] == cur && A.draft_tokens[d0 + i] == tok) nxt = i;
+    const int tok = s_am[cur + 1];
+    if (lane == 0) ot[pos] = tok;
+    int nxt = -1;                         // the first child of cur carrying tok (node order)
+    for (int i0 = 0; i0 < n && nxt < 0; i0 += 32) {
+      const int i = i0 + lane;
+      const unsigned hit = __ballot_sync(0xffffffffu, i < n && s_par[i] == cur && s_tok[i] == tok);
+      if (hit) nxt = i0 + __ffs(hit) - 1;
+    }
     if (nxt < 0 || pos >= A.max_spec) break;
-    op[pos] = nxt;
+    if (lane == 0) op[pos] = nxt;
     cur = nxt;
     ++pos;
   }
-  A.out_len[r] = pos;
+  if (lane == 0) A.out_len[r] = pos;
 }
 
 }  // namespace
@@ -436,6 +451,7 @@ extern "C" cfb_status cfb_tree_verify_greedy(const void* logits, int64_t ld, int
       !row_argmax || !ws)
     return CFB_ERR_INVALID_ARG;
   if (num_rows <= 0 || V <= 0 || batch <= 0 || max_spec_len < 0 || ld < V) return CFB_ERR_INVALID_ARG;
+  if (max_spec_len > kVerifyMaxNodes) return CFB_ERR_UNSUPPORTED;
   if (max_spec_len > 0 && (!draft_tokens || !parents)) return CFB_ERR_INVALID_ARG;
   if (dtype < 0 || dtype > 2) return CFB_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(ws) & 255) || ws_bytes < cfb_tree_verify_workspace(num_rows, batch))

@@ -362,7 +362,8 @@ cfb_status cfb_tree_attn_merge(const void* q, int64_t sq_t, int64_t sq_h, const 
  * logits [num_rows, V] with row stride ld elements: fp32 (dtype 0), fp16 (1) or bf16 (2).
  * ws: cfb_tree_verify_workspace(num_rows, batch) bytes, 256-byte aligned, ZERO before its first
  * use (each launch leaves it zeroed again). err (may be NULL): set non-zero when a request's
- * offsets do not fit the logits rows or max_spec_len (that request then emits nothing). */
+ * offsets do not fit the logits rows or max_spec_len (that request then emits nothing).
+ * Supported: max_spec_len <= 1024. */
 size_t cfb_tree_verify_workspace(int num_rows, int batch);
 cfb_status cfb_tree_verify_greedy(const void* logits, int64_t ld, int num_rows, int V, int dtype,
                                   const int32_t* cu_num_draft, const int32_t* cu_num_sampled,

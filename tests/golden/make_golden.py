@@ -168,7 +168,8 @@ def run_config(ref_src: str, name: str, c: dict) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC"), required="CF_REFERENCE_SRC" not in os.environ,
+                    help="the reference checkout's src/ directory (or set CF_REFERENCE_SRC)")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     for name, c in CONFIGS.items():

@@ -28,7 +28,8 @@ R, C, H, KMAX, STEPS = 6, 8, 16, 6, 7
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC"), required="CF_REFERENCE_SRC" not in os.environ,
+                    help="the reference checkout's src/ directory (or set CF_REFERENCE_SRC)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from chain_flow.vllm_plugin.flow_proposer import FlowDrafterProposer

@@ -30,7 +30,8 @@ TWOPASS_M = {"g64": (64, 128), "g128": (64, 256)}
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC"), required="CF_REFERENCE_SRC" not in os.environ,
+                    help="the reference checkout's src/ directory (or set CF_REFERENCE_SRC)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from chain_flow.vllm_plugin.flow_proposer import FlowDrafterProposer

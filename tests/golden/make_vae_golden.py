@@ -33,7 +33,8 @@ C = dict(H=128, latent=64, inter=128, vae_layers=2, vae_heads=4, heads=4, FM=2, 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC", "/root/reference/src"))
+    ap.add_argument("--ref", default=os.environ.get("CF_REFERENCE_SRC"), required="CF_REFERENCE_SRC" not in os.environ,
+                    help="the reference checkout's src/ directory (or set CF_REFERENCE_SRC)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     from chain_flow.drafters.tree_vae_flow import TreeVAEFlowConfig, TreeVAEFlowDrafter
