@@ -305,14 +305,26 @@ __device__ __forceinline__ void argmax_span(const T* row, int c0, int c1, float&
   }
   const int nvec = (c1 - a) / E;
   const uint4* vp = reinterpret_cast<const uint4*>(row + a);
-  for (int j = threadIdx.x; j < nvec; j += kVerifyThreads) {
-    const uint4 u = __ldcs(vp + j);
-    const T* t = reinterpret_cast<const T*>(&u);
+  // kInFlight vectors per thread are loaded before any is compared, so the loads overlap
+  constexpr int kInFlight = 4;
+  for (int j0 = threadIdx.x; j0 < nvec; j0 += kInFlight * kVerifyThreads) {
+    uint4 u[kInFlight];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float v = (float)t[e];
-      const int c = a + j * E + e;
-      if (argmax_better(v, c, bv, bi)) { bv = v; bi = c; }
+    for (int q = 0; q < kInFlight; ++q) {
+      const int j = j0 + q * kVerifyThreads;
+      if (j < nvec) u[q] = __ldcs(vp + j);
+    }
+#pragma unroll
+    for (int q = 0; q < kInFlight; ++q) {
+      const int j = j0 + q * kVerifyThreads;
+      if (j >= nvec) break;
+      const T* t = reinterpret_cast<const T*>(&u[q]);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float v = (float)t[e];
+        const int c = a + j * E + e;
+        if (argmax_better(v, c, bv, bi)) { bv = v; bi = c; }
+      }
     }
   }
   for (int c = a + nvec * E + (int)threadIdx.x; c < c1; c += kVerifyThreads) {
