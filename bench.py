@@ -43,7 +43,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1, help="requests per GPU")
-    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "gdn", "gdn-verify", "ring",
+    ap.add_argument("--workload", default="4b", choices=["4b", "27b", "cpu", "4b-ncu", "4b-prod", "27b-prod", "gdn", "gdn-verify", "ring",
                                                          "tree-attn", "tree-verify", "4b-head"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
@@ -334,6 +334,30 @@ def run_ours(args, wl):
     torch.cuda.synchronize(dev)
     kernel_ms = max_over_ranks(k0.elapsed_time(k1) / args.steps)
 
+    # ---- a production draft's latent flow alone: the work of the reference's fused-kernel
+    # integrate() (all Euler steps of both chunk experts over the 8-block stack at the latent
+    # width, one persistent-engine launch here), back-to-back launches on resident inputs
+    flow = None
+    flow_plan = getattr(plan, "flow", None)
+    if wl.latent and flow_plan is not None:
+        for _ in range(3):
+            flow_plan.run()
+        torch.cuda.synchronize(dev)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            flow_plan.run()
+        f1.record(stream)
+        torch.cuda.synchronize(dev)
+        flow_plan.check()
+        fbytes = wl.flow_weight_bytes()
+        f_ms = max_over_ranks(f0.elapsed_time(f1) / args.steps)
+        flow = {"ms": f_ms, "latent": wl.latent, "blocks": wl.layers, "euler_steps": wl.steps,
+                "bytes_per_launch": fbytes, "achieved_gbs": fbytes / (f_ms / 1e3) / 1e9,
+                # the reference kernel's published integrate() at B = 1 (RTX PRO 6000, compiled and
+                # graph-replayed; reference docs/BENCHMARKING.md:141-146)
+                "reference_integrate_ms": {640: 0.803, 1024: 1.364}.get(wl.latent)}
+
     # ---- end to end through the proposer API with host buffers
     h_ctx = ctx.cpu().pin_memory()
     h_k0 = known0.cpu().pin_memory()
@@ -463,6 +487,7 @@ def run_ours(args, wl):
                           "tflops": flops / (kernel_ms / 1e3) / 1e12}),
             "clocks": clk,
             "shortlist_head": head,
+            **({"flow_integrate": flow} if flow else {}),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

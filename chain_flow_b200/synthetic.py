@@ -95,6 +95,12 @@ class Workload:
         enc, dec = self.vae_macs_per_row()
         return int(2 * (crosskv + T * per_step + head + enc + dec))
 
+    def flow_weight_bytes(self) -> int:
+        """Packed fp16 weight bytes of the flow alone (cross K/V once, then every block of every
+        chunk expert plus its out_proj per Euler step): what one MODE_FLOW launch streams."""
+        Df, L, T, FM, E = self.flow_width, self.layers, self.steps, self.ffn, self.n_experts
+        return int(2 * (E * L * 2 * Df * Df + T * (E * L * (6 + 2 * FM) * Df * Df + E * Df * Df)))
+
     def flops_per_draft(self, batch: int) -> int:
         """Multiply-add FLOPs (2 per MAC) of the Linear layers of one draft of `batch` requests:
         every Euler step runs each block of chunk expert e over batch x chunk (e+1) rows and
@@ -133,6 +139,12 @@ WORKLOADS = {
     # draft_length 8 in chunks of 4, path order 8
     "4b-prod": Workload("4B-production-vae", hidden=2560, layers=8, steps=2, draft_length=8, chunk=4,
                         path_order=8, latent=640),
+    # the 27B production shape: the same drafter layout with the flow in a 1024-wide latent space
+    # (the reference's fused-kernel D = 1024 instantiation, shared by its 9B and 27B drafters). The
+    # VAE intermediate width keeps the 4B drafter's 3 x latent ratio; the published D = 1024
+    # integrate() figure covers the flow alone, which does not depend on it.
+    "27b-prod": Workload("27B-production-vae", hidden=5120, layers=8, steps=2, draft_length=8, chunk=4,
+                         path_order=8, latent=1024, vae_inter=3072),
 }
 
 

@@ -7,7 +7,8 @@ exactly as bench.py builds them:
 * cfg 2, the 4B shape (D = 2560, FFN x6, 4 blocks, 8 Euler steps, R = 62,642 of 248,320): B = 1
   and B = 8 on the persistent engine, B = 32 on the wide (tcgen05) plan;
 * cfg 3, the 27B shape (D = 5120): B = 1;
-* the shipped 4B production drafter (VAE 2560 -> 640, 8 blocks, 2 steps, draft length 8): B = 1.
+* the shipped 4B production drafter (VAE 2560 -> 640, 8 blocks, 2 steps, draft length 8): B = 1;
+* the 27B production shape (VAE 5120 -> 1024, the same flow layout at 1024 wide): B = 1.
 
 Checks, with the tolerances of BASELINE's north_star:
 
@@ -183,6 +184,10 @@ def test_cfg5_4b_b32_wide_draft(cfg2):
 
 def test_4b_production_vae_b1_draft():
     Bench("4b-prod").check_draft(1, "4B production (VAE) b=1")
+
+
+def test_27b_production_vae_b1_draft():
+    Bench("27b-prod").check_draft(1, "27B production (VAE, flow at 1024) b=1")
 
 
 def test_cfg3_27b_b1_draft():
