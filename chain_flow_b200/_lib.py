@@ -33,7 +33,7 @@ EXPORTED = [
     "cfb_vae_plan_workspace", "cfb_vae_plan_build", "cfb_tree_attn_merge", "cfb_tree_verify_workspace",
     "cfb_tree_verify_greedy", "cfb_tree_gdn_factor",
 ]
-ABI_VERSION = 4
+ABI_VERSION = 5
 XROWS, XFLOATS = 64, 18          # CFB_XROWS, CFB_XFLOATS: the merged-list exchange rows
 BUF_PATH_H16, BUF_PATH_MID, BUF_HEAD_IN, BUF_LASTP, BUF_CUM, BUF_QKV0, BUF_X32_0, BUF_KVC0, BUF_PROF, BUF_PHASES, \
     BUF_TP_CAND, BUF_TP_CHEAD = range(12)

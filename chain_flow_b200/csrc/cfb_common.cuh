@@ -106,6 +106,28 @@ CFB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, const int* err = nullptr,
   }
 }
 
+// The same bounded wait (default budget) on a barrier given by its shared-memory address, for
+// loops that keep their barrier addresses in registers.
+CFB_DEV bool mbar_try_wait_a(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.b32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+CFB_DEV bool mbar_wait_a(uint32_t bar, uint32_t parity, const int* err) {
+  if (mbar_try_wait_a(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (unsigned it = 1;; ++it) {
+    if (mbar_try_wait_a(bar, parity)) return true;
+    if (it % kPollsPerCheck == 0) {
+      if (wait_expired(t0, kWaitBudgetNs)) return false;
+      if (err && ld_volatile_int(err) != 0) return false;
+    }
+  }
+}
+
 // ---- bulk copy global -> shared (the TMA unit, 1-D form; no multicast) -------------------
 CFB_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -162,6 +184,76 @@ CFB_DEV int ld_volatile_int(const int* p) {
   int v;
   asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// ---- 5th-generation tensor cores (tcgen05) and tensor memory ---------------------------------
+CFB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+CFB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// whole warp; writes the allocated TMEM address to *slot
+CFB_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_u32(slot)), "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+CFB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[smem] · B[smem]ᵀ, kind::f16 (fp16 × fp16 -> fp32)
+CFB_DEV void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on `bar` once every tcgen05 op this thread issued before has completed
+CFB_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_u32(bar)) : "memory");
+}
+// Warp forms: the whole warp executes these converged, with warp-uniform operands, and one
+// elected lane issues. Kept converged, the operands stay in the uniform datapath: measured on
+// B200, a warp issues an M = 64 MMA in about 44 cycles this way against about 80 for one lane
+// running the same loop alone.
+CFB_DEV void tc_mma_f16_warp(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %4, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}"
+      :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+CFB_DEV void tc_commit_warp_a(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+      :: "r"(bar) : "memory");
+}
+CFB_DEV void tc_commit_warp(uint64_t* bar) { tc_commit_warp_a(smem_u32(bar)); }
+// 32 lanes × 16 consecutive fp32 columns of TMEM (lane = row of the accumulator)
+CFB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the 128-byte swizzle:
+// 128-byte rows, 8-row groups 1024 bytes apart (SBO), leading offset unused (1), version 1,
+// layout SWIZZLE_128B (2). The tile base must be 1024-byte aligned; stepping K by 16 elements
+// inside the 64-element swizzle row adds 32 bytes to the start address.
+CFB_DEV uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor of kind::f16 with an fp32 accumulator, fp16 A and B, both K-major
+// (bit 4: D format f32; bits 17-22: N / 8; bits 24-28: M / 16).
+CFB_DEV constexpr uint32_t tc_idesc(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 CFB_DEV float gelu_erf(float x) {   // nn.GELU() default (exact erf form)

@@ -51,11 +51,12 @@
 
 namespace cfb {
 
-// ---- thread layout: [0,8) MMA warps, 8 weight producer, 9 activation producer, [10,14) epilogue.
-// 448 threads leave ~144 registers per thread, so accumulators never spill.
+// ---- thread layout: [0,8) worker warps (in GEMM phases warp 0 issues the tensor-core MMAs; all
+// 8 take part in the other phases' work), 8 weight producer, 9 activation producer, [10,14)
+// epilogue.
 constexpr int kMmaWarps = 8;
+constexpr int kMmaIssueWarp = 0;
 constexpr int kMma = kMmaWarps * 32;                // 256
-constexpr int kKSlices = kMmaWarps / 4;             // k slices of a unit (4 m16 tiles per unit)
 constexpr int kWProdWarp = 8, kXProdWarp = 9, kEpiWarp0 = 10;
 constexpr int kEpiWarps = 4;
 constexpr int kEpi = kEpiWarps * 32;                // 128
@@ -63,10 +64,12 @@ constexpr int kThreads = (kMmaWarps + 2 + kEpiWarps) * 32;   // 448
 constexpr int kWorkers = kMma + kEpi;               // threads that take part in phase-level work
 constexpr int kBarWorkers = 1, kBarEpi = 2;         // named barriers (0 is __syncthreads)
 
-constexpr int kTileRows = 64;                       // output features per tile (4 x m16)
+constexpr int kTileRows = 64;                       // output features per tile (the MMA's M)
 constexpr int kUnitK = 8;                           // 16-wide k blocks per streamed unit
-constexpr int kBlockBytes = 512;                    // one 16x16 fp16 fragment tile
-constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB
+constexpr int kBlockBytes = 512;                    // 64 features x 16 k x fp16 of packed weights
+constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB: two 8 KiB [64 x 64] halves
+constexpr int kHalfBytes = kUnitBytes / 2;
+constexpr int kAccCols = 64;                        // TMEM columns of one accumulator (N <= 64 rows)
 constexpr int kMaxStages = 12;
 constexpr int kXRowBytes = 256;                     // activation row of a unit: 128 fp16
 constexpr int kSmemBudget = 232448 - 1024 - 2048;   // dynamic + static shared memory per CTA
@@ -84,12 +87,13 @@ constexpr int kJobCache = 4, kDescBufs = 3, kPhaseSlot = 64;                    
 
 enum XKind : int { XK_F16 = 0 };
 
-// fp16 activations the engine produces for its own GEMMs are stored unit-tiled: each 128-column
-// slice of all R rows is contiguous (one bulk copy per streamed unit), and within a row the
-// 16-byte chunks are XOR-swizzled by the row index so tensor-core fragment reads from shared
-// memory hit 32 distinct banks. Element (r, k) of an R-row buffer:
+// fp16 activations the engine produces for its own GEMMs are stored tiled: each 64-column slice
+// of all R rows is contiguous, one 128-byte row per activation row, its 16-byte chunks XOR-
+// swizzled by (row & 7). A slice copied to a 1024-byte-aligned shared-memory address is then the
+// K-major, 128-byte-swizzled B operand of tcgen05.mma as it stands; a streamed unit (128 k) takes
+// two bulk copies. Element (r, k) of an R-row buffer:
 CFB_DEV size_t tidx(int R, int r, int k) {
-  return ((size_t)(k >> 7) * R + r) * 128 + (size_t)((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7);
+  return ((size_t)(k >> 6) * R + r) * 64 + (size_t)((((k & 63) >> 3) ^ (r & 7)) << 3) + (k & 7);
 }
 enum LnKind : int { LN_NONE = 0, LN_PARTS = 1, LN_DIRECT = 2 };
 enum EKind : int { EK_STORE = 0, EK_GELU16 = 1, EK_RESID = 2, EK_EULER = 3, EK_PATHH = 4,
@@ -170,11 +174,12 @@ constexpr int kAttnCache = (int)(kJobCache * sizeof(Job) / sizeof(AttnTask));
 #define CFB_FIXUP_UNITS 12
 #endif
 
-// Dynamic shared memory, laid out per plan by the host: the ring of streamed units (each stage =
-// 16 KiB of packed weights + the unit's activation rows), mbarriers, the accumulator hand-off
-// slots, the epilogue's scratch (attention / merge ids), one reduced tile, row statistics.
+// Dynamic shared memory, laid out per plan by the host from a 1024-byte-aligned base: the ring of
+// streamed units (each stage = 16 KiB of packed weights + the unit's activation rows as two
+// [xhalf / 128 rows][128 B] halves), mbarriers, a staging tile for accumulators whose rows are
+// gathered, the epilogue's scratch (attention / merge ids), one reduced tile, row statistics.
 struct SmemLayout {
-  int nstages, stage_bytes, rows_pad, nbuf;
+  int nstages, stage_bytes, rows_pad, nbuf, xhalf;
   int off_bar, off_slots, off_scratch, off_red, off_rowstat, off_tile, off_misc, off_desc, total;
 };
 
@@ -216,10 +221,12 @@ struct Plan {
 };
 
 struct Smem {
-  uint8_t* ring; int nstages, stage_bytes, rp, nbuf;
+  uint8_t* ring; int nstages, stage_bytes, rp, nbuf, xhalf;
   uint64_t* full; uint64_t* empty;         // per ring stage
-  uint64_t* accf; uint64_t* acce;          // per accumulator slot buffer
-  float* slots;                            // [nbuf][MMA warps][16][rp]
+  uint64_t* accf; uint64_t* acce;          // per TMEM accumulator buffer
+  uint64_t* fin;                           // the MMA warp's last commit (before TMEM is freed)
+  uint32_t tmem;                           // TMEM base: nbuf accumulators of kAccCols columns
+  float* slots;                            // [kTileRows][kAccCols + 1]: accumulator staging
   float* scratch;                          // attention / merge ids (epilogue only)
   float* red;                              // [kTileRows][rp]
   float2* rowstat;
@@ -235,7 +242,6 @@ struct Smem {
     return reinterpret_cast<const Job*>(desc + (size_t)(p % kDescBufs) * (kPhaseSlot + kJobCache * sizeof(Job)) + kPhaseSlot);
   }
   __device__ uint8_t* stage(int s) const { return ring + (size_t)s * stage_bytes; }
-  __device__ float* slot(int b) const { return slots + (size_t)b * kMmaWarps * 16 * rp; }
 };
 
 // A cooperating thread group: index in group, size, named barrier.
@@ -750,8 +756,8 @@ CFB_DEV void epi_prefetch(const Plan& P, const Job& J, int tile, const Grp& E) {
 constexpr int kFixBatch = 3;   // contributors whose partials one fixup step loads at once
 template <class WaitClock>
 CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
-                      long long ug_first, uint32_t& tseq, Smem& S, HeadState& H, const Grp& E,
-                      WaitClock& wc) {
+                      long long ug_first, uint32_t& tseq, Smem& S,
+                      HeadState& H, const Grp& E, WaitClock& wc) {
   const int rows = J.rows;
   const int b = tseq % S.nbuf;
   epi_prefetch(P, J, tile, E);
@@ -769,18 +775,39 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
   const unsigned long long w0 = wc.now();
   if (!mbar_wait(&S.accf[b], (tseq / S.nbuf) & 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
   if (wc.on) { wc.part = wc.now(); wc.slot += wc.part - w0; wc.atom = wc.fix = 0; }
-  const float* sl = S.slot(b);
-  // feature f = 16 i + ff comes from MMA warps i, i+4, ... (one per k slice), summed in order
-  for (int e = E.t; e < kTileRows * rows; e += E.n) {
-    const int f = e / rows, r = e - f * rows;
-    const int i = f >> 4, ff = f & 15;
-    float s = 0.f;
+  tc_fence_after();
+  // The accumulator of an M = 64 MMA: feature f sits in TMEM lane 32 (f / 16) + f % 16, the
+  // value for slot row c in column c. Each epilogue warp reads its lane quarter (warp % 4), 16
+  // columns at a time; output row r is slot row src_row(r) (the identity but for gathered rows).
+  const bool ident = J.goff == 0 && (J.gin >= rows || J.gstride == J.gin);
+  {
+    const int q = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+    const int f = 16 * q + (lane & 15);
+    const int ncol = ident ? rows : (J.xcopy + 7) & ~7;
+    const uint32_t ta = S.tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kAccCols);
+    for (int c0 = 0; c0 < ncol; c0 += 16) {
+      float v[16];
+      tmem_ld16(ta + (uint32_t)c0, v);
+      if (lane < 16) {
 #pragma unroll
-    for (int w = 0; w < kKSlices; ++w) s += sl[((i + 4 * w) * 16 + ff) * S.rp + r];
-    S.red[f * S.rp + r] = s;
+        for (int i = 0; i < 16; ++i) {
+          if (c0 + i >= ncol) break;
+          if (ident) S.red[f * S.rp + c0 + i] = v[i];
+          else S.slots[f * (kAccCols + 1) + c0 + i] = v[i];
+        }
+      }
+    }
   }
+  tc_fence_before();
   gsync(E);
   if (E.t == 0) mbar_arrive(&S.acce[b]);
+  if (!ident) {
+    for (int e = E.t; e < kTileRows * rows; e += E.n) {
+      const int f = e / rows, r = e - f * rows;
+      S.red[f * S.rp + r] = S.slots[f * (kAccCols + 1) + src_row(J, r)];
+    }
+    gsync(E);
+  }
   ++tseq;
   if (!complete) {
     // A tile split across CTAs (stream-K). Its owner is the CTA whose range holds the tile's
@@ -898,127 +925,89 @@ CFB_DEV bool job_slice(const Job& J, const UnitRange& cu, int& ju0, int& ju1) {
   return true;
 }
 
-// MMA warps: multiply the job's units; hand each finished tile's partials to a slot buffer.
-// Everything the per-unit loop needs is held in registers (job fields, ring stage and parity,
-// tile / k-chunk position): the mbarrier operations are compiler memory barriers, so anything
-// read through the Job reference would otherwise be reloaded on every unit.
-// NSPLIT (jobs of 49-64 rows): instead of splitting a unit's k blocks between the two warps of an
-// m16 tile, each of them takes all k blocks for half of the n-tiles (NT each), which halves the
-// accumulators a thread holds; it writes zeros for the other half's rows so that the
-// epilogue's fixed two-slice sum is unchanged.
-template <int NT, bool NSPLIT, class WaitClock>
-CFB_DEV void mma_job(const Plan& P, const Job& J, int ju0, int ju1, uint32_t& ci, uint32_t& tseq, Smem& S,
-                     WaitClock& wc) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mi = warp & 3, ks = warp >> 2;     // this warp's m16 tile and k slice (or n half) of a unit
-  const int nb = NSPLIT ? ks * NT : 0;         // first n-tile of this warp
-  const int g = lane >> 2, t = lane & 3;
-  const int nkc = J.nkc, Kt = J.Kt, rows = J.rows, nst = S.nstages, rp = S.rp, nbuf = S.nbuf;
-  const int* err = P.err;
-  // shared-memory row of each n-tile's activation row: 256 B per row, 16-byte chunks swizzled
-  // by the row index
-  const int xrs = kXRowBytes, xsw = 7;
-  int xoff[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int r = (nb + nt) * 8 + g;
-    const int sr = r < rows ? src_row(J, r) : -1;
-    // byte offsets of the two 16-byte chunks of k-block 0; k-block blk adds 32*blk before the swizzle
-    xoff[nt][0] = sr < 0 ? -1 : sr * xrs + 4 * t;
-    xoff[nt][1] = sr < 0 ? 0 : (sr & xsw);
-  }
-  float acc[NT][4];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-  int stage = (int)(ci % (uint32_t)nst);
-  uint32_t par = (ci / (uint32_t)nst) & 1u;
-  int tile = ju0 / nkc, kc = ju0 - tile * nkc;
-  int slot = (int)(tseq % (uint32_t)nbuf);
-  uint32_t spar = (tseq / (uint32_t)nbuf) & 1u;
-  for (int ju = ju0; ju < ju1; ++ju) {
-    const int nkb = min(kUnitK, Kt - kc * kUnitK);
-    const unsigned long long w0 = wc.now();
-    if (!mbar_wait(&S.full[stage], par, err)) set_err(P, DEV_TIMEOUT_FULL);
-    if (wc.on) {
-      const unsigned long long w1 = wc.now();
-      wc.full += w1 - w0;
-      if (wc.first == 0) wc.first = w1;
-      wc.last = w1;
-    }
-    const uint8_t* st = S.ring + (size_t)stage * S.stage_bytes;
-    const uint8_t* xs = st + kUnitBytes;
-#pragma unroll
-    for (int i = 0; i < (NSPLIT ? kUnitK : kUnitK / kKSlices); ++i) {
-      const int blk = NSPLIT ? i : ks + kKSlices * i;
-      if (blk < nkb) {
-        const uint4 a = *reinterpret_cast<const uint4*>(st + (blk * 4 + mi) * kBlockBytes + lane * 16);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          uint32_t b0 = 0u, b1 = 0u;
-          if (xoff[nt][0] >= 0) {
-            const uint8_t* xr = xs + xoff[nt][0];
-            const int sw = xoff[nt][1];
-            b0 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk) ^ sw) << 4));
-            b1 = *reinterpret_cast<const uint32_t*>(xr + (((2 * blk + 1) ^ sw) << 4));
-          }
-          mma16816(acc[nt], a, b0, b1);
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&S.empty[stage]);
-    if (++stage == nst) { stage = 0; par ^= 1u; }
-    ++ci;
-    if (kc == nkc - 1 || ju == ju1 - 1) {
-      const unsigned long long w1 = wc.now();
-      if (!mbar_wait(&S.acce[slot], spar ^ 1u, err)) set_err(P, DEV_TIMEOUT_SLOT);
-      if (wc.on) wc.slot += wc.now() - w1;
-      float* sl = S.slots + ((size_t)slot * kMmaWarps + warp) * 16 * rp;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int r0 = (nb + nt) * 8 + 2 * t;
-        if (r0 < rp) {
-          sl[g * rp + r0] = acc[nt][0];
-          sl[g * rp + r0 + 1] = acc[nt][1];
-          sl[(g + 8) * rp + r0] = acc[nt][2];
-          sl[(g + 8) * rp + r0 + 1] = acc[nt][3];
-        }
-        if (NSPLIT) {
-          const int z0 = ((NT - nb) + nt) * 8 + 2 * t;     // the other half's rows
-          if (z0 < rp) {
-            sl[g * rp + z0] = 0.f; sl[g * rp + z0 + 1] = 0.f;
-            sl[(g + 8) * rp + z0] = 0.f; sl[(g + 8) * rp + z0 + 1] = 0.f;
-          }
-        }
-        acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.accf[slot]);
-      if (++slot == nbuf) { slot = 0; spar ^= 1u; }
-      ++tseq;
-    }
-    if (++kc == nkc) { kc = 0; ++tile; }
-  }
-  (void)tile;
-}
-
-// MAXNT: the widest job of the plan in 8-row n-tiles (1, 2, 4 or 8). Each engine_kernel
-// instantiation carries only the MMA loops its plans can need: wider variants cost registers
-// (spills) and instruction-cache room in every phase.
-template <int MAXNT, class WaitClock>
-CFB_DEV void mma_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& ci, uint32_t& tseq, Smem& S,
-                       WaitClock& wc) {
+// The MMA warp (kMmaIssueWarp; all 32 lanes walk this loop converged, so every operand below is
+// warp-uniform, and one elected lane issues): for each of this CTA's units, once its ring stage is
+// full, D[tmem] (+)= W_unit X_unit^T over the unit's k blocks with tcgen05.mma (M = 64 features,
+// N = the job's slot rows padded to 8, K = 16 per instruction, both operands K-major with the
+// 128-byte swizzle, straight from the ring stage), then tcgen05.commit returns the stage to the
+// producers once those MMAs have read it. The last unit of a tile (or of this CTA's share of it)
+// commits the accumulator to the epilogue; a tile's first MMA overwrites the accumulator, after
+// the epilogue has released that TMEM buffer. Nothing here holds accumulators in registers.
+template <class WaitClock>
+CFB_DEV void tc_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& ci, uint32_t& tseq, Smem& S,
+                      WaitClock& wc) {
   const UnitRange cu = cta_units(P, ph, jt);
+  const int* err = P.err;
+  // everything the unit loop touches is held in registers: the asm statements below clobber
+  // memory, so a field read through S or a Job reference would be reloaded at every MMA
+  const int nst = S.nstages, nbuf = S.nbuf;
+  const uint32_t ring = smem_u32(S.ring), sbytes = (uint32_t)S.stage_bytes, xhalf = (uint32_t)S.xhalf;
+  const uint32_t full0 = smem_u32(S.full), empty0 = smem_u32(S.empty);
+  const uint32_t accf0 = smem_u32(S.accf), acce0 = smem_u32(S.acce), tmem = S.tmem;
+  const bool prof = wc.on;
   for (int jx = 0; jx < ph.njobs; ++jx) {
     const Job& J = jt[jx];
     int ju0, ju1;
     if (!job_slice(J, cu, ju0, ju1)) continue;
-    const int nt = (J.rows + 7) / 8;
-    if (MAXNT <= 1 || nt <= 1) mma_job<1, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (MAXNT <= 2 || nt <= 2) mma_job<2, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (MAXNT <= 4 || nt <= 4) mma_job<4, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else if (nt <= 6) mma_job<6, false, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
-    else mma_job<4, true, WaitClock>(P, J, ju0, ju1, ci, tseq, S, wc);
+    const int nkc = J.nkc, Kt = J.Kt;
+    const uint32_t idesc = tc_idesc(kTileRows, (J.xcopy + 7) & ~7);
+    int stage = (int)(ci % (uint32_t)nst);
+    uint32_t par = (ci / (uint32_t)nst) & 1u;
+    int slot = (int)(tseq % (uint32_t)nbuf);
+    uint32_t spar = (tseq / (uint32_t)nbuf) & 1u;
+    int kc = ju0 % nkc;
+    int nkb_left = Kt - kc * kUnitK;   // k blocks of the tile from this unit on
+    bool fresh = true;                 // the next unit starts a tile (of this CTA's share)
+    for (int ju = ju0; ju < ju1; ++ju) {
+      const int nkb = min(kUnitK, nkb_left);
+      if (fresh) {
+        const unsigned long long w1 = prof ? globaltimer() : 0ull;
+        if (!mbar_wait_a(acce0 + 8u * (uint32_t)slot, spar ^ 1u, err)) set_err(P, DEV_TIMEOUT_SLOT);
+        if (prof) wc.slot += globaltimer() - w1;
+        __syncwarp();
+        tc_fence_after();   // the epilogue's reads of this accumulator come before the MMAs below
+      }
+      const unsigned long long w0 = prof ? globaltimer() : 0ull;
+      if (!mbar_wait_a(full0 + 8u * (uint32_t)stage, par, err)) set_err(P, DEV_TIMEOUT_FULL);
+      if (prof) {
+        const unsigned long long w1 = globaltimer();
+        wc.full += w1 - w0;
+        if (wc.first == 0) wc.first = w1;
+        wc.last = w1;
+      }
+      __syncwarp();
+      const uint32_t ws = ring + (uint32_t)stage * sbytes, xs = ws + kUnitBytes;
+      const uint32_t td = tmem + (uint32_t)(slot * kAccCols);
+      const uint64_t a0 = sw128_desc(ws), b0 = sw128_desc(xs);
+      const uint64_t a1 = sw128_desc(ws + kHalfBytes), b1 = sw128_desc(xs + xhalf);
+      // k block kb sits in half kb / 4 at byte offset 32 (kb % 4): +2 in the descriptor's
+      // 16-byte start-address field per k block
+      tc_mma_f16_warp(td, a0, b0, idesc, fresh ? 0u : 1u);
+      if (nkb == kUnitK) {             // a whole unit: no per-MMA test
+#pragma unroll
+        for (int kb = 1; kb < kUnitK; ++kb) {
+          const uint64_t o = (uint64_t)((kb & 3) * 2);
+          tc_mma_f16_warp(td, (kb < 4 ? a0 : a1) + o, (kb < 4 ? b0 : b1) + o, idesc, 1u);
+        }
+      } else {
+        for (int kb = 1; kb < nkb; ++kb) {
+          const uint64_t o = (uint64_t)((kb & 3) * 2);
+          tc_mma_f16_warp(td, (kb < 4 ? a0 : a1) + o, (kb < 4 ? b0 : b1) + o, idesc, 1u);
+        }
+      }
+      fresh = false;
+      tc_commit_warp_a(empty0 + 8u * (uint32_t)stage);
+      if (++stage == nst) { stage = 0; par ^= 1u; }
+      ++ci;
+      nkb_left -= kUnitK;
+      if (++kc == nkc || ju == ju1 - 1) {
+        tc_commit_warp_a(accf0 + 8u * (uint32_t)slot);
+        if (++slot == nbuf) { slot = 0; spar ^= 1u; }
+        ++tseq;
+        fresh = true;
+        if (kc == nkc) { kc = 0; nkb_left = Kt; }
+      }
+    }
   }
 }
 
@@ -1083,8 +1072,9 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
       int tile = ju0 / nkc, kc = ju0 - tile * nkc;
       for (int ju = ju0; ju < ju1; ++ju) {
         const int nkb = min(kUnitK, Kt - kc * kUnitK);
-        const uint8_t* src = wbase + (size_t)tile * tile_bytes + (size_t)kc * kUnitK * 4 * kBlockBytes;
-        const uint32_t bytes = (uint32_t)(nkb * 4 * kBlockBytes);
+        const uint8_t* src = wbase + (size_t)tile * tile_bytes + (size_t)kc * kUnitBytes;
+        // whole [64 x 64] halves: a unit of at most 64 k streams one
+        const uint32_t bytes = nkb > 4 ? (uint32_t)kUnitBytes : (uint32_t)kHalfBytes;
         const unsigned long long w0 = prof ? globaltimer() : 0ull;
         if (!mbar_wait(&S.empty[stage], par, err)) {
           set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
@@ -1108,14 +1098,16 @@ CFB_DEV void weight_producer(const Plan& P, Smem& S, int p0, int p1) {
 }
 
 // Activation producer (one thread): once the grid barrier in front of a phase has passed, copy
-// each unit's activation rows (its 128-column slice of the unit-tiled source: one contiguous
-// block) into the unit's ring slot with a 1-D bulk copy that completes on the slot's full
-// barrier (the same barrier the weight producer's copy completes on).
-CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint64_t* full) {
+// each unit's activation rows (its 128 columns: two 64-column slices of the tiled source, each
+// one contiguous block) into the unit's ring slot with 1-D bulk copies that complete on the
+// slot's full barrier (the same barrier the weight producer's copy completes on). A unit of at
+// most 64 k takes one slice.
+CFB_DEV void x_unit(const Job& J, int ju, uint8_t* xs, uint32_t xhalf, uint64_t* full) {
   const int kc = ju % J.nkc;
-  const uint32_t bytes = (uint32_t)J.xcopy * 256u;
-  mbar_arrive_expect_tx(full, bytes);
-  bulk_g2s(xs, J.x + (size_t)kc * J.xR * 128, bytes, full);
+  const int nh = J.Kt - kc * kUnitK > 4 ? 2 : 1;
+  const uint32_t bytes = (uint32_t)J.xcopy * 128u;
+  mbar_arrive_expect_tx(full, bytes * (uint32_t)nh);
+  for (int h = 0; h < nh; ++h) bulk_g2s(xs + (size_t)h * xhalf, J.x + (size_t)(2 * kc + h) * J.xR * 64, bytes, full);
 }
 
 // The descriptor cache slot of phase p (one thread): the phase record, then, for a GEMM phase of
@@ -1195,7 +1187,7 @@ CFB_DEV void x_producer(const Plan& P, Smem& S, int p0, int p1) {
         if (!mbar_wait(&S.empty[xstage], xpar, P.err)) {
           set_err(P, DEV_TIMEOUT_EMPTY); ok = false; break;
         }
-        x_unit(J, ju, S.ring + (size_t)xstage * S.stage_bytes + kUnitBytes, &S.full[xstage]);
+        x_unit(J, ju, S.ring + (size_t)xstage * S.stage_bytes + kUnitBytes, (uint32_t)S.xhalf, &S.full[xstage]);
         ++xi;
         if (++xstage == S.nstages) { xstage = 0; xpar ^= 1u; }
       }
@@ -1838,49 +1830,23 @@ __device__ __noinline__ void tpsel_phase(const Plan& P, Smem& S, const Grp& W, b
 // takes one 16-row group and a range of 16-column blocks: the two source rows of each lane are
 // looked up once, then 4 blocks' loads are in flight at a time.
 __device__ __noinline__ void tpgath_phase(const Plan& P, const Grp& W, const uint4* head) {
-  const int Kt = (P.D + P.rank) / 16;
-  const int nout = P.B * P.tp_m, Mt = (nout + 63) / 64 * 4;
-  constexpr int kKbChunk = 22, kU = 8;
-  const int nkc = (Kt + kKbChunk - 1) / kKbChunk;
-  const int lane = W.t & 31, g = lane >> 2, t = lane & 3;
-  const long long tasks = (long long)Mt * nkc;
-  const long long wg = (long long)blockIdx.x * (W.n >> 5) + (W.t >> 5), nwg = (long long)P.G * (W.n >> 5);
-  const uint32_t* hw = reinterpret_cast<const uint32_t*>(head);
-  for (long long task = wg; task < tasks; task += nwg) {
-    const int m = (int)(task / nkc), c = (int)(task - (long long)m * nkc);
-    size_t base[2];
-    int hs[2];
-    bool live[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = m * 16 + g + 8 * h;
-      live[h] = row < nout;
-      int s = live[h] ? __ldcg(P.tcd + row) : 0;
-      s = min(max(s, 0), P.R - 1);                       // (always in range; never read outside)
-      const int ms = s >> 4, rs = s & 15;
-      hs[h] = rs >> 3;
-      base[h] = ((size_t)(ms >> 2) * Kt * 4 + (ms & 3)) * 32 + (rs & 7) * 4 + t;   // uint4 index at kb = 0
+  // packed layout (cfb_pack_linear): 64-row tiles of [K/64][64 rows][8 swizzled 16-byte chunks]
+  const int Kh = (P.D + P.rank + 63) / 64;
+  const int nout = P.B * P.tp_m, npad = (nout + 63) / 64 * 64;
+  const size_t tile16 = (size_t)Kh * 512;                 // 16-byte words per 64-row tile
+  const long long tasks = (long long)npad * Kh * 8;
+  const long long gtid = (long long)blockIdx.x * W.n + W.t, gthreads = (long long)P.G * W.n;
+  for (long long i = gtid; i < tasks; i += gthreads) {
+    const int c = (int)(i & 7);
+    const long long rest = i >> 3;
+    const int h = (int)(rest % Kh), d = (int)(rest / Kh);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);                  // padding rows of the last tile: zeros
+    if (d < nout) {
+      int s = __ldcg(P.tcd + d);
+      s = min(max(s, 0), P.R - 1);                         // (always in range; never read outside)
+      v = __ldg(head + (size_t)(s >> 6) * tile16 + (size_t)h * 512 + (size_t)(s & 63) * 8 + (c ^ (s & 7)));
     }
-    const int kb0 = c * kKbChunk, kb1 = min(Kt, kb0 + kKbChunk);
-    for (int kb = kb0; kb < kb1; kb += kU) {
-      uint32_t w[kU][4];
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int k = kb + u;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int h = q & 1;
-          w[u][q] = (k < kb1 && live[h]) ? __ldg(hw + (base[h] + (size_t)k * 128) * 4 + hs[h] + (q & 2)) : 0u;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int k = kb + u;
-        if (k < kb1)
-          P.tchead[(((long long)(m >> 2) * Kt + k) * 4 + (m & 3)) * 32 + lane] =
-              make_uint4(w[u][0], w[u][1], w[u][2], w[u][3]);
-      }
-    }
+    P.tchead[(size_t)(d >> 6) * tile16 + (size_t)h * 512 + (size_t)(d & 63) * 8 + (c ^ (d & 7))] = v;
   }
 }
 
@@ -1906,14 +1872,19 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   constexpr bool kLean = MAXNT > 2;
   constexpr bool kProf = !kLean;                  // profiling code present in this instantiation
   using WaitClock = typename std::conditional<kProf, ProfClock, NoClock>::type;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_dyn[];
+  // the tensor cores' 128-byte-swizzled operands need 1024-byte-aligned stages (the host leaves
+  // 1024 bytes of slack for this)
+  uint8_t* const smem_raw = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
   const SmemLayout L = P.sm;
   Smem S;
   S.ring = smem_raw; S.nstages = L.nstages; S.stage_bytes = L.stage_bytes; S.rp = L.rows_pad; S.nbuf = L.nbuf;
+  S.xhalf = L.xhalf;
   S.full = reinterpret_cast<uint64_t*>(smem_raw + L.off_bar);
   S.empty = S.full + L.nstages;
   S.accf = S.empty + L.nstages;
   S.acce = S.accf + 2;
+  S.fin = S.acce + 2;
   S.slots = reinterpret_cast<float*>(smem_raw + L.off_slots);
   S.scratch = reinterpret_cast<float*>(smem_raw + L.off_scratch);
   S.red = reinterpret_cast<float*>(smem_raw + L.off_red);
@@ -1925,17 +1896,27 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   S.desc_ready = reinterpret_cast<volatile int*>(smem_raw + L.off_misc + 8);
   S.desc = smem_raw + L.off_desc;
   const int tid = threadIdx.x, warp = tid >> 5;
+  __shared__ uint32_t s_tmem;
+  // two accumulators (nbuf) of kAccCols columns
+  constexpr uint32_t tmem_cols = 2u * kAccCols;
+  static_assert(tmem_cols == 128u, "a power of two of at least 32 TMEM columns");
+  if (warp == 0) tmem_alloc(&s_tmem, tmem_cols);   // the accumulators (one CTA per SM: never contended)
   if (tid == 0) {
-    // full: the weight producer's expect_tx arrive + the activation producer's arrive
-    for (int i = 0; i < L.nstages; ++i) { mbar_init(&S.full[i], 2); mbar_init(&S.empty[i], kMmaWarps); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&S.accf[i], kMmaWarps); mbar_init(&S.acce[i], 1); }
+    // full: the weight producer's expect_tx arrive + the activation producer's arrive; empty,
+    // accf, fin: the MMA warp's tcgen05.commit; acce: the epilogue
+    for (int i = 0; i < L.nstages; ++i) { mbar_init(&S.full[i], 2); mbar_init(&S.empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&S.accf[i], 1); mbar_init(&S.acce[i], 1); }
+    mbar_init(S.fin, 1);
     *S.phase_ready = -1;
     *S.desc_ready = -1;
     // a plan whose earlier run failed stays failed: this run leaves every output untouched
     *S.flag = ld_volatile_int(P.err) != 0;
     fence_mbar_init();
   }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  S.tmem = s_tmem;
   const bool dead = *S.flag != 0;
   __syncthreads();
   if (warp == kWProdWarp) {
@@ -2007,7 +1988,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
           prow[19] = wc.rstat;
         }
       } else {
-        mma_phase<MAXNT, WaitClock>(P, ph, jt, ci, tseq, S, wc);
+        if (warp == kMmaIssueWarp) tc_phase<WaitClock>(P, ph, jt, ci, tseq, S, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
@@ -2020,6 +2001,16 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     __threadfence();
     const unsigned old = atomicAdd(P.exitcnt, 1u);
     if (old + 1 == (unsigned)P.G) { *P.bar = 0u; *P.exitcnt = 0u; __threadfence(); }
+  }
+  // every MMA this CTA issued has completed (the epilogue's TMEM reads are behind the last grid
+  // barrier) before its tensor memory is freed
+  static_assert(kMmaIssueWarp == 0, "the MMA warp also allocates and frees the tensor memory");
+  if (warp == 0) {
+    tc_commit_warp(S.fin);
+    if (tid == 0) mbar_wait(S.fin, 0);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(S.tmem, tmem_cols);
   }
 }
 
@@ -2092,7 +2083,7 @@ cfb::Job make_job(const cfb_linear& L, int rows) {
   J.w = static_cast<const uint4*>(L.w);
   J.Mt = (L.nout + cfb::kTileRows - 1) / cfb::kTileRows;
   J.Kt = L.k / 16;
-  J.Kstride = L.k / 16;
+  J.Kstride = (L.k + 63) / 64 * 4;       // the packed tile's k extent (whole 64-k halves), in 16-k blocks
   J.nkc = (J.Kt + cfb::kUnitK - 1) / cfb::kUnitK;
   J.rows = rows;
   J.nout = L.nout;
@@ -2287,7 +2278,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
     o_tcd = A.take(nc * 4);
     o_thist = A.take((size_t)4 * Bq * 256 * 4);
     o_tcnt = A.take((size_t)Bq * G * 2 * 4);
-    o_tchead = A.take((nc + 63) / 64 * 64 * (size_t)(D + rank) * 2);
+    o_tchead = A.take(cfb_packed_bytes(nc, D + rank));
   }
   const size_t o_gpart = A.take((size_t)G * cfb::kTileRows * cfb::kRowsMax * 4);
   const bool profile = (r.flags & CFB_RUN_PROFILE) != 0;
@@ -2584,10 +2575,13 @@ cfb_status lower(Builder& B, size_t* bytes) {
     int rows_max = 1, xrows_max = 1;
     for (const auto& j : B.jobs) { rows_max = std::max(rows_max, j.rows); xrows_max = std::max(xrows_max, std::max(j.rows, j.xcopy)); }
     const int ntb = (rows_max + 7) / 8;
-    const int bucket = ntb <= 2 ? ntb : ntb <= 4 ? 4 : ntb <= 6 ? 6 : 8;   // mma_job<NT> widths
+    const int bucket = ntb <= 2 ? ntb : ntb <= 4 ? 4 : ntb <= 6 ? 6 : 8;
     B.P.maxnt = ntb <= 1 ? 1 : ntb <= 2 ? 2 : ntb <= 4 ? 4 : 8;
     const int RP = bucket * 8;
-    const size_t slot_bytes = (size_t)cfb::kMmaWarps * 16 * RP * 4;
+    // the accumulator staging tile of gathered-row jobs, [kTileRows][kAccCols + 1] fp32
+    const size_t slot_bytes = ((size_t)cfb::kTileRows * (cfb::kAccCols + 1) * 4 + 127) / 128 * 128;
+    // an activation half of a stage: the slot rows padded to the MMA's N granule (8), 128 B each
+    const int xhalf = (xrows_max + 7) / 8 * 8 * 128;
     size_t scratch = (size_t)2 * cfb::kRowsMax * cfb::kTopMax * 4;
     if (flow) {
       const int hd = D / d.heads, Kmax = std::max(DL, C);
@@ -2602,27 +2596,24 @@ cfb_status lower(Builder& B, size_t* bytes) {
     scratch = (scratch + 127) / 128 * 128;
     const int red = cfb::kTileRows * RP * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
     const int desc = cfb::kDescBufs * (cfb::kPhaseSlot + cfb::kJobCache * (int)sizeof(cfb::Job));
-    const int bars = (2 * cfb::kMaxStages + 4) * 8;
-    const int stage_bytes = (cfb::kUnitBytes + xrows_max * cfb::kXRowBytes + 127) / 128 * 128;
-    auto stages_for = [&](int nbuf) {
-      const long fixed = (long)nbuf * slot_bytes + scratch + red + rowstat + misc + bars + 512 +
-                       2 * cfb::kTileRows * 4 + desc + 16;
-      return std::min<long>(cfb::kMaxStages, (cfb::kSmemBudget - fixed) / stage_bytes);
-    };
-    int nbuf = stages_for(2) >= 6 ? 2 : 1;
-    const int nst = (int)stages_for(nbuf);
+    const int bars = (2 * cfb::kMaxStages + 5) * 8;
+    const int stage_bytes = cfb::kUnitBytes + 2 * xhalf;     // a multiple of 1024: stages stay aligned
+    const long fixed = (long)slot_bytes + scratch + red + rowstat + misc + bars + 512 +
+                       2 * cfb::kTileRows * 4 + desc + 16 + 1024;
+    const int nst = (int)std::min<long>(cfb::kMaxStages, (cfb::kSmemBudget - fixed) / stage_bytes);
     if (nst < 3) return CFB_ERR_UNSUPPORTED;
+    const int nbuf = 2;                                        // TMEM accumulators
     cfb::SmemLayout& Lm = B.P.sm;
-    Lm.nstages = nst; Lm.stage_bytes = stage_bytes; Lm.rows_pad = RP; Lm.nbuf = nbuf;
+    Lm.nstages = nst; Lm.stage_bytes = stage_bytes; Lm.rows_pad = RP; Lm.nbuf = nbuf; Lm.xhalf = xhalf;
     Lm.off_bar = nst * stage_bytes;
-    Lm.off_slots = (Lm.off_bar + (2 * nst + 4) * 8 + 127) / 128 * 128;
-    Lm.off_scratch = Lm.off_slots + nbuf * (int)slot_bytes;
+    Lm.off_slots = (Lm.off_bar + (2 * nst + 5) * 8 + 127) / 128 * 128;
+    Lm.off_scratch = Lm.off_slots + (int)slot_bytes;
     Lm.off_red = Lm.off_scratch + (int)scratch;
     Lm.off_rowstat = Lm.off_red + red;
     Lm.off_tile = Lm.off_rowstat + rowstat;
     Lm.off_misc = Lm.off_tile + 2 * cfb::kTileRows * 4;
     Lm.off_desc = (Lm.off_misc + misc + 15) / 16 * 16;
-    Lm.total = Lm.off_desc + desc;
+    Lm.total = Lm.off_desc + desc + 1024;      // + the slack for aligning the base to 1024 bytes
   }
   if (B.too_big) return CFB_ERR_UNSUPPORTED;
   const size_t o_prof = profile ? A.take(ph.size() * (size_t)G * cfb::kProfSlots * 8) : 0;

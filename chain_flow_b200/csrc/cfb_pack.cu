@@ -1,11 +1,13 @@
 // cfb_pack.cu -- one-time weight preparation kernels of libcfb.so (run at drafter load).
 //
 // Packing replaces the reference's per-expert fp16 weight packing (reference
-// src/chain_flow/cuda_block.py:266-311) with the streaming layout the engine reads:
-// [rows/64][k/16][4][512 B]; each 512-byte block is a 16x16 tile in the register order of an
-// m16n8k16 A fragment, so a warp loads it as 32 contiguous 16-byte vectors, and the 8 k blocks
-// of one 64-row tile that form a streamed unit are contiguous. LayerNorm gamma is folded into
-// the weight columns here; cfb_fold_bias folds beta into the bias and sums the folded columns.
+// src/chain_flow/cuda_block.py:266-311) with the streaming layout the engine reads: tiles of 64
+// output rows, each [K/64][64 rows][128 B]; a 128-byte row holds 64 consecutive k of one output
+// row with its 16-byte chunks XOR-swizzled by (row & 7). Each 8 KiB [64 x 64] block is the
+// shared-memory image of a K-major, 128-byte-swizzled tcgen05 operand, and the two blocks of a
+// 128-k streamed unit are contiguous, so the engine moves a unit with one bulk copy and the
+// tensor cores read it in place. LayerNorm gamma is folded into the weight columns here;
+// cfb_fold_bias folds beta into the bias and sums the folded columns.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -19,36 +21,28 @@ namespace {
 __global__ void pack_kernel(const __half* __restrict__ w, int64_t ldw, const int64_t* __restrict__ rows,
                             int nout, int k, const float* __restrict__ gamma, uint4* __restrict__ dst,
                             int ktotal, int kofs) {
-  const int Mt = (nout + 63) / 64 * 4, Kt = k / 16, Ktot = ktotal / 16, kb0 = kofs / 16;
-  const long long n = (long long)Mt * Kt * 32;
+  const int Mt = (nout + 63) / 64, nch = k / 8;
+  const size_t tile_bytes = (size_t)64 * ((ktotal + 63) / 64 * 64) * 2;
+  const long long n = (long long)Mt * 64 * nch;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
-    const int lane = (int)(i & 31);
-    const long long tk = i >> 5;
-    const int kb = (int)(tk % Kt), m = (int)(tk / Kt);
-    const int g = lane >> 2, t = lane & 3;
+    const int ch = (int)(i % nch), row = (int)(i / nch);
     __half h[8];
-    // register order of the A fragment: (row g, cols 2t,2t+1), (row g+8, cols 2t,2t+1),
-    // (row g, cols 2t+8,2t+9), (row g+8, cols 2t+8,2t+9)
-    const int rr[4] = {g, g + 8, g, g + 8};
-    const int cc[4] = {2 * t, 2 * t, 2 * t + 8, 2 * t + 8};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int row = m * 16 + rr[q];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int col = kb * 16 + cc[q] + e;
-        float v = 0.f;
-        if (row < nout) {
-          const int64_t src = rows ? rows[row] : row;
-          v = __half2float(w[src * ldw + col]);
-          if (gamma) v *= gamma[col];
-        }
-        h[2 * q + e] = __float2half_rn(v);
+    for (int e = 0; e < 8; ++e) {
+      const int col = ch * 8 + e;
+      float v = 0.f;
+      if (row < nout) {
+        const int64_t src = rows ? rows[row] : row;
+        v = __half2float(w[src * ldw + col]);
+        if (gamma) v *= gamma[col];
       }
+      h[e] = __float2half_rn(v);
     }
-    dst[(((long long)(m >> 2) * Ktot + kb0 + kb) * 4 + (m & 3)) * 32 + lane] =
-        *reinterpret_cast<const uint4*>(h);
+    const int k0 = kofs + ch * 8, m = row & 63, c = (k0 & 63) >> 3;
+    const size_t byte = (size_t)(row >> 6) * tile_bytes + (size_t)(k0 >> 6) * 8192 + (size_t)m * 128 +
+                        (size_t)((c ^ (m & 7)) << 4);
+    dst[byte / 16] = *reinterpret_cast<const uint4*>(h);
   }
 }
 
@@ -100,7 +94,7 @@ extern "C" {
 
 size_t cfb_packed_bytes(int nout, int k) {
   if (nout <= 0 || k <= 0 || k % 16) return 0;
-  return (size_t)((nout + 63) / 64) * 64u * (size_t)k * 2u;
+  return (size_t)((nout + 63) / 64) * 64u * (size_t)((k + 63) / 64 * 64) * 2u;
 }
 
 cfb_status cfb_pack_linear(const void* w, int64_t ldw, const int64_t* rows, int nout, int k,
@@ -109,7 +103,7 @@ cfb_status cfb_pack_linear(const void* w, int64_t ldw, const int64_t* rows, int 
       ldw < k)
     return CFB_ERR_INVALID_ARG;
   if (reinterpret_cast<uintptr_t>(dst) % 16) return CFB_ERR_INVALID_ARG;
-  const long long n = (long long)((nout + 63) / 64 * 4) * (k / 16) * 32;
+  const long long n = (long long)((nout + 63) / 64) * 64 * (k / 8);
   const int threads = 256;
   const int blocks = (int)((n + threads - 1) / threads < 65535 ? (n + threads - 1) / threads : 65535);
   pack_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(

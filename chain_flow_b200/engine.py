@@ -27,12 +27,12 @@ def tree_levels(keep: int, topb: int, depth: int) -> list[int]:
 
 
 def untile(buf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
-    """Row-major [rows, cols] view of a unit-tiled fp16 activation buffer (layout in cfb.h)."""
-    kp = (cols + 127) // 128 * 128
-    t = buf.reshape(-1)[: rows * kp].view(kp // 128, rows, 16, 8)      # [slice, r, chunk, 8]
+    """Row-major [rows, cols] view of a tiled fp16 activation buffer (layout in cfb.h)."""
+    kp = (cols + 63) // 64 * 64
+    t = buf.reshape(-1)[: rows * kp].view(kp // 64, rows, 8, 8)        # [slice, r, chunk, 8]
     r = torch.arange(rows, device=buf.device).view(1, rows, 1)
-    c = torch.arange(16, device=buf.device).view(1, 1, 16)
-    src = (c ^ (r & 7)).expand(kp // 128, rows, 16)                     # chunk holding logical c
+    c = torch.arange(8, device=buf.device).view(1, 1, 8)
+    src = (c ^ (r & 7)).expand(kp // 64, rows, 8)                       # chunk holding logical c
     t = torch.gather(t, 2, src.unsqueeze(-1).expand(-1, -1, -1, 8))
     return t.permute(1, 0, 2, 3).reshape(rows, kp)[:, :cols]
 

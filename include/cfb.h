@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define CFB_ABI_VERSION 4
+#define CFB_ABI_VERSION 5
 
 typedef enum cfb_status {
   CFB_OK = 0,
@@ -42,10 +42,11 @@ typedef enum cfb_status {
 
 /* ---- packed weights --------------------------------------------------------------------
  * A packed linear holds W (fp16, [nout, k] like nn.Linear.weight) in the engine's streaming
- * layout: rows padded to a multiple of 64, then [nout/64][k/16][4][512 B], where each 512-byte
- * block is one 16x16 tile pre-swizzled into the register order of a tensor-core A fragment
- * (one warp reads it as 32 contiguous 16-byte vectors). A streamed unit is 8 consecutive k
- * blocks of one 64-row tile: 16 KiB, contiguous. A LayerNorm in front of the linear is folded
+ * layout: rows padded to a multiple of 64 and k to a multiple of 64, then
+ * [nout/64][k/64][64 rows][128 B]: each 128-byte row holds 64 consecutive k of one output row,
+ * its 16-byte chunks XOR-swizzled by (row & 7), so every [64 x 64] block (8 KiB) is the
+ * shared-memory image of a K-major, 128-byte-swizzled tcgen05 operand. A streamed unit is two
+ * consecutive blocks (128 k) of one 64-row tile: 16 KiB, contiguous. A LayerNorm in front of the linear is folded
  * in: W' = fp16(W diag(gamma)), bias' = b + W beta and colsum = sum_k W'[:, k]; the engine then
  * computes y = (W' x - mean * colsum) * rstd + bias' from the un-normalised fp16 input. */
 typedef struct cfb_linear {
@@ -206,8 +207,10 @@ cfb_status cfb_plan_error(void* ws, int* device_error);
 cfb_status cfb_plan_info(void* ws, int* grid, int* threads, int* smem, int* phases);
 
 /* Device address and size of one intermediate buffer of a built plan (stage-by-stage checks).
- * fp16 activation buffers are unit-tiled: for R rows and K columns (K padded up to a multiple of
- * 128), element (r, k) is at ((k >> 7) * R + r) * 128 + ((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7).
+ * fp16 activation buffers are tiled: for R rows and K columns (K padded up to a multiple of 128),
+ * element (r, k) is at ((k >> 6) * R + r) * 64 + ((((k & 63) >> 3) ^ (r & 7)) << 3) + (k & 7): each
+ * 64-column slice of all rows is contiguous, one 128-byte row per activation row with its 16-byte
+ * chunks XOR-swizzled by (r & 7) (the tensor cores' K-major 128-byte-swizzled operand image).
  * CFB_BUF_PATH_H16   fp16 tiled [rows, D]     path offsets sum h (rows = B * frontier width)
  * CFB_BUF_PATH_MID   fp16 tiled [rows, 2D]    gelu(LN(h) W_up^T + b)
  * CFB_BUF_HEAD_IN    fp16 tiled [rows, D + r] [pred + residual | markov w1 row], the head input

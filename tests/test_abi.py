@@ -25,13 +25,13 @@ def test_library_exports_every_declared_symbol():
     lib = _lib.load()
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert lib.cfb_abi_version() == _lib.ABI_VERSION == 4
+    assert lib.cfb_abi_version() == _lib.ABI_VERSION == 5
 
 
 def test_packed_bytes():
     lib = _lib.load()
-    assert lib.cfb_packed_bytes(64, 16) == 64 * 16 * 2
-    assert lib.cfb_packed_bytes(65, 32) == 128 * 32 * 2          # rows padded to 64
+    assert lib.cfb_packed_bytes(64, 16) == 64 * 64 * 2           # k padded to 64
+    assert lib.cfb_packed_bytes(65, 32) == 128 * 64 * 2          # rows padded to 64
     assert lib.cfb_packed_bytes(62642, 2816) == 62656 * 2816 * 2
     assert lib.cfb_packed_bytes(64, 15) == 0                     # k must be a multiple of 16
 
@@ -116,7 +116,7 @@ def test_untile_inverts_the_tiled_activation_layout():
         buf = torch.full((R * kp,), float("nan"))
         for r in range(R):
             for k in range(K):
-                idx = ((k >> 7) * R + r) * 128 + ((((k & 127) >> 3) ^ (r & 7)) << 3) + (k & 7)
+                idx = ((k >> 6) * R + r) * 64 + ((((k & 63) >> 3) ^ (r & 7)) << 3) + (k & 7)
                 buf[idx] = x[r, k]
         assert torch.equal(untile(buf, R, K), x)
 
