@@ -439,7 +439,10 @@ def run_ours(args, wl):
         traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "engine_dram_traffic.json"
         if tf.exists():
-            t = json.loads(tf.read_text()).get(wl.name)
+            tj = json.loads(tf.read_text())
+            t = tj.get(wl.name)
+            if not (t and int(t.get("batch", -1)) == B):
+                t = tj.get(f"{wl.name}-b{B}")
             if t and int(t.get("batch", -1)) == B:
                 traffic = t.get("bytes_per_launch")
                 traffic_note = "measured" if t.get("measured") else f"scaled from {t.get('scaled_from')}"
