@@ -116,7 +116,18 @@ CFB_DEV bool mbar_try_wait_a(uint32_t bar, uint32_t parity) {
                : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
 }
+CFB_DEV bool mbar_test_wait_a(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.b32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// (a first non-suspending look: a phase already complete, the common case of a streaming ring,
+// costs less this way)
 CFB_DEV bool mbar_wait_a(uint32_t bar, uint32_t parity, const int* err) {
+  if (mbar_test_wait_a(bar, parity)) return true;
   if (mbar_try_wait_a(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (unsigned it = 1;; ++it) {
@@ -230,6 +241,30 @@ CFB_DEV void tc_commit_warp_a(uint32_t bar) {
       :: "r"(bar) : "memory");
 }
 CFB_DEV void tc_commit_warp(uint64_t* bar) { tc_commit_warp_a(smem_u32(bar)); }
+// A whole 128-k unit in one statement: one elected lane issues the 8 MMAs of k blocks 0-3 (the
+// 64-k half at descriptors a0 / b0) and 4-7 (a1 / b1), each k block 32 bytes (+2 in the
+// descriptors' 16-byte address field) after the last, then the commit on `bar`. One election and
+// one statement per unit measured ~15 % less issue time per unit than eight single-MMA statements.
+CFB_DEV void tc_unit8_warp(uint32_t td, uint64_t a0, uint64_t b0, uint64_t a1, uint64_t b1, uint32_t idesc,
+                           uint32_t accumulate, uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "setp.ne.b32 q, %6, 0;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %5, q;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %9, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %10, %11, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %12, %13, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %4, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %14, %15, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %16, %17, %5, 1;\n\t"
+      "@p tcgen05.mma.cta_group::1.kind::f16 [%0], %18, %19, %5, 1;\n\t"
+      "@p tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}"
+      :: "r"(td), "l"(a0), "l"(b0), "l"(a1), "l"(b1), "r"(idesc), "r"(accumulate), "r"(bar),
+         "l"(a0 + 2), "l"(b0 + 2), "l"(a0 + 4), "l"(b0 + 4), "l"(a0 + 6), "l"(b0 + 6),
+         "l"(a1 + 2), "l"(b1 + 2), "l"(a1 + 4), "l"(b1 + 4), "l"(a1 + 6), "l"(b1 + 6)
+      : "memory");
+}
 // 32 lanes × 16 consecutive fp32 columns of TMEM (lane = row of the accumulator)
 CFB_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];

@@ -982,21 +982,17 @@ CFB_DEV void tc_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& c
       const uint64_t a1 = sw128_desc(ws + kHalfBytes), b1 = sw128_desc(xs + xhalf);
       // k block kb sits in half kb / 4 at byte offset 32 (kb % 4): +2 in the descriptor's
       // 16-byte start-address field per k block
-      tc_mma_f16_warp(td, a0, b0, idesc, fresh ? 0u : 1u);
-      if (nkb == kUnitK) {             // a whole unit: no per-MMA test
-#pragma unroll
-        for (int kb = 1; kb < kUnitK; ++kb) {
-          const uint64_t o = (uint64_t)((kb & 3) * 2);
-          tc_mma_f16_warp(td, (kb < 4 ? a0 : a1) + o, (kb < 4 ? b0 : b1) + o, idesc, 1u);
-        }
+      if (nkb == kUnitK) {             // a whole unit: 8 MMAs and the stage's commit in one go
+        tc_unit8_warp(td, a0, b0, a1, b1, idesc, fresh ? 0u : 1u, empty0 + 8u * (uint32_t)stage);
       } else {
+        tc_mma_f16_warp(td, a0, b0, idesc, fresh ? 0u : 1u);
         for (int kb = 1; kb < nkb; ++kb) {
           const uint64_t o = (uint64_t)((kb & 3) * 2);
           tc_mma_f16_warp(td, (kb < 4 ? a0 : a1) + o, (kb < 4 ? b0 : b1) + o, idesc, 1u);
         }
+        tc_commit_warp_a(empty0 + 8u * (uint32_t)stage);
       }
       fresh = false;
-      tc_commit_warp_a(empty0 + 8u * (uint32_t)stage);
       if (++stage == nst) { stage = 0; par ^= 1u; }
       ++ci;
       nkb_left -= kUnitK;
