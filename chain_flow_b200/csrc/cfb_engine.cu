@@ -2606,7 +2606,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
     // a split tile's owner lists the other contributors (at most G) in the scratch
     scratch = std::max(scratch, (size_t)(G + 1) * 4);
     scratch = (scratch + 127) / 128 * 128;
-    const int red = cfb::kTileRows * RP * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
+    // the reduced tile [kTileRows][RP + 1]: an odd row stride, so that threads walking consecutive
+    // features of one row (and the accumulator readout's 16 lanes) hit distinct banks
+    const int RPs = RP + 1;
+    const int red = cfb::kTileRows * RPs * 4, rowstat = cfb::kRowsMax * 8, misc = 64;
     const int desc = cfb::kDescBufs * (cfb::kPhaseSlot + cfb::kJobCache * (int)sizeof(cfb::Job));
     const int bars = (2 * cfb::kMaxStages + 5) * 8;
     const int stage_bytes = cfb::kUnitBytes + 2 * xhalf;     // a multiple of 1024: stages stay aligned
@@ -2616,7 +2619,7 @@ cfb_status lower(Builder& B, size_t* bytes) {
     if (nst < 3) return CFB_ERR_UNSUPPORTED;
     const int nbuf = 2;                                        // TMEM accumulators
     cfb::SmemLayout& Lm = B.P.sm;
-    Lm.nstages = nst; Lm.stage_bytes = stage_bytes; Lm.rows_pad = RP; Lm.nbuf = nbuf; Lm.xhalf = xhalf;
+    Lm.nstages = nst; Lm.stage_bytes = stage_bytes; Lm.rows_pad = RPs; Lm.nbuf = nbuf; Lm.xhalf = xhalf;
     Lm.off_bar = nst * stage_bytes;
     Lm.off_slots = (Lm.off_bar + (2 * nst + 5) * 8 + 127) / 128 * 128;
     Lm.off_scratch = Lm.off_slots + (int)slot_bytes;
