@@ -321,7 +321,8 @@ cfb_status cfb_tree_gdn_factor(const void* A_log, int A_log_dtype, const void* d
  * library holds until the process exits. Calls with B*N*H*Dk*Dv above that return
  * CFB_ERR_WORKSPACE. The first call on a device looks up the array's address on that device
  * (cudaGetSymbolAddress, with that device current): make that first call before any stream
- * capture. Every call shares the array and leaves its node states there; none of it needs to
+ * capture. The address is kept for the life of the process, so a cudaDeviceReset of that device
+ * after the first call is not supported (the kept address would be stale). Every call shares the array and leaves its node states there; none of it needs to
  * start at zero, but calls that overlap on the GPU (other streams, other host threads) race on
  * it, so order them on one stream. Arguments and supported shapes are those of cfb_tree_gdn. */
 #define CFB_TREE_GDN_NOALLOC_MAX_FLOATS (16 * 1024 * 1024)
