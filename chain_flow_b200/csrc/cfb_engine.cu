@@ -63,6 +63,10 @@ constexpr int kEpi = kEpiWarps * 32;                // 128
 constexpr int kThreads = (kMmaWarps + 2 + kEpiWarps) * 32;   // 448
 constexpr int kWorkers = kMma + kEpi;               // threads that take part in phase-level work
 constexpr int kBarWorkers = 1, kBarEpi = 2;         // named barriers (0 is __syncthreads)
+// GEMM phases of the wide-row builds (engine_kernel<4|8>) other than head phases: worker warps
+// 1..7, idle there, join the epilogue warps for everything but the accumulator readout
+constexpr int kBarWide = 11;                        // (3..10 are the beam merge's row groups)
+constexpr int kEpiWide = kEpi + (kMmaWarps - 1) * 32;   // 352
 
 constexpr int kTileRows = 64;                       // output features per tile (the MMA's M)
 constexpr int kUnitK = 8;                           // 16-wide k blocks per streamed unit
@@ -423,9 +427,10 @@ CFB_DEV float epi_val(const Smem& S, int f, int r) {
 // Row/slice mapping of the epilogue threads for per-row work: `sl` threads per row (8, 4 or 2),
 // each owning 64 / sl consecutive features of a 64-feature tile; whole warps take part.
 struct RowMap { int r, q, sl, nf; };
-CFB_DEV RowMap row_map(int rows, int et) {
+CFB_DEV RowMap row_map(int rows, int et, int n) {
   const int rp = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
-  const int sl = kEpi / rp;
+  const int per = n / rp;                                 // threads per row the group affords
+  const int sl = per >= 8 ? 8 : per >= 4 ? 4 : 2;         // a power of two: 8 or more features each
   return {et / sl, et % sl, sl, kTileRows / sl};
 }
 
@@ -620,7 +625,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     }
     case EK_RESID:
     case EK_PATHH: {
-      const RowMap M = row_map(rows, E.t);
+      const RowMap M = row_map(rows, E.t, E.n);
       float m = 0.f, M2 = 0.f;
       int ng = 0;
       if (M.r < rows) {
@@ -660,7 +665,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
       break;
     }
     case EK_EULER: {
-      const RowMap M = row_map(rows, E.t);
+      const RowMap M = row_map(rows, E.t, E.n);
       const int b = M.r / P.chunk, c = M.r - b * P.chunk;
       const int pos = P.ex[J.e_idx].start + c;
       const int nx = (J.step + 1) & 1;
@@ -754,10 +759,13 @@ CFB_DEV void epi_prefetch(const Plan& P, const Job& J, int tile, const Grp& E) {
 // Epilogue side of one tile: take the MMA warps' partials from slot buffer `b`, reduce them in a
 // fixed order, release the slot, then finish the tile directly or through the stream-K fixup.
 constexpr int kFixBatch = 3;   // contributors whose partials one fixup step loads at once
+// E: the threads that finish the tile (the epilogue warps, or in a wide-epilogue phase those and
+// worker warps 1..7); `reader`: this thread is an epilogue warp's, which alone wait for and read
+// the accumulator (tensor-memory lane quarters are per warp).
 template <class WaitClock>
 CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long long U,
                       long long ug_first, uint32_t& tseq, Smem& S,
-                      HeadState& H, const Grp& E, WaitClock& wc) {
+                      HeadState& H, const Grp& E, bool reader, WaitClock& wc) {
   const int rows = J.rows;
   const int b = tseq % S.nbuf;
   epi_prefetch(P, J, tile, E);
@@ -772,6 +780,8 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
       S.tcsum[E.t - kTileRows] = (J.colsum && col < J.nout) ? J.colsum[col] : 0.f;
     }
   }
+  const bool ident = J.goff == 0 && (J.gin >= rows || J.gstride == J.gin);
+  if (reader) {
   const unsigned long long w0 = wc.now();
   if (!mbar_wait(&S.accf[b], (tseq / S.nbuf) & 1, P.err)) set_err(P, DEV_TIMEOUT_SLOT);
   if (wc.on) { wc.part = wc.now(); wc.slot += wc.part - w0; wc.atom = wc.fix = 0; }
@@ -779,7 +789,6 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
   // The accumulator of an M = 64 MMA: feature f sits in TMEM lane 32 (f / 16) + f % 16, the
   // value for slot row c in column c. Each epilogue warp reads its lane quarter (warp % 4), 16
   // columns at a time; output row r is slot row src_row(r) (the identity but for gathered rows).
-  const bool ident = J.goff == 0 && (J.gin >= rows || J.gstride == J.gin);
   {
     const int q = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
     const int f = 16 * q + (lane & 15);
@@ -799,6 +808,7 @@ CFB_DEV void epi_tile(const Plan& P, const Job& J, int tile, bool complete, long
     }
   }
   tc_fence_before();
+  }
   gsync(E);
   if (E.t == 0) mbar_arrive(&S.acce[b]);
   if (!ident) {
@@ -1010,7 +1020,7 @@ CFB_DEV void tc_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& c
 // Epilogue warps: the same tiles in the same order.
 template <class WaitClock>
 CFB_DEV void epi_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& tseq, Smem& S, HeadState& H,
-                       const Grp& E, WaitClock& wc) {
+                       const Grp& E, bool reader, WaitClock& wc) {
   const long long U = ph.nunits;
   const UnitRange cu = cta_units(P, ph, jt);
   for (int jx = 0; jx < ph.njobs; ++jx) {
@@ -1021,7 +1031,7 @@ CFB_DEV void epi_phase(const Plan& P, const Phase& ph, const Job* jt, uint32_t& 
     if (wc.on) wc.rstat = wc.now();
     for (int tile = ju0 / J.nkc; tile <= (ju1 - 1) / J.nkc; ++tile) {
       const bool complete = (ju0 <= tile * J.nkc) && (ju1 >= (tile + 1) * J.nkc);
-      epi_tile(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, tseq, S, H, E, wc);
+      epi_tile(P, J, tile, complete, U, (long long)J.unit_base + (long long)tile * J.nkc, tseq, S, H, E, reader, wc);
     }
   }
 }
@@ -1942,6 +1952,8 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
   const bool is_epi = warp >= kEpiWarp0;
   const Grp Wk{is_epi ? kMma + (tid - kEpiWarp0 * 32) : tid, kWorkers, kBarWorkers};
   const Grp E{tid - kEpiWarp0 * 32, kEpi, kBarEpi};
+  // the wide epilogue group: epilogue threads first (0..127), then worker warps 1..7
+  const Grp EW{is_epi ? tid - kEpiWarp0 * 32 : kEpi + tid - 32, kEpiWide, kBarWide};
   uint32_t ci = 0, tseq = 0;
   unsigned epoch = 0;
   bool ok = !dead;
@@ -1990,9 +2002,11 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     } else if (ph.kind == PK_RMERGE) {
       rmerge_phase(P, ph, S, Wk);
     } else {
+      // wide-row builds widen the epilogue of non-head GEMM phases onto worker warps 1..7
+      const bool wide = kLean && ph.post == PO_NONE;
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
-        epi_phase(P, ph, jt, tseq, S, H, E, wc);
+        epi_phase(P, ph, jt, tseq, S, H, wide ? EW : E, true, wc);
         if (ph.post != PO_NONE) head_post(P, ph, jt, H, E);
         if (rec) {
           prow[5] = wc.slot; prow[6] = globaltimer();
@@ -2001,6 +2015,7 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
         }
       } else {
         if (warp == kMmaIssueWarp) tc_phase<WaitClock>(P, ph, jt, ci, tseq, S, wc);
+        else if (wide) epi_phase(P, ph, jt, tseq, S, H, EW, false, wc);
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
