@@ -63,8 +63,8 @@ constexpr int kEpi = kEpiWarps * 32;                // 128
 constexpr int kThreads = (kMmaWarps + 2 + kEpiWarps) * 32;   // 448
 constexpr int kWorkers = kMma + kEpi;               // threads that take part in phase-level work
 constexpr int kBarWorkers = 1, kBarEpi = 2;         // named barriers (0 is __syncthreads)
-// GEMM phases of the wide-row builds (engine_kernel<4|8>) other than head phases: worker warps
-// 1..7, idle there, join the epilogue warps for everything but the accumulator readout
+// GEMM phases of the wide-row builds (engine_kernel<4|8>): worker warps 1..7, idle there, join
+// the epilogue warps for everything but the accumulator readout
 constexpr int kBarWide = 11;                        // (3..10 are the beam merge's row groups)
 constexpr int kEpiWide = kEpi + (kMmaWarps - 1) * 32;   // 352
 
@@ -436,9 +436,10 @@ CFB_DEV RowMap row_map(int rows, int et, int n) {
 
 // the head epilogue's map: a row gets kEpi / rows lanes (at least 2 features each), so small
 // row counts keep every epilogue thread busy
-CFB_DEV RowMap head_map(int rows, int et) {
+CFB_DEV RowMap head_map(int rows, int et, int n) {
   const int rp = rows <= 4 ? 4 : rows <= 8 ? 8 : rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
-  const int sl = kEpi / rp;
+  const int per = n / rp;                                 // threads per row the group affords
+  const int sl = per >= 32 ? 32 : per >= 16 ? 16 : per >= 8 ? 8 : per >= 4 ? 4 : 2;
   return {et / sl, et % sl, sl, kTileRows / sl};
 }
 
@@ -713,7 +714,7 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
       break;
     }
     case EK_HEAD: {
-      const RowMap M = head_map(rows, E.t);
+      const RowMap M = head_map(rows, E.t, E.n);
       if (M.r < rows) {
         const int rq = J.cmask ? M.r / J.wrows : 0;
         for (int f = M.q * M.nf; f < (M.q + 1) * M.nf; ++f) {
@@ -1372,7 +1373,7 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
 // row's slice lanes (their sorted lists) by TB rounds of a lane argmax
 __device__ __noinline__ void head_post(const Plan& P, const Phase& ph, const Job* jt, HeadState& H, const Grp& E) {
   const int rows = ph.rows, TB = ph.topb;
-  const RowMap M = head_map(rows, E.t);
+  const RowMap M = head_map(rows, E.t, E.n);
   float m = H.m, ssum = H.s;
   lse_lanes(m, ssum, M.sl);
   float* hp = P.hpart + ((size_t)blockIdx.x * kRowsMax + M.r) * kHeadPartFloats;
@@ -2002,20 +2003,25 @@ __global__ void __launch_bounds__(kThreads, 1) engine_kernel(const Plan* __restr
     } else if (ph.kind == PK_RMERGE) {
       rmerge_phase(P, ph, S, Wk);
     } else {
-      // wide-row builds widen the epilogue of non-head GEMM phases onto worker warps 1..7
-      const bool wide = kLean && ph.post == PO_NONE;
+      // wide-row builds widen the epilogue of GEMM phases onto worker warps 1..7
+      const bool wide = kLean;
       if (is_epi) {
         if (ph.post != PO_NONE) head_reset(H);
         epi_phase(P, ph, jt, tseq, S, H, wide ? EW : E, true, wc);
-        if (ph.post != PO_NONE) head_post(P, ph, jt, H, E);
+        if (ph.post != PO_NONE) head_post(P, ph, jt, H, wide ? EW : E);
         if (rec) {
           prow[5] = wc.slot; prow[6] = globaltimer();
           prow[12] = wc.part; prow[13] = wc.atom; prow[14] = wc.fix; prow[15] = wc.tdone;
           prow[19] = wc.rstat;
         }
       } else {
-        if (warp == kMmaIssueWarp) tc_phase<WaitClock>(P, ph, jt, ci, tseq, S, wc);
-        else if (wide) epi_phase(P, ph, jt, tseq, S, H, EW, false, wc);
+        if (warp == kMmaIssueWarp) {
+          tc_phase<WaitClock>(P, ph, jt, ci, tseq, S, wc);
+        } else if (wide) {
+          if (ph.post != PO_NONE) head_reset(H);
+          epi_phase(P, ph, jt, tseq, S, H, EW, false, wc);
+          if (ph.post != PO_NONE) head_post(P, ph, jt, H, EW);
+        }
         if (rec) { prow[3] = wc.full; prow[4] = wc.slot; prow[10] = wc.first; prow[11] = wc.last; }
       }
     }
