@@ -177,6 +177,11 @@ constexpr int kAttnCache = (int)(kJobCache * sizeof(Job) / sizeof(AttnTask));
 #ifndef CFB_FIXUP_UNITS
 #define CFB_FIXUP_UNITS 12
 #endif
+// The same for jobs of more than 16 rows: a contributor's published partial and the owner's sum
+// grow with the rows, and the fixup then measured dearer.
+#ifndef CFB_FIXUP_UNITS_WIDE
+#define CFB_FIXUP_UNITS_WIDE 24
+#endif
 
 // Dynamic shared memory, laid out per plan by the host from a 1024-byte-aligned base: the ring of
 // streamed units (each stage = 16 KiB of packed weights + the unit's activation rows as two
@@ -2141,9 +2146,10 @@ void add_phase(Builder& B, cfb::Phase ph, const std::vector<cfb::Job>& js) {
   if ((unsigned long long)u * (unsigned long long)(B.G + 1) >= (1ull << 32)) B.too_big = true;
   // Whole tiles per CTA (no cross-CTA fixup) unless splitting tiles finishes sooner even after
   // paying for the fixup, which costs about as much as streaming kFixupUnits units.
-  constexpr long long kFixupUnits = CFB_FIXUP_UNITS;
   long long nkc_max = 1;
-  for (const auto& j : js) nkc_max = std::max<long long>(nkc_max, j.nkc);
+  int rows_max = 1;
+  for (const auto& j : js) { nkc_max = std::max<long long>(nkc_max, j.nkc); rows_max = std::max(rows_max, j.rows); }
+  const long long kFixupUnits = rows_max > 16 ? CFB_FIXUP_UNITS_WIDE : CFB_FIXUP_UNITS;
   const long long G = B.G;
   const long long whole_units = (t + G - 1) / G * nkc_max;
   const long long split_units = (u + G - 1) / G + kFixupUnits;
