@@ -281,6 +281,16 @@ struct VerifyArgs {
 // shared-memory offset of state element (row r, key c)
 __device__ __forceinline__ int tile_off(int r, int c) { return r * kTileLd + c; }
 
+// 16-byte global -> shared copy that does not hold the issuing thread (all of a thread's copies
+// are in flight together; cp_async_wait_all before the data is read)
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const VerifyArgs A) {
   __shared__ float4 ks[kMaxChain][kDk / 4];   // normalised keys, processing order (root first)
@@ -304,12 +314,13 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const V
   const long long crow = (long long)t * A.chain_stride;
   const int vrows = min(kVerifyRows, A.V - (int)blockIdx.z * kVerifyRows);
   constexpr int kWarps = kVerifyThreads / 32;
-  // the state rows of this CTA, row-contiguous from global memory (a warp per row)
+  // the state rows of this CTA, row-contiguous from global memory (a warp per row), every copy
+  // in flight at once
   {
     const float4* src = reinterpret_cast<const float4*>(
         A.state + (long long)A.init_slot[t] * A.slot_stride + ((long long)hv * A.V + blockIdx.z * kVerifyRows) * kDk);
     for (int rr = warp; rr < vrows; rr += kWarps)
-      *reinterpret_cast<float4*>(&st_tile[tile_off(rr, lane * 4)]) = src[rr * (kDk / 4) + lane];
+      cp_async16(&st_tile[tile_off(rr, lane * 4)], src + rr * (kDk / 4) + lane);
   }
   // the chain's node ids first, so that every later load of the CTA issues at once
   if (tid < nd) chs[tid] = A.chain[crow + (nd - 1 - tid)];   // j = 0: the root end of the chain
@@ -330,11 +341,16 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const V
       bts[j] = 1.f / (1.f + expf(-ld_code(A.b, A.c_b, (long long)n * A.HV + hv)));
     }
   }
-  for (int e = tid; e < nd * kVerifyRows; e += kVerifyThreads) {
-    const int j = e / kVerifyRows, rr = e - j * kVerifyRows;
-    const int n = chs[j];
-    const int vr = blockIdx.z * kVerifyRows + rr;
-    vs[j][rr] = vr < A.V ? to_f(v[((long long)n * A.HV + hv) * A.V + vr]) : 0.f;
+  {   // every chain node's value for this thread's row: all loads issued before the first store
+    static_assert(kVerifyThreads == kVerifyRows, "one thread per value row");
+    const int vr = blockIdx.z * kVerifyRows + tid;
+    T vv[kMaxChain];
+#pragma unroll
+    for (int j = 0; j < kMaxChain; ++j)
+      if (j < nd && vr < A.V) vv[j] = v[((long long)chs[j] * A.HV + hv) * A.V + vr];
+#pragma unroll
+    for (int j = 0; j < kMaxChain; ++j)
+      if (j < nd) vs[j][tid] = vr < A.V ? to_f(vv[j]) : 0.f;
   }
   if (A.write_out && warp == kWarps - 1) {
     const T* qr = q + ((long long)t * A.H + h) * kDk + lane * 4;
@@ -344,6 +360,7 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const V
     const float inv = rsqrtf(ss + 1e-6f) * A.scale;
     qs[lane] = make_float4(q0 * inv, q1 * inv, q2 * inv, q3 * inv);
   }
+  cp_async_wait_all();
   __syncthreads();
   const bool live = vrow < A.V;
   float S[kDk];
