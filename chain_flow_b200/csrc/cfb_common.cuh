@@ -157,15 +157,6 @@ CFB_DEV void consumer_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" :: "r"(nthreads) : "memory");
 }
 
-// ---- tensor core (legacy warp-level MMA, m16n8k16, fp16 in, fp32 accumulate) -------------
-CFB_DEV void mma16816(float (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
-}
-
 CFB_DEV uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

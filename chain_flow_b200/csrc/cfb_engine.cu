@@ -75,7 +75,6 @@ constexpr int kUnitBytes = 4 * kUnitK * kBlockBytes;    // 16 KiB: two 8 KiB [64
 constexpr int kHalfBytes = kUnitBytes / 2;
 constexpr int kAccCols = 64;                        // TMEM columns of one accumulator (N <= 64 rows)
 constexpr int kMaxStages = 12;
-constexpr int kXRowBytes = 256;                     // activation row of a unit: 128 fp16
 constexpr int kSmemBudget = 232448 - 1024 - 2048;   // dynamic + static shared memory per CTA
 constexpr int kRowsMax = 64;                        // activation rows per job
 constexpr int kTopMax = 8;                          // top-k per beam row
@@ -110,7 +109,7 @@ enum PKind : int { PK_PREP = 0, PK_GEMM = 1, PK_ATTN = 2, PK_BEAM = 3, PK_RMERGE
 enum Post : int { PO_NONE = 0, PO_BEAM_CHAIN = 1, PO_BEAM_TREE = 2, PO_PUBLISH = 3 };
 
 // Attention of one (expert, block): q rows [B*Sq] and k/v rows [B*Kn] (fp32, written by the
-// projection phase before it), output fp16 unit-tiled with outR rows. One task = (request, head).
+// projection phase before it), output fp16 tiled with outR rows. One task = (request, head).
 struct alignas(16) AttnTask {
   const float* q; int ldq, qoff;
   const float* k; int ldk, koff;
@@ -133,7 +132,7 @@ struct alignas(16) Job {
   int unit_base, tile_base;
   // activation source (fp16 rows, or a gather of embedding rows by path token)
   int xkind;
-  const __half* x; int ldx;                // unit-tiled source with xR rows
+  const __half* x; int ldx;                // tiled source with xR rows
   int xR, xcopy;                           // tiled rows of the source; rows copied per unit
   int gin, gstride, goff;                  // source row = (r / gin) * gstride + goff + r % gin
   int ln; const float2* stats; int nparts; const float* colsum;
@@ -1288,7 +1287,7 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
     for (long long i = gtid; i < 2LL * P.B * P.G; i += gthreads) P.tcnt[i] = 0;
   }
   if (P.mode == kModeVae) {
-    // the input rows, unit-tiled for the in-projection's activation copies; the residual stream
+    // the input rows, tiled for the in-projection's activation copies; the residual stream
     // starts at the learned position rows (the in-projection adds to it)
     const int Din = P.vDin, D = P.D, M = P.B * P.vS;
     for (long long i = gtid; i < (long long)M * Din; i += gthreads) {
@@ -1335,7 +1334,7 @@ __device__ __noinline__ void prep_phase(const Plan& P, const Grp& W) {
         if (lane == 0) X.xstat[0][(size_t)row * nparts + part] = make_float2(mean, m2);
       }
     }
-    // the context rows, unit-tiled for the cross K/V projection's activation copies
+    // the context rows, tiled for the cross K/V projection's activation copies
     for (long long i = gtid; i < (long long)P.B * P.C * D; i += gthreads) {
       const int r = (int)(i / D), c = (int)(i % D);
       P.ctx16[tidx(P.B * P.C, r, c)] = P.ctx[i];

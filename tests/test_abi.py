@@ -107,7 +107,7 @@ def test_plan_rejects_unsupported_shapes():
 
 
 def test_untile_inverts_the_tiled_activation_layout():
-    """The unit-tiled fp16 activation layout documented in cfb.h, and engine.untile's inverse."""
+    """The tiled fp16 activation layout documented in cfb.h, and engine.untile's inverse."""
     import torch
     from chain_flow_b200.engine import untile
     for R, K in ((6, 2560), (4, 160), (3, 64), (8, 256)):
