@@ -112,3 +112,28 @@ def test_twopass_over_the_whole_shortlist_is_the_one_pass_head(name):
     one_t = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5)
     two_t = oracle.beam_tree(W, cfg, g["emb"], hw, w2, sl, g["pred"], g["known0"], 4, 4, 5, twopass_m=R)
     assert torch.equal(one_t, two_t)
+
+
+@pytest.mark.gpu
+def test_gpu_twopass_engine_eight_requests():
+    """The two-pass head in a plan of 8 requests (the wide-row engine build, whose head epilogue
+    runs on the epilogue and worker warps together): g64's two requests repeated four times must
+    give each copy the reference's candidate set and a chain the oracle accepts."""
+    from chain_flow_b200 import _lib
+    from gpu_util import golden_weights, run_plan
+    g, t = load_golden("g64"), _gtp()
+    M, rep = 64, 4
+    W, sl, B0 = g["W"], g["sl"], g["B"]
+    hw, w2 = g["lm_w"][sl], W["markov.w2.weight"][sl]
+    cfg = golden_flow_config(g)
+    w = golden_weights(g)
+    g8 = dict(g)
+    g8["pred"] = g["pred"].repeat(rep, 1, 1)
+    g8["known0"] = g["known0"].repeat(rep)
+    B = B0 * rep
+    p = run_plan(w, _lib.MODE_BEAM_CHAIN, B, known0=g8["known0"], pred=g8["pred"], width=4, depth=5, twopass_m=M)
+    cand = p.candidates().long().cpu()
+    assert bool((cand[:, 1:] > cand[:, :-1]).all())
+    _check_set(cand, t[f"g64.m{M}.cand"].repeat(rep, 1), _scores(hw, g8["pred"], 1, 6), M)
+    _check_chain(p.tokens.cpu(), W, cfg, g8, hw, w2, sl, g8["pred"], cand)
+    assert p.device_error() == 0
