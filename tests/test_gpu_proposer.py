@@ -143,6 +143,13 @@ def test_batch8_flow_and_chain_match_oracle():
     assert _rel(p.pred, want) < HIDDEN_RTOL, _rel(p.pred, want)
     ch = oracle.beam_chains(sd, ocfg, emb, lm[sl], sd["markov.w2.weight"][sl], sl, p.pred.cpu(), known0, 4, 5)
     assert torch.equal(p.tokens.cpu(), ch), (p.tokens.cpu(), ch)
+    # the tree draft of the same batch (the wide-row build's head epilogue in tree mode)
+    t = run_plan(w, _lib.MODE_TREE, B, ctx=ctx, z0=z0, known0=known0, depth=5, tree_keep=4, tree_topb=4)
+    tr = oracle.beam_tree(sd, ocfg, emb, lm[sl], sd["markov.w2.weight"][sl], sl, t.pred.cpu(), known0, 4, 4, 5)
+    if not torch.equal(t.tokens.cpu(), tr):
+        from beam_check import check_tree
+        check_tree(t.tokens.cpu(), sd, ocfg, emb, lm[sl], sd["markov.w2.weight"][sl], sl, t.pred.cpu(), known0,
+                   4, 4, 5)
 
 
 def test_batches_above_one_engine_plan_run_on_the_wide_plan():
