@@ -239,21 +239,30 @@ extern "C" cfb_status cfb_tree_gdn_noalloc(const void* q, const void* k, const v
 // query row t re-walks its ancestor chain chain[t, depth[t]] .. chain[t, 0] from its initial
 // slot, then writes its output row and its state to its own slot.
 //
-// One CTA per (query row, value head, 128 value rows), one thread per value row holding the
-// row's 128 state values in registers: the walk needs no barrier and no cross-thread sum (and
-// two CTAs of 255 registers share an SM). Before it, the CTA stages the ancestor chain (at most
-// kMaxChain nodes) in shared memory: the node ids first, then, all loads at once, each node's
-// normalised key (fp32), decay and beta, the value column of every row, and the query. The
-// state rows move between global and shared memory as 512-byte rows (a warp per row), and
-// between shared memory and registers per thread (rows padded so the accesses spread over banks).
+// One CTA per (query row, value head, kVRows value rows). Each value row's 128 keys are split over
+// kRowParts = 8 lanes, and a lane holds kLaneRows = 2 rows: lane l = 8 g + c holds key chunks c,
+// c + 8, c + 16, c + 24 (16 columns) of rows 2g and 2g + 1 of its warp's 8 rows. A warp's 16-byte
+// access then covers 4 rows x 128 contiguous bytes, so every state load and store moves whole
+// lines straight between global memory and registers. A row's S k (and S q) sum closes over its
+// 8 lanes with 3 shuffles that leave row 2g + (l >> 2) % 2's total in lane l, and 2 indexed
+// shuffles return the rows' updates. The per-node decay is a scalar shared by every element of
+// the CTA, so the state is held as S = G U: a node's decay multiplies only G, and U takes the
+// update divided by G (when G falls below kFoldBelow it is folded into U). The state loads are
+// issued first; while they are in flight the CTA stages the ancestor chain (at most kMaxChain
+// nodes) in shared memory: the chain row, then, all loads at once, each node's normalised key
+// (fp32), decay and beta, the value of every row of the CTA, and the query.
 namespace {
 
 enum { GV_F32 = 0, GV_F16 = 1, GV_BF16 = 2 };
 constexpr int kMaxChain = 16;              // nodes on one row's chain (tree depth + 1)
-constexpr int kVerifyRows = 128;           // value rows per CTA
-constexpr int kVerifyThreads = kVerifyRows;
-constexpr int kTileLd = kDk + 4;           // a staged row + 4 floats of padding
-constexpr int kVerifySmem = kVerifyRows * kTileLd * 4;
+constexpr int kRowParts = 8;               // lanes sharing one value row's keys
+constexpr int kLaneRows = 2;               // value rows a lane holds
+constexpr int kWarpRows = 32 / kRowParts * kLaneRows;      // 8
+constexpr int kLaneChunks = kDk / 4 / kRowParts;           // 16-byte key chunks of a row per lane
+constexpr int kVerifyThreads = 128;
+constexpr int kVerifyMinBlocks = 6;        // CTAs per SM the register budget is cut for
+constexpr int kVRows = kVerifyThreads / 32 * kWarpRows;   // value rows per CTA
+constexpr float kFoldBelow = 1e-20f;       // the decay product folded into the state below this
 
 __device__ __forceinline__ float ld_code(const void* p, int code, long long i) {
   if (code == GV_F32) return static_cast<const float*>(p)[i];
@@ -278,56 +287,69 @@ struct VerifyArgs {
   int H, HV, V, write_out, write_state;
 };
 
-// shared-memory offset of state element (row r, key c)
-__device__ __forceinline__ int tile_off(int r, int c) { return r * kTileLd + c; }
-
-// 16-byte global -> shared copy that does not hold the issuing thread (all of a thread's copies
-// are in flight together; cp_async_wait_all before the data is read)
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-               :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))), "l"(gmem_src) : "memory");
+// The sum over a row's 8 lanes of a[(lane >> 2) % 2]: lane bit 2 picks the row it keeps (adding
+// its partner's copy of that row), then the sum runs over lane bits 1 and 0.
+__device__ __forceinline__ float row_pair_sum(const float (&a)[kLaneRows], int lane) {
+  const bool b2 = lane & 4;
+  float d = (b2 ? a[1] : a[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a[0] : a[1], 4);
+  d += __shfl_xor_sync(0xffffffffu, d, 2);
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
+  return d;
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
+
+// (x . y) over a lane's chunks
+__device__ __forceinline__ float chunk_dot(const float4 (&x)[kLaneChunks], const float4 (&y)[kLaneChunks]) {
+  float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLaneChunks; ++i) {
+    p0 += x[i].x * y[i].x; p1 += x[i].y * y[i].y; p2 += x[i].z * y[i].z; p3 += x[i].w * y[i].w;
+  }
+  return (p0 + p1) + (p2 + p3);
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const VerifyArgs A) {
+__global__ void __launch_bounds__(kVerifyThreads, kVerifyMinBlocks) tree_gdn_verify_kernel(const VerifyArgs A) {
   __shared__ float4 ks[kMaxChain][kDk / 4];   // normalised keys, processing order (root first)
-  __shared__ float vs[kMaxChain][kVerifyRows];
+  __shared__ float vs[kMaxChain][kVRows];
   __shared__ float egs[kMaxChain], bts[kMaxChain];
   __shared__ float4 qs[kDk / 4];
-  __shared__ int chs[kMaxChain];              // the chain's node ids, processing order
-  extern __shared__ float st_tile[];          // [kVerifyRows][kTileLd]
+  __shared__ int chs[kMaxChain];              // the row's chain: chs[0] is the row's own node
   const int tt = blockIdx.x, hv = blockIdx.y;
+  const int vbase = blockIdx.z * kVRows;                  // the CTA's first value row
   const int t = A.rows ? A.rows[tt] : tt;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r = tid;                                      // value row of the CTA
-  const int vrow = blockIdx.z * kVerifyRows + r;
+  const int row0 = vbase + warp * kWarpRows;              // the warp's first value row
+  const int nlive = min(kWarpRows, A.V - row0);           // the warp's rows inside V
   const int h = hv / (A.HV / A.H);
   const T* q = static_cast<const T*>(A.q);
   const T* k = static_cast<const T*>(A.k);
   const T* v = static_cast<const T*>(A.v);
+  const int g = lane >> 3, c = lane & (kRowParts - 1);    // row pair, part of the row
+  const long long sbase = ((long long)hv * A.V + row0 + kLaneRows * g) * kDk;
+  // one round trip for everything the later loads are addressed by: the row's slots, depth and
+  // whole chain row (chain[t, depth] .. chain[t, 0] is the walk from the root end)
+  const int islot = A.init_slot[t];
+  const int oslot = A.write_state ? A.out_slot[t] : 0;
   const int nd = min(A.depth[t] + 1, kMaxChain);
+  const int chv = tid < A.chain_stride ? A.chain[(long long)t * A.chain_stride + tid] : 0;
   const float negA = -expf(ld_code(A.A_log, A.c_alog, hv));
   const float dtb = ld_code(A.dt_bias, A.c_dtb, hv);
-  const long long crow = (long long)t * A.chain_stride;
-  const int vrows = min(kVerifyRows, A.V - (int)blockIdx.z * kVerifyRows);
-  constexpr int kWarps = kVerifyThreads / 32;
-  // the state rows of this CTA, row-contiguous from global memory (a warp per row), every copy
-  // in flight at once
+  // the lane's chunks of its two state rows, in flight while the chain is staged
+  float4 S[kLaneRows][kLaneChunks];
   {
-    const float4* src = reinterpret_cast<const float4*>(
-        A.state + (long long)A.init_slot[t] * A.slot_stride + ((long long)hv * A.V + blockIdx.z * kVerifyRows) * kDk);
-    for (int rr = warp; rr < vrows; rr += kWarps)
-      cp_async16(&st_tile[tile_off(rr, lane * 4)], src + rr * (kDk / 4) + lane);
+    const float4* src = reinterpret_cast<const float4*>(A.state + (long long)islot * A.slot_stride + sbase) + c;
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr)
+#pragma unroll
+      for (int i = 0; i < kLaneChunks; ++i)
+        S[rr][i] = kLaneRows * g + rr < nlive ? __ldcg(src + rr * (kDk / 4) + kRowParts * i) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  // the chain's node ids first, so that every later load of the CTA issues at once
-  if (tid < nd) chs[tid] = A.chain[crow + (nd - 1 - tid)];   // j = 0: the root end of the chain
+  if (tid < A.chain_stride) chs[tid] = chv;
+  constexpr int kWarps = kVerifyThreads / 32;
   __syncthreads();
   // warp w takes nodes j = w, w + kWarps, ...; lane l holds key columns 4l .. 4l+3
   for (int j = warp; j < nd; j += kWarps) {
-    const int n = chs[j];
+    const int n = chs[nd - 1 - j];
     const T* kr = k + ((long long)n * A.H + h) * kDk + lane * 4;
     const float k0 = to_f(kr[0]), k1 = to_f(kr[1]), k2 = to_f(kr[2]), k3 = to_f(kr[3]);
     float ss = (k0 * k0 + k1 * k1) + (k2 * k2 + k3 * k3);
@@ -341,16 +363,19 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const V
       bts[j] = 1.f / (1.f + expf(-ld_code(A.b, A.c_b, (long long)n * A.HV + hv)));
     }
   }
-  {   // every chain node's value for this thread's row: all loads issued before the first store
-    static_assert(kVerifyThreads == kVerifyRows, "one thread per value row");
-    const int vr = blockIdx.z * kVerifyRows + tid;
-    T vv[kMaxChain];
+  {   // every (chain node, value row) of the CTA: element e = j * kVRows + row, all loads first
+    constexpr int kPer = (kMaxChain * kVRows + kVerifyThreads - 1) / kVerifyThreads;
+    T vv[kPer];
 #pragma unroll
-    for (int j = 0; j < kMaxChain; ++j)
-      if (j < nd && vr < A.V) vv[j] = v[((long long)chs[j] * A.HV + hv) * A.V + vr];
+    for (int i = 0; i < kPer; ++i) {
+      const int e = tid + kVerifyThreads * i, j = e / kVRows, vr = vbase + e % kVRows;
+      if (j < nd && vr < A.V) vv[i] = v[((long long)chs[nd - 1 - j] * A.HV + hv) * A.V + vr];
+    }
 #pragma unroll
-    for (int j = 0; j < kMaxChain; ++j)
-      if (j < nd) vs[j][tid] = vr < A.V ? to_f(vv[j]) : 0.f;
+    for (int i = 0; i < kPer; ++i) {
+      const int e = tid + kVerifyThreads * i, j = e / kVRows, vr = vbase + e % kVRows;
+      if (j < nd) vs[j][e % kVRows] = vr < A.V ? to_f(vv[i]) : 0.f;
+    }
   }
   if (A.write_out && warp == kWarps - 1) {
     const T* qr = q + ((long long)t * A.H + h) * kDk + lane * 4;
@@ -360,53 +385,59 @@ __global__ void __launch_bounds__(kVerifyThreads) tree_gdn_verify_kernel(const V
     const float inv = rsqrtf(ss + 1e-6f) * A.scale;
     qs[lane] = make_float4(q0 * inv, q1 * inv, q2 * inv, q3 * inv);
   }
-  cp_async_wait_all();
   __syncthreads();
-  const bool live = vrow < A.V;
-  float S[kDk];
-  float* mine = &st_tile[r * kTileLd];
-#pragma unroll
-  for (int i = 0; i < kDk / 4; ++i) {
-    const float4 f = *reinterpret_cast<const float4*>(mine + 4 * i);
-    S[4 * i] = f.x; S[4 * i + 1] = f.y; S[4 * i + 2] = f.z; S[4 * i + 3] = f.w;
-  }
+  const int myrow = kLaneRows * g + ((lane >> 2) & 1);   // the row whose sums this lane receives
+  // the walk: S <- S exp(g); S += beta (v - S k) k^T, node by node from the root end, on S = G U
+  float G = 1.f;
   for (int j = 0; j < nd; ++j) {
-    const float eg = egs[j];
-    float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+    float Gj = G * egs[j];
+    if (Gj < kFoldBelow) {       // the same for every thread of the CTA
 #pragma unroll
-    for (int i = 0; i < kDk / 4; ++i) {
-      const float4 kk = ks[j][i];
-      S[4 * i] *= eg; S[4 * i + 1] *= eg; S[4 * i + 2] *= eg; S[4 * i + 3] *= eg;
-      p0 += S[4 * i] * kk.x; p1 += S[4 * i + 1] * kk.y; p2 += S[4 * i + 2] * kk.z; p3 += S[4 * i + 3] * kk.w;
-    }
-    const float d = (vs[j][r] - ((p0 + p1) + (p2 + p3))) * bts[j];
+      for (int rr = 0; rr < kLaneRows; ++rr)
 #pragma unroll
-    for (int i = 0; i < kDk / 4; ++i) {
-      const float4 kk = ks[j][i];
-      S[4 * i] += d * kk.x; S[4 * i + 1] += d * kk.y; S[4 * i + 2] += d * kk.z; S[4 * i + 3] += d * kk.w;
+        for (int i = 0; i < kLaneChunks; ++i) { S[rr][i].x *= Gj; S[rr][i].y *= Gj; S[rr][i].z *= Gj; S[rr][i].w *= Gj; }
+      Gj = 1.f;
     }
+    float4 kk[kLaneChunks];
+#pragma unroll
+    for (int i = 0; i < kLaneChunks; ++i) kk[i] = ks[j][c + kRowParts * i];
+    float a[kLaneRows];
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr) a[rr] = chunk_dot(S[rr], kk);
+    const float p = Gj * row_pair_sum(a, lane);
+    const float dm = (vs[j][warp * kWarpRows + myrow] - p) * bts[j] / Gj;
+    float d[kLaneRows];
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr) d[rr] = __shfl_sync(0xffffffffu, dm, kRowParts * g + 4 * rr);
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr)
+#pragma unroll
+      for (int i = 0; i < kLaneChunks; ++i) {
+        S[rr][i].x += d[rr] * kk[i].x; S[rr][i].y += d[rr] * kk[i].y;
+        S[rr][i].z += d[rr] * kk[i].z; S[rr][i].w += d[rr] * kk[i].w;
+      }
+    G = Gj;
   }
   if (A.write_out) {
-    float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+    float4 qq[kLaneChunks];
 #pragma unroll
-    for (int i = 0; i < kDk / 4; ++i) {
-      const float4 qq = qs[i];
-      r0 += S[4 * i] * qq.x; r1 += S[4 * i + 1] * qq.y; r2 += S[4 * i + 2] * qq.z; r3 += S[4 * i + 3] * qq.w;
-    }
-    const float o = (r0 + r1) + (r2 + r3);
-    if (live) from_f(static_cast<T*>(A.o)[((long long)t * A.HV + hv) * A.V + vrow], o);
+    for (int i = 0; i < kLaneChunks; ++i) qq[i] = qs[c + kRowParts * i];
+    float a[kLaneRows];
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr) a[rr] = chunk_dot(S[rr], qq);
+    const float o = G * row_pair_sum(a, lane);
+    if ((lane & 3) == 0 && myrow < nlive)
+      from_f(static_cast<T*>(A.o)[((long long)t * A.HV + hv) * A.V + row0 + myrow], o);
   }
   if (A.write_state) {
-    // own row into shared memory (each thread only ever touches its own row there after the
-    // barrier above), then every row back out row-contiguously
+    float4* dst = reinterpret_cast<float4*>(A.state + (long long)oslot * A.slot_stride + sbase) + c;
 #pragma unroll
-    for (int i = 0; i < kDk / 4; ++i)
-      *reinterpret_cast<float4*>(mine + 4 * i) = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
-    __syncthreads();
-    float4* dst = reinterpret_cast<float4*>(
-        A.state + (long long)A.out_slot[t] * A.slot_stride + ((long long)hv * A.V + blockIdx.z * kVerifyRows) * kDk);
-    for (int rr = warp; rr < vrows; rr += kWarps)
-      dst[rr * (kDk / 4) + lane] = *reinterpret_cast<const float4*>(&st_tile[tile_off(rr, lane * 4)]);
+    for (int rr = 0; rr < kLaneRows; ++rr)
+      if (kLaneRows * g + rr < nlive) {
+#pragma unroll
+        for (int i = 0; i < kLaneChunks; ++i)
+          dst[rr * (kDk / 4) + kRowParts * i] = make_float4(G * S[rr][i].x, G * S[rr][i].y, G * S[rr][i].z, G * S[rr][i].w);
+      }
   }
 }
 
@@ -433,26 +464,11 @@ extern "C" cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, co
   VerifyArgs A{A_log, A_log_dtype, dt_bias, dt_bias_dtype, a, a_dtype, b, b_dtype, q, k, v, o, state,
                slot_stride, chain, chain_stride, depth, out_slot, init_slot, rows, scale, 20.0f,
                H, HV, V, write_out, write_state};
-  const dim3 grid((unsigned)T_rows, (unsigned)HV, (unsigned)((V + kVerifyRows - 1) / kVerifyRows));
-  {
-    static std::mutex mu;
-    static bool done[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    if (dev < 64 && !done[dev]) {
-      if (cudaFuncSetAttribute(tree_gdn_verify_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kVerifySmem) != cudaSuccess ||
-          cudaFuncSetAttribute(tree_gdn_verify_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kVerifySmem) != cudaSuccess)
-        return cfb_launch_status("cudaFuncSetAttribute(tree_gdn_verify_kernel)");
-      done[dev] = true;
-    }
-  }
+  const dim3 grid((unsigned)T_rows, (unsigned)HV, (unsigned)((V + kVRows - 1) / kVRows));
   if (qkv_dtype == GV_F16)
-    tree_gdn_verify_kernel<__half><<<grid, kVerifyThreads, kVerifySmem, static_cast<cudaStream_t>(stream)>>>(A);
+    tree_gdn_verify_kernel<__half><<<grid, kVerifyThreads, 0, static_cast<cudaStream_t>(stream)>>>(A);
   else
-    tree_gdn_verify_kernel<__nv_bfloat16><<<grid, kVerifyThreads, kVerifySmem, static_cast<cudaStream_t>(stream)>>>(A);
+    tree_gdn_verify_kernel<__nv_bfloat16><<<grid, kVerifyThreads, 0, static_cast<cudaStream_t>(stream)>>>(A);
   return cfb_launch_status("tree_gdn_verify_kernel");
 }
 
