@@ -527,13 +527,8 @@ def run_gdn(args):
         for _ in range(max(3, args.warmup)):
             tree_gdn_batched(q, k, v, gl, beta, par, init, states=states)
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            tree_gdn_batched(q, k, v, gl, beta, par, init, states=states)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
+        # device time from graph replays: one request's launch is shorter than a Python call
+        ms, timed = _graph_time_ms(lambda: tree_gdn_batched(q, k, v, gl, beta, par, init, states=states), args.steps)
         achieved = B * per_req / (ms / 1e3) / 1e9
         # CPU baseline: the reference recurrence (oracle) on the host cores, one request
         torch.set_num_threads(os.cpu_count() or 1)
@@ -548,11 +543,12 @@ def run_gdn(args):
             oracle.tree_gdn_scan(qc, kc, vc, gc, bc, pc, dep, ic)
         cpu_s = (time.perf_counter() - t0) / reps
         line = {"metric": "tree GDN verification: requests/s (16-node trees, 16 heads, Dk=Dv=128)",
-                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": timed,
                 "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded q,k,v,alpha,beta,trees)",
-                "config": {"workload": "cfg4-tree-gdn", "batch": B, "nodes": N, "heads": H, "dk": Dk, "dv": Dv},
-                "gpu_launches": args.steps,
+                "config": {"workload": "cfg4-tree-gdn", "batch": B, "nodes": N, "heads": H, "dk": Dk, "dv": Dv,
+                           "timing": f"CUDA graph replays, {timed} launches"},
+                "gpu_launches": timed,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
                              "kernel": "tree_gdn_kernel", "algorithmic_bytes_per_launch": B * per_req},
@@ -601,13 +597,8 @@ def run_gdn_verify(args):
         for _ in range(max(3, args.warmup)):
             run()
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            run()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
+        # device time from graph replays: one request's launch is about as long as a Python call
+        ms, timed = _graph_time_ms(run, args.steps)
         achieved = B * per_req / (ms / 1e3) / 1e9
         # CPU baseline: the oracle's restatement of the reference kernel, one request, all threads
         torch.set_num_threads(os.cpu_count() or 1)
@@ -619,13 +610,14 @@ def run_gdn_verify(args):
                                torch.zeros(N, dtype=torch.int32), K ** -0.5, write_state=False)
         cpu_s = time.perf_counter() - t0
         line = {"metric": "in-engine tree GDN verify: requests/s (41-row trees, 32 value heads, K=V=128)",
-                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "value": B / (ms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": timed,
                 "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32 state, bf16 q/k/v",
                 "data": "synthetic (seeded q,k,v,a,b,A_log,dt_bias,trees)",
                 "config": {"workload": "gdn-verify (reference in-engine shape)", "batch": B, "rows_per_request": N,
-                           "heads": H, "value_heads": HV, "dk": K, "dv": V},
-                "gpu_launches": args.steps,
+                           "heads": H, "value_heads": HV, "dk": K, "dv": V,
+                           "timing": f"CUDA graph replays, {timed} launches"},
+                "gpu_launches": timed,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": None, "peak_source": peak_kind,
                              "kernel": "tree_gdn_verify_kernel", "algorithmic_bytes_per_launch": B * per_req},
@@ -642,26 +634,22 @@ def run_gdn_verify(args):
         for _ in range(max(3, args.warmup)):
             fac()
         torch.cuda.synchronize(dev)
-        e0.record()
-        for _ in range(args.steps):
-            fac()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        fms = e0.elapsed_time(e1) / args.steps
+        fms, ftimed = _graph_time_ms(fac, args.steps)
         fbytes = B * (slot + N * (H * K * 2 * 2 + HV * V * 2 * 2 + HV * 8))
         t0 = time.perf_counter()
         oracle.tree_gdn_factor(*args_c, st_c, chain[sl].cpu(), depth[sl].cpu(), torch.zeros(N, dtype=torch.int32),
                                torch.zeros(1, dtype=torch.int32), torch.full((1,), N, dtype=torch.int32), K ** -0.5)
         fcpu = time.perf_counter() - t0
         line = {"metric": "tree GDN verify outputs, shared-root factorisation: requests/s (41-row trees, 32 value heads)",
-                "value": B / (fms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": args.steps,
+                "value": B / (fms / 1e3), "unit": "req/s", "n_gpus": 1, "steps": ftimed,
                 "warmup": max(3, args.warmup), "ms_per_step": fms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32 state, bf16 q/k/v",
                 "data": "synthetic (seeded q,k,v,a,b,A_log,dt_bias,trees)",
                 "config": {"workload": "gdn-factor (reference in-engine shape)", "batch": B, "rows_per_request": N,
                            "heads": H, "value_heads": HV, "dk": K, "dv": V,
-                           "note": "outputs only; the accepted leaf's state is materialised afterwards by the verify"},
-                "gpu_launches": args.steps,
+                           "note": "outputs only; the accepted leaf's state is materialised afterwards by the verify",
+                           "timing": f"CUDA graph replays, {ftimed} launches"},
+                "gpu_launches": ftimed,
                 "roofline": {"bound": "latency (hbm figure for context)", "achieved": fbytes / (fms / 1e3) / 1e9,
                              "peak": peak, "unit": "GB/s", "frac": fbytes / (fms / 1e3) / 1e9 / peak, "traffic": None,
                              "peak_source": peak_kind, "kernel": "tree_gdn_factor_kernel",

@@ -29,6 +29,11 @@ constexpr int kRowsPerThread = kDk / kQ;
 constexpr int kColsPerBlock = 32;     // value columns per CTA (128 threads)
 constexpr int kMaxNodes = 64;         // nodes per tree a CTA stages in shared memory
 constexpr int kMinBlocks = 4;         // CTAs per SM the register budget is cut for
+// cfb_tree_gdn runs path-parallel (tree_gdn_path_kernel) when the node-by-node grid has fewer
+// (request, head, column block) CTAs than this
+#ifndef CFB_TREE_GDN_PATH_BELOW
+#define CFB_TREE_GDN_PATH_BELOW 256
+#endif
 // dynamic shared memory of a launch over N-node trees: q, k (fp32) and 5 scalars per node
 inline size_t gdn_smem(int N) { return (size_t)N * (2 * kDk + 5) * 4; }
 
@@ -140,6 +145,134 @@ tree_gdn_kernel(const __half* __restrict__ q, const __half* __restrict__ k, cons
   }
 }
 
+// The same recurrence, path-parallel, for launches too small to fill the GPU node by node: one CTA
+// per (request, node, head, 32 value columns), with tree_gdn_kernel's thread layout. The CTA
+// issues its prefix-state loads first, finds its node's ancestor chain in the tree's parent array,
+// stages only the chain's keys (fp32, with their L2 norms, g and beta) and its own node's query,
+// and walks the chain with the state in registers, node by node with tree_gdn_kernel's arithmetic
+// (the same operations in the same order). It writes only its own node's state and output, so no
+// state is re-read; ancestors are recomputed instead (about depth + 1 node steps a node). A
+// parent that is neither -1 nor an earlier node of the tree gives NaN on every node below it, as
+// in tree_gdn_kernel; the bad index is never dereferenced.
+inline size_t gdn_path_smem(int N) { return (size_t)(N + 1) * kDk * 4 + (size_t)N * (5 * 4 + kColsPerBlock * 4); }
+
+__global__ void __launch_bounds__(kColsPerBlock * kQ, kMinBlocks)
+tree_gdn_path_kernel(const __half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+                     const float* __restrict__ g, const float* __restrict__ beta, const int32_t* __restrict__ parent,
+                     const float* __restrict__ init, float* __restrict__ o, float* __restrict__ states, int N,
+                     int H, int Dv, int use_l2norm) {
+  extern __shared__ float gsm[];
+  float (*ks)[kDk] = reinterpret_cast<float (*)[kDk]>(gsm);           // [N] chain keys, root first
+  float* qs = gsm + (size_t)N * kDk;                                  // [kDk] the node's query
+  float* nk = qs + kDk;                                               // [N] key norms
+  float* gd = nk + N;                                                 // [N] exp(g)
+  float* bt = gd + N;                                                 // [N] beta
+  int* ch = reinterpret_cast<int*>(bt + N);                           // [N] chain node ids, root first
+  float (*vs)[kColsPerBlock] = reinterpret_cast<float (*)[kColsPerBlock]>(ch + N);   // [N] v of the columns
+  __shared__ float red[2][2][kQ][kColsPerBlock];
+  __shared__ int s_nd, s_bad;
+  __shared__ float s_nq;
+  const int bn = blockIdx.x;
+  const int b = bn / N, n = bn % N, h = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int j = blockIdx.z * kColsPerBlock + lane;     // value column
+  const int k0 = warp * kRowsPerThread;
+  const float scale = rsqrtf((float)kDk);
+  const bool live = j < Dv;
+  // the prefix state first: its loads are in flight while the chain is found and staged
+  float S[kRowsPerThread];
+  {
+    const float* src = init + ((size_t)b * H + h) * kDk * Dv;
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) S[i] = live ? src[(size_t)(k0 + i) * Dv + j] : 0.f;
+  }
+  // the tree's parent array, one load a thread, then the chain walked in shared memory
+  int* pr = reinterpret_cast<int*>(vs + N);                         // [N]
+  for (int m = tid; m < N; m += blockDim.x) pr[m] = parent[(size_t)b * N + m];
+  __syncthreads();
+  if (tid == 0) {   // the chain, leaf first in ch, then reversed to root first
+    int nd = 0, bad = 0;
+    for (int c = n; c >= 0 && nd < N;) {
+      ch[nd++] = c;
+      const int p = pr[c];
+      if (p >= c || p < -1) { bad = 1; break; }
+      c = p;
+    }
+    for (int i = 0; i < nd / 2; ++i) { const int t = ch[i]; ch[i] = ch[nd - 1 - i]; ch[nd - 1 - i] = t; }
+    s_nd = nd; s_bad = bad;
+  }
+  __syncthreads();
+  const int nd = s_nd;
+  // stage the chain's keys and the node's query (fp16 -> fp32), 16-byte loads all in flight
+  for (int e = tid; e < (nd + 1) * (kDk / 8); e += blockDim.x) {
+    const int r = e / (kDk / 8), c = e - r * (kDk / 8);
+    const int m = r < nd ? ch[r] : n;
+    const size_t nh = ((size_t)b * N + m) * H + h;
+    const uint4 a = *reinterpret_cast<const uint4*>((r < nd ? k : q) + nh * kDk + c * 8);
+    const __half2* a2 = reinterpret_cast<const __half2*>(&a);
+    float* dst = r < nd ? ks[r] : qs;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(a2[i]);
+      dst[c * 8 + 2 * i] = f.x; dst[c * 8 + 2 * i + 1] = f.y;
+    }
+  }
+  for (int e = tid; e < nd * kColsPerBlock; e += blockDim.x) {
+    const int r = e / kColsPerBlock, c = e - r * kColsPerBlock;
+    const int col = blockIdx.z * kColsPerBlock + c;
+    const size_t nh = ((size_t)b * N + ch[r]) * H + h;
+    vs[r][c] = col < Dv ? __half2float(v[nh * Dv + col]) : 0.f;
+  }
+  for (int r = tid; r < nd; r += blockDim.x) {
+    const size_t nh = ((size_t)b * N + ch[r]) * H + h;
+    gd[r] = __expf(g[nh]);
+    bt[r] = beta[nh];
+  }
+  __syncthreads();
+  // L2 norms as tree_gdn_kernel takes them (one warp per row)
+  for (int rr = warp; rr <= nd; rr += blockDim.x >> 5) {
+    const float* src = rr < nd ? ks[rr] : qs;
+    float ss = 0.f;
+    for (int i = lane; i < kDk; i += 32) ss += src[i] * src[i];
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) {
+      const float inv = use_l2norm ? 1.f / (sqrtf(ss) + 1e-6f) : 1.f;
+      if (rr < nd) nk[rr] = inv; else s_nq = inv * scale;
+    }
+  }
+  __syncthreads();
+  if (s_bad) {
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) S[i] = __int_as_float(0x7fc00000);
+  }
+  for (int r = 0; r < nd; ++r) {
+    const int par = r & 1;
+    const float decay = gd[r], kn = nk[r];
+    float kv = 0.f;
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) { S[i] *= decay; kv += S[i] * ks[r][k0 + i]; }
+    red[par][0][warp][lane] = kv;
+    __syncthreads();
+    kv = (red[par][0][0][lane] + red[par][0][1][lane] + red[par][0][2][lane] + red[par][0][3][lane]) * kn;
+    const float delta = (vs[r][lane] - kv) * bt[r];
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) S[i] += (ks[r][k0 + i] * kn) * delta;
+  }
+  float on = 0.f;
+  const size_t nh = ((size_t)b * N + n) * H + h;
+  float* dst = states + nh * kDk * Dv;
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) {
+    on += S[i] * qs[k0 + i];
+    if (live) __stcs(dst + (size_t)(k0 + i) * Dv + j, S[i]);
+  }
+  red[nd & 1][1][warp][lane] = on;
+  __syncthreads();
+  if (warp == 0 && live)
+    o[nh * Dv + j] = (red[nd & 1][1][0][lane] + red[nd & 1][1][1][lane] + red[nd & 1][1][2][lane] +
+                      red[nd & 1][1][3][lane]) * s_nq;
+}
+
 // trees of up to kMaxNodes nodes need more than the default 48 KB of dynamic shared memory
 cfb_status gdn_smem_attr() {
   static std::mutex mu;
@@ -151,6 +284,9 @@ cfb_status gdn_smem_attr() {
   if (cudaFuncSetAttribute(tree_gdn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_smem(kMaxNodes)) !=
       cudaSuccess)
     return cfb_launch_status("tree_gdn_kernel shared-memory attribute");
+  if (cudaFuncSetAttribute(tree_gdn_path_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)gdn_path_smem(kMaxNodes)) != cudaSuccess)
+    return cfb_launch_status("tree_gdn_path_kernel shared-memory attribute");
   if (dev >= 0 && dev < 128) done[dev] = true;
   return CFB_OK;
 }
@@ -167,6 +303,14 @@ extern "C" cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, 
   if (Dk != kDk || Dv <= 0 || Dv % kColsPerBlock || N > kMaxNodes) return CFB_ERR_UNSUPPORTED;
   const cfb_status sa = gdn_smem_attr();
   if (sa != CFB_OK) return sa;
+  // node by node while the (request, head, column block) CTAs fill the GPU; path-parallel below
+  if ((long long)B * H * (Dv / kColsPerBlock) < CFB_TREE_GDN_PATH_BELOW) {
+    const dim3 grid(B * N, H, Dv / kColsPerBlock);
+    tree_gdn_path_kernel<<<grid, kColsPerBlock * kQ, gdn_path_smem(N), static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), g, beta,
+        parent, init, o, states, N, H, Dv, use_l2norm);
+    return cfb_launch_status("tree_gdn_path_kernel");
+  }
   const dim3 grid(B * H, Dv / kColsPerBlock);
   tree_gdn_kernel<<<grid, kColsPerBlock * kQ, gdn_smem(N), static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), g, beta,

@@ -261,6 +261,9 @@ cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);
  * out o [B,N,H,Dv] fp32; states [B,N,H,Dk,Dv] fp32 (every node's state; also where a child
  * reads its parent's state, so it is required).
  * use_l2norm: q,k <- x / (||x|| + 1e-6); q is scaled by Dk**-0.5.
+ * Small launches (fewer than 256 (request, head, 32-column) blocks) run path-parallel: every node
+ * walks its ancestor chain from init with the same per-node arithmetic; larger ones run node by
+ * node. Both write the same states and outputs.
  * Supported: Dk == 128; Dv a multiple of 32; N <= 64 nodes per tree. */
 cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, const float* g,
                         const float* beta, const int32_t* parent, const float* init,

@@ -181,3 +181,43 @@ def test_head_topk_depth1(gw):
         v, i = lp[b * 4].topk(4)
         assert torch.equal(lastp[b * 4:(b + 1) * 4, 0], sl[i]), (b, lastp[b * 4:(b + 1) * 4, 0], sl[i])
         assert torch.allclose(cum[b * 4:(b + 1) * 4], v, atol=1e-4), (b, cum[b * 4:(b + 1) * 4], v)
+
+
+def test_tree_gdn_path_and_node_forms_agree_and_mark_bad_parents():
+    """cfb_tree_gdn runs a launch too small to fill the GPU path-parallel (one request here) and a
+    larger one node by node (eight requests): the same request gets the same states and outputs
+    from both forms, and a parent that is not an earlier node of the tree gives NaN on that node
+    and on every node below it, in both forms, while the other nodes stay finite."""
+    from chain_flow_b200.gdn import make_tree, tree_gdn_batched
+    N, H, Dk, Dv, B = 16, 16, 128, 128, 8
+    g = torch.Generator().manual_seed(77)
+    q = torch.randn(B, N, H, Dk, generator=g).half().cuda()
+    k = torch.randn(B, N, H, Dk, generator=g).half().cuda()
+    v = torch.randn(B, N, H, Dv, generator=g).half().cuda()
+    gl = torch.sigmoid(torch.randn(B, N, H, generator=g)).log().cuda()
+    beta = torch.sigmoid(torch.randn(B, N, H, generator=g)).cuda()
+    init = (torch.randn(B, H, Dk, Dv, generator=g) * 0.1).cuda()
+    par = torch.stack([make_tree(N, 5, 4, seed=30 + b)[0] for b in range(B)])
+    par[0, 5] = 9                                    # not an earlier node: node 5 of request 0 is bad
+    bad = set()
+    for n in range(N):                               # node 5 and everything below it
+        c = n
+        while c >= 0:
+            if c == 5:
+                bad.add(n)
+                break
+            c = int(par[0, c])
+    good = [n for n in range(N) if n not in bad]
+    o8, st8 = tree_gdn_batched(q, k, v, gl, beta, par.cuda(), init)           # node by node
+    o1, st1 = tree_gdn_batched(q[:1], k[:1], v[:1], gl[:1], beta[:1], par[:1].cuda(), init[:1])   # path-parallel
+    torch.cuda.synchronize()
+    o8, st8, o1, st1 = o8.cpu(), st8.cpu(), o1.cpu(), st1.cpu()
+    for o, st in ((o8[0], st8[0]), (o1[0], st1[0])):
+        for n in range(N):
+            assert bool(torch.isnan(o[n]).all()) == (n in bad), n
+            assert bool(torch.isnan(st[n]).all()) == (n in bad), n
+            if n not in bad:
+                assert torch.isfinite(o[n]).all() and torch.isfinite(st[n]).all(), n
+    assert _rel(o1[0, good], o8[0, good]) < 1e-5
+    assert _rel(st1[0, good], st8[0, good]) < 1e-5
+    assert torch.isfinite(o8[1:]).all() and torch.isfinite(st8[1:]).all()
