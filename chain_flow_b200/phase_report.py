@@ -29,7 +29,10 @@ def summarize(t: torch.Tensor, tab: torch.Tensor) -> dict:
     t = t.double()
     start = t[0, :, 0].min()
     ends = t[:, :, 2].max(dim=1).values
-    done = torch.maximum(t[:, :, 1].max(dim=1).values, t[:, :, 6].max(dim=1).values)
+    # the epilogue-done stamp (slot 6) is written by GEMM phases only (kind 1); other phases leave
+    # whatever the slot held, so only their work-done stamp (slot 1) counts
+    gemm = (tab[:, 0] == 1).unsqueeze(1)
+    done = torch.where(gemm, torch.maximum(t[:, :, 1], t[:, :, 6]), t[:, :, 1]).max(dim=1).values
     rows, classes = [], {}
     for i in range(t.shape[0]):
         prev = ends[i - 1] if i else start

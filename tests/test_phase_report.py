@@ -13,8 +13,11 @@ def test_summarize_wall_and_barrier_tail():
     t[0, :, 1] = torch.tensor([2000, 3000])
     t[0, :, 6] = torch.tensor([2500, 3500])
     t[0, :, 2] = torch.tensor([4400, 4500])
-    # phase 1: no epilogue stamps (a non-GEMM phase); work done at 6000, barrier passed at 7000
+    # phase 1: a non-GEMM phase, which writes no epilogue stamp: its slot 6 holds whatever an
+    # earlier run left there (here a stale value far outside the run); work done at 6000,
+    # barrier passed at 7000
     t[1, :, 1] = torch.tensor([6000, 5500])
+    t[1, :, 6] = torch.tensor([-(1 << 62), 1 << 62])
     t[1, :, 2] = torch.tensor([7000, 6900])
     # phase 2: same class as phase 0
     t[2, :, 1] = torch.tensor([9000, 8000])
