@@ -607,14 +607,32 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
     case EK_STORE:
     case EK_STORE16:
     case EK_GELU16: {
-      for (int e = E.t; e < kTileRows * rows; e += E.n) {
-        const int r = e / kTileRows, f = e - r * kTileRows;      // consecutive threads: columns
-        const int col = col0 + f;
-        if (col >= J.nout) continue;
-        const float v = epi_val(S, f, r);
-        if (J.ekind == EK_STORE) J.out32[(size_t)r * J.ldo + col] = v;
-        else if (J.ekind == EK_STORE16) J.out16[(size_t)r * J.ldo + col] = __float2half_rn(v);   // row-major
-        else J.out16[tidx(J.oR, r, col)] = __float2half_rn(gelu_erf(v));
+      // the job's fields in registers (a store through a generic pointer could alias the cached
+      // job in shared memory), and four elements' operands loaded before the first store
+      const int ek = J.ekind, nout = J.nout, oR = J.oR, total = kTileRows * rows;
+      const size_t ldo = (size_t)J.ldo;
+      float* const out32 = J.out32;
+      __half* const out16 = J.out16;
+      constexpr int kU = 4;
+      for (int e0 = E.t; e0 < total; e0 += kU * E.n) {
+        float v[kU];
+        int rr[kU], cc[kU];
+        bool ok[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int e = e0 + u * E.n;
+          const int r = e / kTileRows, f = e - r * kTileRows;      // consecutive threads: columns
+          rr[u] = r; cc[u] = col0 + f;
+          ok[u] = e < total && cc[u] < nout;
+          v[u] = ok[u] ? epi_val(S, f, r) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (!ok[u]) continue;
+          if (ek == EK_STORE) out32[(size_t)rr[u] * ldo + cc[u]] = v[u];
+          else if (ek == EK_STORE16) out16[(size_t)rr[u] * ldo + cc[u]] = __float2half_rn(v[u]);   // row-major
+          else out16[tidx(oR, rr[u], cc[u])] = __float2half_rn(gelu_erf(v[u]));
+        }
       }
       break;
     }
@@ -637,8 +655,11 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
         for (int f0 = M.q * M.nf; f0 < (M.q + 1) * M.nf; f0 += 8) {
           float add[8];
           if (J.ekind == EK_RESID) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) add[i] = J.out32[(size_t)M.r * J.ldo + col0 + f0 + i];
+            // 8 consecutive fp32 columns from a multiple of 8: two 16-byte loads
+            const float4* a4 = reinterpret_cast<const float4*>(J.out32 + (size_t)M.r * J.ldo + col0 + f0);
+            const float4 a = a4[0], c = a4[1];
+            add[0] = a.x; add[1] = a.y; add[2] = a.z; add[3] = a.w;
+            add[4] = c.x; add[5] = c.y; add[6] = c.z; add[7] = c.w;
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) add[i] = 0.f;
@@ -675,45 +696,66 @@ CFB_DEV void tile_epilogue(const Plan& P, const Job& J, int tile, Smem& S, HeadS
       const int pos = P.ex[J.e_idx].start + c;
       const int nx = (J.step + 1) & 1;
       const bool live = M.r < rows;
-      const int f0 = M.q * M.nf;
-      // z <- z + dt * v on this tile's columns of the chunk rows (reference tree_flow.py:229-235)
-      if (live) {
-        for (int f = f0; f < f0 + M.nf; f += 8) {
-          float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f;
+      const bool next = !J.last_step;
+      const int f0 = M.q * M.nf, ne = P.n_experts;
+      const float dt = J.dt;
+      // per expert that sees this position: the running statistics of its next-step input row
+      float m[kMaxExperts], M2[kMaxExperts];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) zp[i] += J.dt * epi_val(S, f + i, M.r);
-        }
-      }
-      if (J.last_step) break;
-      // next step's inputs of every expert that sees this position: z + pos (+ time on its chunk)
-#pragma unroll 1
-      for (int e = 0; e < P.n_experts; ++e) {
-        const ExpertRT& X = P.ex[e];
-        float m = 0.f, M2 = 0.f;
+      for (int e = 0; e < kMaxExperts; ++e) { m[e] = 0.f; M2[e] = 0.f; }
+      if (live) {
         int ng = 0;
-        const bool has = live && pos < X.S;
-        if (has) {
-          const bool cur = pos >= X.start;
-          const int xrow = b * X.S + pos;
-          for (int f = f0; f < f0 + M.nf; f += 8) {
-            const float* zp = P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f;
-            const float* pe = X.pos + (size_t)pos * P.D + col0 + f;
-            const float* te = X.temb + (size_t)(J.step + 1) * P.D + col0 + f;
-            const size_t xi = (size_t)xrow * P.D + col0 + f;
+        for (int f = f0; f < f0 + M.nf; f += 8, ++ng) {
+          // z <- z + dt * v on this tile's columns of the chunk rows (reference tree_flow.py:229-235);
+          // 8 consecutive fp32 columns from a multiple of 8 move as two 16-byte accesses
+          float4* z4 = reinterpret_cast<float4*>(P.pred + ((size_t)b * P.DL + pos) * P.D + col0 + f);
+          const float4 za = z4[0], zb = z4[1];
+          float z[8] = {za.x, za.y, za.z, za.w, zb.x, zb.y, zb.z, zb.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) z[i] += dt * epi_val(S, f + i, M.r);
+          z4[0] = make_float4(z[0], z[1], z[2], z[3]);
+          z4[1] = make_float4(z[4], z[5], z[6], z[7]);
+          if (!next) continue;
+          // next step's inputs of every expert that sees this position: z + pos (+ time on its
+          // chunk), from the z just computed
+#pragma unroll
+          for (int e = 0; e < kMaxExperts; ++e) {
+            if (e >= ne) break;
+            const ExpertRT& X = P.ex[e];
+            if (pos >= X.S) continue;
+            const bool cur = pos >= X.start;
+            const int xrow = b * X.S + pos;
+            const float4* pe4 = reinterpret_cast<const float4*>(X.pos + (size_t)pos * P.D + col0 + f);
+            const float4* te4 = reinterpret_cast<const float4*>(X.temb + (size_t)(J.step + 1) * P.D + col0 + f);
+            const float4 pa = pe4[0], pb = pe4[1];
+            float4 ta = make_float4(0.f, 0.f, 0.f, 0.f), tb = ta;
+            if (cur) { ta = te4[0]; tb = te4[1]; }
+            const float pe[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+            const float te[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
             float xv[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              xv[i] = zp[i] + pe[i] + (cur ? te[i] : 0.f);
-              X.x32[nx][xi + i] = xv[i];
-              X.x16[nx][tidx(P.B * X.S, xrow, col0 + f + i)] = __float2half_rn(xv[i]);
-            }
+            for (int i = 0; i < 8; ++i) xv[i] = z[i] + pe[i] + (cur ? te[i] : 0.f);
+            float4* x4 = reinterpret_cast<float4*>(X.x32[nx] + (size_t)xrow * P.D + col0 + f);
+            x4[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+            x4[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+            // 8 consecutive columns from a multiple of 8 are 16 contiguous bytes of the tiled layout
+            *reinterpret_cast<uint4*>(X.x16[nx] + tidx(P.B * X.S, xrow, col0 + f)) =
+                make_uint4(pack_half2(xv[0], xv[1]), pack_half2(xv[2], xv[3]), pack_half2(xv[4], xv[5]),
+                           pack_half2(xv[6], xv[7]));
             float mb, qb;
             stats8(xv, mb, qb);
-            stats8_add(m, M2, ng++, mb, qb);
+            stats8_add(m[e], M2[e], ng, mb, qb);
           }
         }
-        eq_group(m, M2, (float)M.nf, M.sl);
-        if (M.q == 0 && has) X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m, M2);
+      }
+      if (!next) break;
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e) {
+        if (e >= ne) break;
+        const ExpertRT& X = P.ex[e];
+        const bool has = live && pos < X.S;
+        eq_group(m[e], M2[e], (float)M.nf, M.sl);
+        if (M.q == 0 && has) X.xstat[nx][((size_t)b * X.S + pos) * (P.D / kStatCols) + tile] = make_float2(m[e], M2[e]);
       }
       break;
     }
@@ -2682,7 +2724,10 @@ cfb_status lower(Builder& B, size_t* bytes) {
       }
       X.S = (e + 1) * d.chunk; X.start = e * d.chunk;
       X.pos = d.experts[e].pos_emb; X.temb = d.experts[e].temb;
-      if (!X.pos || !X.temb) return CFB_ERR_INVALID_ARG;
+      // the Euler epilogue moves 8-column groups of these rows (and of pred) as 16-byte accesses
+      if (!X.pos || !X.temb || ((reinterpret_cast<uintptr_t>(X.pos) | reinterpret_cast<uintptr_t>(X.temb) |
+                                 reinterpret_cast<uintptr_t>(r.pred)) & 15))
+        return CFB_ERR_INVALID_ARG;
     }
   }
   P.buf[CFB_BUF_PHASES] = const_cast<cfb::Phase*>(P.phases);

@@ -70,8 +70,8 @@ typedef struct cfb_block {
 
 /* one HiddenKVFlowExpert (reference drafters/chunked_flow.py:205-414) */
 typedef struct cfb_expert {
-  const float* pos_emb;     /* fp32 [draft_len, D]: position_embedding.weight */
-  const float* temb;        /* fp32 [steps, D]: time_mlp(s / steps), from cfb_time_embed */
+  const float* pos_emb;     /* fp32 [draft_len, D]: position_embedding.weight (16-byte aligned) */
+  const float* temb;        /* fp32 [steps, D]: time_mlp(s / steps), from cfb_time_embed (16-byte aligned) */
   cfb_linear out_proj;      /* out_proj, out_norm folded [D, D] */
   const cfb_block* blocks;  /* HOST array [layers] */
 } cfb_expert;
@@ -132,7 +132,8 @@ typedef struct cfb_run {
   const void* ctx;     /* fp16 [B, ctx_rows, D] */
   const void* z0;      /* fp16 [B, draft_len, D] initial latents (CFB_INIT_GIVEN only) */
   const int64_t* known0;  /* int64 [B] committed token per request */
-  float* pred;         /* fp32 [B, draft_len, D]: output of the flow, input of BEAM_* modes */
+  float* pred;         /* fp32 [B, draft_len, D]: output of the flow, input of BEAM_* modes (16-byte
+                          aligned in the flow modes) */
   int64_t* tokens;     /* int64 chain [B, depth]; tree [B, 2N] (N tokens, then N parents) */
   /* Row-sharded shortlist head across `ranks` GPUs (ranks > 1): every rank runs the same
    * requests with the same inputs; the flow is computed on every rank, the head only over this
