@@ -221,3 +221,28 @@ def test_tree_gdn_path_and_node_forms_agree_and_mark_bad_parents():
     assert _rel(o1[0, good], o8[0, good]) < 1e-5
     assert _rel(st1[0, good], st8[0, good]) < 1e-5
     assert torch.isfinite(o8[1:]).all() and torch.isfinite(st8[1:]).all()
+
+
+def test_flow_plan_rejects_a_misaligned_pred():
+    """In the flow modes the Euler epilogue moves pred (and each expert's position and time rows)
+    in 16-byte accesses: cfb_plan_build refuses a pred that is not 16-byte aligned with
+    CFB_ERR_INVALID_ARG, on the host, before anything runs; the same plan then builds and runs
+    with an aligned pred."""
+    from chain_flow_b200 import _lib
+    from chain_flow_b200.engine import Plan
+    from gpu_util import golden_weights
+    g = load_golden("g64")
+    w = golden_weights(g)
+    p = Plan(w, _lib.MODE_FLOW, g["B"])
+    spare = torch.zeros(p.pred.numel() + 4, device="cuda")
+    p.run_desc.pred = spare.data_ptr() + 4
+    with pytest.raises(_lib.CfbError, match="CFB_ERR_INVALID_ARG"):
+        p.rebuild()
+    p.run_desc.pred = p.pred.data_ptr()
+    p.rebuild()
+    p.ctx.copy_(g["ctx"].to(torch.float16))
+    p.z0.copy_(g["z0"].to(torch.float16))
+    p.run()
+    torch.cuda.synchronize()
+    p.check()
+    assert torch.isfinite(p.pred).all()
