@@ -1,17 +1,19 @@
 // cfb_gdn.cu -- tree-aware Gated-DeltaNet verification (sm_100a).
 //
 // Restates the recurrence of the reference's tree scan (src/chain_flow/kernels/tree_scan.py:29-78)
-// and the fork's path-parallel verify kernels (patch tree_gdn.py:3285-3385,
-// tree_gdn_verify.cu:4401-4562), node-serial instead of path-parallel: nodes arrive in BFS order
-// (parent < child), so walking them in index order finds every parent state already written.
+// and the fork's verify kernels (patch tree_gdn.py:3285-3385, tree_gdn_verify.cu:4401-4562).
 // Per node n with parent p (p < 0: the shared prefix state):
 //     S = S_p * exp(g_n);  S += k_n (x) beta_n (v_n - S^T k_n);  o_n = S^T q_n
 // q, k are L2-normalised as x / (||x|| + 1e-6) and q is scaled by Dk**-0.5 (tree_scan.py:25-27).
 //
-// One CTA per (request, head, 128 value columns). A thread owns one value column j and a quarter of the Dk = 128
-// key rows (32 fp32 registers); the S^T k and S^T q column sums reduce over the 4 quarter
-// threads with two shuffles. Every node state is written to `states` ([B,N,H,Dk,Dv] fp32,
-// coalesced along j) and re-read from there as a parent: the same thread wrote it.
+// cfb_tree_gdn runs it node by node (tree_gdn_kernel: nodes arrive in BFS order, parent < child,
+// so walking them in index order finds every parent state already written; one CTA per request,
+// head and 32 value columns, a warp per quarter of the Dk = 128 key rows, a lane per value
+// column), or, for launches too small to fill the GPU that way, path-parallel
+// (tree_gdn_path_kernel: one CTA per node, head and 32 value columns, walking the node's ancestor
+// chain from the prefix state with the same per-node arithmetic). cfb_tree_gdn_verify is the
+// in-engine verify (gate from A_log / dt_bias / a / b, state slots, ancestor chains), and
+// cfb_tree_gdn_factor its shared-root factorisation.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
