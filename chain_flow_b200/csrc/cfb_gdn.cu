@@ -476,7 +476,11 @@ __global__ void __launch_bounds__(kVerifyThreads, kVerifyMinBlocks) tree_gdn_ver
   // whole chain row (chain[t, depth] .. chain[t, 0] is the walk from the root end)
   const int islot = A.init_slot[t];
   const int oslot = A.write_state ? A.out_slot[t] : 0;
-  const int nd = min(A.depth[t] + 1, kMaxChain);
+  // a depth that does not fit the chain row walks nothing and gives NaN (no entry past the row
+  // is ever used as a node index)
+  const int dep = A.depth[t];
+  const bool bad_depth = dep < 0 || dep >= A.chain_stride;
+  const int nd = bad_depth ? 0 : dep + 1;                // chain_stride <= kMaxChain
   const int chv = tid < A.chain_stride ? A.chain[(long long)t * A.chain_stride + tid] : 0;
   const float negA = -expf(ld_code(A.A_log, A.c_alog, hv));
   const float dtb = ld_code(A.dt_bias, A.c_dtb, hv);
@@ -489,6 +493,15 @@ __global__ void __launch_bounds__(kVerifyThreads, kVerifyMinBlocks) tree_gdn_ver
 #pragma unroll
       for (int i = 0; i < kLaneChunks; ++i)
         S[rr][i] = kLaneRows * g + rr < nlive ? __ldcg(src + rr * (kDk / 4) + kRowParts * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (bad_depth) {
+#pragma unroll
+    for (int rr = 0; rr < kLaneRows; ++rr)
+#pragma unroll
+      for (int i = 0; i < kLaneChunks; ++i) {
+        const float nan = __int_as_float(0x7fc00000);
+        S[rr][i] = make_float4(nan, nan, nan, nan);
+      }
   }
   if (tid < A.chain_stride) chs[tid] = chv;
   constexpr int kWarps = kVerifyThreads / 32;

@@ -81,6 +81,36 @@ def test_verify_kernel_matches_oracle(dtype, codes):
     assert _rel(o2.cpu()[rows.long()], want_o[rows.long()]) < GDN_RTOL
 
 
+@pytest.mark.gpu
+def test_verify_depth_past_the_chain_row_gives_nan():
+    """A row whose depth does not fit its chain row (depth >= chain_stride, or < 0) walks nothing
+    from memory: its output and state are NaN, and every other row still matches the oracle."""
+    from chain_flow_b200.gdn import gdn_verify
+    c = _case(11)
+    T, K = c["q"].shape[0], c["q"].shape[2]
+    want_o, want_st = oracle.tree_gdn_verify(c["A_log"], c["dt_bias"], c["a"], c["b"], c["q"], c["k"], c["v"],
+                                             c["state"], c["chain"], c["depth"], c["out_slot"], c["init_slot"],
+                                             K ** -0.5)
+    depth = c["depth"].clone()
+    bad = [4, 9]
+    depth[4] = c["chain"].shape[1]          # one past the row
+    depth[9] = -1
+    dev = "cuda"
+    st = c["state"].to(dev)
+    o = torch.zeros(T, c["v"].shape[1], c["v"].shape[2], dtype=torch.float16, device=dev)
+    gdn_verify(*(c[n].to(dev) for n in ("A_log", "dt_bias", "a", "b", "q", "k", "v")), o, st,
+               c["chain"].to(dev), depth.to(dev), c["out_slot"].to(dev), c["init_slot"].to(dev), scale=K ** -0.5)
+    torch.cuda.synchronize()
+    o, st = o.float().cpu(), st.cpu()
+    good = [t for t in range(T) if t not in bad]
+    for t in bad:
+        assert torch.isnan(o[t]).all()
+        assert torch.isnan(st[int(c["out_slot"][t])]).all()
+    assert _rel(o[good], want_o[good]) < GDN_RTOL
+    good_slots = c["out_slot"][good].long()
+    assert _rel(st[good_slots], want_st[good_slots]) < GDN_RTOL
+
+
 def _batched_case(seed, S=2, N=20, H=2, HV=4, V=64, K=128, max_depth=5):
     """S requests of N rows each, request s's rows starting from state slot s (the shared root)."""
     from chain_flow_b200.gdn import ancestor_chains, make_tree
