@@ -284,8 +284,9 @@ cfb_status cfb_tree_gdn(const void* q, const void* k, const void* v, const float
  * slot stride slot_stride floats; chain, depth, out_slot, init_slot, rows int32; rows (may be
  * NULL) selects the T_rows query rows. Out slots must not be read as init slots by other rows
  * of the same call. A row whose depth does not fit its chain row (depth < 0 or >= chain_stride)
- * gets NaN output and state. Supported: K == 128, V a multiple of 32, HV a multiple of H,
- * chain_stride <= 16. */
+ * gets NaN output and state. The chain entries chain[t, 0 .. depth[t]] themselves are used as row
+ * indices of k, v, a and b as given (the call has no row count to check them against). Supported:
+ * K == 128, V a multiple of 32, HV a multiple of H, chain_stride <= 16. */
 cfb_status cfb_tree_gdn_verify(const void* A_log, int A_log_dtype, const void* dt_bias,
                                int dt_bias_dtype, const void* a, int a_dtype, const void* b,
                                int b_dtype, const void* q, const void* k, const void* v, void* o,
