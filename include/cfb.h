@@ -262,7 +262,8 @@ cfb_status cfb_plan_buffer(void* ws, int which, void** ptr, size_t* bytes);
  * out o [B,N,H,Dv] fp32; states [B,N,H,Dk,Dv] fp32 (every node's state; also where a child
  * reads its parent's state, so it is required).
  * use_l2norm: q,k <- x / (||x|| + 1e-6); q is scaled by Dk**-0.5.
- * Small launches (fewer than 256 (request, head, 32-column) blocks) run path-parallel: every node
+ * Launches whose node-by-node grid would have fewer (request, head, 32-column) blocks than the
+ * device has SMs run path-parallel: every node
  * walks its ancestor chain from init with the same per-node arithmetic; larger ones run node by
  * node. Both write the same states and outputs.
  * Supported: Dk == 128; Dv a multiple of 32; N <= 64 nodes per tree. */
